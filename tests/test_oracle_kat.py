@@ -1,0 +1,107 @@
+"""The CPU oracle against the reference's own known-answer fixtures.
+
+The saved models under ``tests/golden/`` were written by hessboost 0.4.9's
+``tests/native_format.rs`` (see ``make_golden.py``).  Two of them are full
+training runs of the hist path on the 160 x 4 probe; every one of them pins
+prediction.  The oracle must reproduce them bit for bit, in the reference's
+f64 summation and in the int64 fixed-point summation the CUDA path uses.
+"""
+
+import numpy as np
+import pytest
+
+import oracle_lib as O
+
+TRAIN_KATS = [("early_stopping", "y1"), ("multi_target", "y2")]
+
+
+def _model(g, name):
+    return [m for m in g["models"] if m["name"] == name][-1]
+
+
+def _assert_trees_equal(nodes, ptr, gnodes, gptr):
+    assert len(ptr) == len(gptr)
+    for t in range(len(gptr) - 1):
+        a = nodes[int(ptr[t]) : int(ptr[t + 1])]
+        b = gnodes[int(gptr[t]) : int(gptr[t + 1])]
+        assert len(a) == len(b), f"tree {t}: {len(a)} vs {len(b)} nodes"
+        for k in ("left", "right", "split_feature", "default_left"):
+            np.testing.assert_array_equal(a[k], b[k], err_msg=f"tree {t} {k}")
+        for k in ("split_cond", "leaf_value", "sum_hess", "split_gain"):
+            np.testing.assert_array_equal(O.f32_to_bits(a[k]), O.f32_to_bits(b[k]), err_msg=f"tree {t} {k}")
+
+
+@pytest.mark.parametrize("fixed", [False, True], ids=["f64", "fixed_point"])
+@pytest.mark.parametrize("name,ykey", TRAIN_KATS)
+def test_training_kat_bit_exact(name, ykey, fixed):
+    g = O.golden()
+    m = _model(g, name)
+    nodes, ptr, base, margins = O.train(g["x"], g[ykey], 4, max_depth=3, eta=0.3, fixed_point=fixed)
+    np.testing.assert_array_equal(O.f32_to_bits(base), O.f32_to_bits(np.array(m["base_score"], np.float32)))
+    gnodes, gptr = O.golden_nodes(m)
+    _assert_trees_equal(nodes, ptr, gnodes, gptr)
+
+
+def test_prediction_kats_bit_exact():
+    g = O.golden()
+    assert len(g["models"]) >= 9
+    for m in g["models"]:
+        nodes, ptr = O.golden_nodes(m)
+        n, outs, w = O.golden_layout(m)
+        got = O.predict(nodes, ptr[: n + 1], m["n_outputs"], np.array(m["base_score"], np.float32), g["x"], outs, w)
+        np.testing.assert_array_equal(O.f32_to_bits(got).ravel(), np.array(m["margins_bits"], np.uint32), err_msg=m["name"])
+
+
+def test_sketch_known_answers():
+    # src/data/sketch.rs:876-895: the minimum is never a cut, a sentinel
+    # closes the last bin, an empty feature gets the upstream placeholder.
+    off, cuts = O.cuts_dense(np.array([[2.0], [0.0], [1.0], [1.0]], np.float32), 256)
+    np.testing.assert_array_equal(cuts, np.array([1.0, 2.0, np.float32(2.0) + (np.float32(2.0) + np.float32(1e-5))], np.float32))
+    off, cuts = O.cuts_dense(np.full((3, 1), np.nan, np.float32), 256)
+    np.testing.assert_array_equal(cuts, np.array([1e-5], np.float32))
+    vals = ((np.arange(5000) * 7919) % 5000).astype(np.float32) * np.float32(0.001)
+    off, cuts = O.cuts_dense(vals.reshape(-1, 1), 64)
+    assert len(cuts) <= 64 and np.all(np.diff(cuts) > 0) and cuts[-1] > 4.999
+
+
+def test_gain_closed_forms():
+    # src/tree/gain.rs:155-196 style closed form through a one-split tree:
+    # two rows, g = (-1, +1), h = 1, lambda = 1 -> leaves -(-1)/(1+1) * eta.
+    x = np.array([[0.0], [1.0]], np.float32)
+    y = np.array([1.0, -1.0], np.float32)  # base = 0 -> g = 0 - y
+    nodes, ptr, base, _ = O.train(x, y, 1, max_depth=1, eta=1.0, min_child_weight=0.0)
+    assert base[0] == 0.0
+    leaves = nodes[nodes["left"] == -1]["leaf_value"]
+    np.testing.assert_array_equal(np.sort(leaves), np.array([-0.5, 0.5], np.float32))
+
+
+def test_logistic_gradient_closed_form():
+    # classification.rs:251-290: p = sigmoid(m), g = p - y, h = p(1-p).
+    m = np.linspace(-6, 6, 1003).astype(np.float32)
+    y = (np.arange(1003) % 2).astype(np.float32)
+    gp = O.gradients(1, m, y)
+    p = 1.0 / (1.0 + np.exp(-m.astype(np.float64)))
+    np.testing.assert_allclose(gp[:, 0], p - y, rtol=0, atol=2e-7)
+    np.testing.assert_allclose(gp[:, 1], p * (1 - p), rtol=1e-4, atol=2e-7)
+
+
+def test_fixed_scale_bounds():
+    for max_abs in [1e-30, 0.25, 0.9999, 1.0, 3.5, 1e20]:
+        for n in [1, 2, 3, 160, 10_000_000]:
+            s = O.fixed_scale(max_abs, n)
+            q = np.rint(np.float64(np.float32(max_abs)) * 2.0 ** s)
+            assert q * n <= 2.0 ** 62
+    assert O.fixed_scale(0.0, 10) == 0
+
+
+@pytest.mark.parametrize("missing", [False, True])
+def test_fixed_point_matches_f64_structure(missing):
+    # On data whose f64 sums are exact, the two summation modes agree.
+    rng = np.random.default_rng(3)
+    x = rng.integers(0, 50, size=(3000, 6)).astype(np.float32)
+    if missing:
+        x[rng.random(x.shape) < 0.05] = np.nan
+    y = (np.nan_to_num(x[:, 0]) * 0.5 - np.nan_to_num(x[:, 1]) * 0.25).astype(np.float32)
+    a = O.train(x, y, 3, max_depth=4, eta=0.5)
+    b = O.train(x, y, 3, max_depth=4, eta=0.5, fixed_point=True)
+    _assert_trees_equal(a[0], a[1], b[0], b[1])
