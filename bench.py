@@ -1,0 +1,344 @@
+#!/usr/bin/env python
+"""Benchmark of the hist path: boosting rounds per second at config C2.
+
+Workload: binary logistic on 10,000,000 x 28 f32 rows,
+N(0,1) with 5% NaN, max_bin 256, max_depth 8, eta 0.1, every row in every
+tree; seeded synthetic data of that shape (hessboost_b200.synth). A step is
+one boosting round: gradients at the device margins, one depth-8 tree grown
+on the device, its leaves added to the margins, the tree read back.
+
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl reference]
+
+With N > 1 (launched by torch.distributed.run, one process per GPU) the rows
+are sharded over the ranks (strong scaling: the 10M rows stay 10M) and every
+histogram is summed with NCCL; rank 0 prints one JSON line.
+
+`--impl reference` times the reference's CPU path instead. The reference
+(Rust) cannot be built in this image, so its arm runs the C++ restatement
+under oracle/ on the host cores (rank 0 only).
+"""
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+METRIC = "boost rounds/s at 10M×28 depth-8 on 1/2/4/8 B200; hist-build GB/s vs HBM peak"
+UNIT = "rounds/s"
+N_ROWS = 10_000_000
+N_COLS = 28
+MISSING = 0.05
+PARAMS = dict(objective="binary:logistic", max_depth=8, eta=0.1, max_bin=256)
+
+
+def log(*a):
+    print(*a, file=sys.stderr, flush=True)
+
+
+def config(n_gpus):
+    return {
+        "workload": "C2: binary:logistic, 10,000,000 x 28 f32 N(0,1) with 5% NaN, max_bin 256, "
+        "max_depth 8, eta 0.1, lambda 1, every row in every tree",
+        "rows": N_ROWS,
+        "features": N_COLS,
+        "max_depth": 8,
+        "max_bin": 256,
+        "parallelism": f"rows sharded over {n_gpus} GPU(s), one NCCL allreduce per level"
+        if n_gpus > 1 else "1 GPU",
+        "l2": "inputs larger than L2: the binned rows (320 MB records + 280 MB columns) and "
+        "80 MB of gradients are re-read every round",
+    }
+
+
+def peaks():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as fh:
+            p = json.load(fh)
+        return float(p["hbm_gbs"]), "measured"
+    except Exception:  # noqa: BLE001
+        return 6650.0, "fallback"
+
+
+class ClockSampler:
+    """nvidia-smi clocks and throttle reasons during the timed region."""
+
+    def __init__(self, gpus):
+        self.path = tempfile.mktemp(suffix=".csv")
+        q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={q}", "--format=csv,noheader,nounits", "-lms", "200",
+                 "-i", ",".join(str(g) for g in gpus)],
+                stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+        except Exception:  # noqa: BLE001
+            self.proc = None
+
+    def stop(self):
+        if self.proc is None:
+            return None
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except Exception:  # noqa: BLE001
+            self.proc.kill()
+        sm, mx, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        try:
+            for line in open(self.path):
+                f = [x.strip() for x in line.split(",")]
+                if len(f) < 9:
+                    continue
+                try:
+                    sm.append(float(f[1]))
+                    mx.append(float(f[2]))
+                except ValueError:
+                    continue
+                for name, v in zip(names, f[5:9]):
+                    if v.lower().startswith("active"):
+                        reasons.add(name)
+        finally:
+            try:
+                os.unlink(self.path)
+            except OSError:
+                pass
+        if not sm:
+            return None
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": max(mx), "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+def make_data():
+    from hessboost_b200 import synth
+
+    return synth.logistic_c2(N_ROWS, N_COLS, seed=0, missing=MISSING)
+
+
+# ------------------------------------------------------------------ reference
+def cpu_rounds(x, y, k_max, budget_s, warm=1):
+    """The oracle (the reference's CPU hist path restated in C++, OpenMP over
+    the host cores): preparation untimed, then rounds timed, at most
+    `k_max`, stopping once `budget_s` seconds are spent."""
+    sys.path.insert(0, os.path.join(ROOT, "tests"))
+    import oracle_lib as O
+
+    O.build()
+    tr = O.Trainer(x, y, objective=1, max_depth=8, eta=0.1, max_bin=256)
+    for _ in range(warm):
+        tr.rounds(1)
+    done, t0 = 0, time.perf_counter()
+    while done < k_max:
+        tr.rounds(1)
+        done += 1
+        if time.perf_counter() - t0 > budget_s:
+            break
+    dt = time.perf_counter() - t0
+    tr.close()
+    return done, dt
+
+
+def run_reference(args):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    cores = os.cpu_count() or 1
+    x, y = make_data()
+    k, dt = cpu_rounds(x, y, max(1, args.steps), budget_s=120.0, warm=min(args.warmup, 1))
+    value = k / dt
+    sample = (f"{k} timed round(s) of the full C2 workload after binning and 1 untimed round "
+              f"(C++ restatement of hessboost's CPU hist path, OpenMP on {cores} threads; "
+              "the Rust reference cannot be built offline)")
+    print(json.dumps({
+        "impl": "reference", "metric": METRIC, "value": value, "unit": UNIT,
+        "n_gpus": args.gpus, "steps": k, "warmup": min(args.warmup, 1),
+        "ms_per_step": 1000.0 * dt / k, "higher_is_better": True, "scaling": "strong",
+        "vs_baseline": None, "dtype": "f64", "data": "synthetic", "config": config(args.gpus),
+        "cpu_baseline": {"value": value, "unit": UNIT, "cores": cores, "kind": "port", "sample": sample},
+        "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }), flush=True)
+
+
+# ------------------------------------------------------------------ ours
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.impl == "reference":
+        run_reference(args)
+        return
+
+    import torch
+    import torch.distributed as dist
+
+    import hessboost_b200 as H
+    from hessboost_b200 import dist as hdist
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    if world > 1:
+        from datetime import timedelta
+
+        dist.init_process_group("nccl", timeout=timedelta(seconds=600), device_id=torch.device("cuda", local))
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    def allreduce_max(v):
+        if world == 1:
+            return v
+        t = torch.tensor([v], dtype=torch.float64, device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    def allreduce_sum(v):
+        if world == 1:
+            return v
+        t = torch.tensor([v], dtype=torch.float64, device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.SUM)
+        return float(t.item())
+
+    t_data = time.perf_counter()
+    x, y = make_data()
+    params = H.TrainingParams(**PARAMS)
+    # cut table over the whole matrix (rank 0), shared so every rank bins
+    # against the same cuts
+    if rank == 0:
+        off, cuts = H.cuts_dense(x, 256)
+    else:
+        off = cuts = None
+    if world > 1:
+        obj = [off, cuts]
+        dist.broadcast_object_list(obj, src=0)
+        off, cuts = obj
+    begin, end = hdist.shard_bounds(N_ROWS, world, rank)
+    cols, miss, dense = H.bin_dense(x[begin:end], off, cuts)
+    shard = H.BinnedMatrix(off, cuts, cols, miss, dense)
+    base = H.base_margin(params, y)
+    log(f"[rank {rank}] data + binning {time.perf_counter() - t_data:.1f}s rows [{begin}, {end})")
+
+    eng = H.Engine(local)
+    eng.set_shard(begin, N_ROWS)
+    if world > 1:
+        uid = hdist.broadcast_unique_id(dist, hdist.unique_id)
+        eng.comm_init(world, rank, uid, N_ROWS)
+    eng.upload(shard)
+    y_shard = np.ascontiguousarray(y[begin:end])
+    eng.train_begin(y_shard, base)
+    eng.train_rounds(params, args.warmup)
+
+    # ---- timed region: K rounds, device time, max over ranks
+    sampler = ClockSampler([local]) if rank == 0 else None
+    eng.reset_stats(timing=True)
+    stream = torch.cuda.ExternalStream(eng.stream(), device=torch.device("cuda", local))
+    ev0 = torch.cuda.Event(enable_timing=True)
+    ev1 = torch.cuda.Event(enable_timing=True)
+    barrier()
+    torch.cuda.synchronize()
+    ev0.record(stream)
+    nodes, tree_ptr = eng.train_rounds(params, args.steps)
+    ev1.record(stream)
+    torch.cuda.synchronize()
+    barrier()
+    ms = allreduce_max(ev0.elapsed_time(ev1))
+    clocks = sampler.stop() if sampler else None
+    st = eng.stats()
+    launches = int(allreduce_sum(st["kernel_launches"]))
+    value = args.steps / (ms / 1000.0)
+
+    # roofline of the histogram kernel (root + level launches of k_hist)
+    hist_ms = st["ms"]["hist"] + st["ms"]["root_hist"]
+    hist_launches = st["timed_launches"]["hist"] + st["timed_launches"]["root_hist"]
+    bitmap = N_COLS / 8.0 if not dense else 0.0
+    alg_bytes = (st["rows_built_contiguous"] * (N_COLS + 8 + bitmap)
+                 + st["rows_built_gathered"] * (N_COLS + 8 + 4 + bitmap))
+    achieved = alg_bytes / (hist_ms / 1000.0) / 1e9 if hist_ms > 0 else 0.0
+    peak, peak_kind = peaks()
+    traffic = None
+    prof = os.path.join(ROOT, "profiles", "hist_traffic.json")
+    if os.path.exists(prof):
+        try:
+            traffic = json.load(open(prof)).get("bytes_per_launch")
+        except Exception:  # noqa: BLE001
+            traffic = None
+    log(f"[rank {rank}] {args.steps} rounds {ms:.1f} ms; kernel ms {json.dumps(st['ms'])}")
+
+    # ---- end to end through the C ABI from pinned host buffers
+    barrier()
+    pin = lambda a: torch.from_numpy(np.ascontiguousarray(a)).pin_memory().numpy()  # noqa: E731
+    pcols, plab = pin(cols), pin(y_shard)
+    pmiss = pin(miss) if not dense else None
+    e2e_shard = H.BinnedMatrix(off, cuts, pcols, pmiss, dense)
+    eng2 = H.Engine(local)
+    eng2.set_shard(begin, N_ROWS)
+    if world > 1:
+        uid2 = hdist.broadcast_unique_id(dist, hdist.unique_id)
+        eng2.comm_init(world, rank, uid2, N_ROWS)
+    barrier()
+    t0 = time.perf_counter()
+    eng2.upload(e2e_shard)
+    eng2.train_begin(plab, base)
+    nodes2, ptr2 = eng2.train_rounds(params, args.steps)
+    torch.cuda.synchronize()
+    e2e_s = allreduce_max(time.perf_counter() - t0)
+    barrier()
+    h2d = (pcols.nbytes + (pmiss.nbytes if pmiss is not None else 0) + plab.nbytes + 4 * (end - begin)
+           + off.nbytes + cuts.nbytes)
+    h2d_total = allreduce_sum(h2d)
+    d2h_total = allreduce_sum(len(nodes2) * H.NODE_DTYPE.itemsize)
+    e2e = {"value": args.steps / e2e_s, "unit": UNIT,
+           "h2d_bytes_per_step": h2d_total / args.steps, "d2h_bytes_per_step": d2h_total / args.steps,
+           "scope": "hb_engine_upload of the binned shard + hb_train_begin + hb_train_rounds(K) from "
+                    "pinned host buffers; trees read back"}
+    eng2.close()
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        cores = os.cpu_count() or 1
+        k, dt = cpu_rounds(x, y, 3, budget_s=25.0, warm=0)
+        cpu = {"value": k / dt, "unit": UNIT, "cores": cores, "kind": "port",
+               "sample": f"{k} round(s) of the full C2 workload after binning (C++ restatement of "
+                         f"hessboost's CPU hist path, OpenMP, {cores} threads)"}
+
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True,
+            "scaling": "strong", "vs_baseline": None, "dtype": "int64", "data": "synthetic",
+            "config": dict(config(world), rows_per_s=value * N_ROWS,
+                           trees_nodes=int(len(nodes)), kernel_ms=st["ms"]),
+            "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
+                         "frac": achieved / peak, "traffic": traffic,
+                         "kernel": "k_hist", "launches": hist_launches,
+                         "avg_launch_ms": hist_ms / max(hist_launches, 1),
+                         "alg_bytes_per_launch": alg_bytes / max(hist_launches, 1),
+                         "peak_kind": peak_kind + " (MEASURED_PEAKS.json hbm_gbs)"},
+            "cpu_baseline": cpu,
+            "e2e": e2e,
+            "gpu_launches": launches,
+            "clocks": clocks,
+        }
+        print(json.dumps(line), flush=True)
+    eng.close()
+    if world > 1:
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,1167 @@
+// The engine behind the C ABI: one GPU, one shard of rows, the binned
+// matrix resident in HBM, and the per-round pipeline of kernels that grows a
+// tree without returning to the host between levels.
+#include <cuda_runtime.h>
+#include <nccl.h>
+
+#include <algorithm>
+#include <cmath>
+#include <cstdio>
+#include <cstring>
+#include <string>
+#include <vector>
+
+#include "hb_internal.h"
+#include "hb_kernels.cuh"
+
+using namespace hb;
+
+namespace {
+
+template <class T>
+struct DevBuf {
+  T* p = nullptr;
+  size_t n = 0;
+  cudaError_t alloc(size_t count) {
+    if (count <= n && p) return cudaSuccess;
+    if (p) cudaFree(p);
+    p = nullptr;
+    n = 0;
+    if (count == 0) return cudaSuccess;
+    cudaError_t e = cudaMalloc(&p, count * sizeof(T));
+    if (e == cudaSuccess) n = count;
+    return e;
+  }
+  void release() {
+    if (p) cudaFree(p);
+    p = nullptr;
+    n = 0;
+  }
+};
+
+constexpr int kTimers = 8;  // gradients, root hist, scan, apply, partition, hist, subtract, other
+enum Timer { T_GRAD, T_ROOT, T_SCAN, T_APPLY, T_PART, T_HIST, T_SUB, T_OTHER };
+
+}  // namespace
+
+struct hb_engine {
+  int device = 0;
+  cudaStream_t stream = nullptr;
+  int n_sm = 148;
+  bool failed = false;
+  std::string err;
+
+  // the binned matrix
+  bool uploaded = false;
+  DevConst c{};
+  std::vector<uint32_t> h_fo;
+  std::vector<float> h_cuts;
+  DevBuf<uint8_t> rec, col;
+  DevBuf<uint64_t> colmiss;
+  bool has_missing = false;
+  DevBuf<uint32_t> fo;
+  DevBuf<float> cuts;
+
+  // rows
+  DevBuf<float2> gpair;
+  DevBuf<float> margin, label, weight;
+  const float* label_key = nullptr;
+  const float* weight_key = nullptr;
+  bool margins_loaded = false;
+  DevBuf<uint32_t> rows[2];
+  DevBuf<Scale> scale;
+  bool staged = false;
+
+  // tree growth
+  int alloc_depth = -1;
+  DevBuf<longlong2> hist_all;  // [1 totals][slots][total_bins]
+  DevBuf<Front> front[2];
+  DevBuf<Cand> cand;
+  DevBuf<Decision> dec;
+  DevBuf<PItem> items;
+  DevBuf<uint32_t> dirbits, item_left, item_off;
+  DevBuf<HEntry> entries;
+  DevBuf<Triple> pairs;
+  DevBuf<LevelState> ls;
+  DevBuf<hb_tree_node> tree;
+  int max_items = 0;
+  DevBuf<hb_tree_node> forest;
+  DevBuf<uint32_t> counts;
+  DevBuf<int32_t> tree_counter;
+
+  // RowEngine per-call state
+  uint64_t tree_stamp = 0;
+  DevBuf<uint32_t> call_rows;
+  DevBuf<longlong2> call_hist;
+  DevBuf<double> call_out;
+  DevBuf<longlong2> resident;
+  uint32_t resident_slots = 0;
+  DevBuf<long long> seg_total;
+
+  // sharding
+  ncclComm_t comm = nullptr;
+  int nranks = 1, rank = 0;
+  uint64_t row_begin = 0;
+
+  // timing and counters (hb_engine_get_stats)
+  bool timing = false;
+  std::vector<cudaEvent_t> ev;
+  std::vector<int> ev_kind;
+  size_t ev_used = 0;
+  double timer_ms[kTimers] = {0};
+  uint64_t timer_launches[kTimers] = {0};
+  uint64_t kernel_launches = 0;
+  uint64_t rounds_done = 0;
+  DevBuf<unsigned long long> row_stats;  // [contiguous rows built, gathered rows built]
+  bool train_begun = false;
+};
+
+namespace {
+
+thread_local std::string g_last_error;
+
+hb_status fail(hb_engine* e, const char* what, cudaError_t code) {
+  e->failed = true;
+  e->err = std::string(what) + ": " + cudaGetErrorString(code);
+  g_last_error = e->err;
+  return HB_DEVICE_FAILED;
+}
+
+hb_status refuse(hb_engine* e, const std::string& why) {
+  e->err = why;
+  g_last_error = why;
+  return HB_REFUSED;
+}
+
+#define HB_CK(e, call)                             \
+  do {                                             \
+    cudaError_t _c = (call);                       \
+    if (_c != cudaSuccess) return fail(e, #call, _c); \
+  } while (0)
+
+#define HB_NCCL(e, call)                                              \
+  do {                                                                \
+    ncclResult_t _r = (call);                                         \
+    if (_r != ncclSuccess) {                                          \
+      (e)->failed = true;                                             \
+      (e)->err = std::string(#call) + ": " + ncclGetErrorString(_r);  \
+      g_last_error = (e)->err;                                        \
+      return HB_DEVICE_FAILED;                                        \
+    }                                                                 \
+  } while (0)
+
+#define HB_ENTER(e)                                                   \
+  do {                                                                \
+    if (!(e)) return HB_INVALID_ARGUMENT;                             \
+    if ((e)->failed) return HB_REFUSED;                               \
+    cudaError_t _d = cudaSetDevice((e)->device);                      \
+    if (_d != cudaSuccess) return fail((e), "cudaSetDevice", _d);     \
+  } while (0)
+
+// Timing marks (CUDA events on the engine's stream), enabled per train call.
+void mark_begin(hb_engine* e, int kind) {
+  if (!e->timing) return;
+  if (e->ev_used + 2 > e->ev.size()) {
+    for (int i = 0; i < 256; ++i) {
+      cudaEvent_t x;
+      cudaEventCreate(&x);
+      e->ev.push_back(x);
+      e->ev_kind.push_back(0);
+    }
+  }
+  e->ev_kind[e->ev_used] = kind;
+  cudaEventRecord(e->ev[e->ev_used++], e->stream);
+}
+void mark_end(hb_engine* e) {
+  if (!e->timing) return;
+  e->ev_kind[e->ev_used] = -1;
+  cudaEventRecord(e->ev[e->ev_used++], e->stream);
+}
+void collect_timers(hb_engine* e) {
+  if (!e->timing || e->ev_used == 0) return;
+  cudaStreamSynchronize(e->stream);
+  for (size_t i = 0; i + 1 < e->ev_used; i += 2) {
+    float ms = 0.0f;
+    if (cudaEventElapsedTime(&ms, e->ev[i], e->ev[i + 1]) == cudaSuccess) {
+      e->timer_ms[e->ev_kind[i]] += ms;
+      e->timer_launches[e->ev_kind[i]] += 1;
+    }
+  }
+  e->ev_used = 0;
+}
+
+hb_status ensure_growth_buffers(hb_engine* e, int max_depth) {
+  if (e->alloc_depth >= max_depth) return HB_OK;
+  const DevConst& c = e->c;
+  const int max_front = 1 << max_depth;
+  const size_t slots = (size_t(1) << max_depth) - 1;
+  HB_CK(e, e->hist_all.alloc(1 + slots * c.total_bins));
+  HB_CK(e, e->front[0].alloc(max_front));
+  HB_CK(e, e->front[1].alloc(max_front));
+  HB_CK(e, e->cand.alloc((size_t)max_front * c.n_cols));
+  HB_CK(e, e->dec.alloc(max_front));
+  e->max_items = (int)((c.n_rows + kTile - 1) / kTile) + max_front + 1;
+  HB_CK(e, e->items.alloc(e->max_items));
+  HB_CK(e, e->dirbits.alloc((size_t)e->max_items * kTileWords));
+  HB_CK(e, e->item_left.alloc(e->max_items));
+  HB_CK(e, e->item_off.alloc(e->max_items));
+  HB_CK(e, e->entries.alloc(max_front));
+  HB_CK(e, e->pairs.alloc(max_front));
+  HB_CK(e, e->ls.alloc(kMaxDepth + 2));
+  HB_CK(e, e->tree.alloc((size_t)2 * max_front));
+  e->alloc_depth = max_depth;
+  return HB_OK;
+}
+
+// Stage this tree's scale: reduce the maxima over ranks, then the exponents.
+hb_status finish_scale(hb_engine* e) {
+  if (e->comm) {
+    HB_NCCL(e, ncclAllReduce(&e->scale.p->maxg_bits, &e->scale.p->maxg_bits, 3, ncclUint32,
+                             ncclMax, e->comm, e->stream));
+  }
+  launch_scale(e->scale.p, e->c.global_rows, e->stream);
+  HB_CK(e, cudaGetLastError());
+  return HB_OK;
+}
+
+uint64_t vector_rows(hb_engine* e) {
+  const uint64_t g = e->c.global_rows;
+  const uint64_t vg = g >= 16 ? g - g % 8 : 0;
+  if (vg <= e->row_begin) return 0;
+  return std::min<uint64_t>(vg - e->row_begin, e->c.n_rows);
+}
+
+hb_status run_gradients(hb_engine* e, int kind, float spw, float min_hess) {
+  HB_CK(e, cudaMemsetAsync(e->scale.p, 0, sizeof(Scale), e->stream));
+  mark_begin(e, T_GRAD);
+  launch_gradients(kind, e->margin.p, e->label.p, e->weight_key ? e->weight.p : nullptr, spw,
+                   min_hess, e->c.n_rows, vector_rows(e), e->gpair.p, e->scale.p, e->n_sm,
+                   e->stream);
+  mark_end(e);
+  e->kernel_launches += 2;  // gradients + scale
+  HB_CK(e, cudaGetLastError());
+  hb_status st = finish_scale(e);
+  if (st != HB_OK) return st;
+  e->staged = true;
+  return HB_OK;
+}
+
+// Grow one tree on the device from the staged gradients (depthwise). Writes
+// the tree to e->tree and appends it to the forest buffer when `forest`.
+hb_status grow_device(hb_engine* e, const hb_train_params* p, bool to_forest) {
+  DevConst& c = e->c;
+  const int D = p->max_depth;
+  hb_status st = ensure_growth_buffers(e, D);
+  if (st != HB_OK) return st;
+  c.lambda = (double)p->lambda;
+  c.alpha = (double)p->alpha;
+  c.gamma = (double)p->gamma;
+  c.mcw = (double)p->min_child_weight;
+  c.mds = (double)p->max_delta_step;
+  c.eta = p->eta;
+  c.max_depth = D;
+  cudaStream_t s = e->stream;
+  const size_t slots = (size_t(1) << D) - 1;
+  longlong2* hist = e->hist_all.p + 1;
+  long long* totals = reinterpret_cast<long long*>(e->hist_all.p);
+
+  HB_CK(e, cudaMemsetAsync(e->ls.p, 0, sizeof(LevelState) * (kMaxDepth + 2), s));
+  HB_CK(e, cudaMemsetAsync(e->hist_all.p, 0, sizeof(longlong2) * (1 + slots * c.total_bins), s));
+  launch_root_setup(c.n_rows, e->front[0].p, e->entries.p, e->ls.p, s);
+  const size_t smem = hist_smem_bytes(c);
+  const int hgrid = hist_grid(e->n_sm);
+  mark_begin(e, T_ROOT);
+  launch_hist(c, e->fo.p, e->rec.p, e->gpair.p, e->scale.p, nullptr, e->entries.p, e->ls.p, hist,
+              totals, e->row_stats.p, hgrid, smem, s);
+  mark_end(e);
+  HB_CK(e, cudaGetLastError());
+  if (e->comm) {
+    HB_NCCL(e, ncclAllReduce(e->hist_all.p, e->hist_all.p, 2 * (1 + (size_t)c.total_bins), ncclInt64,
+                             ncclSum, e->comm, s));
+  }
+  launch_root_stats(e->front[0].p, totals, s);
+
+  int cur = 0;
+  uint32_t* rows_in = e->rows[0].p;
+  uint32_t* rows_out = e->rows[1].p;
+  for (int d = 0; d <= D; ++d) {
+    const bool leaf_only = d == D;
+    const int max_front = 1 << d;
+    LevelState* lsd = e->ls.p + d;
+    LevelState* lsn = e->ls.p + d + 1;
+    Front* fr = e->front[cur].p;
+    Front* nx = e->front[cur ^ 1].p;
+    if (!leaf_only) {
+      mark_begin(e, T_SCAN);
+      launch_scan(c, e->fo.p, hist, fr, lsd, e->scale.p, max_front, e->cand.p, s);
+      mark_end(e);
+    }
+    mark_begin(e, T_APPLY);
+    launch_apply(c, e->fo.p, e->cuts.p, e->cand.p, fr, nx, e->dec.p, e->items.p, lsd, lsn,
+                 e->tree.p, e->scale.p, d, leaf_only ? 1 : 0, s);
+    mark_end(e);
+    const int max_items = std::min(e->max_items, (int)((c.n_rows + kTile - 1) / kTile) + max_front);
+    mark_begin(e, T_PART);
+    launch_part_count(c, e->col.p, e->has_missing ? e->colmiss.p : nullptr, rows_in, d == 0, fr,
+                      e->dec.p, e->items.p, lsd, max_items, e->dirbits.p, e->item_left.p,
+                      e->margin.p, s);
+    if (!leaf_only) {
+      launch_part_scan(fr, e->dec.p, lsd, max_front, e->item_left.p, e->item_off.p, nx, s);
+      launch_part_scatter(fr, e->dec.p, e->items.p, lsd, max_items, e->dirbits.p, e->item_off.p,
+                          nx, rows_in, d == 0, rows_out, s);
+    }
+    mark_end(e);
+    HB_CK(e, cudaGetLastError());
+    if (leaf_only) break;
+    const bool terminal = d + 1 >= D;
+    if (!terminal) {
+      launch_hist_plan(fr, e->dec.p, lsd, nx, e->entries.p, e->pairs.p, lsn, 0, s);
+      mark_begin(e, T_HIST);
+      launch_hist(c, e->fo.p, e->rec.p, e->gpair.p, e->scale.p, rows_out, e->entries.p, lsn, hist,
+                  nullptr, e->row_stats.p, hgrid, smem, s);
+      mark_end(e);
+      if (e->comm) {
+        const size_t base = (size_t(1) << (d + 1)) - 1, half = size_t(1) << d;
+        HB_NCCL(e, ncclAllReduce(hist + base * c.total_bins, hist + base * c.total_bins,
+                                 2 * half * c.total_bins, ncclInt64, ncclSum, e->comm, s));
+      }
+      mark_begin(e, T_SUB);
+      launch_subtract(e->pairs.p, lsn, max_front, c.total_bins, hist, s);
+      mark_end(e);
+    }
+    HB_CK(e, cudaGetLastError());
+    std::swap(rows_in, rows_out);
+    cur ^= 1;
+  }
+  if (to_forest) {
+    launch_finish_tree(e->tree.p, e->ls.p + D + 1, e->forest.p, e->counts.p, e->tree_counter.p,
+                       (uint32_t)(2u << D), s);
+    HB_CK(e, cudaGetLastError());
+  }
+  // root setup + root hist + root stats; per level below D: scan, apply,
+  // 3 partition passes, and (above the last level) plan, hist, subtract;
+  // the leaf level: apply + partition; the forest copy.
+  e->kernel_launches += 3 + 5 * (uint64_t)D + 3 * (uint64_t)(D > 1 ? D - 1 : 0) + 2 + (to_forest ? 1 : 0);
+  e->rounds_done += 1;
+  return HB_OK;
+}
+
+hb_status check_params(hb_engine* e, const hb_train_params* p) {
+  if (!p) return HB_INVALID_ARGUMENT;
+  if (p->grow_policy != HB_GROW_DEPTHWISE)
+    return refuse(e, "device growth supports grow_policy = depthwise");
+  if (p->max_depth < 1 || p->max_depth > kMaxDepth)
+    return refuse(e, "device growth supports 1 <= max_depth <= 10");
+  if (p->objective != HB_LOSS_SQUARED_ERROR && p->objective != HB_LOSS_LOGISTIC)
+    return HB_INVALID_ARGUMENT;
+  return HB_OK;
+}
+
+}  // namespace
+
+// ===========================================================================
+// C ABI
+extern "C" {
+
+hb_status hb_engine_create(int32_t device_ordinal, hb_engine** out) {
+  if (!out) return HB_INVALID_ARGUMENT;
+  *out = nullptr;
+  int n = 0;
+  cudaError_t ce = cudaGetDeviceCount(&n);
+  if (ce != cudaSuccess || device_ordinal < 0 || device_ordinal >= n) {
+    g_last_error = "no such CUDA device";
+    return HB_REFUSED;
+  }
+  hb_engine* e = new hb_engine();
+  e->device = device_ordinal;
+  if (cudaSetDevice(device_ordinal) != cudaSuccess ||
+      cudaStreamCreateWithFlags(&e->stream, cudaStreamNonBlocking) != cudaSuccess) {
+    delete e;
+    g_last_error = "cannot open the CUDA device";
+    return HB_DEVICE_FAILED;
+  }
+  cudaDeviceGetAttribute(&e->n_sm, cudaDevAttrMultiProcessorCount, device_ordinal);
+  if (e->scale.alloc(1) != cudaSuccess || e->tree_counter.alloc(1) != cudaSuccess ||
+      e->seg_total.alloc(2) != cudaSuccess || e->row_stats.alloc(2) != cudaSuccess ||
+      cudaMemset(e->row_stats.p, 0, 16) != cudaSuccess) {
+    delete e;
+    return HB_DEVICE_FAILED;
+  }
+  *out = e;
+  return HB_OK;
+}
+
+hb_status hb_engine_destroy(hb_engine* e) {
+  if (!e) return HB_INVALID_ARGUMENT;
+  cudaSetDevice(e->device);
+  if (e->stream) cudaStreamSynchronize(e->stream);
+  if (e->comm) ncclCommDestroy(e->comm);
+  for (auto x : e->ev) cudaEventDestroy(x);
+  e->rec.release();
+  e->col.release();
+  e->colmiss.release();
+  e->fo.release();
+  e->cuts.release();
+  e->gpair.release();
+  e->margin.release();
+  e->label.release();
+  e->weight.release();
+  e->rows[0].release();
+  e->rows[1].release();
+  e->scale.release();
+  e->hist_all.release();
+  e->front[0].release();
+  e->front[1].release();
+  e->cand.release();
+  e->dec.release();
+  e->items.release();
+  e->dirbits.release();
+  e->item_left.release();
+  e->item_off.release();
+  e->entries.release();
+  e->pairs.release();
+  e->ls.release();
+  e->tree.release();
+  e->forest.release();
+  e->counts.release();
+  e->tree_counter.release();
+  e->call_rows.release();
+  e->call_hist.release();
+  e->call_out.release();
+  e->resident.release();
+  e->seg_total.release();
+  e->row_stats.release();
+  if (e->stream) cudaStreamDestroy(e->stream);
+  delete e;
+  return HB_OK;
+}
+
+const char* hb_engine_last_error(const hb_engine* e) {
+  return e ? e->err.c_str() : g_last_error.c_str();
+}
+
+hb_status hb_engine_upload(hb_engine* e, const hb_ghist* g) {
+  HB_ENTER(e);
+  if (!g || !g->feature_offset || !g->cut_values || !g->columns || g->n_rows == 0 ||
+      g->n_cols == 0)
+    return HB_INVALID_ARGUMENT;
+  if (g->n_rows >= (1ull << 32)) return refuse(e, "at most 2^32 - 1 rows per device");
+  if (g->n_cols > 224) return refuse(e, "at most 224 features per device index");
+  DevConst& c = e->c;
+  const uint64_t shard_rows = c.global_rows;
+  c = DevConst{};
+  c.n_rows = g->n_rows;
+  c.global_rows = shard_rows > g->n_rows ? shard_rows : g->n_rows;
+  c.n_cols = g->n_cols;
+  e->h_fo.assign(g->feature_offset, g->feature_offset + g->n_cols + 1);
+  c.total_bins = e->h_fo.back();
+  uint32_t widest = 0;
+  for (uint32_t f = 0; f < g->n_cols; ++f) widest = std::max(widest, e->h_fo[f + 1] - e->h_fo[f]);
+  if (widest > 256) return refuse(e, "features of more than 256 bins need 16-bit bins");
+  c.max_bins = widest;
+  c.mask_off = (g->n_cols + 3) / 4 * 4;
+  c.stride = (c.mask_off + 4 * ((g->n_cols + 31) / 32) + 15) / 16 * 16;
+  c.dense = g->dense ? 1 : 0;
+  c.n_groups = (g->n_cols + kGroupFeatures - 1) / kGroupFeatures;
+  e->h_cuts.assign(g->cut_values, g->cut_values + c.total_bins);
+  e->has_missing = g->missing != nullptr;
+
+  const uint64_t n = c.n_rows, words = (n + 63) / 64;
+  HB_CK(e, e->fo.alloc(c.n_cols + 1));
+  HB_CK(e, e->cuts.alloc(c.total_bins));
+  HB_CK(e, e->col.alloc((size_t)c.n_cols * n));
+  HB_CK(e, e->rec.alloc((size_t)c.stride * n + 64));
+  if (e->has_missing) HB_CK(e, e->colmiss.alloc((size_t)c.n_cols * words));
+  HB_CK(e, e->gpair.alloc(n));
+  HB_CK(e, e->margin.alloc(n));
+  HB_CK(e, e->label.alloc(n));
+  HB_CK(e, e->rows[0].alloc(n));
+  HB_CK(e, e->rows[1].alloc(n));
+  cudaStream_t s = e->stream;
+  HB_CK(e, cudaMemcpyAsync(e->fo.p, e->h_fo.data(), 4 * (c.n_cols + 1), cudaMemcpyHostToDevice, s));
+  HB_CK(e, cudaMemcpyAsync(e->cuts.p, e->h_cuts.data(), 4 * c.total_bins, cudaMemcpyHostToDevice, s));
+  HB_CK(e, cudaMemcpyAsync(e->col.p, g->columns, (size_t)c.n_cols * n, cudaMemcpyHostToDevice, s));
+  if (e->has_missing)
+    HB_CK(e, cudaMemcpyAsync(e->colmiss.p, g->missing, 8 * (size_t)c.n_cols * words,
+                             cudaMemcpyHostToDevice, s));
+  HB_CK(e, cudaMemsetAsync(e->rec.p, 0, (size_t)c.stride * n + 64, s));
+  launch_encode(e->col.p, e->has_missing ? e->colmiss.p : nullptr, n, c.n_cols, c.stride,
+                c.mask_off, e->rec.p, s);
+  HB_CK(e, cudaGetLastError());
+  HB_CK(e, cudaStreamSynchronize(s));
+  e->uploaded = true;
+  e->alloc_depth = -1;
+  e->label_key = e->weight_key = nullptr;
+  e->margins_loaded = false;
+  e->staged = false;
+  return HB_OK;
+}
+
+// ---- HistogramBackend ------------------------------------------------------
+hb_status hb_prepare(hb_engine* e, const hb_grad_pair* gpair, uint64_t n) {
+  HB_ENTER(e);
+  if (!e->uploaded) return refuse(e, "no index uploaded");
+  if (!gpair || n != e->c.n_rows) return HB_INVALID_ARGUMENT;
+  cudaStream_t s = e->stream;
+  HB_CK(e, cudaMemcpyAsync(e->gpair.p, gpair, 8 * n, cudaMemcpyHostToDevice, s));
+  HB_CK(e, cudaMemsetAsync(e->scale.p, 0, sizeof(Scale), s));
+  launch_pair_maxima(e->gpair.p, n, e->scale.p, e->n_sm, s);
+  HB_CK(e, cudaGetLastError());
+  hb_status st = finish_scale(e);
+  if (st != HB_OK) return st;
+  Scale h;
+  HB_CK(e, cudaMemcpyAsync(&h, e->scale.p, sizeof(Scale), cudaMemcpyDeviceToHost, s));
+  HB_CK(e, cudaStreamSynchronize(s));
+  if (h.nonfinite) {
+    e->staged = false;
+    return refuse(e, "non-finite gradients");
+  }
+  e->staged = true;
+  return HB_OK;
+}
+
+// Histograms of `n` row lists already on the device (call_rows, entries
+// back to back) into call_hist slots 0..n-1, dequantised into `out`.
+static hb_status build_entries(hb_engine* e, const std::vector<HEntry>& en, longlong2* dst,
+                               uint32_t n_slots_to_zero, const uint32_t* rows_dev) {
+  DevConst& c = e->c;
+  cudaStream_t s = e->stream;
+  HB_CK(e, e->entries.alloc(std::max<size_t>(en.size(), 1)));
+  HB_CK(e, e->ls.alloc(kMaxDepth + 2));
+  LevelState lsh{};
+  lsh.n_hentries = (int32_t)en.size();
+  uint64_t total = 0;
+  for (const auto& x : en) total += x.len;
+  lsh.hist_rows = total;
+  HB_CK(e, cudaMemcpyAsync(e->entries.p, en.data(), sizeof(HEntry) * en.size(), cudaMemcpyHostToDevice, s));
+  HB_CK(e, cudaMemcpyAsync(e->ls.p, &lsh, sizeof(LevelState), cudaMemcpyHostToDevice, s));
+  if (n_slots_to_zero)
+    HB_CK(e, cudaMemsetAsync(dst, 0, sizeof(longlong2) * (size_t)n_slots_to_zero * c.total_bins, s));
+  launch_hist(c, e->fo.p, e->rec.p, e->gpair.p, e->scale.p, rows_dev, e->entries.p, e->ls.p, dst,
+              nullptr, nullptr, hist_grid(e->n_sm), hist_smem_bytes(c), s);
+  HB_CK(e, cudaGetLastError());
+  return HB_OK;
+}
+
+static hb_status download_hist(hb_engine* e, const longlong2* src, uint32_t n_hists,
+                               hb_grad_stats* out) {
+  const size_t bins = (size_t)n_hists * e->c.total_bins;
+  HB_CK(e, e->call_out.alloc(2 * bins));
+  launch_dequantize(src, (uint32_t)bins, e->scale.p, e->call_out.p, e->stream);
+  HB_CK(e, cudaGetLastError());
+  HB_CK(e, cudaMemcpyAsync(out, e->call_out.p, 16 * bins, cudaMemcpyDeviceToHost, e->stream));
+  HB_CK(e, cudaStreamSynchronize(e->stream));
+  return HB_OK;
+}
+
+hb_status hb_build(hb_engine* e, const uint32_t* rows, uint64_t n, hb_grad_stats* out) {
+  HB_ENTER(e);
+  if (!e->uploaded || !e->staged) return refuse(e, "no staged gradients");
+  if ((!rows && n) || !out) return HB_INVALID_ARGUMENT;
+  for (uint64_t i = 0; i < n; ++i)
+    if (rows[i] >= e->c.n_rows || (i && rows[i] <= rows[i - 1])) return refuse(e, "rows must ascend within the index");
+  HB_CK(e, e->call_rows.alloc(std::max<uint64_t>(n, 1)));
+  HB_CK(e, e->call_hist.alloc(e->c.total_bins));
+  if (n) HB_CK(e, cudaMemcpyAsync(e->call_rows.p, rows, 4 * n, cudaMemcpyHostToDevice, e->stream));
+  std::vector<HEntry> en(1);
+  en[0].slot = 0;
+  en[0].identity = 0;
+  en[0].begin = 0;
+  en[0].len = (uint32_t)n;
+  en[0].prefix = 0;
+  hb_status st = build_entries(e, en, e->call_hist.p, 1, e->call_rows.p);
+  if (st != HB_OK) return st;
+  return download_hist(e, e->call_hist.p, 1, out);
+}
+
+hb_status hb_build_features(hb_engine* e, const uint32_t* rows, uint64_t n,
+                            const uint32_t* features, uint32_t n_features, hb_grad_stats* out) {
+  (void)features;
+  (void)n_features;
+  return hb_build(e, rows, n, out);
+}
+
+// ---- RowEngine ----------------------------------------------------------
+static bool seg_ok(const hb_engine* e, const hb_segment* s) {
+  return s && s->tree == e->tree_stamp && s->offset + s->len <= e->c.n_rows;
+}
+
+hb_status hb_begin_tree(hb_engine* e, const uint32_t* rows, uint64_t n, hb_segment* root) {
+  HB_ENTER(e);
+  if (!e->uploaded) return refuse(e, "no index uploaded");
+  if ((!rows && n) || !root || n > e->c.n_rows) return HB_INVALID_ARGUMENT;
+  for (uint64_t i = 0; i < n; ++i)
+    if (rows[i] >= e->c.n_rows || (i && rows[i] <= rows[i - 1])) return refuse(e, "rows must be ascending and distinct");
+  if (n) HB_CK(e, cudaMemcpyAsync(e->rows[0].p, rows, 4 * n, cudaMemcpyHostToDevice, e->stream));
+  HB_CK(e, cudaStreamSynchronize(e->stream));
+  ++e->tree_stamp;
+  root->offset = 0;
+  root->len = n;
+  root->contiguous = (n == 0 || (uint64_t)(rows[n - 1] - rows[0]) + 1 == n) ? 1 : 0;
+  root->reserved = 0;
+  root->tree = e->tree_stamp;
+  return HB_OK;
+}
+
+hb_status hb_histograms(hb_engine* e, const hb_segment* segs, uint32_t n, hb_grad_stats* out) {
+  HB_ENTER(e);
+  if (!e->uploaded || !e->staged) return refuse(e, "no staged gradients");
+  if ((!segs && n) || (!out && n)) return HB_INVALID_ARGUMENT;
+  std::vector<HEntry> en;
+  uint64_t prefix = 0;
+  for (uint32_t k = 0; k < n; ++k) {
+    if (!seg_ok(e, &segs[k])) return refuse(e, "stale or foreign segment");
+    HEntry x{};
+    x.slot = (int32_t)k;
+    x.identity = 0;
+    x.begin = (uint32_t)segs[k].offset;
+    x.len = (uint32_t)segs[k].len;
+    x.prefix = prefix;
+    prefix += x.len;
+    en.push_back(x);
+  }
+  if (!n) return HB_OK;
+  HB_CK(e, e->call_hist.alloc((size_t)n * e->c.total_bins));
+  hb_status st = build_entries(e, en, e->call_hist.p, n, e->rows[0].p);
+  if (st != HB_OK) return st;
+  return download_hist(e, e->call_hist.p, n, out);
+}
+
+hb_status hb_root_total(hb_engine* e, const hb_segment* seg, hb_grad_stats* out) {
+  HB_ENTER(e);
+  if (!e->uploaded || !e->staged) return refuse(e, "no staged gradients");
+  if (!seg_ok(e, seg) || !out) return HB_INVALID_ARGUMENT;
+  // The total is any feature's bins plus that feature's missing rows; the
+  // histogram kernel's totals path sums every row exactly.
+  std::vector<HEntry> en(1);
+  en[0].slot = 0;
+  en[0].identity = 0;
+  en[0].begin = (uint32_t)seg->offset;
+  en[0].len = (uint32_t)seg->len;
+  en[0].prefix = 0;
+  DevConst& c = e->c;
+  HB_CK(e, e->call_hist.alloc(c.total_bins));
+  HB_CK(e, e->entries.alloc(1));
+  HB_CK(e, e->ls.alloc(kMaxDepth + 2));
+  LevelState lsh{};
+  lsh.n_hentries = 1;
+  lsh.hist_rows = seg->len;
+  cudaStream_t s = e->stream;
+  HB_CK(e, cudaMemcpyAsync(e->entries.p, en.data(), sizeof(HEntry), cudaMemcpyHostToDevice, s));
+  HB_CK(e, cudaMemcpyAsync(e->ls.p, &lsh, sizeof(LevelState), cudaMemcpyHostToDevice, s));
+  HB_CK(e, cudaMemsetAsync(e->call_hist.p, 0, sizeof(longlong2) * c.total_bins, s));
+  HB_CK(e, cudaMemsetAsync(e->seg_total.p, 0, 16, s));
+  launch_hist(c, e->fo.p, e->rec.p, e->gpair.p, e->scale.p, e->rows[0].p, e->entries.p, e->ls.p,
+              e->call_hist.p, e->seg_total.p, nullptr, hist_grid(e->n_sm), hist_smem_bytes(c), s);
+  HB_CK(e, cudaGetLastError());
+  long long t[2];
+  Scale h;
+  HB_CK(e, cudaMemcpyAsync(t, e->seg_total.p, 16, cudaMemcpyDeviceToHost, s));
+  HB_CK(e, cudaMemcpyAsync(&h, e->scale.p, sizeof(Scale), cudaMemcpyDeviceToHost, s));
+  HB_CK(e, cudaStreamSynchronize(s));
+  out->grad = (double)t[0] * std::ldexp(1.0, -h.sg);
+  out->hess = (double)t[1] * std::ldexp(1.0, -h.sh);
+  return HB_OK;
+}
+
+hb_status hb_partition(hb_engine* e, const hb_row_split* splits, uint32_t n, hb_partitioned* out) {
+  HB_ENTER(e);
+  if (!e->uploaded) return refuse(e, "no index uploaded");
+  if ((!splits || !out) && n) return HB_INVALID_ARGUMENT;
+  if (!n) return HB_OK;
+  hb_status st = ensure_growth_buffers(e, 1);
+  if (st != HB_OK) return st;
+  DevConst& c = e->c;
+  std::vector<Front> fr(n);
+  std::vector<Decision> dc(n);
+  std::vector<PItem> it;
+  for (uint32_t k = 0; k < n; ++k) {
+    const hb_row_split& sp = splits[k];
+    if (!seg_ok(e, &sp.seg)) return refuse(e, "stale or foreign segment");
+    if (sp.feature >= c.n_cols) return HB_INVALID_ARGUMENT;
+    for (uint32_t j = 0; j < k; ++j) {
+      const hb_segment& o = splits[j].seg;
+      if (sp.seg.offset < o.offset + o.len && o.offset < sp.seg.offset + sp.seg.len)
+        return refuse(e, "overlapping segments");
+    }
+    fr[k].begin = (uint32_t)sp.seg.offset;
+    fr[k].len = (uint32_t)sp.seg.len;
+    dc[k].split = 1;
+    dc[k].pair = (int32_t)k;
+    dc[k].feature = sp.feature;
+    dc[k].limit = sp.limit;
+    dc[k].default_left = sp.default_left ? 1 : 0;
+    dc[k].item_begin = (int32_t)it.size();
+    uint32_t tiles = (fr[k].len + kTile - 1) / kTile;
+    dc[k].item_count = (int32_t)tiles;
+    for (uint32_t t = 0; t < tiles; ++t) {
+      PItem p{};
+      p.k = (int32_t)k;
+      p.kind = 1;
+      p.off = t * kTile;
+      p.len = std::min<uint32_t>(kTile, fr[k].len - t * kTile);
+      it.push_back(p);
+    }
+  }
+  const int n_items = (int)it.size();
+  HB_CK(e, e->front[0].alloc(n));
+  HB_CK(e, e->front[1].alloc(2 * (size_t)n));
+  HB_CK(e, e->dec.alloc(n));
+  HB_CK(e, e->items.alloc(std::max(n_items, 1)));
+  HB_CK(e, e->dirbits.alloc((size_t)std::max(n_items, 1) * kTileWords));
+  HB_CK(e, e->item_left.alloc(std::max(n_items, 1)));
+  HB_CK(e, e->item_off.alloc(std::max(n_items, 1)));
+  e->alloc_depth = -1;  // the growth buffers were resized for this call
+  LevelState lsh{};
+  lsh.n_front = (int32_t)n;
+  lsh.n_items = n_items;
+  cudaStream_t s = e->stream;
+  HB_CK(e, cudaMemcpyAsync(e->front[0].p, fr.data(), sizeof(Front) * n, cudaMemcpyHostToDevice, s));
+  HB_CK(e, cudaMemcpyAsync(e->dec.p, dc.data(), sizeof(Decision) * n, cudaMemcpyHostToDevice, s));
+  if (n_items)
+    HB_CK(e, cudaMemcpyAsync(e->items.p, it.data(), sizeof(PItem) * n_items, cudaMemcpyHostToDevice, s));
+  HB_CK(e, cudaMemcpyAsync(e->ls.p, &lsh, sizeof(LevelState), cudaMemcpyHostToDevice, s));
+  if (n_items) {
+    launch_part_count(c, e->col.p, e->has_missing ? e->colmiss.p : nullptr, e->rows[0].p, 0,
+                      e->front[0].p, e->dec.p, e->items.p, e->ls.p, n_items, e->dirbits.p,
+                      e->item_left.p, e->margin.p, s);
+  }
+  launch_part_scan(e->front[0].p, e->dec.p, e->ls.p, (int)n, e->item_left.p, e->item_off.p,
+                   e->front[1].p, s);
+  if (n_items) {
+    launch_part_scatter(e->front[0].p, e->dec.p, e->items.p, e->ls.p, n_items, e->dirbits.p,
+                        e->item_off.p, e->front[1].p, e->rows[0].p, 0, e->rows[1].p, s);
+  }
+  HB_CK(e, cudaGetLastError());
+  for (uint32_t k = 0; k < n; ++k) {
+    if (fr[k].len)
+      HB_CK(e, cudaMemcpyAsync(e->rows[0].p + fr[k].begin, e->rows[1].p + fr[k].begin, 4ull * fr[k].len,
+                               cudaMemcpyDeviceToDevice, s));
+  }
+  std::vector<Front> nx(2 * (size_t)n);
+  HB_CK(e, cudaMemcpyAsync(nx.data(), e->front[1].p, sizeof(Front) * 2 * n, cudaMemcpyDeviceToHost, s));
+  HB_CK(e, cudaStreamSynchronize(s));
+  for (uint32_t k = 0; k < n; ++k) {
+    for (int side = 0; side < 2; ++side) {
+      const Front& f = nx[2 * k + side];
+      hb_segment& sg = side ? out[k].right : out[k].left;
+      sg.offset = f.begin;
+      sg.len = f.len;
+      sg.tree = e->tree_stamp;
+      sg.reserved = 0;
+      sg.contiguous = 0;
+      if (f.len) {
+        uint32_t ends[2];
+        HB_CK(e, cudaMemcpy(&ends[0], e->rows[0].p + f.begin, 4, cudaMemcpyDeviceToHost));
+        HB_CK(e, cudaMemcpy(&ends[1], e->rows[0].p + f.begin + f.len - 1, 4, cudaMemcpyDeviceToHost));
+        sg.contiguous = (uint64_t)(ends[1] - ends[0]) + 1 == f.len ? 1 : 0;
+      } else {
+        sg.contiguous = 1;
+      }
+    }
+  }
+  return HB_OK;
+}
+
+hb_status hb_rows(hb_engine* e, const hb_segment* segs, uint32_t n, uint32_t* out) {
+  HB_ENTER(e);
+  uint64_t at = 0;
+  for (uint32_t k = 0; k < n; ++k) {
+    if (!seg_ok(e, &segs[k])) return refuse(e, "stale or foreign segment");
+    if (segs[k].len)
+      HB_CK(e, cudaMemcpyAsync(out + at, e->rows[0].p + segs[k].offset, 4 * segs[k].len,
+                               cudaMemcpyDeviceToHost, e->stream));
+    at += segs[k].len;
+  }
+  HB_CK(e, cudaStreamSynchronize(e->stream));
+  return HB_OK;
+}
+
+hb_status hb_load_margins(hb_engine* e, const float* margins, uint64_t n) {
+  HB_ENTER(e);
+  if (!e->uploaded) return refuse(e, "no index uploaded");
+  if (!margins || n != e->c.n_rows) return HB_INVALID_ARGUMENT;
+  HB_CK(e, cudaMemcpyAsync(e->margin.p, margins, 4 * n, cudaMemcpyHostToDevice, e->stream));
+  HB_CK(e, cudaStreamSynchronize(e->stream));
+  e->margins_loaded = true;
+  e->label_key = e->weight_key = nullptr;
+  return HB_OK;
+}
+
+hb_status hb_read_margins(hb_engine* e, float* out, uint64_t n) {
+  HB_ENTER(e);
+  if (!e->margins_loaded) return refuse(e, "no margin run");
+  if (!out || n != e->c.n_rows) return HB_INVALID_ARGUMENT;
+  HB_CK(e, cudaMemcpyAsync(out, e->margin.p, 4 * n, cudaMemcpyDeviceToHost, e->stream));
+  HB_CK(e, cudaStreamSynchronize(e->stream));
+  return HB_OK;
+}
+
+static hb_status stage_labels(hb_engine* e, const float* labels, const float* weights, uint64_t n) {
+  cudaStream_t s = e->stream;
+  if (e->label_key != labels) {
+    HB_CK(e, cudaMemcpyAsync(e->label.p, labels, 4 * n, cudaMemcpyHostToDevice, s));
+    e->label_key = labels;
+  }
+  if (weights && e->weight_key != weights) {
+    HB_CK(e, e->weight.alloc(n));
+    HB_CK(e, cudaMemcpyAsync(e->weight.p, weights, 4 * n, cudaMemcpyHostToDevice, s));
+  }
+  e->weight_key = weights;
+  return HB_OK;
+}
+
+hb_status hb_gradients(hb_engine* e, const hb_device_loss* loss, const float* labels,
+                       const float* weights, uint64_t n, int32_t* all_finite) {
+  HB_ENTER(e);
+  if (!e->uploaded || !e->margins_loaded) return refuse(e, "no margin run");
+  if (!loss || !labels || n != e->c.n_rows || !all_finite) return HB_INVALID_ARGUMENT;
+  if (loss->kind != HB_LOSS_SQUARED_ERROR && loss->kind != HB_LOSS_LOGISTIC) return HB_INVALID_ARGUMENT;
+  if (e->row_begin % 8) return refuse(e, "shards must start on a multiple of 8 rows");
+  hb_status st = stage_labels(e, labels, weights, n);
+  if (st != HB_OK) return st;
+  st = run_gradients(e, loss->kind, loss->scale_pos_weight, loss->min_hess);
+  if (st != HB_OK) return st;
+  Scale h;
+  HB_CK(e, cudaMemcpyAsync(&h, e->scale.p, sizeof(Scale), cudaMemcpyDeviceToHost, e->stream));
+  HB_CK(e, cudaStreamSynchronize(e->stream));
+  *all_finite = h.nonfinite ? 0 : 1;
+  if (h.nonfinite) e->staged = false;
+  return HB_OK;
+}
+
+hb_status hb_add_leaf_values(hb_engine* e, const hb_segment* segs, const float* values, uint32_t n) {
+  HB_ENTER(e);
+  if (!e->margins_loaded) return refuse(e, "no margin run");
+  for (uint32_t k = 0; k < n; ++k)
+    if (!seg_ok(e, &segs[k])) return refuse(e, "stale or foreign segment");
+  for (uint32_t k = 0; k < n; ++k) {
+    if (segs[k].len)
+      launch_add_segment(e->rows[0].p, (uint32_t)segs[k].offset, (uint32_t)segs[k].len, values[k],
+                         e->margin.p, e->stream);
+  }
+  HB_CK(e, cudaGetLastError());
+  HB_CK(e, cudaStreamSynchronize(e->stream));
+  return HB_OK;
+}
+
+hb_status hb_reserve_hists(hb_engine* e, uint32_t slots, int32_t* reserved) {
+  HB_ENTER(e);
+  if (!e->uploaded || !reserved) return HB_INVALID_ARGUMENT;
+  size_t free_b = 0, total_b = 0;
+  cudaMemGetInfo(&free_b, &total_b);
+  const size_t need = (size_t)slots * e->c.total_bins * sizeof(longlong2);
+  if (need > free_b / 2) {
+    *reserved = 0;
+    return HB_OK;
+  }
+  HB_CK(e, e->resident.alloc(std::max<size_t>((size_t)slots * e->c.total_bins, 1)));
+  e->resident_slots = slots;
+  *reserved = 1;
+  return HB_OK;
+}
+
+hb_status hb_build_resident(hb_engine* e, const hb_segment* segs, const uint32_t* slots, uint32_t n,
+                            const uint32_t* siblings, uint32_t n_siblings) {
+  HB_ENTER(e);
+  if (!e->uploaded || !e->staged) return refuse(e, "no staged gradients");
+  std::vector<HEntry> en;
+  uint64_t prefix = 0;
+  for (uint32_t k = 0; k < n; ++k) {
+    if (!seg_ok(e, &segs[k])) return refuse(e, "stale or foreign segment");
+    if (slots[k] >= e->resident_slots) return refuse(e, "slot not reserved");
+    HEntry x{};
+    x.slot = (int32_t)slots[k];
+    x.begin = (uint32_t)segs[k].offset;
+    x.len = (uint32_t)segs[k].len;
+    x.prefix = prefix;
+    prefix += x.len;
+    en.push_back(x);
+  }
+  cudaStream_t s = e->stream;
+  const uint32_t tb = e->c.total_bins;
+  for (uint32_t k = 0; k < n; ++k)
+    HB_CK(e, cudaMemsetAsync(e->resident.p + (size_t)slots[k] * tb, 0, sizeof(longlong2) * tb, s));
+  if (n) {
+    hb_status st = build_entries(e, en, e->resident.p, 0, e->rows[0].p);
+    if (st != HB_OK) return st;
+  }
+  if (n_siblings) {
+    std::vector<Triple> tr(n_siblings);
+    for (uint32_t j = 0; j < n_siblings; ++j) {
+      uint32_t parent = siblings[2 * j], built = siblings[2 * j + 1];
+      if (parent >= e->resident_slots || built >= e->resident_slots) return refuse(e, "slot not reserved");
+      tr[j].parent = (int32_t)parent;
+      tr[j].built = (int32_t)built;
+      tr[j].sibling = (int32_t)parent;
+    }
+    HB_CK(e, e->pairs.alloc(n_siblings));
+    e->alloc_depth = std::min(e->alloc_depth, 0);
+    LevelState lsh{};
+    lsh.n_pairs = (int32_t)n_siblings;
+    HB_CK(e, cudaMemcpyAsync(e->pairs.p, tr.data(), sizeof(Triple) * n_siblings, cudaMemcpyHostToDevice, s));
+    HB_CK(e, cudaMemcpyAsync(e->ls.p, &lsh, sizeof(LevelState), cudaMemcpyHostToDevice, s));
+    launch_subtract(e->pairs.p, e->ls.p, (int)n_siblings, tb, e->resident.p, s);
+  }
+  HB_CK(e, cudaGetLastError());
+  HB_CK(e, cudaStreamSynchronize(s));
+  return HB_OK;
+}
+
+hb_status hb_scan_resident(hb_engine* e, const hb_reg_params* reg, const hb_scan_request* req,
+                           uint32_t n, hb_node_scan* out) {
+  HB_ENTER(e);
+  if (!e->uploaded || !e->staged) return refuse(e, "no staged gradients");
+  if (!reg || ((!req || !out) && n)) return HB_INVALID_ARGUMENT;
+  if (!n) return HB_OK;
+  DevConst c = e->c;
+  c.lambda = reg->lambda;
+  c.alpha = reg->alpha;
+  c.mds = reg->max_delta_step;
+  c.mcw = reg->min_child_weight;
+  cudaStream_t s = e->stream;
+  Scale h;
+  HB_CK(e, cudaMemcpyAsync(&h, e->scale.p, sizeof(Scale), cudaMemcpyDeviceToHost, s));
+  HB_CK(e, cudaStreamSynchronize(s));
+  std::vector<Front> fr(n);
+  for (uint32_t k = 0; k < n; ++k) {
+    if (req[k].slot >= e->resident_slots) return refuse(e, "slot not reserved");
+    fr[k].slot = (int32_t)req[k].slot;
+    fr[k].g = std::llrint(std::ldexp(req[k].total.grad, h.sg));
+    fr[k].h = std::llrint(std::ldexp(req[k].total.hess, h.sh));
+  }
+  HB_CK(e, e->front[0].alloc(n));
+  HB_CK(e, e->cand.alloc((size_t)n * c.n_cols));
+  e->alloc_depth = -1;
+  LevelState lsh{};
+  lsh.n_front = (int32_t)n;
+  HB_CK(e, cudaMemcpyAsync(e->front[0].p, fr.data(), sizeof(Front) * n, cudaMemcpyHostToDevice, s));
+  HB_CK(e, cudaMemcpyAsync(e->ls.p, &lsh, sizeof(LevelState), cudaMemcpyHostToDevice, s));
+  launch_scan(c, e->fo.p, e->resident.p, e->front[0].p, e->ls.p, e->scale.p, (int)n, e->cand.p, s);
+  HB_CK(e, cudaGetLastError());
+  std::vector<Cand> cd((size_t)n * c.n_cols);
+  HB_CK(e, cudaMemcpyAsync(cd.data(), e->cand.p, sizeof(Cand) * cd.size(), cudaMemcpyDeviceToHost, s));
+  HB_CK(e, cudaStreamSynchronize(s));
+  const double ig = std::ldexp(1.0, -h.sg), ih = std::ldexp(1.0, -h.sh);
+  for (uint32_t k = 0; k < n; ++k) {
+    float best = 0.0f;
+    int best_f = -1;
+    for (uint32_t j = 0; j < req[k].n_features; ++j) {
+      const uint32_t f = req[k].features[j];
+      if (f >= c.n_cols) return HB_INVALID_ARGUMENT;
+      const Cand& x = cd[(size_t)k * c.n_cols + f];
+      if (x.loss > best) {
+        best = x.loss;
+        best_f = (int)f;
+      }
+    }
+    hb_node_scan& o = out[k];
+    std::memset(&o, 0, sizeof(o));
+    if (best_f < 0) {
+      o.kind = HB_SCAN_EMPTY;
+      continue;
+    }
+    const Cand& x = cd[(size_t)k * c.n_cols + best_f];
+    const uint32_t fs = e->h_fo[best_f];
+    o.kind = HB_SCAN_NUMERIC;
+    o.feature = (uint32_t)best_f;
+    o.loss_chg = x.loss;
+    o.backward = x.default_left ? 1 : 0;
+    if (!x.default_left) {
+      o.offset = (uint32_t)(x.bin - (int)fs);
+      o.acc.grad = (double)x.lg * ig;
+      o.acc.hess = (double)x.lh * ih;
+    } else {
+      o.offset = x.bin < 0 ? 0 : (uint32_t)(x.bin - (int)fs + 1);
+      o.acc.grad = (double)(fr[k].g - x.lg) * ig;
+      o.acc.hess = (double)(fr[k].h - x.lh) * ih;
+    }
+  }
+  return HB_OK;
+}
+
+hb_status hb_read_hist(hb_engine* e, uint32_t slot, hb_grad_stats* out) {
+  HB_ENTER(e);
+  if (slot >= e->resident_slots || !out) return HB_INVALID_ARGUMENT;
+  return download_hist(e, e->resident.p + (size_t)slot * e->c.total_bins, 1, out);
+}
+
+hb_status hb_read_gradients(hb_engine* e, hb_grad_pair* out, uint64_t n, int32_t* sg, int32_t* sh) {
+  HB_ENTER(e);
+  if (!e->uploaded || !e->staged) return refuse(e, "no staged gradients");
+  if (!out || n != e->c.n_rows || !sg || !sh) return HB_INVALID_ARGUMENT;
+  Scale h;
+  HB_CK(e, cudaMemcpyAsync(out, e->gpair.p, 8 * n, cudaMemcpyDeviceToHost, e->stream));
+  HB_CK(e, cudaMemcpyAsync(&h, e->scale.p, sizeof(Scale), cudaMemcpyDeviceToHost, e->stream));
+  HB_CK(e, cudaStreamSynchronize(e->stream));
+  *sg = h.sg;
+  *sh = h.sh;
+  return HB_OK;
+}
+
+// ---- whole-tree growth -------------------------------------------------------
+hb_status hb_grow_tree(hb_engine* e, const hb_train_params* p, hb_tree_node* nodes,
+                       uint32_t nodes_cap, uint32_t* n_nodes) {
+  HB_ENTER(e);
+  hb_status st = check_params(e, p);
+  if (st != HB_OK) return st;
+  if (!e->uploaded || !e->staged || !e->margins_loaded) return refuse(e, "no staged gradients or margins");
+  if (!nodes || !n_nodes) return HB_INVALID_ARGUMENT;
+  st = grow_device(e, p, false);
+  if (st != HB_OK) return st;
+  LevelState last;
+  HB_CK(e, cudaMemcpyAsync(&last, e->ls.p + p->max_depth + 1, sizeof(LevelState), cudaMemcpyDeviceToHost, e->stream));
+  HB_CK(e, cudaStreamSynchronize(e->stream));
+  if ((uint32_t)last.n_nodes > nodes_cap) return refuse(e, "nodes_cap too small");
+  HB_CK(e, cudaMemcpyAsync(nodes, e->tree.p, sizeof(hb_tree_node) * last.n_nodes, cudaMemcpyDeviceToHost, e->stream));
+  HB_CK(e, cudaStreamSynchronize(e->stream));
+  *n_nodes = (uint32_t)last.n_nodes;
+  e->staged = false;
+  return HB_OK;
+}
+
+hb_status hb_train_begin(hb_engine* e, const float* labels, uint64_t n, float base_margin) {
+  HB_ENTER(e);
+  if (!e->uploaded) return refuse(e, "no index uploaded");
+  if (!labels || n != e->c.n_rows) return HB_INVALID_ARGUMENT;
+  if (e->row_begin % 8) return refuse(e, "shards must start on a multiple of 8 rows");
+  cudaStream_t s = e->stream;
+  {
+    std::vector<float> m(n, base_margin);
+    HB_CK(e, cudaMemcpyAsync(e->margin.p, m.data(), 4 * n, cudaMemcpyHostToDevice, s));
+    HB_CK(e, cudaStreamSynchronize(s));
+  }
+  e->margins_loaded = true;
+  e->label_key = nullptr;
+  hb_status st = stage_labels(e, labels, nullptr, n);
+  if (st != HB_OK) return st;
+  HB_CK(e, cudaStreamSynchronize(s));
+  e->train_begun = true;
+  return HB_OK;
+}
+
+hb_status hb_train_rounds(hb_engine* e, const hb_train_params* p, int32_t rounds,
+                          hb_tree_node* nodes, uint64_t nodes_cap, uint64_t* tree_ptr) {
+  HB_ENTER(e);
+  hb_status st = check_params(e, p);
+  if (st != HB_OK) return st;
+  if (!e->train_begun || !e->margins_loaded) return refuse(e, "no training run (hb_train_begin)");
+  if (rounds < 0 || !tree_ptr || (!nodes && rounds)) return HB_INVALID_ARGUMENT;
+  cudaStream_t s = e->stream;
+  const uint32_t max_nodes = 2u << p->max_depth;
+  HB_CK(e, e->forest.alloc(std::max<size_t>((size_t)rounds * max_nodes, 1)));
+  HB_CK(e, e->counts.alloc(std::max(rounds, 1)));
+  HB_CK(e, cudaMemsetAsync(e->tree_counter.p, 0, 4, s));
+  for (int r = 0; r < rounds; ++r) {
+    st = run_gradients(e, p->objective, p->scale_pos_weight, 1e-16f);
+    if (st != HB_OK) return st;
+    st = grow_device(e, p, true);
+    if (st != HB_OK) return st;
+    if (e->timing && e->ev_used + 128 > e->ev.size()) collect_timers(e);
+  }
+  std::vector<uint32_t> cnt(std::max(rounds, 1));
+  HB_CK(e, cudaMemcpyAsync(cnt.data(), e->counts.p, 4 * (size_t)std::max(rounds, 1), cudaMemcpyDeviceToHost, s));
+  HB_CK(e, cudaStreamSynchronize(s));
+  collect_timers(e);
+  uint64_t used = 0;
+  tree_ptr[0] = 0;
+  for (int r = 0; r < rounds; ++r) {
+    used += cnt[r];
+    tree_ptr[r + 1] = used;
+  }
+  if (used > nodes_cap) return refuse(e, "nodes_cap too small");
+  for (int r = 0; r < rounds; ++r) {
+    HB_CK(e, cudaMemcpyAsync(nodes + tree_ptr[r], e->forest.p + (size_t)r * max_nodes,
+                             sizeof(hb_tree_node) * cnt[r], cudaMemcpyDeviceToHost, s));
+  }
+  HB_CK(e, cudaStreamSynchronize(s));
+  e->staged = false;
+  return HB_OK;
+}
+
+hb_status hb_train(hb_engine* e, const hb_train_params* p, const float* labels, uint64_t n,
+                   float base_margin, int32_t rounds, hb_tree_node* nodes, uint64_t nodes_cap,
+                   uint64_t* tree_ptr) {
+  HB_ENTER(e);
+  hb_status st = check_params(e, p);
+  if (st != HB_OK) return st;
+  st = hb_train_begin(e, labels, n, base_margin);
+  if (st != HB_OK) return st;
+  return hb_train_rounds(e, p, rounds, nodes, nodes_cap, tree_ptr);
+}
+
+hb_status hb_engine_reset_stats(hb_engine* e, int32_t timing) {
+  HB_ENTER(e);
+  for (int k = 0; k < kTimers; ++k) {
+    e->timer_ms[k] = 0.0;
+    e->timer_launches[k] = 0;
+  }
+  e->ev_used = 0;
+  e->kernel_launches = 0;
+  e->rounds_done = 0;
+  e->timing = timing != 0;
+  HB_CK(e, cudaMemsetAsync(e->row_stats.p, 0, 16, e->stream));
+  HB_CK(e, cudaStreamSynchronize(e->stream));
+  return HB_OK;
+}
+
+hb_status hb_engine_get_stats(hb_engine* e, hb_engine_stats* out) {
+  HB_ENTER(e);
+  if (!out) return HB_INVALID_ARGUMENT;
+  collect_timers(e);
+  unsigned long long rs[2];
+  HB_CK(e, cudaMemcpyAsync(rs, e->row_stats.p, 16, cudaMemcpyDeviceToHost, e->stream));
+  HB_CK(e, cudaStreamSynchronize(e->stream));
+  for (int k = 0; k < kTimers; ++k) {
+    out->ms[k] = e->timer_ms[k];
+    out->timed_launches[k] = e->timer_launches[k];
+  }
+  out->kernel_launches = e->kernel_launches;
+  out->rows_built_contiguous = rs[0];
+  out->rows_built_gathered = rs[1];
+  out->rounds = e->rounds_done;
+  return HB_OK;
+}
+
+hb_status hb_engine_stream(hb_engine* e, void** stream) {
+  HB_ENTER(e);
+  if (!stream) return HB_INVALID_ARGUMENT;
+  *stream = (void*)e->stream;
+  return HB_OK;
+}
+
+// ---- sharding -------------------------------------------------------------
+hb_status hb_comm_unique_id(uint8_t id[128]) {
+  if (!id) return HB_INVALID_ARGUMENT;
+  ncclUniqueId u;
+  if (ncclGetUniqueId(&u) != ncclSuccess) return HB_DEVICE_FAILED;
+  std::memcpy(id, u.internal, 128);
+  return HB_OK;
+}
+
+hb_status hb_comm_init(hb_engine* e, int32_t nranks, int32_t rank, const uint8_t id[128],
+                       uint64_t global_rows) {
+  HB_ENTER(e);
+  if (!id || nranks < 1 || rank < 0 || rank >= nranks) return HB_INVALID_ARGUMENT;
+  ncclUniqueId u;
+  std::memcpy(u.internal, id, 128);
+  if (e->comm) {
+    ncclCommDestroy(e->comm);
+    e->comm = nullptr;
+  }
+  HB_NCCL(e, ncclCommInitRank(&e->comm, nranks, u, rank));
+  e->nranks = nranks;
+  e->rank = rank;
+  e->c.global_rows = global_rows;
+  return HB_OK;
+}
+
+}  // extern "C"
+
+extern "C" hb_status hb_engine_set_shard(hb_engine* e, uint64_t row_begin, uint64_t global_rows) {
+  HB_ENTER(e);
+  if (row_begin % 8) return refuse(e, "shards must start on a multiple of 8 rows");
+  e->row_begin = row_begin;
+  e->c.global_rows = global_rows;
+  return HB_OK;
+}

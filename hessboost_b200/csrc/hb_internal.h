@@ -1,0 +1,127 @@
+// Internal declarations shared by the engine (host) and the kernels.
+//
+// Data layout in HBM (one engine = one GPU = one shard of rows):
+//   rec      [n_rows][stride] u8   row-major record: the feature-local bins
+//                                  (one byte per feature) followed by the
+//                                  missing mask (one bit per feature, u32
+//                                  words at mask_off); what the histogram
+//                                  kernels gather by row
+//   col      [n_cols][n_rows] u8   feature-major bins: what the partition
+//                                  reads for the split feature
+//   colmiss  [n_cols][words] u64   missing bitmap, feature-major
+//   gpair    [n_rows] float2       this tree's (g, h)
+//   margin   [n_rows] f32, label [n_rows] f32
+//   rows[2]  [n_rows] u32          row ids, one segment per node (ping-pong)
+//   hist     [slots][total_bins] longlong2 (fixed-point g, h), level-major
+//            slot layout: level L owns slots [2^L - 1, 2^(L+1) - 1); within
+//            a level the built children come first, their siblings second
+#pragma once
+
+#include <cstddef>
+#include <cstdint>
+
+#include "../../include/hb_backend.h"
+
+namespace hb {
+
+constexpr int kMaxDepth = 10;            // device growth supports depth <= 10
+constexpr int kMaxFront = 1 << kMaxDepth;
+constexpr int kTile = 2048;              // partition tile (rows per CTA)
+constexpr int kTileWords = kTile / 32;
+constexpr int kHistThreads = 1024;
+constexpr int kGroupFeatures = 32;       // features per histogram CTA group
+
+// Per-tree scale of the fixed-point gradients: q = rint(v * 2^s).
+struct Scale {
+  int32_t sg, sh;
+  double fg, fh;      // 2^sg, 2^sh
+  double ig, ih;      // 2^-sg, 2^-sh
+  uint32_t maxg_bits, maxh_bits;  // largest |g|, |h| (f32 bits)
+  uint32_t nonfinite;
+  uint32_t pad;
+};
+
+// Constants of the binned matrix and of the training run.
+struct DevConst {
+  uint64_t n_rows;        // rows on this device
+  uint64_t global_rows;   // rows over every rank (fixed-point scale)
+  uint32_t n_cols;
+  uint32_t total_bins;
+  uint32_t max_bins;      // largest per-feature bin count
+  uint32_t stride;        // record bytes
+  uint32_t mask_off;      // byte offset of the mask words in a record
+  uint32_t dense;         // index-level: no missing cell anywhere
+  uint32_t n_groups;      // feature groups of kGroupFeatures
+  // training parameters (RegParams rounded to f32 then widened)
+  double lambda, alpha, gamma, mcw, mds;
+  float eta;
+  int32_t max_depth;
+};
+
+// One frontier entry of the level being grown.
+struct Front {
+  int32_t node;       // tree node id
+  int32_t slot;       // histogram slot (or -1)
+  uint32_t begin;     // segment in the current row buffer
+  uint32_t len;
+  long long g, h;     // node statistics (fixed point)
+};
+
+// The best candidate of one (node, feature) pair.
+struct Cand {
+  float loss;         // -inf: none
+  int32_t bin;        // last global bin going left, -1 = below every bin
+  int32_t default_left;
+  int32_t pad;
+  long long lg, lh;   // left child statistics
+};
+
+// Decision for one frontier node of the level.
+struct Decision {
+  int32_t split;      // 1: splits, 0: becomes a leaf
+  int32_t pair;       // index among the level's splits
+  uint32_t feature;
+  uint32_t limit;     // local bins below it go left
+  int32_t default_left;
+  float leaf_value;   // eta-scaled leaf value when it becomes a leaf
+  int32_t item_begin; // first partition work item
+  int32_t item_count;
+  long long lg, lh;   // left child stats
+};
+
+// A partition work item: a tile of one frontier node's segment.
+struct PItem {
+  int32_t k;          // frontier index
+  int32_t kind;       // 1 split, 2 leaf margin add
+  uint32_t off;       // tile offset within the segment
+  uint32_t len;
+};
+
+// One histogram build entry: rows [begin, begin + len) of the row buffer
+// into slot `slot`; `prefix` = rows of the entries before it.
+struct HEntry {
+  int32_t slot;
+  int32_t identity;   // rows are the positions themselves
+  uint32_t begin;
+  uint32_t len;
+  uint64_t prefix;
+};
+
+// Level bookkeeping written by the device, read by the next kernels.
+struct LevelState {
+  int32_t n_front;        // frontier entries at this level
+  int32_t n_items;        // partition work items
+  int32_t n_split;        // splitting nodes
+  int32_t n_nodes;        // tree nodes so far
+  int32_t n_hentries;     // histogram entries
+  int32_t n_pairs;        // sibling subtractions
+  uint64_t hist_rows;     // rows to build this level
+  int32_t tree_index;     // slot in the forest buffer
+  int32_t pad;
+};
+
+struct Triple {
+  int32_t parent, built, sibling, pad;
+};
+
+}  // namespace hb

@@ -1,0 +1,1033 @@
+// CUDA kernels of the hist path for sm_100a.
+//
+// Built with -fmad=false: every f32/f64 expression below is evaluated with
+// one IEEE rounding per operation, as the reference's Rust does, and the
+// only fused multiply-adds are the explicit __fmaf_rn of the reference's
+// own vector exponential.
+#include <cub/block/block_scan.cuh>
+#include <cub/block/block_reduce.cuh>
+
+#include <cfloat>
+#include <climits>
+#include <cmath>
+
+#include "hb_kernels.cuh"
+
+namespace hb {
+
+namespace {
+
+constexpr unsigned kFull = 0xffffffffu;
+constexpr float kBelowAll = -FLT_MAX;         // src/tree/builder/mod.rs:308
+constexpr double kRtEps = 1e-6;               // src/lib.rs:366
+
+__device__ __forceinline__ double ll2d(long long v) { return __ll2double_rn(v); }
+
+// ---------------------------------------------------------------------------
+// Objectives.
+
+// src/simd/x86_64.rs:20 `exp_f32`: range reduction to [-ln2/2, ln2/2] and a
+// seventh-order polynomial in Estrin pairs, operation for operation.
+__device__ __forceinline__ float exp_vector(float v) {
+  const float log2e = 1.44269504088896340736f;
+  float t = __fmul_rn(v, log2e);
+  int e = __float2int_rn(t);
+  float ef = __int2float_rn(e);
+  float r = __fmaf_rn(-ef, 0.6933594f, v);
+  r = __fmaf_rn(ef, 2.1219444e-4f, r);
+  float sq = __fmul_rn(r, r);
+  float fo = __fmul_rn(sq, sq);
+  float p0 = __fadd_rn(1.0f, r);
+  float p1 = __fmaf_rn(1.0f / 6.0f, r, 0.5f);
+  float p2 = __fmaf_rn(1.0f / 120.0f, r, 1.0f / 24.0f);
+  float p3 = __fmaf_rn(1.0f / 5040.0f, r, 1.0f / 720.0f);
+  float lo = __fmaf_rn(p1, sq, p0);
+  float hi = __fmaf_rn(p3, sq, p2);
+  float poly = __fmaf_rn(hi, fo, lo);
+  float scale = __int_as_float((e + 127) << 23);
+  return __fmul_rn(poly, scale);
+}
+
+// src/simd/x86_64.rs:63 `sigmoid_f32`
+__device__ __forceinline__ float sigmoid_vector(float v) {
+  float e = exp_vector(__fsub_rn(0.0f, fabsf(v)));
+  float den = __fadd_rn(1.0f, e);
+  float pos = __fdiv_rn(1.0f, den);
+  float neg = __fdiv_rn(e, den);
+  return v >= 0.0f ? pos : neg;
+}
+
+// src/simd/mod.rs:421 `sigmoid_scalar`, 1 / (expf(min(-x, 88.7)) + 1). The
+// exponential is CUDA's double exp rounded once to f32 (the correctly
+// rounded expf except where the double result lies within one double ulp
+// of an f32 rounding boundary).
+__device__ __forceinline__ float sigmoid_scalar(float x) {
+  float t = fminf(-x, 88.7f);
+  float e = __double2float_rn(exp((double)t));
+  return __fdiv_rn(1.0f, __fadd_rn(e, 1.0f));
+}
+
+__device__ __forceinline__ void fold_max(float g, float h, float& mg, float& mh, bool& nonfinite) {
+  if (!isfinite(g) || !isfinite(h)) nonfinite = true;
+  mg = fmaxf(mg, fabsf(g));
+  mh = fmaxf(mh, fabsf(h));
+}
+
+__device__ __forceinline__ void reduce_scale(float mg, float mh, bool nonfinite, Scale* scale) {
+  for (int o = 16; o > 0; o >>= 1) {
+    mg = fmaxf(mg, __shfl_xor_sync(kFull, mg, o));
+    mh = fmaxf(mh, __shfl_xor_sync(kFull, mh, o));
+  }
+  unsigned nf = __ballot_sync(kFull, nonfinite);
+  if ((threadIdx.x & 31) == 0) {
+    if (mg > 0.0f) atomicMax(&scale->maxg_bits, __float_as_uint(mg));
+    if (mh > 0.0f) atomicMax(&scale->maxh_bits, __float_as_uint(mh));
+    if (nf) atomicOr(&scale->nonfinite, 1u);
+  }
+}
+
+// Gradients (one thread per row, grid-stride in whole warps):
+//  * reg:squarederror (src/objective/regression.rs:50): g = (p - y) w, h = w,
+//    w scaled by scale_pos_weight when y == 1;
+//  * binary:logistic (src/simd/x86_64.rs:106 + scalar.rs:8): over the first
+//    `vrows` rows (n - n % 8 for n >= 16, objective/mod.rs:195) every aligned
+//    group of 8 margins whose magnitudes are all <= 80 takes the vector
+//    sigmoid, any other group and the tail the scalar one.
+__global__ void k_gradients(int kind, const float* __restrict__ margin,
+                            const float* __restrict__ label, const float* __restrict__ weight,
+                            float spw, float min_hess, uint64_t n, uint64_t vrows,
+                            float2* __restrict__ gpair, Scale* scale) {
+  float mg = 0.0f, mh = 0.0f;
+  bool nonfinite = false;
+  const unsigned lane = threadIdx.x & 31;
+  const uint64_t step = (uint64_t)gridDim.x * blockDim.x;
+  for (uint64_t base = (uint64_t)blockIdx.x * blockDim.x; base < n; base += step) {
+    uint64_t i = base + threadIdx.x;
+    bool in = i < n;
+    float m = in ? margin[i] : 0.0f;
+    float y = in ? label[i] : 0.0f;
+    float w = (in && weight) ? weight[i] : 1.0f;
+    float g = 0.0f, h = 0.0f;
+    if (kind == HB_LOSS_LOGISTIC) {
+      bool regular = fabsf(m) <= 80.0f;
+      unsigned bal = __ballot_sync(kFull, regular || !in);
+      bool group_regular = ((bal >> (lane & ~7u)) & 0xffu) == 0xffu;
+      float p = (i < vrows && group_regular) ? sigmoid_vector(m) : sigmoid_scalar(m);
+      if (y == 1.0f) w = __fmul_rn(w, spw);
+      g = __fmul_rn(__fsub_rn(p, y), w);
+      float ph = __fmul_rn(p, __fsub_rn(1.0f, p));
+      h = __fmul_rn(ph > min_hess ? ph : min_hess, w);
+    } else {
+      if (y == 1.0f) w = __fmul_rn(w, spw);
+      g = __fmul_rn(__fsub_rn(m, y), w);
+      h = w;
+    }
+    if (in) {
+      gpair[i] = make_float2(g, h);
+      fold_max(g, h, mg, mh, nonfinite);
+    }
+  }
+  reduce_scale(mg, mh, nonfinite, scale);
+}
+
+__global__ void k_pair_maxima(const float2* __restrict__ gpair, uint64_t n, Scale* scale) {
+  float mg = 0.0f, mh = 0.0f;
+  bool nonfinite = false;
+  const uint64_t step = (uint64_t)gridDim.x * blockDim.x;
+  for (uint64_t base = (uint64_t)blockIdx.x * blockDim.x; base < n; base += step) {
+    uint64_t i = base + threadIdx.x;
+    if (i < n) {
+      float2 p = gpair[i];
+      fold_max(p.x, p.y, mg, mh, nonfinite);
+    }
+  }
+  reduce_scale(mg, mh, nonfinite, scale);
+}
+
+// The exponent s with |rint(v * 2^s)| * n <= 2^62 for every |v| <= max.
+__device__ int fixed_scale(float max_abs, uint64_t n) {
+  if (!(max_abs > 0.0f) || !isfinite(max_abs)) return 0;
+  int e;
+  frexpf(max_abs, &e);  // max_abs < 2^e
+  int c = 0;
+  while (c < 64 && (1ull << c) < n) ++c;
+  return 62 - c - e;
+}
+
+__device__ __forceinline__ double pow2d(int e) {
+  return __longlong_as_double((long long)(1023 + e) << 52);  // e in [-1022, 1023]
+}
+
+__global__ void k_scale(Scale* scale, uint64_t global_rows) {
+  Scale s = *scale;
+  s.sg = fixed_scale(__uint_as_float(s.maxg_bits), global_rows);
+  s.sh = fixed_scale(__uint_as_float(s.maxh_bits), global_rows);
+  s.fg = pow2d(s.sg);
+  s.fh = pow2d(s.sh);
+  s.ig = pow2d(-s.sg);
+  s.ih = pow2d(-s.sh);
+  *scale = s;
+}
+
+// ---------------------------------------------------------------------------
+// Upload: feature-major bins -> row-major records (GHistIndex columns ->
+// the layout the histogram gathers).
+__global__ void k_encode(const uint8_t* __restrict__ col, const uint64_t* __restrict__ colmiss,
+                         uint64_t n_rows, uint32_t n_cols, uint32_t stride, uint32_t mask_off,
+                         uint8_t* __restrict__ rec) {
+  const uint64_t words = (n_rows + 63) / 64;
+  for (uint64_t r = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; r < n_rows;
+       r += (uint64_t)gridDim.x * blockDim.x) {
+    uint32_t* out = reinterpret_cast<uint32_t*>(rec + r * stride);
+    uint32_t word = 0;
+    for (uint32_t f = 0; f < n_cols; ++f) {
+      word |= (uint32_t)col[(uint64_t)f * n_rows + r] << ((f & 3) * 8);
+      if ((f & 3) == 3 || f + 1 == n_cols) {
+        out[f >> 2] = word;
+        word = 0;
+      }
+    }
+    for (uint32_t b = ((n_cols + 3) / 4) * 4; b < mask_off; b += 4) out[b >> 2] = 0;
+    uint32_t n_mask = (n_cols + 31) / 32;
+    for (uint32_t w = 0; w < n_mask; ++w) {
+      uint32_t m = 0;
+      if (colmiss) {
+        for (uint32_t f = w * 32; f < min(n_cols, w * 32 + 32); ++f) {
+          uint64_t bit = (colmiss[(uint64_t)f * words + (r >> 6)] >> (r & 63)) & 1ull;
+          m |= (uint32_t)bit << (f - w * 32);
+        }
+      }
+      out[(mask_off >> 2) + w] = m;
+    }
+    for (uint32_t b = mask_off + 4 * n_mask; b < stride; b += 4) out[b >> 2] = 0;
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Histogram. One CTA per SM (1024 threads) per feature group of up to 32
+// features; the CTA's share of the level's rows is contiguous in the
+// concatenation of the entries, so it flushes its shared histogram once per
+// entry it touches. Shared layout: g[bin][32] then h[bin][32] as int64, a
+// feature's bins in one bank pair; lane l starts at feature l % nf and walks
+// the features cyclically, so a warp's 32 atomics hit distinct features.
+__device__ __forceinline__ uint32_t pick_word(const uint4& a, const uint4& b, int k) {
+  uint32_t w = a.x;
+  w = k == 1 ? a.y : w;
+  w = k == 2 ? a.z : w;
+  w = k == 3 ? a.w : w;
+  w = k == 4 ? b.x : w;
+  w = k == 5 ? b.y : w;
+  w = k == 6 ? b.z : w;
+  w = k == 7 ? b.w : w;
+  return w;
+}
+
+__global__ void __launch_bounds__(kHistThreads, 1)
+    k_hist(DevConst c, const uint32_t* __restrict__ fo, const uint8_t* __restrict__ rec,
+           const float2* __restrict__ gpair, const Scale* __restrict__ scale,
+           const uint32_t* __restrict__ rows, const HEntry* __restrict__ entries,
+           const LevelState* __restrict__ ls, longlong2* __restrict__ hist,
+           long long* __restrict__ totals, unsigned long long* __restrict__ row_stats) {
+  extern __shared__ unsigned long long smem[];
+  const int n_entries = ls->n_hentries;
+  const uint64_t total = ls->hist_rows;
+  if (n_entries <= 0 || total == 0) return;
+  if (row_stats && blockIdx.x == 0 && blockIdx.y == 0 && threadIdx.x == 0)
+    atomicAdd(&row_stats[entries[0].identity ? 0 : 1], (unsigned long long)total);
+  const uint64_t per = (total + gridDim.x - 1) / gridDim.x;
+  const uint64_t a = (uint64_t)blockIdx.x * per;
+  const uint64_t b = min(total, a + per);
+  if (a >= b) return;
+
+  const int g = blockIdx.y;
+  const int f0 = g * kGroupFeatures;
+  const int nf = min(kGroupFeatures, (int)c.n_cols - f0);
+  const int nslots = (int)c.max_bins * 32;
+  unsigned long long* sg = smem;
+  unsigned long long* sh = smem + nslots;
+  for (int i = threadIdx.x; i < 2 * nslots; i += blockDim.x) smem[i] = 0ull;
+  __syncthreads();
+
+  const double fg = scale->fg, fh = scale->fh;
+  const int lane = threadIdx.x & 31;
+  const int start_f = lane % nf;
+  const bool wide = c.stride >= (uint32_t)(32 * g + 32);
+  const bool want_totals = totals != nullptr && g == 0;
+  long long tg = 0, th = 0;
+
+  int e = 0;
+  while (e + 1 < n_entries && entries[e + 1].prefix <= a) ++e;
+  uint64_t pos = a;
+  while (pos < b && e < n_entries) {
+    const HEntry en = entries[e];
+    const uint64_t end_e = min(b, en.prefix + en.len);
+    for (uint64_t i = pos + threadIdx.x; i < end_e; i += blockDim.x) {
+      const uint32_t at = en.begin + (uint32_t)(i - en.prefix);
+      const uint32_t row = en.identity ? at : rows[at];
+      const uint8_t* rp = rec + (uint64_t)row * c.stride;
+      const uint4 v0 = *reinterpret_cast<const uint4*>(rp + 32 * g);
+      const uint4 v1 = wide ? *reinterpret_cast<const uint4*>(rp + 32 * g + 16) : make_uint4(0, 0, 0, 0);
+      const uint32_t mask = *reinterpret_cast<const uint32_t*>(rp + c.mask_off + 4 * g);
+      const float2 p = gpair[row];
+      const long long qg = __double2ll_rn((double)p.x * fg);
+      const long long qh = __double2ll_rn((double)p.y * fh);
+      if (want_totals) {
+        tg += qg;
+        th += qh;
+      }
+      int f = start_f;
+      for (int s = 0; s < nf; ++s) {
+        if (!((mask >> f) & 1u)) {
+          const uint32_t w = pick_word(v0, v1, f >> 2);
+          const uint32_t bin = (w >> ((f & 3) * 8)) & 0xffu;
+          atomicAdd(&sg[bin * 32 + f], (unsigned long long)qg);
+          atomicAdd(&sh[bin * 32 + f], (unsigned long long)qh);
+        }
+        f = (f + 1 == nf) ? 0 : f + 1;
+      }
+    }
+    __syncthreads();
+    longlong2* dst = hist + (uint64_t)en.slot * c.total_bins;
+    for (int i = threadIdx.x; i < nslots; i += blockDim.x) {
+      const int bin = i >> 5, fl = i & 31;
+      if (fl < nf) {
+        const uint32_t fs = fo[f0 + fl];
+        const uint32_t nb = fo[f0 + fl + 1] - fs;
+        if ((uint32_t)bin < nb) {
+          const unsigned long long vg = sg[i], vh = sh[i];
+          if (vg) atomicAdd(reinterpret_cast<unsigned long long*>(&dst[fs + bin].x), vg);
+          if (vh) atomicAdd(reinterpret_cast<unsigned long long*>(&dst[fs + bin].y), vh);
+        }
+      }
+      sg[i] = 0ull;
+      sh[i] = 0ull;
+    }
+    __syncthreads();
+    pos = end_e;
+    ++e;
+  }
+  if (want_totals) {
+    using BR = cub::BlockReduce<long long, kHistThreads>;
+    __shared__ typename BR::TempStorage tmp;
+    long long sgt = BR(tmp).Sum(tg);
+    __syncthreads();
+    long long sht = BR(tmp).Sum(th);
+    if (threadIdx.x == 0) {
+      atomicAdd(reinterpret_cast<unsigned long long*>(&totals[0]), (unsigned long long)sgt);
+      atomicAdd(reinterpret_cast<unsigned long long*>(&totals[1]), (unsigned long long)sht);
+    }
+  }
+}
+
+// sibling = parent - built (int64, exact; src/tree/hist/mod.rs:32).
+__global__ void k_subtract(const Triple* __restrict__ pairs, const LevelState* __restrict__ ls,
+                           uint32_t total_bins, longlong2* __restrict__ hist) {
+  const int n_pairs = ls->n_pairs;
+  const uint64_t work = (uint64_t)n_pairs * total_bins;
+  for (uint64_t i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; i < work;
+       i += (uint64_t)gridDim.x * blockDim.x) {
+    const Triple t = pairs[i / total_bins];
+    const uint32_t bin = (uint32_t)(i % total_bins);
+    const longlong2 p = hist[(uint64_t)t.parent * total_bins + bin];
+    const longlong2 q = hist[(uint64_t)t.built * total_bins + bin];
+    hist[(uint64_t)t.sibling * total_bins + bin] = make_longlong2(p.x - q.x, p.y - q.y);
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Split scoring, XGBoost's f32 arithmetic as the reference states it
+// (src/tree/builder/shared.rs:87-141, split.rs:37-58).
+__device__ __forceinline__ double threshold_l1(double g, double alpha) {
+  if (g > alpha) return g - alpha;
+  if (g < -alpha) return g + alpha;
+  return 0.0;
+}
+
+__device__ __forceinline__ double xgb_calc_weight(double g, double h, const DevConst& c) {
+  if (h <= 0.0) return 0.0;
+  double w = -threshold_l1(g, c.alpha) / (h + c.lambda);
+  if (c.mds != 0.0 && fabs(w) > c.mds) w = copysign(c.mds, w);
+  return w;
+}
+
+// xgb_weight with the default (infinite) monotone bounds.
+__device__ __forceinline__ float xgb_weight(double g, double h, const DevConst& c) {
+  return __double2float_rn(xgb_calc_weight(g, h, c));
+}
+
+__device__ __forceinline__ double gain_given_weight(double g, double h, const DevConst& c, float w) {
+  const float ww = __fmul_rn(w, w);
+  return -(2.0 * g * (double)w + (h + c.lambda) * (double)ww + 2.0 * c.alpha * (double)fabsf(w));
+}
+
+__device__ __forceinline__ float node_gain(double g, double h, const DevConst& c) {
+  if (h <= 0.0) return 0.0f;
+  return __double2float_rn(gain_given_weight(g, h, c, xgb_weight(g, h, c)));
+}
+
+__device__ __forceinline__ float cand_loss(double lg, double lh, double rg, double rh,
+                                           float root_gain, const DevConst& c) {
+  if (!(lh > 0.0 && rh > 0.0 && lh >= c.mcw && rh >= c.mcw)) return -INFINITY;
+  const float wl = xgb_weight(lg, lh, c);
+  const float wr = xgb_weight(rg, rh, c);
+  const float gain = __fadd_rn(__double2float_rn(gain_given_weight(lg, lh, c, wl)),
+                               __double2float_rn(gain_given_weight(rg, rh, c, wr)));
+  return __fsub_rn(gain, root_gain);
+}
+
+// gain.rs:107 `calc_weight` (leaf values).
+__device__ __forceinline__ double calc_weight(double g, double h, const DevConst& c) {
+  if (h < c.mcw || h <= 0.0) return 0.0;
+  double w = -threshold_l1(g, c.alpha) / (h + c.lambda);
+  if (c.mds > 0.0) w = fmin(fmax(w, -c.mds), c.mds);
+  return w;
+}
+
+__device__ __forceinline__ long long shfl_ll(long long v, int src) {
+  return __shfl_sync(kFull, v, src);
+}
+
+// One warp per (frontier node, feature): the feature's first best candidate
+// in for_each_numeric_split order (split.rs:391): the forward pass over the
+// bins, then, when the node has missing values of the feature, the
+// backward pass. Prefix sums are exact integers; the backward pass's
+// suffix at offset o is (feature total - exclusive prefix at o).
+__global__ void k_scan(DevConst c, const uint32_t* __restrict__ fo,
+                       const longlong2* __restrict__ hist, const Front* __restrict__ front,
+                       const LevelState* __restrict__ ls, const Scale* __restrict__ scale,
+                       Cand* __restrict__ cand) {
+  const int warp = (int)((blockIdx.x * blockDim.x + threadIdx.x) >> 5);
+  const int lane = threadIdx.x & 31;
+  const int n_front = ls->n_front;
+  const int k = warp / (int)c.n_cols;
+  const int f = warp % (int)c.n_cols;
+  if (k >= n_front) return;
+  const Front fr = front[k];
+  const uint32_t fs = fo[f];
+  const int nb = (int)(fo[f + 1] - fs);
+  Cand out;
+  out.loss = -INFINITY;
+  out.bin = -1;
+  out.default_left = 0;
+  out.pad = 0;
+  out.lg = out.lh = 0;
+  if (nb <= 1 || fr.slot < 0) {
+    if (lane == 0) cand[(uint64_t)k * c.n_cols + f] = out;
+    return;
+  }
+  const longlong2* H = hist + (uint64_t)fr.slot * c.total_bins + fs;
+  const double ig = scale->ig, ih = scale->ih;
+  const float root_gain = node_gain(ll2d(fr.g) * ig, ll2d(fr.h) * ih, c);
+  const int K = (nb + 31) / 32;  // <= 8 bins per lane (features of <= 256 bins)
+  long long vg[8], vh[8];
+  long long lsg = 0, lsh = 0;
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    const int o = lane * K + j;
+    longlong2 v = make_longlong2(0, 0);
+    if (j < K && o < nb) v = H[o];
+    vg[j] = v.x;
+    vh[j] = v.y;
+    lsg += v.x;
+    lsh += v.y;
+  }
+  // exclusive warp scan of the lane sums
+  long long ig_ = lsg, ih_ = lsh;
+#pragma unroll
+  for (int d = 1; d < 32; d <<= 1) {
+    const long long tg = shfl_ll(ig_, (lane - d) & 31);
+    const long long th = shfl_ll(ih_, (lane - d) & 31);
+    if (lane >= d) {
+      ig_ += tg;
+      ih_ += th;
+    }
+  }
+  const long long tot_g = shfl_ll(ig_, 31), tot_h = shfl_ll(ih_, 31);
+  long long ag = ig_ - lsg, ah = ih_ - lsh;
+  const bool has_missing = !c.dense && !(tot_g == fr.g && tot_h == fr.h);
+
+  float best = -INFINITY;
+  int best_seq = INT_MAX;
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    const int o = lane * K + j;
+    if (j < K && o < nb) {
+      const long long pg = ag, ph = ah;
+      ag += vg[j];
+      ah += vh[j];
+      {
+        const float l = cand_loss(ll2d(ag) * ig, ll2d(ah) * ih, ll2d(fr.g - ag) * ig,
+                                  ll2d(fr.h - ah) * ih, root_gain, c);
+        if (isfinite(l) && (l > best || (l == best && o < best_seq))) {
+          best = l;
+          best_seq = o;
+          out.bin = (int)fs + o;
+          out.default_left = 0;
+          out.lg = ag;
+          out.lh = ah;
+        }
+      }
+      if (has_missing) {
+        const long long rg = tot_g - pg, rh = tot_h - ph;
+        const long long lg2 = fr.g - rg, lh2 = fr.h - rh;
+        const float l = cand_loss(ll2d(lg2) * ig, ll2d(lh2) * ih, ll2d(rg) * ig, ll2d(rh) * ih,
+                                  root_gain, c);
+        const int seq = nb + (nb - 1 - o);
+        if (isfinite(l) && (l > best || (l == best && seq < best_seq))) {
+          best = l;
+          best_seq = seq;
+          out.bin = o == 0 ? -1 : (int)fs + o - 1;
+          out.default_left = 1;
+          out.lg = lg2;
+          out.lh = lh2;
+        }
+      }
+    }
+  }
+  // first maximum over the warp: larger loss, then earlier candidate
+  int src = lane;
+#pragma unroll
+  for (int d = 16; d > 0; d >>= 1) {
+    const float ob = __shfl_xor_sync(kFull, best, d);
+    const int os = __shfl_xor_sync(kFull, best_seq, d);
+    const int osrc = __shfl_xor_sync(kFull, src, d);
+    if (ob > best || (ob == best && os < best_seq)) {
+      best = ob;
+      best_seq = os;
+      src = osrc;
+    }
+  }
+  if (best_seq == INT_MAX) {  // no finite candidate in this feature
+    if (lane == 0) {
+      out.loss = -INFINITY;
+      out.bin = -1;
+      out.default_left = 0;
+      out.lg = out.lh = 0;
+      cand[(uint64_t)k * c.n_cols + f] = out;
+    }
+  } else if (lane == src) {
+    out.loss = best;
+    cand[(uint64_t)k * c.n_cols + f] = out;
+  }
+}
+
+// ---------------------------------------------------------------------------
+// One CTA decides the whole level: each frontier node's split (features
+// merged in order with need_replace, builder/mod.rs:313), validity
+// (BestSplit::valid, :167), child ids in frontier order (RegTree::expand,
+// regtree.rs:549), child statistics, which child's histogram is built, and
+// the partition work items.
+__device__ __forceinline__ hb_tree_node make_leaf(float value, float sum_hess) {
+  hb_tree_node n;
+  n.left = -1;
+  n.right = -1;
+  n.split_feature = 0;
+  n.split_cond = 0.0f;
+  n.default_left = 1;
+  n.leaf_value = value;
+  n.sum_hess = sum_hess;
+  n.split_gain = 0.0f;
+  n.split_bin = -1;
+  n.reserved = 0;
+  return n;
+}
+
+constexpr int kApplyThreads = 1024;
+
+__global__ void __launch_bounds__(kApplyThreads)
+    k_apply(DevConst c, const uint32_t* __restrict__ fo, const float* __restrict__ cuts,
+            const Cand* __restrict__ cand, const Front* __restrict__ front, Front* __restrict__ next,
+            Decision* __restrict__ dec, PItem* __restrict__ items, LevelState* ls,
+            LevelState* ls_next, hb_tree_node* __restrict__ tree, const Scale* __restrict__ scale,
+            int depth, int leaf_only) {
+  using Scan = cub::BlockScan<int, kApplyThreads>;
+  __shared__ typename Scan::TempStorage tmp;
+  const int n_front = ls->n_front;
+  const int n_nodes = ls->n_nodes;
+  const int k = threadIdx.x;
+  const double ig = scale->ig, ih = scale->ih;
+  if (depth == 0 && k == 0 && n_front > 0) tree[0] = make_leaf(0.0f, (float)(ll2d(front[0].h) * ih));
+
+  Front fr{};
+  Cand best{};
+  uint32_t best_f = 0;
+  int valid = 0;
+  if (k < n_front) {
+    fr = front[k];
+    if (!leaf_only) {
+      best.loss = 0.0f;
+      best.bin = -1;
+      best.default_left = 1;
+      for (uint32_t f = 0; f < c.n_cols; ++f) {
+        const Cand cf = cand[(uint64_t)k * c.n_cols + f];
+        if (cf.loss > best.loss) {  // need_replace in ascending feature order
+          best = cf;
+          best_f = f;
+        }
+      }
+      const double lh = ll2d(best.lh) * ih;
+      const double rh = ll2d(fr.h - best.lh) * ih;
+      valid = (double)best.loss > kRtEps && (double)best.loss >= c.gamma && lh > 0.0 &&
+              rh > 0.0 && lh >= c.mcw && rh >= c.mcw;
+    }
+  }
+  int pos = 0, n_split = 0;
+  Scan(tmp).ExclusiveSum(valid, pos, n_split);
+  __syncthreads();
+
+  int n_items_k = 0;
+  if (k < n_front) {
+    Decision d{};
+    d.split = valid;
+    d.pair = pos;
+    if (valid) {
+      const long long lg = best.lg, lh = best.lh;
+      const long long rg = fr.g - lg, rh = fr.h - lh;
+      const double dlg = ll2d(lg) * ig, dlh = ll2d(lh) * ih;
+      const double drg = ll2d(rg) * ig, drh = ll2d(rh) * ih;
+      const int left_id = n_nodes + 2 * pos;
+      hb_tree_node nd = tree[fr.node];
+      nd.split_feature = best_f;
+      nd.split_cond = best.bin < 0 ? kBelowAll : cuts[best.bin];
+      nd.default_left = best.default_left ? 1u : 0u;
+      nd.left = left_id;
+      nd.right = left_id + 1;
+      nd.split_bin = best.bin;
+      nd.split_gain = best.loss;
+      tree[fr.node] = nd;
+      tree[left_id] = make_leaf(xgb_weight(dlg, dlh, c), (float)dlh);
+      tree[left_id + 1] = make_leaf(xgb_weight(drg, drh, c), (float)drh);
+      const bool terminal = c.max_depth > 0 && depth + 1 >= c.max_depth;
+      int lslot = -1, rslot = -1;
+      if (!terminal) {
+        const int base = (1 << (depth + 1)) - 1, half = 1 << depth;
+        const bool left_built = lh <= rh;  // the child with the smaller Hessian sum
+        lslot = left_built ? base + pos : base + half + pos;
+        rslot = left_built ? base + half + pos : base + pos;
+      }
+      Front l{}, r{};
+      l.node = left_id;
+      l.slot = lslot;
+      l.g = lg;
+      l.h = lh;
+      r.node = left_id + 1;
+      r.slot = rslot;
+      r.g = rg;
+      r.h = rh;
+      next[2 * pos] = l;
+      next[2 * pos + 1] = r;
+      d.feature = best_f;
+      const uint32_t fs = fo[best_f];
+      d.limit = best.bin < 0 ? 0u : (uint32_t)(best.bin + 1) - fs;
+      d.default_left = best.default_left;
+      d.lg = lg;
+      d.lh = lh;
+    } else {
+      // finalize_leaf_values (shared.rs:174) then scale_leaves(eta).
+      const float w = __double2float_rn(calc_weight(ll2d(fr.g) * ig, ll2d(fr.h) * ih, c));
+      const float v = __fmul_rn(w, c.eta);
+      tree[fr.node].leaf_value = v;
+      d.leaf_value = v;
+    }
+    n_items_k = (int)((fr.len + kTile - 1) / kTile);
+    dec[k] = d;
+  }
+  int item0 = 0, n_items = 0;
+  Scan(tmp).ExclusiveSum(n_items_k, item0, n_items);
+  if (k < n_front) {
+    dec[k].item_begin = item0;
+    dec[k].item_count = n_items_k;
+    for (int t = 0; t < n_items_k; ++t) {
+      PItem it;
+      it.k = k;
+      it.kind = valid ? 1 : 2;
+      it.off = (uint32_t)t * kTile;
+      it.len = min((uint32_t)kTile, fr.len - (uint32_t)t * kTile);
+      items[item0 + t] = it;
+    }
+  }
+  if (k == 0) {
+    ls->n_items = n_items;
+    ls->n_split = n_split;
+    ls_next->n_front = 2 * n_split;
+    ls_next->n_nodes = n_nodes + 2 * n_split;
+    ls_next->tree_index = ls->tree_index;
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Stable partition (partition.rs:106, route_column :206): present local bin
+// < limit goes left, missing follows default_left; the left child keeps the
+// segment's first rows, both in ascending order. Three passes over tiles:
+// direction bits + counts, per-node exclusive scan, scatter. Leaf items add
+// the node's eta-scaled leaf value to the margins of its rows instead.
+constexpr int kPartThreads = 256;
+
+__global__ void __launch_bounds__(kPartThreads)
+    k_part_count(DevConst c, const uint8_t* __restrict__ col, const uint64_t* __restrict__ colmiss,
+                 const uint32_t* __restrict__ rows_in, int identity, const Front* __restrict__ front,
+                 const Decision* __restrict__ dec, const PItem* __restrict__ items,
+                 const LevelState* __restrict__ ls, uint32_t* __restrict__ dirbits,
+                 uint32_t* __restrict__ item_left, float* __restrict__ margin) {
+  const int it = blockIdx.x;
+  if (it >= ls->n_items) return;
+  const PItem pi = items[it];
+  const Front fr = front[pi.k];
+  const Decision d = dec[pi.k];
+  if (pi.kind == 2) {
+    for (uint32_t i = threadIdx.x; i < pi.len; i += blockDim.x) {
+      const uint32_t at = fr.begin + pi.off + i;
+      const uint32_t row = identity ? at : rows_in[at];
+      margin[row] = __fadd_rn(margin[row], d.leaf_value);
+    }
+    return;
+  }
+  const uint8_t* colf = col + (uint64_t)d.feature * c.n_rows;
+  const uint64_t words = (c.n_rows + 63) / 64;
+  const uint64_t* missf = colmiss ? colmiss + (uint64_t)d.feature * words : nullptr;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  int cnt = 0;
+  for (int j = 0; j < kTile / kPartThreads; ++j) {
+    const uint32_t i = j * kPartThreads + threadIdx.x;
+    bool left = false;
+    if (i < pi.len) {
+      const uint32_t at = fr.begin + pi.off + i;
+      const uint32_t row = identity ? at : rows_in[at];
+      const bool miss = missf && ((missf[row >> 6] >> (row & 63)) & 1ull);
+      left = miss ? (d.default_left != 0) : (colf[row] < d.limit);
+    }
+    const unsigned bal = __ballot_sync(kFull, left);
+    if (lane == 0) {
+      dirbits[(uint64_t)it * kTileWords + j * (kPartThreads / 32) + warp] = bal;
+      cnt += __popc(bal);
+    }
+  }
+  using BR = cub::BlockReduce<int, kPartThreads>;
+  __shared__ typename BR::TempStorage tmp;
+  const int total = BR(tmp).Sum(cnt);
+  if (threadIdx.x == 0) item_left[it] = (uint32_t)total;
+}
+
+// One warp per splitting frontier node: exclusive scan of its tiles' left
+// counts; the children's segments.
+__global__ void k_part_scan(const Front* __restrict__ front, const Decision* __restrict__ dec,
+                            const LevelState* __restrict__ ls, const uint32_t* __restrict__ item_left,
+                            uint32_t* __restrict__ item_left_off, Front* __restrict__ next) {
+  const int k = (int)((blockIdx.x * blockDim.x + threadIdx.x) >> 5);
+  const int lane = threadIdx.x & 31;
+  if (k >= ls->n_front) return;
+  const Decision d = dec[k];
+  if (!d.split) return;
+  uint32_t run = 0;
+  for (int base = 0; base < d.item_count; base += 32) {
+    const int t = base + lane;
+    const uint32_t v = t < d.item_count ? item_left[d.item_begin + t] : 0u;
+    uint32_t inc = v;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const uint32_t x = __shfl_up_sync(kFull, inc, o);
+      if (lane >= o) inc += x;
+    }
+    if (t < d.item_count) item_left_off[d.item_begin + t] = run + inc - v;
+    run += __shfl_sync(kFull, inc, 31);
+  }
+  if (lane == 0) {
+    const Front fr = front[k];
+    next[2 * d.pair].begin = fr.begin;
+    next[2 * d.pair].len = run;
+    next[2 * d.pair + 1].begin = fr.begin + run;
+    next[2 * d.pair + 1].len = fr.len - run;
+  }
+}
+
+__global__ void __launch_bounds__(kPartThreads)
+    k_part_scatter(const Front* __restrict__ front, const Decision* __restrict__ dec,
+                   const PItem* __restrict__ items, const LevelState* __restrict__ ls,
+                   const uint32_t* __restrict__ dirbits, const uint32_t* __restrict__ item_left_off,
+                   const Front* __restrict__ next, const uint32_t* __restrict__ rows_in,
+                   int identity, uint32_t* __restrict__ rows_out) {
+  const int it = blockIdx.x;
+  if (it >= ls->n_items) return;
+  const PItem pi = items[it];
+  if (pi.kind != 1) return;
+  const Front fr = front[pi.k];
+  const Decision d = dec[pi.k];
+  const uint32_t L = next[2 * d.pair].len;
+  const uint32_t loff = item_left_off[it];
+  const uint32_t base_left = fr.begin + loff;
+  const uint32_t base_right = fr.begin + L + (pi.off - loff);
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  constexpr int kWarps = kPartThreads / 32;
+  __shared__ uint32_t s_cnt[kWarps];
+  uint32_t running = 0;
+  for (int j = 0; j < kTile / kPartThreads; ++j) {
+    const unsigned bal = dirbits[(uint64_t)it * kTileWords + j * kWarps + warp];
+    if (lane == 0) s_cnt[warp] = __popc(bal);
+    __syncthreads();
+    uint32_t before = running;
+    uint32_t blk = 0;
+    for (int w = 0; w < kWarps; ++w) {
+      const uint32_t cw = s_cnt[w];
+      if (w < warp) before += cw;
+      blk += cw;
+    }
+    before += __popc(bal & ((1u << lane) - 1u));
+    const uint32_t i = j * kPartThreads + threadIdx.x;
+    if (i < pi.len) {
+      const uint32_t at = fr.begin + pi.off + i;
+      const uint32_t row = identity ? at : rows_in[at];
+      if ((bal >> lane) & 1u) {
+        rows_out[base_left + (before - 0)] = row;
+      } else {
+        rows_out[base_right + (i - before)] = row;
+      }
+    }
+    running += blk;
+    __syncthreads();
+  }
+}
+
+// Histogram plan of the next level: for every split (not at the depth
+// limit) the child with the smaller Hessian sum is built, its sibling is
+// parent - built. Entries are in pair order with running row prefixes.
+__global__ void __launch_bounds__(kApplyThreads)
+    k_hist_plan(const Front* __restrict__ front, const Decision* __restrict__ dec,
+                const LevelState* __restrict__ ls, const Front* __restrict__ next,
+                HEntry* __restrict__ entries, Triple* __restrict__ pairs,
+                LevelState* __restrict__ ls_next, int terminal) {
+  using Scan = cub::BlockScan<unsigned long long, kApplyThreads>;
+  __shared__ typename Scan::TempStorage tmp;
+  const int k = threadIdx.x;
+  const int n_front = ls->n_front;
+  unsigned long long rows = 0;
+  HEntry en{};
+  Triple tr{};
+  bool active = false;
+  if (!terminal && k < n_front) {
+    const Decision d = dec[k];
+    if (d.split) {
+      active = true;
+      const Front l = next[2 * d.pair], r = next[2 * d.pair + 1];
+      const bool left_built = l.h <= r.h;
+      const Front& b = left_built ? l : r;
+      const Front& s = left_built ? r : l;
+      en.slot = b.slot;
+      en.identity = 0;
+      en.begin = b.begin;
+      en.len = b.len;
+      rows = b.len;
+      tr.parent = front[k].slot;
+      tr.built = b.slot;
+      tr.sibling = s.slot;
+    }
+  }
+  unsigned long long prefix = 0, total = 0;
+  Scan(tmp).ExclusiveSum(rows, prefix, total);
+  if (active) {
+    const int p = dec[k].pair;
+    en.prefix = prefix;
+    entries[p] = en;
+    pairs[p] = tr;
+  }
+  if (k == 0) {
+    const int n = terminal ? 0 : ls->n_split;
+    ls_next->n_hentries = n;
+    ls_next->n_pairs = n;
+    ls_next->hist_rows = total;
+  }
+}
+
+__global__ void k_root_setup(uint64_t n_rows, Front* front, HEntry* entries, LevelState* ls) {
+  Front f{};
+  f.node = 0;
+  f.slot = 0;
+  f.begin = 0;
+  f.len = (uint32_t)n_rows;
+  front[0] = f;
+  HEntry e{};
+  e.slot = 0;
+  e.identity = 1;
+  e.begin = 0;
+  e.len = (uint32_t)n_rows;
+  e.prefix = 0;
+  entries[0] = e;
+  ls->n_front = 1;
+  ls->n_nodes = 1;
+  ls->n_hentries = 1;
+  ls->hist_rows = n_rows;
+}
+
+__global__ void k_root_stats(Front* front, const long long* totals) {
+  front[0].g = totals[0];
+  front[0].h = totals[1];
+}
+
+__global__ void k_finish_tree(const hb_tree_node* __restrict__ tree, const LevelState* ls_last,
+                              hb_tree_node* __restrict__ forest, uint32_t* counts,
+                              int32_t* tree_counter, uint32_t max_nodes) {
+  const int t = *tree_counter;
+  const int n = ls_last->n_nodes;
+  for (int i = threadIdx.x; i < n; i += blockDim.x) forest[(uint64_t)t * max_nodes + i] = tree[i];
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    counts[t] = (uint32_t)n;
+    *tree_counter = t + 1;
+  }
+}
+
+__global__ void k_dequantize(const longlong2* __restrict__ hist, uint32_t n,
+                             const Scale* __restrict__ scale, double* __restrict__ out) {
+  const double ig = scale->ig, ih = scale->ih;
+  for (uint32_t i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) {
+    const longlong2 v = hist[i];
+    out[2 * i] = ll2d(v.x) * ig;
+    out[2 * i + 1] = ll2d(v.y) * ih;
+  }
+}
+
+__global__ void k_add_segment(const uint32_t* __restrict__ rows, uint32_t begin, uint32_t len,
+                              float value, float* __restrict__ margin) {
+  for (uint32_t i = blockIdx.x * blockDim.x + threadIdx.x; i < len; i += gridDim.x * blockDim.x) {
+    const uint32_t r = rows[begin + i];
+    margin[r] = __fadd_rn(margin[r], value);
+  }
+}
+
+}  // namespace
+
+// ---------------------------------------------------------------------------
+// Launchers.
+void launch_gradients(int kind, const float* margin, const float* label, const float* weight,
+                      float spw, float min_hess, uint64_t n, uint64_t vrows, float2* gpair,
+                      Scale* scale, int n_sm, cudaStream_t s) {
+  int grid = (int)std::min<uint64_t>((n + 255) / 256, (uint64_t)n_sm * 8);
+  if (grid < 1) grid = 1;
+  k_gradients<<<grid, 256, 0, s>>>(kind, margin, label, weight, spw, min_hess, n, vrows, gpair, scale);
+}
+
+void launch_pair_maxima(const float2* gpair, uint64_t n, Scale* scale, int n_sm, cudaStream_t s) {
+  int grid = (int)std::min<uint64_t>((n + 255) / 256, (uint64_t)n_sm * 8);
+  if (grid < 1) grid = 1;
+  k_pair_maxima<<<grid, 256, 0, s>>>(gpair, n, scale);
+}
+
+void launch_scale(Scale* scale, uint64_t global_rows, cudaStream_t s) {
+  k_scale<<<1, 1, 0, s>>>(scale, global_rows);
+}
+
+void launch_encode(const uint8_t* col, const uint64_t* colmiss, uint64_t n_rows, uint32_t n_cols,
+                   uint32_t stride, uint32_t mask_off, uint8_t* rec, cudaStream_t s) {
+  int grid = (int)std::min<uint64_t>((n_rows + 255) / 256, 4096);
+  if (grid < 1) grid = 1;
+  k_encode<<<grid, 256, 0, s>>>(col, colmiss, n_rows, n_cols, stride, mask_off, rec);
+}
+
+size_t hist_smem_bytes(const DevConst& c) { return (size_t)c.max_bins * 32 * 16; }
+
+int hist_grid(int n_sm) { return n_sm; }
+
+void launch_hist(const DevConst& c, const uint32_t* fo, const uint8_t* rec, const float2* gpair,
+                 const Scale* scale, const uint32_t* rows, const HEntry* entries,
+                 const LevelState* ls, longlong2* hist, long long* totals,
+                 unsigned long long* row_stats, int grid_x, size_t smem, cudaStream_t s) {
+  // The dynamic shared memory this launch needs, granted per device (the
+  // attribute is per device); the launch reports the error if it cannot be.
+  static size_t granted[64] = {0};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 0 || dev >= 64 || granted[dev] < smem) {
+    if (cudaFuncSetAttribute(k_hist, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) ==
+            cudaSuccess &&
+        dev >= 0 && dev < 64)
+      granted[dev] = smem;
+  }
+  dim3 grid(grid_x, c.n_groups);
+  k_hist<<<grid, kHistThreads, smem, s>>>(c, fo, rec, gpair, scale, rows, entries, ls, hist, totals,
+                                          row_stats);
+}
+
+void launch_subtract(const Triple* pairs, const LevelState* ls, int max_pairs, uint32_t total_bins,
+                     longlong2* hist, cudaStream_t s) {
+  uint64_t work = (uint64_t)max_pairs * total_bins;
+  int grid = (int)std::min<uint64_t>((work + 255) / 256, 148 * 16);
+  if (grid < 1) grid = 1;
+  k_subtract<<<grid, 256, 0, s>>>(pairs, ls, total_bins, hist);
+}
+
+void launch_scan(const DevConst& c, const uint32_t* fo, const longlong2* hist, const Front* front,
+                 const LevelState* ls, const Scale* scale, int max_front, Cand* cand,
+                 cudaStream_t s) {
+  uint64_t warps = (uint64_t)max_front * c.n_cols;
+  int grid = (int)((warps * 32 + 255) / 256);
+  k_scan<<<grid, 256, 0, s>>>(c, fo, hist, front, ls, scale, cand);
+}
+
+void launch_apply(const DevConst& c, const uint32_t* fo, const float* cuts, const Cand* cand,
+                  const Front* front, Front* next, Decision* dec, PItem* items, LevelState* ls,
+                  LevelState* ls_next, hb_tree_node* tree, const Scale* scale, int depth,
+                  int leaf_only, cudaStream_t s) {
+  k_apply<<<1, kApplyThreads, 0, s>>>(c, fo, cuts, cand, front, next, dec, items, ls, ls_next, tree,
+                                      scale, depth, leaf_only);
+}
+
+void launch_part_count(const DevConst& c, const uint8_t* col, const uint64_t* colmiss,
+                       const uint32_t* rows_in, int identity, const Front* front,
+                       const Decision* dec, const PItem* items, const LevelState* ls,
+                       int max_items, uint32_t* dirbits, uint32_t* item_left, float* margin,
+                       cudaStream_t s) {
+  k_part_count<<<max_items, kPartThreads, 0, s>>>(c, col, colmiss, rows_in, identity, front, dec,
+                                                  items, ls, dirbits, item_left, margin);
+}
+
+void launch_part_scan(const Front* front, const Decision* dec, const LevelState* ls, int max_front,
+                      const uint32_t* item_left, uint32_t* item_left_off, Front* next,
+                      cudaStream_t s) {
+  int grid = (max_front * 32 + 255) / 256;
+  k_part_scan<<<grid, 256, 0, s>>>(front, dec, ls, item_left, item_left_off, next);
+}
+
+void launch_part_scatter(const Front* front, const Decision* dec, const PItem* items,
+                         const LevelState* ls, int max_items, const uint32_t* dirbits,
+                         const uint32_t* item_left_off, const Front* next,
+                         const uint32_t* rows_in, int identity, uint32_t* rows_out,
+                         cudaStream_t s) {
+  k_part_scatter<<<max_items, kPartThreads, 0, s>>>(front, dec, items, ls, dirbits, item_left_off,
+                                                    next, rows_in, identity, rows_out);
+}
+
+void launch_hist_plan(const Front* front, const Decision* dec, const LevelState* ls,
+                      const Front* next, HEntry* entries, Triple* pairs, LevelState* ls_next,
+                      int terminal, cudaStream_t s) {
+  k_hist_plan<<<1, kApplyThreads, 0, s>>>(front, dec, ls, next, entries, pairs, ls_next, terminal);
+}
+
+void launch_root_setup(uint64_t n_rows, Front* front, HEntry* entries, LevelState* ls,
+                       cudaStream_t s) {
+  k_root_setup<<<1, 1, 0, s>>>(n_rows, front, entries, ls);
+}
+
+void launch_root_stats(Front* front, const long long* totals, cudaStream_t s) {
+  k_root_stats<<<1, 1, 0, s>>>(front, totals);
+}
+
+void launch_finish_tree(const hb_tree_node* tree, const LevelState* ls_last, hb_tree_node* forest,
+                        uint32_t* counts, int32_t* tree_counter, uint32_t max_nodes,
+                        cudaStream_t s) {
+  k_finish_tree<<<1, 256, 0, s>>>(tree, ls_last, forest, counts, tree_counter, max_nodes);
+}
+
+void launch_dequantize(const longlong2* hist, uint32_t n, const Scale* scale, double* out,
+                       cudaStream_t s) {
+  int grid = (int)std::min<uint32_t>((n + 255) / 256, 1024u);
+  if (grid < 1) grid = 1;
+  k_dequantize<<<grid, 256, 0, s>>>(hist, n, scale, out);
+}
+
+void launch_add_segment(const uint32_t* rows, uint32_t begin, uint32_t len, float value,
+                        float* margin, cudaStream_t s) {
+  int grid = (int)std::min<uint32_t>((len + 255) / 256, 2048u);
+  if (grid < 1) grid = 1;
+  k_add_segment<<<grid, 256, 0, s>>>(rows, begin, len, value, margin);
+}
+
+}  // namespace hb

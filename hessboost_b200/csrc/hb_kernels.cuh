@@ -1,0 +1,66 @@
+// Kernel launchers of the hist path (definitions in hb_kernels.cu).
+#pragma once
+
+#include <cuda_runtime.h>
+
+#include "hb_internal.h"
+
+namespace hb {
+
+// Objective gradients at `margin` (the host's bits, see hb_kernels.cu) plus
+// the largest |g|, |h| and a non-finite flag, folded into `scale`.
+void launch_gradients(int kind, const float* margin, const float* label, const float* weight,
+                      float spw, float min_hess, uint64_t n, uint64_t vrows, float2* gpair,
+                      Scale* scale, int n_sm, cudaStream_t s);
+// |g|, |h| maxima of staged pairs (HistogramBackend::prepare).
+void launch_pair_maxima(const float2* gpair, uint64_t n, Scale* scale, int n_sm, cudaStream_t s);
+// Fixed-point exponents from the (reduced) maxima and the global row count.
+void launch_scale(Scale* scale, uint64_t global_rows, cudaStream_t s);
+// Feature-major bins (+ bitmap) -> row-major records.
+void launch_encode(const uint8_t* col, const uint64_t* colmiss, uint64_t n_rows, uint32_t n_cols,
+                   uint32_t stride, uint32_t mask_off, uint8_t* rec, cudaStream_t s);
+// Histograms of `entries` (level state `ls`) into `hist`; with `totals`
+// non-null also the fixed-point (g, h) totals of the rows.
+void launch_hist(const DevConst& c, const uint32_t* fo, const uint8_t* rec, const float2* gpair,
+                 const Scale* scale, const uint32_t* rows, const HEntry* entries,
+                 const LevelState* ls, longlong2* hist, long long* totals,
+                 unsigned long long* row_stats, int grid_x, size_t smem, cudaStream_t s);
+size_t hist_smem_bytes(const DevConst& c);
+int hist_grid(int n_sm);
+void launch_subtract(const Triple* pairs, const LevelState* ls, int max_pairs, uint32_t total_bins,
+                     longlong2* hist, cudaStream_t s);
+void launch_scan(const DevConst& c, const uint32_t* fo, const longlong2* hist, const Front* front,
+                 const LevelState* ls, const Scale* scale, int max_front, Cand* cand,
+                 cudaStream_t s);
+void launch_apply(const DevConst& c, const uint32_t* fo, const float* cuts, const Cand* cand,
+                  const Front* front, Front* next, Decision* dec, PItem* items, LevelState* ls,
+                  LevelState* ls_next, hb_tree_node* tree, const Scale* scale, int depth,
+                  int leaf_only, cudaStream_t s);
+void launch_part_count(const DevConst& c, const uint8_t* col, const uint64_t* colmiss,
+                       const uint32_t* rows_in, int identity, const Front* front,
+                       const Decision* dec, const PItem* items, const LevelState* ls,
+                       int max_items, uint32_t* dirbits, uint32_t* item_left, float* margin,
+                       cudaStream_t s);
+void launch_part_scan(const Front* front, const Decision* dec, const LevelState* ls, int max_front,
+                      const uint32_t* item_left, uint32_t* item_left_off, Front* next,
+                      cudaStream_t s);
+void launch_part_scatter(const Front* front, const Decision* dec, const PItem* items,
+                         const LevelState* ls, int max_items, const uint32_t* dirbits,
+                         const uint32_t* item_left_off, const Front* next,
+                         const uint32_t* rows_in, int identity, uint32_t* rows_out,
+                         cudaStream_t s);
+void launch_hist_plan(const Front* front, const Decision* dec, const LevelState* ls,
+                      const Front* next, HEntry* entries, Triple* pairs, LevelState* ls_next,
+                      int terminal, cudaStream_t s);
+void launch_root_setup(uint64_t n_rows, Front* front, HEntry* entries, LevelState* ls,
+                       cudaStream_t s);
+void launch_root_stats(Front* front, const long long* totals, cudaStream_t s);
+void launch_finish_tree(const hb_tree_node* tree, const LevelState* ls_last, hb_tree_node* forest,
+                        uint32_t* counts, int32_t* tree_counter, uint32_t max_nodes,
+                        cudaStream_t s);
+void launch_dequantize(const longlong2* hist, uint32_t n, const Scale* scale, double* out,
+                       cudaStream_t s);
+void launch_add_segment(const uint32_t* rows, uint32_t begin, uint32_t len, float value,
+                        float* margin, cudaStream_t s);
+
+}  // namespace hb

@@ -1,0 +1,320 @@
+/*
+ * hb_backend.h -- C ABI of the B200 hist backend (libhb_cuda.so).
+ *
+ * One function per method of hessboost's histogram backend seam, with the
+ * same meaning, so the Rust side (`CudaHistBackend` in hessboost 0.4.9)
+ * could bind it with `extern "C"` unchanged:
+ *
+ *   trait HistogramBackend   src/tree/hist/mod.rs:73-105
+ *   trait RowEngine          src/tree/hist/mod.rs:213-295
+ *   CudaHistBackend          src/backend/cuda/mod.rs:1445 (new :1626, upload :1687)
+ *   BoostedModel::to_cuda    src/backend/cuda/predict.rs:501
+ *   GpuModel::predict_margin src/backend/cuda/predict.rs:401
+ *
+ * plus entry points the reference does not have: whole-tree growth on the
+ * device (`hb_grow_tree`, `hb_train`), the row-sharded communicator
+ * (`hb_comm_*`) and the host binning helpers (`hb_cuts_dense`,
+ * `hb_bin_dense`).
+ *
+ * Conventions (the reference's, src/tree/hist/mod.rs:107-212):
+ *   - every call returns an hb_status; HB_REFUSED means "did not run"
+ *     (the trait's `None`): the caller keeps its host path;
+ *     HB_DEVICE_FAILED is sticky: after a CUDA or NCCL error every later
+ *     call on the engine is refused;
+ *   - the caller owns every host buffer and passes pointers and lengths; the
+ *     engine copies what it keeps;
+ *   - segments carry their tree's stamp; a segment from an earlier tree is
+ *     refused;
+ *   - calls on one engine must not overlap (one calling thread at a time);
+ *     different engines are independent.
+ *
+ * Histograms are summed in int64 fixed point: each tree's gradients are
+ * rounded once to multiples of 2^-s (s per component, chosen from the
+ * largest magnitude and the row count so no sum can overflow 2^62) and every
+ * sum is then exact, so a histogram does not depend on row order, block
+ * order or GPU count. The f64 values returned are those exact sums rounded
+ * once to f64.
+ */
+#ifndef HB_BACKEND_H
+#define HB_BACKEND_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef int32_t hb_status;
+#define HB_OK 0
+#define HB_REFUSED 1
+#define HB_DEVICE_FAILED 2
+#define HB_INVALID_ARGUMENT 3
+
+typedef struct hb_engine hb_engine;
+typedef struct hb_predictor hb_predictor;
+
+/* GradStats (src/tree/gain.rs:21). */
+typedef struct hb_grad_stats {
+  double grad;
+  double hess;
+} hb_grad_stats;
+
+/* GradPair (src/objective/mod.rs). */
+typedef struct hb_grad_pair {
+  float grad;
+  float hess;
+} hb_grad_pair;
+
+/* Segment (src/tree/hist/mod.rs:115): `len` ascending row ids at `offset`
+ * of the engine's row buffer. */
+typedef struct hb_segment {
+  uint64_t offset;
+  uint64_t len;
+  uint32_t contiguous;
+  uint32_t reserved;
+  uint64_t tree;
+} hb_segment;
+
+/* RowSplit (src/tree/hist/mod.rs:183) with RowRule::Below(limit): present
+ * feature-local bins below `limit` go left, missing values follow
+ * `default_left`. */
+typedef struct hb_row_split {
+  hb_segment seg;
+  uint32_t feature;
+  uint32_t limit;
+  uint32_t default_left;
+  uint32_t reserved;
+} hb_row_split;
+
+/* Partitioned (src/tree/hist/mod.rs:196). */
+typedef struct hb_partitioned {
+  hb_segment left;
+  hb_segment right;
+} hb_partitioned;
+
+/* RegParams (src/tree/gain.rs:62), every value already rounded to f32. */
+typedef struct hb_reg_params {
+  double lambda;
+  double alpha;
+  double max_delta_step;
+  double min_child_weight;
+} hb_reg_params;
+
+/* ScanRequest (src/tree/hist/mod.rs:303) for numeric features without
+ * monotone constraints: `features` lists the features to scan. */
+typedef struct hb_scan_request {
+  uint32_t slot;
+  uint32_t n_features;
+  const uint32_t* features;
+  hb_grad_stats total;
+  float root_gain;
+  float lower;
+  float upper;
+  uint32_t reserved;
+} hb_scan_request;
+
+#define HB_SCAN_EMPTY 0
+#define HB_SCAN_REPLAY 1
+#define HB_SCAN_NUMERIC 2
+/* NodeScan (src/tree/hist/mod.rs:327): the winning numeric split of a node
+ * after the feature-order merge; `acc` is the pass's accumulated statistics
+ * (the left child for a forward pass, the right child for a backward one). */
+typedef struct hb_node_scan {
+  uint32_t kind;
+  uint32_t feature;
+  float loss_chg;
+  uint32_t backward;
+  uint32_t offset;
+  uint32_t reserved;
+  hb_grad_stats acc;
+} hb_node_scan;
+
+#define HB_LOSS_SQUARED_ERROR 0
+#define HB_LOSS_LOGISTIC 1
+/* DeviceLoss (src/tree/hist/mod.rs:352). */
+typedef struct hb_device_loss {
+  int32_t kind;
+  float scale_pos_weight;
+  float min_hess;
+  int32_t reserved;
+} hb_device_loss;
+
+/* The binned matrix the backend uploads (GHistIndex, src/data/ghist.rs:195):
+ * every feature's local bins, feature-major, one byte each (features of at
+ * most 256 bins), and the missing bitmap of an index with missing entries. */
+typedef struct hb_ghist {
+  uint64_t n_rows;
+  uint32_t n_cols;
+  uint32_t dense;                 /* every row holds every feature */
+  const uint32_t* feature_offset; /* n_cols + 1 */
+  const float* cut_values;        /* feature_offset[n_cols] */
+  const uint8_t* columns;         /* bins[f * n_rows + r] */
+  const uint64_t* missing;        /* NULL, or bit r%64 of word f*ceil(n_rows/64) + r/64 */
+} hb_ghist;
+
+/* One tree node: the reference's Node (src/tree/regtree.rs:37) plus the
+ * split's global bin (-1: below every bin). 40 bytes. */
+typedef struct hb_tree_node {
+  int32_t left;
+  int32_t right;
+  uint32_t split_feature;
+  float split_cond;
+  uint32_t default_left;
+  float leaf_value;
+  float sum_hess;
+  float split_gain;
+  int32_t split_bin;
+  uint32_t reserved;
+} hb_tree_node;
+
+#define HB_GROW_DEPTHWISE 0
+#define HB_GROW_LOSSGUIDE 1
+/* The TrainingParams fields the hist path reads (src/config/params.rs:653). */
+typedef struct hb_train_params {
+  int32_t objective;        /* HB_LOSS_* */
+  int32_t max_depth;        /* 0: unlimited */
+  int32_t max_leaves;       /* 0: unlimited */
+  int32_t grow_policy;      /* HB_GROW_* */
+  float eta;
+  float lambda;
+  float alpha;
+  float gamma;
+  float min_child_weight;
+  float max_delta_step;
+  float scale_pos_weight;
+  float base_score;         /* NaN: estimate from the labels */
+} hb_train_params;
+
+/* ---- engine (CudaHistBackend::new + upload) ------------------------- */
+hb_status hb_engine_create(int32_t device_ordinal, hb_engine** out);
+hb_status hb_engine_destroy(hb_engine* e);
+/* CudaHistBackend::upload (src/backend/cuda/mod.rs:1687). */
+hb_status hb_engine_upload(hb_engine* e, const hb_ghist* ghist);
+/* Human-readable text of the engine's last error (static storage). */
+const char* hb_engine_last_error(const hb_engine* e);
+
+/* ---- HistogramBackend (src/tree/hist/mod.rs:73) -------------------- */
+/* `prepare`: stage this tree's gradients (one pair per row). */
+hb_status hb_prepare(hb_engine* e, const hb_grad_pair* gpair, uint64_t n_rows);
+/* `build`: the histogram of `rows` (ascending) into out[total_bins]. */
+hb_status hb_build(hb_engine* e, const uint32_t* rows, uint64_t n, hb_grad_stats* out);
+/* `build_features`: every bin is built; the feature list only says which
+ * bins the caller reads. */
+hb_status hb_build_features(hb_engine* e, const uint32_t* rows, uint64_t n,
+                            const uint32_t* features, uint32_t n_features, hb_grad_stats* out);
+
+/* ---- RowEngine (src/tree/hist/mod.rs:213) -------------------------- */
+hb_status hb_begin_tree(hb_engine* e, const uint32_t* rows, uint64_t n, hb_segment* root);
+hb_status hb_root_total(hb_engine* e, const hb_segment* seg, hb_grad_stats* out);
+hb_status hb_partition(hb_engine* e, const hb_row_split* splits, uint32_t n,
+                       hb_partitioned* out);
+/* `histograms`: out[k * total_bins + bin] for the k-th segment. */
+hb_status hb_histograms(hb_engine* e, const hb_segment* segs, uint32_t n, hb_grad_stats* out);
+/* `rows`: the row ids of each segment, back to back. */
+hb_status hb_rows(hb_engine* e, const hb_segment* segs, uint32_t n, uint32_t* out);
+hb_status hb_load_margins(hb_engine* e, const float* margins, uint64_t n);
+/* `gradients`: the loss's pairs at the device margins; *all_finite as the
+ * trait's bool. */
+hb_status hb_gradients(hb_engine* e, const hb_device_loss* loss, const float* labels,
+                       const float* weights, uint64_t n, int32_t* all_finite);
+hb_status hb_add_leaf_values(hb_engine* e, const hb_segment* segs, const float* values,
+                             uint32_t n);
+hb_status hb_read_margins(hb_engine* e, float* out, uint64_t n);
+hb_status hb_reserve_hists(hb_engine* e, uint32_t slots, int32_t* reserved);
+/* `build_resident`: build nodes[k] into slots[k], then for each pair
+ * (siblings[2j] = parent, siblings[2j+1] = built) turn the parent slot into
+ * parent - built. */
+hb_status hb_build_resident(hb_engine* e, const hb_segment* segs, const uint32_t* slots,
+                            uint32_t n, const uint32_t* siblings, uint32_t n_siblings);
+hb_status hb_scan_resident(hb_engine* e, const hb_reg_params* reg,
+                           const hb_scan_request* requests, uint32_t n, hb_node_scan* out);
+hb_status hb_read_hist(hb_engine* e, uint32_t slot, hb_grad_stats* out);
+/* Diagnostics (src/backend/cuda/diagnostics.rs): the staged gradient pairs
+ * and the fixed-point exponents (sg, sh) of the current tree. */
+hb_status hb_read_gradients(hb_engine* e, hb_grad_pair* out, uint64_t n, int32_t* sg, int32_t* sh);
+
+/* ---- whole-tree growth on the device (no reference counterpart) ---- */
+/* Grow one tree from the device gradients (hb_gradients or hb_prepare)
+ * with every row, the host builder's semantics (HistTreeBuilder,
+ * src/tree/builder/hist/mod.rs:261), add its eta-scaled leaves to the
+ * device margins, and return its nodes. */
+hb_status hb_grow_tree(hb_engine* e, const hb_train_params* p, hb_tree_node* nodes,
+                       uint32_t nodes_cap, uint32_t* n_nodes);
+/* `rounds` boosting rounds (train_trees, src/training/train.rs:222) of a
+ * single-output objective from `base_margin`: hb_train_begin then
+ * hb_train_rounds. */
+hb_status hb_train(hb_engine* e, const hb_train_params* p, const float* labels, uint64_t n,
+                   float base_margin, int32_t rounds, hb_tree_node* nodes, uint64_t nodes_cap,
+                   uint64_t* tree_ptr);
+/* Start a training run: stage the labels and set every device margin to
+ * `base_margin`. */
+hb_status hb_train_begin(hb_engine* e, const float* labels, uint64_t n, float base_margin);
+/* Continue the run by `rounds` rounds (gradients at the device margins, one
+ * tree grown on the device, its leaves added to the margins), writing the
+ * rounds' trees back to back: tree t at nodes[tree_ptr[t] .. tree_ptr[t+1]). */
+hb_status hb_train_rounds(hb_engine* e, const hb_train_params* p, int32_t rounds,
+                          hb_tree_node* nodes, uint64_t nodes_cap, uint64_t* tree_ptr);
+
+/* Counters of the engine since the last hb_engine_reset_stats: device time
+ * per kernel family (CUDA events on the engine's stream, recorded only when
+ * `timing` was switched on), kernel launches, and rows the histogram kernel
+ * built with and without a row list. */
+#define HB_TIMERS 8 /* gradients, root hist, scan, apply, partition, hist, subtract, other */
+typedef struct hb_engine_stats {
+  double ms[HB_TIMERS];
+  uint64_t timed_launches[HB_TIMERS];
+  uint64_t kernel_launches;
+  uint64_t rows_built_contiguous;
+  uint64_t rows_built_gathered;
+  uint64_t rounds;
+} hb_engine_stats;
+hb_status hb_engine_reset_stats(hb_engine* e, int32_t timing);
+hb_status hb_engine_get_stats(hb_engine* e, hb_engine_stats* out);
+/* The engine's CUDA stream (a cudaStream_t), for callers that order their
+ * own work or events against it. */
+hb_status hb_engine_stream(hb_engine* e, void** stream);
+
+/* ---- row sharding over several GPUs (no reference counterpart) ------ */
+/* The engine holds rows [row_begin, row_begin + n_rows) of a matrix of
+ * `global_rows`; histograms, totals and scales are summed (max-reduced)
+ * over every rank with NCCL, so each rank grows the same tree. */
+/* Declare this engine's shard before hb_engine_upload: its first row's
+ * global index (a multiple of 8, so the logistic gradient's 8-row vectors
+ * line up with the whole matrix's) and the matrix's total row count. */
+hb_status hb_engine_set_shard(hb_engine* e, uint64_t row_begin, uint64_t global_rows);
+hb_status hb_comm_unique_id(uint8_t id[128]);
+hb_status hb_comm_init(hb_engine* e, int32_t nranks, int32_t rank, const uint8_t id[128],
+                       uint64_t global_rows);
+
+/* ---- prediction (BoostedModel::to_cuda / GpuModel) ----------------- */
+hb_status hb_predictor_create(int32_t device_ordinal, const hb_tree_node* nodes,
+                              const uint64_t* tree_ptr, uint64_t n_trees,
+                              const uint32_t* tree_output, const float* tree_weight,
+                              int32_t n_outputs, const float* base, uint32_t n_features,
+                              hb_predictor** out);
+hb_status hb_predictor_destroy(hb_predictor* p);
+/* Host rows in, host margins out (row-major, n_outputs per row). */
+hb_status hb_predict_margin(hb_predictor* p, const float* rows, uint64_t n_rows, float* out);
+/* Device rows in, device margins out, on `stream` (a cudaStream_t; NULL =
+ * the predictor's stream). */
+hb_status hb_predict_margin_device(hb_predictor* p, const float* d_rows, uint64_t n_rows,
+                                   float* d_out, void* stream);
+
+/* ---- host binning (HistCuts::from_dmatrix, GHistIndex::from_dmatrix) */
+/* Cuts of a dense row-major f32 matrix (NaN missing); *total = bin count.
+ * HB_REFUSED when `cap` is too small. */
+hb_status hb_cuts_dense(const float* x, uint64_t n_rows, uint32_t n_cols, uint32_t max_bin,
+                        uint32_t* feature_offset, float* cut_values, uint64_t cap,
+                        uint64_t* total);
+/* Feature-local one-byte bins (feature-major) and the missing bitmap;
+ * *dense = 1 when no cell is missing. HB_REFUSED when a feature has more
+ * than 256 bins. */
+hb_status hb_bin_dense(const float* x, uint64_t n_rows, uint32_t n_cols,
+                       const uint32_t* feature_offset, const float* cut_values,
+                       uint8_t* columns, uint64_t* missing, int32_t* dense);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* HB_BACKEND_H */

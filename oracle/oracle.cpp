@@ -750,14 +750,20 @@ void orc_intercepts(int32_t objective, const float* labels, uint64_t n, int32_t 
 
 int32_t orc_fixed_scale(float max_abs, uint64_t n) { return fixed_scale(max_abs, n); }
 
-int64_t orc_train(const orc_params* pp, const float* x, uint64_t n, uint64_t nc,
-                  const float* labels, int32_t rounds, orc_node* nodes, uint64_t nodes_cap,
-                  uint64_t* tree_ptr, float* base_out, float* margins_out) {
-  if (!pp || !x || !labels || n == 0 || nc == 0 || rounds < 0) return -2;
-#ifdef _OPENMP
-  if (pp->n_threads > 0) omp_set_num_threads(pp->n_threads);
-#endif
-  Params p;
+}  // extern "C"
+
+struct orc_trainer {
+  orc::Params p;
+  orc::Index ix;
+  std::vector<float> base, margins, labels;
+  size_t n = 0;
+  int k = 1;
+};
+
+namespace {
+
+orc::Params params_from(const orc_params* pp) {
+  orc::Params p;
   p.objective = pp->objective;
   p.n_outputs = pp->objective == 1 ? 1 : std::max(1, pp->n_outputs);
   p.max_depth = pp->max_depth;
@@ -772,20 +778,17 @@ int64_t orc_train(const orc_params* pp, const float* x, uint64_t n, uint64_t nc,
   p.mds = (double)pp->max_delta_step;
   p.spw = pp->scale_pos_weight;
   p.fixed = pp->fixed_point != 0;
-  const int k = p.n_outputs;
+  return p;
+}
 
-  Index ix = make_index(x, n, nc, cuts_from_dense(x, n, nc, nullptr, (size_t)p.max_bin, NAN));
-
-  std::vector<float> base(k);
-  if (std::isnan(pp->base_score)) {
-    orc_intercepts(p.objective, labels, n, k, base.data());
-  } else {
-    for (int t = 0; t < k; ++t) base[t] = p.objective == 1 ? logistic_link(pp->base_score) : pp->base_score;
-  }
-  std::vector<float> margins(n * k);
-  for (size_t r = 0; r < n; ++r)
-    for (int t = 0; t < k; ++t) margins[r * k + t] = base[t];
-
+// `rounds` rounds of train_trees (src/training/train.rs:222) from the
+// trainer's margins.
+int64_t run_rounds(orc_trainer* tr, int rounds, orc_node* nodes, uint64_t nodes_cap,
+                   uint64_t* tree_ptr) {
+  using namespace orc;
+  const Params& p = tr->p;
+  const size_t n = tr->n;
+  const int k = tr->k;
   std::vector<GradPair> gp(n), gp_all(n * k);
   std::vector<float> mk(n), yk(n);
   std::vector<IS> q(n);
@@ -796,8 +799,8 @@ int64_t orc_train(const orc_params* pp, const float* x, uint64_t n, uint64_t nc,
     // 1. Gradients of every output from this round's margins (round.rs:253).
     for (int t = 0; t < k; ++t) {
       for (size_t r = 0; r < n; ++r) {
-        mk[r] = margins[r * k + t];
-        yk[r] = labels[r * k + t];
+        mk[r] = tr->margins[r * k + t];
+        yk[r] = tr->labels[r * k + t];
       }
       if (p.objective == 1)
         logistic_gradient(mk.data(), yk.data(), n, p.spw, gp.data());
@@ -825,10 +828,10 @@ int64_t orc_train(const orc_params* pp, const float* x, uint64_t n, uint64_t nc,
           q[r].grad = std::llrint((double)gp[r].grad * fg);
           q[r].hess = std::llrint((double)gp[r].hess * fh);
         }
-        Builder<FixMode> b(ix, p, mode);
+        Builder<FixMode> b(tr->ix, p, mode);
         tree = b.grow(q.data(), leaves);
       } else {
-        Builder<F64Mode> b(ix, p, F64Mode{});
+        Builder<F64Mode> b(tr->ix, p, F64Mode{});
         tree = b.grow(gp.data(), leaves);
       }
       // round.rs:143 `scale_leaves(eta)` (leaves only, regtree.rs:599).
@@ -837,7 +840,7 @@ int64_t orc_train(const orc_params* pp, const float* x, uint64_t n, uint64_t nc,
         if (nd.left == -1) nd.leaf_value = nd.leaf_value * eta;
       for (auto& lr : leaves) {
         float v = tree.nodes[lr.first].leaf_value;
-        for (uint32_t r : lr.second) margins[(size_t)r * k + t] += v;
+        for (uint32_t r : lr.second) tr->margins[(size_t)r * k + t] += v;
       }
       if (used + tree.nodes.size() > nodes_cap) return -1;
       std::copy(tree.nodes.begin(), tree.nodes.end(), nodes + used);
@@ -846,9 +849,59 @@ int64_t orc_train(const orc_params* pp, const float* x, uint64_t n, uint64_t nc,
       tree_ptr[n_trees] = used;
     }
   }
-  std::copy(base.begin(), base.end(), base_out);
-  if (margins_out) std::copy(margins.begin(), margins.end(), margins_out);
   return n_trees;
+}
+
+}  // namespace
+
+extern "C" {
+
+orc_trainer* orc_trainer_new(const orc_params* pp, const float* x, uint64_t n, uint64_t nc,
+                             const float* labels) {
+  using namespace orc;
+  if (!pp || !x || !labels || n == 0 || nc == 0) return nullptr;
+#ifdef _OPENMP
+  if (pp->n_threads > 0) omp_set_num_threads(pp->n_threads);
+#endif
+  orc_trainer* tr = new orc_trainer();
+  tr->p = params_from(pp);
+  tr->n = n;
+  tr->k = tr->p.n_outputs;
+  const int k = tr->k;
+  tr->ix = make_index(x, n, nc, cuts_from_dense(x, n, nc, nullptr, (size_t)tr->p.max_bin, NAN));
+  tr->labels.assign(labels, labels + n * k);
+  tr->base.assign(k, 0.0f);
+  if (std::isnan(pp->base_score)) {
+    orc_intercepts(tr->p.objective, labels, n, k, tr->base.data());
+  } else {
+    for (int t = 0; t < k; ++t)
+      tr->base[t] = tr->p.objective == 1 ? logistic_link(pp->base_score) : pp->base_score;
+  }
+  tr->margins.resize(n * k);
+  for (size_t r = 0; r < n; ++r)
+    for (int t = 0; t < k; ++t) tr->margins[r * k + t] = tr->base[t];
+  return tr;
+}
+
+int64_t orc_trainer_rounds(orc_trainer* tr, int32_t rounds, orc_node* nodes, uint64_t nodes_cap,
+                           uint64_t* tree_ptr) {
+  if (!tr || rounds < 0 || !tree_ptr) return -2;
+  return run_rounds(tr, rounds, nodes, nodes_cap, tree_ptr);
+}
+
+void orc_trainer_free(orc_trainer* tr) { delete tr; }
+
+int64_t orc_train(const orc_params* pp, const float* x, uint64_t n, uint64_t nc,
+                  const float* labels, int32_t rounds, orc_node* nodes, uint64_t nodes_cap,
+                  uint64_t* tree_ptr, float* base_out, float* margins_out) {
+  if (!pp || !x || !labels || n == 0 || nc == 0 || rounds < 0) return -2;
+  orc_trainer* tr = orc_trainer_new(pp, x, n, nc, labels);
+  if (!tr) return -2;
+  int64_t got = run_rounds(tr, rounds, nodes, nodes_cap, tree_ptr);
+  std::copy(tr->base.begin(), tr->base.end(), base_out);
+  if (margins_out && got >= 0) std::copy(tr->margins.begin(), tr->margins.end(), margins_out);
+  orc_trainer_free(tr);
+  return got;
 }
 
 void orc_predict(const orc_node* nodes, const uint64_t* tree_ptr, uint64_t n_trees,

@@ -73,6 +73,16 @@ int64_t orc_train(const orc_params* p, const float* x, uint64_t n, uint64_t n_co
                   const float* labels, int32_t rounds, orc_node* nodes, uint64_t nodes_cap,
                   uint64_t* tree_ptr, float* base_out, float* margins_out);
 
+/* A training session: cuts, binning and intercepts once (orc_trainer_new),
+ * then rounds from the session's margins (orc_trainer_rounds), so the rounds
+ * can be timed alone. */
+typedef struct orc_trainer orc_trainer;
+orc_trainer* orc_trainer_new(const orc_params* p, const float* x, uint64_t n, uint64_t n_cols,
+                             const float* labels);
+int64_t orc_trainer_rounds(orc_trainer* t, int32_t rounds, orc_node* nodes, uint64_t nodes_cap,
+                           uint64_t* tree_ptr);
+void orc_trainer_free(orc_trainer* t);
+
 /* Raw margins: base + sum over trees in order of weight * leaf, tree t
  * adding to output tree_output[t] (NULL: t % n_outputs) with weight
  * tree_weight[t] (NULL: 1). */

@@ -305,8 +305,10 @@ Cuts cuts_from_dense(const float* x, size_t n_rows, size_t n_cols, const float* 
                      size_t max_bin, float missing) {
   Cuts cuts;
   cuts.feature_offset.push_back(0);
-  std::vector<float> out;
-  for (size_t f = 0; f < n_cols; ++f) {
+  std::vector<std::vector<float>> per(n_cols);
+  // Features are independent sketches (quantile.rs:188 runs them in parallel too).
+#pragma omp parallel for schedule(dynamic, 1)
+  for (long long f = 0; f < (long long)n_cols; ++f) {
     size_t present = 0;
     for (size_t r = 0; r < n_rows; ++r) present += !is_missing(x[r * n_cols + f], missing);
     WQSketch sketch(present, max_bin, weights == nullptr);
@@ -315,9 +317,10 @@ Cuts cuts_from_dense(const float* x, size_t n_rows, size_t n_cols, const float* 
       if (is_missing(v, missing)) continue;
       sketch.push(v, weights ? weights[r] : 1.0f);
     }
-    out.clear();
-    sketch.cut_values(out);
-    cuts.values.insert(cuts.values.end(), out.begin(), out.end());
+    sketch.cut_values(per[f]);
+  }
+  for (size_t f = 0; f < n_cols; ++f) {
+    cuts.values.insert(cuts.values.end(), per[f].begin(), per[f].end());
     cuts.feature_offset.push_back((uint32_t)cuts.values.size());
   }
   return cuts;

