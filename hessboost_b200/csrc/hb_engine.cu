@@ -7,6 +7,7 @@
 #include <algorithm>
 #include <cmath>
 #include <cstdio>
+#include <cstdlib>
 #include <cstring>
 #include <string>
 #include <vector>
@@ -463,6 +464,10 @@ hb_status hb_engine_upload(hb_engine* e, const hb_ghist* g) {
   c.stride = (c.mask_off + 4 * ((g->n_cols + 31) / 32) + 15) / 16 * 16;
   c.dense = g->dense ? 1 : 0;
   c.n_groups = (g->n_cols + kGroupFeatures - 1) / kGroupFeatures;
+  // Both histogram kernels give the same exact sums; HB_HIST_KERNEL=64
+  // selects the 64-bit-atomic one for every size (comparison runs).
+  const char* hk = std::getenv("HB_HIST_KERNEL");
+  c.hist64 = (hk && std::strcmp(hk, "64") == 0) ? 1u : 0u;
   e->h_cuts.assign(g->cut_values, g->cut_values + c.total_bins);
   e->has_missing = g->missing != nullptr;
 

@@ -52,6 +52,7 @@ struct DevConst {
   uint32_t mask_off;      // byte offset of the mask words in a record
   uint32_t dense;         // index-level: no missing cell anywhere
   uint32_t n_groups;      // feature groups of kGroupFeatures
+  uint32_t hist64;        // 1: always the 64-bit-atomic histogram kernel
   // training parameters (RegParams rounded to f32 then widened)
   double lambda, alpha, gamma, mcw, mds;
   float eta;

@@ -5,9 +5,12 @@
 // only fused multiply-adds are the explicit __fmaf_rn of the reference's
 // own vector exponential.
 #include <cub/block/block_scan.cuh>
+#include <cuda_pipeline.h>
 #include <cub/block/block_reduce.cuh>
 
+#include <algorithm>
 #include <cfloat>
+#include <cstdlib>
 #include <climits>
 #include <cmath>
 
@@ -313,6 +316,223 @@ __global__ void __launch_bounds__(kHistThreads, 1)
     __syncthreads();
     long long sht = BR(tmp).Sum(th);
     if (threadIdx.x == 0) {
+      atomicAdd(reinterpret_cast<unsigned long long*>(&totals[0]), (unsigned long long)sgt);
+      atomicAdd(reinterpret_cast<unsigned long long*>(&totals[1]), (unsigned long long)sht);
+    }
+  }
+}
+
+// The same histograms with 32-bit shared atomics, which B200 shared memory
+// executes several times faster than 64-bit ones. Each fixed-point value q
+// (|q| <= 2^(62-c), c = ceil(log2 rows)) is split as q = hi * 2^K + lo with
+// 0 <= lo < 2^K; a bin keeps four 32-bit sums (lo and hi of g and of h) in
+// shared memory. Both stay exact for R = 2^r rows, K = ceil((64-c)/2),
+// r = min(32-K, c+K-32): R * (2^K - 1) < 2^32 and R * 2^(62-c-K) <= 2^30.
+// Every R rows the CTA folds them into int64 sums held in registers (each
+// thread owns kSlotsPerThread slots), and at the end of an entry adds those
+// to the global int64 histogram. Lane l starts at feature l, and the
+// record is rotated by l bytes once per row, so step s reads byte s.
+constexpr int kH32Threads = 512;
+constexpr int kSlotsPerThread = 16;  // 256 bins x 32 feature slots / 512 threads
+constexpr int kStages = 3;           // rows staged ahead with cp.async
+
+// Staging of one pass of rows (one row per thread): the group's 32 record
+// bytes, the (g, h) pair and the group's missing-mask word.
+struct StageRow {
+  uint4 a, b;
+};
+
+__global__ void __launch_bounds__(kH32Threads, 1)
+    k_hist32(DevConst c, const uint32_t* __restrict__ fo, const uint8_t* __restrict__ rec,
+             const float2* __restrict__ gpair, const Scale* __restrict__ scale,
+             const uint32_t* __restrict__ rows, const HEntry* __restrict__ entries,
+             const LevelState* __restrict__ ls, longlong2* __restrict__ hist,
+             long long* __restrict__ totals, unsigned long long* __restrict__ row_stats, int lo_bits,
+             int flush_rows) {
+  extern __shared__ __align__(16) uint32_t s32[];
+  const int n_entries = ls->n_hentries;
+  const uint64_t total = ls->hist_rows;
+  if (n_entries <= 0 || total == 0) return;
+  if (row_stats && blockIdx.x == 0 && blockIdx.y == 0 && threadIdx.x == 0)
+    atomicAdd(&row_stats[entries[0].identity ? 0 : 1], (unsigned long long)total);
+  const uint64_t per = (total + gridDim.x - 1) / gridDim.x;
+  const uint64_t a = (uint64_t)blockIdx.x * per;
+  const uint64_t b = min(total, a + per);
+  if (a >= b) return;
+
+  const int g = blockIdx.y;
+  const int f0 = g * kGroupFeatures;
+  const int nf = min(kGroupFeatures, (int)c.n_cols - f0);
+  const int nslots = (int)c.max_bins * 32;
+  uint32_t* lo_g = s32;
+  uint32_t* hi_g = s32 + nslots;
+  uint32_t* lo_h = s32 + 2 * nslots;
+  uint32_t* hi_h = s32 + 3 * nslots;
+  StageRow* srec = reinterpret_cast<StageRow*>(s32 + 4 * nslots);        // [kStages][threads]
+  float2* sgp = reinterpret_cast<float2*>(srec + kStages * kH32Threads);  // [kStages][threads]
+  uint32_t* smask = reinterpret_cast<uint32_t*>(sgp + kStages * kH32Threads);
+  for (int i = threadIdx.x; i < 4 * nslots; i += blockDim.x) s32[i] = 0u;
+
+  long long acc_g[kSlotsPerThread], acc_h[kSlotsPerThread];
+#pragma unroll
+  for (int j = 0; j < kSlotsPerThread; ++j) acc_g[j] = acc_h[j] = 0;
+  __syncthreads();
+
+  const double fg = scale->fg, fh = scale->fh;
+  const int tid = threadIdx.x;
+  const int lane = tid & 31;
+  const bool wide = c.stride >= (uint32_t)(32 * g + 32);
+  const uint32_t mask_at = c.mask_off + 4 * g;
+  const bool mask_in_block = mask_at >= (uint32_t)(32 * g) && mask_at + 4 <= (uint32_t)(32 * g + (wide ? 32 : 16));
+  const bool want_totals = totals != nullptr && g == 0;
+  const uint32_t lo_mask = (uint32_t)((1ull << lo_bits) - 1ull);
+  const uint32_t dummy = nf >= 32 ? 0u : (0xffffffffu << nf);  // padded features: skipped
+  long long tg = 0, th = 0;
+
+  auto fold = [&]() {
+#pragma unroll
+    for (int j = 0; j < kSlotsPerThread; ++j) {
+      const int slot = tid + j * kH32Threads;
+      if (slot < nslots) {
+        acc_g[j] += ((long long)(int)hi_g[slot] << lo_bits) + (long long)lo_g[slot];
+        acc_h[j] += ((long long)(int)hi_h[slot] << lo_bits) + (long long)lo_h[slot];
+        lo_g[slot] = 0u;
+        hi_g[slot] = 0u;
+        lo_h[slot] = 0u;
+        hi_h[slot] = 0u;
+      }
+    }
+  };
+
+  int e = 0;
+  while (e + 1 < n_entries && entries[e + 1].prefix <= a) ++e;
+  uint64_t pos = a;
+  int since_fold = 0;
+  while (pos < b && e < n_entries) {
+    const HEntry en = entries[e];
+    const uint64_t end_e = min(b, en.prefix + en.len);
+    const int n_it = (int)((end_e - pos + kH32Threads - 1) / kH32Threads);
+    auto row_at = [&](uint64_t i) -> uint32_t {
+      const uint32_t at = en.begin + (uint32_t)(i - en.prefix);
+      return en.identity ? at : rows[at];
+    };
+    // Every thread copies its own future rows into its own staging slots
+    // and later reads only those, so the pipeline needs no CTA barrier.
+    auto issue = [&](int it, uint32_t row, bool valid) {
+      const int st = it % kStages;
+      if (valid) {
+        const uint8_t* rp = rec + (uint64_t)row * c.stride + 32 * g;
+        StageRow* d = &srec[st * kH32Threads + tid];
+        __pipeline_memcpy_async(&d->a, rp, 16);
+        if (wide) __pipeline_memcpy_async(&d->b, rp + 16, 16);
+        __pipeline_memcpy_async(&sgp[st * kH32Threads + tid], &gpair[row], 8);
+        if (!mask_in_block)
+          __pipeline_memcpy_async(&smask[st * kH32Threads + tid],
+                                  rec + (uint64_t)row * c.stride + mask_at, 4);
+      }
+      __pipeline_commit();
+    };
+    for (int p = 0; p < kStages - 1; ++p) {
+      const uint64_t i = pos + (uint64_t)p * kH32Threads + tid;
+      const bool v = i < end_e;
+      issue(p, v ? row_at(i) : 0u, v);
+    }
+    uint64_t ip = pos + (uint64_t)(kStages - 1) * kH32Threads + tid;
+    bool pend_valid = ip < end_e;
+    uint32_t pend_row = pend_valid ? row_at(ip) : 0u;
+    for (int it = 0; it < n_it; ++it) {
+      issue(it + kStages - 1, pend_row, pend_valid);
+      ip = pos + (uint64_t)(it + kStages) * kH32Threads + tid;
+      pend_valid = ip < end_e;
+      pend_row = pend_valid ? row_at(ip) : 0u;
+      __pipeline_wait_prior(kStages - 1);
+      const uint64_t i = pos + (uint64_t)it * kH32Threads + tid;
+      if (i < end_e) {
+        const int st = it % kStages;
+        const StageRow sr = srec[st * kH32Threads + tid];
+        const float2 pr = sgp[st * kH32Threads + tid];
+        const uint4 v1 = wide ? sr.b : make_uint4(0, 0, 0, 0);
+        uint32_t mask;
+        if (mask_in_block) {
+          const int mw = (int)(mask_at - 32 * g) >> 2;
+          mask = pick_word(sr.a, v1, mw);
+        } else {
+          mask = smask[st * kH32Threads + tid];
+        }
+        mask |= dummy;
+        const long long qg = __double2ll_rn((double)pr.x * fg);
+        const long long qh = __double2ll_rn((double)pr.y * fh);
+        if (want_totals) {
+          tg += qg;
+          th += qh;
+        }
+        const uint32_t lg = (uint32_t)qg & lo_mask, lh = (uint32_t)qh & lo_mask;
+        const uint32_t hg = (uint32_t)(qg >> lo_bits), hh = (uint32_t)(qh >> lo_bits);
+        // rotate the 32 record bytes right by `lane` bytes: word rotation by
+        // lane / 4 (three select stages), then a byte funnel shift
+        uint32_t w[8] = {sr.a.x, sr.a.y, sr.a.z, sr.a.w, v1.x, v1.y, v1.z, v1.w};
+        const int q = lane >> 2;
+        uint32_t t[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) t[j] = (q & 4) ? w[(j + 4) & 7] : w[j];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) w[j] = (q & 2) ? t[(j + 2) & 7] : t[j];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) t[j] = (q & 1) ? w[(j + 1) & 7] : w[j];
+        const int sh = (lane & 3) * 8;
+#pragma unroll
+        for (int j = 0; j < 8; ++j) w[j] = __funnelshift_r(t[j], t[(j + 1) & 7], sh);
+        const uint32_t mrot = __funnelshift_r(mask, mask, lane);
+#pragma unroll
+        for (int s = 0; s < 32; ++s) {
+          if (!((mrot >> s) & 1u)) {
+            const uint32_t bin = (w[s >> 2] >> ((s & 3) * 8)) & 0xffu;
+            const int slot = (int)(bin * 32u) + ((lane + s) & 31);
+            atomicAdd(&lo_g[slot], lg);
+            atomicAdd(&hi_g[slot], hg);
+            atomicAdd(&lo_h[slot], lh);
+            atomicAdd(&hi_h[slot], hh);
+          }
+        }
+      }
+      since_fold += kH32Threads;
+      if (since_fold + kH32Threads > flush_rows) {
+        __syncthreads();
+        fold();
+        __syncthreads();
+        since_fold = 0;
+      }
+    }
+    __pipeline_wait_prior(0);
+    __syncthreads();
+    fold();
+    __syncthreads();
+    since_fold = 0;
+    longlong2* dst = hist + (uint64_t)en.slot * c.total_bins;
+#pragma unroll
+    for (int j = 0; j < kSlotsPerThread; ++j) {
+      const int slot = tid + j * kH32Threads;
+      const int bin = slot >> 5, fl = slot & 31;
+      if (slot < nslots && fl < nf) {
+        const uint32_t fs = fo[f0 + fl];
+        const uint32_t nb = fo[f0 + fl + 1] - fs;
+        if ((uint32_t)bin < nb) {
+          if (acc_g[j]) atomicAdd(reinterpret_cast<unsigned long long*>(&dst[fs + bin].x), (unsigned long long)acc_g[j]);
+          if (acc_h[j]) atomicAdd(reinterpret_cast<unsigned long long*>(&dst[fs + bin].y), (unsigned long long)acc_h[j]);
+        }
+      }
+      acc_g[j] = acc_h[j] = 0;
+    }
+    pos = end_e;
+    ++e;
+  }
+  if (want_totals) {
+    using BR = cub::BlockReduce<long long, kH32Threads>;
+    __shared__ typename BR::TempStorage tmp;
+    long long sgt = BR(tmp).Sum(tg);
+    __syncthreads();
+    long long sht = BR(tmp).Sum(th);
+    if (tid == 0) {
       atomicAdd(reinterpret_cast<unsigned long long*>(&totals[0]), (unsigned long long)sgt);
       atomicAdd(reinterpret_cast<unsigned long long*>(&totals[1]), (unsigned long long)sht);
     }
@@ -637,14 +857,6 @@ __global__ void __launch_bounds__(kApplyThreads)
   if (k < n_front) {
     dec[k].item_begin = item0;
     dec[k].item_count = n_items_k;
-    for (int t = 0; t < n_items_k; ++t) {
-      PItem it;
-      it.k = k;
-      it.kind = valid ? 1 : 2;
-      it.off = (uint32_t)t * kTile;
-      it.len = min((uint32_t)kTile, fr.len - (uint32_t)t * kTile);
-      items[item0 + t] = it;
-    }
   }
   if (k == 0) {
     ls->n_items = n_items;
@@ -663,6 +875,23 @@ __global__ void __launch_bounds__(kApplyThreads)
 // the node's eta-scaled leaf value to the margins of its rows instead.
 constexpr int kPartThreads = 256;
 
+// The frontier node owning work item `it` (items are laid out node after
+// node, dec[k].item_begin ascending) and the item's tile.
+__device__ __forceinline__ PItem locate_item(const Decision* __restrict__ dec, int n_front, int it,
+                                             const Front* __restrict__ front) {
+  int lo = 0, hi = n_front - 1;
+  while (lo < hi) {
+    const int mid = (lo + hi + 1) >> 1;
+    if (dec[mid].item_begin <= it) lo = mid; else hi = mid - 1;
+  }
+  PItem p;
+  p.k = lo;
+  p.kind = dec[lo].split ? 1 : 2;
+  p.off = (uint32_t)(it - dec[lo].item_begin) * kTile;
+  p.len = min((uint32_t)kTile, front[lo].len - p.off);
+  return p;
+}
+
 __global__ void __launch_bounds__(kPartThreads)
     k_part_count(DevConst c, const uint8_t* __restrict__ col, const uint64_t* __restrict__ colmiss,
                  const uint32_t* __restrict__ rows_in, int identity, const Front* __restrict__ front,
@@ -671,7 +900,7 @@ __global__ void __launch_bounds__(kPartThreads)
                  uint32_t* __restrict__ item_left, float* __restrict__ margin) {
   const int it = blockIdx.x;
   if (it >= ls->n_items) return;
-  const PItem pi = items[it];
+  const PItem pi = locate_item(dec, ls->n_front, it, front);
   const Front fr = front[pi.k];
   const Decision d = dec[pi.k];
   if (pi.kind == 2) {
@@ -748,7 +977,7 @@ __global__ void __launch_bounds__(kPartThreads)
                    int identity, uint32_t* __restrict__ rows_out) {
   const int it = blockIdx.x;
   if (it >= ls->n_items) return;
-  const PItem pi = items[it];
+  const PItem pi = locate_item(dec, ls->n_front, it, front);
   if (pi.kind != 1) return;
   const Front fr = front[pi.k];
   const Decision d = dec[pi.k];
@@ -922,7 +1151,29 @@ void launch_encode(const uint8_t* col, const uint64_t* colmiss, uint64_t n_rows,
   k_encode<<<grid, 256, 0, s>>>(col, colmiss, n_rows, n_cols, stride, mask_off, rec);
 }
 
-size_t hist_smem_bytes(const DevConst& c) { return (size_t)c.max_bins * 32 * 16; }
+// The split of the 32-bit kernel for `global_rows` rows: lo bits K and the
+// rows between folds R (0: the 32-bit kernel does not apply).
+static void split_for_rows(uint64_t global_rows, int& lo_bits, int& flush_rows) {
+  int c = 0;
+  while (c < 64 && (1ull << c) < global_rows) ++c;
+  const int K = (64 - c + 1) / 2;
+  const int r = std::min(32 - K, c + K - 32);
+  lo_bits = K;
+  flush_rows = (r >= 10 && r < 31) ? (1 << r) : 0;  // at least two 512-row passes per fold
+}
+
+static bool use_hist32(const DevConst& c) {
+  int K, R;
+  split_for_rows(c.global_rows, K, R);
+  return !c.hist64 && R > 0 && c.max_bins * 32 <= kSlotsPerThread * kH32Threads;
+}
+
+size_t hist_smem_bytes(const DevConst& c) {
+  if (use_hist32(c))
+    return (size_t)c.max_bins * 32 * 16 +
+           (size_t)kStages * kH32Threads * (sizeof(StageRow) + sizeof(float2) + sizeof(uint32_t));
+  return (size_t)c.max_bins * 32 * 16;
+}
 
 int hist_grid(int n_sm) { return n_sm; }
 
@@ -942,6 +1193,20 @@ void launch_hist(const DevConst& c, const uint32_t* fo, const uint8_t* rec, cons
       granted[dev] = smem;
   }
   dim3 grid(grid_x, c.n_groups);
+  if (use_hist32(c)) {
+    static size_t granted32[64] = {0};
+    if (dev < 0 || dev >= 64 || granted32[dev] < smem) {
+      if (cudaFuncSetAttribute(k_hist32, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) ==
+              cudaSuccess &&
+          dev >= 0 && dev < 64)
+        granted32[dev] = smem;
+    }
+    int K, R;
+    split_for_rows(c.global_rows, K, R);
+    k_hist32<<<grid, kH32Threads, smem, s>>>(c, fo, rec, gpair, scale, rows, entries, ls, hist,
+                                             totals, row_stats, K, R);
+    return;
+  }
   k_hist<<<grid, kHistThreads, smem, s>>>(c, fo, rec, gpair, scale, rows, entries, ls, hist, totals,
                                           row_stats);
 }

@@ -107,6 +107,9 @@ CASES = {
                                 max_delta_step=0.7)),
     "few_bins": dict(gen=lambda: synth.logistic_c2(6000, 12, seed=8), rounds=3,
                      kw=dict(objective="binary:logistic", max_depth=6, max_bin=16)),
+    # enough rows for the 32-bit split-accumulator histogram kernel
+    "c2_large": dict(gen=lambda: synth.logistic_c2(600_003, 28, seed=6), rounds=2,
+                     kw=dict(objective="binary:logistic", max_depth=8, eta=0.1)),
 }
 
 
@@ -277,3 +280,16 @@ def test_non_ascending_rows_are_refused():
     with pytest.raises(H.HbError):
         e.begin_tree(np.array([3, 2, 1]))
     e.close()
+
+
+def test_histogram_kernels_agree(monkeypatch):
+    """The 32-bit split-accumulator kernel and the 64-bit-atomic one give
+    the same exact int64 sums (large enough for the 32-bit kernel)."""
+    x, y = synth.logistic_c2(1_100_000, 28, seed=13)
+    m = H.BinnedMatrix.from_dense(x)
+    p = H.TrainingParams(objective="binary:logistic", max_depth=8)
+    runs = []
+    for kernel in ("32", "64"):
+        monkeypatch.setenv("HB_HIST_KERNEL", kernel)
+        runs.append(H.train(p, y=y, rounds=2, matrix=m))
+    assert_forest_equal(runs[0].nodes, runs[0].tree_ptr, runs[1].nodes, runs[1].tree_ptr, "32 vs 64")
