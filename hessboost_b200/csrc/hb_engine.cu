@@ -85,6 +85,9 @@ struct hb_engine {
   DevBuf<Triple> pairs;
   DevBuf<LevelState> ls;
   DevBuf<hb_tree_node> tree;
+  DevBuf<WNode> wtree;
+  bool pending_tree = false;  // the last grown tree's leaves are not yet in the margins
+  int pending_depth = 0;
   int max_items = 0;
   DevBuf<hb_tree_node> forest;
   DevBuf<uint32_t> counts;
@@ -210,6 +213,7 @@ hb_status ensure_growth_buffers(hb_engine* e, int max_depth) {
   HB_CK(e, e->pairs.alloc(max_front));
   HB_CK(e, e->ls.alloc(kMaxDepth + 2));
   HB_CK(e, e->tree.alloc((size_t)2 * max_front));
+  HB_CK(e, e->wtree.alloc((size_t)2 * max_front));
   e->alloc_depth = max_depth;
   return HB_OK;
 }
@@ -232,14 +236,31 @@ uint64_t vector_rows(hb_engine* e) {
   return std::min<uint64_t>(vg - e->row_begin, e->c.n_rows);
 }
 
+// Add the last grown tree's leaves to the margins now (the next round's
+// gradient kernel does it otherwise).
+hb_status flush_pending(hb_engine* e) {
+  if (!e->pending_tree) return HB_OK;
+  mark_begin(e, T_OTHER);
+  launch_walk(e->wtree.p, e->ls.p + e->pending_depth + 1, 2 << e->pending_depth, e->rec.p,
+              e->c.stride, e->c.mask_off, e->c.n_rows, e->margin.p, e->n_sm, e->stream);
+  mark_end(e);
+  e->kernel_launches += 1;
+  e->pending_tree = false;
+  HB_CK(e, cudaGetLastError());
+  return HB_OK;
+}
+
 hb_status run_gradients(hb_engine* e, int kind, float spw, float min_hess) {
   HB_CK(e, cudaMemsetAsync(e->scale.p, 0, sizeof(Scale), e->stream));
   mark_begin(e, T_GRAD);
+  const bool walk = e->pending_tree;
   launch_gradients(kind, e->margin.p, e->label.p, e->weight_key ? e->weight.p : nullptr, spw,
-                   min_hess, e->c.n_rows, vector_rows(e), e->gpair.p, e->scale.p, e->n_sm,
-                   e->stream);
+                   min_hess, e->c.n_rows, vector_rows(e), e->gpair.p, e->scale.p,
+                   walk ? e->wtree.p : nullptr, e->ls.p + e->pending_depth + 1,
+                   2 << e->pending_depth, e->rec.p, e->c.stride, e->c.mask_off, e->n_sm, e->stream);
   mark_end(e);
-  e->kernel_launches += 2;  // gradients + scale
+  e->pending_tree = false;
+  e->kernel_launches += 2;  // gradients (+ last tree's leaves) + scale
   HB_CK(e, cudaGetLastError());
   hb_status st = finish_scale(e);
   if (st != HB_OK) return st;
@@ -285,6 +306,7 @@ hb_status grow_device(hb_engine* e, const hb_train_params* p, bool to_forest) {
   int cur = 0;
   uint32_t* rows_in = e->rows[0].p;
   uint32_t* rows_out = e->rows[1].p;
+  uint64_t launches = 3;
   for (int d = 0; d <= D; ++d) {
     const bool leaf_only = d == D;
     const int max_front = 1 << d;
@@ -296,53 +318,58 @@ hb_status grow_device(hb_engine* e, const hb_train_params* p, bool to_forest) {
       mark_begin(e, T_SCAN);
       launch_scan(c, e->fo.p, hist, fr, lsd, e->scale.p, max_front, e->cand.p, s);
       mark_end(e);
+      ++launches;
     }
     mark_begin(e, T_APPLY);
     launch_apply(c, e->fo.p, e->cuts.p, e->cand.p, fr, nx, e->dec.p, e->items.p, lsd, lsn,
-                 e->tree.p, e->scale.p, d, leaf_only ? 1 : 0, s);
+                 e->tree.p, e->wtree.p, e->scale.p, d, leaf_only ? 1 : 0, s);
     mark_end(e);
+    ++launches;
+    HB_CK(e, cudaGetLastError());
+    // Children at the depth limit need no rows: their leaves reach the
+    // margins through the tree walk of the next gradient pass.
+    if (d + 2 > D) {
+      cur ^= 1;
+      continue;
+    }
     const int max_items = std::min(e->max_items, (int)((c.n_rows + kTile - 1) / kTile) + max_front);
     mark_begin(e, T_PART);
-    launch_part_count(c, e->col.p, e->has_missing ? e->colmiss.p : nullptr, rows_in, d == 0, fr,
-                      e->dec.p, e->items.p, lsd, max_items, e->dirbits.p, e->item_left.p,
-                      e->margin.p, s);
-    if (!leaf_only) {
-      launch_part_scan(fr, e->dec.p, lsd, max_front, e->item_left.p, e->item_off.p, nx, s);
-      launch_part_scatter(fr, e->dec.p, e->items.p, lsd, max_items, e->dirbits.p, e->item_off.p,
-                          nx, rows_in, d == 0, rows_out, s);
-    }
+    launch_part_count(c, e->col.p, e->has_missing ? e->colmiss.p : nullptr, e->rec.p, 0,
+                      rows_in, d == 0, fr, e->dec.p, e->items.p, lsd, max_items, e->dirbits.p,
+                      e->item_left.p, s);
+    launch_part_scan(fr, e->dec.p, lsd, max_front, e->item_left.p, e->item_off.p, nx, s);
+    launch_part_scatter(fr, e->dec.p, e->items.p, lsd, max_items, e->dirbits.p, e->item_off.p,
+                        nx, rows_in, d == 0, rows_out, s);
     mark_end(e);
-    HB_CK(e, cudaGetLastError());
-    if (leaf_only) break;
-    const bool terminal = d + 1 >= D;
-    if (!terminal) {
-      launch_hist_plan(fr, e->dec.p, lsd, nx, e->entries.p, e->pairs.p, lsn, 0, s);
-      mark_begin(e, T_HIST);
-      launch_hist(c, e->fo.p, e->rec.p, e->gpair.p, e->scale.p, rows_out, e->entries.p, lsn, hist,
-                  nullptr, e->row_stats.p, hgrid, smem, s);
-      mark_end(e);
-      if (e->comm) {
-        const size_t base = (size_t(1) << (d + 1)) - 1, half = size_t(1) << d;
-        HB_NCCL(e, ncclAllReduce(hist + base * c.total_bins, hist + base * c.total_bins,
-                                 2 * half * c.total_bins, ncclInt64, ncclSum, e->comm, s));
-      }
-      mark_begin(e, T_SUB);
-      launch_subtract(e->pairs.p, lsn, max_front, c.total_bins, hist, s);
-      mark_end(e);
+    launch_hist_plan(fr, e->dec.p, lsd, nx, e->entries.p, e->pairs.p, lsn, 0, s);
+    mark_begin(e, T_HIST);
+    launch_hist(c, e->fo.p, e->rec.p, e->gpair.p, e->scale.p, rows_out, e->entries.p, lsn, hist,
+                nullptr, e->row_stats.p, hgrid, smem, s);
+    mark_end(e);
+    if (e->comm) {
+      const size_t base = (size_t(1) << (d + 1)) - 1, half = size_t(1) << d;
+      HB_NCCL(e, ncclAllReduce(hist + base * c.total_bins, hist + base * c.total_bins,
+                               2 * half * c.total_bins, ncclInt64, ncclSum, e->comm, s));
     }
+    mark_begin(e, T_SUB);
+    launch_subtract(e->pairs.p, lsn, max_front, c.total_bins, hist, s);
+    mark_end(e);
+    launches += 6;
     HB_CK(e, cudaGetLastError());
     std::swap(rows_in, rows_out);
     cur ^= 1;
   }
+  e->pending_tree = true;
+  e->pending_depth = D;
   if (to_forest) {
     launch_finish_tree(e->tree.p, e->ls.p + D + 1, e->forest.p, e->counts.p, e->tree_counter.p,
                        (uint32_t)(2u << D), s);
     HB_CK(e, cudaGetLastError());
   }
-  // root setup + root hist + root stats; per level below D: scan, apply,
-  // 3 partition passes, and (above the last level) plan, hist, subtract;
-  // the leaf level: apply + partition; the forest copy.
-  e->kernel_launches += 3 + 5 * (uint64_t)D + 3 * (uint64_t)(D > 1 ? D - 1 : 0) + 2 + (to_forest ? 1 : 0);
+  // root setup + root hist + root stats, per level scan + apply (+ 3
+  // partition passes, plan, hist, subtract above the last two levels), the
+  // forest copy
+  e->kernel_launches += launches + (to_forest ? 1 : 0);
   e->rounds_done += 1;
   return HB_OK;
 }
@@ -423,6 +450,7 @@ hb_status hb_engine_destroy(hb_engine* e) {
   e->pairs.release();
   e->ls.release();
   e->tree.release();
+  e->wtree.release();
   e->forest.release();
   e->counts.release();
   e->tree_counter.release();
@@ -727,9 +755,9 @@ hb_status hb_partition(hb_engine* e, const hb_row_split* splits, uint32_t n, hb_
     HB_CK(e, cudaMemcpyAsync(e->items.p, it.data(), sizeof(PItem) * n_items, cudaMemcpyHostToDevice, s));
   HB_CK(e, cudaMemcpyAsync(e->ls.p, &lsh, sizeof(LevelState), cudaMemcpyHostToDevice, s));
   if (n_items) {
-    launch_part_count(c, e->col.p, e->has_missing ? e->colmiss.p : nullptr, e->rows[0].p, 0,
-                      e->front[0].p, e->dec.p, e->items.p, e->ls.p, n_items, e->dirbits.p,
-                      e->item_left.p, e->margin.p, s);
+    launch_part_count(c, e->col.p, e->has_missing ? e->colmiss.p : nullptr, e->rec.p, 0,
+                      e->rows[0].p, 0, e->front[0].p, e->dec.p, e->items.p, e->ls.p, n_items,
+                      e->dirbits.p, e->item_left.p, s);
   }
   launch_part_scan(e->front[0].p, e->dec.p, e->ls.p, (int)n, e->item_left.p, e->item_off.p,
                    e->front[1].p, s);
@@ -789,6 +817,7 @@ hb_status hb_load_margins(hb_engine* e, const float* margins, uint64_t n) {
   HB_CK(e, cudaMemcpyAsync(e->margin.p, margins, 4 * n, cudaMemcpyHostToDevice, e->stream));
   HB_CK(e, cudaStreamSynchronize(e->stream));
   e->margins_loaded = true;
+  e->pending_tree = false;
   e->label_key = e->weight_key = nullptr;
   return HB_OK;
 }
@@ -1014,6 +1043,8 @@ hb_status hb_grow_tree(hb_engine* e, const hb_train_params* p, hb_tree_node* nod
   if (!nodes || !n_nodes) return HB_INVALID_ARGUMENT;
   st = grow_device(e, p, false);
   if (st != HB_OK) return st;
+  st = flush_pending(e);
+  if (st != HB_OK) return st;
   LevelState last;
   HB_CK(e, cudaMemcpyAsync(&last, e->ls.p + p->max_depth + 1, sizeof(LevelState), cudaMemcpyDeviceToHost, e->stream));
   HB_CK(e, cudaStreamSynchronize(e->stream));
@@ -1037,6 +1068,7 @@ hb_status hb_train_begin(hb_engine* e, const float* labels, uint64_t n, float ba
     HB_CK(e, cudaStreamSynchronize(s));
   }
   e->margins_loaded = true;
+  e->pending_tree = false;
   e->label_key = nullptr;
   hb_status st = stage_labels(e, labels, nullptr, n);
   if (st != HB_OK) return st;
@@ -1064,6 +1096,8 @@ hb_status hb_train_rounds(hb_engine* e, const hb_train_params* p, int32_t rounds
     if (st != HB_OK) return st;
     if (e->timing && e->ev_used + 128 > e->ev.size()) collect_timers(e);
   }
+  st = flush_pending(e);
+  if (st != HB_OK) return st;
   std::vector<uint32_t> cnt(std::max(rounds, 1));
   HB_CK(e, cudaMemcpyAsync(cnt.data(), e->counts.p, 4 * (size_t)std::max(rounds, 1), cudaMemcpyDeviceToHost, s));
   HB_CK(e, cudaStreamSynchronize(s));

@@ -121,6 +121,16 @@ struct LevelState {
   int32_t pad;
 };
 
+// The grown tree as the margin update walks it: a row at a node goes left
+// when its feature-local bin is below `limit`, or, missing, when bit 31 of
+// `feature` (default_left) is set; the same rule as the partition.
+struct WNode {
+  int32_t left;       // first child (right = left + 1); -1 for a leaf
+  uint32_t feature;   // split feature | default_left << 31
+  uint32_t limit;
+  float leaf;         // eta-scaled leaf value of a leaf
+};
+
 struct Triple {
   int32_t parent, built, sibling, pad;
 };

@@ -26,6 +26,20 @@ constexpr double kRtEps = 1e-6;               // src/lib.rs:366
 
 __device__ __forceinline__ double ll2d(long long v) { return __ll2double_rn(v); }
 
+// Word k (0..7) of a 32-byte record held as two uint4.
+__device__ __forceinline__ uint32_t pick_word(const uint4& a, const uint4& b, int k) {
+  uint32_t w = a.x;
+  w = k == 1 ? a.y : w;
+  w = k == 2 ? a.z : w;
+  w = k == 3 ? a.w : w;
+  w = k == 4 ? b.x : w;
+  w = k == 5 ? b.y : w;
+  w = k == 6 ? b.z : w;
+  w = k == 7 ? b.w : w;
+  return w;
+}
+
+
 // ---------------------------------------------------------------------------
 // Objectives.
 
@@ -96,10 +110,62 @@ __device__ __forceinline__ void reduce_scale(float mg, float mh, bool nonfinite,
 //    `vrows` rows (n - n % 8 for n >= 16, objective/mod.rs:195) every aligned
 //    group of 8 margins whose magnitudes are all <= 80 takes the vector
 //    sigmoid, any other group and the tail the scalar one.
-__global__ void k_gradients(int kind, const float* __restrict__ margin,
+// The leaf of row r in the walked tree (WNode, staged in shared memory).
+__device__ __forceinline__ float walk_leaf(const WNode* __restrict__ t, const uint8_t* __restrict__ rp,
+                                           uint32_t stride, uint32_t mask_off) {
+  WNode nd = t[0];
+  if (stride == 32 && mask_off == 28) {
+    // the whole record (28 bins + the mask word) in registers
+    const uint4 a = *reinterpret_cast<const uint4*>(rp);
+    const uint4 b = *reinterpret_cast<const uint4*>(rp + 16);
+    const uint32_t m = b.w;
+    while (nd.left >= 0) {
+      const uint32_t f = nd.feature & 0x7fffffffu;
+      const bool miss = (m >> f) & 1u;
+      const uint32_t bin = (pick_word(a, b, (int)(f >> 2)) >> ((f & 3) * 8)) & 0xffu;
+      const bool left = miss ? (nd.feature >> 31) != 0u : bin < nd.limit;
+      nd = t[nd.left + (left ? 0 : 1)];
+    }
+    return nd.leaf;
+  }
+  while (nd.left >= 0) {
+    const uint32_t f = nd.feature & 0x7fffffffu;
+    const uint32_t m = *reinterpret_cast<const uint32_t*>(rp + mask_off + 4 * (f >> 5));
+    const bool miss = (m >> (f & 31)) & 1u;
+    const bool left = miss ? (nd.feature >> 31) != 0u : (uint32_t)rp[f] < nd.limit;
+    nd = t[nd.left + (left ? 0 : 1)];
+  }
+  return nd.leaf;
+}
+
+__device__ __forceinline__ void stage_tree(const WNode* __restrict__ wtree, const LevelState* ls_last,
+                                           WNode* s_tree) {
+  const int n = ls_last->n_nodes;
+  for (int i = threadIdx.x; i < n; i += blockDim.x) s_tree[i] = wtree[i];
+  __syncthreads();
+}
+
+// Add the previous tree's leaves to the margins: each row walks the tree
+// over its binned record (the partition's routing rule), in row order.
+__global__ void k_walk(const WNode* __restrict__ wtree, const LevelState* __restrict__ ls_last,
+                       const uint8_t* __restrict__ rec, uint32_t stride, uint32_t mask_off, uint64_t n,
+                       float* __restrict__ margin) {
+  extern __shared__ WNode s_tree[];
+  stage_tree(wtree, ls_last, s_tree);
+  for (uint64_t i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n;
+       i += (uint64_t)gridDim.x * blockDim.x) {
+    margin[i] = __fadd_rn(margin[i], walk_leaf(s_tree, rec + i * stride, stride, mask_off));
+  }
+}
+
+__global__ void k_gradients(int kind, float* __restrict__ margin,
                             const float* __restrict__ label, const float* __restrict__ weight,
                             float spw, float min_hess, uint64_t n, uint64_t vrows,
-                            float2* __restrict__ gpair, Scale* scale) {
+                            float2* __restrict__ gpair, Scale* scale, const WNode* __restrict__ wtree,
+                            const LevelState* __restrict__ ls_last, const uint8_t* __restrict__ rec,
+                            uint32_t stride, uint32_t mask_off) {
+  extern __shared__ WNode s_tree[];
+  if (wtree) stage_tree(wtree, ls_last, s_tree);
   float mg = 0.0f, mh = 0.0f;
   bool nonfinite = false;
   const unsigned lane = threadIdx.x & 31;
@@ -108,6 +174,10 @@ __global__ void k_gradients(int kind, const float* __restrict__ margin,
     uint64_t i = base + threadIdx.x;
     bool in = i < n;
     float m = in ? margin[i] : 0.0f;
+    if (wtree && in) {
+      m = __fadd_rn(m, walk_leaf(s_tree, rec + i * stride, stride, mask_off));
+      margin[i] = m;
+    }
     float y = in ? label[i] : 0.0f;
     float w = (in && weight) ? weight[i] : 1.0f;
     float g = 0.0f, h = 0.0f;
@@ -213,17 +283,6 @@ __global__ void k_encode(const uint8_t* __restrict__ col, const uint64_t* __rest
 // entry it touches. Shared layout: g[bin][32] then h[bin][32] as int64, a
 // feature's bins in one bank pair; lane l starts at feature l % nf and walks
 // the features cyclically, so a warp's 32 atomics hit distinct features.
-__device__ __forceinline__ uint32_t pick_word(const uint4& a, const uint4& b, int k) {
-  uint32_t w = a.x;
-  w = k == 1 ? a.y : w;
-  w = k == 2 ? a.z : w;
-  w = k == 3 ? a.w : w;
-  w = k == 4 ? b.x : w;
-  w = k == 5 ? b.y : w;
-  w = k == 6 ? b.z : w;
-  w = k == 7 ? b.w : w;
-  return w;
-}
 
 __global__ void __launch_bounds__(kHistThreads, 1)
     k_hist(DevConst c, const uint32_t* __restrict__ fo, const uint8_t* __restrict__ rec,
@@ -334,6 +393,7 @@ __global__ void __launch_bounds__(kHistThreads, 1)
 // record is rotated by l bytes once per row, so step s reads byte s.
 constexpr int kH32Threads = 512;
 constexpr int kSlotsPerThread = 16;  // 256 bins x 32 feature slots / 512 threads
+constexpr int kNSlots = kSlotsPerThread * kH32Threads;  // shared accumulator slots per array
 constexpr int kStages = 3;           // rows staged ahead with cp.async
 
 // Staging of one pass of rows (one row per thread): the group's 32 record
@@ -363,7 +423,7 @@ __global__ void __launch_bounds__(kH32Threads, 1)
   const int g = blockIdx.y;
   const int f0 = g * kGroupFeatures;
   const int nf = min(kGroupFeatures, (int)c.n_cols - f0);
-  const int nslots = (int)c.max_bins * 32;
+  constexpr int nslots = kNSlots;  // every layout fits 256 bins x 32 feature slots
   uint32_t* lo_g = s32;
   uint32_t* hi_g = s32 + nslots;
   uint32_t* lo_h = s32 + 2 * nslots;
@@ -758,8 +818,8 @@ __global__ void __launch_bounds__(kApplyThreads)
     k_apply(DevConst c, const uint32_t* __restrict__ fo, const float* __restrict__ cuts,
             const Cand* __restrict__ cand, const Front* __restrict__ front, Front* __restrict__ next,
             Decision* __restrict__ dec, PItem* __restrict__ items, LevelState* ls,
-            LevelState* ls_next, hb_tree_node* __restrict__ tree, const Scale* __restrict__ scale,
-            int depth, int leaf_only) {
+            LevelState* ls_next, hb_tree_node* __restrict__ tree, WNode* __restrict__ wtree,
+            const Scale* __restrict__ scale, int depth, int leaf_only) {
   using Scan = cub::BlockScan<int, kApplyThreads>;
   __shared__ typename Scan::TempStorage tmp;
   const int n_front = ls->n_front;
@@ -768,6 +828,35 @@ __global__ void __launch_bounds__(kApplyThreads)
   const double ig = scale->ig, ih = scale->ih;
   if (depth == 0 && k == 0 && n_front > 0) tree[0] = make_leaf(0.0f, (float)(ll2d(front[0].h) * ih));
 
+  // Merge each node's per-feature winners, a warp per node: the largest
+  // loss change, the lowest feature among equals, and only above the empty
+  // split's 0 -- need_replace over ascending features.
+  __shared__ int s_best[kApplyThreads];
+  if (!leaf_only) {
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    for (int kk = warp; kk < n_front; kk += kApplyThreads / 32) {
+      float bl = 0.0f;
+      int bf = -1;
+      for (uint32_t f = lane; f < c.n_cols; f += 32) {
+        const float l = cand[(uint64_t)kk * c.n_cols + f].loss;
+        if (l > bl) {
+          bl = l;
+          bf = (int)f;
+        }
+      }
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) {
+        const float ol = __shfl_xor_sync(kFull, bl, o);
+        const int of = __shfl_xor_sync(kFull, bf, o);
+        if (ol > bl || (ol == bl && of >= 0 && (bf < 0 || of < bf))) {
+          bl = ol;
+          bf = of;
+        }
+      }
+      if (lane == 0) s_best[kk] = bf;
+    }
+    __syncthreads();
+  }
   Front fr{};
   Cand best{};
   uint32_t best_f = 0;
@@ -778,12 +867,10 @@ __global__ void __launch_bounds__(kApplyThreads)
       best.loss = 0.0f;
       best.bin = -1;
       best.default_left = 1;
-      for (uint32_t f = 0; f < c.n_cols; ++f) {
-        const Cand cf = cand[(uint64_t)k * c.n_cols + f];
-        if (cf.loss > best.loss) {  // need_replace in ascending feature order
-          best = cf;
-          best_f = f;
-        }
+      const int bf = s_best[k];
+      if (bf >= 0) {
+        best = cand[(uint64_t)k * c.n_cols + bf];
+        best_f = (uint32_t)bf;
       }
       const double lh = ll2d(best.lh) * ih;
       const double rh = ll2d(fr.h - best.lh) * ih;
@@ -842,14 +929,26 @@ __global__ void __launch_bounds__(kApplyThreads)
       d.default_left = best.default_left;
       d.lg = lg;
       d.lh = lh;
+      WNode wn;
+      wn.left = left_id;
+      wn.feature = best_f | (best.default_left ? 0x80000000u : 0u);
+      wn.limit = d.limit;
+      wn.leaf = 0.0f;
+      wtree[fr.node] = wn;
+      n_items_k = (int)((fr.len + kTile - 1) / kTile);
     } else {
       // finalize_leaf_values (shared.rs:174) then scale_leaves(eta).
       const float w = __double2float_rn(calc_weight(ll2d(fr.g) * ig, ll2d(fr.h) * ih, c));
       const float v = __fmul_rn(w, c.eta);
       tree[fr.node].leaf_value = v;
       d.leaf_value = v;
+      WNode wn;
+      wn.left = -1;
+      wn.feature = 0u;
+      wn.limit = 0u;
+      wn.leaf = v;
+      wtree[fr.node] = wn;
     }
-    n_items_k = (int)((fr.len + kTile - 1) / kTile);
     dec[k] = d;
   }
   int item0 = 0, n_items = 0;
@@ -894,36 +993,51 @@ __device__ __forceinline__ PItem locate_item(const Decision* __restrict__ dec, i
 
 __global__ void __launch_bounds__(kPartThreads)
     k_part_count(DevConst c, const uint8_t* __restrict__ col, const uint64_t* __restrict__ colmiss,
+                 const uint8_t* __restrict__ rec, int use_record,
                  const uint32_t* __restrict__ rows_in, int identity, const Front* __restrict__ front,
                  const Decision* __restrict__ dec, const PItem* __restrict__ items,
                  const LevelState* __restrict__ ls, uint32_t* __restrict__ dirbits,
-                 uint32_t* __restrict__ item_left, float* __restrict__ margin) {
+                 uint32_t* __restrict__ item_left) {
   const int it = blockIdx.x;
   if (it >= ls->n_items) return;
   const PItem pi = locate_item(dec, ls->n_front, it, front);
+  if (pi.kind != 1) return;
   const Front fr = front[pi.k];
   const Decision d = dec[pi.k];
-  if (pi.kind == 2) {
-    for (uint32_t i = threadIdx.x; i < pi.len; i += blockDim.x) {
-      const uint32_t at = fr.begin + pi.off + i;
-      const uint32_t row = identity ? at : rows_in[at];
-      margin[row] = __fadd_rn(margin[row], d.leaf_value);
-    }
-    return;
-  }
+  // Shallow levels read the feature's column (a node's rows are dense in
+  // it); deep ones the row's record, whose sector also holds the mask.
   const uint8_t* colf = col + (uint64_t)d.feature * c.n_rows;
   const uint64_t words = (c.n_rows + 63) / 64;
   const uint64_t* missf = colmiss ? colmiss + (uint64_t)d.feature * words : nullptr;
+  const uint32_t mword = c.mask_off + 4 * (d.feature >> 5);
+  const uint32_t mbit = d.feature & 31;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  constexpr int kPer = kTile / kPartThreads;
+  uint32_t row[kPer];
+#pragma unroll
+  for (int j = 0; j < kPer; ++j) {
+    const uint32_t i = j * kPartThreads + threadIdx.x;
+    const uint32_t at = fr.begin + pi.off + min(i, pi.len - 1);
+    row[j] = identity ? at : rows_in[at];
+  }
   int cnt = 0;
-  for (int j = 0; j < kTile / kPartThreads; ++j) {
+#pragma unroll
+  for (int j = 0; j < kPer; ++j) {
     const uint32_t i = j * kPartThreads + threadIdx.x;
     bool left = false;
     if (i < pi.len) {
-      const uint32_t at = fr.begin + pi.off + i;
-      const uint32_t row = identity ? at : rows_in[at];
-      const bool miss = missf && ((missf[row >> 6] >> (row & 63)) & 1ull);
-      left = miss ? (d.default_left != 0) : (colf[row] < d.limit);
+      const uint32_t r = row[j];
+      bool miss;
+      uint32_t bin;
+      if (use_record) {
+        const uint8_t* rp = rec + (uint64_t)r * c.stride;
+        bin = rp[d.feature];
+        miss = (*reinterpret_cast<const uint32_t*>(rp + mword) >> mbit) & 1u;
+      } else {
+        bin = colf[r];
+        miss = missf && ((missf[r >> 6] >> (r & 63)) & 1ull);
+      }
+      left = miss ? (d.default_left != 0) : (bin < d.limit);
     }
     const unsigned bal = __ballot_sync(kFull, left);
     if (lane == 0) {
@@ -937,30 +1051,30 @@ __global__ void __launch_bounds__(kPartThreads)
   if (threadIdx.x == 0) item_left[it] = (uint32_t)total;
 }
 
-// One warp per splitting frontier node: exclusive scan of its tiles' left
+// One CTA per splitting frontier node: exclusive scan of its tiles' left
 // counts; the children's segments.
-__global__ void k_part_scan(const Front* __restrict__ front, const Decision* __restrict__ dec,
-                            const LevelState* __restrict__ ls, const uint32_t* __restrict__ item_left,
-                            uint32_t* __restrict__ item_left_off, Front* __restrict__ next) {
-  const int k = (int)((blockIdx.x * blockDim.x + threadIdx.x) >> 5);
-  const int lane = threadIdx.x & 31;
+constexpr int kScanThreads = 256;
+__global__ void __launch_bounds__(kScanThreads)
+    k_part_scan(const Front* __restrict__ front, const Decision* __restrict__ dec,
+                const LevelState* __restrict__ ls, const uint32_t* __restrict__ item_left,
+                uint32_t* __restrict__ item_left_off, Front* __restrict__ next) {
+  using Scan = cub::BlockScan<uint32_t, kScanThreads>;
+  __shared__ typename Scan::TempStorage tmp;
+  const int k = blockIdx.x;
   if (k >= ls->n_front) return;
   const Decision d = dec[k];
   if (!d.split) return;
   uint32_t run = 0;
-  for (int base = 0; base < d.item_count; base += 32) {
-    const int t = base + lane;
+  for (int base = 0; base < d.item_count; base += kScanThreads) {
+    const int t = base + threadIdx.x;
     const uint32_t v = t < d.item_count ? item_left[d.item_begin + t] : 0u;
-    uint32_t inc = v;
-#pragma unroll
-    for (int o = 1; o < 32; o <<= 1) {
-      const uint32_t x = __shfl_up_sync(kFull, inc, o);
-      if (lane >= o) inc += x;
-    }
-    if (t < d.item_count) item_left_off[d.item_begin + t] = run + inc - v;
-    run += __shfl_sync(kFull, inc, 31);
+    uint32_t ex = 0, agg = 0;
+    Scan(tmp).ExclusiveSum(v, ex, agg);
+    __syncthreads();
+    if (t < d.item_count) item_left_off[d.item_begin + t] = run + ex;
+    run += agg;
   }
-  if (lane == 0) {
+  if (threadIdx.x == 0) {
     const Front fr = front[k];
     next[2 * d.pair].begin = fr.begin;
     next[2 * d.pair].len = run;
@@ -1126,12 +1240,25 @@ __global__ void k_add_segment(const uint32_t* __restrict__ rows, uint32_t begin,
 
 // ---------------------------------------------------------------------------
 // Launchers.
-void launch_gradients(int kind, const float* margin, const float* label, const float* weight,
-                      float spw, float min_hess, uint64_t n, uint64_t vrows, float2* gpair,
-                      Scale* scale, int n_sm, cudaStream_t s) {
+void launch_gradients(int kind, float* margin, const float* label, const float* weight, float spw,
+                      float min_hess, uint64_t n, uint64_t vrows, float2* gpair, Scale* scale,
+                      const WNode* wtree, const LevelState* ls_last, int max_nodes,
+                      const uint8_t* rec, uint32_t stride, uint32_t mask_off, int n_sm,
+                      cudaStream_t s) {
   int grid = (int)std::min<uint64_t>((n + 255) / 256, (uint64_t)n_sm * 8);
   if (grid < 1) grid = 1;
-  k_gradients<<<grid, 256, 0, s>>>(kind, margin, label, weight, spw, min_hess, n, vrows, gpair, scale);
+  const size_t smem = wtree ? sizeof(WNode) * (size_t)max_nodes : 0;
+  k_gradients<<<grid, 256, smem, s>>>(kind, margin, label, weight, spw, min_hess, n, vrows, gpair, scale,
+                                      wtree, ls_last, rec, stride, mask_off);
+}
+
+void launch_walk(const WNode* wtree, const LevelState* ls_last, int max_nodes, const uint8_t* rec,
+                 uint32_t stride, uint32_t mask_off, uint64_t n, float* margin, int n_sm,
+                 cudaStream_t s) {
+  int grid = (int)std::min<uint64_t>((n + 255) / 256, (uint64_t)n_sm * 8);
+  if (grid < 1) grid = 1;
+  k_walk<<<grid, 256, sizeof(WNode) * (size_t)max_nodes, s>>>(wtree, ls_last, rec, stride, mask_off, n,
+                                                              margin);
 }
 
 void launch_pair_maxima(const float2* gpair, uint64_t n, Scale* scale, int n_sm, cudaStream_t s) {
@@ -1165,12 +1292,12 @@ static void split_for_rows(uint64_t global_rows, int& lo_bits, int& flush_rows) 
 static bool use_hist32(const DevConst& c) {
   int K, R;
   split_for_rows(c.global_rows, K, R);
-  return !c.hist64 && R > 0 && c.max_bins * 32 <= kSlotsPerThread * kH32Threads;
+  return !c.hist64 && R > 0 && c.max_bins * 32 <= kNSlots;
 }
 
 size_t hist_smem_bytes(const DevConst& c) {
   if (use_hist32(c))
-    return (size_t)c.max_bins * 32 * 16 +
+    return (size_t)kNSlots * 16 +
            (size_t)kStages * kH32Threads * (sizeof(StageRow) + sizeof(float2) + sizeof(uint32_t));
   return (size_t)c.max_bins * 32 * 16;
 }
@@ -1229,26 +1356,25 @@ void launch_scan(const DevConst& c, const uint32_t* fo, const longlong2* hist, c
 
 void launch_apply(const DevConst& c, const uint32_t* fo, const float* cuts, const Cand* cand,
                   const Front* front, Front* next, Decision* dec, PItem* items, LevelState* ls,
-                  LevelState* ls_next, hb_tree_node* tree, const Scale* scale, int depth,
-                  int leaf_only, cudaStream_t s) {
+                  LevelState* ls_next, hb_tree_node* tree, WNode* wtree, const Scale* scale,
+                  int depth, int leaf_only, cudaStream_t s) {
   k_apply<<<1, kApplyThreads, 0, s>>>(c, fo, cuts, cand, front, next, dec, items, ls, ls_next, tree,
-                                      scale, depth, leaf_only);
+                                      wtree, scale, depth, leaf_only);
 }
 
 void launch_part_count(const DevConst& c, const uint8_t* col, const uint64_t* colmiss,
-                       const uint32_t* rows_in, int identity, const Front* front,
-                       const Decision* dec, const PItem* items, const LevelState* ls,
-                       int max_items, uint32_t* dirbits, uint32_t* item_left, float* margin,
+                       const uint8_t* rec, int use_record, const uint32_t* rows_in, int identity,
+                       const Front* front, const Decision* dec, const PItem* items,
+                       const LevelState* ls, int max_items, uint32_t* dirbits, uint32_t* item_left,
                        cudaStream_t s) {
-  k_part_count<<<max_items, kPartThreads, 0, s>>>(c, col, colmiss, rows_in, identity, front, dec,
-                                                  items, ls, dirbits, item_left, margin);
+  k_part_count<<<max_items, kPartThreads, 0, s>>>(c, col, colmiss, rec, use_record, rows_in, identity,
+                                                  front, dec, items, ls, dirbits, item_left);
 }
 
 void launch_part_scan(const Front* front, const Decision* dec, const LevelState* ls, int max_front,
                       const uint32_t* item_left, uint32_t* item_left_off, Front* next,
                       cudaStream_t s) {
-  int grid = (max_front * 32 + 255) / 256;
-  k_part_scan<<<grid, 256, 0, s>>>(front, dec, ls, item_left, item_left_off, next);
+  k_part_scan<<<max_front, kScanThreads, 0, s>>>(front, dec, ls, item_left, item_left_off, next);
 }
 
 void launch_part_scatter(const Front* front, const Decision* dec, const PItem* items,

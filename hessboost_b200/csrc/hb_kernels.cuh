@@ -9,9 +9,16 @@ namespace hb {
 
 // Objective gradients at `margin` (the host's bits, see hb_kernels.cu) plus
 // the largest |g|, |h| and a non-finite flag, folded into `scale`.
-void launch_gradients(int kind, const float* margin, const float* label, const float* weight,
-                      float spw, float min_hess, uint64_t n, uint64_t vrows, float2* gpair,
-                      Scale* scale, int n_sm, cudaStream_t s);
+// With `wtree`, each row first adds its leaf of that tree to its margin.
+void launch_gradients(int kind, float* margin, const float* label, const float* weight, float spw,
+                      float min_hess, uint64_t n, uint64_t vrows, float2* gpair, Scale* scale,
+                      const WNode* wtree, const LevelState* ls_last, int max_nodes,
+                      const uint8_t* rec, uint32_t stride, uint32_t mask_off, int n_sm,
+                      cudaStream_t s);
+// Add each row's leaf of `wtree` to its margin.
+void launch_walk(const WNode* wtree, const LevelState* ls_last, int max_nodes, const uint8_t* rec,
+                 uint32_t stride, uint32_t mask_off, uint64_t n, float* margin, int n_sm,
+                 cudaStream_t s);
 // |g|, |h| maxima of staged pairs (HistogramBackend::prepare).
 void launch_pair_maxima(const float2* gpair, uint64_t n, Scale* scale, int n_sm, cudaStream_t s);
 // Fixed-point exponents from the (reduced) maxima and the global row count.
@@ -34,12 +41,12 @@ void launch_scan(const DevConst& c, const uint32_t* fo, const longlong2* hist, c
                  cudaStream_t s);
 void launch_apply(const DevConst& c, const uint32_t* fo, const float* cuts, const Cand* cand,
                   const Front* front, Front* next, Decision* dec, PItem* items, LevelState* ls,
-                  LevelState* ls_next, hb_tree_node* tree, const Scale* scale, int depth,
-                  int leaf_only, cudaStream_t s);
+                  LevelState* ls_next, hb_tree_node* tree, WNode* wtree, const Scale* scale,
+                  int depth, int leaf_only, cudaStream_t s);
 void launch_part_count(const DevConst& c, const uint8_t* col, const uint64_t* colmiss,
-                       const uint32_t* rows_in, int identity, const Front* front,
-                       const Decision* dec, const PItem* items, const LevelState* ls,
-                       int max_items, uint32_t* dirbits, uint32_t* item_left, float* margin,
+                       const uint8_t* rec, int use_record, const uint32_t* rows_in, int identity,
+                       const Front* front, const Decision* dec, const PItem* items,
+                       const LevelState* ls, int max_items, uint32_t* dirbits, uint32_t* item_left,
                        cudaStream_t s);
 void launch_part_scan(const Front* front, const Decision* dec, const LevelState* ls, int max_front,
                       const uint32_t* item_left, uint32_t* item_left_off, Front* next,
