@@ -991,6 +991,11 @@ __device__ __forceinline__ PItem locate_item(const Decision* __restrict__ dec, i
   return p;
 }
 
+// Positions of a tile: warp w owns 256 consecutive ones, lane l of pass j
+// position w * 256 + j * 32 + l, so a warp's directions are 8 ballot words
+// in position order and its prefix needs no other warp until the end.
+constexpr int kPerThread = kTile / kPartThreads;  // 8
+
 __global__ void __launch_bounds__(kPartThreads)
     k_part_count(DevConst c, const uint8_t* __restrict__ col, const uint64_t* __restrict__ colmiss,
                  const uint8_t* __restrict__ rec, int use_record,
@@ -1004,51 +1009,51 @@ __global__ void __launch_bounds__(kPartThreads)
   if (pi.kind != 1) return;
   const Front fr = front[pi.k];
   const Decision d = dec[pi.k];
-  // Shallow levels read the feature's column (a node's rows are dense in
-  // it); deep ones the row's record, whose sector also holds the mask.
   const uint8_t* colf = col + (uint64_t)d.feature * c.n_rows;
   const uint64_t words = (c.n_rows + 63) / 64;
   const uint64_t* missf = colmiss ? colmiss + (uint64_t)d.feature * words : nullptr;
   const uint32_t mword = c.mask_off + 4 * (d.feature >> 5);
   const uint32_t mbit = d.feature & 31;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  constexpr int kPer = kTile / kPartThreads;
-  uint32_t row[kPer];
+  const uint32_t base = fr.begin + pi.off;
+  uint32_t row[kPerThread];
 #pragma unroll
-  for (int j = 0; j < kPer; ++j) {
-    const uint32_t i = j * kPartThreads + threadIdx.x;
-    const uint32_t at = fr.begin + pi.off + min(i, pi.len - 1);
+  for (int j = 0; j < kPerThread; ++j) {
+    const uint32_t i = warp * 256 + j * 32 + lane;
+    const uint32_t at = base + min(i, pi.len - 1);
     row[j] = identity ? at : rows_in[at];
+  }
+  uint32_t bin[kPerThread];
+  bool miss[kPerThread];
+#pragma unroll
+  for (int j = 0; j < kPerThread; ++j) {
+    const uint32_t r = row[j];
+    if (use_record) {
+      const uint8_t* rp = rec + (uint64_t)r * c.stride;
+      bin[j] = rp[d.feature];
+      miss[j] = (*reinterpret_cast<const uint32_t*>(rp + mword) >> mbit) & 1u;
+    } else {
+      bin[j] = colf[r];
+      miss[j] = missf && ((missf[r >> 6] >> (r & 63)) & 1ull);
+    }
   }
   int cnt = 0;
 #pragma unroll
-  for (int j = 0; j < kPer; ++j) {
-    const uint32_t i = j * kPartThreads + threadIdx.x;
-    bool left = false;
-    if (i < pi.len) {
-      const uint32_t r = row[j];
-      bool miss;
-      uint32_t bin;
-      if (use_record) {
-        const uint8_t* rp = rec + (uint64_t)r * c.stride;
-        bin = rp[d.feature];
-        miss = (*reinterpret_cast<const uint32_t*>(rp + mword) >> mbit) & 1u;
-      } else {
-        bin = colf[r];
-        miss = missf && ((missf[r >> 6] >> (r & 63)) & 1ull);
-      }
-      left = miss ? (d.default_left != 0) : (bin < d.limit);
-    }
+  for (int j = 0; j < kPerThread; ++j) {
+    const uint32_t i = warp * 256 + j * 32 + lane;
+    const bool left = i < pi.len && (miss[j] ? (d.default_left != 0) : (bin[j] < d.limit));
     const unsigned bal = __ballot_sync(kFull, left);
-    if (lane == 0) {
-      dirbits[(uint64_t)it * kTileWords + j * (kPartThreads / 32) + warp] = bal;
-      cnt += __popc(bal);
-    }
+    if (lane == j) dirbits[(uint64_t)it * kTileWords + warp * kPerThread + j] = bal;
+    cnt += __popc(bal);
   }
-  using BR = cub::BlockReduce<int, kPartThreads>;
-  __shared__ typename BR::TempStorage tmp;
-  const int total = BR(tmp).Sum(cnt);
-  if (threadIdx.x == 0) item_left[it] = (uint32_t)total;
+  __shared__ int s_cnt[kPartThreads / 32];
+  if (lane == 0) s_cnt[warp] = cnt;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    int t = 0;
+    for (int w = 0; w < kPartThreads / 32; ++w) t += s_cnt[w];
+    item_left[it] = (uint32_t)t;
+  }
 }
 
 // One CTA per splitting frontier node: exclusive scan of its tiles' left
@@ -1100,33 +1105,40 @@ __global__ void __launch_bounds__(kPartThreads)
   const uint32_t base_left = fr.begin + loff;
   const uint32_t base_right = fr.begin + L + (pi.off - loff);
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  constexpr int kWarps = kPartThreads / 32;
-  __shared__ uint32_t s_cnt[kWarps];
-  uint32_t running = 0;
-  for (int j = 0; j < kTile / kPartThreads; ++j) {
-    const unsigned bal = dirbits[(uint64_t)it * kTileWords + j * kWarps + warp];
-    if (lane == 0) s_cnt[warp] = __popc(bal);
-    __syncthreads();
-    uint32_t before = running;
-    uint32_t blk = 0;
-    for (int w = 0; w < kWarps; ++w) {
-      const uint32_t cw = s_cnt[w];
-      if (w < warp) before += cw;
-      blk += cw;
-    }
-    before += __popc(bal & ((1u << lane) - 1u));
-    const uint32_t i = j * kPartThreads + threadIdx.x;
+  const uint32_t base = fr.begin + pi.off;
+  uint32_t row[kPerThread];
+#pragma unroll
+  for (int j = 0; j < kPerThread; ++j) {
+    const uint32_t i = warp * 256 + j * 32 + lane;
+    const uint32_t at = base + min(i, pi.len - 1);
+    row[j] = identity ? at : rows_in[at];
+  }
+  const uint32_t mine = lane < kPerThread ? dirbits[(uint64_t)it * kTileWords + warp * kPerThread + lane] : 0u;
+  uint32_t bal[kPerThread];
+  uint32_t wcount = 0;
+#pragma unroll
+  for (int j = 0; j < kPerThread; ++j) {
+    bal[j] = __shfl_sync(kFull, mine, j);
+    wcount += __popc(bal[j]);
+  }
+  __shared__ uint32_t s_cnt[kPartThreads / 32];
+  if (lane == 0) s_cnt[warp] = wcount;
+  __syncthreads();
+  uint32_t before = 0;  // left positions of the tile before this warp's
+  for (int w = 0; w < warp; ++w) before += s_cnt[w];
+  const uint32_t lt = (1u << lane) - 1u;
+#pragma unroll
+  for (int j = 0; j < kPerThread; ++j) {
+    const uint32_t i = warp * 256 + j * 32 + lane;
+    const uint32_t lrank = before + __popc(bal[j] & lt);
     if (i < pi.len) {
-      const uint32_t at = fr.begin + pi.off + i;
-      const uint32_t row = identity ? at : rows_in[at];
-      if ((bal >> lane) & 1u) {
-        rows_out[base_left + (before - 0)] = row;
+      if ((bal[j] >> lane) & 1u) {
+        rows_out[base_left + lrank] = row[j];
       } else {
-        rows_out[base_right + (i - before)] = row;
+        rows_out[base_right + (i - lrank)] = row[j];
       }
     }
-    running += blk;
-    __syncthreads();
+    before += __popc(bal[j]);
   }
 }
 
