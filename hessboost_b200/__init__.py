@@ -172,6 +172,7 @@ class EngineStats(ctypes.Structure):
         ("rows_built_contiguous", ctypes.c_uint64),
         ("rows_built_gathered", ctypes.c_uint64),
         ("rounds", ctypes.c_uint64),
+        ("last_rounds_ms", ctypes.c_double),
     ]
 
 
@@ -581,8 +582,9 @@ class Engine:
                                       cap, _ptr(tree_ptr, ctypes.c_uint64)), "hb_train_rounds")
         return nodes[: int(tree_ptr[-1])].copy(), tree_ptr
 
-    def reset_stats(self, timing=False):
-        self._c(lib().hb_engine_reset_stats(self.h, 1 if timing else 0), "hb_engine_reset_stats")
+    def reset_stats(self, timing=0):
+        """timing: 0 off, 1 events around the histogram kernel, 2 around every family."""
+        self._c(lib().hb_engine_reset_stats(self.h, int(timing)), "hb_engine_reset_stats")
 
     def stats(self):
         st = EngineStats()
@@ -594,6 +596,7 @@ class Engine:
             "rows_built_contiguous": int(st.rows_built_contiguous),
             "rows_built_gathered": int(st.rows_built_gathered),
             "rounds": int(st.rounds),
+            "last_rounds_ms": float(st.last_rounds_ms),
         }
 
     def stream(self):

@@ -86,8 +86,16 @@ struct hb_engine {
   DevBuf<LevelState> ls;
   DevBuf<hb_tree_node> tree;
   DevBuf<WNode> wtree;
-  bool pending_tree = false;  // the last grown tree's leaves are not yet in the margins
+  bool pending_tree = false;  // host mirror of flags[0]: a grown tree's leaves await the margins
   int pending_depth = 0;
+  DevBuf<int> flags;          // [0]: pending tree (read by the next gradient or walk kernel)
+  // the captured round (CUDA graph) and what it was captured for
+  cudaGraphExec_t round_exec = nullptr;
+  std::vector<unsigned char> round_key;
+  uint64_t round_launches = 0;
+  bool use_graphs = true;
+  cudaEvent_t run_ev[2] = {nullptr, nullptr};  // around the last train_rounds' rounds
+  double last_rounds_ms = 0.0;
   int max_items = 0;
   DevBuf<hb_tree_node> forest;
   DevBuf<uint32_t> counts;
@@ -109,6 +117,8 @@ struct hb_engine {
 
   // timing and counters (hb_engine_get_stats)
   bool timing = false;
+  uint32_t timing_mask = 0;  // kernel families bracketed by events
+  bool mark_open = false;
   std::vector<cudaEvent_t> ev;
   std::vector<int> ev_kind;
   size_t ev_used = 0;
@@ -163,8 +173,21 @@ hb_status refuse(hb_engine* e, const std::string& why) {
   } while (0)
 
 // Timing marks (CUDA events on the engine's stream), enabled per train call.
+// Under stream capture a mark must become an event-record node of the graph
+// (cudaEventRecordExternal); a plain record would only order the capture.
+void record_mark(hb_engine* e, cudaEvent_t ev) {
+  cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+  cudaStreamIsCapturing(e->stream, &cs);
+  if (cs == cudaStreamCaptureStatusActive)
+    cudaEventRecordWithFlags(ev, e->stream, cudaEventRecordExternal);
+  else
+    cudaEventRecord(ev, e->stream);
+}
+
 void mark_begin(hb_engine* e, int kind) {
-  if (!e->timing) return;
+  e->mark_open = false;
+  if (!e->timing || !(e->timing_mask & (1u << kind))) return;
+  e->mark_open = true;
   if (e->ev_used + 2 > e->ev.size()) {
     for (int i = 0; i < 256; ++i) {
       cudaEvent_t x;
@@ -174,12 +197,13 @@ void mark_begin(hb_engine* e, int kind) {
     }
   }
   e->ev_kind[e->ev_used] = kind;
-  cudaEventRecord(e->ev[e->ev_used++], e->stream);
+  record_mark(e, e->ev[e->ev_used++]);
 }
 void mark_end(hb_engine* e) {
-  if (!e->timing) return;
+  if (!e->timing || !e->mark_open) return;
+  e->mark_open = false;
   e->ev_kind[e->ev_used] = -1;
-  cudaEventRecord(e->ev[e->ev_used++], e->stream);
+  record_mark(e, e->ev[e->ev_used++]);
 }
 void collect_timers(hb_engine* e) {
   if (!e->timing || e->ev_used == 0) return;
@@ -224,7 +248,7 @@ hb_status finish_scale(hb_engine* e) {
     HB_NCCL(e, ncclAllReduce(&e->scale.p->maxg_bits, &e->scale.p->maxg_bits, 3, ncclUint32,
                              ncclMax, e->comm, e->stream));
   }
-  launch_scale(e->scale.p, e->c.global_rows, e->stream);
+  launch_scale(e->scale.p, e->c.global_rows, e->flags.p, e->stream);
   HB_CK(e, cudaGetLastError());
   return HB_OK;
 }
@@ -242,22 +266,25 @@ hb_status flush_pending(hb_engine* e) {
   if (!e->pending_tree) return HB_OK;
   mark_begin(e, T_OTHER);
   launch_walk(e->wtree.p, e->ls.p + e->pending_depth + 1, 2 << e->pending_depth, e->rec.p,
-              e->c.stride, e->c.mask_off, e->c.n_rows, e->margin.p, e->n_sm, e->stream);
+              e->c.stride, e->c.mask_off, e->c.n_rows, e->margin.p, e->flags.p, e->n_sm, e->stream);
   mark_end(e);
+  HB_CK(e, cudaMemsetAsync(e->flags.p, 0, sizeof(int), e->stream));
   e->kernel_launches += 1;
   e->pending_tree = false;
   HB_CK(e, cudaGetLastError());
   return HB_OK;
 }
 
-hb_status run_gradients(hb_engine* e, int kind, float spw, float min_hess) {
+// Gradients at the margins, first adding a pending tree's leaves when the
+// device flag says one waits (so a captured round serves every round).
+hb_status run_gradients(hb_engine* e, int kind, float spw, float min_hess, int tree_depth) {
   HB_CK(e, cudaMemsetAsync(e->scale.p, 0, sizeof(Scale), e->stream));
   mark_begin(e, T_GRAD);
-  const bool walk = e->pending_tree;
+  const int pd = tree_depth > 0 ? tree_depth : e->pending_depth;
   launch_gradients(kind, e->margin.p, e->label.p, e->weight_key ? e->weight.p : nullptr, spw,
                    min_hess, e->c.n_rows, vector_rows(e), e->gpair.p, e->scale.p,
-                   walk ? e->wtree.p : nullptr, e->ls.p + e->pending_depth + 1,
-                   2 << e->pending_depth, e->rec.p, e->c.stride, e->c.mask_off, e->n_sm, e->stream);
+                   e->wtree.p, e->ls.p + pd + 1, 2 << pd, e->rec.p, e->c.stride, e->c.mask_off,
+                   e->flags.p, e->n_sm, e->stream);
   mark_end(e);
   e->pending_tree = false;
   e->kernel_launches += 2;  // gradients (+ last tree's leaves) + scale
@@ -359,6 +386,7 @@ hb_status grow_device(hb_engine* e, const hb_train_params* p, bool to_forest) {
     std::swap(rows_in, rows_out);
     cur ^= 1;
   }
+  HB_CK(e, cudaMemsetAsync(e->flags.p, 0x01, sizeof(int), s));
   e->pending_tree = true;
   e->pending_depth = D;
   if (to_forest) {
@@ -409,9 +437,15 @@ hb_status hb_engine_create(int32_t device_ordinal, hb_engine** out) {
     return HB_DEVICE_FAILED;
   }
   cudaDeviceGetAttribute(&e->n_sm, cudaDevAttrMultiProcessorCount, device_ordinal);
+  hist_configure();
+  cudaEventCreate(&e->run_ev[0]);
+  cudaEventCreate(&e->run_ev[1]);
+  const char* ng = std::getenv("HB_NO_GRAPHS");
+  e->use_graphs = !(ng && ng[0] == '1');
   if (e->scale.alloc(1) != cudaSuccess || e->tree_counter.alloc(1) != cudaSuccess ||
       e->seg_total.alloc(2) != cudaSuccess || e->row_stats.alloc(2) != cudaSuccess ||
-      cudaMemset(e->row_stats.p, 0, 16) != cudaSuccess) {
+      cudaMemset(e->row_stats.p, 0, 16) != cudaSuccess || e->flags.alloc(4) != cudaSuccess ||
+      cudaMemset(e->flags.p, 0, 16) != cudaSuccess) {
     delete e;
     return HB_DEVICE_FAILED;
   }
@@ -425,6 +459,8 @@ hb_status hb_engine_destroy(hb_engine* e) {
   if (e->stream) cudaStreamSynchronize(e->stream);
   if (e->comm) ncclCommDestroy(e->comm);
   for (auto x : e->ev) cudaEventDestroy(x);
+  for (auto x : e->run_ev)
+    if (x) cudaEventDestroy(x);
   e->rec.release();
   e->col.release();
   e->colmiss.release();
@@ -460,6 +496,8 @@ hb_status hb_engine_destroy(hb_engine* e) {
   e->resident.release();
   e->seg_total.release();
   e->row_stats.release();
+  e->flags.release();
+  if (e->round_exec) cudaGraphExecDestroy(e->round_exec);
   if (e->stream) cudaStreamDestroy(e->stream);
   delete e;
   return HB_OK;
@@ -524,6 +562,8 @@ hb_status hb_engine_upload(hb_engine* e, const hb_ghist* g) {
   HB_CK(e, cudaStreamSynchronize(s));
   e->uploaded = true;
   e->alloc_depth = -1;
+  if (e->round_exec) cudaGraphExecDestroy(e->round_exec);
+  e->round_exec = nullptr;
   e->label_key = e->weight_key = nullptr;
   e->margins_loaded = false;
   e->staged = false;
@@ -815,6 +855,7 @@ hb_status hb_load_margins(hb_engine* e, const float* margins, uint64_t n) {
   if (!e->uploaded) return refuse(e, "no index uploaded");
   if (!margins || n != e->c.n_rows) return HB_INVALID_ARGUMENT;
   HB_CK(e, cudaMemcpyAsync(e->margin.p, margins, 4 * n, cudaMemcpyHostToDevice, e->stream));
+  HB_CK(e, cudaMemsetAsync(e->flags.p, 0, sizeof(int), e->stream));
   HB_CK(e, cudaStreamSynchronize(e->stream));
   e->margins_loaded = true;
   e->pending_tree = false;
@@ -854,7 +895,7 @@ hb_status hb_gradients(hb_engine* e, const hb_device_loss* loss, const float* la
   if (e->row_begin % 8) return refuse(e, "shards must start on a multiple of 8 rows");
   hb_status st = stage_labels(e, labels, weights, n);
   if (st != HB_OK) return st;
-  st = run_gradients(e, loss->kind, loss->scale_pos_weight, loss->min_hess);
+  st = run_gradients(e, loss->kind, loss->scale_pos_weight, loss->min_hess, 0);
   if (st != HB_OK) return st;
   Scale h;
   HB_CK(e, cudaMemcpyAsync(&h, e->scale.p, sizeof(Scale), cudaMemcpyDeviceToHost, e->stream));
@@ -1056,6 +1097,96 @@ hb_status hb_grow_tree(hb_engine* e, const hb_train_params* p, hb_tree_node* nod
   return HB_OK;
 }
 
+// One boosting round (gradients, with the previous tree's leaves, and a
+// tree) as stream work.
+static hb_status round_work(hb_engine* e, const hb_train_params* p) {
+  hb_status st = run_gradients(e, p->objective, p->scale_pos_weight, 1e-16f, p->max_depth);
+  if (st != HB_OK) return st;
+  return grow_device(e, p, true);
+}
+
+// Rounds as CUDA graphs: the kernels of a round are captured once and the
+// graph replayed, so no launch gaps separate them. With timing on, all the
+// rounds are captured into one graph, each kernel family bracketed by event
+// nodes, so the per-kernel times come from the same run.
+static hb_status graph_rounds(hb_engine* e, const hb_train_params* p, int rounds) {
+  cudaStream_t s = e->stream;
+  auto capture = [&](int n, cudaGraphExec_t* exec) -> hb_status {
+    HB_CK(e, cudaStreamBeginCapture(s, cudaStreamCaptureModeThreadLocal));
+    hb_status st = HB_OK;
+    for (int r = 0; r < n && st == HB_OK; ++r) st = round_work(e, p);
+    cudaGraph_t g = nullptr;
+    cudaError_t ce = cudaStreamEndCapture(s, &g);
+    if (st != HB_OK) {
+      if (g) cudaGraphDestroy(g);
+      return st;
+    }
+    if (ce != cudaSuccess) return fail(e, "cudaStreamEndCapture", ce);
+    ce = cudaGraphInstantiate(exec, g, 0);
+    cudaGraphDestroy(g);
+    if (ce != cudaSuccess) return fail(e, "cudaGraphInstantiate", ce);
+    return HB_OK;
+  };
+  if (e->timing) {
+    // enough events for every mark of every round, created before capture
+    const size_t need = e->ev_used + (size_t)rounds * 64 + 64;
+    while (e->ev.size() < need) {
+      cudaEvent_t x;
+      HB_CK(e, cudaEventCreate(&x));
+      e->ev.push_back(x);
+      e->ev_kind.push_back(0);
+    }
+    cudaGraphExec_t exec = nullptr;
+    hb_status st = capture(rounds, &exec);
+    if (st != HB_OK) return st;
+    HB_CK(e, cudaEventRecord(e->run_ev[0], s));
+    cudaError_t ce = cudaGraphLaunch(exec, s);
+    if (ce == cudaSuccess) ce = cudaEventRecord(e->run_ev[1], s);
+    cudaError_t ce2 = cudaStreamSynchronize(s);
+    cudaGraphExecDestroy(exec);
+    if (ce != cudaSuccess) return fail(e, "cudaGraphLaunch", ce);
+    if (ce2 != cudaSuccess) return fail(e, "cudaStreamSynchronize", ce2);
+    return HB_OK;
+  }
+  // the round graph depends on the parameters, the communicator and every
+  // buffer it touches (a buffer that grew has moved)
+  const void* ptrs[] = {e->comm, e->rec.p, e->col.p, e->colmiss.p, e->fo.p, e->cuts.p,
+                        e->gpair.p, e->margin.p, e->label.p, e->weight.p, e->rows[0].p,
+                        e->rows[1].p, e->scale.p, e->hist_all.p, e->front[0].p, e->front[1].p,
+                        e->cand.p, e->dec.p, e->items.p, e->dirbits.p, e->item_left.p,
+                        e->item_off.p, e->entries.p, e->pairs.p, e->ls.p, e->tree.p,
+                        e->wtree.p, e->forest.p, e->counts.p, e->tree_counter.p,
+                        e->row_stats.p, e->flags.p};
+  const int weighted = e->weight_key ? 1 : 0;
+  std::vector<unsigned char> key(sizeof(hb_train_params) + sizeof(ptrs) + sizeof(int) * 2);
+  std::memcpy(key.data(), p, sizeof(hb_train_params));
+  std::memcpy(key.data() + sizeof(hb_train_params), ptrs, sizeof(ptrs));
+  std::memcpy(key.data() + sizeof(hb_train_params) + sizeof(ptrs), &weighted, sizeof(int));
+  std::memcpy(key.data() + sizeof(hb_train_params) + sizeof(ptrs) + sizeof(int), &e->max_items,
+              sizeof(int));
+  if (!e->round_exec || key != e->round_key) {
+    if (e->round_exec) cudaGraphExecDestroy(e->round_exec);
+    e->round_exec = nullptr;
+    const uint64_t l0 = e->kernel_launches, r0 = e->rounds_done;
+    hb_status st = capture(1, &e->round_exec);
+    if (st != HB_OK) return st;
+    e->round_launches = e->kernel_launches - l0;
+    e->kernel_launches = l0;
+    e->rounds_done = r0;
+    e->round_key = key;
+  }
+  HB_CK(e, cudaEventRecord(e->run_ev[0], s));
+  for (int r = 0; r < rounds; ++r) {
+    HB_CK(e, cudaGraphLaunch(e->round_exec, s));
+    e->kernel_launches += e->round_launches;
+    e->rounds_done += 1;
+  }
+  HB_CK(e, cudaEventRecord(e->run_ev[1], s));
+  e->pending_tree = true;
+  e->pending_depth = p->max_depth;
+  return HB_OK;
+}
+
 hb_status hb_train_begin(hb_engine* e, const float* labels, uint64_t n, float base_margin) {
   HB_ENTER(e);
   if (!e->uploaded) return refuse(e, "no index uploaded");
@@ -1069,6 +1200,7 @@ hb_status hb_train_begin(hb_engine* e, const float* labels, uint64_t n, float ba
   }
   e->margins_loaded = true;
   e->pending_tree = false;
+  HB_CK(e, cudaMemsetAsync(e->flags.p, 0, sizeof(int), s));
   e->label_key = nullptr;
   hb_status st = stage_labels(e, labels, nullptr, n);
   if (st != HB_OK) return st;
@@ -1089,12 +1221,21 @@ hb_status hb_train_rounds(hb_engine* e, const hb_train_params* p, int32_t rounds
   HB_CK(e, e->forest.alloc(std::max<size_t>((size_t)rounds * max_nodes, 1)));
   HB_CK(e, e->counts.alloc(std::max(rounds, 1)));
   HB_CK(e, cudaMemsetAsync(e->tree_counter.p, 0, 4, s));
-  for (int r = 0; r < rounds; ++r) {
-    st = run_gradients(e, p->objective, p->scale_pos_weight, 1e-16f);
+  if (e->use_graphs && rounds > 0) {
+    st = ensure_growth_buffers(e, p->max_depth);
     if (st != HB_OK) return st;
-    st = grow_device(e, p, true);
+    st = graph_rounds(e, p, rounds);
     if (st != HB_OK) return st;
-    if (e->timing && e->ev_used + 128 > e->ev.size()) collect_timers(e);
+  } else {
+    HB_CK(e, cudaEventRecord(e->run_ev[0], s));
+    for (int r = 0; r < rounds; ++r) {
+      st = run_gradients(e, p->objective, p->scale_pos_weight, 1e-16f, p->max_depth);
+      if (st != HB_OK) return st;
+      st = grow_device(e, p, true);
+      if (st != HB_OK) return st;
+      if (e->timing && e->ev_used + 128 > e->ev.size()) collect_timers(e);
+    }
+    HB_CK(e, cudaEventRecord(e->run_ev[1], s));
   }
   st = flush_pending(e);
   if (st != HB_OK) return st;
@@ -1102,6 +1243,10 @@ hb_status hb_train_rounds(hb_engine* e, const hb_train_params* p, int32_t rounds
   HB_CK(e, cudaMemcpyAsync(cnt.data(), e->counts.p, 4 * (size_t)std::max(rounds, 1), cudaMemcpyDeviceToHost, s));
   HB_CK(e, cudaStreamSynchronize(s));
   collect_timers(e);
+  {
+    float ms = 0.0f;
+    e->last_rounds_ms = (rounds > 0 && cudaEventElapsedTime(&ms, e->run_ev[0], e->run_ev[1]) == cudaSuccess) ? ms : 0.0;
+  }
   uint64_t used = 0;
   tree_ptr[0] = 0;
   for (int r = 0; r < rounds; ++r) {
@@ -1138,7 +1283,9 @@ hb_status hb_engine_reset_stats(hb_engine* e, int32_t timing) {
   e->ev_used = 0;
   e->kernel_launches = 0;
   e->rounds_done = 0;
+  // 1: events around the histogram launches only; 2: around every family
   e->timing = timing != 0;
+  e->timing_mask = timing >= 2 ? 0xffu : ((1u << T_ROOT) | (1u << T_HIST));
   HB_CK(e, cudaMemsetAsync(e->row_stats.p, 0, 16, e->stream));
   HB_CK(e, cudaStreamSynchronize(e->stream));
   return HB_OK;
@@ -1159,6 +1306,7 @@ hb_status hb_engine_get_stats(hb_engine* e, hb_engine_stats* out) {
   out->rows_built_contiguous = rs[0];
   out->rows_built_gathered = rs[1];
   out->rounds = e->rounds_done;
+  out->last_rounds_ms = e->last_rounds_ms;
   return HB_OK;
 }
 

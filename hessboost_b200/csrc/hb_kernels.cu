@@ -149,8 +149,9 @@ __device__ __forceinline__ void stage_tree(const WNode* __restrict__ wtree, cons
 // over its binned record (the partition's routing rule), in row order.
 __global__ void k_walk(const WNode* __restrict__ wtree, const LevelState* __restrict__ ls_last,
                        const uint8_t* __restrict__ rec, uint32_t stride, uint32_t mask_off, uint64_t n,
-                       float* __restrict__ margin) {
+                       float* __restrict__ margin, const int* __restrict__ pending) {
   extern __shared__ WNode s_tree[];
+  if (!*pending) return;
   stage_tree(wtree, ls_last, s_tree);
   for (uint64_t i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n;
        i += (uint64_t)gridDim.x * blockDim.x) {
@@ -163,8 +164,9 @@ __global__ void k_gradients(int kind, float* __restrict__ margin,
                             float spw, float min_hess, uint64_t n, uint64_t vrows,
                             float2* __restrict__ gpair, Scale* scale, const WNode* __restrict__ wtree,
                             const LevelState* __restrict__ ls_last, const uint8_t* __restrict__ rec,
-                            uint32_t stride, uint32_t mask_off) {
+                            uint32_t stride, uint32_t mask_off, const int* __restrict__ pending) {
   extern __shared__ WNode s_tree[];
+  if (wtree && !(pending && *pending)) wtree = nullptr;  // no tree waiting for the margins
   if (wtree) stage_tree(wtree, ls_last, s_tree);
   float mg = 0.0f, mh = 0.0f;
   bool nonfinite = false;
@@ -231,7 +233,8 @@ __device__ __forceinline__ double pow2d(int e) {
   return __longlong_as_double((long long)(1023 + e) << 52);  // e in [-1022, 1023]
 }
 
-__global__ void k_scale(Scale* scale, uint64_t global_rows) {
+__global__ void k_scale(Scale* scale, uint64_t global_rows, int* pending) {
+  if (pending) *pending = 0;  // the gradient pass before has added the pending tree
   Scale s = *scale;
   s.sg = fixed_scale(__uint_as_float(s.maxg_bits), global_rows);
   s.sh = fixed_scale(__uint_as_float(s.maxh_bits), global_rows);
@@ -1255,22 +1258,27 @@ __global__ void k_add_segment(const uint32_t* __restrict__ rows, uint32_t begin,
 void launch_gradients(int kind, float* margin, const float* label, const float* weight, float spw,
                       float min_hess, uint64_t n, uint64_t vrows, float2* gpair, Scale* scale,
                       const WNode* wtree, const LevelState* ls_last, int max_nodes,
-                      const uint8_t* rec, uint32_t stride, uint32_t mask_off, int n_sm,
-                      cudaStream_t s) {
+                      const uint8_t* rec, uint32_t stride, uint32_t mask_off, const int* pending,
+                      int n_sm, cudaStream_t s) {
   int grid = (int)std::min<uint64_t>((n + 255) / 256, (uint64_t)n_sm * 8);
   if (grid < 1) grid = 1;
   const size_t smem = wtree ? sizeof(WNode) * (size_t)max_nodes : 0;
   k_gradients<<<grid, 256, smem, s>>>(kind, margin, label, weight, spw, min_hess, n, vrows, gpair, scale,
-                                      wtree, ls_last, rec, stride, mask_off);
+                                      wtree, ls_last, rec, stride, mask_off, pending);
 }
 
 void launch_walk(const WNode* wtree, const LevelState* ls_last, int max_nodes, const uint8_t* rec,
-                 uint32_t stride, uint32_t mask_off, uint64_t n, float* margin, int n_sm,
-                 cudaStream_t s) {
+                 uint32_t stride, uint32_t mask_off, uint64_t n, float* margin, const int* pending,
+                 int n_sm, cudaStream_t s) {
   int grid = (int)std::min<uint64_t>((n + 255) / 256, (uint64_t)n_sm * 8);
   if (grid < 1) grid = 1;
   k_walk<<<grid, 256, sizeof(WNode) * (size_t)max_nodes, s>>>(wtree, ls_last, rec, stride, mask_off, n,
-                                                              margin);
+                                                              margin, pending);
+}
+
+void hist_configure() {
+  cudaFuncSetAttribute(k_hist, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024 - 1024);
+  cudaFuncSetAttribute(k_hist32, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024 - 1024);
 }
 
 void launch_pair_maxima(const float2* gpair, uint64_t n, Scale* scale, int n_sm, cudaStream_t s) {
@@ -1279,8 +1287,8 @@ void launch_pair_maxima(const float2* gpair, uint64_t n, Scale* scale, int n_sm,
   k_pair_maxima<<<grid, 256, 0, s>>>(gpair, n, scale);
 }
 
-void launch_scale(Scale* scale, uint64_t global_rows, cudaStream_t s) {
-  k_scale<<<1, 1, 0, s>>>(scale, global_rows);
+void launch_scale(Scale* scale, uint64_t global_rows, int* pending, cudaStream_t s) {
+  k_scale<<<1, 1, 0, s>>>(scale, global_rows, pending);
 }
 
 void launch_encode(const uint8_t* col, const uint64_t* colmiss, uint64_t n_rows, uint32_t n_cols,

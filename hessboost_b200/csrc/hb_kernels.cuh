@@ -9,20 +9,25 @@ namespace hb {
 
 // Objective gradients at `margin` (the host's bits, see hb_kernels.cu) plus
 // the largest |g|, |h| and a non-finite flag, folded into `scale`.
-// With `wtree`, each row first adds its leaf of that tree to its margin.
+// With `wtree` and *pending set, each row first adds its leaf of that tree
+// to its margin.
 void launch_gradients(int kind, float* margin, const float* label, const float* weight, float spw,
                       float min_hess, uint64_t n, uint64_t vrows, float2* gpair, Scale* scale,
                       const WNode* wtree, const LevelState* ls_last, int max_nodes,
-                      const uint8_t* rec, uint32_t stride, uint32_t mask_off, int n_sm,
-                      cudaStream_t s);
-// Add each row's leaf of `wtree` to its margin.
+                      const uint8_t* rec, uint32_t stride, uint32_t mask_off, const int* pending,
+                      int n_sm, cudaStream_t s);
+// When *pending is set, add each row's leaf of `wtree` to its margin.
 void launch_walk(const WNode* wtree, const LevelState* ls_last, int max_nodes, const uint8_t* rec,
-                 uint32_t stride, uint32_t mask_off, uint64_t n, float* margin, int n_sm,
-                 cudaStream_t s);
+                 uint32_t stride, uint32_t mask_off, uint64_t n, float* margin, const int* pending,
+                 int n_sm, cudaStream_t s);
 // |g|, |h| maxima of staged pairs (HistogramBackend::prepare).
 void launch_pair_maxima(const float2* gpair, uint64_t n, Scale* scale, int n_sm, cudaStream_t s);
 // Fixed-point exponents from the (reduced) maxima and the global row count.
-void launch_scale(Scale* scale, uint64_t global_rows, cudaStream_t s);
+// ... and clear the pending-tree flag (`pending` may be null).
+void launch_scale(Scale* scale, uint64_t global_rows, int* pending, cudaStream_t s);
+// Grant the histogram kernels their shared memory (once per device, before
+// any stream capture).
+void hist_configure();
 // Feature-major bins (+ bitmap) -> row-major records.
 void launch_encode(const uint8_t* col, const uint64_t* colmiss, uint64_t n_rows, uint32_t n_cols,
                    uint32_t stride, uint32_t mask_off, uint8_t* rec, cudaStream_t s);

@@ -268,7 +268,13 @@ typedef struct hb_engine_stats {
   uint64_t rows_built_contiguous;
   uint64_t rows_built_gathered;
   uint64_t rounds;
+  /* device time of the last hb_train_rounds call's rounds: CUDA events on
+   * the engine's stream right before the first round's work and after the
+   * last (graph capture and the trees' read-back excluded) */
+  double last_rounds_ms;
 } hb_engine_stats;
+/* timing: 0 none, 1 events around the histogram kernel only (the light
+ * setting for a timed run), 2 events around every kernel family. */
 hb_status hb_engine_reset_stats(hb_engine* e, int32_t timing);
 hb_status hb_engine_get_stats(hb_engine* e, hb_engine_stats* out);
 /* The engine's CUDA stream (a cudaStream_t), for callers that order their
