@@ -207,6 +207,7 @@ SIGNATURES = {
     "hb_prepare": [_vp, _f32p, ctypes.c_uint64],
     "hb_build": [_vp, _u32p, ctypes.c_uint64, _P(GradStats)],
     "hb_build_features": [_vp, _u32p, ctypes.c_uint64, _u32p, ctypes.c_uint32, _P(GradStats)],
+    "hb_build_noalloc": [_vp, ctypes.c_void_p, ctypes.c_uint64, ctypes.c_void_p],
     "hb_begin_tree": [_vp, _u32p, ctypes.c_uint64, _P(Segment)],
     "hb_root_total": [_vp, _P(Segment), _P(GradStats)],
     "hb_partition": [_vp, _P(RowSplit), ctypes.c_uint32, _P(Partitioned)],
@@ -449,6 +450,11 @@ class Engine:
         out = (GradStats * self.matrix.total_bins)()
         self._c(lib().hb_build(self.h, _ptr(rows, ctypes.c_uint32), rows.size, out), "hb_build")
         return np.ctypeslib.as_array(out).view(np.float64).reshape(-1, 2).copy()
+
+    def build_noalloc(self, rows_ptr, n, out_ptr):
+        """hb_build_noalloc on caller-owned device buffers: `rows_ptr` holds n
+        ascending u32 row ids, `out_ptr` receives total_bins (g, h) f64 pairs."""
+        self._c(lib().hb_build_noalloc(self.h, rows_ptr, n, out_ptr), "hb_build_noalloc")
 
     # RowEngine
     def begin_tree(self, rows):

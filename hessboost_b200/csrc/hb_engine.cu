@@ -12,6 +12,7 @@
 #include <string>
 #include <vector>
 
+#include "hb_engine_view.h"
 #include "hb_internal.h"
 #include "hb_kernels.cuh"
 
@@ -1352,3 +1353,26 @@ extern "C" hb_status hb_engine_set_shard(hb_engine* e, uint64_t row_begin, uint6
   e->c.global_rows = global_rows;
   return HB_OK;
 }
+
+// ---- engine view for entry points in other files --------------------------
+namespace hb {
+
+void engine_view(const hb_engine* e, EngineView* v) {
+  v->device = e->device;
+  v->stream = e->stream;
+  v->n_sm = e->n_sm;
+  v->failed = e->failed;
+  v->uploaded = e->uploaded;
+  v->staged = e->staged;
+  v->c = &e->c;
+  v->fo = e->fo.p;
+  v->rec = e->rec.p;
+  v->gpair = e->gpair.p;
+  v->scale = e->scale.p;
+}
+
+hb_status engine_fail(hb_engine* e, const char* what, cudaError_t code) { return fail(e, what, code); }
+
+hb_status engine_refuse(hb_engine* e, const char* why) { return refuse(e, why); }
+
+}  // namespace hb

@@ -204,6 +204,21 @@ hb_status hb_build(hb_engine* e, const uint32_t* rows, uint64_t n, hb_grad_stats
 hb_status hb_build_features(hb_engine* e, const uint32_t* rows, uint64_t n,
                             const uint32_t* features, uint32_t n_features, hb_grad_stats* out);
 
+/* hb_build for callers that may not allocate device memory while they run
+ * (a host framework that owns all of HBM through its own pool, say). No
+ * counterpart in the reference. `rows_dev` (n ascending row ids, u32) and
+ * `out_dev` (total_bins (grad, hess) pairs, f64) are device memory of the
+ * engine's GPU; the histogram is written to out_dev and the call returns
+ * after its kernels finish. Its working memory is one static device array
+ * of 512 KiB per device, which limits the index to 32,768 bins (refused
+ * above that). It allocates nothing: the first call on a device only looks
+ * up that array's address, and should come before any stream capture.
+ * Calls on one device share the array; the library serialises them, since
+ * overlapping calls would race on it. Bad row ids (not ascending, or past
+ * the index) are refused with out_dev zeroed; no row is read. */
+hb_status hb_build_noalloc(hb_engine* e, const uint32_t* rows_dev, uint64_t n,
+                           hb_grad_stats* out_dev);
+
 /* ---- RowEngine (src/tree/hist/mod.rs:213) -------------------------- */
 hb_status hb_begin_tree(hb_engine* e, const uint32_t* rows, uint64_t n, hb_segment* root);
 hb_status hb_root_total(hb_engine* e, const hb_segment* seg, hb_grad_stats* out);
