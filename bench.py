@@ -40,13 +40,18 @@ MISSING = 0.05
 PARAMS = dict(objective="binary:logistic", max_depth=8, eta=0.1, max_bin=256)
 
 
+def set_rows(n):
+    global N_ROWS
+    N_ROWS = int(n)
+
+
 def log(*a):
     print(*a, file=sys.stderr, flush=True)
 
 
 def config(n_gpus):
     return {
-        "workload": "C2: binary:logistic, 10,000,000 x 28 f32 N(0,1) with 5% NaN, max_bin 256, "
+        "workload": f"C2: binary:logistic, {N_ROWS:,} x 28 f32 N(0,1) with 5% NaN, max_bin 256, "
         "max_depth 8, eta 0.1, lambda 1, every row in every tree",
         "rows": N_ROWS,
         "features": N_COLS,
@@ -176,7 +181,11 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--rows", type=int, default=N_ROWS,
+                    help="rows of the synthetic matrix (default: the C2 workload's 10M; smaller "
+                         "values are for profiling captures)")
     args = ap.parse_args()
+    set_rows(args.rows)
     if args.impl == "reference":
         run_reference(args)
         return
@@ -218,18 +227,16 @@ def main():
     x, y = make_data()
     params = H.TrainingParams(**PARAMS)
     # cut table over the whole matrix (rank 0), shared so every rank bins
-    # against the same cuts
-    if rank == 0:
-        off, cuts = H.cuts_dense(x, 256)
-    else:
-        off = cuts = None
+    # against the same cuts; the index-level dense flag is the whole matrix's
     if world > 1:
-        obj = [off, cuts]
-        dist.broadcast_object_list(obj, src=0)
-        off, cuts = obj
-    begin, end = hdist.shard_bounds(N_ROWS, world, rank)
-    cols, miss, dense = H.bin_dense(x[begin:end], off, cuts)
-    shard = H.BinnedMatrix(off, cuts, cols, miss, dense)
+        shard, begin, end = hdist.shard_matrix(dist, x, 256)
+    else:
+        begin, end = 0, N_ROWS
+        off, cuts = H.cuts_dense(x, 256)
+        cols, miss, dense = H.bin_dense(x, off, cuts)
+        shard = H.BinnedMatrix(off, cuts, cols, miss, dense)
+    off, cuts, cols, miss, dense = (shard.feature_offset, shard.cut_values, shard.columns,
+                                    shard.missing, shard.dense)
     base = H.base_margin(params, y)
     log(f"[rank {rank}] data + binning {time.perf_counter() - t_data:.1f}s rows [{begin}, {end})")
 

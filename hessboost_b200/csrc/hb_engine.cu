@@ -458,6 +458,9 @@ hb_status hb_engine_destroy(hb_engine* e) {
   if (!e) return HB_INVALID_ARGUMENT;
   cudaSetDevice(e->device);
   if (e->stream) cudaStreamSynchronize(e->stream);
+  // the round graph holds the level allreduces: release it before the communicator
+  if (e->round_exec) cudaGraphExecDestroy(e->round_exec);
+  e->round_exec = nullptr;
   if (e->comm) ncclCommDestroy(e->comm);
   for (auto x : e->ev) cudaEventDestroy(x);
   for (auto x : e->run_ev)
@@ -498,7 +501,6 @@ hb_status hb_engine_destroy(hb_engine* e) {
   e->seg_total.release();
   e->row_stats.release();
   e->flags.release();
-  if (e->round_exec) cudaGraphExecDestroy(e->round_exec);
   if (e->stream) cudaStreamDestroy(e->stream);
   delete e;
   return HB_OK;
@@ -1334,6 +1336,9 @@ hb_status hb_comm_init(hb_engine* e, int32_t nranks, int32_t rank, const uint8_t
   ncclUniqueId u;
   std::memcpy(u.internal, id, 128);
   if (e->comm) {
+    HB_CK(e, cudaStreamSynchronize(e->stream));
+    if (e->round_exec) cudaGraphExecDestroy(e->round_exec);  // captured with the old communicator
+    e->round_exec = nullptr;
     ncclCommDestroy(e->comm);
     e->comm = nullptr;
   }
