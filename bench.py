@@ -40,6 +40,24 @@ MISSING = 0.05
 PARAMS = dict(objective="binary:logistic", max_depth=8, eta=0.1, max_bin=256)
 
 
+# The one JSON line goes to the real stdout; everything else that writes to
+# file descriptor 1 (NCCL's version banner, library messages) goes to stderr.
+_RESULT = None
+
+
+def claim_stdout():
+    global _RESULT
+    sys.stdout.flush()
+    _RESULT = os.fdopen(os.dup(1), "w")
+    os.dup2(2, 1)
+
+
+def emit(line):
+    out = _RESULT or sys.stdout
+    out.write(json.dumps(line) + "\n")
+    out.flush()
+
+
 def set_rows(n):
     global N_ROWS
     N_ROWS = int(n)
@@ -163,14 +181,14 @@ def run_reference(args):
     sample = (f"{k} timed round(s) of the full C2 workload after binning and 1 untimed round "
               f"(C++ restatement of hessboost's CPU hist path, OpenMP on {cores} threads; "
               "the Rust reference cannot be built offline)")
-    print(json.dumps({
+    emit({
         "impl": "reference", "metric": METRIC, "value": value, "unit": UNIT,
         "n_gpus": args.gpus, "steps": k, "warmup": min(args.warmup, 1),
         "ms_per_step": 1000.0 * dt / k, "higher_is_better": True, "scaling": "strong",
         "vs_baseline": None, "dtype": "f64", "data": "synthetic", "config": config(args.gpus),
         "cpu_baseline": {"value": value, "unit": UNIT, "cores": cores, "kind": "port", "sample": sample},
         "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
-    }), flush=True)
+    })
 
 
 # ------------------------------------------------------------------ ours
@@ -186,6 +204,7 @@ def main():
                          "values are for profiling captures)")
     args = ap.parse_args()
     set_rows(args.rows)
+    claim_stdout()
     if args.impl == "reference":
         run_reference(args)
         return
@@ -355,7 +374,7 @@ def main():
             "gpu_launches": launches,
             "clocks": clocks,
         }
-        print(json.dumps(line), flush=True)
+        emit(line)
     eng.close()
     if world > 1:
         dist.destroy_process_group()

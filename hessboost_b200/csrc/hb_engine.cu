@@ -5,6 +5,7 @@
 #include <nccl.h>
 
 #include <algorithm>
+#include <climits>
 #include <cmath>
 #include <cstdio>
 #include <cstdlib>
@@ -344,7 +345,11 @@ hb_status grow_device(hb_engine* e, const hb_train_params* p, bool to_forest) {
     Front* nx = e->front[cur ^ 1].p;
     if (!leaf_only) {
       mark_begin(e, T_SCAN);
-      launch_scan(c, e->fo.p, hist, fr, lsd, e->scale.p, max_front, e->cand.p, s);
+      // level d's sibling slots start at base + half; their histograms are
+      // parent - built, made by the scan itself
+      const int sib_base = d == 0 ? INT_MAX : (1 << d) - 1 + (1 << (d - 1));
+      launch_scan(c, e->fo.p, hist, fr, lsd, d == 0 ? nullptr : e->pairs.p, sib_base, e->scale.p,
+                  max_front, e->cand.p, s);
       mark_end(e);
       ++launches;
     }
@@ -379,10 +384,7 @@ hb_status grow_device(hb_engine* e, const hb_train_params* p, bool to_forest) {
       HB_NCCL(e, ncclAllReduce(hist + base * c.total_bins, hist + base * c.total_bins,
                                2 * half * c.total_bins, ncclInt64, ncclSum, e->comm, s));
     }
-    mark_begin(e, T_SUB);
-    launch_subtract(e->pairs.p, lsn, max_front, c.total_bins, hist, s);
-    mark_end(e);
-    launches += 6;
+    launches += 5;
     HB_CK(e, cudaGetLastError());
     std::swap(rows_in, rows_out);
     cur ^= 1;
@@ -396,8 +398,8 @@ hb_status grow_device(hb_engine* e, const hb_train_params* p, bool to_forest) {
     HB_CK(e, cudaGetLastError());
   }
   // root setup + root hist + root stats, per level scan + apply (+ 3
-  // partition passes, plan, hist, subtract above the last two levels), the
-  // forest copy
+  // partition passes, plan and hist above the last two levels), the forest
+  // copy
   e->kernel_launches += launches + (to_forest ? 1 : 0);
   e->rounds_done += 1;
   return HB_OK;
@@ -1015,7 +1017,13 @@ hb_status hb_scan_resident(hb_engine* e, const hb_reg_params* reg, const hb_scan
   lsh.n_front = (int32_t)n;
   HB_CK(e, cudaMemcpyAsync(e->front[0].p, fr.data(), sizeof(Front) * n, cudaMemcpyHostToDevice, s));
   HB_CK(e, cudaMemcpyAsync(e->ls.p, &lsh, sizeof(LevelState), cudaMemcpyHostToDevice, s));
-  launch_scan(c, e->fo.p, e->resident.p, e->front[0].p, e->ls.p, e->scale.p, (int)n, e->cand.p, s);
+  for (uint32_t k0 = 0; k0 < n; k0 += 65535) {  // grid.y holds at most 65,535 nodes
+    const uint32_t m = std::min<uint32_t>(65535u, n - k0);
+    lsh.n_front = (int32_t)m;
+    HB_CK(e, cudaMemcpyAsync(e->ls.p, &lsh, sizeof(LevelState), cudaMemcpyHostToDevice, s));
+    launch_scan(c, e->fo.p, e->resident.p, e->front[0].p + k0, e->ls.p, nullptr, 0, e->scale.p,
+                (int)m, e->cand.p + (size_t)k0 * c.n_cols, s);
+  }
   HB_CK(e, cudaGetLastError());
   std::vector<Cand> cd((size_t)n * c.n_cols);
   HB_CK(e, cudaMemcpyAsync(cd.data(), e->cand.p, sizeof(Cand) * cd.size(), cudaMemcpyDeviceToHost, s));

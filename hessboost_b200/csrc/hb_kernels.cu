@@ -397,6 +397,11 @@ __global__ void __launch_bounds__(kHistThreads, 1)
 constexpr int kH32Threads = 512;
 constexpr int kSlotsPerThread = 16;  // 256 bins x 32 feature slots / 512 threads
 constexpr int kNSlots = kSlotsPerThread * kH32Threads;  // shared accumulator slots per array
+// Bin 256 of every array is a trash row: a missing cell (or a padding
+// feature of the group) adds there instead of branching around its update,
+// and the row is never folded.
+constexpr int kTrashBin = 256;
+constexpr int kSlotStride = kNSlots + 32;  // words per array, trash row included
 constexpr int kStages = 3;           // rows staged ahead with cp.async
 
 // Staging of one pass of rows (one row per thread): the group's 32 record
@@ -428,13 +433,13 @@ __global__ void __launch_bounds__(kH32Threads, 1)
   const int nf = min(kGroupFeatures, (int)c.n_cols - f0);
   constexpr int nslots = kNSlots;  // every layout fits 256 bins x 32 feature slots
   uint32_t* lo_g = s32;
-  uint32_t* hi_g = s32 + nslots;
-  uint32_t* lo_h = s32 + 2 * nslots;
-  uint32_t* hi_h = s32 + 3 * nslots;
-  StageRow* srec = reinterpret_cast<StageRow*>(s32 + 4 * nslots);        // [kStages][threads]
+  uint32_t* hi_g = s32 + kSlotStride;
+  uint32_t* lo_h = s32 + 2 * kSlotStride;
+  uint32_t* hi_h = s32 + 3 * kSlotStride;
+  StageRow* srec = reinterpret_cast<StageRow*>(s32 + 4 * kSlotStride);  // [kStages][threads]
   float2* sgp = reinterpret_cast<float2*>(srec + kStages * kH32Threads);  // [kStages][threads]
   uint32_t* smask = reinterpret_cast<uint32_t*>(sgp + kStages * kH32Threads);
-  for (int i = threadIdx.x; i < 4 * nslots; i += blockDim.x) s32[i] = 0u;
+  for (int i = threadIdx.x; i < 4 * kSlotStride; i += blockDim.x) s32[i] = 0u;
 
   long long acc_g[kSlotsPerThread], acc_h[kSlotsPerThread];
 #pragma unroll
@@ -444,6 +449,8 @@ __global__ void __launch_bounds__(kH32Threads, 1)
   const double fg = scale->fg, fh = scale->fh;
   const int tid = threadIdx.x;
   const int lane = tid & 31;
+  const uint32_t lane4 = (uint32_t)lane << 2;
+  const uint32_t sbase = (uint32_t)__cvta_generic_to_shared(s32);
   const bool wide = c.stride >= (uint32_t)(32 * g + 32);
   const uint32_t mask_at = c.mask_off + 4 * g;
   const bool mask_in_block = mask_at >= (uint32_t)(32 * g) && mask_at + 4 <= (uint32_t)(32 * g + (wide ? 32 : 16));
@@ -452,20 +459,32 @@ __global__ void __launch_bounds__(kH32Threads, 1)
   const uint32_t dummy = nf >= 32 ? 0u : (0xffffffffu << nf);  // padded features: skipped
   long long tg = 0, th = 0;
 
+  // Each thread owns kSlotsPerThread / 4 runs of four consecutive slots
+  // (slot_of below), moved with 128-bit shared loads and stores.
   auto fold = [&]() {
 #pragma unroll
-    for (int j = 0; j < kSlotsPerThread; ++j) {
-      const int slot = tid + j * kH32Threads;
-      if (slot < nslots) {
-        acc_g[j] += ((long long)(int)hi_g[slot] << lo_bits) + (long long)lo_g[slot];
-        acc_h[j] += ((long long)(int)hi_h[slot] << lo_bits) + (long long)lo_h[slot];
-        lo_g[slot] = 0u;
-        hi_g[slot] = 0u;
-        lo_h[slot] = 0u;
-        hi_h[slot] = 0u;
-      }
+    for (int j = 0; j < kSlotsPerThread / 4; ++j) {
+      const int base = 4 * (tid + j * kH32Threads);
+      const uint4 a = *reinterpret_cast<const uint4*>(&lo_g[base]);
+      const uint4 b = *reinterpret_cast<const uint4*>(&hi_g[base]);
+      const uint4 p = *reinterpret_cast<const uint4*>(&lo_h[base]);
+      const uint4 q = *reinterpret_cast<const uint4*>(&hi_h[base]);
+      const uint4 zero = make_uint4(0u, 0u, 0u, 0u);
+      *reinterpret_cast<uint4*>(&lo_g[base]) = zero;
+      *reinterpret_cast<uint4*>(&hi_g[base]) = zero;
+      *reinterpret_cast<uint4*>(&lo_h[base]) = zero;
+      *reinterpret_cast<uint4*>(&hi_h[base]) = zero;
+      acc_g[4 * j + 0] += ((long long)(int)b.x << lo_bits) + (long long)a.x;
+      acc_g[4 * j + 1] += ((long long)(int)b.y << lo_bits) + (long long)a.y;
+      acc_g[4 * j + 2] += ((long long)(int)b.z << lo_bits) + (long long)a.z;
+      acc_g[4 * j + 3] += ((long long)(int)b.w << lo_bits) + (long long)a.w;
+      acc_h[4 * j + 0] += ((long long)(int)q.x << lo_bits) + (long long)p.x;
+      acc_h[4 * j + 1] += ((long long)(int)q.y << lo_bits) + (long long)p.y;
+      acc_h[4 * j + 2] += ((long long)(int)q.z << lo_bits) + (long long)p.z;
+      acc_h[4 * j + 3] += ((long long)(int)q.w << lo_bits) + (long long)p.w;
     }
   };
+  auto slot_of = [&](int j) { return 4 * (tid + (j >> 2) * kH32Threads) + (j & 3); };
 
   int e = 0;
   while (e + 1 < n_entries && entries[e + 1].prefix <= a) ++e;
@@ -546,16 +565,23 @@ __global__ void __launch_bounds__(kH32Threads, 1)
 #pragma unroll
         for (int j = 0; j < 8; ++j) w[j] = __funnelshift_r(t[j], t[(j + 1) & 7], sh);
         const uint32_t mrot = __funnelshift_r(mask, mask, lane);
+        // slot byte offset = bin * 128 + 4 * ((lane + s) & 31); the four
+        // arrays sit kSlotStride words apart, one address for all four reds
 #pragma unroll
         for (int s = 0; s < 32; ++s) {
-          if (!((mrot >> s) & 1u)) {
-            const uint32_t bin = (w[s >> 2] >> ((s & 3) * 8)) & 0xffu;
-            const int slot = (int)(bin * 32u) + ((lane + s) & 31);
-            atomicAdd(&lo_g[slot], lg);
-            atomicAdd(&hi_g[slot], hg);
-            atomicAdd(&lo_h[slot], lh);
-            atomicAdd(&hi_h[slot], hh);
-          }
+          const uint32_t word = w[s >> 2];
+          const int k = s & 3;
+          const uint32_t binx = (k == 0 ? (word << 7) : (word >> (8 * k - 7))) & 0x7f80u;
+          const uint32_t rowx = ((mrot >> s) & 1u) ? (uint32_t)(kTrashBin << 7) : binx;
+          const uint32_t a = sbase + (rowx | ((lane4 + 4u * (uint32_t)s) & 124u));
+          asm volatile(
+              "red.shared.add.u32 [%0], %1;\n\t"
+              "red.shared.add.u32 [%0+%5], %2;\n\t"
+              "red.shared.add.u32 [%0+%6], %3;\n\t"
+              "red.shared.add.u32 [%0+%7], %4;" ::"r"(a),
+              "r"(lg), "r"(hg), "r"(lh), "r"(hh), "n"(kSlotStride * 4), "n"(kSlotStride * 8),
+              "n"(kSlotStride * 12)
+              : "memory");
         }
       }
       since_fold += kH32Threads;
@@ -574,7 +600,7 @@ __global__ void __launch_bounds__(kH32Threads, 1)
     longlong2* dst = hist + (uint64_t)en.slot * c.total_bins;
 #pragma unroll
     for (int j = 0; j < kSlotsPerThread; ++j) {
-      const int slot = tid + j * kH32Threads;
+      const int slot = slot_of(j);
       const int bin = slot >> 5, fl = slot & 31;
       if (slot < nslots && fl < nf) {
         const uint32_t fs = fo[f0 + fl];
@@ -666,131 +692,169 @@ __device__ __forceinline__ double calc_weight(double g, double h, const DevConst
   return w;
 }
 
-__device__ __forceinline__ long long shfl_ll(long long v, int src) {
-  return __shfl_sync(kFull, v, src);
+// One CTA per (frontier node, feature), one bin per thread: the feature's
+// first best candidate in for_each_numeric_split order (split.rs:391): the
+// forward pass over the bins (candidate sequence number = bin offset), then,
+// when the node has missing values of the feature, the backward pass
+// (sequence nb + (nb - 1 - offset)). Prefix sums are exact integers; the
+// backward pass's suffix at offset o is (feature total - exclusive prefix
+// at o). A node whose slot is a sibling (slot >= sib_base, with `pairs`)
+// first gets its histogram as parent - built (src/tree/hist/mod.rs:32),
+// stored for the next level, in the same pass.
+constexpr int kSplitThreads = 256;  // features of <= 256 bins
+
+__device__ __forceinline__ bool cand_better(float l, int seq, float bl, int bseq) {
+  return l > bl || (l == bl && seq < bseq);
 }
 
-// One warp per (frontier node, feature): the feature's first best candidate
-// in for_each_numeric_split order (split.rs:391): the forward pass over the
-// bins, then, when the node has missing values of the feature, the
-// backward pass. Prefix sums are exact integers; the backward pass's
-// suffix at offset o is (feature total - exclusive prefix at o).
-__global__ void k_scan(DevConst c, const uint32_t* __restrict__ fo,
-                       const longlong2* __restrict__ hist, const Front* __restrict__ front,
-                       const LevelState* __restrict__ ls, const Scale* __restrict__ scale,
-                       Cand* __restrict__ cand) {
-  const int warp = (int)((blockIdx.x * blockDim.x + threadIdx.x) >> 5);
-  const int lane = threadIdx.x & 31;
-  const int n_front = ls->n_front;
-  const int k = warp / (int)c.n_cols;
-  const int f = warp % (int)c.n_cols;
-  if (k >= n_front) return;
+__global__ void __launch_bounds__(kSplitThreads)
+    k_scan(DevConst c, const uint32_t* __restrict__ fo, longlong2* __restrict__ hist,
+           const Front* __restrict__ front, const LevelState* __restrict__ ls,
+           const Triple* __restrict__ pairs, int sib_base, const Scale* __restrict__ scale,
+           Cand* __restrict__ cand) {
+  const int f = blockIdx.x;
+  const int k = blockIdx.y;
+  if (k >= ls->n_front) return;
+  const int t = threadIdx.x, lane = t & 31, warp = t >> 5;
   const Front fr = front[k];
   const uint32_t fs = fo[f];
   const int nb = (int)(fo[f + 1] - fs);
-  Cand out;
-  out.loss = -INFINITY;
-  out.bin = -1;
-  out.default_left = 0;
-  out.pad = 0;
-  out.lg = out.lh = 0;
+  Cand* out = cand + (uint64_t)k * c.n_cols + f;
+  longlong2 v = make_longlong2(0, 0);
+  if (fr.slot >= 0 && t < nb) {
+    if (pairs != nullptr && fr.slot >= sib_base) {
+      const Triple tr = pairs[fr.slot - sib_base];
+      const longlong2 pv = hist[(uint64_t)tr.parent * c.total_bins + fs + t];
+      const longlong2 bv = hist[(uint64_t)tr.built * c.total_bins + fs + t];
+      v = make_longlong2(pv.x - bv.x, pv.y - bv.y);
+      hist[(uint64_t)fr.slot * c.total_bins + fs + t] = v;
+    } else {
+      v = hist[(uint64_t)fr.slot * c.total_bins + fs + t];
+    }
+  }
   if (nb <= 1 || fr.slot < 0) {
-    if (lane == 0) cand[(uint64_t)k * c.n_cols + f] = out;
+    if (t == 0) {
+      Cand e;
+      e.loss = -INFINITY;
+      e.bin = -1;
+      e.default_left = 0;
+      e.pad = 0;
+      e.lg = e.lh = 0;
+      *out = e;
+    }
     return;
   }
-  const longlong2* H = hist + (uint64_t)fr.slot * c.total_bins + fs;
-  const double ig = scale->ig, ih = scale->ih;
-  const float root_gain = node_gain(ll2d(fr.g) * ig, ll2d(fr.h) * ih, c);
-  const int K = (nb + 31) / 32;  // <= 8 bins per lane (features of <= 256 bins)
-  long long vg[8], vh[8];
-  long long lsg = 0, lsh = 0;
-#pragma unroll
-  for (int j = 0; j < 8; ++j) {
-    const int o = lane * K + j;
-    longlong2 v = make_longlong2(0, 0);
-    if (j < K && o < nb) v = H[o];
-    vg[j] = v.x;
-    vh[j] = v.y;
-    lsg += v.x;
-    lsh += v.y;
-  }
-  // exclusive warp scan of the lane sums
-  long long ig_ = lsg, ih_ = lsh;
+  // block inclusive scan of the exact (g, h) sums
+  __shared__ long long s_wg[kSplitThreads / 32], s_wh[kSplitThreads / 32];
+  __shared__ float s_bl[kSplitThreads / 32];
+  __shared__ int s_bs[kSplitThreads / 32];
+  long long ig_ = v.x, ih_ = v.y;
 #pragma unroll
   for (int d = 1; d < 32; d <<= 1) {
-    const long long tg = shfl_ll(ig_, (lane - d) & 31);
-    const long long th = shfl_ll(ih_, (lane - d) & 31);
+    const long long tg = __shfl_up_sync(kFull, ig_, d);
+    const long long th = __shfl_up_sync(kFull, ih_, d);
     if (lane >= d) {
       ig_ += tg;
       ih_ += th;
     }
   }
-  const long long tot_g = shfl_ll(ig_, 31), tot_h = shfl_ll(ih_, 31);
-  long long ag = ig_ - lsg, ah = ih_ - lsh;
+  if (lane == 31) {
+    s_wg[warp] = ig_;
+    s_wh[warp] = ih_;
+  }
+  __syncthreads();
+  long long off_g = 0, off_h = 0, tot_g = 0, tot_h = 0;
+#pragma unroll
+  for (int w = 0; w < kSplitThreads / 32; ++w) {
+    const long long a = s_wg[w], b = s_wh[w];
+    if (w < warp) {
+      off_g += a;
+      off_h += b;
+    }
+    tot_g += a;
+    tot_h += b;
+  }
+  const long long incl_g = ig_ + off_g, incl_h = ih_ + off_h;
+  const long long excl_g = incl_g - v.x, excl_h = incl_h - v.y;
   const bool has_missing = !c.dense && !(tot_g == fr.g && tot_h == fr.h);
 
+  const double ig = scale->ig, ih = scale->ih;
+  const float root_gain = node_gain(ll2d(fr.g) * ig, ll2d(fr.h) * ih, c);
   float best = -INFINITY;
   int best_seq = INT_MAX;
-#pragma unroll
-  for (int j = 0; j < 8; ++j) {
-    const int o = lane * K + j;
-    if (j < K && o < nb) {
-      const long long pg = ag, ph = ah;
-      ag += vg[j];
-      ah += vh[j];
-      {
-        const float l = cand_loss(ll2d(ag) * ig, ll2d(ah) * ih, ll2d(fr.g - ag) * ig,
-                                  ll2d(fr.h - ah) * ih, root_gain, c);
-        if (isfinite(l) && (l > best || (l == best && o < best_seq))) {
-          best = l;
-          best_seq = o;
-          out.bin = (int)fs + o;
-          out.default_left = 0;
-          out.lg = ag;
-          out.lh = ah;
-        }
-      }
-      if (has_missing) {
-        const long long rg = tot_g - pg, rh = tot_h - ph;
-        const long long lg2 = fr.g - rg, lh2 = fr.h - rh;
-        const float l = cand_loss(ll2d(lg2) * ig, ll2d(lh2) * ih, ll2d(rg) * ig, ll2d(rh) * ih,
-                                  root_gain, c);
-        const int seq = nb + (nb - 1 - o);
-        if (isfinite(l) && (l > best || (l == best && seq < best_seq))) {
-          best = l;
-          best_seq = seq;
-          out.bin = o == 0 ? -1 : (int)fs + o - 1;
-          out.default_left = 1;
-          out.lg = lg2;
-          out.lh = lh2;
-        }
+  long long blg = 0, blh = 0;
+  int bbin = -1, bdl = 0;
+  if (t < nb) {
+    const float l = cand_loss(ll2d(incl_g) * ig, ll2d(incl_h) * ih, ll2d(fr.g - incl_g) * ig,
+                              ll2d(fr.h - incl_h) * ih, root_gain, c);
+    if (isfinite(l)) {
+      best = l;
+      best_seq = t;
+      blg = incl_g;
+      blh = incl_h;
+      bbin = (int)fs + t;
+      bdl = 0;
+    }
+    if (has_missing) {
+      const long long rg = tot_g - excl_g, rh = tot_h - excl_h;
+      const long long lg2 = fr.g - rg, lh2 = fr.h - rh;
+      const float lb = cand_loss(ll2d(lg2) * ig, ll2d(lh2) * ih, ll2d(rg) * ig, ll2d(rh) * ih,
+                                 root_gain, c);
+      const int seq = nb + (nb - 1 - t);
+      if (isfinite(lb) && cand_better(lb, seq, best, best_seq)) {
+        best = lb;
+        best_seq = seq;
+        blg = lg2;
+        blh = lh2;
+        bbin = t == 0 ? -1 : (int)fs + t - 1;
+        bdl = 1;
       }
     }
   }
-  // first maximum over the warp: larger loss, then earlier candidate
-  int src = lane;
+  // first maximum over the block: larger loss, then earlier candidate
+  float wb = best;
+  int ws = best_seq;
 #pragma unroll
   for (int d = 16; d > 0; d >>= 1) {
-    const float ob = __shfl_xor_sync(kFull, best, d);
-    const int os = __shfl_xor_sync(kFull, best_seq, d);
-    const int osrc = __shfl_xor_sync(kFull, src, d);
-    if (ob > best || (ob == best && os < best_seq)) {
-      best = ob;
-      best_seq = os;
-      src = osrc;
+    const float ob = __shfl_xor_sync(kFull, wb, d);
+    const int os = __shfl_xor_sync(kFull, ws, d);
+    if (cand_better(ob, os, wb, ws)) {
+      wb = ob;
+      ws = os;
     }
   }
-  if (best_seq == INT_MAX) {  // no finite candidate in this feature
-    if (lane == 0) {
-      out.loss = -INFINITY;
-      out.bin = -1;
-      out.default_left = 0;
-      out.lg = out.lh = 0;
-      cand[(uint64_t)k * c.n_cols + f] = out;
+  if (lane == 0) {
+    s_bl[warp] = wb;
+    s_bs[warp] = ws;
+  }
+  __syncthreads();
+  float gb = s_bl[0];
+  int gs = s_bs[0];
+#pragma unroll
+  for (int w = 1; w < kSplitThreads / 32; ++w)
+    if (cand_better(s_bl[w], s_bs[w], gb, gs)) {
+      gb = s_bl[w];
+      gs = s_bs[w];
     }
-  } else if (lane == src) {
-    out.loss = best;
-    cand[(uint64_t)k * c.n_cols + f] = out;
+  if (gs == INT_MAX) {  // no finite candidate in this feature
+    if (t == 0) {
+      Cand e;
+      e.loss = -INFINITY;
+      e.bin = -1;
+      e.default_left = 0;
+      e.pad = 0;
+      e.lg = e.lh = 0;
+      *out = e;
+    }
+  } else if (best_seq == gs) {
+    Cand e;
+    e.loss = best;
+    e.bin = bbin;
+    e.default_left = bdl;
+    e.pad = 0;
+    e.lg = blg;
+    e.lh = blh;
+    *out = e;
   }
 }
 
@@ -1317,7 +1381,7 @@ static bool use_hist32(const DevConst& c) {
 
 size_t hist_smem_bytes(const DevConst& c) {
   if (use_hist32(c))
-    return (size_t)kNSlots * 16 +
+    return (size_t)kSlotStride * 16 +
            (size_t)kStages * kH32Threads * (sizeof(StageRow) + sizeof(float2) + sizeof(uint32_t));
   return (size_t)c.max_bins * 32 * 16;
 }
@@ -1366,12 +1430,12 @@ void launch_subtract(const Triple* pairs, const LevelState* ls, int max_pairs, u
   k_subtract<<<grid, 256, 0, s>>>(pairs, ls, total_bins, hist);
 }
 
-void launch_scan(const DevConst& c, const uint32_t* fo, const longlong2* hist, const Front* front,
-                 const LevelState* ls, const Scale* scale, int max_front, Cand* cand,
-                 cudaStream_t s) {
-  uint64_t warps = (uint64_t)max_front * c.n_cols;
-  int grid = (int)((warps * 32 + 255) / 256);
-  k_scan<<<grid, 256, 0, s>>>(c, fo, hist, front, ls, scale, cand);
+void launch_scan(const DevConst& c, const uint32_t* fo, longlong2* hist, const Front* front,
+                 const LevelState* ls, const Triple* pairs, int sib_base, const Scale* scale,
+                 int max_front, Cand* cand, cudaStream_t s) {
+  if (max_front < 1 || c.n_cols == 0) return;
+  dim3 grid(c.n_cols, max_front);
+  k_scan<<<grid, kSplitThreads, 0, s>>>(c, fo, hist, front, ls, pairs, sib_base, scale, cand);
 }
 
 void launch_apply(const DevConst& c, const uint32_t* fo, const float* cuts, const Cand* cand,
