@@ -367,6 +367,8 @@ hb_status grow_device(hb_engine* e, const hb_train_params* p, bool to_forest) {
     }
     const int max_items = std::min(e->max_items, (int)((c.n_rows + kTile - 1) / kTile) + max_front);
     mark_begin(e, T_PART);
+    // feature columns, not row records: a level's gathers of one feature's
+    // column and bitmap stay in L2, records do not
     launch_part_count(c, e->col.p, e->has_missing ? e->colmiss.p : nullptr, e->rec.p, 0,
                       rows_in, d == 0, fr, e->dec.p, e->items.p, lsd, max_items, e->dirbits.p,
                       e->item_left.p, s);

@@ -1124,8 +1124,10 @@ __global__ void __launch_bounds__(kPartThreads)
 }
 
 // One CTA per splitting frontier node: exclusive scan of its tiles' left
-// counts; the children's segments.
-constexpr int kScanThreads = 256;
+// counts (each thread sums kScanPer consecutive tiles, then one block scan
+// covers kScanThreads * kScanPer tiles); the children's segments.
+constexpr int kScanThreads = 1024;
+constexpr int kScanPer = 8;
 __global__ void __launch_bounds__(kScanThreads)
     k_part_scan(const Front* __restrict__ front, const Decision* __restrict__ dec,
                 const LevelState* __restrict__ ls, const uint32_t* __restrict__ item_left,
@@ -1137,13 +1139,24 @@ __global__ void __launch_bounds__(kScanThreads)
   const Decision d = dec[k];
   if (!d.split) return;
   uint32_t run = 0;
-  for (int base = 0; base < d.item_count; base += kScanThreads) {
-    const int t = base + threadIdx.x;
-    const uint32_t v = t < d.item_count ? item_left[d.item_begin + t] : 0u;
+  for (int base = 0; base < d.item_count; base += kScanThreads * kScanPer) {
+    const int t0 = base + (int)threadIdx.x * kScanPer;
+    uint32_t v[kScanPer];
+    uint32_t sum = 0;
+#pragma unroll
+    for (int i = 0; i < kScanPer; ++i) {
+      v[i] = t0 + i < d.item_count ? item_left[d.item_begin + t0 + i] : 0u;
+      sum += v[i];
+    }
     uint32_t ex = 0, agg = 0;
-    Scan(tmp).ExclusiveSum(v, ex, agg);
+    Scan(tmp).ExclusiveSum(sum, ex, agg);
     __syncthreads();
-    if (t < d.item_count) item_left_off[d.item_begin + t] = run + ex;
+    uint32_t at = run + ex;
+#pragma unroll
+    for (int i = 0; i < kScanPer; ++i) {
+      if (t0 + i < d.item_count) item_left_off[d.item_begin + t0 + i] = at;
+      at += v[i];
+    }
     run += agg;
   }
   if (threadIdx.x == 0) {
