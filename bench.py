@@ -96,7 +96,7 @@ class ClockSampler:
 
     def __init__(self, gpus):
         self.path = tempfile.mktemp(suffix=".csv")
-        q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+        q = ("timestamp,index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
         try:
@@ -107,7 +107,10 @@ class ClockSampler:
         except Exception:  # noqa: BLE001
             self.proc = None
 
-    def stop(self):
+    def stop(self, t0=None, t1=None):
+        """Median SM clock and throttle reasons of the samples taken in
+        [t0 - 0.25 s, t1 + 0.05 s] (host wall clock), or of all samples when
+        none fall in that window."""
         if self.proc is None:
             return None
         self.proc.terminate()
@@ -115,30 +118,37 @@ class ClockSampler:
             self.proc.wait(timeout=5)
         except Exception:  # noqa: BLE001
             self.proc.kill()
-        sm, mx, reasons = [], [], set()
+        from datetime import datetime
+
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        samples = []
         try:
             for line in open(self.path):
                 f = [x.strip() for x in line.split(",")]
-                if len(f) < 9:
+                if len(f) < 10:
                     continue
                 try:
-                    sm.append(float(f[1]))
-                    mx.append(float(f[2]))
+                    ts = datetime.strptime(f[0], "%Y/%m/%d %H:%M:%S.%f").timestamp()
+                    sm, mx = float(f[2]), float(f[3])
                 except ValueError:
                     continue
-                for name, v in zip(names, f[5:9]):
-                    if v.lower().startswith("active"):
-                        reasons.add(name)
+                rs = {name for name, v in zip(names, f[6:10]) if v.lower().startswith("active")}
+                samples.append((ts, sm, mx, rs))
         finally:
             try:
                 os.unlink(self.path)
             except OSError:
                 pass
-        if not sm:
+        if t0 is not None and t1 is not None:
+            inside = [x for x in samples if t0 - 0.25 <= x[0] <= t1 + 0.05]
+            if inside:
+                samples = inside
+        if not samples:
             return None
-        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": max(mx), "reasons": sorted(reasons),
-                "samples": len(sm)}
+        reasons = set().union(*(x[3] for x in samples))
+        return {"sm_mhz": statistics.median(x[1] for x in samples),
+                "sm_max_mhz": max(x[2] for x in samples), "reasons": sorted(reasons),
+                "samples": len(samples)}
 
 
 def make_data():
@@ -267,27 +277,31 @@ def main():
     eng.upload(shard)
     y_shard = np.ascontiguousarray(y[begin:end])
     eng.train_begin(y_shard, base)
+    # clocks sampled from before the warm-up to the end of the timed region
+    # (nvidia-smi needs a moment to start)
+    sampler = ClockSampler([local]) if rank == 0 else None
     eng.train_rounds(params, args.warmup)
 
     # ---- timed region: K rounds, device time, max over ranks
-    sampler = ClockSampler([local]) if rank == 0 else None
     eng.reset_stats(timing=1)  # CUDA events around every histogram launch only
     stream = torch.cuda.ExternalStream(eng.stream(), device=torch.device("cuda", local))
     ev0 = torch.cuda.Event(enable_timing=True)
     ev1 = torch.cuda.Event(enable_timing=True)
     barrier()
     torch.cuda.synchronize()
+    t_wall0 = time.time()
     ev0.record(stream)
     nodes, tree_ptr = eng.train_rounds(params, args.steps)
     ev1.record(stream)
     torch.cuda.synchronize()
+    t_wall1 = time.time()
     barrier()
     st = eng.stats()
     # the K rounds' device time: CUDA events the engine records on its
     # stream around the rounds (the bracketing events above also hold the
     # host-side graph capture); max over ranks
     ms = allreduce_max(st["last_rounds_ms"] if st["last_rounds_ms"] > 0 else ev0.elapsed_time(ev1))
-    clocks = sampler.stop() if sampler else None
+    clocks = sampler.stop(t_wall0, t_wall1) if sampler else None
     launches = int(allreduce_sum(st["kernel_launches"]))
     value = args.steps / (ms / 1000.0)
 
@@ -299,11 +313,16 @@ def main():
                  + st["rows_built_gathered"] * (N_COLS + 8 + 4 + bitmap))
     achieved = alg_bytes / (hist_ms / 1000.0) / 1e9 if hist_ms > 0 else 0.0
     peak, peak_kind = peaks()
+    # DRAM bytes per launch: the ratio of DRAM traffic to algorithmic bytes
+    # that one ncu capture of a round's histogram launches measured (traffic
+    # grows with the rows, so it carries to this workload), times this run's
+    # algorithmic bytes per launch
     traffic = None
-    prof = os.path.join(ROOT, "profiles", "hist_traffic.json")
-    if os.path.exists(prof):
+    prof = os.path.join(ROOT, "profiles", "k_hist32_traffic.json")
+    if os.path.exists(prof) and hist_launches:
         try:
-            traffic = json.load(open(prof)).get("bytes_per_launch")
+            ratio = float(json.load(open(prof))["dram_bytes_per_algorithmic_byte"])
+            traffic = ratio * alg_bytes / hist_launches
         except Exception:  # noqa: BLE001
             traffic = None
     log(f"[rank {rank}] {args.steps} rounds {ms:.1f} ms; kernel ms {json.dumps(st['ms'])}")
@@ -365,7 +384,9 @@ def main():
                                   "breakdown from a separate instrumented run"),
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                          "frac": achieved / peak, "traffic": traffic,
-                         "kernel": "k_hist", "launches": hist_launches,
+                         "kernel": "k_hist32", "launches": hist_launches,
+                         "traffic_source": "profiles/k_hist32_c2_5M.md (DRAM/algorithmic ratio "
+                                           "of one ncu capture, scaled to these launches)",
                          "avg_launch_ms": hist_ms / max(hist_launches, 1),
                          "alg_bytes_per_launch": alg_bytes / max(hist_launches, 1),
                          "peak_kind": peak_kind + " (MEASURED_PEAKS.json hbm_gbs)"},
