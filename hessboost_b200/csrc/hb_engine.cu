@@ -372,11 +372,11 @@ hb_status grow_device(hb_engine* e, const hb_train_params* p, bool to_forest) {
     launch_part_count(c, e->col.p, e->has_missing ? e->colmiss.p : nullptr, e->rec.p, 0,
                       rows_in, d == 0, fr, e->dec.p, e->items.p, lsd, max_items, e->dirbits.p,
                       e->item_left.p, s);
-    launch_part_scan(fr, e->dec.p, lsd, max_front, e->item_left.p, e->item_off.p, nx, s);
+    launch_part_scan(fr, e->dec.p, lsd, max_front, e->item_left.p, e->item_off.p, nx,
+                     e->entries.p, e->pairs.p, lsn, s);
     launch_part_scatter(fr, e->dec.p, e->items.p, lsd, max_items, e->dirbits.p, e->item_off.p,
                         nx, rows_in, d == 0, rows_out, s);
     mark_end(e);
-    launch_hist_plan(fr, e->dec.p, lsd, nx, e->entries.p, e->pairs.p, lsn, 0, s);
     mark_begin(e, T_HIST);
     launch_hist(c, e->fo.p, e->rec.p, e->gpair.p, e->scale.p, rows_out, e->entries.p, lsn, hist,
                 nullptr, e->row_stats.p, hgrid, smem, s);
@@ -386,7 +386,7 @@ hb_status grow_device(hb_engine* e, const hb_train_params* p, bool to_forest) {
       HB_NCCL(e, ncclAllReduce(hist + base * c.total_bins, hist + base * c.total_bins,
                                2 * half * c.total_bins, ncclInt64, ncclSum, e->comm, s));
     }
-    launches += 5;
+    launches += 4;
     HB_CK(e, cudaGetLastError());
     std::swap(rows_in, rows_out);
     cur ^= 1;
@@ -400,8 +400,8 @@ hb_status grow_device(hb_engine* e, const hb_train_params* p, bool to_forest) {
     HB_CK(e, cudaGetLastError());
   }
   // root setup + root hist + root stats, per level scan + apply (+ 3
-  // partition passes, plan and hist above the last two levels), the forest
-  // copy
+  // partition passes, the last also planning, and hist above the last two
+  // levels), the forest copy
   e->kernel_launches += launches + (to_forest ? 1 : 0);
   e->rounds_done += 1;
   return HB_OK;
@@ -807,7 +807,7 @@ hb_status hb_partition(hb_engine* e, const hb_row_split* splits, uint32_t n, hb_
                       e->dirbits.p, e->item_left.p, s);
   }
   launch_part_scan(e->front[0].p, e->dec.p, e->ls.p, (int)n, e->item_left.p, e->item_off.p,
-                   e->front[1].p, s);
+                   e->front[1].p, nullptr, nullptr, nullptr, s);
   if (n_items) {
     launch_part_scatter(e->front[0].p, e->dec.p, e->items.p, e->ls.p, n_items, e->dirbits.p,
                         e->item_off.p, e->front[1].p, e->rows[0].p, 0, e->rows[1].p, s);

@@ -118,7 +118,7 @@ struct LevelState {
   int32_t n_pairs;        // sibling subtractions
   uint64_t hist_rows;     // rows to build this level
   int32_t tree_index;     // slot in the forest buffer
-  int32_t pad;
+  uint32_t done_ctas;     // CTAs of the level's tile scan that have finished
 };
 
 // The grown tree as the margin update walks it: a row at a node goes left

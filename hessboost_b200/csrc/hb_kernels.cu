@@ -320,8 +320,16 @@ __global__ void __launch_bounds__(kHistThreads, 1)
   const bool want_totals = totals != nullptr && g == 0;
   long long tg = 0, th = 0;
 
+  // the entry holding row position a: the last one whose prefix is <= a
+  // (binary search; prefixes ascend)
   int e = 0;
-  while (e + 1 < n_entries && entries[e + 1].prefix <= a) ++e;
+  {
+    int hi = n_entries - 1;
+    while (e < hi) {
+      const int mid = (e + hi + 1) >> 1;
+      if (entries[mid].prefix <= a) e = mid; else hi = mid - 1;
+    }
+  }
   uint64_t pos = a;
   while (pos < b && e < n_entries) {
     const HEntry en = entries[e];
@@ -486,8 +494,16 @@ __global__ void __launch_bounds__(kH32Threads, 1)
   };
   auto slot_of = [&](int j) { return 4 * (tid + (j >> 2) * kH32Threads) + (j & 3); };
 
+  // the entry holding row position a: the last one whose prefix is <= a
+  // (binary search; prefixes ascend)
   int e = 0;
-  while (e + 1 < n_entries && entries[e + 1].prefix <= a) ++e;
+  {
+    int hi = n_entries - 1;
+    while (e < hi) {
+      const int mid = (e + hi + 1) >> 1;
+      if (entries[mid].prefix <= a) e = mid; else hi = mid - 1;
+    }
+  }
   uint64_t pos = a;
   int since_fold = 0;
   while (pos < b && e < n_entries) {
@@ -784,7 +800,10 @@ __global__ void __launch_bounds__(kSplitThreads)
   int best_seq = INT_MAX;
   long long blg = 0, blh = 0;
   int bbin = -1, bdl = 0;
-  if (t < nb) {
+  // An empty bin's candidates repeat a neighbour's statistics, and that
+  // neighbour comes first in its pass (forward: offset t - 1; backward:
+  // t + 1), so it keeps any tie: an empty bin is never the first maximum.
+  if (t < nb && (v.x != 0 || v.y != 0)) {
     const float l = cand_loss(ll2d(incl_g) * ig, ll2d(incl_h) * ih, ll2d(fr.g - incl_g) * ig,
                               ll2d(fr.h - incl_h) * ih, root_gain, c);
     if (isfinite(l)) {
@@ -1125,47 +1144,65 @@ __global__ void __launch_bounds__(kPartThreads)
 
 // One CTA per splitting frontier node: exclusive scan of its tiles' left
 // counts (each thread sums kScanPer consecutive tiles, then one block scan
-// covers kScanThreads * kScanPer tiles); the children's segments.
+// covers kScanThreads * kScanPer tiles); the children's segments. With
+// `entries`, the last CTA to finish then plans the next level's histograms
+// (hist_plan_body), which needs every node's segments.
+__device__ void hist_plan_body(const Front* __restrict__ front, const Decision* __restrict__ dec,
+                               const LevelState* __restrict__ ls, const Front* next,
+                               HEntry* __restrict__ entries, Triple* __restrict__ pairs,
+                               LevelState* __restrict__ ls_next, int terminal);
 constexpr int kScanThreads = 1024;
 constexpr int kScanPer = 8;
+static_assert(kScanThreads == kApplyThreads, "the plan runs on one tile-scan CTA");
 __global__ void __launch_bounds__(kScanThreads)
     k_part_scan(const Front* __restrict__ front, const Decision* __restrict__ dec,
-                const LevelState* __restrict__ ls, const uint32_t* __restrict__ item_left,
-                uint32_t* __restrict__ item_left_off, Front* __restrict__ next) {
+                LevelState* ls, const uint32_t* __restrict__ item_left,
+                uint32_t* __restrict__ item_left_off, Front* next, HEntry* __restrict__ entries,
+                Triple* __restrict__ pairs, LevelState* __restrict__ ls_next) {
   using Scan = cub::BlockScan<uint32_t, kScanThreads>;
   __shared__ typename Scan::TempStorage tmp;
   const int k = blockIdx.x;
-  if (k >= ls->n_front) return;
-  const Decision d = dec[k];
-  if (!d.split) return;
-  uint32_t run = 0;
-  for (int base = 0; base < d.item_count; base += kScanThreads * kScanPer) {
-    const int t0 = base + (int)threadIdx.x * kScanPer;
-    uint32_t v[kScanPer];
-    uint32_t sum = 0;
+  const Decision d = k < ls->n_front ? dec[k] : Decision{};
+  if (k < ls->n_front && d.split) {
+    uint32_t run = 0;
+    for (int base = 0; base < d.item_count; base += kScanThreads * kScanPer) {
+      const int t0 = base + (int)threadIdx.x * kScanPer;
+      uint32_t v[kScanPer];
+      uint32_t sum = 0;
 #pragma unroll
-    for (int i = 0; i < kScanPer; ++i) {
-      v[i] = t0 + i < d.item_count ? item_left[d.item_begin + t0 + i] : 0u;
-      sum += v[i];
-    }
-    uint32_t ex = 0, agg = 0;
-    Scan(tmp).ExclusiveSum(sum, ex, agg);
-    __syncthreads();
-    uint32_t at = run + ex;
+      for (int i = 0; i < kScanPer; ++i) {
+        v[i] = t0 + i < d.item_count ? item_left[d.item_begin + t0 + i] : 0u;
+        sum += v[i];
+      }
+      uint32_t ex = 0, agg = 0;
+      Scan(tmp).ExclusiveSum(sum, ex, agg);
+      __syncthreads();
+      uint32_t at = run + ex;
 #pragma unroll
-    for (int i = 0; i < kScanPer; ++i) {
-      if (t0 + i < d.item_count) item_left_off[d.item_begin + t0 + i] = at;
-      at += v[i];
+      for (int i = 0; i < kScanPer; ++i) {
+        if (t0 + i < d.item_count) item_left_off[d.item_begin + t0 + i] = at;
+        at += v[i];
+      }
+      run += agg;
     }
-    run += agg;
+    if (threadIdx.x == 0) {
+      const Front fr = front[k];
+      next[2 * d.pair].begin = fr.begin;
+      next[2 * d.pair].len = run;
+      next[2 * d.pair + 1].begin = fr.begin + run;
+      next[2 * d.pair + 1].len = fr.len - run;
+    }
   }
+  if (entries == nullptr) return;
+  __shared__ bool s_last;
   if (threadIdx.x == 0) {
-    const Front fr = front[k];
-    next[2 * d.pair].begin = fr.begin;
-    next[2 * d.pair].len = run;
-    next[2 * d.pair + 1].begin = fr.begin + run;
-    next[2 * d.pair + 1].len = fr.len - run;
+    __threadfence();  // this CTA's segments before its count
+    s_last = atomicAdd(&ls->done_ctas, 1u) == gridDim.x - 1;
   }
+  __syncthreads();
+  if (!s_last) return;
+  __threadfence();
+  hist_plan_body(front, dec, ls, next, entries, pairs, ls_next, 0);
 }
 
 __global__ void __launch_bounds__(kPartThreads)
@@ -1224,12 +1261,26 @@ __global__ void __launch_bounds__(kPartThreads)
 
 // Histogram plan of the next level: for every split (not at the depth
 // limit) the child with the smaller Hessian sum is built, its sibling is
-// parent - built. Entries are in pair order with running row prefixes.
-__global__ void __launch_bounds__(kApplyThreads)
-    k_hist_plan(const Front* __restrict__ front, const Decision* __restrict__ dec,
-                const LevelState* __restrict__ ls, const Front* __restrict__ next,
-                HEntry* __restrict__ entries, Triple* __restrict__ pairs,
-                LevelState* __restrict__ ls_next, int terminal) {
+// parent - built. Entries are in pair order with running row prefixes. Run
+// by one CTA of kApplyThreads; the children's segments are read past L1
+// (other CTAs wrote them).
+__device__ __forceinline__ Front load_front_cg(const Front* p) {
+  const int4* q = reinterpret_cast<const int4*>(p);
+  const int4 x = __ldcg(q), y = __ldcg(q + 1);
+  Front f;
+  f.node = x.x;
+  f.slot = x.y;
+  f.begin = (uint32_t)x.z;
+  f.len = (uint32_t)x.w;
+  f.g = ((long long)(uint32_t)y.y << 32) | (uint32_t)y.x;
+  f.h = ((long long)(uint32_t)y.w << 32) | (uint32_t)y.z;
+  return f;
+}
+
+__device__ void hist_plan_body(const Front* __restrict__ front, const Decision* __restrict__ dec,
+                               const LevelState* __restrict__ ls, const Front* next,
+                               HEntry* __restrict__ entries, Triple* __restrict__ pairs,
+                               LevelState* __restrict__ ls_next, int terminal) {
   using Scan = cub::BlockScan<unsigned long long, kApplyThreads>;
   __shared__ typename Scan::TempStorage tmp;
   const int k = threadIdx.x;
@@ -1242,7 +1293,7 @@ __global__ void __launch_bounds__(kApplyThreads)
     const Decision d = dec[k];
     if (d.split) {
       active = true;
-      const Front l = next[2 * d.pair], r = next[2 * d.pair + 1];
+      const Front l = load_front_cg(&next[2 * d.pair]), r = load_front_cg(&next[2 * d.pair + 1]);
       const bool left_built = l.h <= r.h;
       const Front& b = left_built ? l : r;
       const Front& s = left_built ? r : l;
@@ -1468,10 +1519,11 @@ void launch_part_count(const DevConst& c, const uint8_t* col, const uint64_t* co
                                                   front, dec, items, ls, dirbits, item_left);
 }
 
-void launch_part_scan(const Front* front, const Decision* dec, const LevelState* ls, int max_front,
+void launch_part_scan(const Front* front, const Decision* dec, LevelState* ls, int max_front,
                       const uint32_t* item_left, uint32_t* item_left_off, Front* next,
-                      cudaStream_t s) {
-  k_part_scan<<<max_front, kScanThreads, 0, s>>>(front, dec, ls, item_left, item_left_off, next);
+                      HEntry* entries, Triple* pairs, LevelState* ls_next, cudaStream_t s) {
+  k_part_scan<<<max_front, kScanThreads, 0, s>>>(front, dec, ls, item_left, item_left_off, next,
+                                                 entries, pairs, ls_next);
 }
 
 void launch_part_scatter(const Front* front, const Decision* dec, const PItem* items,
@@ -1483,11 +1535,6 @@ void launch_part_scatter(const Front* front, const Decision* dec, const PItem* i
                                                     next, rows_in, identity, rows_out);
 }
 
-void launch_hist_plan(const Front* front, const Decision* dec, const LevelState* ls,
-                      const Front* next, HEntry* entries, Triple* pairs, LevelState* ls_next,
-                      int terminal, cudaStream_t s) {
-  k_hist_plan<<<1, kApplyThreads, 0, s>>>(front, dec, ls, next, entries, pairs, ls_next, terminal);
-}
 
 void launch_root_setup(uint64_t n_rows, Front* front, HEntry* entries, LevelState* ls,
                        cudaStream_t s) {

@@ -55,17 +55,18 @@ void launch_part_count(const DevConst& c, const uint8_t* col, const uint64_t* co
                        const Front* front, const Decision* dec, const PItem* items,
                        const LevelState* ls, int max_items, uint32_t* dirbits, uint32_t* item_left,
                        cudaStream_t s);
-void launch_part_scan(const Front* front, const Decision* dec, const LevelState* ls, int max_front,
+// Per-node scan of the tiles' left counts and the children's segments; with
+// `entries` (device growth) the last CTA also plans the next level's
+// histograms (built child = smaller Hessian; entries, sibling pairs, ls_next).
+// `ls->done_ctas` must be zero.
+void launch_part_scan(const Front* front, const Decision* dec, LevelState* ls, int max_front,
                       const uint32_t* item_left, uint32_t* item_left_off, Front* next,
-                      cudaStream_t s);
+                      HEntry* entries, Triple* pairs, LevelState* ls_next, cudaStream_t s);
 void launch_part_scatter(const Front* front, const Decision* dec, const PItem* items,
                          const LevelState* ls, int max_items, const uint32_t* dirbits,
                          const uint32_t* item_left_off, const Front* next,
                          const uint32_t* rows_in, int identity, uint32_t* rows_out,
                          cudaStream_t s);
-void launch_hist_plan(const Front* front, const Decision* dec, const LevelState* ls,
-                      const Front* next, HEntry* entries, Triple* pairs, LevelState* ls_next,
-                      int terminal, cudaStream_t s);
 void launch_root_setup(uint64_t n_rows, Front* front, HEntry* entries, LevelState* ls,
                        cudaStream_t s);
 void launch_root_stats(Front* front, const long long* totals, cudaStream_t s);
