@@ -706,6 +706,17 @@ class Predictor:
                "hb_predict_margin")
         return out
 
+    def predict_margin_into(self, x, out):
+        """hb_predict_margin from host rows `x` (n x n_features f32, C order)
+        into the host array `out` (n x n_outputs f32); pinned buffers make
+        the copies asynchronous."""
+        if x.dtype != np.float32 or not x.flags.c_contiguous or out.dtype != np.float32:
+            raise ValueError("x and out must be C-contiguous float32")
+        if out.size != x.shape[0] * self.n_outputs:
+            raise ValueError("out must hold n_rows x n_outputs values")
+        _check(lib().hb_predict_margin(self.h, _ptr(x, ctypes.c_float), x.shape[0], _ptr(out, ctypes.c_float)),
+               "hb_predict_margin")
+
     def predict_margin_device(self, d_rows, n_rows, d_out, stream=None):
         _check(lib().hb_predict_margin_device(self.h, d_rows, n_rows, d_out, stream), "hb_predict_margin_device")
 

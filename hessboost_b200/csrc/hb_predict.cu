@@ -5,6 +5,7 @@
 // weight[t] * leaf_t(row), each term added in f32 to output tree_output[t].
 // A node sends a row left when x[feature] < split_cond, and a missing (NaN)
 // value the node's default direction (src/tree/regtree.rs:39).
+#include <cuda_pipeline.h>
 #include <cuda_runtime.h>
 
 #include <algorithm>
@@ -52,6 +53,133 @@ __global__ void k_predict(const PNode* __restrict__ nodes, const uint32_t* __res
   }
 }
 
+// ---- complete-tree path --------------------------------------------------
+// A single-output forest whose trees are at most kCompleteMaxDepth deep is
+// also laid out as complete trees: a tree of depth d becomes 2^d - 1
+// internal nodes (CNode) in breadth-first order, children of i at 2i + 1 and
+// 2i + 2, followed by its 2^d leaf values. A leaf shallower than d fills its
+// whole subtree below: the padded internal nodes route anywhere and every
+// leaf under them is that leaf, so each row reaches the same value. The
+// walk is then d steps with no child pointers and no leaf test.
+//
+// k_predict_chunked keeps a tile of rows in shared memory (feature-major,
+// stride tile + 1 so a warp's reads of one feature are conflict-free) and
+// streams the forest through two shared buffers of kChunkBytes with
+// cp.async, the next chunk loading while the current one is walked. The
+// margin is summed in tree order with the same f32 operations as k_predict.
+constexpr int kCompleteMaxDepth = 10;
+constexpr int kPredThreads = 512;
+constexpr int kChunkBytes = 48 * 1024;
+constexpr int kPredSmemBudget = 224 * 1024;
+
+struct CNode {
+  float cond;
+  uint32_t meta;  // feature * (tile + 1): its row in the shared tile | default_left << 31
+};
+struct TreeHdr {
+  uint32_t off;    // byte offset of the tree in its chunk
+  uint32_t depth;
+  uint32_t pad;
+  float weight;
+};
+struct ChunkHdr {
+  uint32_t off;    // byte offset of the chunk in the arena
+  uint32_t bytes;  // a multiple of 16
+  uint32_t t0, t1; // its trees
+};
+
+// One step of a complete-tree walk: left iff v < cond; a missing value
+// follows default_left.
+__device__ __forceinline__ uint32_t walk_step(const CNode q, const float* xr, uint32_t idx) {
+  const float v = xr[q.meta & 0x7fffffffu];
+  const bool right = (v != v) ? (q.meta >> 31) == 0u : !(v < q.cond);
+  return 2u * idx + (right ? 2u : 1u);
+}
+
+__global__ void __launch_bounds__(kPredThreads, 1)
+    k_predict_chunked(const unsigned char* __restrict__ arena, const ChunkHdr* __restrict__ chunks,
+                      int n_chunks, const TreeHdr* __restrict__ trees, float base0,
+                      const float* __restrict__ x, uint64_t n_rows, uint32_t n_cols, int tile,
+                      uint32_t x_bytes, float* __restrict__ out) {
+  extern __shared__ __align__(16) unsigned char sm[];
+  float* s_x = reinterpret_cast<float*>(sm);  // [n_cols][tile + 1]
+  unsigned char* const buf0 = sm + x_bytes;  // chunk c lives at buf0 + (c & 1) * kChunkBytes
+  const int tid = threadIdx.x;
+  const uint64_t n_tiles = (n_rows + tile - 1) / tile;
+  for (uint64_t tl = blockIdx.x; tl < n_tiles; tl += gridDim.x) {
+    const uint64_t r0 = tl * (uint64_t)tile;
+    const uint64_t left = n_rows - r0;
+    const int rows = left < (uint64_t)tile ? (int)left : tile;
+    const float* xt = x + r0 * n_cols;
+    const int nv = rows * (int)n_cols;
+    for (int i = tid; i < nv; i += kPredThreads) {
+      const int r = i / (int)n_cols, f = i - r * (int)n_cols;
+      s_x[f * (tile + 1) + r] = __ldg(xt + i);
+    }
+    auto issue = [&](int c) {
+      const ChunkHdr ch = chunks[c];
+      unsigned char* dst = buf0 + (c & 1) * kChunkBytes;
+      for (uint32_t o = (uint32_t)tid * 16u; o < ch.bytes; o += kPredThreads * 16u)
+        __pipeline_memcpy_async(dst + o, arena + ch.off + o, 16);
+      __pipeline_commit();
+    };
+    issue(0);
+    float acc = base0;
+    const float* xr = s_x + tid;
+    for (int c = 0; c < n_chunks; ++c) {
+      if (c + 1 < n_chunks)
+        issue(c + 1);
+      else
+        __pipeline_commit();  // an empty group keeps the wait count uniform
+      __pipeline_wait_prior(1);
+      __syncthreads();        // chunk c (and, at c = 0, the row tile) visible to all
+      const ChunkHdr ch = chunks[c];
+      if (tid < rows) {
+        const unsigned char* cb = buf0 + (c & 1) * kChunkBytes;
+        uint32_t t = ch.t0;
+        // kLanes trees of one depth walked in lockstep: independent chains of
+        // shared loads; their leaves still add in tree order
+        constexpr int kLanes = 8;
+        for (; t + kLanes <= ch.t1; t += kLanes) {
+          TreeHdr h[kLanes];
+          bool same = true;
+#pragma unroll
+          for (int j = 0; j < kLanes; ++j) {
+            h[j] = trees[t + j];
+            same = same && h[j].depth == h[0].depth;
+          }
+          if (!same) break;
+          uint32_t ix[kLanes];
+#pragma unroll
+          for (int j = 0; j < kLanes; ++j) ix[j] = 0;
+          for (uint32_t k = 0; k < h[0].depth; ++k) {
+#pragma unroll
+            for (int j = 0; j < kLanes; ++j)
+              ix[j] = walk_step(reinterpret_cast<const CNode*>(cb + h[j].off)[ix[j]], xr, ix[j]);
+          }
+          const uint32_t internal = (1u << h[0].depth) - 1u;
+#pragma unroll
+          for (int j = 0; j < kLanes; ++j) {
+            const CNode* nd = reinterpret_cast<const CNode*>(cb + h[j].off);
+            acc = __fadd_rn(acc, __fmul_rn(h[j].weight, reinterpret_cast<const float*>(nd + internal)[ix[j] - internal]));
+          }
+        }
+        for (; t < ch.t1; ++t) {
+          const TreeHdr th = trees[t];
+          const CNode* nd = reinterpret_cast<const CNode*>(cb + th.off);
+          uint32_t idx = 0;
+          for (uint32_t k = 0; k < th.depth; ++k) idx = walk_step(nd[idx], xr, idx);
+          const uint32_t internal = (1u << th.depth) - 1u;
+          const float leaf = reinterpret_cast<const float*>(nd + internal)[idx - internal];
+          acc = __fadd_rn(acc, __fmul_rn(th.weight, leaf));
+        }
+      }
+      __syncthreads();  // buffer c & 1 is free for chunk c + 2; the tile for the next one
+    }
+    if (tid < rows) out[r0 + tid] = acc;
+  }
+}
+
 }  // namespace
 
 struct hb_predictor {
@@ -69,7 +197,93 @@ struct hb_predictor {
   float* stage_x = nullptr;
   float* stage_out = nullptr;
   size_t stage_rows = 0;
+  // the complete-tree layout (empty when the forest does not qualify)
+  unsigned char* carena = nullptr;
+  ChunkHdr* chunks = nullptr;
+  TreeHdr* theads = nullptr;
+  int n_chunks = 0;
+  int tile = 0;
+  uint32_t x_bytes = 0;
+  size_t smem = 0;
+  float base0 = 0.0f;
 };
+
+namespace {
+
+// The complete-tree layout of a forest, or false when a tree is deeper than
+// kCompleteMaxDepth, there is more than one output, or a row tile would not
+// fit in shared memory.
+bool build_complete(const hb_tree_node* nodes, const uint64_t* tree_ptr, uint64_t n_trees,
+                    const float* ws, int n_outputs, uint32_t n_features, int& tile,
+                    std::vector<unsigned char>& arena, std::vector<ChunkHdr>& chunks,
+                    std::vector<TreeHdr>& heads) {
+  if (n_outputs != 1 || n_features == 0 || n_trees == 0) return false;
+  const int budget_rows = (kPredSmemBudget - 2 * kChunkBytes) / (4 * (int)n_features) - 1;
+  tile = std::min(kPredThreads, budget_rows) & ~31;
+  if (tile < 32) return false;
+  heads.resize(n_trees);
+  std::vector<int> depth_of;
+  std::vector<std::pair<int32_t, int>> stack;
+  ChunkHdr cur{0, 0, 0, 0};
+  for (uint64_t t = 0; t < n_trees; ++t) {
+    const hb_tree_node* tn = nodes + tree_ptr[t];
+    const int64_t n = (int64_t)(tree_ptr[t + 1] - tree_ptr[t]);
+    // depth of the tree (the trees were checked by the caller)
+    int d = 0;
+    stack.assign(1, {0, 0});
+    while (!stack.empty()) {
+      const auto [id, k] = stack.back();
+      stack.pop_back();
+      if (id < 0 || id >= n || k > kCompleteMaxDepth) return false;
+      if (tn[id].left < 0) {
+        d = std::max(d, k);
+      } else {
+        stack.push_back({tn[id].left, k + 1});
+        stack.push_back({tn[id].right, k + 1});
+      }
+    }
+    const uint32_t internal = (1u << d) - 1u, leaves = 1u << d;
+    const uint32_t bytes = ((8u * internal + 4u * leaves) + 15u) & ~15u;
+    std::vector<unsigned char> rec(bytes, 0);
+    CNode* cn = reinterpret_cast<CNode*>(rec.data());
+    float* lf = reinterpret_cast<float*>(rec.data() + 8u * internal);
+    // fill position p (depth k) of the complete tree from node id
+    struct Item { uint32_t p; int32_t id; int k; };
+    std::vector<Item> work{{0u, 0, 0}};
+    while (!work.empty()) {
+      const Item it = work.back();
+      work.pop_back();
+      const hb_tree_node& s = tn[it.id];
+      if (it.k == d) {
+        lf[it.p - internal] = s.leaf_value;
+        continue;
+      }
+      if (s.left < 0) {  // a shallow leaf: pad its subtree
+        cn[it.p].cond = INFINITY;
+        cn[it.p].meta = 0u;
+        work.push_back({2 * it.p + 1, it.id, it.k + 1});
+        work.push_back({2 * it.p + 2, it.id, it.k + 1});
+      } else {
+        cn[it.p].cond = s.split_cond;
+        cn[it.p].meta = s.split_feature * (uint32_t)(tile + 1) | (s.default_left ? 0x80000000u : 0u);
+        work.push_back({2 * it.p + 1, s.left, it.k + 1});
+        work.push_back({2 * it.p + 2, s.right, it.k + 1});
+      }
+    }
+    if (cur.bytes + bytes > (uint32_t)kChunkBytes) {
+      chunks.push_back(cur);
+      cur = ChunkHdr{(uint32_t)arena.size(), 0, (uint32_t)t, (uint32_t)t};
+    }
+    heads[t] = TreeHdr{cur.bytes, (uint32_t)d, 0u, ws[t]};
+    arena.insert(arena.end(), rec.begin(), rec.end());
+    cur.bytes += bytes;
+    cur.t1 = (uint32_t)t + 1;
+  }
+  chunks.push_back(cur);
+  return true;
+}
+
+}  // namespace
 
 extern "C" {
 
@@ -144,6 +358,28 @@ hb_status hb_predictor_create(int32_t device_ordinal, const hb_tree_node* nodes,
          cudaMemcpy(p->outs, outs.data(), 4 * n_trees, cudaMemcpyHostToDevice) == cudaSuccess &&
          cudaMemcpy(p->weights, ws.data(), 4 * n_trees, cudaMemcpyHostToDevice) == cudaSuccess;
   if (ok) ok = cudaMemcpy(p->base, base, 4 * n_outputs, cudaMemcpyHostToDevice) == cudaSuccess;
+  if (ok) {
+    std::vector<unsigned char> carena;
+    std::vector<ChunkHdr> chunks;
+    std::vector<TreeHdr> heads;
+    int tile = 0;
+    if (build_complete(nodes, tree_ptr, n_trees, ws.data(), n_outputs, n_features, tile, carena,
+                       chunks, heads)) {
+      p->tile = tile;
+      p->n_chunks = (int)chunks.size();
+      p->x_bytes = (uint32_t)((4ull * n_features * (tile + 1) + 15) & ~15ull);
+      p->smem = p->x_bytes + 2 * (size_t)kChunkBytes;
+      p->base0 = base[0];
+      ok = cudaMalloc(&p->carena, carena.size()) == cudaSuccess &&
+           cudaMalloc(&p->chunks, sizeof(ChunkHdr) * chunks.size()) == cudaSuccess &&
+           cudaMalloc(&p->theads, sizeof(TreeHdr) * heads.size()) == cudaSuccess &&
+           cudaMemcpy(p->carena, carena.data(), carena.size(), cudaMemcpyHostToDevice) == cudaSuccess &&
+           cudaMemcpy(p->chunks, chunks.data(), sizeof(ChunkHdr) * chunks.size(), cudaMemcpyHostToDevice) == cudaSuccess &&
+           cudaMemcpy(p->theads, heads.data(), sizeof(TreeHdr) * heads.size(), cudaMemcpyHostToDevice) == cudaSuccess &&
+           cudaFuncSetAttribute(k_predict_chunked, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                (int)p->smem) == cudaSuccess;
+    }
+  }
   if (!ok) {
     hb_predictor_destroy(p);
     return HB_DEVICE_FAILED;
@@ -163,6 +399,9 @@ hb_status hb_predictor_destroy(hb_predictor* p) {
   cudaFree(p->base);
   cudaFree(p->stage_x);
   cudaFree(p->stage_out);
+  cudaFree(p->carena);
+  cudaFree(p->chunks);
+  cudaFree(p->theads);
   if (p->stream) cudaStreamDestroy(p->stream);
   delete p;
   return HB_OK;
@@ -174,6 +413,14 @@ hb_status hb_predict_margin_device(hb_predictor* p, const float* d_rows, uint64_
   if (cudaSetDevice(p->device) != cudaSuccess) return HB_DEVICE_FAILED;
   if (!n_rows) return HB_OK;
   cudaStream_t s = stream ? (cudaStream_t)stream : p->stream;
+  if (p->n_chunks > 0) {
+    const uint64_t tiles = (n_rows + p->tile - 1) / p->tile;
+    const int grid = (int)std::min<uint64_t>(tiles, (uint64_t)p->n_sm);
+    k_predict_chunked<<<grid, kPredThreads, p->smem, s>>>(p->carena, p->chunks, p->n_chunks,
+                                                          p->theads, p->base0, d_rows, n_rows,
+                                                          p->n_features, p->tile, p->x_bytes, d_out);
+    return cudaGetLastError() == cudaSuccess ? HB_OK : HB_DEVICE_FAILED;
+  }
   int grid = (int)std::min<uint64_t>((n_rows + 127) / 128, (uint64_t)p->n_sm * 16);
   k_predict<<<grid, 128, 0, s>>>(p->nodes, p->roots, p->outs, p->weights, p->n_trees, p->n_outputs,
                                  p->base, d_rows, n_rows, p->n_features, d_out);

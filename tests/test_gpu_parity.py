@@ -199,6 +199,55 @@ def test_prediction_random_forest_matches_oracle():
     np.testing.assert_array_equal(_bits(got), _bits(want))
 
 
+def _chain_tree(depth, n_cols, rng):
+    """A tree of one long path (depth `depth`) with leaves hanging off it."""
+    n = 2 * depth + 1
+    a = np.zeros(n, H.NODE_DTYPE)
+    for i in range(depth):
+        a[2 * i]["left"], a[2 * i]["right"] = 2 * i + 1, 2 * i + 2
+        a[2 * i]["split_feature"] = rng.integers(0, n_cols)
+        a[2 * i]["split_cond"] = np.float32(rng.standard_normal())
+        a[2 * i]["default_left"] = rng.integers(0, 2)
+        a[2 * i + 1]["left"] = a[2 * i + 1]["right"] = -1
+        a[2 * i + 1]["leaf_value"] = np.float32(rng.normal(0, 0.1))
+    a[2 * depth]["left"] = a[2 * depth]["right"] = -1
+    a[2 * depth]["leaf_value"] = np.float32(0.5)
+    a["split_bin"] = -1
+    return a
+
+
+@pytest.mark.parametrize("depth", [3, 10, 14])
+def test_prediction_deep_and_shallow_trees(depth):
+    """Trees up to depth 10 take the complete-tree layout (shallow leaves
+    padded), deeper ones the general walk; both equal the oracle."""
+    rng = np.random.default_rng(depth)
+    trees = [_chain_tree(depth, 12, rng) for _ in range(5)]
+    f5, p5 = synth.forest_c5(n_trees=3, depth=4, n_cols=12, seed=depth)
+    nodes = np.concatenate(trees + [f5])
+    ptr = np.concatenate([[0], np.cumsum([len(t) for t in trees])]).astype(np.uint64)
+    ptr = np.concatenate([ptr, ptr[-1] + p5[1:]]).astype(np.uint64)
+    x = synth.rows_c5(5_001, 12, seed=depth, missing=0.2)
+    base = np.array([-0.5], np.float32)
+    w = rng.uniform(0.5, 1.5, len(ptr) - 1).astype(np.float32)
+    p = H.Predictor(nodes, ptr, base, 12, tree_weight=w)
+    got = p.predict_margin(x)
+    p.close()
+    want = O.predict(nodes.view(O.NODE_DTYPE), ptr, 1, base, x, tree_weight=w)
+    np.testing.assert_array_equal(_bits(got), _bits(want))
+
+
+def test_prediction_wide_rows():
+    """300 features: the complete-tree path with a smaller row tile."""
+    nodes, ptr = synth.forest_c5(n_trees=30, depth=8, n_cols=300, seed=8)
+    x = synth.rows_c5(3_001, 300, seed=9)
+    base = np.array([0.0], np.float32)
+    p = H.Predictor(nodes, ptr, base, 300)
+    got = p.predict_margin(x)
+    p.close()
+    want = O.predict(nodes.view(O.NODE_DTYPE), ptr, 1, base, x)
+    np.testing.assert_array_equal(_bits(got), _bits(want))
+
+
 # ------------------------------------------------------ RowEngine calls
 def _setup_engine(n=3001, f=7, seed=21, missing=0.1):
     rng = np.random.default_rng(seed)
