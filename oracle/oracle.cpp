@@ -11,6 +11,7 @@
 //     int64 multiple of a power of two and summed exactly; this is the
 //     arithmetic the CUDA path uses, so the two must agree bit for bit.
 #include <algorithm>
+#include <cfloat>
 #include <cmath>
 #include <cstring>
 #include <numeric>
@@ -665,6 +666,53 @@ void squared_error_gradient(const float* m, const float* y, size_t n, float spw,
   }
 }
 
+// multi:softmax gradients (objective/multiclass.rs:43 through
+// simd/mod.rs:502), the per-row scalar kernel `softmax_gradient_row_scalar`
+// (simd/mod.rs:580), which x86_64 runs for every class count but 2 and 4
+// (simd/mod.rs:156): the shift is max(f32::MIN_POSITIVE, margins...), the
+// exponentials are summed in f64 and the sum rounded to f32, then
+// p = expf(m - shift) / sum, g = (p - [class == label]) w,
+// h = max(((2 p)(1 - p)) w, MIN_HESS). Margins row-major, k per row; out in
+// the same layout.
+void softmax_gradient(const float* m, const float* y, size_t n, int k, GradPair* out) {
+#pragma omp parallel for schedule(static)
+  for (long long i = 0; i < (long long)n; ++i) {
+    const float* row = m + (size_t)i * k;
+    float wmax = FLT_MIN;
+    for (int j = 0; j < k; ++j) wmax = std::fmax(row[j], wmax);
+    double wsum = 0.0;
+    for (int j = 0; j < k; ++j) wsum += (double)expf(row[j] - wmax);
+    const float ws = (float)wsum;
+    const size_t label = (size_t)y[i];
+    const float w = 1.0f;
+    for (int j = 0; j < k; ++j) {
+      const float p = expf(row[j] - wmax) / ws;
+      const float h = std::fmax(((2.0f * p) * (1.0f - p)) * w, MIN_HESS);
+      const float g = ((size_t)j == label ? p - 1.0f : p) * w;
+      out[(size_t)i * k + j].grad = g;
+      out[(size_t)i * k + j].hess = h;
+    }
+  }
+}
+
+// multiclass.rs:68 `base_margins_info` (unweighted): class counts in f32,
+// divided by the f64 row count (n rounded to f32 first), ln(p + 1e-6) in
+// f32, centred by the f32 mean of m / k.
+void softmax_intercepts(const float* y, size_t n, int k, float* out) {
+  for (int j = 0; j < k; ++j) out[j] = 0.0f;
+  for (size_t i = 0; i < n; ++i) {
+    const float v = y[i];
+    if (v >= 0.0f && (size_t)v < (size_t)k) out[(size_t)v] += 1.0f;
+  }
+  const double sum_w = (double)(float)n;
+  const double inv = 1.0 / sum_w;
+  for (int j = 0; j < k; ++j) out[j] = logf((float)((double)out[j] * inv) + 1e-6f);
+  const float kk = (float)k;
+  float mean = 0.0f;
+  for (int j = 0; j < k; ++j) mean += out[j] / kk;
+  for (int j = 0; j < k; ++j) out[j] -= mean;
+}
+
 // objective/mod.rs:645 `weighted_label_mean` (unweighted)
 float label_mean(const float* y, size_t n, size_t stride, size_t col) {
   if (n == 0) return 0.0f;
@@ -740,8 +788,17 @@ void orc_gradients(int32_t objective, const float* margins, const float* labels,
     squared_error_gradient(margins, labels, n, spw, out);
 }
 
+void orc_softmax_gradients(const float* margins, const float* labels, uint64_t n, int32_t k,
+                           float* gpair) {
+  softmax_gradient(margins, labels, n, k, reinterpret_cast<GradPair*>(gpair));
+}
+
 void orc_intercepts(int32_t objective, const float* labels, uint64_t n, int32_t n_outputs,
                     float* out) {
+  if (objective == 2) {
+    softmax_intercepts(labels, n, n_outputs, out);
+    return;
+  }
   for (int t = 0; t < n_outputs; ++t) {
     float mean = label_mean(labels, n, (size_t)n_outputs, (size_t)t);
     out[t] = objective == 1 ? logistic_link(mean) : mean;
@@ -797,7 +854,8 @@ int64_t run_rounds(orc_trainer* tr, int rounds, orc_node* nodes, uint64_t nodes_
   tree_ptr[0] = 0;
   for (int round = 0; round < rounds; ++round) {
     // 1. Gradients of every output from this round's margins (round.rs:253).
-    for (int t = 0; t < k; ++t) {
+    if (p.objective == 2) softmax_gradient(tr->margins.data(), tr->labels.data(), n, k, gp_all.data());
+    for (int t = 0; t < k && p.objective != 2; ++t) {
       for (size_t r = 0; r < n; ++r) {
         mk[r] = tr->margins[r * k + t];
         yk[r] = tr->labels[r * k + t];
@@ -869,7 +927,7 @@ orc_trainer* orc_trainer_new(const orc_params* pp, const float* x, uint64_t n, u
   tr->k = tr->p.n_outputs;
   const int k = tr->k;
   tr->ix = make_index(x, n, nc, cuts_from_dense(x, n, nc, nullptr, (size_t)tr->p.max_bin, NAN));
-  tr->labels.assign(labels, labels + n * k);
+  tr->labels.assign(labels, labels + n * (tr->p.objective == 2 ? 1 : k));  // softmax: class ids
   tr->base.assign(k, 0.0f);
   if (std::isnan(pp->base_score)) {
     orc_intercepts(tr->p.objective, labels, n, k, tr->base.data());

@@ -26,8 +26,8 @@ typedef struct orc_node {
 } orc_node;
 
 typedef struct orc_params {
-  int32_t objective;       /* 0 reg:squarederror, 1 binary:logistic */
-  int32_t n_outputs;       /* label columns (squared error) */
+  int32_t objective;       /* 0 reg:squarederror, 1 binary:logistic, 2 multi:softmax */
+  int32_t n_outputs;       /* label columns (squared error), classes (softmax) */
   int32_t max_depth;
   int32_t max_leaves;      /* 0 = unlimited */
   int32_t grow_policy;     /* 0 depthwise, 1 lossguide */
@@ -60,7 +60,14 @@ int32_t orc_bin_dense(const float* x, uint64_t n_rows, uint64_t n_cols,
 void orc_gradients(int32_t objective, const float* margins, const float* labels, uint64_t n,
                    float scale_pos_weight, float* gpair);
 
-/* Base margin for each of `n_outputs` label columns (labels row-major). */
+/* multi:softmax gradient pairs of `k` classes at row-major margins
+ * (n x k), labels the class ids, pairs row-major like the margins. */
+void orc_softmax_gradients(const float* margins, const float* labels, uint64_t n, int32_t k,
+                           float* gpair);
+
+/* Base margin for each of `n_outputs` label columns (labels row-major); for
+ * multi:softmax (objective 2) the n_outputs class intercepts of the class
+ * ids in `labels`. */
 void orc_intercepts(int32_t objective, const float* labels, uint64_t n, int32_t n_outputs,
                     float* out);
 

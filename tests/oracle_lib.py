@@ -98,6 +98,10 @@ def lib():
         L.orc_intercepts.argtypes = [ctypes.c_int32, f32p, ctypes.c_uint64, ctypes.c_int32, f32p]
         L.orc_train.restype = ctypes.c_int64
         L.orc_train.argtypes = [P(OrcParams), f32p, ctypes.c_uint64, ctypes.c_uint64, f32p, ctypes.c_int32, P(OrcNode), ctypes.c_uint64, u64p, f32p, f32p]
+        L.orc_softmax_gradients.restype = None
+        L.orc_softmax_gradients.argtypes = [f32p, f32p, ctypes.c_uint64, ctypes.c_int32, f32p]
+        L.orc_intercepts.restype = None
+        L.orc_intercepts.argtypes = [ctypes.c_int32, f32p, ctypes.c_uint64, ctypes.c_int32, f32p]
         L.orc_predict.restype = None
         L.orc_predict.argtypes = [P(OrcNode), u64p, ctypes.c_uint64, ctypes.c_int32, u32p, f32p, f32p, f32p, ctypes.c_uint64, ctypes.c_uint64, f32p]
         L.orc_hist.restype = None
@@ -147,6 +151,24 @@ def gradients(objective, margins, labels, spw=1.0):
     return out.reshape(-1, 2)
 
 
+def softmax_gradients(margins, labels):
+    """multi:softmax pairs (n, k, 2) at margins (n, k), labels class ids (n,)."""
+    m = np.ascontiguousarray(margins, np.float32)
+    y = np.ascontiguousarray(labels, np.float32)
+    n, k = m.shape
+    out = np.zeros(2 * m.size, np.float32)
+    lib().orc_softmax_gradients(_p(m, ctypes.c_float), _p(y, ctypes.c_float), n, k, _p(out, ctypes.c_float))
+    return out.reshape(n, k, 2)
+
+
+def intercepts(objective, labels, n_outputs):
+    y = np.ascontiguousarray(labels, np.float32)
+    n = y.shape[0]
+    out = np.zeros(n_outputs, np.float32)
+    lib().orc_intercepts(objective, _p(y, ctypes.c_float), n, n_outputs, _p(out, ctypes.c_float))
+    return out
+
+
 def fixed_scale(max_abs, n):
     return int(lib().orc_fixed_scale(float(max_abs), int(n)))
 
@@ -176,8 +198,12 @@ def train(x, y, rounds, **kw):
     """Returns (nodes structured array, tree_ptr, base (n_out,), margins (n, n_out))."""
     x = np.ascontiguousarray(x, np.float32)
     n, f = x.shape
-    y = np.ascontiguousarray(y, np.float32).reshape(n, -1)
-    k = y.shape[1]
+    if kw.get("objective", 0) == 2:  # multi:softmax: class ids, n_outputs classes
+        y = np.ascontiguousarray(y, np.float32).reshape(n)
+        k = kw["n_outputs"]
+    else:
+        y = np.ascontiguousarray(y, np.float32).reshape(n, -1)
+        k = y.shape[1]
     kw.setdefault("n_outputs", k)
     p = params(**kw)
     n_trees_max = rounds * k
@@ -282,8 +308,11 @@ class Trainer:
     def __init__(self, x, y, **kw):
         self._x = np.ascontiguousarray(x, np.float32)
         n, f = self._x.shape
-        self._y = np.ascontiguousarray(y, np.float32).reshape(n, -1)
-        kw.setdefault("n_outputs", self._y.shape[1])
+        if kw.get("objective", 0) == 2:  # multi:softmax: class ids, n_outputs classes
+            self._y = np.ascontiguousarray(y, np.float32).reshape(n)
+        else:
+            self._y = np.ascontiguousarray(y, np.float32).reshape(n, -1)
+            kw.setdefault("n_outputs", self._y.shape[1])
         self.p = params(**kw)
         self.h = lib().orc_trainer_new(ctypes.byref(self.p), _p(self._x, ctypes.c_float), n, f, _p(self._y, ctypes.c_float))
         assert self.h

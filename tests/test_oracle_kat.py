@@ -105,3 +105,58 @@ def test_fixed_point_matches_f64_structure(missing):
     a = O.train(x, y, 3, max_depth=4, eta=0.5)
     b = O.train(x, y, 3, max_depth=4, eta=0.5, fixed_point=True)
     _assert_trees_equal(a[0], a[1], b[0], b[1])
+
+
+# ------------------------------------------------------------ multi:softmax
+def test_softmax_gradient_kat():
+    """objective/multiclass.rs:124 `gradient_layout_and_values`: all margins
+    0 over 3 classes -> p = 1/3, g = p - [class == label], h = 2 p (1 - p)."""
+    g = O.softmax_gradients(np.zeros((2, 3), np.float32), np.array([0.0, 2.0], np.float32))
+    np.testing.assert_allclose(g[0, 0, 0], 1 / 3 - 1, atol=1e-6)
+    np.testing.assert_allclose(g[0, 1, 0], 1 / 3, atol=1e-6)
+    np.testing.assert_allclose(g[1, 2, 0], 1 / 3 - 1, atol=1e-6)
+    np.testing.assert_allclose(g[:, :, 1], 2 * (1 / 3) * (2 / 3), atol=1e-6)
+
+
+def test_softmax_gradient_shift_and_rounding():
+    """The shift is max(f32::MIN_POSITIVE, margins) and the f64 sum is
+    rounded to f32 before the division (simd/mod.rs:580)."""
+    rng = np.random.default_rng(2)
+    m = (rng.standard_normal((50, 7)) * 3).astype(np.float32)
+    m[0] = -5.0  # every margin negative: the shift stays f32::MIN_POSITIVE
+    y = rng.integers(0, 7, 50).astype(np.float32)
+    got = O.softmax_gradients(m, y)
+    tiny = np.float32(np.finfo(np.float32).tiny)
+    for i in range(50):
+        wmax = max(np.float32(np.max(m[i])), tiny)
+        e = [np.float32(np.exp(np.float64(np.float32(v - wmax)))) for v in m[i]]
+        ws = np.float32(sum(np.float64(v) for v in e))
+        for j in range(7):
+            p = np.float32(e[j] / ws)
+            np.testing.assert_allclose(got[i, j, 0], p - (1.0 if j == y[i] else 0.0), rtol=2e-6, atol=1e-7)
+            np.testing.assert_allclose(got[i, j, 1], max(np.float32(2 * p * (1 - p)), np.float32(1e-16)), rtol=2e-6)
+
+
+def test_softmax_intercepts_kat():
+    """objective/multiclass.rs:146: centred log class frequencies."""
+    m = O.intercepts(2, np.array([0.0, 0.0, 1.0, 2.0], np.float32), 3)
+    assert abs(float(m.sum())) < 1e-6
+    gap = np.log(np.float32(0.5) + np.float32(1e-6)) - np.log(np.float32(0.25) + np.float32(1e-6))
+    assert abs(float(m[0] - m[1]) - gap) < 1e-6
+    assert m[1] == m[2]
+
+
+def test_softmax_training_fixed_matches_f64_structure():
+    rng = np.random.default_rng(5)
+    x = rng.uniform(-1, 1, (3000, 8)).astype(np.float32)
+    w = rng.standard_normal((8, 4))
+    y = np.argmax(x @ w + rng.gumbel(size=(3000, 4)), axis=1).astype(np.float32)
+    kw = dict(objective=2, n_outputs=4, max_depth=4, eta=0.2, max_bin=64)
+    a = O.train(x, y, 3, **kw)
+    b = O.train(x, y, 3, fixed_point=True, **kw)
+    assert len(a[1]) == len(b[1]) == 13  # 3 rounds x 4 classes
+    for key in ("left", "right", "split_feature", "split_bin", "default_left"):
+        np.testing.assert_array_equal(a[0][key], b[0][key])
+    np.testing.assert_allclose(a[0]["leaf_value"], b[0]["leaf_value"], rtol=1e-5, atol=1e-7)
+    np.testing.assert_array_equal(a[2], b[2])
+    np.testing.assert_array_equal(a[2], O.intercepts(2, y, 4))
