@@ -35,7 +35,7 @@ __all__ = [
 ]
 
 HB_OK, HB_REFUSED, HB_DEVICE_FAILED, HB_INVALID_ARGUMENT = 0, 1, 2, 3
-HB_LOSS_SQUARED_ERROR, HB_LOSS_LOGISTIC = 0, 1
+HB_LOSS_SQUARED_ERROR, HB_LOSS_LOGISTIC, HB_LOSS_SOFTMAX = 0, 1, 2
 HB_GROW_DEPTHWISE, HB_GROW_LOSSGUIDE = 0, 1
 
 
@@ -161,6 +161,7 @@ class TrainParamsC(ctypes.Structure):
         ("max_delta_step", ctypes.c_float),
         ("scale_pos_weight", ctypes.c_float),
         ("base_score", ctypes.c_float),
+        ("num_class", ctypes.c_int32),
     ]
 
 
@@ -224,6 +225,7 @@ SIGNATURES = {
     "hb_read_gradients": [_vp, _f32p, ctypes.c_uint64, _i32p, _i32p],
     "hb_grow_tree": [_vp, _P(TrainParamsC), _P(TreeNode), ctypes.c_uint32, _u32p],
     "hb_train": [_vp, _P(TrainParamsC), _f32p, ctypes.c_uint64, ctypes.c_float, ctypes.c_int32, _P(TreeNode), ctypes.c_uint64, _u64p],
+    "hb_train_begin_classes": [_vp, _f32p, ctypes.c_uint64, _f32p, ctypes.c_int32],
     "hb_train_begin": [_vp, _f32p, ctypes.c_uint64, ctypes.c_float],
     "hb_train_rounds": [_vp, _P(TrainParamsC), ctypes.c_int32, _P(TreeNode), ctypes.c_uint64, _u64p],
     "hb_engine_reset_stats": [_vp, ctypes.c_int32],
@@ -292,13 +294,19 @@ class TrainingParams:
     scale_pos_weight: float = 1.0
     base_score: float = float("nan")
     max_bin: int = 256
+    num_class: int = 0
 
     def loss_kind(self):
         if self.objective in ("reg:squarederror",):
             return HB_LOSS_SQUARED_ERROR
         if self.objective in ("binary:logistic", "reg:logistic", "binary:logitraw"):
             return HB_LOSS_LOGISTIC
+        if self.objective in ("multi:softmax", "multi:softprob"):
+            return HB_LOSS_SOFTMAX
         raise ValueError(f"objective {self.objective!r} is not on the device path")
+
+    def n_outputs(self):
+        return self.num_class if self.loss_kind() == HB_LOSS_SOFTMAX else 1
 
     def to_c(self):
         c = TrainParamsC()
@@ -314,6 +322,7 @@ class TrainingParams:
         c.max_delta_step = self.max_delta_step
         c.scale_pos_weight = self.scale_pos_weight
         c.base_score = self.base_score
+        c.num_class = self.num_class
         return c
 
     def reg(self):
@@ -576,13 +585,26 @@ class Engine:
 
     def train_begin(self, labels, base_margin):
         self._labels = np.ascontiguousarray(labels, np.float32)
+        self._classes = 1
         self._c(lib().hb_train_begin(self.h, _ptr(self._labels, ctypes.c_float), self._labels.size,
                                      float(base_margin)), "hb_train_begin")
 
+    def train_begin_classes(self, labels, base_margins):
+        """A multi:softmax run: labels are class ids, one base margin per class."""
+        self._labels = np.ascontiguousarray(labels, np.float32)
+        self._bases = np.ascontiguousarray(base_margins, np.float32)
+        self._classes = self._bases.size
+        self._c(lib().hb_train_begin_classes(self.h, _ptr(self._labels, ctypes.c_float), self._labels.size,
+                                             _ptr(self._bases, ctypes.c_float), self._classes),
+                "hb_train_begin_classes")
+
     def train_rounds(self, params, rounds):
-        cap = max(rounds, 1) * (2 << params.max_depth)
+        """`rounds` rounds; returns every tree's nodes and the tree offsets
+        (a softmax round's trees are its classes', in class order)."""
+        trees = rounds * getattr(self, "_classes", 1)
+        cap = max(trees, 1) * (2 << params.max_depth)
         nodes = np.zeros(cap, NODE_DTYPE)
-        tree_ptr = np.zeros(rounds + 1, np.uint64)
+        tree_ptr = np.zeros(trees + 1, np.uint64)
         p = params.to_c()
         self._c(lib().hb_train_rounds(self.h, ctypes.byref(p), rounds, nodes.ctypes.data_as(ctypes.POINTER(TreeNode)),
                                       cap, _ptr(tree_ptr, ctypes.c_uint64)), "hb_train_rounds")
@@ -612,6 +634,25 @@ class Engine:
 
 
 # ---------------------------------------------------------------- model
+def softmax_intercepts(labels, n_classes):
+    """multi:softmax class intercepts (objective/multiclass.rs:68 in its
+    precision): class counts accumulated in f32 (saturating at 2^24 as
+    sequential f32 adds of 1 do), divided by the f64 row count rounded to
+    f32 first, ln(p + 1e-6) with the C library's logf, centred by the f32
+    mean of m / k summed in class order."""
+    y = np.asarray(labels, np.float32)
+    ids = y[(y >= 0) & (y < n_classes)].astype(np.int64)
+    counts = np.minimum(np.bincount(ids, minlength=n_classes), 2**24).astype(np.float32)
+    inv = 1.0 / np.float64(np.float32(len(y)))
+    m = [np.float32(_libm().logf(float(np.float32(np.float32(np.float64(c) * inv) + np.float32(1e-6)))))
+         for c in counts]
+    kk = np.float32(n_classes)
+    mean = np.float32(0.0)
+    for v in m:
+        mean = np.float32(mean + np.float32(v / kk))
+    return np.array([np.float32(v - mean) for v in m], np.float32)
+
+
 def base_margin(params, labels):
     """The intercept (train.rs:408 `initial_intercepts`): the label mean for
     squared error, its logit for logistic (objective/mod.rs:645,
@@ -646,21 +687,25 @@ def _libm():
 
 @dataclass
 class Model:
-    """A trained single-output ensemble: nodes back to back, per-tree
-    offsets, the base margin."""
+    """A trained ensemble: nodes back to back, per-tree offsets, the base
+    margin (one per output; tree t adds to output t % outputs)."""
 
     nodes: np.ndarray
     tree_ptr: np.ndarray
-    base: float
+    base: object
     n_features: int
 
+    def bases(self):
+        return np.atleast_1d(np.asarray(self.base, np.float32))
+
     def predictor(self, device=0):
-        return Predictor(self.nodes, self.tree_ptr, [self.base], self.n_features, device=device)
+        return Predictor(self.nodes, self.tree_ptr, self.bases(), self.n_features, device=device)
 
     def predict_margin(self, x, device=0):
         p = self.predictor(device)
         try:
-            return p.predict_margin(x)[:, 0]
+            out = p.predict_margin(x)
+            return out[:, 0] if out.shape[1] == 1 else out
         finally:
             p.close()
 
@@ -670,10 +715,18 @@ def train(params, x=None, y=None, rounds=10, device=0, matrix=None, engine=None)
     if matrix is None:
         matrix = BinnedMatrix.from_dense(x, params.max_bin)
     y = np.ascontiguousarray(y, np.float32)
-    base = base_margin(params, y)
     eng = engine or Engine(device)
     try:
         eng.upload(matrix)
+        if params.loss_kind() == HB_LOSS_SOFTMAX:
+            if math.isnan(params.base_score):
+                base = softmax_intercepts(y, params.num_class)
+            else:
+                base = np.full(params.num_class, params.base_score, np.float32)
+            eng.train_begin_classes(y, base)
+            nodes, tree_ptr = eng.train_rounds(params, rounds)
+            return Model(nodes, tree_ptr, base, matrix.n_cols)
+        base = base_margin(params, y)
         nodes, tree_ptr = eng.train(params, y, rounds, base)
     finally:
         if engine is None:

@@ -130,7 +130,19 @@ struct hb_engine {
   uint64_t rounds_done = 0;
   DevBuf<unsigned long long> row_stats;  // [contiguous rows built, gathered rows built]
   bool train_begun = false;
+  // multi:softmax runs: classes, and the class whose tree is being grown
+  // (its slices of gpair, scale and wtree are the ones the level kernels use)
+  int n_out = 1;
+  int cls = 0;
+  size_t wstride = 0;      // WNodes per class in wtree
+  int alloc_classes = 0;
 };
+
+namespace {
+inline float2* cur_gpair(hb_engine* e) { return e->gpair.p + (size_t)e->cls * e->c.n_rows; }
+inline Scale* cur_scale(hb_engine* e) { return e->scale.p + e->cls; }
+inline WNode* cur_wtree(hb_engine* e) { return e->wtree.p + (size_t)e->cls * e->wstride; }
+}  // namespace
 
 namespace {
 
@@ -221,7 +233,7 @@ void collect_timers(hb_engine* e) {
 }
 
 hb_status ensure_growth_buffers(hb_engine* e, int max_depth) {
-  if (e->alloc_depth >= max_depth) return HB_OK;
+  if (e->alloc_depth >= max_depth && e->alloc_classes >= e->n_out) return HB_OK;
   const DevConst& c = e->c;
   const int max_front = 1 << max_depth;
   const size_t slots = (size_t(1) << max_depth) - 1;
@@ -239,18 +251,20 @@ hb_status ensure_growth_buffers(hb_engine* e, int max_depth) {
   HB_CK(e, e->pairs.alloc(max_front));
   HB_CK(e, e->ls.alloc(kMaxDepth + 2));
   HB_CK(e, e->tree.alloc((size_t)2 * max_front));
-  HB_CK(e, e->wtree.alloc((size_t)2 * max_front));
+  e->wstride = (size_t)2 * max_front;
+  HB_CK(e, e->wtree.alloc(e->wstride * std::max(e->n_out, 1)));
   e->alloc_depth = max_depth;
+  e->alloc_classes = e->n_out;
   return HB_OK;
 }
 
 // Stage this tree's scale: reduce the maxima over ranks, then the exponents.
 hb_status finish_scale(hb_engine* e) {
   if (e->comm) {
-    HB_NCCL(e, ncclAllReduce(&e->scale.p->maxg_bits, &e->scale.p->maxg_bits, 3, ncclUint32,
+    HB_NCCL(e, ncclAllReduce(&cur_scale(e)->maxg_bits, &cur_scale(e)->maxg_bits, 3, ncclUint32,
                              ncclMax, e->comm, e->stream));
   }
-  launch_scale(e->scale.p, e->c.global_rows, e->flags.p, e->stream);
+  launch_scale(cur_scale(e), e->c.global_rows, e->flags.p, e->stream);
   HB_CK(e, cudaGetLastError());
   return HB_OK;
 }
@@ -267,8 +281,12 @@ uint64_t vector_rows(hb_engine* e) {
 hb_status flush_pending(hb_engine* e) {
   if (!e->pending_tree) return HB_OK;
   mark_begin(e, T_OTHER);
-  launch_walk(e->wtree.p, e->ls.p + e->pending_depth + 1, 2 << e->pending_depth, e->rec.p,
-              e->c.stride, e->c.mask_off, e->c.n_rows, e->margin.p, e->flags.p, e->n_sm, e->stream);
+  if (e->n_out > 1)
+    launch_walk_classes(e->n_out, e->wtree.p, (uint32_t)e->wstride, e->rec.p, e->c.stride,
+                        e->c.mask_off, e->c.n_rows, e->margin.p, e->flags.p, e->n_sm, e->stream);
+  else
+    launch_walk(e->wtree.p, e->ls.p + e->pending_depth + 1, 2 << e->pending_depth, e->rec.p,
+                e->c.stride, e->c.mask_off, e->c.n_rows, e->margin.p, e->flags.p, e->n_sm, e->stream);
   mark_end(e);
   HB_CK(e, cudaMemsetAsync(e->flags.p, 0, sizeof(int), e->stream));
   e->kernel_launches += 1;
@@ -322,7 +340,7 @@ hb_status grow_device(hb_engine* e, const hb_train_params* p, bool to_forest) {
   const size_t smem = hist_smem_bytes(c);
   const int hgrid = hist_grid(e->n_sm);
   mark_begin(e, T_ROOT);
-  launch_hist(c, e->fo.p, e->rec.p, e->gpair.p, e->scale.p, nullptr, e->entries.p, e->ls.p, hist,
+  launch_hist(c, e->fo.p, e->rec.p, cur_gpair(e), cur_scale(e), nullptr, e->entries.p, e->ls.p, hist,
               totals, e->row_stats.p, hgrid, smem, s);
   mark_end(e);
   HB_CK(e, cudaGetLastError());
@@ -348,14 +366,14 @@ hb_status grow_device(hb_engine* e, const hb_train_params* p, bool to_forest) {
       // level d's sibling slots start at base + half; their histograms are
       // parent - built, made by the scan itself
       const int sib_base = d == 0 ? INT_MAX : (1 << d) - 1 + (1 << (d - 1));
-      launch_scan(c, e->fo.p, hist, fr, lsd, d == 0 ? nullptr : e->pairs.p, sib_base, e->scale.p,
+      launch_scan(c, e->fo.p, hist, fr, lsd, d == 0 ? nullptr : e->pairs.p, sib_base, cur_scale(e),
                   max_front, e->cand.p, s);
       mark_end(e);
       ++launches;
     }
     mark_begin(e, T_APPLY);
     launch_apply(c, e->fo.p, e->cuts.p, e->cand.p, fr, nx, e->dec.p, e->items.p, lsd, lsn,
-                 e->tree.p, e->wtree.p, e->scale.p, d, leaf_only ? 1 : 0, s);
+                 e->tree.p, cur_wtree(e), cur_scale(e), d, leaf_only ? 1 : 0, s);
     mark_end(e);
     ++launches;
     HB_CK(e, cudaGetLastError());
@@ -378,7 +396,7 @@ hb_status grow_device(hb_engine* e, const hb_train_params* p, bool to_forest) {
                         nx, rows_in, d == 0, rows_out, s);
     mark_end(e);
     mark_begin(e, T_HIST);
-    launch_hist(c, e->fo.p, e->rec.p, e->gpair.p, e->scale.p, rows_out, e->entries.p, lsn, hist,
+    launch_hist(c, e->fo.p, e->rec.p, cur_gpair(e), cur_scale(e), rows_out, e->entries.p, lsn, hist,
                 nullptr, e->row_stats.p, hgrid, smem, s);
     mark_end(e);
     if (e->comm) {
@@ -413,8 +431,18 @@ hb_status check_params(hb_engine* e, const hb_train_params* p) {
     return refuse(e, "device growth supports grow_policy = depthwise");
   if (p->max_depth < 1 || p->max_depth > kMaxDepth)
     return refuse(e, "device growth supports 1 <= max_depth <= 10");
-  if (p->objective != HB_LOSS_SQUARED_ERROR && p->objective != HB_LOSS_LOGISTIC)
+  if (p->objective != HB_LOSS_SQUARED_ERROR && p->objective != HB_LOSS_LOGISTIC &&
+      p->objective != HB_LOSS_SOFTMAX)
     return HB_INVALID_ARGUMENT;
+  if (p->objective == HB_LOSS_SOFTMAX) {
+    // x86_64 runs a separate vector kernel for 2 and 4 classes
+    // (simd/mod.rs:156); this engine restates the scalar one only
+    if (p->num_class < 3 || p->num_class == 4 || p->num_class > 64)
+      return refuse(e, "multi:softmax supports num_class 3 or 5..64");
+    if (e->n_out != p->num_class) return refuse(e, "start the run with hb_train_begin_classes");
+  } else if (e->n_out != 1) {
+    return refuse(e, "a multi:softmax run is loaded (hb_train_begin resets it)");
+  }
   return HB_OK;
 }
 
@@ -873,7 +901,7 @@ hb_status hb_load_margins(hb_engine* e, const float* margins, uint64_t n) {
 hb_status hb_read_margins(hb_engine* e, float* out, uint64_t n) {
   HB_ENTER(e);
   if (!e->margins_loaded) return refuse(e, "no margin run");
-  if (!out || n != e->c.n_rows) return HB_INVALID_ARGUMENT;
+  if (!out || (n != e->c.n_rows && n != e->c.n_rows * (uint64_t)e->n_out)) return HB_INVALID_ARGUMENT;
   HB_CK(e, cudaMemcpyAsync(out, e->margin.p, 4 * n, cudaMemcpyDeviceToHost, e->stream));
   HB_CK(e, cudaStreamSynchronize(e->stream));
   return HB_OK;
@@ -1113,6 +1141,33 @@ hb_status hb_grow_tree(hb_engine* e, const hb_train_params* p, hb_tree_node* nod
 // One boosting round (gradients, with the previous tree's leaves, and a
 // tree) as stream work.
 static hb_status round_work(hb_engine* e, const hb_train_params* p) {
+  if (p->objective == HB_LOSS_SOFTMAX) {
+    // every class's gradients from the round's margins (round.rs:253), then
+    // one tree per class in class order (round.rs:318)
+    cudaStream_t s = e->stream;
+    HB_CK(e, cudaMemsetAsync(e->scale.p, 0, sizeof(Scale) * e->n_out, s));
+    mark_begin(e, T_GRAD);
+    launch_softmax_gradients(e->n_out, e->margin.p, e->label.p, e->c.n_rows, 1e-16f, e->gpair.p,
+                             e->scale.p, e->wtree.p, (uint32_t)e->wstride, e->rec.p, e->c.stride,
+                             e->c.mask_off, e->flags.p, e->n_sm, s);
+    mark_end(e);
+    HB_CK(e, cudaGetLastError());
+    e->pending_tree = false;
+    e->kernel_launches += 1;
+    for (int k = 0; k < e->n_out; ++k) {
+      e->cls = k;
+      hb_status st = finish_scale(e);
+      if (st == HB_OK) st = grow_device(e, p, true);
+      if (st != HB_OK) {
+        e->cls = 0;
+        return st;
+      }
+      e->kernel_launches += 1;  // scale
+    }
+    e->cls = 0;
+    e->staged = true;
+    return HB_OK;
+  }
   hb_status st = run_gradients(e, p->objective, p->scale_pos_weight, 1e-16f, p->max_depth);
   if (st != HB_OK) return st;
   return grow_device(e, p, true);
@@ -1142,7 +1197,7 @@ static hb_status graph_rounds(hb_engine* e, const hb_train_params* p, int rounds
   };
   if (e->timing) {
     // enough events for every mark of every round, created before capture
-    const size_t need = e->ev_used + (size_t)rounds * 64 + 64;
+    const size_t need = e->ev_used + (size_t)rounds * 64 * std::max(e->n_out, 1) + 64;
     while (e->ev.size() < need) {
       cudaEvent_t x;
       HB_CK(e, cudaEventCreate(&x));
@@ -1177,6 +1232,7 @@ static hb_status graph_rounds(hb_engine* e, const hb_train_params* p, int rounds
   std::memcpy(key.data() + sizeof(hb_train_params) + sizeof(ptrs), &weighted, sizeof(int));
   std::memcpy(key.data() + sizeof(hb_train_params) + sizeof(ptrs) + sizeof(int), &e->max_items,
               sizeof(int));
+  key.push_back((unsigned char)e->n_out);
   if (!e->round_exec || key != e->round_key) {
     if (e->round_exec) cudaGraphExecDestroy(e->round_exec);
     e->round_exec = nullptr;
@@ -1206,6 +1262,7 @@ hb_status hb_train_begin(hb_engine* e, const float* labels, uint64_t n, float ba
   if (!labels || n != e->c.n_rows) return HB_INVALID_ARGUMENT;
   if (e->row_begin % 8) return refuse(e, "shards must start on a multiple of 8 rows");
   cudaStream_t s = e->stream;
+  e->n_out = 1;
   {
     std::vector<float> m(n, base_margin);
     HB_CK(e, cudaMemcpyAsync(e->margin.p, m.data(), 4 * n, cudaMemcpyHostToDevice, s));
@@ -1222,6 +1279,42 @@ hb_status hb_train_begin(hb_engine* e, const float* labels, uint64_t n, float ba
   return HB_OK;
 }
 
+hb_status hb_train_begin_classes(hb_engine* e, const float* labels, uint64_t n,
+                                 const float* base_margins, int32_t n_classes) {
+  HB_ENTER(e);
+  if (!e->uploaded) return refuse(e, "no index uploaded");
+  if (!labels || !base_margins || n != e->c.n_rows || n_classes < 1 || n_classes > 64)
+    return HB_INVALID_ARGUMENT;
+  if (e->row_begin % 8) return refuse(e, "shards must start on a multiple of 8 rows");
+  for (uint64_t i = 0; i < n; ++i) {
+    const float y = labels[i];
+    if (!(y >= 0.0f) || y >= (float)n_classes || y != std::floor(y))
+      return refuse(e, "labels must be class ids in [0, n_classes)");
+  }
+  cudaStream_t s = e->stream;
+  const size_t kn = (size_t)n_classes * n;
+  HB_CK(e, e->margin.alloc(kn));
+  HB_CK(e, e->gpair.alloc(kn));
+  HB_CK(e, e->scale.alloc(n_classes));
+  {
+    std::vector<float> m(kn);
+    for (int k = 0; k < n_classes; ++k)
+      std::fill(m.begin() + (size_t)k * n, m.begin() + (size_t)(k + 1) * n, base_margins[k]);
+    HB_CK(e, cudaMemcpyAsync(e->margin.p, m.data(), 4 * kn, cudaMemcpyHostToDevice, s));
+    HB_CK(e, cudaMemcpyAsync(e->label.p, labels, 4 * n, cudaMemcpyHostToDevice, s));
+    HB_CK(e, cudaStreamSynchronize(s));
+  }
+  e->label_key = nullptr;
+  e->weight_key = nullptr;
+  e->n_out = n_classes;
+  e->margins_loaded = true;
+  e->pending_tree = false;
+  HB_CK(e, cudaMemsetAsync(e->flags.p, 0, sizeof(int), s));
+  HB_CK(e, cudaStreamSynchronize(s));
+  e->train_begun = true;
+  return HB_OK;
+}
+
 hb_status hb_train_rounds(hb_engine* e, const hb_train_params* p, int32_t rounds,
                           hb_tree_node* nodes, uint64_t nodes_cap, uint64_t* tree_ptr) {
   HB_ENTER(e);
@@ -1231,8 +1324,9 @@ hb_status hb_train_rounds(hb_engine* e, const hb_train_params* p, int32_t rounds
   if (rounds < 0 || !tree_ptr || (!nodes && rounds)) return HB_INVALID_ARGUMENT;
   cudaStream_t s = e->stream;
   const uint32_t max_nodes = 2u << p->max_depth;
-  HB_CK(e, e->forest.alloc(std::max<size_t>((size_t)rounds * max_nodes, 1)));
-  HB_CK(e, e->counts.alloc(std::max(rounds, 1)));
+  const int trees = rounds * e->n_out;  // one tree per class and round
+  HB_CK(e, e->forest.alloc(std::max<size_t>((size_t)trees * max_nodes, 1)));
+  HB_CK(e, e->counts.alloc(std::max(trees, 1)));
   HB_CK(e, cudaMemsetAsync(e->tree_counter.p, 0, 4, s));
   if (e->use_graphs && rounds > 0) {
     st = ensure_growth_buffers(e, p->max_depth);
@@ -1241,10 +1335,10 @@ hb_status hb_train_rounds(hb_engine* e, const hb_train_params* p, int32_t rounds
     if (st != HB_OK) return st;
   } else {
     HB_CK(e, cudaEventRecord(e->run_ev[0], s));
+    st = ensure_growth_buffers(e, p->max_depth);
+    if (st != HB_OK) return st;
     for (int r = 0; r < rounds; ++r) {
-      st = run_gradients(e, p->objective, p->scale_pos_weight, 1e-16f, p->max_depth);
-      if (st != HB_OK) return st;
-      st = grow_device(e, p, true);
+      st = round_work(e, p);
       if (st != HB_OK) return st;
       if (e->timing && e->ev_used + 128 > e->ev.size()) collect_timers(e);
     }
@@ -1252,8 +1346,8 @@ hb_status hb_train_rounds(hb_engine* e, const hb_train_params* p, int32_t rounds
   }
   st = flush_pending(e);
   if (st != HB_OK) return st;
-  std::vector<uint32_t> cnt(std::max(rounds, 1));
-  HB_CK(e, cudaMemcpyAsync(cnt.data(), e->counts.p, 4 * (size_t)std::max(rounds, 1), cudaMemcpyDeviceToHost, s));
+  std::vector<uint32_t> cnt(std::max(trees, 1));
+  HB_CK(e, cudaMemcpyAsync(cnt.data(), e->counts.p, 4 * (size_t)std::max(trees, 1), cudaMemcpyDeviceToHost, s));
   HB_CK(e, cudaStreamSynchronize(s));
   collect_timers(e);
   {
@@ -1262,12 +1356,12 @@ hb_status hb_train_rounds(hb_engine* e, const hb_train_params* p, int32_t rounds
   }
   uint64_t used = 0;
   tree_ptr[0] = 0;
-  for (int r = 0; r < rounds; ++r) {
+  for (int r = 0; r < trees; ++r) {
     used += cnt[r];
     tree_ptr[r + 1] = used;
   }
   if (used > nodes_cap) return refuse(e, "nodes_cap too small");
-  for (int r = 0; r < rounds; ++r) {
+  for (int r = 0; r < trees; ++r) {
     HB_CK(e, cudaMemcpyAsync(nodes + tree_ptr[r], e->forest.p + (size_t)r * max_nodes,
                              sizeof(hb_tree_node) * cnt[r], cudaMemcpyDeviceToHost, s));
   }

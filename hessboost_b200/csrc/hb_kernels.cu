@@ -205,6 +205,78 @@ __global__ void k_gradients(int kind, float* __restrict__ margin,
   reduce_scale(mg, mh, nonfinite, scale);
 }
 
+// multi:softmax gradients (objective/multiclass.rs:43), the reference's
+// per-row scalar kernel (simd/mod.rs:580), which x86_64 runs for every class
+// count but 2 and 4: shift = max(f32::MIN_POSITIVE, margins...), the
+// exponentials summed in f64 and the sum rounded to f32, p = exp(m - shift)
+// / sum, g = p - [class == label], h = max((2 p)(1 - p), min_hess). exp is
+// CUDA's double exp rounded once to f32 (as in sigmoid_scalar). Margins and
+// pairs are class-major ([class][row]); with *pending set each row first
+// adds its leaf of each class's tree (wtree + class * wstride, read from
+// global memory) to that class's margin. Per-class |g|, |h| maxima and a
+// non-finite flag go to scale[class].
+constexpr int kMaxClasses = 64;
+
+__device__ __forceinline__ float exp_rounded(float t) { return __double2float_rn(exp((double)t)); }
+
+__global__ void k_softmax_gradients(int K, float* __restrict__ margin, const float* __restrict__ label,
+                                    uint64_t n, float min_hess, float2* __restrict__ gpair,
+                                    Scale* scale, const WNode* __restrict__ wtree, uint32_t wstride,
+                                    const uint8_t* __restrict__ rec, uint32_t stride,
+                                    uint32_t mask_off, const int* __restrict__ pending) {
+  __shared__ unsigned s_mg[kMaxClasses], s_mh[kMaxClasses], s_nf[kMaxClasses];
+  for (int j = threadIdx.x; j < K; j += blockDim.x) s_mg[j] = s_mh[j] = s_nf[j] = 0u;
+  __syncthreads();
+  const bool walk = pending != nullptr && *pending != 0;
+  const uint64_t step = (uint64_t)gridDim.x * blockDim.x;
+  for (uint64_t i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += step) {
+    const uint8_t* rp = rec + i * stride;
+    float wmax = FLT_MIN;
+    for (int j = 0; j < K; ++j) {
+      float v = margin[(uint64_t)j * n + i];
+      if (walk) {
+        v = __fadd_rn(v, walk_leaf(wtree + (uint64_t)j * wstride, rp, stride, mask_off));
+        margin[(uint64_t)j * n + i] = v;
+      }
+      wmax = fmaxf(v, wmax);
+    }
+    double wsum = 0.0;
+    for (int j = 0; j < K; ++j) wsum += (double)exp_rounded(__fsub_rn(margin[(uint64_t)j * n + i], wmax));
+    const float ws = __double2float_rn(wsum);
+    const float y = label[i];
+    for (int j = 0; j < K; ++j) {
+      const float p = __fdiv_rn(exp_rounded(__fsub_rn(margin[(uint64_t)j * n + i], wmax)), ws);
+      const float h = fmaxf(__fmul_rn(__fmul_rn(2.0f, p), __fsub_rn(1.0f, p)), min_hess);
+      const float g = (float)j == y ? __fsub_rn(p, 1.0f) : p;
+      gpair[(uint64_t)j * n + i] = make_float2(g, h);
+      if (!isfinite(g) || !isfinite(h)) atomicOr(&s_nf[j], 1u);
+      atomicMax(&s_mg[j], __float_as_uint(fabsf(g)));
+      atomicMax(&s_mh[j], __float_as_uint(fabsf(h)));
+    }
+  }
+  __syncthreads();
+  for (int j = threadIdx.x; j < K; j += blockDim.x) {
+    if (s_mg[j]) atomicMax(&scale[j].maxg_bits, s_mg[j]);
+    if (s_mh[j]) atomicMax(&scale[j].maxh_bits, s_mh[j]);
+    if (s_nf[j]) atomicOr(&scale[j].nonfinite, 1u);
+  }
+}
+
+// Add each class's tree leaves to the class-major margins (the last round's
+// trees, when *pending is set).
+__global__ void k_walk_classes(int K, const WNode* __restrict__ wtree, uint32_t wstride,
+                               const uint8_t* __restrict__ rec, uint32_t stride, uint32_t mask_off,
+                               uint64_t n, float* __restrict__ margin, const int* __restrict__ pending) {
+  if (!*pending) return;
+  for (uint64_t i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n;
+       i += (uint64_t)gridDim.x * blockDim.x) {
+    const uint8_t* rp = rec + i * stride;
+    for (int j = 0; j < K; ++j)
+      margin[(uint64_t)j * n + i] = __fadd_rn(margin[(uint64_t)j * n + i],
+                                             walk_leaf(wtree + (uint64_t)j * wstride, rp, stride, mask_off));
+  }
+}
+
 __global__ void k_pair_maxima(const float2* __restrict__ gpair, uint64_t n, Scale* scale) {
   float mg = 0.0f, mh = 0.0f;
   bool nonfinite = false;
@@ -1407,6 +1479,22 @@ void launch_walk(const WNode* wtree, const LevelState* ls_last, int max_nodes, c
 void hist_configure() {
   cudaFuncSetAttribute(k_hist, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024 - 1024);
   cudaFuncSetAttribute(k_hist32, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024 - 1024);
+}
+
+void launch_softmax_gradients(int K, float* margin, const float* label, uint64_t n, float min_hess,
+                              float2* gpair, Scale* scale, const WNode* wtree, uint32_t wstride,
+                              const uint8_t* rec, uint32_t stride, uint32_t mask_off,
+                              const int* pending, int n_sm, cudaStream_t s) {
+  const int grid = (int)std::max<uint64_t>(1, std::min<uint64_t>((n + 255) / 256, (uint64_t)n_sm * 8));
+  k_softmax_gradients<<<grid, 256, 0, s>>>(K, margin, label, n, min_hess, gpair, scale, wtree,
+                                           wstride, rec, stride, mask_off, pending);
+}
+
+void launch_walk_classes(int K, const WNode* wtree, uint32_t wstride, const uint8_t* rec,
+                         uint32_t stride, uint32_t mask_off, uint64_t n, float* margin,
+                         const int* pending, int n_sm, cudaStream_t s) {
+  const int grid = (int)std::max<uint64_t>(1, std::min<uint64_t>((n + 255) / 256, (uint64_t)n_sm * 8));
+  k_walk_classes<<<grid, 256, 0, s>>>(K, wtree, wstride, rec, stride, mask_off, n, margin, pending);
 }
 
 void launch_pair_maxima(const float2* gpair, uint64_t n, Scale* scale, int n_sm, cudaStream_t s) {

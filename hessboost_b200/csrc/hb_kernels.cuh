@@ -20,6 +20,17 @@ void launch_gradients(int kind, float* margin, const float* label, const float* 
 void launch_walk(const WNode* wtree, const LevelState* ls_last, int max_nodes, const uint8_t* rec,
                  uint32_t stride, uint32_t mask_off, uint64_t n, float* margin, const int* pending,
                  int n_sm, cudaStream_t s);
+// multi:softmax gradients of K classes (class-major margins and pairs,
+// K <= 64), first adding each class's pending tree when *pending is set;
+// per-class maxima into scale[0..K).
+void launch_softmax_gradients(int K, float* margin, const float* label, uint64_t n, float min_hess,
+                              float2* gpair, Scale* scale, const WNode* wtree, uint32_t wstride,
+                              const uint8_t* rec, uint32_t stride, uint32_t mask_off,
+                              const int* pending, int n_sm, cudaStream_t s);
+// When *pending is set, add each class's tree leaves to its margins.
+void launch_walk_classes(int K, const WNode* wtree, uint32_t wstride, const uint8_t* rec,
+                         uint32_t stride, uint32_t mask_off, uint64_t n, float* margin,
+                         const int* pending, int n_sm, cudaStream_t s);
 // |g|, |h| maxima of staged pairs (HistogramBackend::prepare).
 void launch_pair_maxima(const float2* gpair, uint64_t n, Scale* scale, int n_sm, cudaStream_t s);
 // Fixed-point exponents from the (reduced) maxima and the global row count.

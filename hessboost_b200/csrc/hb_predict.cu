@@ -27,29 +27,32 @@ struct PNode {
 };
 
 __global__ void k_predict(const PNode* __restrict__ nodes, const uint32_t* __restrict__ roots,
-                          const uint32_t* __restrict__ outs, const float* __restrict__ weights,
-                          uint32_t n_trees, int n_outputs, const float* __restrict__ base,
-                          const float* __restrict__ x, uint64_t n_rows, uint32_t n_cols,
-                          float* __restrict__ out) {
+                          const uint32_t* __restrict__ order, const uint32_t* __restrict__ ostart,
+                          const float* __restrict__ weights, int n_outputs,
+                          const float* __restrict__ base, const float* __restrict__ x,
+                          uint64_t n_rows, uint32_t n_cols, float* __restrict__ out) {
+  // one output at a time over its trees in tree order (order[ostart[o] ..
+  // ostart[o + 1]) lists them), so each output's sum is the reference's
   for (uint64_t r = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; r < n_rows;
        r += (uint64_t)gridDim.x * blockDim.x) {
     const float* row = x + r * n_cols;
-    float acc[8];
-    for (int o = 0; o < n_outputs && o < 8; ++o) acc[o] = base[o];
-    for (uint32_t t = 0; t < n_trees; ++t) {
-      uint32_t id = roots[t];
-      PNode nd = nodes[id];
-      while (nd.left >= 0) {
-        const int f = nd.feature & 0x7fffffff;
-        const float v = __ldg(row + f);
-        const bool left = isnan(v) ? (nd.feature < 0) : (v < nd.cond);
-        id = (uint32_t)nd.left + (left ? 0u : 1u);
-        nd = nodes[id];
+    for (int o = 0; o < n_outputs; ++o) {
+      float acc = base[o];
+      for (uint32_t q = ostart[o]; q < ostart[o + 1]; ++q) {
+        const uint32_t t = order[q];
+        uint32_t id = roots[t];
+        PNode nd = nodes[id];
+        while (nd.left >= 0) {
+          const int f = nd.feature & 0x7fffffff;
+          const float v = __ldg(row + f);
+          const bool left = isnan(v) ? (nd.feature < 0) : (v < nd.cond);
+          id = (uint32_t)nd.left + (left ? 0u : 1u);
+          nd = nodes[id];
+        }
+        acc = __fadd_rn(acc, __fmul_rn(weights[t], nd.cond));
       }
-      const uint32_t o = outs[t];
-      acc[o] = __fadd_rn(acc[o], __fmul_rn(weights[t], nd.cond));
+      out[r * n_outputs + o] = acc;
     }
-    for (int o = 0; o < n_outputs && o < 8; ++o) out[r * n_outputs + o] = acc[o];
   }
 }
 
@@ -187,7 +190,8 @@ struct hb_predictor {
   cudaStream_t stream = nullptr;
   PNode* nodes = nullptr;
   uint32_t* roots = nullptr;
-  uint32_t* outs = nullptr;
+  uint32_t* outs = nullptr;    // trees grouped by output, in tree order within an output
+  uint32_t* ostart = nullptr;  // [n_outputs + 1] offsets into outs
   float* weights = nullptr;
   float* base = nullptr;
   uint32_t n_trees = 0;
@@ -292,7 +296,7 @@ hb_status hb_predictor_create(int32_t device_ordinal, const hb_tree_node* nodes,
                               const uint32_t* tree_output, const float* tree_weight,
                               int32_t n_outputs, const float* base, uint32_t n_features,
                               hb_predictor** out) {
-  if (!out || !tree_ptr || !base || n_outputs < 1 || n_outputs > 8 || (!nodes && n_trees))
+  if (!out || !tree_ptr || !base || n_outputs < 1 || n_outputs > 4096 || (!nodes && n_trees))
     return HB_INVALID_ARGUMENT;
   *out = nullptr;
   int ndev = 0;
@@ -339,6 +343,14 @@ hb_status hb_predictor_create(int32_t device_ordinal, const hb_tree_node* nodes,
       if (order.size() > n + 1) return HB_INVALID_ARGUMENT;
     }
   }
+  // trees grouped by output, stable: output o's trees in tree order
+  std::vector<uint32_t> ostart(n_outputs + 1, 0), grouped(n_trees);
+  for (uint64_t t = 0; t < n_trees; ++t) ++ostart[outs[t] + 1];
+  for (int o = 0; o < n_outputs; ++o) ostart[o + 1] += ostart[o];
+  {
+    std::vector<uint32_t> at(ostart.begin(), ostart.end() - 1);
+    for (uint64_t t = 0; t < n_trees; ++t) grouped[at[outs[t]]++] = (uint32_t)t;
+  }
   hb_predictor* p = new hb_predictor();
   p->device = device_ordinal;
   p->n_trees = (uint32_t)n_trees;
@@ -349,15 +361,17 @@ hb_status hb_predictor_create(int32_t device_ordinal, const hb_tree_node* nodes,
             cudaMalloc(&p->nodes, sizeof(PNode) * std::max<size_t>(arena.size(), 1)) == cudaSuccess &&
             cudaMalloc(&p->roots, 4 * std::max<uint64_t>(n_trees, 1)) == cudaSuccess &&
             cudaMalloc(&p->outs, 4 * std::max<uint64_t>(n_trees, 1)) == cudaSuccess &&
+            cudaMalloc(&p->ostart, 4 * (size_t)(n_outputs + 1)) == cudaSuccess &&
             cudaMalloc(&p->weights, 4 * std::max<uint64_t>(n_trees, 1)) == cudaSuccess &&
             cudaMalloc(&p->base, 4 * n_outputs) == cudaSuccess;
   if (ok && !arena.empty())
     ok = cudaMemcpy(p->nodes, arena.data(), sizeof(PNode) * arena.size(), cudaMemcpyHostToDevice) == cudaSuccess;
   if (ok && n_trees)
     ok = cudaMemcpy(p->roots, roots.data(), 4 * n_trees, cudaMemcpyHostToDevice) == cudaSuccess &&
-         cudaMemcpy(p->outs, outs.data(), 4 * n_trees, cudaMemcpyHostToDevice) == cudaSuccess &&
+         cudaMemcpy(p->outs, grouped.data(), 4 * n_trees, cudaMemcpyHostToDevice) == cudaSuccess &&
          cudaMemcpy(p->weights, ws.data(), 4 * n_trees, cudaMemcpyHostToDevice) == cudaSuccess;
-  if (ok) ok = cudaMemcpy(p->base, base, 4 * n_outputs, cudaMemcpyHostToDevice) == cudaSuccess;
+  if (ok) ok = cudaMemcpy(p->base, base, 4 * n_outputs, cudaMemcpyHostToDevice) == cudaSuccess &&
+               cudaMemcpy(p->ostart, ostart.data(), 4 * (size_t)(n_outputs + 1), cudaMemcpyHostToDevice) == cudaSuccess;
   if (ok) {
     std::vector<unsigned char> carena;
     std::vector<ChunkHdr> chunks;
@@ -395,6 +409,7 @@ hb_status hb_predictor_destroy(hb_predictor* p) {
   cudaFree(p->nodes);
   cudaFree(p->roots);
   cudaFree(p->outs);
+  cudaFree(p->ostart);
   cudaFree(p->weights);
   cudaFree(p->base);
   cudaFree(p->stage_x);
@@ -422,7 +437,7 @@ hb_status hb_predict_margin_device(hb_predictor* p, const float* d_rows, uint64_
     return cudaGetLastError() == cudaSuccess ? HB_OK : HB_DEVICE_FAILED;
   }
   int grid = (int)std::min<uint64_t>((n_rows + 127) / 128, (uint64_t)p->n_sm * 16);
-  k_predict<<<grid, 128, 0, s>>>(p->nodes, p->roots, p->outs, p->weights, p->n_trees, p->n_outputs,
+  k_predict<<<grid, 128, 0, s>>>(p->nodes, p->roots, p->outs, p->ostart, p->weights, p->n_outputs,
                                  p->base, d_rows, n_rows, p->n_features, d_out);
   return cudaGetLastError() == cudaSuccess ? HB_OK : HB_DEVICE_FAILED;
 }

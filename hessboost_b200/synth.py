@@ -36,6 +36,20 @@ def logistic_c2(n_rows=10_000_000, n_cols=28, seed=0, missing=0.05):
     return x, y
 
 
+def multiclass_c3(n_rows=2_000_000, n_cols=100, n_classes=10, seed=0):
+    """C3: U(-1, 1) features; the label is the argmax over n_classes random
+    linear projections (weights N(0, 1)) plus Gumbel(0, 1) noise."""
+    rng = np.random.default_rng(seed)
+    x = rng.uniform(-1.0, 1.0, (n_rows, n_cols)).astype(np.float32)
+    w = rng.standard_normal((n_cols, n_classes)).astype(np.float32)
+    y = np.empty(n_rows, np.float32)
+    step = 1 << 20
+    for a in range(0, n_rows, step):
+        z = x[a:a + step] @ w + rng.gumbel(size=(min(step, n_rows - a), n_classes)).astype(np.float32)
+        y[a:a + step] = np.argmax(z, axis=1)
+    return x, y
+
+
 def forest_c5(n_trees=1000, depth=8, n_cols=50, seed=0):
     """Complete trees as a node array (the library's hb_tree_node layout)."""
     from . import NODE_DTYPE

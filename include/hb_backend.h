@@ -132,6 +132,7 @@ typedef struct hb_node_scan {
 
 #define HB_LOSS_SQUARED_ERROR 0
 #define HB_LOSS_LOGISTIC 1
+#define HB_LOSS_SOFTMAX 2 /* multi:softmax (objective/multiclass.rs), device growth only */
 /* DeviceLoss (src/tree/hist/mod.rs:352). */
 typedef struct hb_device_loss {
   int32_t kind;
@@ -184,6 +185,7 @@ typedef struct hb_train_params {
   float max_delta_step;
   float scale_pos_weight;
   float base_score;         /* NaN: estimate from the labels */
+  int32_t num_class;        /* HB_LOSS_SOFTMAX: classes (3, or 5..64); else 0 or 1 */
 } hb_train_params;
 
 /* ---- engine (CudaHistBackend::new + upload) ------------------------- */
@@ -235,6 +237,8 @@ hb_status hb_gradients(hb_engine* e, const hb_device_loss* loss, const float* la
                        const float* weights, uint64_t n, int32_t* all_finite);
 hb_status hb_add_leaf_values(hb_engine* e, const hb_segment* segs, const float* values,
                              uint32_t n);
+/* n = rows, or rows * classes after hb_train_begin_classes (class-major:
+ * out[k * rows + r]). */
 hb_status hb_read_margins(hb_engine* e, float* out, uint64_t n);
 hb_status hb_reserve_hists(hb_engine* e, uint32_t slots, int32_t* reserved);
 /* `build_resident`: build nodes[k] into slots[k], then for each pair
@@ -265,6 +269,15 @@ hb_status hb_train(hb_engine* e, const hb_train_params* p, const float* labels, 
 /* Start a training run: stage the labels and set every device margin to
  * `base_margin`. */
 hb_status hb_train_begin(hb_engine* e, const float* labels, uint64_t n, float base_margin);
+/* Start a multi:softmax run of `n_classes` outputs (train_trees with
+ * Softmax, src/objective/multiclass.rs): `labels` holds each row's class id
+ * (an integer in [0, n_classes)), `base_margins` one margin per class. Each
+ * hb_train_rounds round then computes the softmax gradients of every class
+ * on the device and grows one tree per class in class order, so the round's
+ * trees are nodes[tree_ptr[r * n_classes + k] ...]; size tree_ptr for
+ * rounds * n_classes + 1. */
+hb_status hb_train_begin_classes(hb_engine* e, const float* labels, uint64_t n,
+                                 const float* base_margins, int32_t n_classes);
 /* Continue the run by `rounds` rounds (gradients at the device margins, one
  * tree grown on the device, its leaves added to the margins), writing the
  * rounds' trees back to back: tree t at nodes[tree_ptr[t] .. tree_ptr[t+1]). */

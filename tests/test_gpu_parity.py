@@ -160,6 +160,53 @@ def test_training_against_reference_f64_mode(case):
         assert rel <= 1e-5, f"tree {t} node {k}: {a[k]} vs {b[k]}"
 
 
+def _first_difference_is_a_tie(on, op, nodes, ptr):
+    """Where two forests first differ in structure, the two splits' gains
+    agree to 1e-5 relative (an f32 gain tie), else False."""
+    t = next(i for i in range(min(len(op), len(ptr)) - 1)
+             if not np.array_equal(on[int(op[i]):int(op[i + 1])]["split_bin"],
+                                   nodes[int(ptr[i]):int(ptr[i + 1])]["split_bin"]))
+    a = on[int(op[t]):int(op[t + 1])]
+    b = nodes[int(ptr[t]):int(ptr[t + 1])]
+    k = next(i for i in range(min(len(a), len(b))) if a[i]["split_bin"] != b[i]["split_bin"])
+    rel = abs(float(a[k]["split_gain"]) - float(b[k]["split_gain"])) / max(abs(float(a[k]["split_gain"])), 1e-30)
+    return rel <= 1e-5
+
+
+@pytest.mark.parametrize("n,f,k,depth,max_bin,rounds", [(20_011, 12, 5, 5, 64, 3),
+                                                        (60_000, 100, 10, 6, 128, 2)])
+def test_softmax_training_matches_oracle(n, f, k, depth, max_bin, rounds):
+    """multi:softmax, gradients on the device (C3's shape at the second
+    size). The device exp is CUDA's double exp rounded once to f32, the
+    oracle's (as the reference's) glibc expf; they can differ in the last
+    bit on rare inputs, so the bar is the north-star criteria: identical
+    structure except gain ties, leaves within 1e-5 relative, margins within
+    1e-6 relative."""
+    x, y = synth.multiclass_c3(n, f, k, seed=n)
+    p = H.TrainingParams(objective="multi:softmax", num_class=k, max_depth=depth, eta=0.2,
+                         max_bin=max_bin)
+    m = H.train(p, x, y, rounds)
+    assert len(m.tree_ptr) == rounds * k + 1
+    on, op, obase, omarg = O.train(x, y, rounds, objective=2, n_outputs=k, max_depth=depth, eta=0.2,
+                                   max_bin=max_bin, fixed_point=True)
+    np.testing.assert_array_equal(m.bases().view(np.uint32), obase.view(np.uint32))
+    if np.array_equal(op, m.tree_ptr) and np.array_equal(on["split_bin"], m.nodes["split_bin"]):
+        np.testing.assert_array_equal(on["split_feature"], m.nodes["split_feature"])
+        np.testing.assert_array_equal(on["default_left"], m.nodes["default_left"])
+        np.testing.assert_allclose(m.nodes["leaf_value"], on["leaf_value"], rtol=1e-5, atol=1e-7)
+        pred = m.predict_margin(x)
+        np.testing.assert_allclose(pred, omarg, rtol=1e-6, atol=1e-6)
+    else:
+        assert _first_difference_is_a_tie(on, op, m.nodes, m.tree_ptr)
+
+
+def test_softmax_refuses_two_or_four_classes():
+    x, y = synth.multiclass_c3(2000, 5, 4, seed=1)
+    p = H.TrainingParams(objective="multi:softmax", num_class=4, max_depth=3)
+    with pytest.raises(H.HbError):
+        H.train(p, x, y, 1)
+
+
 def test_training_is_deterministic():
     x, y = synth.logistic_c2(20_000, 28, seed=11)
     a = gpu_train(x, y, 3, objective="binary:logistic", max_depth=8)

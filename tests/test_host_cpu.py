@@ -112,3 +112,11 @@ def test_shard_split_keeps_bins_and_bitmap():
     for part, lo in ((a, 0), (b, 496)):
         bits = np.unpackbits(part.missing.view(np.uint8), bitorder="little").reshape(5, -1)[:, : part.n_rows]
         np.testing.assert_array_equal(bits.astype(bool), np.isnan(x[lo : lo + part.n_rows].T))
+
+
+def test_softmax_intercepts_match_oracle():
+    rng = np.random.default_rng(6)
+    for n, k in ((1000, 3), (12345, 10), (7, 5)):
+        y = rng.integers(0, k, n).astype(np.float32)
+        np.testing.assert_array_equal(H.softmax_intercepts(y, k).view(np.uint32),
+                                      O.intercepts(2, y, k).view(np.uint32))
