@@ -482,7 +482,6 @@ constexpr int kNSlots = kSlotsPerThread * kH32Threads;  // shared accumulator sl
 // and the row is never folded.
 constexpr int kTrashBin = 256;
 constexpr int kSlotStride = kNSlots + 32;  // words per array, trash row included
-constexpr int kStages = 3;           // rows staged ahead with cp.async
 
 // Staging of one pass of rows (one row per thread): the group's 32 record
 // bytes, the (g, h) pair and the group's missing-mask word.
@@ -490,6 +489,20 @@ struct StageRow {
   uint4 a, b;
 };
 
+// Groups of 32 features a CTA covers: G = 2 when every feature has at most
+// 128 bins (two groups' accumulators then share the 8192 slots, slot row
+// (group << 7) | bin), else 1. A row's pair is staged once for all of them.
+template <int G>
+struct H32 {
+  static constexpr int kStages = G == 1 ? 3 : 2;    // rows staged ahead with cp.async
+  static constexpr int kBinShift = G == 1 ? 8 : 7;  // log2(slot rows per group)
+  static constexpr size_t smem() {
+    return (size_t)kSlotStride * 16 +
+           (size_t)kStages * kH32Threads * (G * sizeof(StageRow) + sizeof(float2) + G * sizeof(uint32_t));
+  }
+};
+
+template <int G>
 __global__ void __launch_bounds__(kH32Threads, 1)
     k_hist32(DevConst c, const uint32_t* __restrict__ fo, const uint8_t* __restrict__ rec,
              const float2* __restrict__ gpair, const Scale* __restrict__ scale,
@@ -497,6 +510,8 @@ __global__ void __launch_bounds__(kH32Threads, 1)
              const LevelState* __restrict__ ls, longlong2* __restrict__ hist,
              long long* __restrict__ totals, unsigned long long* __restrict__ row_stats, int lo_bits,
              int flush_rows) {
+  constexpr int kSt = H32<G>::kStages;
+  constexpr int kBS = H32<G>::kBinShift;
   extern __shared__ __align__(16) uint32_t s32[];
   const int n_entries = ls->n_hentries;
   const uint64_t total = ls->hist_rows;
@@ -508,17 +523,15 @@ __global__ void __launch_bounds__(kH32Threads, 1)
   const uint64_t b = min(total, a + per);
   if (a >= b) return;
 
-  const int g = blockIdx.y;
-  const int f0 = g * kGroupFeatures;
-  const int nf = min(kGroupFeatures, (int)c.n_cols - f0);
-  constexpr int nslots = kNSlots;  // every layout fits 256 bins x 32 feature slots
+  const int g0 = blockIdx.y * G;                          // first group of this CTA
+  const int ng = min(G, (int)c.n_groups - g0);            // its groups
   uint32_t* lo_g = s32;
   uint32_t* hi_g = s32 + kSlotStride;
   uint32_t* lo_h = s32 + 2 * kSlotStride;
   uint32_t* hi_h = s32 + 3 * kSlotStride;
-  StageRow* srec = reinterpret_cast<StageRow*>(s32 + 4 * kSlotStride);  // [kStages][threads]
-  float2* sgp = reinterpret_cast<float2*>(srec + kStages * kH32Threads);  // [kStages][threads]
-  uint32_t* smask = reinterpret_cast<uint32_t*>(sgp + kStages * kH32Threads);
+  StageRow* srec = reinterpret_cast<StageRow*>(s32 + 4 * kSlotStride);       // [kSt][G][threads]
+  float2* sgp = reinterpret_cast<float2*>(srec + kSt * G * kH32Threads);     // [kSt][threads]
+  uint32_t* smask = reinterpret_cast<uint32_t*>(sgp + kSt * kH32Threads);    // [kSt][G][threads]
   for (int i = threadIdx.x; i < 4 * kSlotStride; i += blockDim.x) s32[i] = 0u;
 
   long long acc_g[kSlotsPerThread], acc_h[kSlotsPerThread];
@@ -531,12 +544,21 @@ __global__ void __launch_bounds__(kH32Threads, 1)
   const int lane = tid & 31;
   const uint32_t lane4 = (uint32_t)lane << 2;
   const uint32_t sbase = (uint32_t)__cvta_generic_to_shared(s32);
-  const bool wide = c.stride >= (uint32_t)(32 * g + 32);
-  const uint32_t mask_at = c.mask_off + 4 * g;
-  const bool mask_in_block = mask_at >= (uint32_t)(32 * g) && mask_at + 4 <= (uint32_t)(32 * g + (wide ? 32 : 16));
-  const bool want_totals = totals != nullptr && g == 0;
+  // per group of the CTA: record width, mask placement, padding features
+  bool wide[G], mask_in_block[G];
+  uint32_t mask_at[G], dummy[G];
+#pragma unroll
+  for (int lg = 0; lg < G; ++lg) {
+    const int g = g0 + lg;
+    const int nfg = lg < ng ? min(kGroupFeatures, (int)c.n_cols - g * kGroupFeatures) : 0;
+    wide[lg] = c.stride >= (uint32_t)(32 * g + 32);
+    mask_at[lg] = c.mask_off + 4 * g;
+    mask_in_block[lg] = mask_at[lg] >= (uint32_t)(32 * g) &&
+                        mask_at[lg] + 4 <= (uint32_t)(32 * g + (wide[lg] ? 32 : 16));
+    dummy[lg] = nfg >= 32 ? 0u : (0xffffffffu << nfg);  // padded features: trash row
+  }
+  const bool want_totals = totals != nullptr && g0 == 0;
   const uint32_t lo_mask = (uint32_t)((1ull << lo_bits) - 1ull);
-  const uint32_t dummy = nf >= 32 ? 0u : (0xffffffffu << nf);  // padded features: skipped
   long long tg = 0, th = 0;
 
   // Each thread owns kSlotsPerThread / 4 runs of four consecutive slots
@@ -589,87 +611,99 @@ __global__ void __launch_bounds__(kH32Threads, 1)
     // Every thread copies its own future rows into its own staging slots
     // and later reads only those, so the pipeline needs no CTA barrier.
     auto issue = [&](int it, uint32_t row, bool valid) {
-      const int st = it % kStages;
+      const int st = it % kSt;
       if (valid) {
-        const uint8_t* rp = rec + (uint64_t)row * c.stride + 32 * g;
-        StageRow* d = &srec[st * kH32Threads + tid];
-        __pipeline_memcpy_async(&d->a, rp, 16);
-        if (wide) __pipeline_memcpy_async(&d->b, rp + 16, 16);
+        const uint8_t* rr = rec + (uint64_t)row * c.stride;
+#pragma unroll
+        for (int lg = 0; lg < G; ++lg) {
+          if (lg < ng) {
+            const uint8_t* rp = rr + 32 * (g0 + lg);
+            StageRow* d = &srec[(st * G + lg) * kH32Threads + tid];
+            __pipeline_memcpy_async(&d->a, rp, 16);
+            if (wide[lg]) __pipeline_memcpy_async(&d->b, rp + 16, 16);
+            if (!mask_in_block[lg])
+              __pipeline_memcpy_async(&smask[(st * G + lg) * kH32Threads + tid], rr + mask_at[lg], 4);
+          }
+        }
         __pipeline_memcpy_async(&sgp[st * kH32Threads + tid], &gpair[row], 8);
-        if (!mask_in_block)
-          __pipeline_memcpy_async(&smask[st * kH32Threads + tid],
-                                  rec + (uint64_t)row * c.stride + mask_at, 4);
       }
       __pipeline_commit();
     };
-    for (int p = 0; p < kStages - 1; ++p) {
+    for (int p = 0; p < kSt - 1; ++p) {
       const uint64_t i = pos + (uint64_t)p * kH32Threads + tid;
       const bool v = i < end_e;
       issue(p, v ? row_at(i) : 0u, v);
     }
-    uint64_t ip = pos + (uint64_t)(kStages - 1) * kH32Threads + tid;
+    uint64_t ip = pos + (uint64_t)(kSt - 1) * kH32Threads + tid;
     bool pend_valid = ip < end_e;
     uint32_t pend_row = pend_valid ? row_at(ip) : 0u;
     for (int it = 0; it < n_it; ++it) {
-      issue(it + kStages - 1, pend_row, pend_valid);
-      ip = pos + (uint64_t)(it + kStages) * kH32Threads + tid;
+      issue(it + kSt - 1, pend_row, pend_valid);
+      ip = pos + (uint64_t)(it + kSt) * kH32Threads + tid;
       pend_valid = ip < end_e;
       pend_row = pend_valid ? row_at(ip) : 0u;
-      __pipeline_wait_prior(kStages - 1);
+      __pipeline_wait_prior(kSt - 1);
       const uint64_t i = pos + (uint64_t)it * kH32Threads + tid;
       if (i < end_e) {
-        const int st = it % kStages;
-        const StageRow sr = srec[st * kH32Threads + tid];
+        const int st = it % kSt;
         const float2 pr = sgp[st * kH32Threads + tid];
-        const uint4 v1 = wide ? sr.b : make_uint4(0, 0, 0, 0);
-        uint32_t mask;
-        if (mask_in_block) {
-          const int mw = (int)(mask_at - 32 * g) >> 2;
-          mask = pick_word(sr.a, v1, mw);
-        } else {
-          mask = smask[st * kH32Threads + tid];
-        }
-        mask |= dummy;
         const long long qg = __double2ll_rn((double)pr.x * fg);
         const long long qh = __double2ll_rn((double)pr.y * fh);
         if (want_totals) {
           tg += qg;
           th += qh;
         }
-        const uint32_t lg = (uint32_t)qg & lo_mask, lh = (uint32_t)qh & lo_mask;
+        const uint32_t lg_ = (uint32_t)qg & lo_mask, lh = (uint32_t)qh & lo_mask;
         const uint32_t hg = (uint32_t)(qg >> lo_bits), hh = (uint32_t)(qh >> lo_bits);
-        // rotate the 32 record bytes right by `lane` bytes: word rotation by
-        // lane / 4 (three select stages), then a byte funnel shift
-        uint32_t w[8] = {sr.a.x, sr.a.y, sr.a.z, sr.a.w, v1.x, v1.y, v1.z, v1.w};
-        const int q = lane >> 2;
-        uint32_t t[8];
 #pragma unroll
-        for (int j = 0; j < 8; ++j) t[j] = (q & 4) ? w[(j + 4) & 7] : w[j];
+        for (int lg = 0; lg < G; ++lg) {
+          if (lg >= ng) break;
+          const StageRow sr = srec[(st * G + lg) * kH32Threads + tid];
+          const uint4 v1 = wide[lg] ? sr.b : make_uint4(0, 0, 0, 0);
+          uint32_t mask;
+          if (mask_in_block[lg]) {
+            const int mw = (int)(mask_at[lg] - 32 * (g0 + lg)) >> 2;
+            mask = pick_word(sr.a, v1, mw);
+          } else {
+            mask = smask[(st * G + lg) * kH32Threads + tid];
+          }
+          mask |= dummy[lg];
+          // rotate the 32 record bytes right by `lane` bytes: word rotation by
+          // lane / 4 (three select stages), then a byte funnel shift
+          uint32_t w[8] = {sr.a.x, sr.a.y, sr.a.z, sr.a.w, v1.x, v1.y, v1.z, v1.w};
+          const int q = lane >> 2;
+          uint32_t t[8];
 #pragma unroll
-        for (int j = 0; j < 8; ++j) w[j] = (q & 2) ? t[(j + 2) & 7] : t[j];
+          for (int j = 0; j < 8; ++j) t[j] = (q & 4) ? w[(j + 4) & 7] : w[j];
 #pragma unroll
-        for (int j = 0; j < 8; ++j) t[j] = (q & 1) ? w[(j + 1) & 7] : w[j];
-        const int sh = (lane & 3) * 8;
+          for (int j = 0; j < 8; ++j) w[j] = (q & 2) ? t[(j + 2) & 7] : t[j];
 #pragma unroll
-        for (int j = 0; j < 8; ++j) w[j] = __funnelshift_r(t[j], t[(j + 1) & 7], sh);
-        const uint32_t mrot = __funnelshift_r(mask, mask, lane);
-        // slot byte offset = bin * 128 + 4 * ((lane + s) & 31); the four
-        // arrays sit kSlotStride words apart, one address for all four reds
+          for (int j = 0; j < 8; ++j) t[j] = (q & 1) ? w[(j + 1) & 7] : w[j];
+          const int sh = (lane & 3) * 8;
 #pragma unroll
-        for (int s = 0; s < 32; ++s) {
-          const uint32_t word = w[s >> 2];
-          const int k = s & 3;
-          const uint32_t binx = (k == 0 ? (word << 7) : (word >> (8 * k - 7))) & 0x7f80u;
-          const uint32_t rowx = ((mrot >> s) & 1u) ? (uint32_t)(kTrashBin << 7) : binx;
-          const uint32_t a = sbase + (rowx | ((lane4 + 4u * (uint32_t)s) & 124u));
-          asm volatile(
-              "red.shared.add.u32 [%0], %1;\n\t"
-              "red.shared.add.u32 [%0+%5], %2;\n\t"
-              "red.shared.add.u32 [%0+%6], %3;\n\t"
-              "red.shared.add.u32 [%0+%7], %4;" ::"r"(a),
-              "r"(lg), "r"(hg), "r"(lh), "r"(hh), "n"(kSlotStride * 4), "n"(kSlotStride * 8),
-              "n"(kSlotStride * 12)
-              : "memory");
+          for (int j = 0; j < 8; ++j) w[j] = __funnelshift_r(t[j], t[(j + 1) & 7], sh);
+          const uint32_t mrot = __funnelshift_r(mask, mask, lane);
+          const uint32_t grow = (uint32_t)lg << (kBS + 7);  // this group's slot rows
+          // slot byte offset = row * 128 + 4 * ((lane + s) & 31), row =
+          // (group << kBS) | bin; the four arrays sit kSlotStride words apart,
+          // one address for all four reds
+#pragma unroll
+          for (int s = 0; s < 32; ++s) {
+            const uint32_t word = w[s >> 2];
+            const int k = s & 3;
+            const uint32_t binx = (k == 0 ? (word << 7) : (word >> (8 * k - 7))) &
+                                  (((1u << kBS) - 1u) << 7);
+            const uint32_t rowx = ((mrot >> s) & 1u) ? (uint32_t)(kTrashBin << 7) : (binx | grow);
+            const uint32_t ad = sbase + (rowx | ((lane4 + 4u * (uint32_t)s) & 124u));
+            asm volatile(
+                "red.shared.add.u32 [%0], %1;\n\t"
+                "red.shared.add.u32 [%0+%5], %2;\n\t"
+                "red.shared.add.u32 [%0+%6], %3;\n\t"
+                "red.shared.add.u32 [%0+%7], %4;" ::"r"(ad),
+                "r"(lg_), "r"(hg), "r"(lh), "r"(hh), "n"(kSlotStride * 4), "n"(kSlotStride * 8),
+                "n"(kSlotStride * 12)
+                : "memory");
+          }
         }
       }
       since_fold += kH32Threads;
@@ -689,10 +723,11 @@ __global__ void __launch_bounds__(kH32Threads, 1)
 #pragma unroll
     for (int j = 0; j < kSlotsPerThread; ++j) {
       const int slot = slot_of(j);
-      const int bin = slot >> 5, fl = slot & 31;
-      if (slot < nslots && fl < nf) {
-        const uint32_t fs = fo[f0 + fl];
-        const uint32_t nb = fo[f0 + fl + 1] - fs;
+      const int lgs = slot >> (kBS + 5), bin = (slot >> 5) & ((1 << kBS) - 1), fl = slot & 31;
+      const int f = (g0 + lgs) * kGroupFeatures + fl;
+      if (lgs < ng && f < (int)c.n_cols) {
+        const uint32_t fs = fo[f];
+        const uint32_t nb = fo[f + 1] - fs;
         if ((uint32_t)bin < nb) {
           if (acc_g[j]) atomicAdd(reinterpret_cast<unsigned long long*>(&dst[fs + bin].x), (unsigned long long)acc_g[j]);
           if (acc_h[j]) atomicAdd(reinterpret_cast<unsigned long long*>(&dst[fs + bin].y), (unsigned long long)acc_h[j]);
@@ -1478,7 +1513,8 @@ void launch_walk(const WNode* wtree, const LevelState* ls_last, int max_nodes, c
 
 void hist_configure() {
   cudaFuncSetAttribute(k_hist, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024 - 1024);
-  cudaFuncSetAttribute(k_hist32, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024 - 1024);
+  cudaFuncSetAttribute(k_hist32<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024 - 1024);
+  cudaFuncSetAttribute(k_hist32<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024 - 1024);
 }
 
 void launch_softmax_gradients(int K, float* margin, const float* label, uint64_t n, float min_hess,
@@ -1531,10 +1567,13 @@ static bool use_hist32(const DevConst& c) {
   return !c.hist64 && R > 0 && c.max_bins * 32 <= kNSlots;
 }
 
+// Feature groups per histogram CTA (k_hist32<G>).
+static int hist_groups_per_cta(const DevConst& c) {
+  return (c.max_bins <= 128 && c.n_groups >= 2) ? 2 : 1;
+}
+
 size_t hist_smem_bytes(const DevConst& c) {
-  if (use_hist32(c))
-    return (size_t)kSlotStride * 16 +
-           (size_t)kStages * kH32Threads * (sizeof(StageRow) + sizeof(float2) + sizeof(uint32_t));
+  if (use_hist32(c)) return hist_groups_per_cta(c) == 2 ? H32<2>::smem() : H32<1>::smem();
   return (size_t)c.max_bins * 32 * 16;
 }
 
@@ -1557,17 +1596,23 @@ void launch_hist(const DevConst& c, const uint32_t* fo, const uint8_t* rec, cons
   }
   dim3 grid(grid_x, c.n_groups);
   if (use_hist32(c)) {
-    static size_t granted32[64] = {0};
-    if (dev < 0 || dev >= 64 || granted32[dev] < smem) {
-      if (cudaFuncSetAttribute(k_hist32, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) ==
-              cudaSuccess &&
+    const int G = hist_groups_per_cta(c);
+    static size_t granted32[2][64] = {{0}};
+    if (dev < 0 || dev >= 64 || granted32[G - 1][dev] < smem) {
+      if (cudaFuncSetAttribute(G == 2 ? (const void*)k_hist32<2> : (const void*)k_hist32<1>,
+                               cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) == cudaSuccess &&
           dev >= 0 && dev < 64)
-        granted32[dev] = smem;
+        granted32[G - 1][dev] = smem;
     }
     int K, R;
     split_for_rows(c.global_rows, K, R);
-    k_hist32<<<grid, kH32Threads, smem, s>>>(c, fo, rec, gpair, scale, rows, entries, ls, hist,
-                                             totals, row_stats, K, R);
+    grid.y = (c.n_groups + G - 1) / G;
+    if (G == 2)
+      k_hist32<2><<<grid, kH32Threads, smem, s>>>(c, fo, rec, gpair, scale, rows, entries, ls, hist,
+                                                  totals, row_stats, K, R);
+    else
+      k_hist32<1><<<grid, kH32Threads, smem, s>>>(c, fo, rec, gpair, scale, rows, entries, ls, hist,
+                                                  totals, row_stats, K, R);
     return;
   }
   k_hist<<<grid, kHistThreads, smem, s>>>(c, fo, rec, gpair, scale, rows, entries, ls, hist, totals,

@@ -110,6 +110,12 @@ CASES = {
     # enough rows for the 32-bit split-accumulator histogram kernel
     "c2_large": dict(gen=lambda: synth.logistic_c2(600_003, 28, seed=6), rounds=2,
                      kw=dict(objective="binary:logistic", max_depth=8, eta=0.1)),
+    # several 32-feature groups: one group per histogram CTA (256 bins), and
+    # two groups per CTA (bins <= 128; the last CTA row holds one group)
+    "wide_bins256": dict(gen=lambda: synth.logistic_c2(600_003, 70, seed=12), rounds=1,
+                         kw=dict(objective="binary:logistic", max_depth=5, eta=0.1)),
+    "wide_bins64": dict(gen=lambda: synth.logistic_c2(600_003, 70, seed=13), rounds=1,
+                        kw=dict(objective="binary:logistic", max_depth=5, eta=0.1, max_bin=64)),
 }
 
 
