@@ -709,6 +709,35 @@ class Model:
         finally:
             p.close()
 
+    def save_native(self, path, params):
+        """Write the reference's native JSON model file (loads unchanged in
+        hessboost's Python and Rust APIs); `params` the TrainingParams the
+        model was trained with."""
+        from .model_io import to_native_json
+
+        softmax = params.loss_kind() == HB_LOSS_SOFTMAX
+        text = to_native_json(self.nodes, self.tree_ptr, self.bases(), self.n_features,
+                              objective=params.objective, num_class=params.num_class if softmax else 0,
+                              scale_pos_weight=params.scale_pos_weight,
+                              max_delta_step=float(np.float32(params.max_delta_step)))
+        with open(path, "w") as fh:
+            fh.write(text)
+
+    @staticmethod
+    def load_native(path):
+        """A gbtree model from a native JSON file (numeric scalar-leaf trees)."""
+        from .model_io import from_native_json
+
+        with open(path) as fh:
+            nodes, ptr, base, nf, fields = from_native_json(fh.read())
+        if fields.get("best_iteration") is not None:
+            per = int(fields["n_outputs"]) * int(fields["num_parallel_tree"])
+            n = (int(fields["best_iteration"]) + 1) * per
+            nodes, ptr = nodes[: int(ptr[n])], ptr[: n + 1]
+        if int(fields.get("num_parallel_tree") or 1) != 1:
+            raise ValueError("num_parallel_tree > 1 does not load here")
+        return Model(nodes, ptr, base if base.size > 1 else float(base[0]), nf)
+
 
 def train(params, x=None, y=None, rounds=10, device=0, matrix=None, engine=None):
     """Train ``rounds`` rounds on one GPU (train_trees, train.rs:222)."""

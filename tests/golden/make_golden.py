@@ -15,6 +15,8 @@ reference's tests compute them (f32 arithmetic throughout).
   rounds on the probe (``tests/native_format.rs:441-489``), labels
   ``y_t = 2a - b + t*c + 0.1``.
 * every extracted model (all versions) is a *prediction* known-answer test.
+* ``native/early_stopping.json`` and ``native/multiclass_forest.json`` are
+  two of those files verbatim, the native JSON writer's byte-level fixtures.
 
 Usage: ``python tests/golden/make_golden.py [/path/to/reference]``.  The
 output is committed, so the tests never need the reference at run time.
@@ -125,6 +127,15 @@ def main(ref):
     with open(dst, "w") as fh:
         json.dump(out, fh, separators=(",", ":"))
     print("wrote", dst, "with", len(out["models"]), "models")
+    # two native JSON files verbatim: the model writer's byte-level fixtures
+    os.makedirs(os.path.join(HERE, "native"), exist_ok=True)
+    for name in ("early_stopping", "multiclass_forest"):
+        src = os.path.join(saved, "0.4.9", name + ".json")
+        with open(src, "rb") as fh:
+            raw = fh.read()
+        with open(os.path.join(HERE, "native", name + ".json"), "wb") as fh:
+            fh.write(raw)
+        print("copied", src)
 
 
 if __name__ == "__main__":
