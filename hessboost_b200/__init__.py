@@ -308,11 +308,20 @@ class TrainingParams:
     def n_outputs(self):
         return self.num_class if self.loss_kind() == HB_LOSS_SOFTMAX else 1
 
+    def tree_slots(self):
+        """Nodes one grown tree can have: 2 * leaves (lossguide: max_leaves,
+        else 2^max_depth; depthwise 2^max_depth)."""
+        if self.grow_policy == "lossguide":
+            return 2 * (self.max_leaves if self.max_leaves > 0 else 1 << self.max_depth)
+        return 2 << self.max_depth
+
     def to_c(self):
         c = TrainParamsC()
         c.objective = self.loss_kind()
         c.max_depth = self.max_depth
         c.max_leaves = self.max_leaves
+        if self.grow_policy not in ("depthwise", "lossguide"):
+            raise ValueError(f"grow_policy {self.grow_policy!r}")
         c.grow_policy = HB_GROW_DEPTHWISE if self.grow_policy == "depthwise" else HB_GROW_LOSSGUIDE
         c.eta = self.eta
         c.lambda_ = self.reg_lambda
@@ -571,7 +580,7 @@ class Engine:
 
     # whole-tree growth
     def grow_tree(self, params):
-        cap = 2 << params.max_depth
+        cap = params.tree_slots()
         nodes = np.zeros(cap, NODE_DTYPE)
         n = ctypes.c_uint32()
         p = params.to_c()
@@ -602,7 +611,7 @@ class Engine:
         """`rounds` rounds; returns every tree's nodes and the tree offsets
         (a softmax round's trees are its classes', in class order)."""
         trees = rounds * getattr(self, "_classes", 1)
-        cap = max(trees, 1) * (2 << params.max_depth)
+        cap = max(trees, 1) * params.tree_slots()
         nodes = np.zeros(cap, NODE_DTYPE)
         tree_ptr = np.zeros(trees + 1, np.uint64)
         p = params.to_c()

@@ -88,8 +88,13 @@ struct hb_engine {
   DevBuf<LevelState> ls;
   DevBuf<hb_tree_node> tree;
   DevBuf<WNode> wtree;
+  // lossguide growth: the heap of waiting nodes, its state, node depths
+  DevBuf<LgNode> lg_heap;
+  DevBuf<LgState> lg_state;
+  DevBuf<int32_t> lg_depth;
   bool pending_tree = false;  // host mirror of flags[0]: a grown tree's leaves await the margins
-  int pending_depth = 0;
+  int walk_ls = 1;            // the pending tree: e->ls index holding its node count
+  int walk_nodes = 2;         // and the capacity of its WNode array
   DevBuf<int> flags;          // [0]: pending tree (read by the next gradient or walk kernel)
   // the captured round (CUDA graph) and what it was captured for
   cudaGraphExec_t round_exec = nullptr;
@@ -135,6 +140,7 @@ struct hb_engine {
   int n_out = 1;
   int cls = 0;
   size_t wstride = 0;      // WNodes per class in wtree
+  int lg_alloc = 0;     // leaves the lossguide buffers hold (0: none)
   int alloc_classes = 0;
 };
 
@@ -255,6 +261,7 @@ hb_status ensure_growth_buffers(hb_engine* e, int max_depth) {
   HB_CK(e, e->wtree.alloc(e->wstride * std::max(e->n_out, 1)));
   e->alloc_depth = max_depth;
   e->alloc_classes = e->n_out;
+  e->lg_alloc = 0;
   return HB_OK;
 }
 
@@ -285,8 +292,8 @@ hb_status flush_pending(hb_engine* e) {
     launch_walk_classes(e->n_out, e->wtree.p, (uint32_t)e->wstride, e->rec.p, e->c.stride,
                         e->c.mask_off, e->c.n_rows, e->margin.p, e->flags.p, e->n_sm, e->stream);
   else
-    launch_walk(e->wtree.p, e->ls.p + e->pending_depth + 1, 2 << e->pending_depth, e->rec.p,
-                e->c.stride, e->c.mask_off, e->c.n_rows, e->margin.p, e->flags.p, e->n_sm, e->stream);
+    launch_walk(e->wtree.p, e->ls.p + e->walk_ls, e->walk_nodes, e->rec.p, e->c.stride,
+                e->c.mask_off, e->c.n_rows, e->margin.p, e->flags.p, e->n_sm, e->stream);
   mark_end(e);
   HB_CK(e, cudaMemsetAsync(e->flags.p, 0, sizeof(int), e->stream));
   e->kernel_launches += 1;
@@ -297,13 +304,17 @@ hb_status flush_pending(hb_engine* e) {
 
 // Gradients at the margins, first adding a pending tree's leaves when the
 // device flag says one waits (so a captured round serves every round).
-hb_status run_gradients(hb_engine* e, int kind, float spw, float min_hess, int tree_depth) {
+hb_status run_gradients(hb_engine* e, int kind, float spw, float min_hess, int walk_ls,
+                        int walk_nodes) {
   HB_CK(e, cudaMemsetAsync(e->scale.p, 0, sizeof(Scale), e->stream));
   mark_begin(e, T_GRAD);
-  const int pd = tree_depth > 0 ? tree_depth : e->pending_depth;
+  if (walk_ls < 0) {
+    walk_ls = e->walk_ls;
+    walk_nodes = e->walk_nodes;
+  }
   launch_gradients(kind, e->margin.p, e->label.p, e->weight_key ? e->weight.p : nullptr, spw,
                    min_hess, e->c.n_rows, vector_rows(e), e->gpair.p, e->scale.p,
-                   e->wtree.p, e->ls.p + pd + 1, 2 << pd, e->rec.p, e->c.stride, e->c.mask_off,
+                   e->wtree.p, e->ls.p + walk_ls, walk_nodes, e->rec.p, e->c.stride, e->c.mask_off,
                    e->flags.p, e->n_sm, e->stream);
   mark_end(e);
   e->pending_tree = false;
@@ -313,6 +324,28 @@ hb_status run_gradients(hb_engine* e, int kind, float spw, float min_hess, int t
   if (st != HB_OK) return st;
   e->staged = true;
   return HB_OK;
+}
+
+// Leaves a lossguide tree may reach: max_leaves, else 2^max_depth.
+int lg_leaves(const hb_train_params* p) {
+  return p->max_leaves > 0 ? p->max_leaves : (1 << std::min(p->max_depth, 20));
+}
+
+// Where a grown tree's node count lives (an e->ls index) and how many nodes
+// its WNode array can hold: what the next pass's tree walk needs.
+void walk_shape(const hb_train_params* p, int& ls_index, int& nodes) {
+  if (p->grow_policy == HB_GROW_LOSSGUIDE) {
+    ls_index = 2;
+    nodes = 2 * lg_leaves(p);
+  } else {
+    ls_index = p->max_depth + 1;
+    nodes = 2 << p->max_depth;
+  }
+}
+
+// Node capacity of one tree in the forest buffer.
+uint32_t tree_slots(const hb_train_params* p) {
+  return p->grow_policy == HB_GROW_LOSSGUIDE ? 2u * (uint32_t)lg_leaves(p) : 2u << p->max_depth;
 }
 
 // Grow one tree on the device from the staged gradients (depthwise). Writes
@@ -411,7 +444,8 @@ hb_status grow_device(hb_engine* e, const hb_train_params* p, bool to_forest) {
   }
   HB_CK(e, cudaMemsetAsync(e->flags.p, 0x01, sizeof(int), s));
   e->pending_tree = true;
-  e->pending_depth = D;
+  e->walk_ls = D + 1;
+  e->walk_nodes = 2 << D;
   if (to_forest) {
     launch_finish_tree(e->tree.p, e->ls.p + D + 1, e->forest.p, e->counts.p, e->tree_counter.p,
                        (uint32_t)(2u << D), s);
@@ -425,12 +459,150 @@ hb_status grow_device(hb_engine* e, const hb_train_params* p, bool to_forest) {
   return HB_OK;
 }
 
+// Buffers of lossguide growth with at most L leaves (2L nodes, one
+// histogram slot per node, a frontier of one node and its two children).
+hb_status ensure_lossguide_buffers(hb_engine* e, int L) {
+  if (e->lg_alloc >= L && e->alloc_depth < 0) return HB_OK;
+  const DevConst& c = e->c;
+  const int n_nodes = 2 * L;
+  HB_CK(e, e->hist_all.alloc(1 + (size_t)n_nodes * c.total_bins));
+  HB_CK(e, e->front[0].alloc(2));
+  HB_CK(e, e->front[1].alloc(2));
+  HB_CK(e, e->cand.alloc((size_t)2 * c.n_cols));
+  HB_CK(e, e->dec.alloc(2));
+  e->max_items = std::max(e->max_items, (int)((c.n_rows + kTile - 1) / kTile) + 2);
+  HB_CK(e, e->items.alloc(e->max_items));
+  HB_CK(e, e->dirbits.alloc((size_t)e->max_items * kTileWords));
+  HB_CK(e, e->item_left.alloc(e->max_items));
+  HB_CK(e, e->item_off.alloc(e->max_items));
+  HB_CK(e, e->entries.alloc(2));
+  HB_CK(e, e->pairs.alloc(2));
+  HB_CK(e, e->ls.alloc(kMaxDepth + 2));
+  HB_CK(e, e->tree.alloc(n_nodes));
+  HB_CK(e, e->wtree.alloc(n_nodes));
+  HB_CK(e, e->lg_heap.alloc((size_t)L + 2));
+  HB_CK(e, e->lg_state.alloc(1));
+  HB_CK(e, e->lg_depth.alloc(n_nodes));
+  e->wstride = (size_t)n_nodes;
+  e->alloc_depth = -1;  // the depthwise sizes no longer hold
+  e->lg_alloc = L;
+  return HB_OK;
+}
+
+// The growth buffers the parameters need, allocated before any capture.
+hb_status ensure_buffers(hb_engine* e, const hb_train_params* p) {
+  return p->grow_policy == HB_GROW_LOSSGUIDE ? ensure_lossguide_buffers(e, lg_leaves(p))
+                                             : ensure_growth_buffers(e, p->max_depth);
+}
+
+// Grow one tree with lossguide growth (hist/mod.rs:505) entirely on the
+// device: the root's histogram and scan, then max_leaves - 1 steps, each a
+// heap step (k_lg_step) and, when it expanded a node, that node's partition,
+// the smaller-Hessian child's histogram and both children's scans (the
+// sibling made as parent - built by the scan). Histogram slot = node id, so
+// no slot is reused within a tree. Every node's rows stay in rows[0]: a
+// partition scatters into rows[1] and copies the segment back.
+hb_status grow_lossguide(hb_engine* e, const hb_train_params* p, bool to_forest) {
+  DevConst& c = e->c;
+  const int L = lg_leaves(p);
+  const int n_nodes = 2 * L;
+  c.lambda = (double)p->lambda;
+  c.alpha = (double)p->alpha;
+  c.gamma = (double)p->gamma;
+  c.mcw = (double)p->min_child_weight;
+  c.mds = (double)p->max_delta_step;
+  c.eta = p->eta;
+  c.max_depth = p->max_depth;
+  hb_status st = ensure_lossguide_buffers(e, L);
+  if (st != HB_OK) return st;
+  cudaStream_t s = e->stream;
+  longlong2* hist = e->hist_all.p + 1;
+  long long* totals = reinterpret_cast<long long*>(e->hist_all.p);
+  LevelState* ls0 = e->ls.p;      // the root
+  LevelState* ls1 = e->ls.p + 1;  // the step's expanded node
+  LevelState* ls2 = e->ls.p + 2;  // its children; the tree's node count
+  HB_CK(e, cudaMemsetAsync(e->ls.p, 0, sizeof(LevelState) * 3, s));
+  HB_CK(e, cudaMemsetAsync(e->hist_all.p, 0, sizeof(longlong2) * (1 + (size_t)n_nodes * c.total_bins), s));
+  Front* fr = e->front[0].p;
+  Front* nx = e->front[1].p;
+  launch_root_setup(c.n_rows, fr, e->entries.p, ls0, s);
+  const size_t smem = hist_smem_bytes(c);
+  const int hgrid = hist_grid(e->n_sm);
+  mark_begin(e, T_ROOT);
+  launch_hist(c, e->fo.p, e->rec.p, cur_gpair(e), cur_scale(e), nullptr, e->entries.p, ls0, hist, totals,
+              e->row_stats.p, hgrid, smem, s);
+  mark_end(e);
+  launch_root_stats(fr, totals, s);
+  launch_lg_setup(e->lg_state.p, e->lg_depth.p, e->tree.p, fr, cur_scale(e), ls2, s);
+  mark_begin(e, T_SCAN);
+  launch_scan(c, e->fo.p, hist, fr, ls0, nullptr, 0, cur_scale(e), 1, e->cand.p, s);
+  mark_end(e);
+  HB_CK(e, cudaGetLastError());
+  uint64_t launches = 5;
+  const int max_leaves = p->max_leaves > 0 ? p->max_leaves : INT_MAX;
+  const int depth_limit = p->max_depth > 0 ? p->max_depth : INT_MAX;
+  uint32_t* rows0 = e->rows[0].p;
+  uint32_t* rows1 = e->rows[1].p;
+  for (int k = 0; k < L; ++k) {
+    const bool final_step = k == L - 1;
+    mark_begin(e, T_APPLY);
+    launch_lg_step(c, e->fo.p, e->cuts.p, e->cand.p, k == 0 ? fr : nx, fr, nx, e->dec.p, ls1, ls2,
+                   e->tree.p, e->wtree.p, cur_scale(e), e->lg_heap.p, e->lg_state.p, e->lg_depth.p,
+                   max_leaves, depth_limit, final_step ? 1 : 0, s);
+    mark_end(e);
+    ++launches;
+    if (final_step) break;
+    mark_begin(e, T_PART);
+    launch_part_count(c, e->col.p, e->has_missing ? e->colmiss.p : nullptr, e->rec.p, 0, rows0, k == 0,
+                      fr, e->dec.p, e->items.p, ls1, e->max_items, e->dirbits.p, e->item_left.p, s);
+    launch_part_scan(fr, e->dec.p, ls1, 1, e->item_left.p, e->item_off.p, nx, e->entries.p,
+                     e->pairs.p, ls2, s);
+    launch_part_scatter(fr, e->dec.p, e->items.p, ls1, e->max_items, e->dirbits.p, e->item_off.p, nx,
+                        rows0, k == 0, rows1, s);
+    launch_lg_copy(fr, ls1, rows1, rows0, c.n_rows, e->n_sm, s);
+    mark_end(e);
+    mark_begin(e, T_HIST);
+    launch_hist(c, e->fo.p, e->rec.p, cur_gpair(e), cur_scale(e), rows0, e->entries.p, ls2, hist, nullptr,
+                e->row_stats.p, hgrid, smem, s);
+    mark_end(e);
+    mark_begin(e, T_SCAN);
+    launch_scan(c, e->fo.p, hist, nx, ls2, e->pairs.p, -1, cur_scale(e), 2, e->cand.p, s);
+    mark_end(e);
+    launches += 6;
+    HB_CK(e, cudaGetLastError());
+  }
+  HB_CK(e, cudaMemsetAsync(e->flags.p, 0x01, sizeof(int), s));
+  e->pending_tree = true;
+  walk_shape(p, e->walk_ls, e->walk_nodes);
+  if (to_forest) {
+    launch_finish_tree(e->tree.p, ls2, e->forest.p, e->counts.p, e->tree_counter.p,
+                       (uint32_t)n_nodes, s);
+    HB_CK(e, cudaGetLastError());
+  }
+  e->kernel_launches += launches + (to_forest ? 1 : 0);
+  e->rounds_done += 1;
+  return HB_OK;
+}
+
+hb_status grow_tree_device(hb_engine* e, const hb_train_params* p, bool to_forest) {
+  return p->grow_policy == HB_GROW_LOSSGUIDE ? grow_lossguide(e, p, to_forest)
+                                             : grow_device(e, p, to_forest);
+}
+
 hb_status check_params(hb_engine* e, const hb_train_params* p) {
   if (!p) return HB_INVALID_ARGUMENT;
-  if (p->grow_policy != HB_GROW_DEPTHWISE)
-    return refuse(e, "device growth supports grow_policy = depthwise");
-  if (p->max_depth < 1 || p->max_depth > kMaxDepth)
-    return refuse(e, "device growth supports 1 <= max_depth <= 10");
+  if (p->grow_policy == HB_GROW_LOSSGUIDE) {
+    if (e->comm) return refuse(e, "lossguide growth runs on one GPU");
+    if (p->max_leaves < 0 || p->max_depth < 0 || (p->max_leaves == 0 && p->max_depth == 0))
+      return refuse(e, "lossguide growth needs max_leaves or max_depth");
+    if (lg_leaves(p) < 1 || lg_leaves(p) > 1024)
+      return refuse(e, "lossguide growth supports at most 1024 leaves");
+    if (p->objective == HB_LOSS_SOFTMAX) return refuse(e, "lossguide growth is single-output");
+  } else if (p->grow_policy != HB_GROW_DEPTHWISE) {
+    return HB_INVALID_ARGUMENT;
+  } else if (p->max_depth < 1 || p->max_depth > kMaxDepth) {
+    return refuse(e, "depthwise device growth supports 1 <= max_depth <= 10");
+  }
   if (p->objective != HB_LOSS_SQUARED_ERROR && p->objective != HB_LOSS_LOGISTIC &&
       p->objective != HB_LOSS_SOFTMAX)
     return HB_INVALID_ARGUMENT;
@@ -515,6 +687,9 @@ hb_status hb_engine_destroy(hb_engine* e) {
   e->cand.release();
   e->dec.release();
   e->items.release();
+  e->lg_heap.release();
+  e->lg_state.release();
+  e->lg_depth.release();
   e->dirbits.release();
   e->item_left.release();
   e->item_off.release();
@@ -930,7 +1105,7 @@ hb_status hb_gradients(hb_engine* e, const hb_device_loss* loss, const float* la
   if (e->row_begin % 8) return refuse(e, "shards must start on a multiple of 8 rows");
   hb_status st = stage_labels(e, labels, weights, n);
   if (st != HB_OK) return st;
-  st = run_gradients(e, loss->kind, loss->scale_pos_weight, loss->min_hess, 0);
+  st = run_gradients(e, loss->kind, loss->scale_pos_weight, loss->min_hess, -1, 0);
   if (st != HB_OK) return st;
   Scale h;
   HB_CK(e, cudaMemcpyAsync(&h, e->scale.p, sizeof(Scale), cudaMemcpyDeviceToHost, e->stream));
@@ -1123,12 +1298,13 @@ hb_status hb_grow_tree(hb_engine* e, const hb_train_params* p, hb_tree_node* nod
   if (st != HB_OK) return st;
   if (!e->uploaded || !e->staged || !e->margins_loaded) return refuse(e, "no staged gradients or margins");
   if (!nodes || !n_nodes) return HB_INVALID_ARGUMENT;
-  st = grow_device(e, p, false);
+  st = grow_tree_device(e, p, false);
   if (st != HB_OK) return st;
+  const int walk_ls = e->walk_ls;
   st = flush_pending(e);
   if (st != HB_OK) return st;
   LevelState last;
-  HB_CK(e, cudaMemcpyAsync(&last, e->ls.p + p->max_depth + 1, sizeof(LevelState), cudaMemcpyDeviceToHost, e->stream));
+  HB_CK(e, cudaMemcpyAsync(&last, e->ls.p + walk_ls, sizeof(LevelState), cudaMemcpyDeviceToHost, e->stream));
   HB_CK(e, cudaStreamSynchronize(e->stream));
   if ((uint32_t)last.n_nodes > nodes_cap) return refuse(e, "nodes_cap too small");
   HB_CK(e, cudaMemcpyAsync(nodes, e->tree.p, sizeof(hb_tree_node) * last.n_nodes, cudaMemcpyDeviceToHost, e->stream));
@@ -1157,7 +1333,7 @@ static hb_status round_work(hb_engine* e, const hb_train_params* p) {
     for (int k = 0; k < e->n_out; ++k) {
       e->cls = k;
       hb_status st = finish_scale(e);
-      if (st == HB_OK) st = grow_device(e, p, true);
+      if (st == HB_OK) st = grow_tree_device(e, p, true);
       if (st != HB_OK) {
         e->cls = 0;
         return st;
@@ -1168,9 +1344,11 @@ static hb_status round_work(hb_engine* e, const hb_train_params* p) {
     e->staged = true;
     return HB_OK;
   }
-  hb_status st = run_gradients(e, p->objective, p->scale_pos_weight, 1e-16f, p->max_depth);
+  int wl = 0, wn = 0;
+  walk_shape(p, wl, wn);
+  hb_status st = run_gradients(e, p->objective, p->scale_pos_weight, 1e-16f, wl, wn);
   if (st != HB_OK) return st;
-  return grow_device(e, p, true);
+  return grow_tree_device(e, p, true);
 }
 
 // Rounds as CUDA graphs: the kernels of a round are captured once and the
@@ -1224,7 +1402,8 @@ static hb_status graph_rounds(hb_engine* e, const hb_train_params* p, int rounds
                         e->cand.p, e->dec.p, e->items.p, e->dirbits.p, e->item_left.p,
                         e->item_off.p, e->entries.p, e->pairs.p, e->ls.p, e->tree.p,
                         e->wtree.p, e->forest.p, e->counts.p, e->tree_counter.p,
-                        e->row_stats.p, e->flags.p};
+                        e->row_stats.p, e->flags.p, e->lg_heap.p, e->lg_state.p,
+                        e->lg_depth.p};
   const int weighted = e->weight_key ? 1 : 0;
   std::vector<unsigned char> key(sizeof(hb_train_params) + sizeof(ptrs) + sizeof(int) * 2);
   std::memcpy(key.data(), p, sizeof(hb_train_params));
@@ -1252,7 +1431,7 @@ static hb_status graph_rounds(hb_engine* e, const hb_train_params* p, int rounds
   }
   HB_CK(e, cudaEventRecord(e->run_ev[1], s));
   e->pending_tree = true;
-  e->pending_depth = p->max_depth;
+  walk_shape(p, e->walk_ls, e->walk_nodes);
   return HB_OK;
 }
 
@@ -1323,19 +1502,19 @@ hb_status hb_train_rounds(hb_engine* e, const hb_train_params* p, int32_t rounds
   if (!e->train_begun || !e->margins_loaded) return refuse(e, "no training run (hb_train_begin)");
   if (rounds < 0 || !tree_ptr || (!nodes && rounds)) return HB_INVALID_ARGUMENT;
   cudaStream_t s = e->stream;
-  const uint32_t max_nodes = 2u << p->max_depth;
+  const uint32_t max_nodes = tree_slots(p);
   const int trees = rounds * e->n_out;  // one tree per class and round
   HB_CK(e, e->forest.alloc(std::max<size_t>((size_t)trees * max_nodes, 1)));
   HB_CK(e, e->counts.alloc(std::max(trees, 1)));
   HB_CK(e, cudaMemsetAsync(e->tree_counter.p, 0, 4, s));
   if (e->use_graphs && rounds > 0) {
-    st = ensure_growth_buffers(e, p->max_depth);
+    st = ensure_buffers(e, p);
     if (st != HB_OK) return st;
     st = graph_rounds(e, p, rounds);
     if (st != HB_OK) return st;
   } else {
     HB_CK(e, cudaEventRecord(e->run_ev[0], s));
-    st = ensure_growth_buffers(e, p->max_depth);
+    st = ensure_buffers(e, p);
     if (st != HB_OK) return st;
     for (int r = 0; r < rounds; ++r) {
       st = round_work(e, p);

@@ -135,4 +135,28 @@ struct Triple {
   int32_t parent, built, sibling, pad;
 };
 
+// Lossguide growth (src/tree/builder/hist/mod.rs:505): a node waiting in
+// the max-heap with its best split, keyed by the f64::total_cmp order of
+// that split's loss change.
+struct LgNode {
+  long long key;      // total-order key of (double)loss
+  int32_t nid, depth;
+  uint32_t begin, len;  // its rows in the row buffer
+  long long g, h;     // its statistics (fixed point)
+  float loss;         // best split: loss change (0: none found)
+  int32_t feature;    // -1: none
+  int32_t bin;        // last global bin going left, -1 = below every bin
+  int32_t default_left;
+  long long lg, lh;   // that split's left child statistics
+};
+
+struct LgState {
+  int32_t heap_n;     // nodes in the heap
+  int32_t n_nodes;    // tree nodes so far
+  int32_t n_leaves;   // leaves of the growing tree (a node counts until expanded)
+  int32_t done;       // growth finished: every later step does nothing
+  int32_t n_pending;  // children (in `next`) whose scan awaits merging
+  int32_t pad[3];
+};
+
 }  // namespace hb

@@ -845,8 +845,11 @@ __global__ void __launch_bounds__(kSplitThreads)
   Cand* out = cand + (uint64_t)k * c.n_cols + f;
   longlong2 v = make_longlong2(0, 0);
   if (fr.slot >= 0 && t < nb) {
-    if (pairs != nullptr && fr.slot >= sib_base) {
-      const Triple tr = pairs[fr.slot - sib_base];
+    // depthwise: sibling slots start at sib_base; lossguide (sib_base < 0):
+    // the one pair of the step, pairs[0]
+    const bool sib = pairs != nullptr && (sib_base >= 0 ? fr.slot >= sib_base : fr.slot == pairs[0].sibling);
+    if (sib) {
+      const Triple tr = pairs[sib_base >= 0 ? fr.slot - sib_base : 0];
       const longlong2 pv = hist[(uint64_t)tr.parent * c.total_bins + fs + t];
       const longlong2 bv = hist[(uint64_t)tr.built * c.total_bins + fs + t];
       v = make_longlong2(pv.x - bv.x, pv.y - bv.y);
@@ -1157,6 +1160,268 @@ __global__ void __launch_bounds__(kApplyThreads)
     ls_next->n_nodes = n_nodes + 2 * n_split;
     ls_next->tree_index = ls->tree_index;
   }
+}
+
+// ---------------------------------------------------------------------------
+// Lossguide growth on the device (grow_lossguide, src/tree/builder/hist/
+// mod.rs:505). A step merges the pending nodes' scans into their best splits
+// and pushes them in order, then pops until a node expands or growth ends.
+// A popped node becomes a leaf when the tree already has max_leaves leaves
+// (growth then stops and the nodes left in the heap are leaves too), or when
+// it is too deep or has no valid split. An expanded node is set up as a
+// one-node level for the partition, histogram and scan kernels. The heap is
+// Rust's BinaryHeap as the host builder uses it (push: sift_up; pop: swap
+// the last into the root, sift_down_to_bottom, sift_up), keyed by the
+// f64::total_cmp order of the best loss change.
+constexpr int kLgThreads = 64;  // two warps: one per pending node
+
+__device__ __forceinline__ long long total_key(double v) {
+  const long long b = __double_as_longlong(v);
+  return b ^ (long long)((unsigned long long)(b >> 63) >> 1);
+}
+
+__device__ void lg_sift_up(LgNode* heap, int start, int pos) {
+  const LgNode hole = heap[pos];
+  while (pos > start) {
+    const int parent = (pos - 1) / 2;
+    if (hole.key <= heap[parent].key) break;
+    heap[pos] = heap[parent];
+    pos = parent;
+  }
+  heap[pos] = hole;
+}
+
+__device__ LgNode lg_pop(LgNode* heap, int& n) {
+  LgNode item = heap[n - 1];
+  --n;
+  if (n > 0) {
+    const LgNode root = heap[0];
+    heap[0] = item;
+    item = root;
+    const int end = n;
+    int pos = 0;
+    const LgNode hole = heap[0];
+    int child = 1;
+    while (end >= 2 && child <= end - 2) {
+      if (heap[child].key <= heap[child + 1].key) child += 1;
+      heap[pos] = heap[child];
+      pos = child;
+      child = 2 * pos + 1;
+    }
+    if (child == end - 1) {
+      heap[pos] = heap[child];
+      pos = child;
+    }
+    heap[pos] = hole;
+    lg_sift_up(heap, 0, pos);
+  }
+  return item;
+}
+
+// finalize_leaf_values (shared.rs:174) then scale_leaves(eta), as k_apply
+__device__ void lg_leaf(const LgNode& e, const DevConst& c, double ig, double ih,
+                        hb_tree_node* tree, WNode* wtree) {
+  const float w = __double2float_rn(calc_weight(ll2d(e.g) * ig, ll2d(e.h) * ih, c));
+  const float v = __fmul_rn(w, c.eta);
+  tree[e.nid].leaf_value = v;
+  WNode wn;
+  wn.left = -1;
+  wn.feature = 0u;
+  wn.limit = 0u;
+  wn.leaf = v;
+  wtree[e.nid] = wn;
+}
+
+__global__ void __launch_bounds__(kLgThreads)
+    k_lg_step(DevConst c, const uint32_t* __restrict__ fo, const float* __restrict__ cuts,
+              const Cand* __restrict__ cand, const Front* __restrict__ pend, Front* front,
+              Front* next, Decision* dec, LevelState* ls, LevelState* ls_next,
+              hb_tree_node* __restrict__ tree, WNode* __restrict__ wtree,
+              const Scale* __restrict__ scale, LgNode* __restrict__ heap, LgState* st,
+              int32_t* __restrict__ ndepth, int max_leaves, int depth_limit, int final_step) {
+  __shared__ LgNode s_new[2];
+  const LgState S0 = *st;
+  if (S0.done) return;
+  const double ig = scale->ig, ih = scale->ih;
+  const int np = S0.n_pending;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (warp < np) {
+    // the node's best split over its features: the largest loss change
+    // above 0, the lowest feature among equals (need_replace, builder/mod.rs:313)
+    float bl = 0.0f;
+    int bf = -1;
+    for (uint32_t f = lane; f < c.n_cols; f += 32) {
+      const float l = cand[(uint64_t)warp * c.n_cols + f].loss;
+      if (l > bl) {
+        bl = l;
+        bf = (int)f;
+      }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      const float ol = __shfl_xor_sync(kFull, bl, o);
+      const int of = __shfl_xor_sync(kFull, bf, o);
+      if (ol > bl || (ol == bl && of >= 0 && (bf < 0 || of < bf))) {
+        bl = ol;
+        bf = of;
+      }
+    }
+    if (lane == 0) {
+      const Front fr = pend[warp];
+      LgNode x;
+      x.nid = fr.node;
+      x.depth = ndepth[fr.node];
+      x.begin = fr.begin;
+      x.len = fr.len;
+      x.g = fr.g;
+      x.h = fr.h;
+      if (bf >= 0) {
+        const Cand cd = cand[(uint64_t)warp * c.n_cols + bf];
+        x.loss = cd.loss;
+        x.feature = bf;
+        x.bin = cd.bin;
+        x.default_left = cd.default_left;
+        x.lg = cd.lg;
+        x.lh = cd.lh;
+      } else {
+        x.loss = 0.0f;
+        x.feature = -1;
+        x.bin = -1;
+        x.default_left = 1;
+        x.lg = x.lh = 0;
+      }
+      x.key = total_key((double)x.loss);
+      s_new[warp] = x;
+    }
+  }
+  __syncthreads();
+  if (threadIdx.x != 0) return;
+  LgState S = S0;
+  int n = S.heap_n;
+  for (int k = 0; k < np; ++k) {
+    heap[n] = s_new[k];
+    ++n;
+    lg_sift_up(heap, 0, n - 1);
+  }
+  LevelState idle{};
+  *ls = idle;  // nothing to partition unless a node expands (also resets done_ctas)
+  ls_next->n_front = 0;
+  bool expanded = false;
+  while (n > 0) {
+    const LgNode e = lg_pop(heap, n);
+    if (S.n_leaves >= max_leaves) {
+      lg_leaf(e, c, ig, ih, tree, wtree);
+      S.done = 1;
+      break;
+    }
+    const double lh = ll2d(e.lh) * ih, rh = ll2d(e.h - e.lh) * ih;
+    const bool valid = e.feature >= 0 && (double)e.loss > kRtEps && (double)e.loss >= c.gamma &&
+                       lh > 0.0 && rh > 0.0 && lh >= c.mcw && rh >= c.mcw;
+    if (!(e.depth < depth_limit && valid) || final_step) {
+      lg_leaf(e, c, ig, ih, tree, wtree);
+      continue;
+    }
+    // expand (prepare_split, hist/mod.rs:639): children ids in order
+    const int left_id = S.n_nodes;
+    S.n_nodes += 2;
+    const long long rg_q = e.g - e.lg, rh_q = e.h - e.lh;
+    const double dlg = ll2d(e.lg) * ig, dlh = ll2d(e.lh) * ih;
+    const double drg = ll2d(rg_q) * ig, drh = ll2d(rh_q) * ih;
+    hb_tree_node nd = tree[e.nid];
+    nd.split_feature = (uint32_t)e.feature;
+    nd.split_cond = e.bin < 0 ? kBelowAll : cuts[e.bin];
+    nd.default_left = e.default_left ? 1u : 0u;
+    nd.left = left_id;
+    nd.right = left_id + 1;
+    nd.split_bin = e.bin;
+    nd.split_gain = e.loss;
+    tree[e.nid] = nd;
+    tree[left_id] = make_leaf(xgb_weight(dlg, dlh, c), (float)dlh);
+    tree[left_id + 1] = make_leaf(xgb_weight(drg, drh, c), (float)drh);
+    ndepth[left_id] = ndepth[left_id + 1] = e.depth + 1;
+    const uint32_t fs = fo[e.feature];
+    const uint32_t limit = e.bin < 0 ? 0u : (uint32_t)(e.bin + 1) - fs;
+    WNode wn;
+    wn.left = left_id;
+    wn.feature = (uint32_t)e.feature | (e.default_left ? 0x80000000u : 0u);
+    wn.limit = limit;
+    wn.leaf = 0.0f;
+    wtree[e.nid] = wn;
+    Front f0{};
+    f0.node = e.nid;
+    f0.slot = e.nid;  // histogram slot = node id
+    f0.begin = e.begin;
+    f0.len = e.len;
+    f0.g = e.g;
+    f0.h = e.h;
+    front[0] = f0;
+    Decision d{};
+    d.split = 1;
+    d.pair = 0;
+    d.feature = (uint32_t)e.feature;
+    d.limit = limit;
+    d.default_left = e.default_left;
+    d.item_begin = 0;
+    d.item_count = (int)((e.len + kTile - 1) / kTile);
+    d.lg = e.lg;
+    d.lh = e.lh;
+    dec[0] = d;
+    Front l{}, r{};
+    l.node = left_id;
+    l.slot = left_id;
+    l.g = e.lg;
+    l.h = e.lh;
+    r.node = left_id + 1;
+    r.slot = left_id + 1;
+    r.g = rg_q;
+    r.h = rh_q;
+    next[0] = l;
+    next[1] = r;
+    LevelState lv{};
+    lv.n_front = 1;
+    lv.n_items = d.item_count;
+    lv.n_split = 1;
+    lv.n_nodes = S.n_nodes;
+    *ls = lv;
+    ls_next->n_front = 2;
+    S.n_leaves += 1;
+    expanded = true;
+    break;
+  }
+  if (!expanded) S.done = 1;
+  if (S.done) {  // the nodes left in the heap are leaves
+    for (int i = 0; i < n; ++i) lg_leaf(heap[i], c, ig, ih, tree, wtree);
+    n = 0;
+  }
+  S.heap_n = n;
+  S.n_pending = expanded ? 2 : 0;
+  *st = S;
+  ls_next->n_nodes = S.n_nodes;
+}
+
+// Lossguide state of a new tree: the root pending, one node, one leaf.
+__global__ void k_lg_setup(LgState* st, int32_t* ndepth, hb_tree_node* tree, const Front* root,
+                           const Scale* scale, LevelState* ls_next) {
+  LgState S{};
+  S.heap_n = 0;
+  S.n_nodes = 1;
+  S.n_leaves = 1;
+  S.done = 0;
+  S.n_pending = 1;
+  *st = S;
+  ndepth[0] = 0;
+  tree[0] = make_leaf(0.0f, (float)(ll2d(root->h) * scale->ih));
+  ls_next->n_nodes = 1;
+}
+
+// After a lossguide partition (rows_in -> rows_out over the expanded node's
+// segment), copy the segment back so every node's rows stay in rows_in.
+__global__ void k_lg_copy(const Front* __restrict__ front, const LevelState* __restrict__ ls,
+                          const uint32_t* __restrict__ from, uint32_t* __restrict__ to) {
+  if (ls->n_items == 0) return;
+  const Front fr = front[0];
+  for (uint32_t i = blockIdx.x * blockDim.x + threadIdx.x; i < fr.len; i += gridDim.x * blockDim.x)
+    to[fr.begin + i] = from[fr.begin + i];
 }
 
 // ---------------------------------------------------------------------------
@@ -1668,6 +1933,27 @@ void launch_part_scatter(const Front* front, const Decision* dec, const PItem* i
                                                     next, rows_in, identity, rows_out);
 }
 
+
+void launch_lg_step(const DevConst& c, const uint32_t* fo, const float* cuts, const Cand* cand,
+                    const Front* pend, Front* front, Front* next, Decision* dec, LevelState* ls,
+                    LevelState* ls_next, hb_tree_node* tree, WNode* wtree, const Scale* scale,
+                    LgNode* heap, LgState* st, int32_t* ndepth, int max_leaves, int depth_limit,
+                    int final_step, cudaStream_t s) {
+  k_lg_step<<<1, kLgThreads, 0, s>>>(c, fo, cuts, cand, pend, front, next, dec, ls, ls_next, tree,
+                                     wtree, scale, heap, st, ndepth, max_leaves, depth_limit,
+                                     final_step);
+}
+
+void launch_lg_setup(LgState* st, int32_t* ndepth, hb_tree_node* tree, const Front* root,
+                     const Scale* scale, LevelState* ls_next, cudaStream_t s) {
+  k_lg_setup<<<1, 1, 0, s>>>(st, ndepth, tree, root, scale, ls_next);
+}
+
+void launch_lg_copy(const Front* front, const LevelState* ls, const uint32_t* from, uint32_t* to,
+                    uint64_t n_rows, int n_sm, cudaStream_t s) {
+  const int grid = (int)std::max<uint64_t>(1, std::min<uint64_t>((n_rows + 255) / 256, (uint64_t)n_sm * 4));
+  k_lg_copy<<<grid, 256, 0, s>>>(front, ls, from, to);
+}
 
 void launch_root_setup(uint64_t n_rows, Front* front, HEntry* entries, LevelState* ls,
                        cudaStream_t s) {

@@ -78,6 +78,17 @@ void launch_part_scatter(const Front* front, const Decision* dec, const PItem* i
                          const uint32_t* item_left_off, const Front* next,
                          const uint32_t* rows_in, int identity, uint32_t* rows_out,
                          cudaStream_t s);
+// Lossguide growth: one step (merge + push the pending nodes, pop until one
+// expands), a new tree's state, and the copy-back of a partitioned segment.
+void launch_lg_step(const DevConst& c, const uint32_t* fo, const float* cuts, const Cand* cand,
+                    const Front* pend, Front* front, Front* next, Decision* dec, LevelState* ls,
+                    LevelState* ls_next, hb_tree_node* tree, WNode* wtree, const Scale* scale,
+                    LgNode* heap, LgState* st, int32_t* ndepth, int max_leaves, int depth_limit,
+                    int final_step, cudaStream_t s);
+void launch_lg_setup(LgState* st, int32_t* ndepth, hb_tree_node* tree, const Front* root,
+                     const Scale* scale, LevelState* ls_next, cudaStream_t s);
+void launch_lg_copy(const Front* front, const LevelState* ls, const uint32_t* from, uint32_t* to,
+                    uint64_t n_rows, int n_sm, cudaStream_t s);
 void launch_root_setup(uint64_t n_rows, Front* front, HEntry* entries, LevelState* ls,
                        cudaStream_t s);
 void launch_root_stats(Front* front, const long long* totals, cudaStream_t s);

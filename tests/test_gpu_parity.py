@@ -91,6 +91,12 @@ def test_training_fixture_multi_target_bit_exact():
 
 
 # --------------------------------------------- training: oracle fixed point
+def _step_dataset(n):
+    """training/train/tests.rs:22 `step_dataset`: x = i / n, y = [x >= 0.5]."""
+    x = (np.arange(n, dtype=np.float32) / np.float32(n)).reshape(n, 1)
+    return x, (x[:, 0] >= 0.5).astype(np.float32)
+
+
 CASES = {
     # shape of C1 (dense regression), reduced rows
     "c1_regression": dict(gen=lambda: synth.regression_c1(20_000, 28, seed=3), rounds=4,
@@ -116,6 +122,26 @@ CASES = {
                          kw=dict(objective="binary:logistic", max_depth=5, eta=0.1)),
     "wide_bins64": dict(gen=lambda: synth.logistic_c2(600_003, 70, seed=13), rounds=1,
                         kw=dict(objective="binary:logistic", max_depth=5, eta=0.1, max_bin=64)),
+    # lossguide growth (best loss change first): by max_leaves, by max_depth
+    # alone (2^max_depth leaves), both, with regularisation leaving nodes
+    # unexpandable, a tiny ragged set, and the 32-bit histogram kernel
+    "lossguide_leaves": dict(gen=lambda: synth.logistic_c2(30_011, 28, seed=15), rounds=3,
+                             kw=dict(objective="binary:logistic", grow_policy="lossguide", max_depth=0,
+                                     max_leaves=31, eta=0.1)),
+    "lossguide_depth": dict(gen=lambda: synth.regression_c1(20_000, 12, seed=16), rounds=3,
+                            kw=dict(grow_policy="lossguide", max_depth=5, max_leaves=0)),
+    "lossguide_both": dict(gen=lambda: synth.regression_c1(9000, 10, seed=17), rounds=3,
+                           kw=dict(grow_policy="lossguide", max_depth=4, max_leaves=12, gamma=0.3,
+                                   min_child_weight=40.0, reg_lambda=2.0)),
+    "lossguide_tiny": dict(gen=lambda: synth.logistic_c2(41, 5, seed=18, missing=0.2), rounds=3,
+                           kw=dict(objective="binary:logistic", grow_policy="lossguide", max_depth=0,
+                                   max_leaves=8, eta=0.3)),
+    # the reference's lossguide end-to-end set (training/train/tests.rs:218)
+    "lossguide_step": dict(gen=lambda: _step_dataset(120), rounds=60,
+                           kw=dict(grow_policy="lossguide", max_leaves=16, eta=0.3)),
+    "lossguide_large": dict(gen=lambda: synth.logistic_c2(600_003, 28, seed=19), rounds=2,
+                            kw=dict(objective="binary:logistic", grow_policy="lossguide", max_depth=0,
+                                    max_leaves=96, eta=0.1)),
 }
 
 
@@ -123,6 +149,8 @@ def _orc_kw(kw):
     m = dict(kw)
     if "objective" in m:
         m["objective"] = 1 if m["objective"] == "binary:logistic" else 0
+    if "grow_policy" in m:
+        m["grow_policy"] = 1 if m["grow_policy"] == "lossguide" else 0
     return m
 
 
@@ -204,6 +232,32 @@ def test_softmax_training_matches_oracle(n, f, k, depth, max_bin, rounds):
         np.testing.assert_allclose(pred, omarg, rtol=1e-6, atol=1e-6)
     else:
         assert _first_difference_is_a_tie(on, op, m.nodes, m.tree_ptr)
+
+
+def test_lossguide_grow_tree_matches_oracle_and_refusals():
+    """One lossguide tree through hb_grow_tree (the RowEngine seam) equals the
+    oracle's first tree; softmax and unbounded lossguide are refused."""
+    x, y = synth.logistic_c2(12_007, 9, seed=23)
+    params = H.TrainingParams(objective="binary:logistic", grow_policy="lossguide", max_depth=0,
+                              max_leaves=17, eta=0.3)
+    mtx = H.BinnedMatrix.from_dense(x)
+    base = H.base_margin(params, y)
+    e = H.Engine()
+    try:
+        e.upload(mtx)
+        e.load_margins(np.full(mtx.n_rows, base, np.float32))
+        assert e.gradients(H.HB_LOSS_LOGISTIC, y)
+        got = e.grow_tree(params)
+        on, op, _, _ = O.train(x, y, 1, objective=1, grow_policy=1, max_depth=0, max_leaves=17, eta=0.3,
+                               fixed_point=True)
+        assert_forest_equal(got, [0, len(got)], on, op, "grow_tree")
+        assert e.gradients(H.HB_LOSS_LOGISTIC, y)
+        for bad in (dict(max_depth=0, max_leaves=0), dict(max_depth=0, max_leaves=2000)):
+            p = H.TrainingParams(objective="binary:logistic", grow_policy="lossguide", **bad)
+            with pytest.raises(H.HbError):
+                e.grow_tree(p)
+    finally:
+        e.close()
 
 
 def test_softmax_refuses_two_or_four_classes():

@@ -160,3 +160,37 @@ def test_softmax_training_fixed_matches_f64_structure():
     np.testing.assert_allclose(a[0]["leaf_value"], b[0]["leaf_value"], rtol=1e-5, atol=1e-7)
     np.testing.assert_array_equal(a[2], b[2])
     np.testing.assert_array_equal(a[2], O.intercepts(2, y, 4))
+
+
+def _step_dataset(n):
+    """training/train/tests.rs:22 `step_dataset`: x = i / n, y = [x >= 0.5]."""
+    x = (np.arange(n, dtype=np.float32) / np.float32(n)).reshape(n, 1)
+    return x, (x[:, 0] >= 0.5).astype(np.float32)
+
+
+@pytest.mark.parametrize("fixed", [False, True], ids=["f64", "fixed_point"])
+def test_lossguide_trains_end_to_end(fixed):
+    """training/train/tests.rs:218 `lossguide_trains_end_to_end`: squared
+    error, lossguide, max_leaves 16, eta 0.3, 60 rounds on the 120-row step
+    set; RMSE below 0.06, and no tree above 16 leaves."""
+    x, y = _step_dataset(120)
+    nodes, ptr, base, margins = O.train(x, y, 60, grow_policy=1, max_leaves=16, eta=0.3,
+                                        fixed_point=fixed)
+    rmse = float(np.sqrt(np.mean((margins[:, 0].astype(np.float64) - y) ** 2)))
+    assert rmse < 0.06, rmse
+    sizes = np.diff(np.asarray(ptr, np.int64))
+    assert sizes.max() <= 31 and sizes.min() >= 1
+
+
+def test_lossguide_fixed_matches_f64_structure():
+    """The fixed-point summation grows the same lossguide trees as f64 (no
+    exact-gain ties on this set), leaves within 1e-5 relative."""
+    rng = np.random.default_rng(4)
+    x = rng.standard_normal((3000, 6)).astype(np.float32)
+    y = (x[:, 0] * 2 + np.sin(x[:, 1] * 3) + 0.1 * rng.standard_normal(3000)).astype(np.float32)
+    a = O.train(x, y, 3, grow_policy=1, max_leaves=20, max_depth=0, fixed_point=False)
+    b = O.train(x, y, 3, grow_policy=1, max_leaves=20, max_depth=0, fixed_point=True)
+    np.testing.assert_array_equal(a[1], b[1])
+    for k in ("left", "right", "split_feature", "default_left", "split_bin"):
+        np.testing.assert_array_equal(a[0][k], b[0][k], err_msg=k)
+    np.testing.assert_allclose(a[0]["leaf_value"], b[0]["leaf_value"], rtol=1e-5, atol=1e-7)
