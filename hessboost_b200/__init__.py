@@ -129,6 +129,8 @@ class GHist(ctypes.Structure):
         ("cut_values", ctypes.POINTER(ctypes.c_float)),
         ("columns", ctypes.POINTER(ctypes.c_uint8)),
         ("missing", ctypes.POINTER(ctypes.c_uint64)),
+        ("row_ptr", ctypes.POINTER(ctypes.c_uint64)),
+        ("row_bins", ctypes.POINTER(ctypes.c_uint32)),
     ]
 
 
@@ -239,6 +241,9 @@ SIGNATURES = {
     "hb_predict_margin_device": [_vp, ctypes.c_void_p, ctypes.c_uint64, ctypes.c_void_p, _vp],
     "hb_cuts_dense": [_f32p, ctypes.c_uint64, ctypes.c_uint32, ctypes.c_uint32, _u32p, _f32p, ctypes.c_uint64, _u64p],
     "hb_bin_dense": [_f32p, ctypes.c_uint64, ctypes.c_uint32, _u32p, _f32p, _u8p, _u64p, _i32p],
+    "hb_cuts_csr": [_u64p, _u32p, _f32p, ctypes.c_uint64, ctypes.c_uint32, ctypes.c_uint32, _u32p, _f32p,
+                    ctypes.c_uint64, _u64p],
+    "hb_bin_csr": [_u64p, _u32p, _f32p, ctypes.c_uint64, ctypes.c_uint32, _u32p, _f32p, _u64p, _u32p, _i32p],
 }
 
 _lib = None
@@ -373,16 +378,63 @@ def bin_dense(x, feature_offset, cut_values):
     return cols.reshape(f, n), miss.reshape(f, words), bool(dense.value)
 
 
-class BinnedMatrix:
-    """A GHistIndex-equivalent: cuts, one-byte bins and the missing bitmap."""
+def _csr_arrays(indptr, indices, values):
+    return (np.ascontiguousarray(indptr, np.uint64), np.ascontiguousarray(indices, np.uint32),
+            np.ascontiguousarray(values, np.float32))
 
-    def __init__(self, feature_offset, cut_values, columns, missing, dense):
+
+def cuts_csr(indptr, indices, values, n_cols, max_bin=256):
+    """HistCuts::from_dmatrix of a CSR matrix (absent entries missing)."""
+    ip, ix, vs = _csr_arrays(indptr, indices, values)
+    cap = n_cols * (max_bin + 1)
+    off = np.zeros(n_cols + 1, np.uint32)
+    vals = np.zeros(cap, np.float32)
+    total = ctypes.c_uint64()
+    _check(lib().hb_cuts_csr(_ptr(ip, ctypes.c_uint64), _ptr(ix, ctypes.c_uint32), _ptr(vs, ctypes.c_float),
+                             ip.size - 1, n_cols, max_bin, _ptr(off, ctypes.c_uint32), _ptr(vals, ctypes.c_float),
+                             cap, ctypes.byref(total)), "hb_cuts_csr")
+    return off, vals[: total.value].copy()
+
+
+def bin_csr(indptr, indices, values, n_cols, feature_offset, cut_values):
+    """The CSR index: row offsets and each entry's global bin (ascending in a row)."""
+    ip, ix, vs = _csr_arrays(indptr, indices, values)
+    n = ip.size - 1
+    row_ptr = np.zeros(n + 1, np.uint64)
+    row_bins = np.zeros(max(int(ip[-1]), 1), np.uint32)
+    dense = ctypes.c_int32()
+    off = np.ascontiguousarray(feature_offset, np.uint32)
+    cuts = np.ascontiguousarray(cut_values, np.float32)
+    _check(lib().hb_bin_csr(_ptr(ip, ctypes.c_uint64), _ptr(ix, ctypes.c_uint32), _ptr(vs, ctypes.c_float), n,
+                            n_cols, _ptr(off, ctypes.c_uint32), _ptr(cuts, ctypes.c_float),
+                            _ptr(row_ptr, ctypes.c_uint64), _ptr(row_bins, ctypes.c_uint32), ctypes.byref(dense)),
+           "hb_bin_csr")
+    return row_ptr, row_bins[: int(ip[-1])], bool(dense.value)
+
+
+class BinnedMatrix:
+    """A GHistIndex-equivalent: cuts plus either one-byte feature-major bins
+    and the missing bitmap, or (``from_csr``) the CSR rows of global bins."""
+
+    def __init__(self, feature_offset, cut_values, columns, missing, dense, row_ptr=None, row_bins=None):
         self.feature_offset = np.ascontiguousarray(feature_offset, np.uint32)
         self.cut_values = np.ascontiguousarray(cut_values, np.float32)
+        self.dense = bool(dense)
+        if columns is None:
+            self.columns = self.missing = None
+            self.row_ptr = np.ascontiguousarray(row_ptr, np.uint64)
+            self.row_bins = np.ascontiguousarray(row_bins, np.uint32)
+            self.n_cols = self.feature_offset.size - 1
+            self.n_rows = self.row_ptr.size - 1
+            return
+        self.row_ptr = self.row_bins = None
         self.columns = np.ascontiguousarray(columns, np.uint8)
         self.missing = None if dense else np.ascontiguousarray(missing, np.uint64)
-        self.dense = bool(dense)
         self.n_cols, self.n_rows = self.columns.shape
+
+    @property
+    def is_csr(self):
+        return self.columns is None
 
     @classmethod
     def from_dense(cls, x, max_bin=256, cuts=None):
@@ -390,8 +442,20 @@ class BinnedMatrix:
         cols, miss, dense = bin_dense(x, off, vals)
         return cls(off, vals, cols, miss, dense)
 
+    @classmethod
+    def from_csr(cls, indptr, indices, values, n_cols, max_bin=256, cuts=None):
+        """DMatrix::from_csr + GHistIndex: absent entries are missing."""
+        off, vals = cuts if cuts is not None else cuts_csr(indptr, indices, values, n_cols, max_bin)
+        row_ptr, row_bins, dense = bin_csr(indptr, indices, values, n_cols, off, vals)
+        return cls(off, vals, None, None, dense, row_ptr, row_bins)
+
     def shard(self, begin, end):
         """Rows [begin, end) as their own matrix (the cut table is shared)."""
+        if self.is_csr:
+            a, b = int(self.row_ptr[begin]), int(self.row_ptr[end])
+            ptr = self.row_ptr[begin : end + 1] - np.uint64(a)
+            full = bool(np.all(np.diff(ptr) == self.n_cols))
+            return BinnedMatrix(self.feature_offset, self.cut_values, None, None, full, ptr, self.row_bins[a:b])
         cols = self.columns[:, begin:end]
         n = end - begin
         miss = None
@@ -416,6 +480,12 @@ class BinnedMatrix:
         g.dense = 1 if self.dense else 0
         g.feature_offset = _ptr(self.feature_offset, ctypes.c_uint32)
         g.cut_values = _ptr(self.cut_values, ctypes.c_float)
+        if self.is_csr:
+            g.columns = None
+            g.missing = None
+            g.row_ptr = _ptr(self.row_ptr, ctypes.c_uint64)
+            g.row_bins = _ptr(self.row_bins, ctypes.c_uint32) if self.row_bins.size else None
+            return g
         g.columns = _ptr(self.columns, ctypes.c_uint8)
         g.missing = None if self.missing is None else _ptr(self.missing, ctypes.c_uint64)
         return g

@@ -31,11 +31,31 @@ def needs_build():
     return any(os.path.getmtime(d) > t for d in deps)
 
 
+def nccl_runpath():
+    """The NCCL that PyTorch ships (the nvidia-nccl wheel), searched first at
+    run time so that this library and torch share one libnccl.so.2; None
+    when the wheel is absent (the system NCCL is used)."""
+    try:
+        import importlib.util
+
+        spec = importlib.util.find_spec("nvidia.nccl")
+    except (ImportError, ValueError):
+        return None
+    for root in list(getattr(spec, "submodule_search_locations", None) or []):
+        d = os.path.join(root, "lib")
+        if os.path.exists(os.path.join(d, "libnccl.so.2")):
+            return d
+    return None
+
+
 def build(force=False, verbose=False):
     if not force and not needs_build():
         return LIB
     os.makedirs(OUT_DIR, exist_ok=True)
     cmd = [NVCC, *FLAGS, "-o", LIB, *[os.path.join(CSRC, s) for s in SOURCES], "-lnccl"]
+    rp = nccl_runpath()
+    if rp:
+        cmd += ["-Xlinker", "-rpath=" + rp]
     if verbose:
         print(" ".join(cmd))
     subprocess.run(cmd, check=True)

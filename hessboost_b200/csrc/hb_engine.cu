@@ -19,6 +19,10 @@
 
 using namespace hb;
 
+// The C ABI's struct layouts (the Python bindings check the same sizes).
+static_assert(sizeof(hb_ghist) == 64, "hb_ghist layout");
+static_assert(sizeof(hb_tree_node) == 40, "hb_tree_node layout");
+
 namespace {
 
 template <class T>
@@ -61,6 +65,8 @@ struct hb_engine {
   std::vector<float> h_cuts;
   DevBuf<uint8_t> rec, col;
   DevBuf<uint64_t> colmiss;
+  DevBuf<uint64_t> csr_ptr;  // CSR index: row offsets and global bins
+  DevBuf<uint32_t> csr_bins;
   bool has_missing = false;
   DevBuf<uint32_t> fo;
   DevBuf<float> cuts;
@@ -288,7 +294,10 @@ uint64_t vector_rows(hb_engine* e) {
 hb_status flush_pending(hb_engine* e) {
   if (!e->pending_tree) return HB_OK;
   mark_begin(e, T_OTHER);
-  if (e->n_out > 1)
+  if (e->c.csr)
+    launch_walk_csr(e->c, e->n_out, e->wtree.p, (uint32_t)e->wstride, e->margin.p, e->flags.p, e->n_sm,
+                    e->stream);
+  else if (e->n_out > 1)
     launch_walk_classes(e->n_out, e->wtree.p, (uint32_t)e->wstride, e->rec.p, e->c.stride,
                         e->c.mask_off, e->c.n_rows, e->margin.p, e->flags.p, e->n_sm, e->stream);
   else
@@ -312,10 +321,16 @@ hb_status run_gradients(hb_engine* e, int kind, float spw, float min_hess, int w
     walk_ls = e->walk_ls;
     walk_nodes = e->walk_nodes;
   }
+  const bool csr = e->c.csr != 0;
+  if (csr) {  // the pending tree's walk over CSR rows first
+    launch_walk_csr(e->c, 1, e->wtree.p, (uint32_t)e->wstride, e->margin.p, e->flags.p, e->n_sm,
+                    e->stream);
+    e->kernel_launches += 1;
+  }
   launch_gradients(kind, e->margin.p, e->label.p, e->weight_key ? e->weight.p : nullptr, spw,
                    min_hess, e->c.n_rows, vector_rows(e), e->gpair.p, e->scale.p,
-                   e->wtree.p, e->ls.p + walk_ls, walk_nodes, e->rec.p, e->c.stride, e->c.mask_off,
-                   e->flags.p, e->n_sm, e->stream);
+                   csr ? nullptr : e->wtree.p, e->ls.p + walk_ls, walk_nodes, e->rec.p, e->c.stride,
+                   e->c.mask_off, e->flags.p, e->n_sm, e->stream);
   mark_end(e);
   e->pending_tree = false;
   e->kernel_launches += 2;  // gradients (+ last tree's leaves) + scale
@@ -672,6 +687,8 @@ hb_status hb_engine_destroy(hb_engine* e) {
   e->rec.release();
   e->col.release();
   e->colmiss.release();
+  e->csr_ptr.release();
+  e->csr_bins.release();
   e->fo.release();
   e->cuts.release();
   e->gpair.release();
@@ -717,13 +734,54 @@ const char* hb_engine_last_error(const hb_engine* e) {
   return e ? e->err.c_str() : g_last_error.c_str();
 }
 
+// Engine state after a new index: nothing staged, no cached round graph.
+static hb_status finish_upload(hb_engine* e) {
+  e->uploaded = true;
+  e->alloc_depth = -1;
+  e->lg_alloc = 0;
+  if (e->round_exec) cudaGraphExecDestroy(e->round_exec);
+  e->round_exec = nullptr;
+  e->label_key = e->weight_key = nullptr;
+  e->margins_loaded = false;
+  e->staged = false;
+  return HB_OK;
+}
+
+// The CSR half of the upload (ghist.rs:6-21 `rows`): offsets and global
+// bins as they are; no record or column copy.
+static hb_status upload_csr(hb_engine* e, const hb_ghist* g) {
+  DevConst& c = e->c;
+  const uint64_t n = c.n_rows;
+  if (g->row_ptr[0] != 0) return HB_INVALID_ARGUMENT;
+  const uint64_t nnz = g->row_ptr[n];
+  if (nnz && !g->row_bins) return HB_INVALID_ARGUMENT;
+  for (uint64_t r = 0; r < n; ++r)
+    if (g->row_ptr[r + 1] < g->row_ptr[r]) return HB_INVALID_ARGUMENT;
+  for (uint64_t j = 0; j < nnz; ++j)
+    if (g->row_bins[j] >= c.total_bins) return refuse(e, "row_bins: a bin beyond the cuts");
+  HB_CK(e, e->csr_ptr.alloc(n + 1));
+  HB_CK(e, e->csr_bins.alloc(std::max<uint64_t>(nnz, 1)));
+  cudaStream_t s = e->stream;
+  HB_CK(e, cudaMemcpyAsync(e->csr_ptr.p, g->row_ptr, 8 * (n + 1), cudaMemcpyHostToDevice, s));
+  if (nnz) HB_CK(e, cudaMemcpyAsync(e->csr_bins.p, g->row_bins, 4 * nnz, cudaMemcpyHostToDevice, s));
+  c.csr = 1;
+  c.csr_ptr = e->csr_ptr.p;
+  c.csr_bins = e->csr_bins.p;
+  e->has_missing = !g->dense;
+  e->col.release();
+  e->rec.release();
+  e->colmiss.release();
+  return HB_OK;
+}
+
 hb_status hb_engine_upload(hb_engine* e, const hb_ghist* g) {
   HB_ENTER(e);
-  if (!g || !g->feature_offset || !g->cut_values || !g->columns || g->n_rows == 0 ||
+  const bool csr = g && !g->columns && g->row_ptr;
+  if (!g || !g->feature_offset || !g->cut_values || (!g->columns && !csr) || g->n_rows == 0 ||
       g->n_cols == 0)
     return HB_INVALID_ARGUMENT;
   if (g->n_rows >= (1ull << 32)) return refuse(e, "at most 2^32 - 1 rows per device");
-  if (g->n_cols > 224) return refuse(e, "at most 224 features per device index");
+  if (!csr && g->n_cols > 224) return refuse(e, "at most 224 features per device index");
   DevConst& c = e->c;
   const uint64_t shard_rows = c.global_rows;
   c = DevConst{};
@@ -750,6 +808,21 @@ hb_status hb_engine_upload(hb_engine* e, const hb_ghist* g) {
   const uint64_t n = c.n_rows, words = (n + 63) / 64;
   HB_CK(e, e->fo.alloc(c.n_cols + 1));
   HB_CK(e, e->cuts.alloc(c.total_bins));
+  c.fo = e->fo.p;
+  if (csr) {
+    HB_CK(e, e->gpair.alloc(n));
+    HB_CK(e, e->margin.alloc(n));
+    HB_CK(e, e->label.alloc(n));
+    HB_CK(e, e->rows[0].alloc(n));
+    HB_CK(e, e->rows[1].alloc(n));
+    cudaStream_t s = e->stream;
+    HB_CK(e, cudaMemcpyAsync(e->fo.p, e->h_fo.data(), 4 * (c.n_cols + 1), cudaMemcpyHostToDevice, s));
+    HB_CK(e, cudaMemcpyAsync(e->cuts.p, e->h_cuts.data(), 4 * c.total_bins, cudaMemcpyHostToDevice, s));
+    hb_status st = upload_csr(e, g);
+    if (st != HB_OK) return st;
+    HB_CK(e, cudaStreamSynchronize(s));
+    return finish_upload(e);
+  }
   HB_CK(e, e->col.alloc((size_t)c.n_cols * n));
   HB_CK(e, e->rec.alloc((size_t)c.stride * n + 64));
   if (e->has_missing) HB_CK(e, e->colmiss.alloc((size_t)c.n_cols * words));
@@ -770,14 +843,9 @@ hb_status hb_engine_upload(hb_engine* e, const hb_ghist* g) {
                 c.mask_off, e->rec.p, s);
   HB_CK(e, cudaGetLastError());
   HB_CK(e, cudaStreamSynchronize(s));
-  e->uploaded = true;
-  e->alloc_depth = -1;
-  if (e->round_exec) cudaGraphExecDestroy(e->round_exec);
-  e->round_exec = nullptr;
-  e->label_key = e->weight_key = nullptr;
-  e->margins_loaded = false;
-  e->staged = false;
-  return HB_OK;
+  e->csr_ptr.release();
+  e->csr_bins.release();
+  return finish_upload(e);
 }
 
 // ---- HistogramBackend ------------------------------------------------------
@@ -1323,9 +1391,13 @@ static hb_status round_work(hb_engine* e, const hb_train_params* p) {
     cudaStream_t s = e->stream;
     HB_CK(e, cudaMemsetAsync(e->scale.p, 0, sizeof(Scale) * e->n_out, s));
     mark_begin(e, T_GRAD);
+    if (e->c.csr) {  // the pending trees' walks over CSR rows first
+      launch_walk_csr(e->c, e->n_out, e->wtree.p, (uint32_t)e->wstride, e->margin.p, e->flags.p, e->n_sm, s);
+      e->kernel_launches += 1;
+    }
     launch_softmax_gradients(e->n_out, e->margin.p, e->label.p, e->c.n_rows, 1e-16f, e->gpair.p,
                              e->scale.p, e->wtree.p, (uint32_t)e->wstride, e->rec.p, e->c.stride,
-                             e->c.mask_off, e->flags.p, e->n_sm, s);
+                             e->c.mask_off, e->c.csr ? nullptr : e->flags.p, e->n_sm, s);
     mark_end(e);
     HB_CK(e, cudaGetLastError());
     e->pending_tree = false;
@@ -1403,7 +1475,7 @@ static hb_status graph_rounds(hb_engine* e, const hb_train_params* p, int rounds
                         e->item_off.p, e->entries.p, e->pairs.p, e->ls.p, e->tree.p,
                         e->wtree.p, e->forest.p, e->counts.p, e->tree_counter.p,
                         e->row_stats.p, e->flags.p, e->lg_heap.p, e->lg_state.p,
-                        e->lg_depth.p};
+                        e->lg_depth.p, e->csr_ptr.p, e->csr_bins.p};
   const int weighted = e->weight_key ? 1 : 0;
   std::vector<unsigned char> key(sizeof(hb_train_params) + sizeof(ptrs) + sizeof(int) * 2);
   std::memcpy(key.data(), p, sizeof(hb_train_params));

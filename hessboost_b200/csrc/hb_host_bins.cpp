@@ -322,4 +322,110 @@ hb_status hb_bin_dense(const float* x, uint64_t n_rows, uint32_t n_cols,
   return HB_OK;
 }
 
+// DMatrix::from_csr's checks (src/data/dmatrix.rs:459): offsets start at 0
+// and ascend to nnz, columns in range, values finite, no column twice in a
+// row. `seen` is scratch of n_cols words.
+static bool csr_row_ok(const uint64_t* indptr, const uint32_t* indices, const float* values,
+                       uint64_t r, uint32_t n_cols, std::vector<uint64_t>& seen, uint64_t stamp) {
+  for (uint64_t j = indptr[r]; j < indptr[r + 1]; ++j) {
+    const uint32_t c = indices[j];
+    if (c >= n_cols || !std::isfinite(values[j]) || seen[c] == stamp) return false;
+    seen[c] = stamp;
+  }
+  return true;
+}
+
+static hb_status check_csr(const uint64_t* indptr, const uint32_t* indices, const float* values,
+                           uint64_t n_rows, uint32_t n_cols) {
+  if (!indptr || n_rows == 0 || n_cols == 0 || indptr[0] != 0) return HB_INVALID_ARGUMENT;
+  for (uint64_t r = 0; r < n_rows; ++r)
+    if (indptr[r + 1] < indptr[r]) return HB_INVALID_ARGUMENT;
+  if (indptr[n_rows] && (!indices || !values)) return HB_INVALID_ARGUMENT;
+  std::atomic<int> bad{0};
+  const uint32_t blocks = (uint32_t)std::min<uint64_t>((n_rows + 65535) / 65536, 1u << 30);
+  parallel_for(blocks, [&](uint32_t b) {
+    std::vector<uint64_t> seen(n_cols, 0);
+    const uint64_t r0 = (uint64_t)b * 65536, r1 = std::min<uint64_t>(n_rows, r0 + 65536);
+    for (uint64_t r = r0; r < r1 && !bad.load(std::memory_order_relaxed); ++r)
+      if (!csr_row_ok(indptr, indices, values, r, n_cols, seen, r + 1)) bad.store(1);
+  });
+  return bad.load() ? HB_INVALID_ARGUMENT : HB_OK;
+}
+
+// HistCuts::from_dmatrix of a CSR matrix (quantile.rs:199, the sparse
+// branch): each feature's stored entries in row order through its sketch.
+hb_status hb_cuts_csr(const uint64_t* indptr, const uint32_t* indices, const float* values,
+                      uint64_t n_rows, uint32_t n_cols, uint32_t max_bin, uint32_t* feature_offset,
+                      float* cut_values, uint64_t cap, uint64_t* total) {
+  if (!feature_offset || !cut_values || !total || max_bin == 0) return HB_INVALID_ARGUMENT;
+  hb_status st = check_csr(indptr, indices, values, n_rows, n_cols);
+  if (st != HB_OK) return st;
+  // the CSC view: every column's values in row order (a counting sort)
+  const uint64_t nnz = indptr[n_rows];
+  std::vector<uint64_t> start(n_cols + 1, 0);
+  for (uint64_t j = 0; j < nnz; ++j) ++start[indices[j] + 1];
+  for (uint32_t c = 0; c < n_cols; ++c) start[c + 1] += start[c];
+  std::vector<float> csc(nnz);
+  {
+    std::vector<uint64_t> at(start.begin(), start.end() - 1);
+    for (uint64_t r = 0; r < n_rows; ++r)
+      for (uint64_t j = indptr[r]; j < indptr[r + 1]; ++j) csc[at[indices[j]]++] = values[j];
+  }
+  std::vector<std::vector<float>> per(n_cols);
+  parallel_for(n_cols, [&](uint32_t f) {
+    FeatureSketch sk(start[f + 1] - start[f], max_bin);
+    for (uint64_t j = start[f]; j < start[f + 1]; ++j) sk.add(csc[j]);
+    sk.cuts(per[f]);
+  });
+  uint64_t at = 0;
+  feature_offset[0] = 0;
+  for (uint32_t f = 0; f < n_cols; ++f) {
+    if (at + per[f].size() > cap) return HB_REFUSED;
+    std::copy(per[f].begin(), per[f].end(), cut_values + at);
+    at += per[f].size();
+    feature_offset[f + 1] = (uint32_t)at;
+  }
+  *total = at;
+  return HB_OK;
+}
+
+// GHistIndex::from_dmatrix for CSR (ghist.rs:213): every stored entry's
+// global bin, a row's bins ascending (feature order), row_ptr as indptr.
+// `dense` = every row holds every feature.
+hb_status hb_bin_csr(const uint64_t* indptr, const uint32_t* indices, const float* values,
+                     uint64_t n_rows, uint32_t n_cols, const uint32_t* feature_offset,
+                     const float* cut_values, uint64_t* row_ptr, uint32_t* row_bins,
+                     int32_t* dense) {
+  if (!feature_offset || !cut_values || !row_ptr || !dense) return HB_INVALID_ARGUMENT;
+  hb_status st = check_csr(indptr, indices, values, n_rows, n_cols);
+  if (st != HB_OK) return st;
+  const uint64_t nnz = indptr[n_rows];
+  if (nnz && !row_bins) return HB_INVALID_ARGUMENT;
+  for (uint32_t f = 0; f < n_cols; ++f)
+    if (feature_offset[f + 1] <= feature_offset[f] || feature_offset[f + 1] - feature_offset[f] > 256)
+      return HB_REFUSED;
+  std::copy(indptr, indptr + n_rows + 1, row_ptr);
+  std::atomic<int> short_row{0};
+  const uint32_t blocks = (uint32_t)((n_rows + 65535) / 65536);
+  parallel_for(blocks, [&](uint32_t b) {
+    const uint64_t r0 = (uint64_t)b * 65536, r1 = std::min<uint64_t>(n_rows, r0 + 65536);
+    bool any_short = false;
+    for (uint64_t r = r0; r < r1; ++r) {
+      const uint64_t a = indptr[r], e = indptr[r + 1];
+      any_short |= (e - a) != n_cols;
+      for (uint64_t j = a; j < e; ++j) {
+        const uint32_t f = indices[j];
+        const float* c = cut_values + feature_offset[f];
+        const uint32_t nb = feature_offset[f + 1] - feature_offset[f];
+        const uint32_t k = (uint32_t)(std::upper_bound(c, c + nb, values[j]) - c);
+        row_bins[j] = feature_offset[f] + std::min(k, nb - 1);
+      }
+      std::sort(row_bins + a, row_bins + e);
+    }
+    if (any_short) short_row.store(1);
+  });
+  *dense = short_row.load() ? 0 : 1;
+  return HB_OK;
+}
+
 }  // extern "C"

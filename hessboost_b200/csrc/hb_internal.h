@@ -53,6 +53,12 @@ struct DevConst {
   uint32_t dense;         // index-level: no missing cell anywhere
   uint32_t n_groups;      // feature groups of kGroupFeatures
   uint32_t hist64;        // 1: always the 64-bit-atomic histogram kernel
+  // CSR index (csr = 1): each row's global bins ascending, absent = missing;
+  // fo = the device copy of feature_offset (both layouts)
+  uint32_t csr;
+  const uint64_t* csr_ptr;
+  const uint32_t* csr_bins;
+  const uint32_t* fo;
   // training parameters (RegParams rounded to f32 then widened)
   double lambda, alpha, gamma, mcw, mds;
   float eta;

@@ -145,6 +145,57 @@ __device__ __forceinline__ void stage_tree(const WNode* __restrict__ wtree, cons
   __syncthreads();
 }
 
+// The local bin of feature [lo, hi) (global bins) in a CSR row, whose bins
+// ascend: the first entry >= lo, present when it is below hi.
+__device__ __forceinline__ bool csr_find(const uint32_t* __restrict__ bins, uint64_t a, uint64_t b,
+                                         uint32_t lo, uint32_t hi, uint32_t& local) {
+  uint64_t e = b;
+  while (a < e) {
+    const uint64_t m = (a + e) >> 1;
+    if (__ldg(bins + m) < lo) a = m + 1; else e = m;
+  }
+  if (a < b) {
+    const uint32_t v = __ldg(bins + a);
+    if (v < hi) {
+      local = v - lo;
+      return true;
+    }
+  }
+  return false;
+}
+
+// The leaf a CSR row reaches in one tree (the partition's routing rule:
+// local bin < limit goes left, missing follows default_left).
+__device__ __forceinline__ float walk_leaf_csr(const WNode* __restrict__ t, const DevConst& c,
+                                               uint64_t a, uint64_t b) {
+  WNode nd = t[0];
+  while (nd.left >= 0) {
+    const uint32_t f = nd.feature & 0x7fffffffu;
+    uint32_t bin = 0;
+    const bool present = csr_find(c.csr_bins, a, b, __ldg(c.fo + f), __ldg(c.fo + f + 1), bin);
+    const bool left = present ? bin < nd.limit : (nd.feature >> 31) != 0u;
+    nd = t[nd.left + (left ? 0 : 1)];
+  }
+  return nd.leaf;
+}
+
+// The pending trees' leaves (K outputs, trees wstride nodes apart, margins
+// class-major) added to the margins of CSR rows, when the flag says a tree
+// waits.
+__global__ void k_walk_csr(DevConst c, int K, const WNode* __restrict__ wtree, uint32_t wstride,
+                           float* __restrict__ margin, const int* __restrict__ pending) {
+  if (!*pending) return;
+  const uint64_t n = c.n_rows;
+  for (uint64_t i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n;
+       i += (uint64_t)gridDim.x * blockDim.x) {
+    const uint64_t a = c.csr_ptr[i], b = c.csr_ptr[i + 1];
+    for (int k = 0; k < K; ++k) {
+      float* m = margin + (uint64_t)k * n + i;
+      *m = __fadd_rn(*m, walk_leaf_csr(wtree + (uint64_t)k * wstride, c, a, b));
+    }
+  }
+}
+
 // Add the previous tree's leaves to the margins: each row walks the tree
 // over its binned record (the partition's routing rule), in row order.
 __global__ void k_walk(const WNode* __restrict__ wtree, const LevelState* __restrict__ ls_last,
@@ -348,6 +399,79 @@ __global__ void k_encode(const uint8_t* __restrict__ col, const uint64_t* __rest
       out[(mask_off >> 2) + w] = m;
     }
     for (uint32_t b = mask_off + 4 * n_mask; b < stride; b += 4) out[b >> 2] = 0;
+  }
+}
+
+// ---------------------------------------------------------------------------
+// CSR histogram (hist_sparse, src/backend/cuda/train.rs:1029): one warp per
+// row, its lanes over the row's entries, each adding the row's fixed-point
+// (g, h) to the node's histogram in global memory (L2-resident: total_bins
+// x 16 B) with 64-bit reductions. Rows are split over the CTAs as the dense
+// kernel splits them (contiguous shares of the entries' concatenation).
+constexpr int kCsrThreads = 512;
+
+__global__ void __launch_bounds__(kCsrThreads)
+    k_hist_csr(DevConst c, const float2* __restrict__ gpair, const Scale* __restrict__ scale,
+               const uint32_t* __restrict__ rows, const HEntry* __restrict__ entries,
+               const LevelState* __restrict__ ls, longlong2* __restrict__ hist,
+               long long* __restrict__ totals, unsigned long long* __restrict__ row_stats) {
+  const int n_entries = ls->n_hentries;
+  const uint64_t total = ls->hist_rows;
+  if (n_entries <= 0 || total == 0) return;
+  if (row_stats && blockIdx.x == 0 && threadIdx.x == 0)
+    atomicAdd(&row_stats[entries[0].identity ? 0 : 1], (unsigned long long)total);
+  const uint64_t per = (total + gridDim.x - 1) / gridDim.x;
+  const uint64_t a = (uint64_t)blockIdx.x * per;
+  const uint64_t b = min(total, a + per);
+  const double fg = scale->fg, fh = scale->fh;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  constexpr int kWarps = kCsrThreads / 32;
+  long long tg = 0, th = 0;
+  if (a < b) {
+    int e = 0;
+    {
+      int hi = n_entries - 1;
+      while (e < hi) {
+        const int mid = (e + hi + 1) >> 1;
+        if (entries[mid].prefix <= a) e = mid; else hi = mid - 1;
+      }
+    }
+    uint64_t pos = a;
+    while (pos < b && e < n_entries) {
+      const HEntry en = entries[e];
+      const uint64_t end_e = min(b, en.prefix + en.len);
+      unsigned long long* dst = reinterpret_cast<unsigned long long*>(hist + (uint64_t)en.slot * c.total_bins);
+      for (uint64_t i = pos + warp; i < end_e; i += kWarps) {
+        const uint32_t at = en.begin + (uint32_t)(i - en.prefix);
+        const uint32_t row = en.identity ? at : __ldg(rows + at);
+        const uint64_t r0 = __ldg(c.csr_ptr + row), r1 = __ldg(c.csr_ptr + row + 1);
+        const float2 p = __ldg(gpair + row);
+        const long long qg = __double2ll_rn((double)p.x * fg);
+        const long long qh = __double2ll_rn((double)p.y * fh);
+        if (lane == 0) {
+          tg += qg;
+          th += qh;
+        }
+        for (uint64_t j = r0 + lane; j < r1; j += 32) {
+          const uint32_t bin = __ldg(c.csr_bins + j);
+          atomicAdd(dst + 2 * (uint64_t)bin, (unsigned long long)qg);
+          atomicAdd(dst + 2 * (uint64_t)bin + 1, (unsigned long long)qh);
+        }
+      }
+      pos = end_e;
+      ++e;
+    }
+  }
+  if (totals != nullptr) {
+    using BR = cub::BlockReduce<long long, kCsrThreads>;
+    __shared__ typename BR::TempStorage tmp;
+    const long long sgt = BR(tmp).Sum(tg);
+    __syncthreads();
+    const long long sht = BR(tmp).Sum(th);
+    if (threadIdx.x == 0 && (sgt || sht)) {
+      atomicAdd(reinterpret_cast<unsigned long long*>(&totals[0]), (unsigned long long)sgt);
+      atomicAdd(reinterpret_cast<unsigned long long*>(&totals[1]), (unsigned long long)sht);
+    }
   }
 }
 
@@ -1483,10 +1607,16 @@ __global__ void __launch_bounds__(kPartThreads)
   }
   uint32_t bin[kPerThread];
   bool miss[kPerThread];
+  const uint32_t csr_lo = c.csr ? __ldg(c.fo + d.feature) : 0u;
+  const uint32_t csr_hi = c.csr ? __ldg(c.fo + d.feature + 1) : 0u;
 #pragma unroll
   for (int j = 0; j < kPerThread; ++j) {
     const uint32_t r = row[j];
-    if (use_record) {
+    if (c.csr) {
+      uint32_t lb = 0;
+      miss[j] = !csr_find(c.csr_bins, __ldg(c.csr_ptr + r), __ldg(c.csr_ptr + r + 1), csr_lo, csr_hi, lb);
+      bin[j] = lb;
+    } else if (use_record) {
       const uint8_t* rp = rec + (uint64_t)r * c.stride;
       bin[j] = rp[d.feature];
       miss[j] = (*reinterpret_cast<const uint32_t*>(rp + mword) >> mbit) & 1u;
@@ -1791,6 +1921,12 @@ void launch_softmax_gradients(int K, float* margin, const float* label, uint64_t
                                            wstride, rec, stride, mask_off, pending);
 }
 
+void launch_walk_csr(const DevConst& c, int K, const WNode* wtree, uint32_t wstride, float* margin,
+                     const int* pending, int n_sm, cudaStream_t s) {
+  const int grid = (int)std::max<uint64_t>(1, std::min<uint64_t>((c.n_rows + 255) / 256, (uint64_t)n_sm * 8));
+  k_walk_csr<<<grid, 256, 0, s>>>(c, K, wtree, wstride, margin, pending);
+}
+
 void launch_walk_classes(int K, const WNode* wtree, uint32_t wstride, const uint8_t* rec,
                          uint32_t stride, uint32_t mask_off, uint64_t n, float* margin,
                          const int* pending, int n_sm, cudaStream_t s) {
@@ -1838,6 +1974,7 @@ static int hist_groups_per_cta(const DevConst& c) {
 }
 
 size_t hist_smem_bytes(const DevConst& c) {
+  if (c.csr) return 0;
   if (use_hist32(c)) return hist_groups_per_cta(c) == 2 ? H32<2>::smem() : H32<1>::smem();
   return (size_t)c.max_bins * 32 * 16;
 }
@@ -1848,6 +1985,11 @@ void launch_hist(const DevConst& c, const uint32_t* fo, const uint8_t* rec, cons
                  const Scale* scale, const uint32_t* rows, const HEntry* entries,
                  const LevelState* ls, longlong2* hist, long long* totals,
                  unsigned long long* row_stats, int grid_x, size_t smem, cudaStream_t s) {
+  if (c.csr) {
+    k_hist_csr<<<grid_x * (2048 / kCsrThreads), kCsrThreads, 0, s>>>(c, gpair, scale, rows, entries, ls,
+                                                                    hist, totals, row_stats);
+    return;
+  }
   // The dynamic shared memory this launch needs, granted per device (the
   // attribute is per device); the launch reports the error if it cannot be.
   static size_t granted[64] = {0};

@@ -28,6 +28,9 @@ void launch_softmax_gradients(int K, float* margin, const float* label, uint64_t
                               const uint8_t* rec, uint32_t stride, uint32_t mask_off,
                               const int* pending, int n_sm, cudaStream_t s);
 // When *pending is set, add each class's tree leaves to its margins.
+// The pending trees' leaves added to the margins of a CSR index's rows.
+void launch_walk_csr(const DevConst& c, int K, const WNode* wtree, uint32_t wstride, float* margin,
+                     const int* pending, int n_sm, cudaStream_t s);
 void launch_walk_classes(int K, const WNode* wtree, uint32_t wstride, const uint8_t* rec,
                          uint32_t stride, uint32_t mask_off, uint64_t n, float* margin,
                          const int* pending, int n_sm, cudaStream_t s);

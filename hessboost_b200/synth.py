@@ -5,6 +5,11 @@ C1: regression, rows x 28 N(0,1), y = sin x0 + x1 x2 + 0.5 x3^2 - x4 + N(0, 0.1)
 C2: binary logistic, rows x 28 N(0,1) with 5% of cells NaN (mask drawn
     after the values), y ~ Bernoulli(sigmoid(w . x~ + 0.3 x0 x1)),
     w ~ N(0,1)/sqrt(28), x~ = x with NaN -> 0.
+C4: wide sparse binary, CSR rows x F with each cell stored with
+    probability `density` (column positions uniform), values
+    lognormal(0, 1), absent cells missing; 20 random features carry
+    N(0, 1) weights and y ~ Bernoulli(sigmoid(sum of the weights of the
+    row's stored features)).
 C5: prediction, a forest of complete depth-d trees over F features with
     thresholds from N(0,1) quantiles, uniform default directions and
     N(0, 0.01) leaves; rows N(0,1) with 1% NaN.
@@ -77,4 +82,47 @@ def rows_c5(n_rows, n_cols=50, seed=1, missing=0.01):
     rng = np.random.default_rng(seed)
     x = rng.standard_normal((n_rows, n_cols), dtype=np.float32)
     x[rng.random((n_rows, n_cols), dtype=np.float32) < missing] = np.nan
+    return x
+
+
+def sparse_c4(n_rows=5_000_000, n_cols=2000, density=0.02, seed=0, n_weighted=20):
+    """C4 as CSR arrays: (indptr u64, indices u32 ascending within a row,
+    values f32, y f32). Each cell of the row-major n_rows x n_cols grid is
+    stored independently with probability `density`: the gaps between
+    stored cells are geometric."""
+    rng = np.random.default_rng(seed)
+    k = min(n_weighted, n_cols)
+    w = np.zeros(n_cols, np.float64)
+    w[rng.choice(n_cols, size=k, replace=False)] = rng.standard_normal(k)
+    cells = n_rows * n_cols
+    parts = []
+    at = -1
+    step = 1 << 24
+    while True:
+        pos = at + np.cumsum(rng.geometric(density, size=step).astype(np.int64))
+        keep = pos[pos < cells]
+        parts.append(keep)
+        if keep.size < pos.size:
+            break
+        at = int(pos[-1])
+    pos = np.concatenate(parts)
+    del parts
+    rows = pos // n_cols
+    indices = (pos - rows * n_cols).astype(np.uint32)
+    del pos
+    indptr = np.zeros(n_rows + 1, np.uint64)
+    np.cumsum(np.bincount(rows, minlength=n_rows), out=indptr[1:])
+    logits = np.bincount(rows, weights=w[indices], minlength=n_rows)
+    del rows
+    values = rng.lognormal(0.0, 1.0, size=indices.size).astype(np.float32)
+    y = (rng.random(n_rows) < 1.0 / (1.0 + np.exp(-logits))).astype(np.float32)
+    return indptr, indices, values, y
+
+
+def csr_to_dense(indptr, indices, values, n_cols):
+    """The dense f32 matrix of CSR arrays, absent cells NaN."""
+    n = len(indptr) - 1
+    x = np.full((n, n_cols), np.nan, np.float32)
+    rows = np.repeat(np.arange(n), np.diff(np.asarray(indptr, np.int64)))
+    x[rows, np.asarray(indices, np.int64)] = values
     return x

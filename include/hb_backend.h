@@ -14,7 +14,7 @@
  * plus entry points the reference does not have: whole-tree growth on the
  * device (`hb_grow_tree`, `hb_train`), the row-sharded communicator
  * (`hb_comm_*`) and the host binning helpers (`hb_cuts_dense`,
- * `hb_bin_dense`).
+ * `hb_bin_dense`, `hb_cuts_csr`, `hb_bin_csr`).
  *
  * Conventions (the reference's, src/tree/hist/mod.rs:107-212):
  *   - every call returns an hb_status; HB_REFUSED means "did not run"
@@ -141,17 +141,24 @@ typedef struct hb_device_loss {
   int32_t reserved;
 } hb_device_loss;
 
-/* The binned matrix the backend uploads (GHistIndex, src/data/ghist.rs:195):
- * every feature's local bins, feature-major, one byte each (features of at
- * most 256 bins), and the missing bitmap of an index with missing entries. */
+/* The binned matrix the backend uploads (GHistIndex, src/data/ghist.rs:195),
+ * in one of two layouts (features of at most 256 bins either way):
+ *   columns: every feature's local bins, feature-major, one byte each, and
+ *            the missing bitmap of an index with missing entries (at most
+ *            224 features);
+ *   CSR:     `columns` NULL; the stored entries' global bins row by row
+ *            (ghist.rs:6-21 `rows`), ascending within a row, offsets in
+ *            `row_ptr`; an absent feature is missing. */
 typedef struct hb_ghist {
   uint64_t n_rows;
   uint32_t n_cols;
   uint32_t dense;                 /* every row holds every feature */
   const uint32_t* feature_offset; /* n_cols + 1 */
   const float* cut_values;        /* feature_offset[n_cols] */
-  const uint8_t* columns;         /* bins[f * n_rows + r] */
+  const uint8_t* columns;         /* bins[f * n_rows + r], or NULL for CSR */
   const uint64_t* missing;        /* NULL, or bit r%64 of word f*ceil(n_rows/64) + r/64 */
+  const uint64_t* row_ptr;        /* CSR: n_rows + 1 offsets from 0 */
+  const uint32_t* row_bins;       /* CSR: row_ptr[n_rows] global bins */
 } hb_ghist;
 
 /* One tree node: the reference's Node (src/tree/regtree.rs:37) plus the
@@ -347,6 +354,21 @@ hb_status hb_cuts_dense(const float* x, uint64_t n_rows, uint32_t n_cols, uint32
 hb_status hb_bin_dense(const float* x, uint64_t n_rows, uint32_t n_cols,
                        const uint32_t* feature_offset, const float* cut_values,
                        uint8_t* columns, uint64_t* missing, int32_t* dense);
+
+/* Cuts of a CSR matrix (DMatrix::from_csr, src/data/dmatrix.rs:459: absent
+ * entries missing; stored values finite, columns in range, none twice in a
+ * row, else HB_INVALID_ARGUMENT), each feature's entries in row order
+ * (quantile.rs:199). */
+hb_status hb_cuts_csr(const uint64_t* indptr, const uint32_t* indices, const float* values,
+                      uint64_t n_rows, uint32_t n_cols, uint32_t max_bin, uint32_t* feature_offset,
+                      float* cut_values, uint64_t cap, uint64_t* total);
+/* The CSR index: row_ptr (n_rows + 1, = indptr) and every entry's global
+ * bin, ascending within its row. HB_REFUSED when a feature has more than
+ * 256 bins. */
+hb_status hb_bin_csr(const uint64_t* indptr, const uint32_t* indices, const float* values,
+                     uint64_t n_rows, uint32_t n_cols, const uint32_t* feature_offset,
+                     const float* cut_values, uint64_t* row_ptr, uint32_t* row_bins,
+                     int32_t* dense);
 
 #ifdef __cplusplus
 }

@@ -34,7 +34,7 @@ def test_library_loads_and_exports_every_declared_symbol():
 def test_header_structs_match_bindings():
     assert ctypes.sizeof(H.TreeNode) == 40
     assert ctypes.sizeof(H.Segment) == 32
-    assert ctypes.sizeof(H.GHist) == 48
+    assert ctypes.sizeof(H.GHist) == 64
     assert ctypes.sizeof(H.NodeScan) == 40
 
 
