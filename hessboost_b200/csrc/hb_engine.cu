@@ -1447,7 +1447,9 @@ static hb_status graph_rounds(hb_engine* e, const hb_train_params* p, int rounds
   };
   if (e->timing) {
     // enough events for every mark of every round, created before capture
-    const size_t need = e->ev_used + (size_t)rounds * 64 * std::max(e->n_out, 1) + 64;
+    // (two events a mark; a lossguide tree marks four families a step)
+    const size_t per_tree = p->grow_policy == HB_GROW_LOSSGUIDE ? 8 * (size_t)lg_leaves(p) + 32 : 64;
+    const size_t need = e->ev_used + (size_t)rounds * per_tree * std::max(e->n_out, 1) + 64;
     while (e->ev.size() < need) {
       cudaEvent_t x;
       HB_CK(e, cudaEventCreate(&x));

@@ -11,6 +11,7 @@
 //     int64 multiple of a power of two and summed exactly; this is the
 //     arithmetic the CUDA path uses, so the two must agree bit for bit.
 #include <algorithm>
+#include <functional>
 #include <cfloat>
 #include <cmath>
 #include <cstring>
@@ -42,14 +43,55 @@ inline bool is_missing(float v) { return std::isnan(v); }
 // Binned index (src/data/ghist.rs:195 `GHistIndex`): feature-local bins per
 // cell, the missing flag, and the index-level `dense` flag (every row holds
 // every feature, ghist.rs:205-208).
+// A CSR index (ghist.rs:6-21 `rows`: global bins row by row, no columns)
+// keeps only the stored cells: row_bins ascending within a row.
 struct Index {
   size_t n_rows = 0, n_cols = 0;
   Cuts cuts;
   std::vector<uint16_t> local;   // [row][feature] local bin
   std::vector<uint8_t> missing;  // [row][feature]
   bool dense = true;
+  bool csr = false;
+  std::vector<uint64_t> row_ptr;   // CSR: n_rows + 1
+  std::vector<uint32_t> row_bins;  // CSR: global bins
   uint32_t global(size_t r, size_t f) const { return cuts.feature_offset[f] + local[r * n_cols + f]; }
+  // The cell's local bin, or false when it is missing.
+  bool cell(size_t r, size_t f, uint32_t& bin) const {
+    if (!csr) {
+      if (missing[r * n_cols + f]) return false;
+      bin = local[r * n_cols + f];
+      return true;
+    }
+    const uint32_t lo = cuts.feature_offset[f], hi = cuts.feature_offset[f + 1];
+    const uint32_t* b = row_bins.data() + row_ptr[r];
+    const uint32_t* e = row_bins.data() + row_ptr[r + 1];
+    const uint32_t* it = std::lower_bound(b, e, lo);
+    if (it == e || *it >= hi) return false;
+    bin = *it - lo;
+    return true;
+  }
 };
+
+// GHistIndex::from_dmatrix of CSR input: each stored value's global bin.
+Index make_index_csr(const uint64_t* indptr, const uint32_t* indices, const float* values,
+                     size_t n, size_t nc, Cuts cuts) {
+  Index ix;
+  ix.n_rows = n;
+  ix.n_cols = nc;
+  ix.cuts = std::move(cuts);
+  ix.csr = true;
+  ix.row_ptr.assign(indptr, indptr + n + 1);
+  ix.row_bins.assign(indptr[n], 0);
+  bool full = true;
+  for (size_t r = 0; r < n; ++r) {
+    full = full && indptr[r + 1] - indptr[r] == nc;
+    for (uint64_t j = indptr[r]; j < indptr[r + 1]; ++j)
+      ix.row_bins[j] = ix.cuts.feature_offset[indices[j]] + local_bin_of(ix.cuts, indices[j], values[j]);
+    std::sort(ix.row_bins.begin() + indptr[r], ix.row_bins.begin() + indptr[r + 1]);
+  }
+  ix.dense = full;
+  return ix;
+}
 
 Index make_index(const float* x, size_t n, size_t nc, Cuts cuts) {
   Index ix;
@@ -196,6 +238,18 @@ bool is_contiguous(const std::vector<uint32_t>& rows) {  // walk.rs `contiguous_
 // chain per bin in ascending row order).
 void accumulate_f64(const Index& ix, const std::vector<uint32_t>& rows, size_t b, size_t e,
                     const GradPair* gp, GS* out) {
+  if (ix.csr) {  // the row's stored cells, rows in order
+    for (size_t i = b; i < e; ++i) {
+      uint32_t r = rows[i];
+      double g = (double)gp[r].grad, h = (double)gp[r].hess;
+      for (uint64_t j = ix.row_ptr[r]; j < ix.row_ptr[r + 1]; ++j) {
+        GS& o = out[ix.row_bins[j]];
+        o.grad += g;
+        o.hess += h;
+      }
+    }
+    return;
+  }
   for (size_t i = b; i < e; ++i) {
     uint32_t r = rows[i];
     double g = (double)gp[r].grad, h = (double)gp[r].hess;
@@ -214,6 +268,11 @@ std::vector<GS> build_hist(const Index& ix, const std::vector<uint32_t>& rows, c
   size_t nb = ix.cuts.values.size();
   std::vector<GS> out(nb);
   bool contiguous = ix.dense && is_contiguous(rows);
+  if (chain_order(ix.dense, ix.n_rows, rows.size(), contiguous) && ix.csr) {
+    // one chain per bin in row order: one pass over the rows' cells
+    accumulate_f64(ix, rows, 0, rows.size(), gp, out.data());
+    return out;
+  }
   if (chain_order(ix.dense, ix.n_rows, rows.size(), contiguous)) {
     // One chain per bin; features are independent, so sweep them in parallel.
     size_t nc = ix.n_cols;
@@ -256,6 +315,38 @@ std::vector<IS> build_hist(const Index& ix, const std::vector<uint32_t>& rows, c
                            const FixMode&) {
   size_t nb = ix.cuts.values.size(), nc = ix.n_cols;
   std::vector<IS> out(nb);
+  if (ix.csr) {
+    // stored cells only; exact sums, so any order: row blocks in parallel
+    // into private histograms, then added up
+    auto add_rows = [&](size_t b, size_t e, IS* h) {
+      for (size_t i = b; i < e; ++i) {
+        const uint32_t r = rows[i];
+        for (uint64_t j = ix.row_ptr[r]; j < ix.row_ptr[r + 1]; ++j) {
+          h[ix.row_bins[j]].grad += q[r].grad;
+          h[ix.row_bins[j]].hess += q[r].hess;
+        }
+      }
+    };
+    const size_t grain = 16384;
+    if (rows.size() <= 2 * grain) {
+      add_rows(0, rows.size(), out.data());
+      return out;
+    }
+    const size_t n_chunks = (rows.size() + grain - 1) / grain;
+#pragma omp parallel
+    {
+      std::vector<IS> mine(nb);
+#pragma omp for schedule(dynamic, 1) nowait
+      for (long long c = 0; c < (long long)n_chunks; ++c)
+        add_rows(c * grain, std::min(rows.size(), (size_t)(c + 1) * grain), mine.data());
+#pragma omp critical
+      for (size_t b = 0; b < nb; ++b) {
+        out[b].grad += mine[b].grad;
+        out[b].hess += mine[b].hess;
+      }
+    }
+    return out;
+  }
 #pragma omp parallel for schedule(dynamic, 1)
   for (long long f = 0; f < (long long)nc; ++f) {
     for (uint32_t r : rows) {
@@ -418,8 +509,8 @@ class Builder {
     uint32_t fs = ix_.cuts.feature_offset[b.feature];
     uint32_t limit = b.bin < 0 ? 0 : (uint32_t)(b.bin + 1 - (int32_t)fs);
     for (uint32_t r : e.rows) {
-      size_t cell = (size_t)r * ix_.n_cols + b.feature;
-      bool go_left = ix_.missing[cell] ? b.default_left : ix_.local[cell] < limit;
+      uint32_t bin = 0;
+      bool go_left = ix_.cell(r, b.feature, bin) ? bin < limit : b.default_left;
       (go_left ? left : right).push_back(r);
     }
   }
@@ -914,10 +1005,32 @@ int64_t run_rounds(orc_trainer* tr, int rounds, orc_node* nodes, uint64_t nodes_
 
 extern "C" {
 
+static orc_trainer* trainer_new(const orc_params* pp, uint64_t n, const float* labels,
+                                const std::function<orc::Index(const orc::Params&)>& index);
+
 orc_trainer* orc_trainer_new(const orc_params* pp, const float* x, uint64_t n, uint64_t nc,
                              const float* labels) {
   using namespace orc;
   if (!pp || !x || !labels || n == 0 || nc == 0) return nullptr;
+  return trainer_new(pp, n, labels, [&](const Params& p) {
+    return make_index(x, n, nc, cuts_from_dense(x, n, nc, nullptr, (size_t)p.max_bin, NAN));
+  });
+}
+
+orc_trainer* orc_trainer_new_csr(const orc_params* pp, const uint64_t* indptr, const uint32_t* indices,
+                                 const float* values, uint64_t n, uint64_t nc, const float* labels) {
+  using namespace orc;
+  if (!pp || !indptr || !labels || n == 0 || nc == 0 || (indptr[n] && (!indices || !values)))
+    return nullptr;
+  return trainer_new(pp, n, labels, [&](const Params& p) {
+    return make_index_csr(indptr, indices, values, n, nc,
+                          cuts_from_csr(indptr, indices, values, n, nc, (size_t)p.max_bin));
+  });
+}
+
+static orc_trainer* trainer_new(const orc_params* pp, uint64_t n, const float* labels,
+                                const std::function<orc::Index(const orc::Params&)>& index) {
+  using namespace orc;
 #ifdef _OPENMP
   if (pp->n_threads > 0) omp_set_num_threads(pp->n_threads);
 #endif
@@ -926,7 +1039,7 @@ orc_trainer* orc_trainer_new(const orc_params* pp, const float* x, uint64_t n, u
   tr->n = n;
   tr->k = tr->p.n_outputs;
   const int k = tr->k;
-  tr->ix = make_index(x, n, nc, cuts_from_dense(x, n, nc, nullptr, (size_t)tr->p.max_bin, NAN));
+  tr->ix = index(tr->p);
   tr->labels.assign(labels, labels + n * (tr->p.objective == 2 ? 1 : k));  // softmax: class ids
   tr->base.assign(k, 0.0f);
   if (std::isnan(pp->base_score)) {
@@ -960,6 +1073,31 @@ int64_t orc_train(const orc_params* pp, const float* x, uint64_t n, uint64_t nc,
   if (margins_out && got >= 0) std::copy(tr->margins.begin(), tr->margins.end(), margins_out);
   orc_trainer_free(tr);
   return got;
+}
+
+int64_t orc_train_csr(const orc_params* pp, const uint64_t* indptr, const uint32_t* indices,
+                      const float* values, uint64_t n, uint64_t nc, const float* labels, int32_t rounds,
+                      orc_node* nodes, uint64_t nodes_cap, uint64_t* tree_ptr, float* base_out,
+                      float* margins_out) {
+  if (!pp || !labels || n == 0 || nc == 0 || rounds < 0) return -2;
+  orc_trainer* tr = orc_trainer_new_csr(pp, indptr, indices, values, n, nc, labels);
+  if (!tr) return -2;
+  int64_t got = run_rounds(tr, rounds, nodes, nodes_cap, tree_ptr);
+  std::copy(tr->base.begin(), tr->base.end(), base_out);
+  if (margins_out && got >= 0) std::copy(tr->margins.begin(), tr->margins.end(), margins_out);
+  orc_trainer_free(tr);
+  return got;
+}
+
+int64_t orc_cuts_csr(const uint64_t* indptr, const uint32_t* indices, const float* values,
+                     uint64_t n_rows, uint64_t n_cols, int32_t max_bin, uint32_t* feature_offset,
+                     float* cut_values, uint64_t cap) {
+  using namespace orc;
+  Cuts c = cuts_from_csr(indptr, indices, values, n_rows, n_cols, (size_t)max_bin);
+  if (c.values.size() > cap) return -1;
+  std::copy(c.feature_offset.begin(), c.feature_offset.end(), feature_offset);
+  std::copy(c.values.begin(), c.values.end(), cut_values);
+  return (int64_t)c.values.size();
 }
 
 void orc_predict(const orc_node* nodes, const uint64_t* tree_ptr, uint64_t n_trees,

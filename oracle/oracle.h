@@ -90,6 +90,18 @@ int64_t orc_trainer_rounds(orc_trainer* t, int32_t rounds, orc_node* nodes, uint
                            uint64_t* tree_ptr);
 void orc_trainer_free(orc_trainer* t);
 
+/* The same on a CSR matrix (DMatrix::from_csr: absent cells missing),
+ * binned into a CSR index of global bins (only stored cells are read). */
+orc_trainer* orc_trainer_new_csr(const orc_params* p, const uint64_t* indptr, const uint32_t* indices,
+                                 const float* values, uint64_t n, uint64_t n_cols, const float* labels);
+int64_t orc_train_csr(const orc_params* p, const uint64_t* indptr, const uint32_t* indices,
+                      const float* values, uint64_t n, uint64_t n_cols, const float* labels, int32_t rounds,
+                      orc_node* nodes, uint64_t nodes_cap, uint64_t* tree_ptr, float* base_out,
+                      float* margins_out);
+int64_t orc_cuts_csr(const uint64_t* indptr, const uint32_t* indices, const float* values,
+                     uint64_t n_rows, uint64_t n_cols, int32_t max_bin, uint32_t* feature_offset,
+                     float* cut_values, uint64_t cap);
+
 /* Raw margins: base + sum over trees in order of weight * leaf, tree t
  * adding to output tree_output[t] (NULL: t % n_outputs) with weight
  * tree_weight[t] (NULL: 1). */

@@ -60,4 +60,10 @@ Cuts cuts_from_dense(const float* x, size_t n_rows, size_t n_cols, const float* 
 // (quantile.rs:285-302): count of cuts <= v, clamped to the last bin.
 uint32_t local_bin_of(const Cuts& cuts, size_t f, float v);
 
+// `HistCuts::from_dmatrix` for CSR input (quantile.rs:199, the sparse
+// branch): each feature's stored entries, in row order, through its sketch
+// (unit weights; every stored value is present).
+Cuts cuts_from_csr(const uint64_t* indptr, const uint32_t* indices, const float* values,
+                   size_t n_rows, size_t n_cols, size_t max_bin);
+
 }  // namespace orc

@@ -326,6 +326,35 @@ Cuts cuts_from_dense(const float* x, size_t n_rows, size_t n_cols, const float* 
   return cuts;
 }
 
+Cuts cuts_from_csr(const uint64_t* indptr, const uint32_t* indices, const float* values,
+                   size_t n_rows, size_t n_cols, size_t max_bin) {
+  // DMatrix::to_csc: every column's values in row order
+  std::vector<size_t> start(n_cols + 1, 0);
+  const size_t nnz = indptr[n_rows];
+  for (size_t j = 0; j < nnz; ++j) ++start[indices[j] + 1];
+  for (size_t c = 0; c < n_cols; ++c) start[c + 1] += start[c];
+  std::vector<float> csc(nnz);
+  {
+    std::vector<size_t> at(start.begin(), start.end() - 1);
+    for (size_t r = 0; r < n_rows; ++r)
+      for (uint64_t j = indptr[r]; j < indptr[r + 1]; ++j) csc[at[indices[j]]++] = values[j];
+  }
+  Cuts cuts;
+  cuts.feature_offset.push_back(0);
+  std::vector<std::vector<float>> per(n_cols);
+#pragma omp parallel for schedule(dynamic, 1)
+  for (long long f = 0; f < (long long)n_cols; ++f) {
+    WQSketch sketch(start[f + 1] - start[f], max_bin, true);
+    for (size_t j = start[f]; j < start[f + 1]; ++j) sketch.push(csc[j], 1.0f);
+    sketch.cut_values(per[f]);
+  }
+  for (size_t f = 0; f < n_cols; ++f) {
+    cuts.values.insert(cuts.values.end(), per[f].begin(), per[f].end());
+    cuts.feature_offset.push_back((uint32_t)cuts.values.size());
+  }
+  return cuts;
+}
+
 // quantile.rs:285 `bin_of` (numeric), made feature-local.
 uint32_t local_bin_of(const Cuts& cuts, size_t f, float v) {
   const float* begin = cuts.values.data() + cuts.feature_offset[f];

@@ -112,6 +112,14 @@ def lib():
         L.orc_trainer_rounds.argtypes = [ctypes.c_void_p, ctypes.c_int32, P(OrcNode), ctypes.c_uint64, u64p]
         L.orc_trainer_free.restype = None
         L.orc_trainer_free.argtypes = [ctypes.c_void_p]
+        L.orc_trainer_new_csr.restype = ctypes.c_void_p
+        L.orc_trainer_new_csr.argtypes = [P(OrcParams), u64p, u32p, f32p, ctypes.c_uint64, ctypes.c_uint64, f32p]
+        L.orc_train_csr.restype = ctypes.c_int64
+        L.orc_train_csr.argtypes = [P(OrcParams), u64p, u32p, f32p, ctypes.c_uint64, ctypes.c_uint64, f32p,
+                                    ctypes.c_int32, P(OrcNode), ctypes.c_uint64, u64p, f32p, f32p]
+        L.orc_cuts_csr.restype = ctypes.c_int64
+        L.orc_cuts_csr.argtypes = [u64p, u32p, f32p, ctypes.c_uint64, ctypes.c_uint64, ctypes.c_int32, u32p, f32p,
+                                   ctypes.c_uint64]
         L.orc_fixed_scale.restype = ctypes.c_int32
         L.orc_fixed_scale.argtypes = [ctypes.c_float, ctypes.c_uint64]
         _lib = L
@@ -222,6 +230,54 @@ def train(x, y, rounds, **kw):
     return nodes[: int(tree_ptr[-1])].copy(), tree_ptr.copy(), base, margins.reshape(n, k)
 
 
+def _csr(indptr, indices, values):
+    return (np.ascontiguousarray(indptr, np.uint64), np.ascontiguousarray(indices, np.uint32),
+            np.ascontiguousarray(values, np.float32))
+
+
+def cuts_csr(indptr, indices, values, n_cols, max_bin):
+    ip, ix, vs = _csr(indptr, indices, values)
+    cap = n_cols * (max_bin + 1)
+    off = np.zeros(n_cols + 1, np.uint32)
+    vals = np.zeros(cap, np.float32)
+    total = lib().orc_cuts_csr(_p(ip, ctypes.c_uint64), _p(ix, ctypes.c_uint32), _p(vs, ctypes.c_float),
+                               ip.size - 1, n_cols, max_bin, _p(off, ctypes.c_uint32), _p(vals, ctypes.c_float), cap)
+    assert total >= 0
+    return off, vals[:total].copy()
+
+
+def _tree_cap(p):
+    depth = p.max_depth if p.max_depth > 0 else 16
+    if p.grow_policy == 0:
+        return 2 ** (depth + 1)
+    return 2 * (p.max_leaves if p.max_leaves > 0 else 2 ** depth) + 1
+
+
+def train_csr(indptr, indices, values, n_cols, y, rounds, **kw):
+    """`train` on CSR arrays (absent cells missing): the oracle's CSR index."""
+    ip, ix, vs = _csr(indptr, indices, values)
+    n = ip.size - 1
+    if kw.get("objective", 0) == 2:
+        y = np.ascontiguousarray(y, np.float32).reshape(n)
+        k = kw["n_outputs"]
+    else:
+        y = np.ascontiguousarray(y, np.float32).reshape(n, -1)
+        k = y.shape[1]
+    kw.setdefault("n_outputs", k)
+    p = params(**kw)
+    cap = rounds * k * _tree_cap(p) + 1
+    nodes = np.zeros(cap, NODE_DTYPE)
+    tree_ptr = np.zeros(rounds * k + 1, np.uint64)
+    base = np.zeros(k, np.float32)
+    margins = np.zeros(n * k, np.float32)
+    got = lib().orc_train_csr(ctypes.byref(p), _p(ip, ctypes.c_uint64), _p(ix, ctypes.c_uint32), _p(vs, ctypes.c_float),
+                              n, n_cols, _p(y, ctypes.c_float), rounds, nodes.ctypes.data_as(ctypes.POINTER(OrcNode)),
+                              cap, _p(tree_ptr, ctypes.c_uint64), _p(base, ctypes.c_float), _p(margins, ctypes.c_float))
+    assert got >= 0, got
+    tree_ptr = tree_ptr[: got + 1]
+    return nodes[: int(tree_ptr[-1])].copy(), tree_ptr.copy(), base, margins.reshape(n, k)
+
+
 def predict(nodes, tree_ptr, n_outputs, base, x, tree_output=None, tree_weight=None):
     x = np.ascontiguousarray(x, np.float32)
     n, f = x.shape
@@ -305,21 +361,32 @@ class Trainer:
     """An oracle training session: preparation (cuts, bins, intercepts) in
     the constructor, timed rounds in ``rounds``."""
 
-    def __init__(self, x, y, **kw):
-        self._x = np.ascontiguousarray(x, np.float32)
-        n, f = self._x.shape
+    def __init__(self, x, y, csr=None, **kw):
+        """`x` dense f32 rows, or None with `csr` = (indptr, indices, values, n_cols)."""
+        if csr is not None:
+            self._csr = _csr(*csr[:3])
+            n, f = self._csr[0].size - 1, csr[3]
+            self._x = None
+        else:
+            self._x = np.ascontiguousarray(x, np.float32)
+            n, f = self._x.shape
         if kw.get("objective", 0) == 2:  # multi:softmax: class ids, n_outputs classes
             self._y = np.ascontiguousarray(y, np.float32).reshape(n)
         else:
             self._y = np.ascontiguousarray(y, np.float32).reshape(n, -1)
             kw.setdefault("n_outputs", self._y.shape[1])
         self.p = params(**kw)
-        self.h = lib().orc_trainer_new(ctypes.byref(self.p), _p(self._x, ctypes.c_float), n, f, _p(self._y, ctypes.c_float))
+        if self._x is None:
+            ip, ix, vs = self._csr
+            self.h = lib().orc_trainer_new_csr(ctypes.byref(self.p), _p(ip, ctypes.c_uint64), _p(ix, ctypes.c_uint32),
+                                               _p(vs, ctypes.c_float), n, f, _p(self._y, ctypes.c_float))
+        else:
+            self.h = lib().orc_trainer_new(ctypes.byref(self.p), _p(self._x, ctypes.c_float), n, f,
+                                           _p(self._y, ctypes.c_float))
         assert self.h
 
     def rounds(self, k):
-        depth = self.p.max_depth if self.p.max_depth > 0 else 16
-        cap = max(k, 1) * self.p.n_outputs * (2 ** (depth + 1)) + 1
+        cap = max(k, 1) * self.p.n_outputs * _tree_cap(self.p) + 1
         nodes = np.zeros(cap, NODE_DTYPE)
         ptr = np.zeros(k * self.p.n_outputs + 1, np.uint64)
         got = lib().orc_trainer_rounds(self.h, k, nodes.ctypes.data_as(ctypes.POINTER(OrcNode)), cap, _p(ptr, ctypes.c_uint64))

@@ -105,3 +105,37 @@ def test_synthetic_c4_shape():
         c = indices[int(indptr[r]) : int(indptr[r + 1])]
         assert np.all(np.diff(c.astype(np.int64)) > 0) and (c.size == 0 or c[-1] < 300)
     assert np.all(values > 0) and set(np.unique(y)) <= {0.0, 1.0}
+
+
+@pytest.mark.parametrize("name,kw,max_bin", CASES, ids=[c[0] for c in CASES])
+def test_oracle_csr_cuts_match_dense(name, kw, max_bin):
+    indptr, indices, values = _random_csr(**kw)
+    x = synth.csr_to_dense(indptr, indices, values, kw["f"])
+    off, cuts = O.cuts_csr(indptr, indices, values, kw["f"], max_bin)
+    off_o, cuts_o = O.cuts_dense(x, max_bin)
+    np.testing.assert_array_equal(off, off_o)
+    np.testing.assert_array_equal(cuts.view(np.uint32), cuts_o.view(np.uint32))
+
+
+@pytest.mark.parametrize("fixed", [True, False], ids=["fixed_point", "f64"])
+@pytest.mark.parametrize("policy", [0, 1], ids=["depthwise", "lossguide"])
+def test_oracle_csr_training_equals_dense(fixed, policy):
+    """The oracle's CSR index (stored cells only) trains the trees of its
+    dense index on the same cells: bit for bit in fixed point; in f64 the
+    reference's row-order chains give the same sums too on this set."""
+    indptr, indices, values = _random_csr(2500, 15, 0.3, 9)
+    x = synth.csr_to_dense(indptr, indices, values, 15)
+    rng = np.random.default_rng(2)
+    y = (np.nan_to_num(x[:, 0]) + np.nan_to_num(x[:, 3]) * 0.5 + rng.standard_normal(2500) * 0.1).astype(np.float32)
+    kw = dict(max_depth=5, grow_policy=policy, max_leaves=20 if policy else 0, fixed_point=fixed)
+    a = O.train_csr(indptr, indices, values, 15, y, 3, **kw)
+    b = O.train(x, y, 3, **kw)
+    np.testing.assert_array_equal(a[1], b[1])
+    for k in ("left", "right", "split_feature", "default_left", "split_bin"):
+        np.testing.assert_array_equal(a[0][k], b[0][k], err_msg=k)
+    if fixed:
+        for k in ("leaf_value", "sum_hess", "split_gain", "split_cond"):
+            np.testing.assert_array_equal(a[0][k].view(np.uint32), b[0][k].view(np.uint32), err_msg=k)
+        np.testing.assert_array_equal(a[3].view(np.uint32), b[3].view(np.uint32))
+    else:
+        np.testing.assert_allclose(a[0]["leaf_value"], b[0]["leaf_value"], rtol=1e-5, atol=1e-7)

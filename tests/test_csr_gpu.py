@@ -134,13 +134,23 @@ def test_csr_engine_matches_dense_engine():
 
 
 def test_csr_c4_shape_lossguide():
-    """The C4 shape at test size: 2,000 features at 2% density, 64 bins,
-    lossguide with 255 leaves."""
-    indptr, indices, values, y = synth.sparse_c4(12_000, 2000, seed=11)
-    x = synth.csr_to_dense(indptr, indices, values, 2000)
+    """The C4 shape at test size: 60,000 rows x 2,000 features at 2% density,
+    64 bins, lossguide with 255 leaves; the oracle trains on its own CSR index
+    (stored cells only). Trees, and the training margins read back from the
+    device, bit for bit."""
+    indptr, indices, values, y = synth.sparse_c4(60_000, 2000, seed=11)
     m = H.BinnedMatrix.from_csr(indptr, indices, values, 2000, 64)
     kw = dict(objective="binary:logistic", grow_policy="lossguide", max_depth=0, max_leaves=255, eta=0.3)
-    model = H.train(H.TrainingParams(max_bin=64, **kw), y=y, rounds=2, matrix=m)
-    on, op, ob, omarg = O.train(x, y, 2, fixed_point=True, max_bin=64, **_orc_kw(kw))
-    _assert_forest_equal(model.nodes, model.tree_ptr, on, op, "c4")
-    np.testing.assert_array_equal(_bits(model.predict_margin(x).reshape(-1)), _bits(omarg[:, 0]))
+    params = H.TrainingParams(max_bin=64, **kw)
+    e = H.Engine()
+    try:
+        e.upload(m)
+        base = H.base_margin(params, y)
+        nodes, ptr = e.train(params, y, 3, base)
+        marg = e.read_margins()
+    finally:
+        e.close()
+    on, op, ob, omarg = O.train_csr(indptr, indices, values, 2000, y, 3, fixed_point=True, max_bin=64, **_orc_kw(kw))
+    assert np.float32(base).view(np.uint32) == ob.view(np.uint32)[0]
+    _assert_forest_equal(nodes, ptr, on, op, "c4")
+    np.testing.assert_array_equal(_bits(marg), _bits(omarg[:, 0]))
