@@ -802,6 +802,9 @@ hb_status hb_engine_upload(hb_engine* e, const hb_ghist* g) {
   // selects the 64-bit-atomic one for every size (comparison runs).
   const char* hk = std::getenv("HB_HIST_KERNEL");
   c.hist64 = (hk && std::strcmp(hk, "64") == 0) ? 1u : 0u;
+  // HB_SCAN_KERNEL=cta keeps the CTA-per-feature scan for every width.
+  const char* sk = std::getenv("HB_SCAN_KERNEL");
+  c.scan_cta = (sk && std::strcmp(sk, "cta") == 0) ? 1u : 0u;
   e->h_cuts.assign(g->cut_values, g->cut_values + c.total_bins);
   e->has_missing = g->missing != nullptr;
 

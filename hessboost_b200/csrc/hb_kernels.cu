@@ -1111,6 +1111,156 @@ __global__ void __launch_bounds__(kSplitThreads)
   }
 }
 
+// The same scan with one warp per (node, feature), for features of at most
+// 32 * P bins: lane l holds bins l*P .. l*P+P-1 (its P sums, then a warp
+// scan of the lanes' totals). The candidates, their sequence numbers and
+// the first-maximum rule are k_scan's, so the winner is the same bit for
+// bit; a CTA of kScanWarps warps covers kScanWarps features of one node.
+constexpr int kScanWarps = 8;
+
+template <int P>
+__global__ void __launch_bounds__(kScanWarps * 32)
+    k_scan_w(DevConst c, const uint32_t* __restrict__ fo, longlong2* __restrict__ hist,
+             const Front* __restrict__ front, const LevelState* __restrict__ ls,
+             const Triple* __restrict__ pairs, int sib_base, const Scale* __restrict__ scale,
+             Cand* __restrict__ cand) {
+  const int k = blockIdx.y;
+  if (k >= ls->n_front) return;
+  const int lane = threadIdx.x & 31;
+  const int f = blockIdx.x * kScanWarps + (threadIdx.x >> 5);
+  if (f >= (int)c.n_cols) return;
+  const Front fr = front[k];
+  const uint32_t fs = fo[f];
+  const int nb = (int)(fo[f + 1] - fs);
+  Cand* out = cand + (uint64_t)k * c.n_cols + f;
+  if (nb <= 1 || fr.slot < 0) {
+    if (lane == 0) {
+      Cand e;
+      e.loss = -INFINITY;
+      e.bin = -1;
+      e.default_left = 0;
+      e.pad = 0;
+      e.lg = e.lh = 0;
+      *out = e;
+    }
+    return;
+  }
+  bool sib = false;
+  Triple tr{};
+  if (pairs != nullptr) {
+    sib = sib_base >= 0 ? fr.slot >= sib_base : fr.slot == pairs[0].sibling;
+    if (sib) tr = pairs[sib_base >= 0 ? fr.slot - sib_base : 0];
+  }
+  long long vg[P], vh[P];
+  long long lg_ = 0, lh_ = 0;
+#pragma unroll
+  for (int i = 0; i < P; ++i) {
+    const int t = lane * P + i;
+    longlong2 v = make_longlong2(0, 0);
+    if (t < nb) {
+      if (sib) {
+        const longlong2 pv = hist[(uint64_t)tr.parent * c.total_bins + fs + t];
+        const longlong2 bv = hist[(uint64_t)tr.built * c.total_bins + fs + t];
+        v = make_longlong2(pv.x - bv.x, pv.y - bv.y);
+        hist[(uint64_t)fr.slot * c.total_bins + fs + t] = v;
+      } else {
+        v = hist[(uint64_t)fr.slot * c.total_bins + fs + t];
+      }
+    }
+    vg[i] = v.x;
+    vh[i] = v.y;
+    lg_ += v.x;
+    lh_ += v.y;
+  }
+  // exclusive prefix of the lanes' totals, and the feature's total
+  long long eg = lg_, eh = lh_;
+#pragma unroll
+  for (int d = 1; d < 32; d <<= 1) {
+    const long long tg = __shfl_up_sync(kFull, eg, d);
+    const long long th = __shfl_up_sync(kFull, eh, d);
+    if (lane >= d) {
+      eg += tg;
+      eh += th;
+    }
+  }
+  const long long tot_g = __shfl_sync(kFull, eg, 31), tot_h = __shfl_sync(kFull, eh, 31);
+  eg -= lg_;
+  eh -= lh_;
+  const bool has_missing = !c.dense && !(tot_g == fr.g && tot_h == fr.h);
+  const double ig = scale->ig, ih = scale->ih;
+  const float root_gain = node_gain(ll2d(fr.g) * ig, ll2d(fr.h) * ih, c);
+  float best = -INFINITY;
+  int best_seq = INT_MAX;
+  long long blg = 0, blh = 0;
+  int bbin = -1, bdl = 0;
+  long long run_g = eg, run_h = eh;  // exclusive prefix of bin t
+#pragma unroll
+  for (int i = 0; i < P; ++i) {
+    const int t = lane * P + i;
+    const long long excl_g = run_g, excl_h = run_h;
+    run_g += vg[i];
+    run_h += vh[i];
+    if (t < nb && (vg[i] != 0 || vh[i] != 0)) {
+      const float l = cand_loss(ll2d(run_g) * ig, ll2d(run_h) * ih, ll2d(fr.g - run_g) * ig,
+                                ll2d(fr.h - run_h) * ih, root_gain, c);
+      if (isfinite(l) && cand_better(l, t, best, best_seq)) {
+        best = l;
+        best_seq = t;
+        blg = run_g;
+        blh = run_h;
+        bbin = (int)fs + t;
+        bdl = 0;
+      }
+      if (has_missing) {
+        const long long rg = tot_g - excl_g, rh = tot_h - excl_h;
+        const long long lg2 = fr.g - rg, lh2 = fr.h - rh;
+        const float lb = cand_loss(ll2d(lg2) * ig, ll2d(lh2) * ih, ll2d(rg) * ig, ll2d(rh) * ih,
+                                   root_gain, c);
+        const int seq = nb + (nb - 1 - t);
+        if (isfinite(lb) && cand_better(lb, seq, best, best_seq)) {
+          best = lb;
+          best_seq = seq;
+          blg = lg2;
+          blh = lh2;
+          bbin = t == 0 ? -1 : (int)fs + t - 1;
+          bdl = 1;
+        }
+      }
+    }
+  }
+  float wb = best;
+  int ws = best_seq;
+#pragma unroll
+  for (int d = 16; d > 0; d >>= 1) {
+    const float ob = __shfl_xor_sync(kFull, wb, d);
+    const int os = __shfl_xor_sync(kFull, ws, d);
+    if (cand_better(ob, os, wb, ws)) {
+      wb = ob;
+      ws = os;
+    }
+  }
+  if (ws == INT_MAX) {
+    if (lane == 0) {
+      Cand e;
+      e.loss = -INFINITY;
+      e.bin = -1;
+      e.default_left = 0;
+      e.pad = 0;
+      e.lg = e.lh = 0;
+      *out = e;
+    }
+  } else if (best_seq == ws) {
+    Cand e;
+    e.loss = best;
+    e.bin = bbin;
+    e.default_left = bdl;
+    e.pad = 0;
+    e.lg = blg;
+    e.lh = blh;
+    *out = e;
+  }
+}
+
 // ---------------------------------------------------------------------------
 // One CTA decides the whole level: each frontier node's split (features
 // merged in order with need_replace, builder/mod.rs:313), validity
@@ -2038,6 +2188,17 @@ void launch_scan(const DevConst& c, const uint32_t* fo, longlong2* hist, const F
                  const LevelState* ls, const Triple* pairs, int sib_base, const Scale* scale,
                  int max_front, Cand* cand, cudaStream_t s) {
   if (max_front < 1 || c.n_cols == 0) return;
+  // features of <= 128 bins: a warp per (node, feature); wider: a CTA
+  if (c.max_bins <= 128 && !c.scan_cta) {
+    dim3 grid((c.n_cols + kScanWarps - 1) / kScanWarps, max_front);
+    if (c.max_bins <= 32)
+      k_scan_w<1><<<grid, kScanWarps * 32, 0, s>>>(c, fo, hist, front, ls, pairs, sib_base, scale, cand);
+    else if (c.max_bins <= 64)
+      k_scan_w<2><<<grid, kScanWarps * 32, 0, s>>>(c, fo, hist, front, ls, pairs, sib_base, scale, cand);
+    else
+      k_scan_w<4><<<grid, kScanWarps * 32, 0, s>>>(c, fo, hist, front, ls, pairs, sib_base, scale, cand);
+    return;
+  }
   dim3 grid(c.n_cols, max_front);
   k_scan<<<grid, kSplitThreads, 0, s>>>(c, fo, hist, front, ls, pairs, sib_base, scale, cand);
 }

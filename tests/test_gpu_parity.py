@@ -449,3 +449,21 @@ def test_histogram_kernels_agree(monkeypatch):
         monkeypatch.setenv("HB_HIST_KERNEL", kernel)
         runs.append(H.train(p, y=y, rounds=2, matrix=m))
     assert_forest_equal(runs[0].nodes, runs[0].tree_ptr, runs[1].nodes, runs[1].tree_ptr, "32 vs 64")
+
+
+@pytest.mark.parametrize("max_bin", [16, 48, 128])
+def test_scan_kernels_agree(monkeypatch, max_bin):
+    """The warp-per-feature split scan (features of <= 128 bins) and the
+    CTA-per-feature one pick the same splits, depthwise and lossguide, with
+    missing values (both directions scored)."""
+    x, y = synth.logistic_c2(50_021, 20, seed=max_bin, missing=0.1)
+    m = H.BinnedMatrix.from_dense(x, max_bin)
+    runs = []
+    for kernel in ("warp", "cta"):
+        monkeypatch.setenv("HB_SCAN_KERNEL", kernel)
+        for policy in ("depthwise", "lossguide"):
+            p = H.TrainingParams(objective="binary:logistic", max_depth=6, max_bin=max_bin, grow_policy=policy,
+                                 max_leaves=40 if policy == "lossguide" else 0)
+            runs.append(H.train(p, y=y, rounds=2, matrix=m))
+    for a, b in ((0, 2), (1, 3)):
+        assert_forest_equal(runs[a].nodes, runs[a].tree_ptr, runs[b].nodes, runs[b].tree_ptr, "warp vs cta")
