@@ -244,7 +244,17 @@ SIGNATURES = {
     "hb_cuts_csr": [_u64p, _u32p, _f32p, ctypes.c_uint64, ctypes.c_uint32, ctypes.c_uint32, _u32p, _f32p,
                     ctypes.c_uint64, _u64p],
     "hb_bin_csr": [_u64p, _u32p, _f32p, ctypes.c_uint64, ctypes.c_uint32, _u32p, _f32p, _u64p, _u32p, _i32p],
+    "hb_sketch_dense": [ctypes.c_int32, _f32p, ctypes.c_uint64, ctypes.c_uint32, ctypes.c_uint32, _u32p, _f32p,
+                        ctypes.c_uint64, _u64p, _u8p, _u64p, _i32p],
+    "hb_sketch_csr": [ctypes.c_int32, _u64p, _u32p, _f32p, ctypes.c_uint64, ctypes.c_uint32, ctypes.c_uint32, _u32p,
+                      _f32p, ctypes.c_uint64, _u64p, _u32p, _i32p],
+    "hb_sketch_last_error": [],
+    "hb_engine_upload_dense": [_vp, _f32p, ctypes.c_uint64, ctypes.c_uint32, ctypes.c_uint32, _u32p, _f32p,
+                               ctypes.c_uint64, _u64p],
+    "hb_engine_upload_csr": [_vp, _u64p, _u32p, _f32p, ctypes.c_uint64, ctypes.c_uint32, ctypes.c_uint32, _u32p,
+                             _f32p, ctypes.c_uint64, _u64p],
 }
+_STRING_RESULT = ("hb_engine_last_error", "hb_sketch_last_error")
 
 _lib = None
 
@@ -260,7 +270,7 @@ def lib():
         for name, args in SIGNATURES.items():
             fn = getattr(L, name)
             fn.argtypes = args
-            fn.restype = ctypes.c_char_p if name == "hb_engine_last_error" else ctypes.c_int32
+            fn.restype = ctypes.c_char_p if name in _STRING_RESULT else ctypes.c_int32
         _lib = L
     return _lib
 
@@ -412,6 +422,75 @@ def bin_csr(indptr, indices, values, n_cols, feature_offset, cut_values):
     return row_ptr, row_bins[: int(ip[-1])], bool(dense.value)
 
 
+def _sketch_check(status, where):
+    if status != HB_OK:
+        msg = lib().hb_sketch_last_error()
+        raise HbError(status, where, msg.decode() if msg else "")
+
+
+def sketch_dense(x, max_bin=256, device=0, bins=True):
+    """hb_cuts_dense (+ hb_bin_dense when ``bins``) computed on ``device``:
+    returns (feature_offset, cut_values, columns, missing, dense), the last
+    three None without ``bins``."""
+    x = np.ascontiguousarray(x, np.float32)
+    n, f = x.shape
+    cap = f * max(max_bin, 1)
+    off = np.zeros(f + 1, np.uint32)
+    vals = np.zeros(cap, np.float32)
+    total = ctypes.c_uint64()
+    cols = miss = None
+    dense = ctypes.c_int32()
+    if bins:
+        cols = np.empty((f, n), np.uint8)
+        miss = np.zeros((f, (n + 63) // 64), np.uint64)
+    _sketch_check(lib().hb_sketch_dense(device, _ptr(x, ctypes.c_float), n, f, max_bin, _ptr(off, ctypes.c_uint32),
+                                        _ptr(vals, ctypes.c_float), cap, ctypes.byref(total),
+                                        None if cols is None else _ptr(cols, ctypes.c_uint8),
+                                        None if miss is None else _ptr(miss, ctypes.c_uint64),
+                                        ctypes.byref(dense) if bins else None), "hb_sketch_dense")
+    vals = vals[: total.value].copy()
+    if not bins:
+        return off, vals, None, None, None
+    return off, vals, cols, miss, bool(dense.value)
+
+
+def sketch_csr(indptr, indices, values, n_cols, max_bin=256, device=0, bins=True):
+    """hb_cuts_csr (+ hb_bin_csr when ``bins``) computed on ``device``:
+    returns (feature_offset, cut_values, row_bins, dense)."""
+    ip, ix, vs = _csr_arrays(indptr, indices, values)
+    n = ip.size - 1
+    cap = n_cols * max(max_bin, 1)
+    off = np.zeros(n_cols + 1, np.uint32)
+    vals = np.zeros(cap, np.float32)
+    total = ctypes.c_uint64()
+    dense = ctypes.c_int32()
+    rb = np.empty(max(int(ip[-1]), 1), np.uint32) if bins else None
+    _sketch_check(lib().hb_sketch_csr(device, _ptr(ip, ctypes.c_uint64), _ptr(ix, ctypes.c_uint32),
+                                      _ptr(vs, ctypes.c_float), n, n_cols, max_bin, _ptr(off, ctypes.c_uint32),
+                                      _ptr(vals, ctypes.c_float), cap, ctypes.byref(total),
+                                      None if rb is None else _ptr(rb, ctypes.c_uint32),
+                                      ctypes.byref(dense) if bins else None), "hb_sketch_csr")
+    vals = vals[: total.value].copy()
+    if not bins:
+        return off, vals, None, None
+    return off, vals, rb[: int(ip[-1])], bool(dense.value)
+
+
+class DeviceIndex:
+    """What the host keeps of an index the engine sketched and binned on its
+    own device (hb_engine_upload_dense / _csr): the cuts and the shape."""
+
+    def __init__(self, feature_offset, cut_values, n_rows, n_cols):
+        self.feature_offset = feature_offset
+        self.cut_values = cut_values
+        self.n_rows = n_rows
+        self.n_cols = n_cols
+
+    @property
+    def total_bins(self):
+        return int(self.feature_offset[-1])
+
+
 class BinnedMatrix:
     """A GHistIndex-equivalent: cuts plus either one-byte feature-major bins
     and the missing bitmap, or (``from_csr``) the CSR rows of global bins."""
@@ -437,14 +516,23 @@ class BinnedMatrix:
         return self.columns is None
 
     @classmethod
-    def from_dense(cls, x, max_bin=256, cuts=None):
+    def from_dense(cls, x, max_bin=256, cuts=None, device=None):
+        """Host sketch and binning; with ``device`` (a GPU ordinal) and no
+        given cuts, both run on that GPU (hb_sketch_dense)."""
+        if device is not None and cuts is None:
+            off, vals, cols, miss, dense = sketch_dense(x, max_bin, device)
+            return cls(off, vals, cols, miss, dense)
         off, vals = cuts if cuts is not None else cuts_dense(x, max_bin)
         cols, miss, dense = bin_dense(x, off, vals)
         return cls(off, vals, cols, miss, dense)
 
     @classmethod
-    def from_csr(cls, indptr, indices, values, n_cols, max_bin=256, cuts=None):
-        """DMatrix::from_csr + GHistIndex: absent entries are missing."""
+    def from_csr(cls, indptr, indices, values, n_cols, max_bin=256, cuts=None, device=None):
+        """DMatrix::from_csr + GHistIndex: absent entries are missing. With
+        ``device`` and no given cuts, sketch and bins come from the GPU."""
+        if device is not None and cuts is None:
+            off, vals, rb, dense = sketch_csr(indptr, indices, values, n_cols, max_bin, device)
+            return cls(off, vals, None, None, dense, np.asarray(indptr, np.uint64), rb)
         off, vals = cuts if cuts is not None else cuts_csr(indptr, indices, values, n_cols, max_bin)
         row_ptr, row_bins, dense = bin_csr(indptr, indices, values, n_cols, off, vals)
         return cls(off, vals, None, None, dense, row_ptr, row_bins)
@@ -527,6 +615,36 @@ class Engine:
         self.matrix = m
         g = m.to_c()
         self._c(lib().hb_engine_upload(self.h, ctypes.byref(g)), "hb_engine_upload")
+
+    def upload_dense(self, x, max_bin=256):
+        """Sketch, bin and keep a raw dense matrix on this engine's GPU
+        (hb_engine_upload_dense); returns the DeviceIndex (cuts and shape)."""
+        x = np.ascontiguousarray(x, np.float32)
+        n, f = x.shape
+        cap = f * max(max_bin, 1)
+        off = np.zeros(f + 1, np.uint32)
+        vals = np.zeros(cap, np.float32)
+        total = ctypes.c_uint64()
+        self._c(lib().hb_engine_upload_dense(self.h, _ptr(x, ctypes.c_float), n, f, max_bin, _ptr(off, ctypes.c_uint32),
+                                             _ptr(vals, ctypes.c_float), cap, ctypes.byref(total)),
+                "hb_engine_upload_dense")
+        self.matrix = DeviceIndex(off, vals[: total.value].copy(), n, f)
+        return self.matrix
+
+    def upload_csr(self, indptr, indices, values, n_cols, max_bin=256):
+        """The CSR twin of upload_dense (hb_engine_upload_csr)."""
+        ip, ix, vs = _csr_arrays(indptr, indices, values)
+        n = ip.size - 1
+        cap = n_cols * max(max_bin, 1)
+        off = np.zeros(n_cols + 1, np.uint32)
+        vals = np.zeros(cap, np.float32)
+        total = ctypes.c_uint64()
+        self._c(lib().hb_engine_upload_csr(self.h, _ptr(ip, ctypes.c_uint64), _ptr(ix, ctypes.c_uint32),
+                                           _ptr(vs, ctypes.c_float), n, n_cols, max_bin, _ptr(off, ctypes.c_uint32),
+                                           _ptr(vals, ctypes.c_float), cap, ctypes.byref(total)),
+                "hb_engine_upload_csr")
+        self.matrix = DeviceIndex(off, vals[: total.value].copy(), n, n_cols)
+        return self.matrix
 
     # HistogramBackend
     def prepare(self, gpair):

@@ -16,6 +16,7 @@
 #include "hb_engine_view.h"
 #include "hb_internal.h"
 #include "hb_kernels.cuh"
+#include "hb_sketch.h"
 
 using namespace hb;
 
@@ -747,38 +748,66 @@ static hb_status finish_upload(hb_engine* e) {
   return HB_OK;
 }
 
+// A raw matrix already on the device that the upload bins itself (the
+// device sketch, hb_sketch.cu), in place of the caller's binned index.
+struct RawSource {
+  const float* x = nullptr;      // dense row-major, NaN missing
+  const uint64_t* ip = nullptr;  // CSR offsets, columns, values
+  const uint32_t* ix = nullptr;
+  const float* v = nullptr;
+  uint64_t nnz = 0;
+};
+
 // The CSR half of the upload (ghist.rs:6-21 `rows`): offsets and global
 // bins as they are; no record or column copy.
-static hb_status upload_csr(hb_engine* e, const hb_ghist* g) {
+static hb_status upload_csr(hb_engine* e, const hb_ghist* g, const RawSource* raw) {
   DevConst& c = e->c;
   const uint64_t n = c.n_rows;
-  if (g->row_ptr[0] != 0) return HB_INVALID_ARGUMENT;
-  const uint64_t nnz = g->row_ptr[n];
-  if (nnz && !g->row_bins) return HB_INVALID_ARGUMENT;
-  for (uint64_t r = 0; r < n; ++r)
-    if (g->row_ptr[r + 1] < g->row_ptr[r]) return HB_INVALID_ARGUMENT;
-  for (uint64_t j = 0; j < nnz; ++j)
-    if (g->row_bins[j] >= c.total_bins) return refuse(e, "row_bins: a bin beyond the cuts");
-  HB_CK(e, e->csr_ptr.alloc(n + 1));
-  HB_CK(e, e->csr_bins.alloc(std::max<uint64_t>(nnz, 1)));
   cudaStream_t s = e->stream;
-  HB_CK(e, cudaMemcpyAsync(e->csr_ptr.p, g->row_ptr, 8 * (n + 1), cudaMemcpyHostToDevice, s));
-  if (nnz) HB_CK(e, cudaMemcpyAsync(e->csr_bins.p, g->row_bins, 4 * nnz, cudaMemcpyHostToDevice, s));
+  if (raw) {
+    HB_CK(e, e->csr_ptr.alloc(n + 1));
+    HB_CK(e, e->csr_bins.alloc(std::max<uint64_t>(raw->nnz, 1)));
+    DevBuf<int> flag;
+    HB_CK(e, flag.alloc(1));
+    HB_CK(e, cudaMemcpyAsync(e->csr_ptr.p, raw->ip, 8 * (n + 1), cudaMemcpyDeviceToDevice, s));
+    HB_CK(e, bin_csr_device(raw->ip, raw->ix, raw->v, n, c.n_cols, raw->nnz, e->fo.p, e->cuts.p,
+                            e->csr_bins.p, flag.p, s));
+    int hf = 0;
+    HB_CK(e, cudaMemcpyAsync(&hf, flag.p, 4, cudaMemcpyDeviceToHost, s));
+    HB_CK(e, cudaStreamSynchronize(s));
+    flag.release();
+    e->has_missing = (hf & 4) != 0;
+    c.dense = e->has_missing ? 0 : 1;
+  } else {
+    if (g->row_ptr[0] != 0) return HB_INVALID_ARGUMENT;
+    const uint64_t nnz = g->row_ptr[n];
+    if (nnz && !g->row_bins) return HB_INVALID_ARGUMENT;
+    for (uint64_t r = 0; r < n; ++r)
+      if (g->row_ptr[r + 1] < g->row_ptr[r]) return HB_INVALID_ARGUMENT;
+    for (uint64_t j = 0; j < nnz; ++j)
+      if (g->row_bins[j] >= c.total_bins) return refuse(e, "row_bins: a bin beyond the cuts");
+    HB_CK(e, e->csr_ptr.alloc(n + 1));
+    HB_CK(e, e->csr_bins.alloc(std::max<uint64_t>(nnz, 1)));
+    HB_CK(e, cudaMemcpyAsync(e->csr_ptr.p, g->row_ptr, 8 * (n + 1), cudaMemcpyHostToDevice, s));
+    if (nnz) HB_CK(e, cudaMemcpyAsync(e->csr_bins.p, g->row_bins, 4 * nnz, cudaMemcpyHostToDevice, s));
+    e->has_missing = !g->dense;
+  }
   c.csr = 1;
   c.csr_ptr = e->csr_ptr.p;
   c.csr_bins = e->csr_bins.p;
-  e->has_missing = !g->dense;
   e->col.release();
   e->rec.release();
   e->colmiss.release();
   return HB_OK;
 }
 
-hb_status hb_engine_upload(hb_engine* e, const hb_ghist* g) {
-  HB_ENTER(e);
-  const bool csr = g && !g->columns && g->row_ptr;
-  if (!g || !g->feature_offset || !g->cut_values || (!g->columns && !csr) || g->n_rows == 0 ||
-      g->n_cols == 0)
+// CudaHistBackend::new + upload (src/backend/cuda/mod.rs:1626,1687) of the
+// index `g`; with `raw`, the bins (and the dense flag) come from binning the
+// raw device matrix against g's cuts instead of from g.
+static hb_status upload_index(hb_engine* e, const hb_ghist* g, const RawSource* raw) {
+  const bool csr = raw ? raw->ip != nullptr : (g && !g->columns && g->row_ptr);
+  if (!g || !g->feature_offset || !g->cut_values || (!raw && !g->columns && !csr) ||
+      (raw && !raw->x && !raw->ip) || g->n_rows == 0 || g->n_cols == 0)
     return HB_INVALID_ARGUMENT;
   if (g->n_rows >= (1ull << 32)) return refuse(e, "at most 2^32 - 1 rows per device");
   if (!csr && g->n_cols > 224) return refuse(e, "at most 224 features per device index");
@@ -806,7 +835,9 @@ hb_status hb_engine_upload(hb_engine* e, const hb_ghist* g) {
   const char* sk = std::getenv("HB_SCAN_KERNEL");
   c.scan_cta = (sk && std::strcmp(sk, "cta") == 0) ? 1u : 0u;
   e->h_cuts.assign(g->cut_values, g->cut_values + c.total_bins);
-  e->has_missing = g->missing != nullptr;
+  // a raw dense matrix may have missing cells: the bitmap is kept until the
+  // binning says otherwise
+  e->has_missing = raw ? true : g->missing != nullptr;
 
   const uint64_t n = c.n_rows, words = (n + 63) / 64;
   HB_CK(e, e->fo.alloc(c.n_cols + 1));
@@ -821,7 +852,7 @@ hb_status hb_engine_upload(hb_engine* e, const hb_ghist* g) {
     cudaStream_t s = e->stream;
     HB_CK(e, cudaMemcpyAsync(e->fo.p, e->h_fo.data(), 4 * (c.n_cols + 1), cudaMemcpyHostToDevice, s));
     HB_CK(e, cudaMemcpyAsync(e->cuts.p, e->h_cuts.data(), 4 * c.total_bins, cudaMemcpyHostToDevice, s));
-    hb_status st = upload_csr(e, g);
+    hb_status st = upload_csr(e, g, raw);
     if (st != HB_OK) return st;
     HB_CK(e, cudaStreamSynchronize(s));
     return finish_upload(e);
@@ -837,10 +868,25 @@ hb_status hb_engine_upload(hb_engine* e, const hb_ghist* g) {
   cudaStream_t s = e->stream;
   HB_CK(e, cudaMemcpyAsync(e->fo.p, e->h_fo.data(), 4 * (c.n_cols + 1), cudaMemcpyHostToDevice, s));
   HB_CK(e, cudaMemcpyAsync(e->cuts.p, e->h_cuts.data(), 4 * c.total_bins, cudaMemcpyHostToDevice, s));
-  HB_CK(e, cudaMemcpyAsync(e->col.p, g->columns, (size_t)c.n_cols * n, cudaMemcpyHostToDevice, s));
-  if (e->has_missing)
-    HB_CK(e, cudaMemcpyAsync(e->colmiss.p, g->missing, 8 * (size_t)c.n_cols * words,
-                             cudaMemcpyHostToDevice, s));
+  if (raw) {
+    DevBuf<int> any;
+    HB_CK(e, any.alloc(1));
+    HB_CK(e, bin_dense_device(raw->x, n, c.n_cols, e->fo.p, e->cuts.p, e->col.p, e->colmiss.p, any.p, s));
+    int h_any = 0;
+    HB_CK(e, cudaMemcpyAsync(&h_any, any.p, 4, cudaMemcpyDeviceToHost, s));
+    HB_CK(e, cudaStreamSynchronize(s));
+    any.release();
+    if (!h_any) {
+      e->has_missing = false;
+      e->colmiss.release();
+    }
+    c.dense = h_any ? 0 : 1;
+  } else {
+    HB_CK(e, cudaMemcpyAsync(e->col.p, g->columns, (size_t)c.n_cols * n, cudaMemcpyHostToDevice, s));
+    if (e->has_missing)
+      HB_CK(e, cudaMemcpyAsync(e->colmiss.p, g->missing, 8 * (size_t)c.n_cols * words,
+                               cudaMemcpyHostToDevice, s));
+  }
   HB_CK(e, cudaMemsetAsync(e->rec.p, 0, (size_t)c.stride * n + 64, s));
   launch_encode(e->col.p, e->has_missing ? e->colmiss.p : nullptr, n, c.n_cols, c.stride,
                 c.mask_off, e->rec.p, s);
@@ -849,6 +895,109 @@ hb_status hb_engine_upload(hb_engine* e, const hb_ghist* g) {
   e->csr_ptr.release();
   e->csr_bins.release();
   return finish_upload(e);
+}
+
+hb_status hb_engine_upload(hb_engine* e, const hb_ghist* g) {
+  HB_ENTER(e);
+  return upload_index(e, g, nullptr);
+}
+
+// The sketch's outcome as the engine's: a refusal leaves the engine usable,
+// a device error is sticky.
+static hb_status sketch_status(hb_engine* e, hb_status st, const std::string& why) {
+  if (st == HB_OK) return HB_OK;
+  if (st == HB_REFUSED) return refuse(e, why);
+  if (st == HB_DEVICE_FAILED) {
+    e->failed = true;
+    e->err = why;
+    g_last_error = why;
+  }
+  return st;
+}
+
+static hb_status copy_cuts(hb_engine* e, const std::vector<uint32_t>& fo, const std::vector<float>& cuts,
+                           uint32_t n_cols, uint32_t* feature_offset, float* cut_values, uint64_t cap,
+                           uint64_t* total) {
+  if (cuts.size() > cap) return refuse(e, "cut_values capacity below the cut count");
+  std::memcpy(feature_offset, fo.data(), 4 * (size_t)(n_cols + 1));
+  std::memcpy(cut_values, cuts.data(), 4 * cuts.size());
+  *total = cuts.size();
+  return HB_OK;
+}
+
+hb_status hb_engine_upload_dense(hb_engine* e, const float* x, uint64_t n_rows, uint32_t n_cols,
+                                 uint32_t max_bin, uint32_t* feature_offset, float* cut_values,
+                                 uint64_t cap, uint64_t* total) {
+  HB_ENTER(e);
+  if (!x || !feature_offset || !cut_values || !total || n_rows == 0 || n_cols == 0 || max_bin == 0)
+    return HB_INVALID_ARGUMENT;
+  if (n_rows >= (1ull << 32)) return refuse(e, "at most 2^32 - 1 rows per device");
+  if (n_cols > 224) return refuse(e, "at most 224 features per device index");
+  cudaStream_t s = e->stream;
+  DevBuf<float> dx;
+  HB_CK(e, dx.alloc((size_t)n_rows * n_cols));
+  HB_CK(e, cudaMemcpyAsync(dx.p, x, 4 * (size_t)n_rows * n_cols, cudaMemcpyHostToDevice, s));
+  std::vector<uint32_t> fo;
+  std::vector<float> cuts;
+  std::string why;
+  hb_status st = sketch_status(e, sketch_dense_cuts(e->device, dx.p, n_rows, n_cols, max_bin, s, fo, cuts, why), why);
+  if (st != HB_OK) return st;
+  st = copy_cuts(e, fo, cuts, n_cols, feature_offset, cut_values, cap, total);
+  if (st != HB_OK) return st;
+  hb_ghist g{};
+  g.n_rows = n_rows;
+  g.n_cols = n_cols;
+  g.feature_offset = fo.data();
+  g.cut_values = cuts.data();
+  RawSource raw;
+  raw.x = dx.p;
+  st = upload_index(e, &g, &raw);
+  dx.release();
+  return st;
+}
+
+hb_status hb_engine_upload_csr(hb_engine* e, const uint64_t* indptr, const uint32_t* indices,
+                               const float* values, uint64_t n_rows, uint32_t n_cols, uint32_t max_bin,
+                               uint32_t* feature_offset, float* cut_values, uint64_t cap,
+                               uint64_t* total) {
+  HB_ENTER(e);
+  if (!indptr || !feature_offset || !cut_values || !total || n_rows == 0 || n_cols == 0 ||
+      max_bin == 0 || indptr[0] != 0)
+    return HB_INVALID_ARGUMENT;
+  if (n_rows >= (1ull << 32)) return refuse(e, "at most 2^32 - 1 rows per device");
+  const uint64_t nnz = indptr[n_rows];
+  if (nnz && (!indices || !values)) return HB_INVALID_ARGUMENT;
+  cudaStream_t s = e->stream;
+  DevBuf<uint64_t> dip;
+  DevBuf<uint32_t> dix;
+  DevBuf<float> dv;
+  HB_CK(e, dip.alloc(n_rows + 1));
+  HB_CK(e, dix.alloc(std::max<uint64_t>(nnz, 1)));
+  HB_CK(e, dv.alloc(std::max<uint64_t>(nnz, 1)));
+  HB_CK(e, cudaMemcpyAsync(dip.p, indptr, 8 * (n_rows + 1), cudaMemcpyHostToDevice, s));
+  if (nnz) {
+    HB_CK(e, cudaMemcpyAsync(dix.p, indices, 4 * nnz, cudaMemcpyHostToDevice, s));
+    HB_CK(e, cudaMemcpyAsync(dv.p, values, 4 * nnz, cudaMemcpyHostToDevice, s));
+  }
+  std::vector<uint32_t> fo;
+  std::vector<float> cuts;
+  std::string why;
+  hb_status st = sketch_status(
+      e, sketch_csr_cuts(e->device, dip.p, dix.p, dv.p, n_rows, n_cols, nnz, max_bin, s, fo, cuts, why), why);
+  if (st != HB_OK) return st;
+  st = copy_cuts(e, fo, cuts, n_cols, feature_offset, cut_values, cap, total);
+  if (st != HB_OK) return st;
+  hb_ghist g{};
+  g.n_rows = n_rows;
+  g.n_cols = n_cols;
+  g.feature_offset = fo.data();
+  g.cut_values = cuts.data();
+  RawSource raw;
+  raw.ip = dip.p;
+  raw.ix = dix.p;
+  raw.v = dv.p;
+  raw.nnz = nnz;
+  return upload_index(e, &g, &raw);
 }
 
 // ---- HistogramBackend ------------------------------------------------------

@@ -370,6 +370,41 @@ hb_status hb_bin_csr(const uint64_t* indptr, const uint32_t* indices, const floa
                      const float* cut_values, uint64_t* row_ptr, uint32_t* row_bins,
                      int32_t* dense);
 
+/* ---- device sketch and binning (HistCuts::from_dmatrix,
+ * GHistIndex::from_dmatrix on the GPU) ----------------------------------
+ * The same cut values, bit for bit, as hb_cuts_dense / hb_cuts_csr (the
+ * reference's WQSketch, src/data/sketch.rs:477-667, fed as
+ * src/data/quantile.rs:115 `build` feeds it with unit weights), computed
+ * on `device`. HB_REFUSED (reason in hb_sketch_last_error) where the device
+ * sketch does not apply and the host functions must be used: a feature with
+ * 2^24 or more present values, max_bin above 256, a CSR row whose column
+ * indices do not strictly ascend. */
+/* Cuts of a dense row-major f32 matrix (NaN missing), and, when `columns`
+ * is not NULL, the hb_bin_dense outputs (`missing` may be NULL). */
+hb_status hb_sketch_dense(int32_t device, const float* x, uint64_t n_rows, uint32_t n_cols,
+                          uint32_t max_bin, uint32_t* feature_offset, float* cut_values,
+                          uint64_t cap, uint64_t* total, uint8_t* columns, uint64_t* missing,
+                          int32_t* dense);
+/* Cuts of a CSR matrix (hb_cuts_csr's checks) and, when `row_bins` is not
+ * NULL, the hb_bin_csr bins (row_ptr is `indptr` itself). */
+hb_status hb_sketch_csr(int32_t device, const uint64_t* indptr, const uint32_t* indices,
+                        const float* values, uint64_t n_rows, uint32_t n_cols, uint32_t max_bin,
+                        uint32_t* feature_offset, float* cut_values, uint64_t cap, uint64_t* total,
+                        uint32_t* row_bins, int32_t* dense);
+const char* hb_sketch_last_error(void);
+/* CudaHistBackend::new(index) for a raw host matrix: the engine copies it
+ * to its device, sketches and bins it there into its resident index, and
+ * returns the cuts (the caller keeps them for the model's split values).
+ * Equivalent to hb_cuts_dense + hb_bin_dense + hb_engine_upload. */
+hb_status hb_engine_upload_dense(hb_engine* e, const float* x, uint64_t n_rows, uint32_t n_cols,
+                                 uint32_t max_bin, uint32_t* feature_offset, float* cut_values,
+                                 uint64_t cap, uint64_t* total);
+/* The CSR twin: hb_cuts_csr + hb_bin_csr + hb_engine_upload. */
+hb_status hb_engine_upload_csr(hb_engine* e, const uint64_t* indptr, const uint32_t* indices,
+                               const float* values, uint64_t n_rows, uint32_t n_cols,
+                               uint32_t max_bin, uint32_t* feature_offset, float* cut_values,
+                               uint64_t cap, uint64_t* total);
+
 #ifdef __cplusplus
 }
 #endif
