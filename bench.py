@@ -547,13 +547,31 @@ def main():
     params = H.TrainingParams(**PARAMS)
     # cut table over the whole matrix (rank 0), shared so every rank bins
     # against the same cuts; the index-level dense flag is the whole matrix's
+    prep = None
     if world > 1:
-        shard, begin, end = hdist.shard_matrix(dist, x, 256)
+        shard, begin, end = hdist.shard_matrix(dist, x, 256, device=local)
     else:
+        # sketch + binning of the whole matrix on the GPU (hb_sketch_dense:
+        # the f32 matrix up, cuts and binned columns back), then the same on
+        # the host's threads (hb_cuts_dense + hb_bin_dense), for the record
         begin, end = 0, N_ROWS
-        off, cuts = H.cuts_dense(x, 256)
-        cols, miss, dense = H.bin_dense(x, off, cuts)
+        H.sketch_dense(x[:4096], 256, local)  # context and module load
+        t0 = time.perf_counter()
+        off, cuts, cols, miss, dense = H.sketch_dense(x, 256, local)
+        t_dev = time.perf_counter() - t0
+        t0 = time.perf_counter()
+        hoff, hcuts = H.cuts_dense(x, 256)
+        hcols, _, _ = H.bin_dense(x, hoff, hcuts)
+        t_host = time.perf_counter() - t0
+        if not (np.array_equal(hcuts.view(np.uint32), cuts.view(np.uint32)) and np.array_equal(hcols, cols)):
+            raise SystemExit("device sketch and host sketch disagree")
+        del hcols
         shard = H.BinnedMatrix(off, cuts, cols, miss, dense)
+        prep = {"device_sketch_and_bins_s": t_dev, "host_sketch_and_bins_s": t_host,
+                "host_threads": os.cpu_count() or 1,
+                "scope": "HistCuts + GHistIndex of the 10M x 28 f32 matrix from host memory "
+                         "(device: hb_sketch_dense, upload and download included; host: "
+                         "hb_cuts_dense + hb_bin_dense); same cuts and bins, checked"}
     off, cuts, cols, miss, dense = (shard.feature_offset, shard.cut_values, shard.columns,
                                     shard.missing, shard.dense)
     base = H.base_margin(params, y)
@@ -668,6 +686,7 @@ def main():
             "config": dict(config(world), rows_per_s=value * N_ROWS,
                            trees_nodes=int(len(nodes)),
                            kernel_ms_per_round=per_round,
+                           prep=prep,
                            timing="device time of the K rounds from CUDA events the engine records "
                                   "on its stream around them (rounds replayed as a CUDA graph; "
                                   "event nodes around each histogram launch); per-family "

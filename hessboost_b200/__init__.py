@@ -937,13 +937,25 @@ class Model:
 
 
 def train(params, x=None, y=None, rounds=10, device=0, matrix=None, engine=None):
-    """Train ``rounds`` rounds on one GPU (train_trees, train.rs:222)."""
-    if matrix is None:
-        matrix = BinnedMatrix.from_dense(x, params.max_bin)
+    """Train ``rounds`` rounds on one GPU (train_trees, train.rs:222).
+
+    With a raw matrix ``x`` (and no ``matrix``) the engine sketches and bins
+    it on its own GPU (hb_engine_upload_dense); where the device sketch
+    refuses the input (a feature with 2^24 or more present values), the
+    reference's host sketch bins it instead, with the same cuts."""
     y = np.ascontiguousarray(y, np.float32)
     eng = engine or Engine(device)
     try:
-        eng.upload(matrix)
+        if matrix is None:
+            try:
+                matrix = eng.upload_dense(x, params.max_bin)
+            except HbError as err:
+                if err.status != HB_REFUSED:
+                    raise
+                matrix = BinnedMatrix.from_dense(x, params.max_bin)
+                eng.upload(matrix)
+        else:
+            eng.upload(matrix)
         if params.loss_kind() == HB_LOSS_SOFTMAX:
             if math.isnan(params.base_score):
                 base = softmax_intercepts(y, params.num_class)

@@ -53,14 +53,30 @@ def all_dense(dist, local_dense):
     return bool(int(t.item()))
 
 
-def shard_matrix(dist, x, max_bin):
+def whole_matrix_cuts(x, max_bin, device=None):
+    """Cuts of the whole matrix: the device sketch on `device` when given
+    (hb_sketch_dense), else, or where it refuses the input, the host sketch;
+    both give the same cuts."""
+    from . import HB_REFUSED, HbError, cuts_dense, sketch_dense
+
+    if device is not None:
+        try:
+            off, cuts, _, _, _ = sketch_dense(x, max_bin, device, bins=False)
+            return off, cuts
+        except HbError as err:
+            if err.status != HB_REFUSED:
+                raise
+    return cuts_dense(x, max_bin)
+
+
+def shard_matrix(dist, x, max_bin, device=None):
     """This rank's rows of `x` (every rank holds the same `x`), binned
-    against cuts rank 0 computes over the whole matrix: (BinnedMatrix,
-    begin, end)."""
-    from . import BinnedMatrix, bin_dense, cuts_dense
+    against cuts rank 0 computes over the whole matrix (on its GPU
+    `device` when given): (BinnedMatrix, begin, end)."""
+    from . import BinnedMatrix, bin_dense
 
     world, rank = dist.get_world_size(), dist.get_rank()
-    obj = list(cuts_dense(x, max_bin)) if rank == 0 else [None, None]
+    obj = list(whole_matrix_cuts(x, max_bin, device)) if rank == 0 else [None, None]
     dist.broadcast_object_list(obj, src=0)
     off, cuts = obj
     begin, end = shard_bounds(x.shape[0], world, rank)
@@ -82,7 +98,7 @@ def train_sharded(params, x, y, rounds, dist, device=None):
     if device is None:
         device = torch.cuda.current_device()
     n = x.shape[0]
-    shard, begin, end = shard_matrix(dist, x, params.max_bin)
+    shard, begin, end = shard_matrix(dist, x, params.max_bin, device)
     y = np.ascontiguousarray(y, np.float32)
     base = base_margin(params, y)
     eng = Engine(device)
