@@ -843,21 +843,44 @@ __global__ void __launch_bounds__(kH32Threads, 1)
     fold();
     __syncthreads();
     since_fold = 0;
-    longlong2* dst = hist + (uint64_t)en.slot * c.total_bins;
+    // Flush: stage the entry's sums feature-major in the (now zero)
+    // accumulator arrays, row = group-local feature, bins XOR-swizzled by
+    // row / 4 against bank conflicts; then each warp adds one feature's
+    // (g, h) words to the node histogram, 32 consecutive 8-byte words (256
+    // contiguous bytes) per 64-bit red instruction.
+    {
+      constexpr int kNB = 1 << kBS;  // bins per feature row
+      long long* stg = reinterpret_cast<long long*>(s32);
 #pragma unroll
-    for (int j = 0; j < kSlotsPerThread; ++j) {
-      const int slot = slot_of(j);
-      const int lgs = slot >> (kBS + 5), bin = (slot >> 5) & ((1 << kBS) - 1), fl = slot & 31;
-      const int f = (g0 + lgs) * kGroupFeatures + fl;
-      if (lgs < ng && f < (int)c.n_cols) {
+      for (int j = 0; j < kSlotsPerThread; ++j) {
+        const int slot = slot_of(j);
+        const int row = ((slot >> (kBS + 5)) << 5) | (slot & 31);
+        const int bin = (slot >> 5) & (kNB - 1);
+        const int at = 2 * (row * kNB + (bin ^ ((row >> 2) & 7)));
+        stg[at] = acc_g[j];
+        stg[at + 1] = acc_h[j];
+        acc_g[j] = acc_h[j] = 0;
+      }
+      __syncthreads();
+      unsigned long long* dstw = reinterpret_cast<unsigned long long*>(hist + (uint64_t)en.slot * c.total_bins);
+      const int warp = tid >> 5;
+      for (int row = warp; row < G * 32; row += kH32Threads / 32) {
+        const int lgs = row >> 5;
+        const int f = (g0 + lgs) * kGroupFeatures + (row & 31);
+        if (lgs >= ng || f >= (int)c.n_cols) continue;
         const uint32_t fs = fo[f];
-        const uint32_t nb = fo[f + 1] - fs;
-        if ((uint32_t)bin < nb) {
-          if (acc_g[j]) atomicAdd(reinterpret_cast<unsigned long long*>(&dst[fs + bin].x), (unsigned long long)acc_g[j]);
-          if (acc_h[j]) atomicAdd(reinterpret_cast<unsigned long long*>(&dst[fs + bin].y), (unsigned long long)acc_h[j]);
+        const uint32_t nw = 2 * (fo[f + 1] - fs);
+        for (uint32_t w = lane; w < nw; w += 32) {
+          const int bin = (int)(w >> 1);
+          const long long v = stg[2 * (row * kNB + (bin ^ ((row >> 2) & 7))) + (w & 1)];
+          if (v) atomicAdd(dstw + 2 * (uint64_t)fs + w, (unsigned long long)v);
         }
       }
-      acc_g[j] = acc_h[j] = 0;
+      __syncthreads();
+      // the accumulators start the next entry at zero
+      uint4* z = reinterpret_cast<uint4*>(s32);
+      for (int i = tid; i < kSlotStride; i += kH32Threads) z[i] = make_uint4(0u, 0u, 0u, 0u);
+      __syncthreads();
     }
     pos = end_e;
     ++e;
