@@ -198,8 +198,12 @@ struct hb_predictor {
   int n_outputs = 1;
   uint32_t n_features = 0;
   int n_sm = 148;
-  float* stage_x = nullptr;
-  float* stage_out = nullptr;
+  // host-row prediction: two staging sets, block b on stream b & 1 (the
+  // predictor's stream and a second one), so one block's copies overlap
+  // the other's kernel
+  cudaStream_t stream2 = nullptr;
+  float* stage_x[2] = {nullptr, nullptr};
+  float* stage_out[2] = {nullptr, nullptr};
   size_t stage_rows = 0;
   // the complete-tree layout (empty when the forest does not qualify)
   unsigned char* carena = nullptr;
@@ -412,12 +416,16 @@ hb_status hb_predictor_destroy(hb_predictor* p) {
   cudaFree(p->ostart);
   cudaFree(p->weights);
   cudaFree(p->base);
-  cudaFree(p->stage_x);
-  cudaFree(p->stage_out);
+  if (p->stream2) cudaStreamSynchronize(p->stream2);
+  for (int b = 0; b < 2; ++b) {
+    cudaFree(p->stage_x[b]);
+    cudaFree(p->stage_out[b]);
+  }
   cudaFree(p->carena);
   cudaFree(p->chunks);
   cudaFree(p->theads);
   if (p->stream) cudaStreamDestroy(p->stream);
+  if (p->stream2) cudaStreamDestroy(p->stream2);
   delete p;
   return HB_OK;
 }
@@ -442,34 +450,48 @@ hb_status hb_predict_margin_device(hb_predictor* p, const float* d_rows, uint64_
   return cudaGetLastError() == cudaSuccess ? HB_OK : HB_DEVICE_FAILED;
 }
 
-// Host rows in, host margins out: blocks of rows copied in, predicted and
-// copied back on the predictor's stream (GpuModel::predict_margin, :401).
+// Host rows in, host margins out (GpuModel::predict_margin, :401): blocks of
+// rows copied in, predicted and copied back, alternating between two
+// streams and two staging sets so that a block's transfers overlap the
+// neighbouring block's kernel (with pageable host memory the copies are
+// staged by the driver and overlap less). Returns once every margin is back.
 hb_status hb_predict_margin(hb_predictor* p, const float* rows, uint64_t n_rows, float* out) {
   if (!p || (!rows && n_rows) || (!out && n_rows)) return HB_INVALID_ARGUMENT;
   if (cudaSetDevice(p->device) != cudaSuccess) return HB_DEVICE_FAILED;
-  const uint64_t block = 1ull << 22;
+  const uint64_t block = 1ull << 21;
   const uint64_t want = std::min<uint64_t>(std::max<uint64_t>(n_rows, 1), block);
+  if (!p->stream2 && cudaStreamCreateWithFlags(&p->stream2, cudaStreamNonBlocking) != cudaSuccess)
+    return HB_DEVICE_FAILED;
   if (p->stage_rows < want) {
-    cudaFree(p->stage_x);
-    cudaFree(p->stage_out);
-    p->stage_x = p->stage_out = nullptr;
-    if (cudaMalloc(&p->stage_x, 4 * want * p->n_features) != cudaSuccess ||
-        cudaMalloc(&p->stage_out, 4 * want * p->n_outputs) != cudaSuccess)
-      return HB_DEVICE_FAILED;
+    for (int b = 0; b < 2; ++b) {
+      cudaFree(p->stage_x[b]);
+      cudaFree(p->stage_out[b]);
+      p->stage_x[b] = p->stage_out[b] = nullptr;
+    }
+    p->stage_rows = 0;
+    for (int b = 0; b < 2; ++b)
+      if (cudaMalloc(&p->stage_x[b], 4 * want * p->n_features) != cudaSuccess ||
+          cudaMalloc(&p->stage_out[b], 4 * want * p->n_outputs) != cudaSuccess)
+        return HB_DEVICE_FAILED;
     p->stage_rows = want;
   }
-  for (uint64_t at = 0; at < n_rows; at += block) {
+  uint64_t k = 0;
+  for (uint64_t at = 0; at < n_rows; at += block, ++k) {
+    const int b = (int)(k & 1);
+    cudaStream_t s = b ? p->stream2 : p->stream;
     const uint64_t m = std::min(block, n_rows - at);
-    if (cudaMemcpyAsync(p->stage_x, rows + at * p->n_features, 4 * m * p->n_features,
-                        cudaMemcpyHostToDevice, p->stream) != cudaSuccess)
+    if (cudaMemcpyAsync(p->stage_x[b], rows + at * p->n_features, 4 * m * p->n_features,
+                        cudaMemcpyHostToDevice, s) != cudaSuccess)
       return HB_DEVICE_FAILED;
-    hb_status st = hb_predict_margin_device(p, p->stage_x, m, p->stage_out, p->stream);
+    hb_status st = hb_predict_margin_device(p, p->stage_x[b], m, p->stage_out[b], s);
     if (st != HB_OK) return st;
-    if (cudaMemcpyAsync(out + at * p->n_outputs, p->stage_out, 4 * m * p->n_outputs,
-                        cudaMemcpyDeviceToHost, p->stream) != cudaSuccess)
+    if (cudaMemcpyAsync(out + at * p->n_outputs, p->stage_out[b], 4 * m * p->n_outputs,
+                        cudaMemcpyDeviceToHost, s) != cudaSuccess)
       return HB_DEVICE_FAILED;
   }
-  return cudaStreamSynchronize(p->stream) == cudaSuccess ? HB_OK : HB_DEVICE_FAILED;
+  const bool ok = cudaStreamSynchronize(p->stream) == cudaSuccess &&
+                  cudaStreamSynchronize(p->stream2) == cudaSuccess;
+  return ok ? HB_OK : HB_DEVICE_FAILED;
 }
 
 }  // extern "C"

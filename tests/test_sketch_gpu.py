@@ -84,6 +84,15 @@ def test_sketch_repeats_and_runs():
     _check_dense(x, 16)
 
 
+def test_sketch_many_features():
+    # 70 features (three feature groups of the index), mixed missing rates
+    rng = np.random.default_rng(21)
+    x = rng.standard_normal((40_000, 70)).astype(np.float32)
+    x[:, ::3] = np.round(x[:, ::3] * 4)            # repeated values
+    x[rng.random(x.shape) < np.linspace(0.0, 0.5, 70)] = np.nan
+    _check_dense(x, 256)
+
+
 def test_sketch_tiny_and_ragged():
     rng = np.random.default_rng(11)
     for n in (1, 2, 3, 7, 64, 65, 257):
@@ -156,10 +165,6 @@ def test_sketch_csr_rejects():
     assert e.value.status == H.HB_INVALID_ARGUMENT
 
 
-def _forest(nodes, ptr):
-    return nodes, np.asarray(ptr, np.uint64)
-
-
 def _assert_same(a_nodes, a_ptr, b_nodes, b_ptr):
     np.testing.assert_array_equal(np.asarray(a_ptr, np.uint64), np.asarray(b_ptr, np.uint64))
     for k in ("left", "right", "split_feature", "default_left", "split_bin"):
@@ -180,6 +185,17 @@ def test_engine_upload_dense_trains_like_host_index():
     finally:
         eng.close()
     _assert_same(nodes, ptr, host.nodes, host.tree_ptr)
+
+
+def test_engine_upload_dense_many_features_trains_like_host_index():
+    rng = np.random.default_rng(8)
+    x = rng.standard_normal((60_000, 70)).astype(np.float32)
+    x[rng.random(x.shape) < 0.05] = np.nan
+    y = (np.nan_to_num(x[:, :5]).sum(1) + 0.1 * rng.standard_normal(60_000)).astype(np.float32)
+    params = H.TrainingParams(objective="reg:squarederror", max_depth=5, eta=0.3)
+    host = H.train(params, y=y, rounds=3, device=0, matrix=H.BinnedMatrix.from_dense(x, 256))
+    dev = H.train(params, x, y, rounds=3, device=0)  # sketches and bins on the device
+    _assert_same(dev.nodes, dev.tree_ptr, host.nodes, host.tree_ptr)
 
 
 def test_engine_upload_csr_trains_like_host_index():
