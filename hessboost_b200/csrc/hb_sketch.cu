@@ -417,18 +417,38 @@ struct FeatPlan {
   uint32_t limit;
   uint32_t n_levels;     // level buffers in the pool
   uint64_t pool;         // SEntry offset: n_levels + 2 buffers of 2 * limit
+  uint32_t fin_begin;    // the merge tree's level summaries the final summary
+  uint32_t fin_count;    //   combines (FinItem), lowest level first
 };
+
+// One summary of the merge tree: its SEntry offset and the index of its
+// length.
+struct FinItem {
+  uint64_t off;
+  uint32_t len;
+  uint32_t pad;
+};
+
+// One merge of the tree: V = P(C(A, B)) with A the newer block (2j + 1), B
+// the older (2j), into `out`; `w` is scratch of 2 * limit entries.
+struct MergeTask {
+  uint32_t f, limit;
+  uint32_t la, lb, lo, pad;  // indices of the lengths of A, B, out
+  uint64_t a, b, out, w;
+};
+
+
 
 // WQSummary::SetCombine (sketch.rs:217) of A and B into O, then FixError
 // (:180). Values within a summary are strictly ascending, so entry a of A
 // lands after the |B < a| entries of B and the merged pairs before it; an
 // unmerged entry takes its rank bounds from its neighbours in the other
 // summary exactly as the sequential merge would. Returns |O|.
+template <int T>
 __device__ uint32_t combine_block(const SEntry* A, uint32_t na, const SEntry* B, uint32_t nb,
                                   SEntry* O, uint32_t* cnt, uint32_t* eq,
-                                  cub::BlockScan<uint32_t, kLadderThreads>::TempStorage& us,
-                                  cub::BlockScan<float, kLadderThreads>::TempStorage& fs) {
-  const int T = kLadderThreads;
+                                  typename cub::BlockScan<uint32_t, T>::TempStorage& us,
+                                  typename cub::BlockScan<float, T>::TempStorage& fs) {
   if (nb == 0 || na == 0) {
     const SEntry* src = nb == 0 ? A : B;
     const uint32_t n = nb == 0 ? na : nb;
@@ -498,14 +518,45 @@ __device__ uint32_t combine_block(const SEntry* A, uint32_t na, const SEntry* B,
   return no;
 }
 
+template <int T>
 __device__ uint32_t prune_global(const SEntry* src, uint32_t n, uint32_t maxsize, SEntry* dst,
-                                 uint32_t* ik,
-                                 cub::BlockScan<uint32_t, kLadderThreads>::TempStorage& us) {
-  const uint32_t len = prune_block<kLadderThreads>(
+                                 uint32_t* ik, typename cub::BlockScan<uint32_t, T>::TempStorage& us) {
+  const uint32_t len = prune_block<T>(
       n, maxsize, [&](uint32_t i) { return src[i]; },
       [&](uint32_t j, const SEntry& e) { dst[j] = e; }, ik, us);
   __syncthreads();
   return len;
+}
+
+constexpr int kMergeThreads = 512;
+
+// The ladder as a merge tree (one launch per level, every feature's merges
+// at once). While every merge the reference's push_summary performs holds
+// more than `limit` entries, each one carries, and level l of the ladder
+// then holds exactly V_l(j) = prune(combine(V_{l-1}(2j+1), V_{l-1}(2j)))
+// for the block of 2^l flushes its set bit stands for. A merge of `limit`
+// or fewer entries would not have carried: it flags its feature, whose
+// ladder k_sk_ladder then replays in order instead.
+__global__ void __launch_bounds__(kMergeThreads)
+    k_sk_merge(const MergeTask* __restrict__ tasks, SEntry* __restrict__ store,
+               uint32_t* __restrict__ lens, int* __restrict__ bad) {
+  using UScan = cub::BlockScan<uint32_t, kMergeThreads>;
+  using FScan = cub::BlockScan<float, kMergeThreads>;
+  __shared__ typename UScan::TempStorage us;
+  __shared__ typename FScan::TempStorage fs;
+  extern __shared__ __align__(16) uint32_t dyn[];
+  const MergeTask t = tasks[blockIdx.x];
+  uint32_t* cnt = dyn;
+  uint32_t* eq = dyn + (t.limit + 1);
+  uint32_t* ik = dyn + 2 * (t.limit + 1);
+  const uint32_t na = lens[t.la], nb = lens[t.lb];
+  SEntry* w = store + t.w;
+  const uint32_t m = combine_block<kMergeThreads>(store + t.a, na, store + t.b, nb, w, cnt, eq, us, fs);
+  if (m <= t.limit) {
+    if (threadIdx.x == 0) atomicOr(&bad[t.f], 1);
+  }
+  const uint32_t len = prune_global<kMergeThreads>(w, m, t.limit, store + t.out, ik, us);
+  if (threadIdx.x == 0) lens[t.lo] = len;
 }
 
 // WQSummary::QueryCutValues (sketch.rs:427), sequential.
@@ -560,7 +611,8 @@ __global__ void __launch_bounds__(kLadderThreads, 1)
     k_sk_ladder(const FeatPlan* __restrict__ plans, const Chunk* __restrict__ chunks,
                 const SEntry* __restrict__ temps, const uint32_t* __restrict__ temp_len,
                 SEntry* __restrict__ pool, uint32_t max_bin, float* __restrict__ cuts,
-                uint32_t* __restrict__ n_cuts, int* __restrict__ err) {
+                uint32_t* __restrict__ n_cuts, int* __restrict__ err, const int* __restrict__ bad,
+                const FinItem* __restrict__ fin) {
   using UScan = cub::BlockScan<uint32_t, kLadderThreads>;
   using FScan = cub::BlockScan<float, kLadderThreads>;
   __shared__ typename UScan::TempStorage us;
@@ -577,6 +629,30 @@ __global__ void __launch_bounds__(kLadderThreads, 1)
   auto level = [&](uint32_t l) { return base + l * cap; };
   SEntry* W0 = base + (uint64_t)p.n_levels * cap;
   SEntry* W1 = W0 + cap;
+  if (!bad[blockIdx.x]) {
+    // every merge carried: the ladder's levels are the merge tree's
+    // summaries of the flush count's set bits; summary() combines them from
+    // the lowest level up
+    uint32_t outlen = 0;
+    for (uint32_t k = 0; k < p.fin_count; ++k) {
+      const FinItem it = fin[p.fin_begin + k];
+      const uint32_t ll = temp_len[it.len];
+      if (ll == 0) continue;
+      if (outlen == 0) {
+        for (uint32_t i = threadIdx.x; i < ll; i += blockDim.x) W1[i] = temps[it.off + i];
+        __syncthreads();
+        outlen = ll;
+        continue;
+      }
+      const uint32_t m = combine_block<kLadderThreads>(W1, outlen, temps + it.off, ll, W0, cnt, eq, us, fs);
+      outlen = prune_global<kLadderThreads>(W0, m, L, W1, ik, us);
+    }
+    if (threadIdx.x == 0) {
+      const uint32_t mb = min(outlen, max_bin);
+      n_cuts[blockIdx.x] = query_cuts(W1, outlen, mb, cuts + (uint64_t)blockIdx.x * max_bin);
+    }
+    return;
+  }
   for (uint32_t l = threadIdx.x; l < kMaxLevels; l += blockDim.x) lvl_len[l] = 0;
   __syncthreads();
   uint32_t used = 0;  // levels ever touched
@@ -591,7 +667,7 @@ __global__ void __launch_bounds__(kLadderThreads, 1)
       }
       used = max(used, l + 1);
       if (l > 0) {
-        curlen = prune_global(cur, curlen, L, W1, ik, us);
+        curlen = prune_global<kLadderThreads>(cur, curlen, L, W1, ik, us);
         cur = W1;
       }
       const uint32_t ll = lvl_len[l];
@@ -602,7 +678,7 @@ __global__ void __launch_bounds__(kLadderThreads, 1)
         __syncthreads();
         break;
       }
-      curlen = combine_block(cur, curlen, level(l), ll, W0, cnt, eq, us, fs);
+      curlen = combine_block<kLadderThreads>(cur, curlen, level(l), ll, W0, cnt, eq, us, fs);
       cur = W0;
       if (curlen <= L) {
         for (uint32_t i = threadIdx.x; i < curlen; i += blockDim.x) level(l)[i] = cur[i];
@@ -626,8 +702,8 @@ __global__ void __launch_bounds__(kLadderThreads, 1)
       outlen = ll;
       continue;
     }
-    const uint32_t m = combine_block(W1, outlen, level(l), ll, W0, cnt, eq, us, fs);
-    outlen = prune_global(W0, m, L, W1, ik, us);
+    const uint32_t m = combine_block<kLadderThreads>(W1, outlen, level(l), ll, W0, cnt, eq, us, fs);
+    outlen = prune_global<kLadderThreads>(W0, m, L, W1, ik, us);
   }
   if (threadIdx.x == 0) {
     const uint32_t mb = min(outlen, max_bin);
@@ -821,6 +897,69 @@ hb_status sketch_streams(const float* d_vals, const std::vector<uint64_t>& S, ui
     why = "a queue larger than one CTA sorts (max_bin above 256)";
     return HB_REFUSED;
   }
+  // The merge tree: V_l(j) (l >= 1) of every complete block of 2^l flushes,
+  // stored after the flushes' summaries (`store`), lengths after theirs
+  // (`lens`); per level the merges of every feature, each with its own
+  // scratch; per feature the summaries of its flush count's set bits.
+  std::vector<std::vector<MergeTask>> levels;
+  std::vector<FinItem> fin;
+  uint64_t vstore = 0;
+  uint32_t n_lens = n_chunks;
+  uint64_t wmax = 0;
+  {
+    std::vector<uint64_t> wlevel;
+    for (uint32_t f = 0; f < F; ++f) {
+      FeatPlan& p = plans[f];
+      const uint32_t C = p.n_chunks, L = p.limit;
+      // offsets and length indices of V_l(j), l >= 1, of this feature
+      std::vector<uint64_t> off_l(1, 0);
+      std::vector<uint32_t> len_l(1, 0);
+      uint64_t at = temp_total + vstore;
+      uint32_t li = n_lens;
+      for (uint32_t l = 1; (C >> l) > 0; ++l) {
+        off_l.push_back(at);
+        len_l.push_back(li);
+        at += (uint64_t)(C >> l) * L;
+        li += C >> l;
+      }
+      auto v_off = [&](uint32_t l, uint32_t j) -> uint64_t {
+        return l == 0 ? hch[p.chunk_begin + j].out : off_l[l] + (uint64_t)j * L;
+      };
+      auto v_len = [&](uint32_t l, uint32_t j) -> uint32_t {
+        return l == 0 ? p.chunk_begin + j : len_l[l] + j;
+      };
+      for (uint32_t l = 1; (C >> l) > 0; ++l) {
+        if (levels.size() < l) levels.emplace_back(), wlevel.push_back(0);
+        for (uint32_t j = 0; j < (C >> l); ++j) {
+          MergeTask t{};
+          t.f = f;
+          t.limit = L;
+          t.a = v_off(l - 1, 2 * j + 1);
+          t.la = v_len(l - 1, 2 * j + 1);
+          t.b = v_off(l - 1, 2 * j);
+          t.lb = v_len(l - 1, 2 * j);
+          t.out = v_off(l, j);
+          t.lo = v_len(l, j);
+          t.w = wlevel[l - 1];  // relative; the scratch base is added below
+          wlevel[l - 1] += 2ull * L;
+          levels[l - 1].push_back(t);
+        }
+      }
+      p.fin_begin = (uint32_t)fin.size();
+      for (uint32_t l = 0; (C >> l) > 0; ++l)
+        if ((C >> l) & 1u) {
+          const uint32_t j = (C >> (l + 1)) << 1;
+          fin.push_back(FinItem{v_off(l, j), v_len(l, j), 0u});
+        }
+      p.fin_count = (uint32_t)fin.size() - p.fin_begin;
+      vstore = at - temp_total;
+      n_lens = li;
+    }
+    for (uint64_t w : wlevel) wmax = std::max(wmax, w);
+  }
+  const uint64_t wbase = temp_total + vstore;
+  for (auto& lv : levels)
+    for (auto& t : lv) t.w += wbase;
   Chunk* dch;
   FeatPlan* dplans;
   SEntry *temps, *pool;
@@ -829,8 +968,15 @@ hb_status sketch_streams(const float* d_vals, const std::vector<uint64_t>& S, ui
   int* err;
   SK_CK(sc.get(&dch, n_chunks));
   SK_CK(sc.get(&dplans, F));
-  SK_CK(sc.get(&temps, temp_total));
-  SK_CK(sc.get(&temp_len, n_chunks));
+  SK_CK(sc.get(&temps, temp_total + vstore + wmax));
+  SK_CK(sc.get(&temp_len, n_lens));
+  int* bad;
+  FinItem* dfin;
+  SK_CK(sc.get(&bad, F));
+  SK_CK(sc.get(&dfin, std::max<size_t>(fin.size(), 1)));
+  SK_CK(cudaMemsetAsync(bad, 0, 4 * (size_t)F, s));
+  if (!fin.empty())
+    SK_CK(cudaMemcpyAsync(dfin, fin.data(), sizeof(FinItem) * fin.size(), cudaMemcpyHostToDevice, s));
   SK_CK(sc.get(&pool, pool_total));
   SK_CK(sc.get(&dcuts, (uint64_t)F * max_bin));
   SK_CK(sc.get(&ncuts, F));
@@ -848,8 +994,26 @@ hb_status sketch_streams(const float* d_vals, const std::vector<uint64_t>& S, ui
     SK_CK(e);
   }
   const size_t dsm = (size_t)3 * (limit_max + 1) * 4;
+  if (!levels.empty()) {
+    size_t n_tasks = 0;
+    for (const auto& lv : levels) n_tasks += lv.size();
+    std::vector<MergeTask> flat;
+    flat.reserve(n_tasks);
+    for (const auto& lv : levels) flat.insert(flat.end(), lv.begin(), lv.end());
+    MergeTask* dtasks;
+    SK_CK(sc.get(&dtasks, n_tasks));
+    SK_CK(cudaMemcpyAsync(dtasks, flat.data(), sizeof(MergeTask) * n_tasks, cudaMemcpyHostToDevice, s));
+    SK_CK(cudaFuncSetAttribute(k_sk_merge, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)dsm));
+    size_t at = 0;
+    for (const auto& lv : levels) {  // one launch per tree level, in order
+      k_sk_merge<<<(unsigned)lv.size(), kMergeThreads, dsm, s>>>(dtasks + at, temps, temp_len, bad);
+      SK_CK(cudaGetLastError());
+      at += lv.size();
+    }
+  }
   SK_CK(cudaFuncSetAttribute(k_sk_ladder, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)dsm));
-  k_sk_ladder<<<F, kLadderThreads, dsm, s>>>(dplans, dch, temps, temp_len, pool, max_bin, dcuts, ncuts, err);
+  k_sk_ladder<<<F, kLadderThreads, dsm, s>>>(dplans, dch, temps, temp_len, pool, max_bin, dcuts, ncuts, err,
+                                             bad, dfin);
   SK_CK(cudaGetLastError());
   std::vector<float> hc((size_t)F * max_bin);
   std::vector<uint32_t> hn(F);

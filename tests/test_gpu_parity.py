@@ -122,6 +122,12 @@ CASES = {
                          kw=dict(objective="binary:logistic", max_depth=5, eta=0.1)),
     "wide_bins64": dict(gen=lambda: synth.logistic_c2(600_003, 70, seed=13), rounds=1,
                         kw=dict(objective="binary:logistic", max_depth=5, eta=0.1, max_bin=64)),
+    # narrow last groups (<= 8 features, accumulated in column copies): 4
+    # features (C3's 100 at 128 bins, two groups per CTA) and 1 feature
+    "narrow_group4": dict(gen=lambda: synth.logistic_c2(600_003, 100, seed=18), rounds=1,
+                          kw=dict(objective="binary:logistic", max_depth=4, eta=0.1, max_bin=128)),
+    "narrow_group1": dict(gen=lambda: synth.logistic_c2(600_003, 33, seed=19), rounds=1,
+                          kw=dict(objective="binary:logistic", max_depth=4, eta=0.1)),
     # lossguide growth (best loss change first): by max_leaves, by max_depth
     # alone (2^max_depth leaves), both, with regularisation leaving nodes
     # unexpandable, a tiny ragged set, and the 32-bit histogram kernel
