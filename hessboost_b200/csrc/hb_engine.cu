@@ -128,6 +128,7 @@ struct hb_engine {
   ncclComm_t comm = nullptr;
   int nranks = 1, rank = 0;
   uint64_t row_begin = 0;
+  uint64_t shard_global = 0;  // rows of the whole matrix when this engine holds a shard (0: not sharded)
 
   // timing and counters (hb_engine_get_stats)
   bool timing = false;
@@ -812,7 +813,7 @@ static hb_status upload_index(hb_engine* e, const hb_ghist* g, const RawSource* 
   if (g->n_rows >= (1ull << 32)) return refuse(e, "at most 2^32 - 1 rows per device");
   if (!csr && g->n_cols > 224) return refuse(e, "at most 224 features per device index");
   DevConst& c = e->c;
-  const uint64_t shard_rows = c.global_rows;
+  const uint64_t shard_rows = e->shard_global;
   c = DevConst{};
   c.n_rows = g->n_rows;
   c.global_rows = shard_rows > g->n_rows ? shard_rows : g->n_rows;
@@ -931,6 +932,9 @@ hb_status hb_engine_upload_dense(hb_engine* e, const float* x, uint64_t n_rows, 
   HB_ENTER(e);
   if (!x || !feature_offset || !cut_values || !total || n_rows == 0 || n_cols == 0 || max_bin == 0)
     return HB_INVALID_ARGUMENT;
+  if (e->comm || e->shard_global > n_rows)
+    return refuse(e, "a row shard needs the whole matrix's cuts: hb_sketch_dense of the whole "
+                     "matrix, then hb_bin_dense of the shard and hb_engine_upload");
   if (n_rows >= (1ull << 32)) return refuse(e, "at most 2^32 - 1 rows per device");
   if (n_cols > 224) return refuse(e, "at most 224 features per device index");
   cudaStream_t s = e->stream;
@@ -964,6 +968,9 @@ hb_status hb_engine_upload_csr(hb_engine* e, const uint64_t* indptr, const uint3
   if (!indptr || !feature_offset || !cut_values || !total || n_rows == 0 || n_cols == 0 ||
       max_bin == 0 || indptr[0] != 0)
     return HB_INVALID_ARGUMENT;
+  if (e->comm || e->shard_global > n_rows)
+    return refuse(e, "a row shard needs the whole matrix's cuts: hb_sketch_csr of the whole "
+                     "matrix, then hb_bin_csr of the shard and hb_engine_upload");
   if (n_rows >= (1ull << 32)) return refuse(e, "at most 2^32 - 1 rows per device");
   const uint64_t nnz = indptr[n_rows];
   if (nnz && (!indices || !values)) return HB_INVALID_ARGUMENT;
@@ -1854,6 +1861,7 @@ hb_status hb_comm_init(hb_engine* e, int32_t nranks, int32_t rank, const uint8_t
   HB_NCCL(e, ncclCommInitRank(&e->comm, nranks, u, rank));
   e->nranks = nranks;
   e->rank = rank;
+  e->shard_global = global_rows;
   e->c.global_rows = global_rows;
   return HB_OK;
 }
@@ -1864,6 +1872,7 @@ extern "C" hb_status hb_engine_set_shard(hb_engine* e, uint64_t row_begin, uint6
   HB_ENTER(e);
   if (row_begin % 8) return refuse(e, "shards must start on a multiple of 8 rows");
   e->row_begin = row_begin;
+  e->shard_global = global_rows;
   e->c.global_rows = global_rows;
   return HB_OK;
 }

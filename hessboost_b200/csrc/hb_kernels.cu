@@ -69,9 +69,9 @@ __device__ __forceinline__ float exp_vector(float v) {
 __device__ __forceinline__ float sigmoid_vector(float v) {
   float e = exp_vector(__fsub_rn(0.0f, fabsf(v)));
   float den = __fadd_rn(1.0f, e);
-  float pos = __fdiv_rn(1.0f, den);
-  float neg = __fdiv_rn(e, den);
-  return v >= 0.0f ? pos : neg;
+  // 1 / den for v >= 0, e / den otherwise: one correctly rounded division of
+  // the selected numerator (the same result as dividing both and selecting)
+  return __fdiv_rn(v >= 0.0f ? 1.0f : e, den);
 }
 
 // src/simd/mod.rs:421 `sigmoid_scalar`, 1 / (expf(min(-x, 88.7)) + 1). The

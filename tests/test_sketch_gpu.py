@@ -211,3 +211,31 @@ def test_engine_upload_csr_trains_like_host_index():
     finally:
         eng.close()
     _assert_same(nodes, ptr, host.nodes, host.tree_ptr)
+
+
+def test_engine_reupload_smaller_matrix_matches_fresh_engine():
+    # an engine keeps no row count from an earlier index: the fixed-point
+    # scale of the second index is its own
+    x, y = synth.logistic_c2(120_000, 28, seed=22)
+    params = H.TrainingParams(objective="binary:logistic", max_depth=5, eta=0.1)
+    fresh = H.train(params, x[:50_000], y[:50_000], rounds=2, device=0)
+    eng = H.Engine(0)
+    try:
+        eng.upload_dense(x, 256)
+        eng.upload_dense(x[:50_000], 256)
+        nodes, ptr = eng.train(params, y[:50_000], 2, H.base_margin(params, y[:50_000]))
+    finally:
+        eng.close()
+    _assert_same(nodes, ptr, fresh.nodes, fresh.tree_ptr)
+
+
+def test_engine_upload_dense_refused_on_a_shard():
+    x, _ = synth.logistic_c2(10_000, 8, seed=23)
+    eng = H.Engine(0)
+    try:
+        eng.set_shard(0, 20_000)  # these rows are half of a larger matrix
+        with pytest.raises(H.HbError) as e:
+            eng.upload_dense(x, 256)
+        assert e.value.status == H.HB_REFUSED
+    finally:
+        eng.close()
