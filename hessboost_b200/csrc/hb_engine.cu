@@ -564,7 +564,7 @@ hb_status grow_lossguide(hb_engine* e, const hb_train_params* p, bool to_forest)
     const bool final_step = k == L - 1;
     mark_begin(e, T_APPLY);
     launch_lg_step(c, e->fo.p, e->cuts.p, e->cand.p, k == 0 ? fr : nx, fr, nx, e->dec.p, ls1, ls2,
-                   e->tree.p, e->wtree.p, cur_scale(e), e->lg_heap.p, e->lg_state.p, e->lg_depth.p,
+                   e->tree.p, e->wtree.p, cur_scale(e), e->lg_heap.p, L + 2, e->lg_state.p, e->lg_depth.p,
                    max_leaves, depth_limit, final_step ? 1 : 0, s);
     mark_end(e);
     ++launches;

@@ -1470,7 +1470,8 @@ __global__ void __launch_bounds__(kApplyThreads)
 // Rust's BinaryHeap as the host builder uses it (push: sift_up; pop: swap
 // the last into the root, sift_down_to_bottom, sift_up), keyed by the
 // f64::total_cmp order of the best loss change.
-constexpr int kLgThreads = 64;  // two warps: one per pending node
+constexpr int kLgThreads = 512;  // 8 warps per pending node (at most two)
+constexpr int kLgWarpsPerNode = 8;
 
 __device__ __forceinline__ long long total_key(double v) {
   const long long b = __double_as_longlong(v);
@@ -1529,6 +1530,14 @@ __device__ void lg_leaf(const LgNode& e, const DevConst& c, double ig, double ih
   wtree[e.nid] = wn;
 }
 
+__device__ void lg_step_serial(const DevConst& c, const uint32_t* __restrict__ fo,
+                               const float* __restrict__ cuts, Front* front, Front* next,
+                               Decision* dec, LevelState* ls, LevelState* ls_next,
+                               hb_tree_node* __restrict__ tree, WNode* __restrict__ wtree, double ig,
+                               double ih, LgNode* heap, LgState* st, const LgState S0,
+                               const LgNode* s_new, int32_t* __restrict__ ndepth, int max_leaves,
+                               int depth_limit, int final_step, int& n_out);
+
 __global__ void __launch_bounds__(kLgThreads)
     k_lg_step(DevConst c, const uint32_t* __restrict__ fo, const float* __restrict__ cuts,
               const Cand* __restrict__ cand, const Front* __restrict__ pend, Front* front,
@@ -1537,18 +1546,33 @@ __global__ void __launch_bounds__(kLgThreads)
               const Scale* __restrict__ scale, LgNode* __restrict__ heap, LgState* st,
               int32_t* __restrict__ ndepth, int max_leaves, int depth_limit, int final_step) {
   __shared__ LgNode s_new[2];
+  __shared__ float s_bl[kLgThreads / 32];
+  __shared__ int s_bf[kLgThreads / 32];
+  __shared__ int s_n;
+  extern __shared__ __align__(16) unsigned char lg_dyn[];
+  LgNode* sheap = reinterpret_cast<LgNode*>(lg_dyn);  // the heap, worked in shared memory
   const LgState S0 = *st;
   if (S0.done) return;
   const double ig = scale->ig, ih = scale->ih;
   const int np = S0.n_pending;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  if (warp < np) {
-    // the node's best split over its features: the largest loss change
-    // above 0, the lowest feature among equals (need_replace, builder/mod.rs:313)
+  {  // bring the heap in (8-byte words, all threads)
+    const unsigned long long* src = reinterpret_cast<const unsigned long long*>(heap);
+    unsigned long long* dst = reinterpret_cast<unsigned long long*>(sheap);
+    const int words = S0.heap_n * (int)(sizeof(LgNode) / 8);
+    for (int i = threadIdx.x; i < words; i += kLgThreads) dst[i] = src[i];
+  }
+  // each pending node's best split over its features: the largest loss
+  // change above 0, the lowest feature among equals (need_replace,
+  // builder/mod.rs:313); kLgWarpsPerNode warps a node, each over every
+  // kLgWarpsPerNode-th block of 32 features, then the warps' results merged
+  // by the same rule (it is associative)
+  const int node = warp / kLgWarpsPerNode, sub = warp % kLgWarpsPerNode;
+  if (node < np) {
     float bl = 0.0f;
     int bf = -1;
-    for (uint32_t f = lane; f < c.n_cols; f += 32) {
-      const float l = cand[(uint64_t)warp * c.n_cols + f].loss;
+    for (uint32_t f = sub * 32 + lane; f < c.n_cols; f += 32 * kLgWarpsPerNode) {
+      const float l = cand[(uint64_t)node * c.n_cols + f].loss;
       if (l > bl) {
         bl = l;
         bf = (int)f;
@@ -1564,6 +1588,24 @@ __global__ void __launch_bounds__(kLgThreads)
       }
     }
     if (lane == 0) {
+      s_bl[warp] = bl;
+      s_bf[warp] = bf;
+    }
+  }
+  __syncthreads();
+  if (node < np && sub == 0 && lane == 0) {
+    float bl = s_bl[warp];
+    int bf = s_bf[warp];
+    for (int k = 1; k < kLgWarpsPerNode; ++k) {
+      const float ol = s_bl[warp + k];
+      const int of = s_bf[warp + k];
+      if (ol > bl || (ol == bl && of >= 0 && (bf < 0 || of < bf))) {
+        bl = ol;
+        bf = of;
+      }
+    }
+    {
+      const int warp = node;  // the pending node's index below
       const Front fr = pend[warp];
       LgNode x;
       x.nid = fr.node;
@@ -1592,7 +1634,28 @@ __global__ void __launch_bounds__(kLgThreads)
     }
   }
   __syncthreads();
-  if (threadIdx.x != 0) return;
+  if (threadIdx.x == 0) lg_step_serial(c, fo, cuts, front, next, dec, ls, ls_next, tree, wtree, ig, ih,
+                                       sheap, st, S0, s_new, ndepth, max_leaves, depth_limit, final_step, s_n);
+  __syncthreads();
+  {  // the heap back out
+    const unsigned long long* src = reinterpret_cast<const unsigned long long*>(sheap);
+    unsigned long long* dst = reinterpret_cast<unsigned long long*>(heap);
+    const int words = s_n * (int)(sizeof(LgNode) / 8);
+    for (int i = threadIdx.x; i < words; i += kLgThreads) dst[i] = src[i];
+  }
+}
+
+// The heap work of a lossguide step, one thread, on the shared copy of the
+// heap: the new children pushed, then pops in BinaryHeap order until one
+// node expands (its split, children, partition decision) or growth ends.
+__device__ void lg_step_serial(const DevConst& c, const uint32_t* __restrict__ fo,
+                               const float* __restrict__ cuts, Front* front, Front* next,
+                               Decision* dec, LevelState* ls, LevelState* ls_next,
+                               hb_tree_node* __restrict__ tree, WNode* __restrict__ wtree, double ig,
+                               double ih, LgNode* heap, LgState* st, const LgState S0,
+                               const LgNode* s_new, int32_t* __restrict__ ndepth, int max_leaves,
+                               int depth_limit, int final_step, int& n_out) {
+  const int np = S0.n_pending;
   LgState S = S0;
   int n = S.heap_n;
   for (int k = 0; k < np; ++k) {
@@ -1694,6 +1757,7 @@ __global__ void __launch_bounds__(kLgThreads)
   S.n_pending = expanded ? 2 : 0;
   *st = S;
   ls_next->n_nodes = S.n_nodes;
+  n_out = n;
 }
 
 // Lossguide state of a new tree: the root pending, one node, one leaf.
@@ -2263,11 +2327,21 @@ void launch_part_scatter(const Front* front, const Decision* dec, const PItem* i
 void launch_lg_step(const DevConst& c, const uint32_t* fo, const float* cuts, const Cand* cand,
                     const Front* pend, Front* front, Front* next, Decision* dec, LevelState* ls,
                     LevelState* ls_next, hb_tree_node* tree, WNode* wtree, const Scale* scale,
-                    LgNode* heap, LgState* st, int32_t* ndepth, int max_leaves, int depth_limit,
-                    int final_step, cudaStream_t s) {
-  k_lg_step<<<1, kLgThreads, 0, s>>>(c, fo, cuts, cand, pend, front, next, dec, ls, ls_next, tree,
-                                     wtree, scale, heap, st, ndepth, max_leaves, depth_limit,
-                                     final_step);
+                    LgNode* heap, int heap_cap, LgState* st, int32_t* ndepth, int max_leaves,
+                    int depth_limit, int final_step, cudaStream_t s) {
+  const size_t smem = sizeof(LgNode) * (size_t)heap_cap;
+  static size_t granted[64] = {0};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (smem > 48 * 1024 && (dev < 0 || dev >= 64 || granted[dev] < smem)) {
+    if (cudaFuncSetAttribute(k_lg_step, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) ==
+            cudaSuccess &&
+        dev >= 0 && dev < 64)
+      granted[dev] = smem;
+  }
+  k_lg_step<<<1, kLgThreads, smem, s>>>(c, fo, cuts, cand, pend, front, next, dec, ls, ls_next, tree,
+                                        wtree, scale, heap, st, ndepth, max_leaves, depth_limit,
+                                        final_step);
 }
 
 void launch_lg_setup(LgState* st, int32_t* ndepth, hb_tree_node* tree, const Front* root,
