@@ -570,13 +570,16 @@ hb_status grow_lossguide(hb_engine* e, const hb_train_params* p, bool to_forest)
     ++launches;
     if (final_step) break;
     mark_begin(e, T_PART);
+    // the count pass leaves a copy of the node's row ids in rows1, and the
+    // scatter writes the children from it back into rows0, where every
+    // pending node's rows stay
     launch_part_count(c, e->col.p, e->has_missing ? e->colmiss.p : nullptr, e->rec.p, 0, rows0, k == 0,
-                      fr, e->dec.p, e->items.p, ls1, e->max_items, e->dirbits.p, e->item_left.p, s);
+                      fr, e->dec.p, e->items.p, ls1, e->max_items, e->dirbits.p, e->item_left.p, s,
+                      rows1);
     launch_part_scan(fr, e->dec.p, ls1, 1, e->item_left.p, e->item_off.p, nx, e->entries.p,
                      e->pairs.p, ls2, s);
     launch_part_scatter(fr, e->dec.p, e->items.p, ls1, e->max_items, e->dirbits.p, e->item_off.p, nx,
-                        rows0, k == 0, rows1, s);
-    launch_lg_copy(fr, ls1, rows1, rows0, c.n_rows, e->n_sm, s);
+                        rows1, 0, rows0, s);
     mark_end(e);
     mark_begin(e, T_HIST);
     launch_hist(c, e->fo.p, e->rec.p, cur_gpair(e), cur_scale(e), rows0, e->entries.p, ls2, hist, nullptr,
@@ -585,7 +588,7 @@ hb_status grow_lossguide(hb_engine* e, const hb_train_params* p, bool to_forest)
     mark_begin(e, T_SCAN);
     launch_scan(c, e->fo.p, hist, nx, ls2, e->pairs.p, -1, cur_scale(e), 2, e->cand.p, s);
     mark_end(e);
-    launches += 6;
+    launches += 5;
     HB_CK(e, cudaGetLastError());
   }
   HB_CK(e, cudaMemsetAsync(e->flags.p, 0x01, sizeof(int), s));

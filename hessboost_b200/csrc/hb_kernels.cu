@@ -1775,15 +1775,6 @@ __global__ void k_lg_setup(LgState* st, int32_t* ndepth, hb_tree_node* tree, con
   ls_next->n_nodes = 1;
 }
 
-// After a lossguide partition (rows_in -> rows_out over the expanded node's
-// segment), copy the segment back so every node's rows stay in rows_in.
-__global__ void k_lg_copy(const Front* __restrict__ front, const LevelState* __restrict__ ls,
-                          const uint32_t* __restrict__ from, uint32_t* __restrict__ to) {
-  if (ls->n_items == 0) return;
-  const Front fr = front[0];
-  for (uint32_t i = blockIdx.x * blockDim.x + threadIdx.x; i < fr.len; i += gridDim.x * blockDim.x)
-    to[fr.begin + i] = from[fr.begin + i];
-}
 
 // ---------------------------------------------------------------------------
 // Stable partition (partition.rs:106, route_column :206): present local bin
@@ -1821,7 +1812,7 @@ __global__ void __launch_bounds__(kPartThreads)
                  const uint32_t* __restrict__ rows_in, int identity, const Front* __restrict__ front,
                  const Decision* __restrict__ dec, const PItem* __restrict__ items,
                  const LevelState* __restrict__ ls, uint32_t* __restrict__ dirbits,
-                 uint32_t* __restrict__ item_left) {
+                 uint32_t* __restrict__ item_left, uint32_t* __restrict__ rows_copy) {
   const int it = blockIdx.x;
   if (it >= ls->n_items) return;
   const PItem pi = locate_item(dec, ls->n_front, it, front);
@@ -1841,6 +1832,13 @@ __global__ void __launch_bounds__(kPartThreads)
     const uint32_t i = warp * 256 + j * 32 + lane;
     const uint32_t at = base + min(i, pi.len - 1);
     row[j] = identity ? at : rows_in[at];
+  }
+  if (rows_copy) {  // the tile's row ids, for a scatter that writes back in place
+#pragma unroll
+    for (int j = 0; j < kPerThread; ++j) {
+      const uint32_t i = warp * 256 + j * 32 + lane;
+      if (i < pi.len) rows_copy[base + i] = row[j];
+    }
   }
   uint32_t bin[kPerThread];
   bool miss[kPerThread];
@@ -2302,9 +2300,9 @@ void launch_part_count(const DevConst& c, const uint8_t* col, const uint64_t* co
                        const uint8_t* rec, int use_record, const uint32_t* rows_in, int identity,
                        const Front* front, const Decision* dec, const PItem* items,
                        const LevelState* ls, int max_items, uint32_t* dirbits, uint32_t* item_left,
-                       cudaStream_t s) {
+                       cudaStream_t s, uint32_t* rows_copy) {
   k_part_count<<<max_items, kPartThreads, 0, s>>>(c, col, colmiss, rec, use_record, rows_in, identity,
-                                                  front, dec, items, ls, dirbits, item_left);
+                                                  front, dec, items, ls, dirbits, item_left, rows_copy);
 }
 
 void launch_part_scan(const Front* front, const Decision* dec, LevelState* ls, int max_front,
@@ -2349,11 +2347,6 @@ void launch_lg_setup(LgState* st, int32_t* ndepth, hb_tree_node* tree, const Fro
   k_lg_setup<<<1, 1, 0, s>>>(st, ndepth, tree, root, scale, ls_next);
 }
 
-void launch_lg_copy(const Front* front, const LevelState* ls, const uint32_t* from, uint32_t* to,
-                    uint64_t n_rows, int n_sm, cudaStream_t s) {
-  const int grid = (int)std::max<uint64_t>(1, std::min<uint64_t>((n_rows + 255) / 256, (uint64_t)n_sm * 4));
-  k_lg_copy<<<grid, 256, 0, s>>>(front, ls, from, to);
-}
 
 void launch_root_setup(uint64_t n_rows, Front* front, HEntry* entries, LevelState* ls,
                        cudaStream_t s) {

@@ -68,7 +68,7 @@ void launch_part_count(const DevConst& c, const uint8_t* col, const uint64_t* co
                        const uint8_t* rec, int use_record, const uint32_t* rows_in, int identity,
                        const Front* front, const Decision* dec, const PItem* items,
                        const LevelState* ls, int max_items, uint32_t* dirbits, uint32_t* item_left,
-                       cudaStream_t s);
+                       cudaStream_t s, uint32_t* rows_copy = nullptr);
 // Per-node scan of the tiles' left counts and the children's segments; with
 // `entries` (device growth) the last CTA also plans the next level's
 // histograms (built child = smaller Hessian; entries, sibling pairs, ls_next).
@@ -90,8 +90,6 @@ void launch_lg_step(const DevConst& c, const uint32_t* fo, const float* cuts, co
                     int depth_limit, int final_step, cudaStream_t s);
 void launch_lg_setup(LgState* st, int32_t* ndepth, hb_tree_node* tree, const Front* root,
                      const Scale* scale, LevelState* ls_next, cudaStream_t s);
-void launch_lg_copy(const Front* front, const LevelState* ls, const uint32_t* from, uint32_t* to,
-                    uint64_t n_rows, int n_sm, cudaStream_t s);
 void launch_root_setup(uint64_t n_rows, Front* front, HEntry* entries, LevelState* ls,
                        cudaStream_t s);
 void launch_root_stats(Front* front, const long long* totals, cudaStream_t s);
