@@ -1806,6 +1806,7 @@ __device__ __forceinline__ PItem locate_item(const Decision* __restrict__ dec, i
 // in position order and its prefix needs no other warp until the end.
 constexpr int kPerThread = kTile / kPartThreads;  // 8
 
+template <bool CSR>
 __global__ void __launch_bounds__(kPartThreads)
     k_part_count(DevConst c, const uint8_t* __restrict__ col, const uint64_t* __restrict__ colmiss,
                  const uint8_t* __restrict__ rec, int use_record,
@@ -1847,7 +1848,7 @@ __global__ void __launch_bounds__(kPartThreads)
 #pragma unroll
   for (int j = 0; j < kPerThread; ++j) {
     const uint32_t r = row[j];
-    if (c.csr) {
+    if (CSR) {
       uint32_t lb = 0;
       miss[j] = !csr_find(c.csr_bins, __ldg(c.csr_ptr + r), __ldg(c.csr_ptr + r + 1), csr_lo, csr_hi, lb);
       bin[j] = lb;
@@ -2301,8 +2302,12 @@ void launch_part_count(const DevConst& c, const uint8_t* col, const uint64_t* co
                        const Front* front, const Decision* dec, const PItem* items,
                        const LevelState* ls, int max_items, uint32_t* dirbits, uint32_t* item_left,
                        cudaStream_t s, uint32_t* rows_copy) {
-  k_part_count<<<max_items, kPartThreads, 0, s>>>(c, col, colmiss, rec, use_record, rows_in, identity,
-                                                  front, dec, items, ls, dirbits, item_left, rows_copy);
+  if (c.csr)
+    k_part_count<true><<<max_items, kPartThreads, 0, s>>>(c, col, colmiss, rec, use_record, rows_in, identity,
+                                                        front, dec, items, ls, dirbits, item_left, rows_copy);
+  else
+    k_part_count<false><<<max_items, kPartThreads, 0, s>>>(c, col, colmiss, rec, use_record, rows_in, identity,
+                                                         front, dec, items, ls, dirbits, item_left, rows_copy);
 }
 
 void launch_part_scan(const Front* front, const Decision* dec, LevelState* ls, int max_front,
