@@ -1,9 +1,12 @@
 """The reference's own known answers for cuts, binning and histogram sum order
 (src/data/quantile.rs tests `few_distinct_values_one_bin_each`,
 `monotone_binning`, `constant_feature_has_one_bin`,
-`split_threshold_consistency`), checked against the CPU oracle and against
-the library's host binning (hb_cuts_dense / hb_bin_dense), which the device
-sketch equals bit for bit (tests/test_sketch_gpu.py)."""
+`split_threshold_consistency`; src/tree/hist/mod.rs tests
+`histograms_do_not_depend_on_the_thread_count`,
+`blocked_build_matches_the_block_order_reference`), checked against the CPU
+oracle and, for cuts and bins, against the library's host binning
+(hb_cuts_dense / hb_bin_dense), which the device sketch equals bit for bit
+(tests/test_sketch_gpu.py)."""
 
 import numpy as np
 import pytest
