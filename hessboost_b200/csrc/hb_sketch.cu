@@ -1175,7 +1175,8 @@ struct DevicePick {
   }
 };
 
-std::string g_sketch_error;
+// the calling thread's last sketch failure, as hb_engine_last_error(NULL) keeps its own
+thread_local std::string g_sketch_error;
 
 hb_status copy_cuts_out(const std::vector<uint32_t>& fo, const std::vector<float>& cuts, uint32_t F,
                         uint32_t* feature_offset, float* cut_values, uint64_t cap, uint64_t* total) {

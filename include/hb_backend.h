@@ -391,6 +391,8 @@ hb_status hb_sketch_csr(int32_t device, const uint64_t* indptr, const uint32_t* 
                         const float* values, uint64_t n_rows, uint32_t n_cols, uint32_t max_bin,
                         uint32_t* feature_offset, float* cut_values, uint64_t cap, uint64_t* total,
                         uint32_t* row_bins, int32_t* dense);
+/* The reason for the calling thread's last hb_sketch_* failure ("" after a
+ * success); valid until that thread's next hb_sketch_* call. */
 const char* hb_sketch_last_error(void);
 /* CudaHistBackend::new(index) for a raw host matrix: the engine copies it
  * to its device, sketches and bins it there into its resident index, and
