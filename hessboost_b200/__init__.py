@@ -249,6 +249,7 @@ SIGNATURES = {
     "hb_sketch_csr": [ctypes.c_int32, _u64p, _u32p, _f32p, ctypes.c_uint64, ctypes.c_uint32, ctypes.c_uint32, _u32p,
                       _f32p, ctypes.c_uint64, _u64p, _u32p, _i32p],
     "hb_sketch_last_error": [],
+    "hb_xxh64": [ctypes.c_void_p, ctypes.c_uint64, _u64p],
     "hb_engine_upload_dense": [_vp, _f32p, ctypes.c_uint64, ctypes.c_uint32, ctypes.c_uint32, _u32p, _f32p,
                                ctypes.c_uint64, _u64p],
     "hb_engine_upload_csr": [_vp, _u64p, _u32p, _f32p, ctypes.c_uint64, ctypes.c_uint32, ctypes.c_uint32, _u32p,
@@ -906,27 +907,43 @@ class Model:
         finally:
             p.close()
 
-    def save_native(self, path, params):
-        """Write the reference's native JSON model file (loads unchanged in
-        hessboost's Python and Rust APIs); `params` the TrainingParams the
-        model was trained with."""
-        from .model_io import to_native_json
+    def save_native(self, path, params, format="json"):
+        """Write the reference's native model file (loads unchanged in
+        hessboost's Python and Rust APIs): `format` "json" (the pretty
+        serde form) or "binary" (the checksummed section container as a
+        zstd frame, BoostedModel::save with ModelFormat::Binary); `params`
+        the TrainingParams the model was trained with."""
+        from . import model_io
 
         softmax = params.loss_kind() == HB_LOSS_SOFTMAX
-        text = to_native_json(self.nodes, self.tree_ptr, self.bases(), self.n_features,
-                              objective=params.objective, num_class=params.num_class if softmax else 0,
-                              scale_pos_weight=params.scale_pos_weight,
-                              max_delta_step=float(np.float32(params.max_delta_step)))
-        with open(path, "w") as fh:
-            fh.write(text)
+        kw = dict(objective=params.objective, num_class=params.num_class if softmax else 0,
+                  scale_pos_weight=params.scale_pos_weight,
+                  max_delta_step=float(np.float32(params.max_delta_step)))
+        if format == "json":
+            data = model_io.to_native_json(self.nodes, self.tree_ptr, self.bases(), self.n_features,
+                                           **kw).encode()
+        elif format == "binary":
+            data = model_io.to_native_binary(self.nodes, self.tree_ptr, self.bases(), self.n_features, **kw)
+        else:
+            raise ValueError(f"unknown model format {format!r} (json or binary)")
+        with open(path, "wb") as fh:
+            fh.write(data)
 
     @staticmethod
     def load_native(path):
-        """A gbtree model from a native JSON file (numeric scalar-leaf trees)."""
-        from .model_io import from_native_json
+        """A gbtree model (numeric scalar-leaf trees) from a native JSON or
+        binary file, told apart by their first bytes (ModelFormat::detect)."""
+        from . import model_io
 
-        with open(path) as fh:
-            nodes, ptr, base, nf, fields = from_native_json(fh.read())
+        with open(path, "rb") as fh:
+            data = fh.read()
+        kind = model_io.detect(data)
+        if kind == "binary":
+            nodes, ptr, base, nf, fields = model_io.from_native_binary(data)
+        elif kind == "json":
+            nodes, ptr, base, nf, fields = model_io.from_native_json(data.decode())
+        else:
+            raise ValueError(f"{path}: not a native hessboost model file")
         if fields.get("best_iteration") is not None:
             per = int(fields["n_outputs"]) * int(fields["num_parallel_tree"])
             n = (int(fields["best_iteration"]) + 1) * per

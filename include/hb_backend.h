@@ -13,8 +13,9 @@
  *
  * plus entry points the reference does not have: whole-tree growth on the
  * device (`hb_grow_tree`, `hb_train`), the row-sharded communicator
- * (`hb_comm_*`) and the host binning helpers (`hb_cuts_dense`,
- * `hb_bin_dense`, `hb_cuts_csr`, `hb_bin_csr`).
+ * (`hb_comm_*`), the host binning helpers (`hb_cuts_dense`,
+ * `hb_bin_dense`, `hb_cuts_csr`, `hb_bin_csr`) and the model-file checksum
+ * (`hb_xxh64`).
  *
  * Conventions (the reference's, src/tree/hist/mod.rs:107-212):
  *   - every call returns an hb_status; HB_REFUSED means "did not run"
@@ -406,6 +407,13 @@ hb_status hb_engine_upload_csr(hb_engine* e, const uint64_t* indptr, const uint3
                                const float* values, uint64_t n_rows, uint32_t n_cols,
                                uint32_t max_bin, uint32_t* feature_offset, float* cut_values,
                                uint64_t cap, uint64_t* total);
+
+/* ---- native binary model files (BoostedModel::encode/decode,
+ * src/model/native.rs, src/model/container.rs) ---------------------------
+ * XXH64 (seed 0) of `len` bytes: the checksum that closes a native model
+ * container (container.rs:245 `xxh64`). The section table itself is laid
+ * out by the Python host (model_io.to_native_binary). */
+hb_status hb_xxh64(const void* data, uint64_t len, uint64_t* out);
 
 #ifdef __cplusplus
 }

@@ -16,7 +16,9 @@ reference's tests compute them (f32 arithmetic throughout).
   ``y_t = 2a - b + t*c + 0.1``.
 * every extracted model (all versions) is a *prediction* known-answer test.
 * ``native/early_stopping.json`` and ``native/multiclass_forest.json`` are
-  two of those files verbatim, the native JSON writer's byte-level fixtures.
+  two of those files verbatim, the native JSON writer's byte-level fixtures;
+  ``native/{early_stopping,multi_target,multiclass_forest}.bin`` likewise for
+  the native binary format.
 
 Usage: ``python tests/golden/make_golden.py [/path/to/reference]``.  The
 output is committed, so the tests never need the reference at run time.
@@ -129,11 +131,15 @@ def main(ref):
     print("wrote", dst, "with", len(out["models"]), "models")
     # two native JSON files verbatim: the model writer's byte-level fixtures
     os.makedirs(os.path.join(HERE, "native"), exist_ok=True)
-    for name in ("early_stopping", "multiclass_forest"):
-        src = os.path.join(saved, "0.4.9", name + ".json")
+    # and three native binary files (zstd frames of the section container)
+    # verbatim: the binary writer's and reader's fixtures
+    for name, ext in (("early_stopping", ".json"), ("multiclass_forest", ".json"),
+                      ("early_stopping", ".bin"), ("multi_target", ".bin"),
+                      ("multiclass_forest", ".bin")):
+        src = os.path.join(saved, "0.4.9", name + ext)
         with open(src, "rb") as fh:
             raw = fh.read()
-        with open(os.path.join(HERE, "native", name + ".json"), "wb") as fh:
+        with open(os.path.join(HERE, "native", name + ext), "wb") as fh:
             fh.write(raw)
         print("copied", src)
 
