@@ -335,12 +335,19 @@ def _expansion_accepted(compressed, decompressed):
 
 def to_native_binary(nodes, tree_ptr, base, n_features, objective="reg:squarederror", num_class=0,
                      best_iteration=None, scale_pos_weight=1.0, max_delta_step=0.0, tree_weights=None,
-                     num_parallel_tree=1, writer=WRITER, compress=True):
+                     num_parallel_tree=1, writer=WRITER, compress=True, n_targets=None,
+                     objective_sections=None):
     """The native binary file of a gbtree model (arguments as
     `to_native_json`): the section container as one zstd frame when
     `compress` and a zstd codec is present (the reference's `seal`,
     container.rs:81, keeps it uncompressed when the frame would expand past
-    what its reader accepts), else the container itself."""
+    what its reader accepts), else the container itself.
+
+    `n_targets` defaults to 1 for multi:* objectives and to the output
+    count otherwise; `objective_sections` ([(name, payload)], as
+    `from_native_binary` returns them), when given, replaces the objective
+    parameters written from `scale_pos_weight` and `max_delta_step`, so a
+    model read here writes back unchanged."""
     nodes = np.asarray(nodes, NODE_DTYPE)
     tree_ptr = np.asarray(tree_ptr, np.uint64)
     base = np.atleast_1d(np.asarray(base, np.float32))
@@ -359,13 +366,34 @@ def to_native_binary(nodes, tree_ptr, base, n_features, objective="reg:squareder
     w.array("model.base_score", base, np.float32)
     w.u64("model.num_class", num_class)
     w.u64("model.n_outputs", n_outputs)
-    w.u64("model.n_targets", 1 if objective.startswith("multi:") else n_outputs)
+    if n_targets is None:
+        n_targets = 1 if objective.startswith("multi:") else n_outputs
+    w.u64("model.n_targets", n_targets)
     w.u64("model.n_features", n_features)
     if best_iteration is not None:
         w.u64("model.best_iteration", best_iteration)
     w.array("model.tree_weights", weights, np.float32)
     w.u64("model.num_parallel_tree", num_parallel_tree)
     # objective.* (native.rs:767), the objective's stored defaults otherwise
+    if objective_sections is not None:
+        for name, payload in objective_sections:
+            if not name.startswith("objective.") or name not in _KNOWN:
+                raise ValueError(f"{name!r} is not an objective section")
+            w.raw(name, payload)
+    else:
+        _default_objective_sections(w, scale_pos_weight, max_delta_step)
+    _tree_sections(w, nodes, tree_ptr, n_trees)
+    container = w.container()
+    pa = _zstd() if compress else None
+    if pa is None:
+        return container
+    frame = pa.Codec("zstd", compression_level=_ZSTD_LEVEL).compress(container, asbytes=True)
+    return frame if _expansion_accepted(len(frame), len(container)) else container
+
+
+def _default_objective_sections(w, scale_pos_weight, max_delta_step):
+    """The objective parameters this library trains with, the others at
+    the reference's stored defaults (objective.rs:166)."""
     w.f64("objective.scale_pos_weight", np.float32(scale_pos_weight))
     w.f64("objective.max_delta_step", max_delta_step)
     w.f64("objective.tweedie_variance_power", 1.5)
@@ -377,7 +405,11 @@ def to_native_binary(nodes, tree_ptr, base, n_features, objective="reg:squareder
     w.f64("objective.aft_loss_distribution_scale", 1.0)
     w.str("objective.dist_gradient", "fisher")
     w.str("objective.dist_split_direction", "random")
-    # the trees column-wise (native.rs:463)
+
+
+def _tree_sections(w, nodes, tree_ptr, n_trees):
+    """The trees column-wise (native.rs:463 `write_tree_sections`), numeric
+    scalar-leaf trees only: no categories, leaf vectors or linear leaves."""
     counts = np.diff(tree_ptr.astype(np.int64)).astype(np.uint32)
     leaf = nodes["left"] < 0
     w.array("tree.node_count", counts, np.uint32)
@@ -402,12 +434,6 @@ def to_native_binary(nodes, tree_ptr, base, n_features, objective="reg:squareder
     w.array("leaf_linear.intercepts", [], np.float64)
     w.array("leaf_linear.features", [], np.uint32)
     w.array("leaf_linear.coeffs", [], np.float64)
-    container = w.container()
-    pa = _zstd() if compress else None
-    if pa is None:
-        return container
-    frame = pa.Codec("zstd", compression_level=_ZSTD_LEVEL).compress(container, asbytes=True)
-    return frame if _expansion_accepted(len(frame), len(container)) else container
 
 
 def _zstd_content_size(frame):
@@ -576,6 +602,7 @@ def from_native_binary(data):
         "tree_weights": [float(v) for v in arr("model.tree_weights", np.float32)],
         "num_parallel_tree": u64("model.num_parallel_tree"),
         "writer": s["model.writer"].decode(errors="replace") if "model.writer" in s else None,
+        "objective_sections": [(k, v) for k, v in s.items() if k.startswith("objective.")],
     }
     for name in ("scale_pos_weight", "max_delta_step"):
         key = "objective." + name

@@ -18,7 +18,8 @@ reference's tests compute them (f32 arithmetic throughout).
 * ``native/early_stopping.json`` and ``native/multiclass_forest.json`` are
   two of those files verbatim, the native JSON writer's byte-level fixtures;
   ``native/{early_stopping,multi_target,multiclass_forest}.bin`` likewise for
-  the native binary format.
+  the native binary format, and ``native/saved_<version>_<name>.bin`` is the
+  binary file of every extracted prediction model.
 
 Usage: ``python tests/golden/make_golden.py [/path/to/reference]``.  The
 output is committed, so the tests never need the reference at run time.
@@ -111,6 +112,12 @@ def main(ref):
             if key in seen:
                 continue
             seen.add(key)
+            # the same model's native binary file, for the binary reader
+            os.makedirs(os.path.join(HERE, "native"), exist_ok=True)
+            with open(os.path.join(saved, version, name + ".bin"), "rb") as fh:
+                raw_bin = fh.read()
+            with open(os.path.join(HERE, "native", f"saved_{version}_{name}.bin"), "wb") as fh:
+                fh.write(raw_bin)
             out["models"].append(
                 {
                     "name": name,

@@ -274,3 +274,44 @@ def test_model_save_load_both_formats(tmp_path, fmt):
     np.testing.assert_array_equal(got.view(np.uint32), margins.view(np.uint32))
     with pytest.raises(ValueError):
         m.save_native(tmp_path / "x", H.TrainingParams(), format="ubjson")
+
+
+def _saved_models():
+    return [(m["version"], m["name"]) for m in O.golden()["models"]]
+
+
+@needs_zstd
+@pytest.mark.parametrize("version,name", _saved_models(), ids=[f"{v}-{n}" for v, n in _saved_models()])
+def test_every_saved_model_reads_predicts_and_writes_back(version, name):
+    # every prediction known answer, through its binary file: the trees
+    # equal the JSON file's, the margins are the recorded ones bit for bit,
+    # and the file writes back to the same container
+    g = O.golden()
+    m = next(x for x in g["models"] if (x["version"], x["name"]) == (version, name))
+    data = _bin(f"saved_{version}_{name}")
+    nodes, ptr, base, nf, f = M.from_native_binary(data)
+    gnodes, gptr = O.golden_nodes(m)
+    np.testing.assert_array_equal(ptr, gptr)
+    for k in ("left", "right", "default_left"):
+        np.testing.assert_array_equal(nodes[k], gnodes[k], err_msg=k)
+    inner = nodes["left"] >= 0
+    np.testing.assert_array_equal(nodes["split_feature"][inner], gnodes["split_feature"][inner])
+    for k in ("split_cond", "leaf_value"):
+        np.testing.assert_array_equal(nodes[k].view(np.uint32), gnodes[k].view(np.uint32), err_msg=k)
+    np.testing.assert_array_equal(base.view(np.uint32), O.f32_to_bits(np.array(m["base_score"], np.float32)))
+    n, outs, w = O.golden_layout(m)
+    got = O.predict(nodes.view(O.NODE_DTYPE), ptr[: n + 1], m["n_outputs"], base, g["x"], outs, w)
+    np.testing.assert_array_equal(O.f32_to_bits(got).ravel(), np.array(m["margins_bits"], np.uint32))
+    out = M.to_native_binary(nodes, ptr, base, nf, objective=f["objective"], num_class=f["num_class"],
+                             best_iteration=f["best_iteration"], tree_weights=f["tree_weights"],
+                             num_parallel_tree=f["num_parallel_tree"], n_targets=f["n_targets"],
+                             objective_sections=f["objective_sections"], writer=f["writer"], compress=False)
+    assert out == M._unpack(data)
+    assert f["writer"] == f"hessboost {version}"
+
+
+def test_objective_sections_must_be_objective_sections():
+    g = O.golden()
+    nodes, ptr, base, _ = O.train(g["x"], g["y1"], 1, max_depth=2)
+    with pytest.raises(ValueError, match="not an objective section"):
+        M.to_native_binary(nodes.view(H.NODE_DTYPE), ptr, base, 4, objective_sections=[("model.n_features", b"")])
