@@ -886,18 +886,35 @@ def _libm():
 @dataclass
 class Model:
     """A trained ensemble: nodes back to back, per-tree offsets, the base
-    margin (one per output; tree t adds to output t % outputs)."""
+    margin (one per output). Tree t adds to output
+    (t // num_parallel_tree) % outputs, scaled by tree_weights[t] when the
+    model has per-tree weights (a DART model read from a file)."""
 
     nodes: np.ndarray
     tree_ptr: np.ndarray
     base: object
     n_features: int
+    num_parallel_tree: int = 1
+    tree_weights: object = None
 
     def bases(self):
         return np.atleast_1d(np.asarray(self.base, np.float32))
 
+    def tree_layout(self):
+        """(output of each tree, weight of each tree or None), the layout
+        BoostedModel::predict_margin walks (model/predict.rs:701)."""
+        n_trees = len(self.tree_ptr) - 1
+        outs = (np.arange(n_trees) // max(int(self.num_parallel_tree), 1)) % self.bases().size
+        w = None if self.tree_weights is None else np.asarray(self.tree_weights, np.float32)
+        if w is not None and w.size != n_trees:
+            raise ValueError("tree_weights needs one weight per tree")
+        return outs.astype(np.uint32), w
+
     def predictor(self, device=0):
-        return Predictor(self.nodes, self.tree_ptr, self.bases(), self.n_features, device=device)
+        outs, w = self.tree_layout()
+        return Predictor(self.nodes, self.tree_ptr, self.bases(), self.n_features,
+                         tree_output=outs if self.num_parallel_tree != 1 else None, tree_weight=w,
+                         device=device)
 
     def predict_margin(self, x, device=0):
         p = self.predictor(device)
@@ -918,7 +935,8 @@ class Model:
         softmax = params.loss_kind() == HB_LOSS_SOFTMAX
         kw = dict(objective=params.objective, num_class=params.num_class if softmax else 0,
                   scale_pos_weight=params.scale_pos_weight,
-                  max_delta_step=float(np.float32(params.max_delta_step)))
+                  max_delta_step=float(np.float32(params.max_delta_step)),
+                  num_parallel_tree=self.num_parallel_tree, tree_weights=self.tree_weights)
         if format == "json":
             data = model_io.to_native_json(self.nodes, self.tree_ptr, self.bases(), self.n_features,
                                            **kw).encode()
@@ -944,13 +962,14 @@ class Model:
             nodes, ptr, base, nf, fields = model_io.from_native_json(data.decode())
         else:
             raise ValueError(f"{path}: not a native hessboost model file")
+        npt = int(fields.get("num_parallel_tree") or 1)
+        weights = np.asarray(fields.get("tree_weights") or np.ones(len(ptr) - 1), np.float32)
         if fields.get("best_iteration") is not None:
-            per = int(fields["n_outputs"]) * int(fields["num_parallel_tree"])
-            n = (int(fields["best_iteration"]) + 1) * per
-            nodes, ptr = nodes[: int(ptr[n])], ptr[: n + 1]
-        if int(fields.get("num_parallel_tree") or 1) != 1:
-            raise ValueError("num_parallel_tree > 1 does not load here")
-        return Model(nodes, ptr, base if base.size > 1 else float(base[0]), nf)
+            # predictions stop at the best iteration (model/predict.rs:701)
+            n = (int(fields["best_iteration"]) + 1) * int(fields["n_outputs"]) * npt
+            nodes, ptr, weights = nodes[: int(ptr[n])], ptr[: n + 1], weights[:n]
+        return Model(nodes, ptr, base if base.size > 1 else float(base[0]), nf, num_parallel_tree=npt,
+                     tree_weights=None if np.all(weights == 1.0) else weights)
 
 
 def train(params, x=None, y=None, rounds=10, device=0, matrix=None, engine=None):

@@ -315,3 +315,31 @@ def test_objective_sections_must_be_objective_sections():
     nodes, ptr, base, _ = O.train(g["x"], g["y1"], 1, max_depth=2)
     with pytest.raises(ValueError, match="not an objective section"):
         M.to_native_binary(nodes.view(H.NODE_DTYPE), ptr, base, 4, objective_sections=[("model.n_features", b"")])
+
+
+@needs_zstd
+@pytest.mark.parametrize("version,name,ext", [("0.4.9", "multiclass_forest", ".bin"), ("0.4.9", "multiclass_forest", ".json"),
+                                              ("0.2.0", "dart", ".bin"), ("0.4.3", "dart", ".bin"),
+                                              ("0.4.9", "early_stopping", ".bin")])
+def test_model_load_native_keeps_the_tree_layout(tmp_path, version, name, ext):
+    # Model.load_native keeps num_parallel_tree (the softprob forest grows 3
+    # trees per class and round) and DART's per-tree weights, stops at the
+    # best iteration, and its layout predicts the recorded margins
+    g = O.golden()
+    src = name + ext if version == "0.4.9" else f"saved_{version}_{name}{ext}"
+    m = H.Model.load_native(os.path.join(NATIVE, src))
+    ref = next(x for x in g["models"] if x["name"] == name and (x["version"] == version or version == "0.4.9"))
+    n, outs, w = O.golden_layout(ref)
+    got_outs, got_w = m.tree_layout()
+    assert len(m.tree_ptr) - 1 == n
+    np.testing.assert_array_equal(got_outs, outs)
+    np.testing.assert_array_equal(np.ones(n, np.float32) if got_w is None else got_w, w)
+    pred = O.predict(m.nodes.view(O.NODE_DTYPE), m.tree_ptr, m.bases().size, m.bases(), g["x"], got_outs, got_w)
+    np.testing.assert_array_equal(O.f32_to_bits(pred).ravel(), np.array(ref["margins_bits"], np.uint32))
+    # and saves with that layout
+    path = tmp_path / "again.bin"
+    m.save_native(path, H.TrainingParams(objective="multi:softmax", num_class=3) if name == "multiclass_forest"
+                  else H.TrainingParams(), format="binary")
+    back = H.Model.load_native(path)
+    assert back.num_parallel_tree == m.num_parallel_tree
+    np.testing.assert_array_equal(back.tree_layout()[0], got_outs)
