@@ -77,9 +77,16 @@ def config(n_gpus):
         "max_bin": 256,
         "parallelism": f"rows sharded over {n_gpus} GPU(s), one NCCL allreduce per level"
         if n_gpus > 1 else "1 GPU",
-        "l2": "inputs larger than L2: the binned rows (320 MB records + 280 MB columns) and "
-        "80 MB of gradients are re-read every round",
+        "l2": _l2_note(),
     }
+
+
+def _l2_note():
+    rec, col, gp = N_ROWS * 32 / 1e6, N_ROWS * 28 / 1e6, N_ROWS * 8 / 1e6
+    sizes = (f"the binned rows ({rec:,.0f} MB records + {col:,.0f} MB columns) and {gp:,.0f} MB of "
+             "gradients are re-read every round")
+    # 126 MB of L2 on a B200
+    return ("inputs larger than L2: " if rec + gp > 126 else "inputs SMALLER than L2 at this size: ") + sizes
 
 
 def peaks():
@@ -186,9 +193,10 @@ def run_reference(args):
         return
     cores = os.cpu_count() or 1
     x, y = make_data()
-    k, dt = cpu_rounds(x, y, max(1, args.steps), budget_s=120.0, warm=min(args.warmup, 1))
+    warm = min(args.warmup, 1)
+    k, dt = cpu_rounds(x, y, max(1, args.steps), budget_s=120.0, warm=warm)
     value = k / dt
-    sample = (f"{k} timed round(s) of the full C2 workload after binning and 1 untimed round "
+    sample = (f"{k} timed round(s) of the C2 workload ({N_ROWS:,} rows) after binning and {warm} untimed round(s) "
               f"(C++ restatement of hessboost's CPU hist path, OpenMP on {cores} threads; "
               "the Rust reference cannot be built offline)")
     emit({
@@ -285,7 +293,9 @@ def run_c5(args):
         "config": {"workload": f"C5: {C5_TREES} complete depth-{C5_DEPTH} trees (features U[0,50), "
                                "thresholds from N(0,1) quantiles, leaves N(0,0.01)), "
                                f"{n:,} x {C5_COLS} f32 rows N(0,1) with 1% NaN, raw margin",
-                   "l2": "rows (20 GB) far larger than L2; the forest (8 MB) stays in L2",
+                   "l2": f"rows ({n * C5_COLS * 4 / 1e9:.2f} GB) "
+                         f"{'larger' if n * C5_COLS * 4 > 126e6 else 'SMALLER'} than L2; "
+                         "the forest (8 MB) stays in L2",
                    "parity_sample_bit_exact": exact},
         "roofline": {"bound": "hbm", "achieved": step_bytes / (ms / args.steps / 1000.0) / 1e9,
                      "peak": peaks()[0], "unit": "GB/s",
@@ -371,7 +381,8 @@ def run_c3(args):
                                "max_depth 6, eta 0.2",
                    "trees": int(len(ptr) - 1),
                    "kernel_ms_per_round": per_round,
-                   "l2": "inputs larger than L2: 2M x 128 B records + 10 x 16 MB pairs per round"},
+                   "l2": f"inputs {'larger' if n * 128 > 126e6 else 'SMALLER'} than L2: "
+                         f"{n:,} x 128 B records + 10 x {n * 8 / 1e6:,.0f} MB pairs per round"},
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                      "frac": achieved / peak, "traffic": None, "kernel": "k_hist32",
                      "launches": hist_launches},
@@ -675,7 +686,7 @@ def main():
         cores = os.cpu_count() or 1
         k, dt = cpu_rounds(x, y, 3, budget_s=25.0, warm=0)
         cpu = {"value": k / dt, "unit": UNIT, "cores": cores, "kind": "port",
-               "sample": f"{k} round(s) of the full C2 workload after binning (C++ restatement of "
+               "sample": f"{k} round(s) of the C2 workload ({N_ROWS:,} rows) after binning (C++ restatement of "
                          f"hessboost's CPU hist path, OpenMP, {cores} threads)"}
 
     if rank == 0:
