@@ -11,6 +11,7 @@
 //     int64 multiple of a power of two and summed exactly; this is the
 //     arithmetic the CUDA path uses, so the two must agree bit for bit.
 #include <algorithm>
+#include <cassert>
 #include <functional>
 #include <cfloat>
 #include <cmath>
@@ -45,21 +46,26 @@ inline bool is_missing(float v) { return std::isnan(v); }
 // every feature, ghist.rs:205-208).
 // A CSR index (ghist.rs:6-21 `rows`: global bins row by row, no columns)
 // keeps only the stored cells: row_bins ascending within a row.
+// A dense index keeps each cell's local bin twice, row-major for the
+// histograms (one row's cells together) and feature-major for the partition
+// (one feature's cells together); a missing cell holds kMissingBin.
+constexpr uint16_t kMissingBin = 0xFFFF;
+
 struct Index {
   size_t n_rows = 0, n_cols = 0;
   Cuts cuts;
-  std::vector<uint16_t> local;   // [row][feature] local bin
-  std::vector<uint8_t> missing;  // [row][feature]
+  std::vector<uint16_t> local;  // [row][feature] local bin or kMissingBin
+  std::vector<uint16_t> cols;   // [feature][row], the same bins
   bool dense = true;
   bool csr = false;
   std::vector<uint64_t> row_ptr;   // CSR: n_rows + 1
   std::vector<uint32_t> row_bins;  // CSR: global bins
-  uint32_t global(size_t r, size_t f) const { return cuts.feature_offset[f] + local[r * n_cols + f]; }
   // The cell's local bin, or false when it is missing.
   bool cell(size_t r, size_t f, uint32_t& bin) const {
     if (!csr) {
-      if (missing[r * n_cols + f]) return false;
-      bin = local[r * n_cols + f];
+      const uint16_t b = cols[f * n_rows + r];
+      if (b == kMissingBin) return false;
+      bin = b;
       return true;
     }
     const uint32_t lo = cuts.feature_offset[f], hi = cuts.feature_offset[f + 1];
@@ -98,24 +104,25 @@ Index make_index(const float* x, size_t n, size_t nc, Cuts cuts) {
   ix.n_rows = n;
   ix.n_cols = nc;
   ix.cuts = std::move(cuts);
+  for (size_t f = 0; f < nc; ++f) assert(ix.cuts.num_bins(f) < kMissingBin);  // u16 local bins
   ix.local.assign(n * nc, 0);
-  ix.missing.assign(n * nc, 0);
-#pragma omp parallel for schedule(static)
+  ix.cols.assign(n * nc, 0);
+  bool any_missing = false;
+#pragma omp parallel for schedule(static) reduction(|| : any_missing)
   for (long long r = 0; r < (long long)n; ++r) {
     for (size_t f = 0; f < nc; ++f) {
       float v = x[r * nc + f];
+      uint16_t b = kMissingBin;
       if (is_missing(v)) {
-        ix.missing[r * nc + f] = 1;
+        any_missing = true;
       } else {
-        ix.local[r * nc + f] = (uint16_t)local_bin_of(ix.cuts, f, v);
+        b = (uint16_t)local_bin_of(ix.cuts, f, v);
       }
+      ix.local[r * nc + f] = b;
+      ix.cols[f * n + r] = b;
     }
   }
-  for (uint8_t m : ix.missing)
-    if (m) {
-      ix.dense = false;
-      break;
-    }
+  ix.dense = !any_missing;
   return ix;
 }
 
@@ -234,6 +241,43 @@ bool is_contiguous(const std::vector<uint32_t>& rows) {  // walk.rs `contiguous_
   return rows.empty() || (size_t)(rows.back() - rows.front()) + 1 == rows.size();
 }
 
+// Add rows[b..e) of a dense index into `out`, features [f0, f1) of each
+// row, rows in order: each bin sees its rows' values in row order, which is
+// all the sum orders below rely on. `Val` is GradPair (f64 sums) or IS
+// (fixed point).
+template <class Val, class Stat>
+void accumulate_dense(const Index& ix, const std::vector<uint32_t>& rows, size_t b, size_t e,
+                      size_t f0, size_t f1, const Val* v, Stat* out) {
+  const size_t nc = ix.n_cols;
+  const uint32_t* off = ix.cuts.feature_offset.data();
+  for (size_t i = b; i < e; ++i) {
+    const uint32_t r = rows[i];
+    const uint16_t* cell = ix.local.data() + (size_t)r * nc;
+    const auto g = v[r].grad, h = v[r].hess;
+    for (size_t f = f0; f < f1; ++f) {
+      if (cell[f] == kMissingBin) continue;
+      Stat& o = out[off[f] + cell[f]];
+      o.grad += g;
+      o.hess += h;
+    }
+  }
+}
+
+// All rows of a dense index into `out`, the features split into one
+// contiguous range per thread, each thread walking every row in order over
+// its own range: every bin is one chain in row order.
+template <class Val, class Stat>
+void accumulate_dense_by_features(const Index& ix, const std::vector<uint32_t>& rows, const Val* v,
+                                  Stat* out) {
+  const size_t nc = ix.n_cols;
+  const long long parts = std::max(1, std::min(omp_get_max_threads(), (int)nc));
+#pragma omp parallel for schedule(static, 1)
+  for (long long t = 0; t < parts; ++t) {
+    const size_t f0 = nc * t / parts, f1 = nc * (t + 1) / parts;
+    accumulate_dense(ix, rows, 0, rows.size(), f0, f1, v, out);
+  }
+}
+
 // Accumulate `rows[b..e)` into `out` (walk.rs:46 `accumulate`: one f64
 // chain per bin in ascending row order).
 void accumulate_f64(const Index& ix, const std::vector<uint32_t>& rows, size_t b, size_t e,
@@ -250,16 +294,7 @@ void accumulate_f64(const Index& ix, const std::vector<uint32_t>& rows, size_t b
     }
     return;
   }
-  for (size_t i = b; i < e; ++i) {
-    uint32_t r = rows[i];
-    double g = (double)gp[r].grad, h = (double)gp[r].hess;
-    for (size_t f = 0; f < ix.n_cols; ++f) {
-      if (ix.missing[(size_t)r * ix.n_cols + f]) continue;
-      GS& o = out[ix.global(r, f)];
-      o.grad += g;
-      o.hess += h;
-    }
-  }
+  accumulate_dense(ix, rows, b, e, 0, ix.n_cols, gp, out);
 }
 
 // CpuBackend::build (src/tree/hist/mod.rs:510): the reference's f64 sums.
@@ -274,17 +309,8 @@ std::vector<GS> build_hist(const Index& ix, const std::vector<uint32_t>& rows, c
     return out;
   }
   if (chain_order(ix.dense, ix.n_rows, rows.size(), contiguous)) {
-    // One chain per bin; features are independent, so sweep them in parallel.
-    size_t nc = ix.n_cols;
-#pragma omp parallel for schedule(dynamic, 1)
-    for (long long f = 0; f < (long long)nc; ++f) {
-      for (uint32_t r : rows) {
-        if (ix.missing[(size_t)r * nc + f]) continue;
-        GS& o = out[ix.global(r, f)];
-        o.grad += (double)gp[r].grad;
-        o.hess += (double)gp[r].hess;
-      }
-    }
+    // One chain per bin; features are independent, so split them over threads.
+    accumulate_dense_by_features(ix, rows, gp, out.data());
     return out;
   }
   // SumOrder::Blocked: chunks of `grain` rows, each summed from zero, then
@@ -313,7 +339,7 @@ std::vector<GS> build_hist(const Index& ix, const std::vector<uint32_t>& rows, c
 // The fixed-point histogram: exact int64 sums (order-free).
 std::vector<IS> build_hist(const Index& ix, const std::vector<uint32_t>& rows, const IS* q,
                            const FixMode&) {
-  size_t nb = ix.cuts.values.size(), nc = ix.n_cols;
+  size_t nb = ix.cuts.values.size();
   std::vector<IS> out(nb);
   if (ix.csr) {
     // stored cells only; exact sums, so any order: row blocks in parallel
@@ -347,15 +373,7 @@ std::vector<IS> build_hist(const Index& ix, const std::vector<uint32_t>& rows, c
     }
     return out;
   }
-#pragma omp parallel for schedule(dynamic, 1)
-  for (long long f = 0; f < (long long)nc; ++f) {
-    for (uint32_t r : rows) {
-      if (ix.missing[(size_t)r * nc + f]) continue;
-      IS& o = out[ix.global(r, f)];
-      o.grad += q[r].grad;
-      o.hess += q[r].hess;
-    }
-  }
+  accumulate_dense_by_features(ix, rows, q, out.data());
   return out;
 }
 
@@ -450,9 +468,30 @@ class Builder {
   // HistTreeBuilder::evaluate (search.rs:37) over every feature, with the
   // sequential candidate order of for_each_numeric_split (split.rs:391)
   // and xgb_update's tie rule (builder/mod.rs:334).
+  //
+  // The features are scored in parallel, each from the empty split, and
+  // their winners merged in feature order: the incumbent's feature never
+  // exceeds the candidate's, so need_replace is a strict `>` throughout,
+  // and the merge keeps the first maximum of the sequential scan.
   Best<S> evaluate(const std::vector<S>& hist, S total) const {
-    Best<S> best;
     const float root_gain = xgb_node_gain(mode_.g(total), mode_.h(total), p_);
+    const long long nc = (long long)ix_.n_cols;
+    std::vector<Best<S>> per(nc);
+    std::vector<uint8_t> found(nc, 0);
+#pragma omp parallel for schedule(dynamic, 4) if (nc >= 16)
+    for (long long f = 0; f < nc; ++f) found[f] = evaluate_feature(hist, total, root_gain, (uint32_t)f, per[f]);
+    Best<S> best;
+    for (long long f = 0; f < nc; ++f)
+      if (found[f] && need_replace((float)best.loss_chg, best.feature, (float)per[f].loss_chg, (uint32_t)f))
+        best = per[f];
+    return best;
+  }
+
+  // One feature's candidates in scan order, from the empty split; true when
+  // one of them replaced it.
+  bool evaluate_feature(const std::vector<S>& hist, S total, float root_gain, uint32_t f,
+                        Best<S>& best) const {
+    bool found = false;
     auto offer = [&](uint32_t f, int32_t bin, bool default_left, S left, S right) {
       double lg = mode_.g(left), lh = mode_.h(left), rg = mode_.g(right), rh = mode_.h(right);
       if (!children_valid(lh, rh, p_.mcw)) return;  // split.rs:37 `loss_chg`
@@ -461,6 +500,7 @@ class Builder {
       float gain = (float)gain_given_weight(lg, lh, p_, wl) + (float)gain_given_weight(rg, rh, p_, wr);
       float loss = gain - root_gain;
       if (need_replace((float)best.loss_chg, best.feature, loss, f)) {
+        found = true;
         best.loss_chg = (double)loss;
         best.feature = f;
         best.bin = bin;
@@ -471,24 +511,22 @@ class Builder {
         best.w_right = (double)wr;
       }
     };
-    for (uint32_t f = 0; f < ix_.n_cols; ++f) {
-      uint32_t fs = ix_.cuts.feature_offset[f], fe = ix_.cuts.feature_offset[f + 1];
-      if (fe <= fs + 1) continue;  // search.rs:214 degenerate feature
-      S acc{};
-      for (uint32_t b = fs; b < fe; ++b) {
-        acc = Mode::add(acc, hist[b]);
-        offer(f, (int32_t)b, false, acc, Mode::sub(total, acc));
-      }
-      if (ix_.dense || Mode::eq(acc, total)) continue;
-      S suffix{};
-      for (uint32_t off = fe - fs; off-- > 0;) {
-        suffix = Mode::add(suffix, hist[fs + off]);
-        // SplitPos::backward (builder/mod.rs:263)
-        int32_t bin = off == 0 ? -1 : (int32_t)(fs + off - 1);
-        offer(f, bin, true, Mode::sub(total, suffix), suffix);
-      }
+    uint32_t fs = ix_.cuts.feature_offset[f], fe = ix_.cuts.feature_offset[f + 1];
+    if (fe <= fs + 1) return false;  // search.rs:214 degenerate feature
+    S acc{};
+    for (uint32_t b = fs; b < fe; ++b) {
+      acc = Mode::add(acc, hist[b]);
+      offer(f, (int32_t)b, false, acc, Mode::sub(total, acc));
     }
-    return best;
+    if (ix_.dense || Mode::eq(acc, total)) return found;
+    S suffix{};
+    for (uint32_t off = fe - fs; off-- > 0;) {
+      suffix = Mode::add(suffix, hist[fs + off]);
+      // SplitPos::backward (builder/mod.rs:263)
+      int32_t bin = off == 0 ? -1 : (int32_t)(fs + off - 1);
+      offer(f, bin, true, Mode::sub(total, suffix), suffix);
+    }
+    return found;
   }
 
   // prepare_split (hist/mod.rs:639): expand the node, record child stats.
@@ -508,11 +546,19 @@ class Builder {
     const Best<S>& b = e.best;
     uint32_t fs = ix_.cuts.feature_offset[b.feature];
     uint32_t limit = b.bin < 0 ? 0 : (uint32_t)(b.bin + 1 - (int32_t)fs);
-    for (uint32_t r : e.rows) {
+    // each row's side (in parallel: a gather of one feature's cells), then
+    // the stable split in row order
+    const long long n = (long long)e.rows.size();
+    std::vector<uint8_t> go(n);
+#pragma omp parallel for schedule(static) if (n >= 65536)
+    for (long long i = 0; i < n; ++i) {
       uint32_t bin = 0;
-      bool go_left = ix_.cell(r, b.feature, bin) ? bin < limit : b.default_left;
-      (go_left ? left : right).push_back(r);
+      go[i] = ix_.cell(e.rows[i], b.feature, bin) ? bin < limit : b.default_left;
     }
+    const size_t n_left = (size_t)std::count(go.begin(), go.end(), uint8_t(1));
+    left.reserve(left.size() + n_left);
+    right.reserve(right.size() + (size_t)n - n_left);
+    for (long long i = 0; i < n; ++i) (go[i] ? left : right).push_back(e.rows[i]);
   }
 
   // build_children (hist/mod.rs:692) + finish_children.
