@@ -555,10 +555,28 @@ class Builder {
       uint32_t bin = 0;
       go[i] = ix_.cell(e.rows[i], b.feature, bin) ? bin < limit : b.default_left;
     }
-    const size_t n_left = (size_t)std::count(go.begin(), go.end(), uint8_t(1));
-    left.reserve(left.size() + n_left);
-    right.reserve(right.size() + (size_t)n - n_left);
-    for (long long i = 0; i < n; ++i) (go[i] ? left : right).push_back(e.rows[i]);
+    // stable split: per-chunk left counts, their prefix, then each chunk
+    // writes its rows at its offsets, in row order
+    const long long chunk = 1 << 16, n_chunks = (n + chunk - 1) / chunk;
+    std::vector<size_t> lefts(n_chunks + 1, 0);
+#pragma omp parallel for schedule(static) if (n_chunks > 1)
+    for (long long c = 0; c < n_chunks; ++c) {
+      size_t cnt = 0;
+      for (long long i = c * chunk; i < std::min(n, (c + 1) * chunk); ++i) cnt += go[i];
+      lefts[c + 1] = cnt;
+    }
+    for (long long c = 0; c < n_chunks; ++c) lefts[c + 1] += lefts[c];
+    const size_t l0 = left.size(), r0 = right.size();
+    left.resize(l0 + lefts[n_chunks]);
+    right.resize(r0 + (size_t)n - lefts[n_chunks]);
+#pragma omp parallel for schedule(static) if (n_chunks > 1)
+    for (long long c = 0; c < n_chunks; ++c) {
+      size_t li = l0 + lefts[c], ri = r0 + (size_t)(c * chunk) - lefts[c];
+      for (long long i = c * chunk; i < std::min(n, (c + 1) * chunk); ++i) {
+        if (go[i]) left[li++] = e.rows[i];
+        else right[ri++] = e.rows[i];
+      }
+    }
   }
 
   // build_children (hist/mod.rs:692) + finish_children.
@@ -952,6 +970,11 @@ struct orc_trainer {
   std::vector<float> base, margins, labels;
   size_t n = 0;
   int k = 1;
+  // per-round scratch, kept across orc_trainer_rounds calls (every element
+  // is written before it is read in a round)
+  std::vector<orc::GradPair> gp, gp_all;
+  std::vector<float> mk, yk;
+  std::vector<orc::IS> q;
 };
 
 namespace {
@@ -983,9 +1006,17 @@ int64_t run_rounds(orc_trainer* tr, int rounds, orc_node* nodes, uint64_t nodes_
   const Params& p = tr->p;
   const size_t n = tr->n;
   const int k = tr->k;
-  std::vector<GradPair> gp(n), gp_all(n * k);
-  std::vector<float> mk(n), yk(n);
-  std::vector<IS> q(n);
+  tr->gp.resize(n);
+  tr->gp_all.resize(n * k);
+  tr->mk.resize(n);
+  tr->yk.resize(n);
+  if (p.fixed) tr->q.resize(n);
+  std::vector<GradPair>& gp = tr->gp;
+  std::vector<GradPair>& gp_all = tr->gp_all;
+  std::vector<float>& mk = tr->mk;
+  std::vector<float>& yk = tr->yk;
+  std::vector<IS>& q = tr->q;
+  const long long nn = (long long)n;
   uint64_t used = 0;
   int64_t n_trees = 0;
   tree_ptr[0] = 0;
@@ -993,7 +1024,8 @@ int64_t run_rounds(orc_trainer* tr, int rounds, orc_node* nodes, uint64_t nodes_
     // 1. Gradients of every output from this round's margins (round.rs:253).
     if (p.objective == 2) softmax_gradient(tr->margins.data(), tr->labels.data(), n, k, gp_all.data());
     for (int t = 0; t < k && p.objective != 2; ++t) {
-      for (size_t r = 0; r < n; ++r) {
+#pragma omp parallel for schedule(static)
+      for (long long r = 0; r < nn; ++r) {
         mk[r] = tr->margins[r * k + t];
         yk[r] = tr->labels[r * k + t];
       }
@@ -1001,11 +1033,13 @@ int64_t run_rounds(orc_trainer* tr, int rounds, orc_node* nodes, uint64_t nodes_
         logistic_gradient(mk.data(), yk.data(), n, p.spw, gp.data());
       else
         squared_error_gradient(mk.data(), yk.data(), n, p.spw, gp.data());
-      for (size_t r = 0; r < n; ++r) gp_all[r * k + t] = gp[r];
+#pragma omp parallel for schedule(static)
+      for (long long r = 0; r < nn; ++r) gp_all[r * k + t] = gp[r];
     }
     // 2. One tree per output, output-major (round.rs:318).
     for (int t = 0; t < k; ++t) {
-      for (size_t r = 0; r < n; ++r) gp[r] = gp_all[r * k + t];
+#pragma omp parallel for schedule(static)
+      for (long long r = 0; r < nn; ++r) gp[r] = gp_all[r * k + t];
       std::vector<std::pair<int, std::vector<uint32_t>>> leaves;
       Tree tree(0.0f);
       if (p.fixed) {
@@ -1019,7 +1053,8 @@ int64_t run_rounds(orc_trainer* tr, int rounds, orc_node* nodes, uint64_t nodes_
         mode.sg = fixed_scale(mg, n);
         mode.sh = fixed_scale(mh, n);
         double fg = pow2(mode.sg), fh = pow2(mode.sh);
-        for (size_t r = 0; r < n; ++r) {
+#pragma omp parallel for schedule(static)
+        for (long long r = 0; r < nn; ++r) {
           q[r].grad = std::llrint((double)gp[r].grad * fg);
           q[r].hess = std::llrint((double)gp[r].hess * fh);
         }
@@ -1033,9 +1068,11 @@ int64_t run_rounds(orc_trainer* tr, int rounds, orc_node* nodes, uint64_t nodes_
       float eta = p.eta;
       for (auto& nd : tree.nodes)
         if (nd.left == -1) nd.leaf_value = nd.leaf_value * eta;
-      for (auto& lr : leaves) {
-        float v = tree.nodes[lr.first].leaf_value;
-        for (uint32_t r : lr.second) tr->margins[(size_t)r * k + t] += v;
+      // each row is in one leaf: the leaves update disjoint margins
+#pragma omp parallel for schedule(dynamic, 1)
+      for (long long li = 0; li < (long long)leaves.size(); ++li) {
+        const float v = tree.nodes[leaves[li].first].leaf_value;
+        for (uint32_t r : leaves[li].second) tr->margins[(size_t)r * k + t] += v;
       }
       if (used + tree.nodes.size() > nodes_cap) return -1;
       std::copy(tree.nodes.begin(), tree.nodes.end(), nodes + used);
