@@ -1,6 +1,7 @@
 """Host logic of row sharding, on CPU: shard bounds, and the helpers that
 run over torch.distributed (unique-id broadcast, the global dense flag,
-per-rank binning against rank 0's cuts) as two gloo ranks."""
+per-rank binning against rank 0's cuts) as two gloo ranks; and a rank that
+leaves between steps, which the other learns of from its next collective."""
 
 import os
 import socket
@@ -80,3 +81,53 @@ def test_gloo_two_ranks_shard_the_matrix():
         bits = np.unpackbits(whole.missing.view(np.uint8), bitorder="little").reshape(6, -1)[:, begin:end]
         got = np.unpackbits(miss.view(np.uint8), bitorder="little").reshape(6, -1)[:, : end - begin]
         np.testing.assert_array_equal(got, bits)
+
+
+def _leaving_worker(rank, world, port, x, out):
+    import datetime
+    import time
+
+    import torch.distributed as dist
+
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=10))
+    if rank == 1:
+        # this rank leaves between steps, before the sharding's collectives,
+        # without a word to the others
+        out.put((rank, "left", 0.0))
+        out.close()
+        out.join_thread()  # the message leaves before the process does
+        os._exit(3)
+    t0 = time.monotonic()
+    try:
+        hdist.shard_matrix(dist, x, 64)
+        out.put((rank, "no error", time.monotonic() - t0))
+    except Exception as err:  # noqa: BLE001 - the peer's departure, whatever its form
+        out.put((rank, type(err).__name__, time.monotonic() - t0))
+    out.close()
+    out.join_thread()
+    os._exit(0)
+
+
+def test_gloo_rank_that_leaves_ends_the_others_collectives_with_an_error():
+    # failure detection on the host: the remaining rank learns of the
+    # departure from its next collective, which ends with an error within the
+    # process group's timeout instead of waiting for good
+    import torch.multiprocessing as mp
+
+    x = np.random.default_rng(5).standard_normal((500, 4)).astype(np.float32)
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_leaving_worker, args=(r, 2, port, x, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    res = dict((r, (what, dt)) for r, what, dt in [q.get(timeout=120) for _ in procs])
+    for p in procs:
+        p.join(timeout=60)
+    assert procs[1].exitcode == 3
+    assert procs[0].exitcode == 0
+    what, dt = res[0]
+    assert what != "no error", "the collective finished without its peer"
+    assert dt < 60.0
