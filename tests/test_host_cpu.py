@@ -120,3 +120,10 @@ def test_softmax_intercepts_match_oracle():
         y = rng.integers(0, k, n).astype(np.float32)
         np.testing.assert_array_equal(H.softmax_intercepts(y, k).view(np.uint32),
                                       O.intercepts(2, y, k).view(np.uint32))
+
+
+def test_integration_ffi_block_binds_every_entry_point():
+    # the Rust `extern "C"` block a maintainer would add declares exactly the
+    # header's entry points
+    doc = open(os.path.join(os.path.dirname(HEADER), "..", "INTEGRATION.md")).read()
+    assert sorted(set(re.findall(r"pub fn (hb_\w+)\(", doc))) == declared_symbols()
