@@ -312,6 +312,49 @@ class TrainingParams:
     max_bin: int = 256
     num_class: int = 0
 
+    def validate(self):
+        """The reference's parameter checks for these fields
+        (TrainingParams::validate, src/config/params.rs:906-918 and :1036;
+        the helpers of src/check.rs; scale_pos_weight,
+        src/objective/params.rs:330): ValueError naming the first
+        parameter that fails. Returns self."""
+        def ensure(name, ok, reason):
+            if not ok:
+                raise ValueError(f"invalid parameter `{name}`: {reason}")
+
+        def finite(v):
+            return math.isfinite(float(v))
+
+        def narrows(name, v, positive):
+            # stays finite (and > 0) once narrowed to f32
+            with np.errstate(over="ignore"):
+                n = np.float32(v)
+            ensure(name, np.isfinite(n) and (not positive or n > 0),
+                   f"must stay {'positive and ' if positive else ''}finite in f32, got {v}")
+
+        ensure("eta", finite(self.eta) and self.eta > 0, f"must be > 0, got {self.eta}")
+        narrows("eta", self.eta, True)
+        for name in ("gamma", "min_child_weight", "reg_lambda", "alpha"):
+            v = getattr(self, name)
+            ensure(name, finite(v) and v >= 0, f"must be >= 0, got {v}")
+            narrows(name, v, False)
+        # 0 is "no bound"; a bound must be finite and > 0
+        ensure("max_delta_step", finite(self.max_delta_step) and self.max_delta_step >= 0,
+               f"a bound must be > 0 (0 for none), got {self.max_delta_step}")
+        if self.max_delta_step > 0:
+            narrows("max_delta_step", self.max_delta_step, True)
+        ensure("scale_pos_weight", finite(self.scale_pos_weight) and self.scale_pos_weight > 0,
+               f"must be > 0, got {self.scale_pos_weight}")
+        narrows("scale_pos_weight", self.scale_pos_weight, True)
+        ensure("max_bin", self.max_bin >= 2, f"must be >= 2, got {self.max_bin}")
+        ensure("max_depth", self.max_depth >= 0, f"must be >= 0 (0 for no limit), got {self.max_depth}")
+        ensure("max_leaves", self.max_leaves >= 0, f"must be >= 0 (0 for no limit), got {self.max_leaves}")
+        ensure("max_leaves", not (self.grow_policy == "lossguide" and self.max_leaves == 0 and self.max_depth == 0),
+               "lossguide growth needs a bound: set max_leaves or max_depth")
+        ensure("grow_policy", self.grow_policy in ("depthwise", "lossguide"),
+               f"must be depthwise or lossguide, got {self.grow_policy!r}")
+        return self
+
     def loss_kind(self):
         if self.objective in ("reg:squarederror",):
             return HB_LOSS_SQUARED_ERROR
@@ -979,6 +1022,7 @@ def train(params, x=None, y=None, rounds=10, device=0, matrix=None, engine=None)
     it on its own GPU (hb_engine_upload_dense); where the device sketch
     refuses the input (a feature with 2^24 or more present values), the
     reference's host sketch bins it instead, with the same cuts."""
+    params.validate()
     y = np.ascontiguousarray(y, np.float32)
     eng = engine or Engine(device)
     try:

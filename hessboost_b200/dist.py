@@ -94,6 +94,7 @@ def train_sharded(params, x, y, rounds, dist, device=None):
 
     from . import Engine, Model, base_margin
 
+    params.validate()
     world, rank = dist.get_world_size(), dist.get_rank()
     if device is None:
         device = torch.cuda.current_device()

@@ -127,3 +127,29 @@ def test_integration_ffi_block_binds_every_entry_point():
     # header's entry points
     doc = open(os.path.join(os.path.dirname(HEADER), "..", "INTEGRATION.md")).read()
     assert sorted(set(re.findall(r"pub fn (hb_\w+)\(", doc))) == declared_symbols()
+
+
+@pytest.mark.parametrize("bad,name", [
+    (dict(eta=0.0), "eta"), (dict(eta=float("nan")), "eta"), (dict(eta=1e-50), "eta"),
+    (dict(gamma=-1.0), "gamma"), (dict(min_child_weight=float("inf")), "min_child_weight"),
+    (dict(reg_lambda=-0.5), "reg_lambda"), (dict(alpha=1e300), "alpha"),
+    (dict(max_delta_step=-1.0), "max_delta_step"), (dict(scale_pos_weight=0.0), "scale_pos_weight"),
+    (dict(max_bin=1), "max_bin"), (dict(max_depth=-1), "max_depth"),
+    (dict(grow_policy="lossguide", max_depth=0, max_leaves=0), "max_leaves"),
+    (dict(grow_policy="symmetric"), "grow_policy"),
+])
+def test_training_params_validate_like_the_reference(bad, name):
+    # TrainingParams::validate (src/config/params.rs:906-918, :1036): the
+    # first failing parameter is named
+    with pytest.raises(ValueError, match=f"`{name}`"):
+        H.TrainingParams(**bad).validate()
+
+
+def test_training_params_defaults_and_config_shapes_are_valid():
+    H.TrainingParams().validate()
+    H.TrainingParams(objective="binary:logistic", max_depth=8, eta=0.1).validate()
+    H.TrainingParams(objective="multi:softmax", num_class=10, max_depth=6, eta=0.2, max_bin=128).validate()
+    H.TrainingParams(grow_policy="lossguide", max_depth=0, max_leaves=255, max_bin=64).validate()
+    H.TrainingParams(max_depth=5, reg_lambda=3.0, alpha=0.5, gamma=0.2, min_child_weight=20.0,
+                     max_delta_step=0.7).validate()
+    H.TrainingParams(max_bin=2, min_child_weight=0.0, reg_lambda=0.0).validate()
