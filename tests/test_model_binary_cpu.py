@@ -343,3 +343,22 @@ def test_model_load_native_keeps_the_tree_layout(tmp_path, version, name, ext):
     back = H.Model.load_native(path)
     assert back.num_parallel_tree == m.num_parallel_tree
     np.testing.assert_array_equal(back.tree_layout()[0], got_outs)
+
+
+def test_c5_forest_round_trips_at_full_size():
+    # the prediction workload's forest (1,000 complete depth-8 trees,
+    # 511,000 nodes): the binary file gives back every node bit for bit
+    from hessboost_b200 import synth
+
+    nodes, ptr = synth.forest_c5()
+    base = np.array([0.25], np.float32)
+    data = M.to_native_binary(nodes, ptr, base, 50)
+    back = M.from_native_binary(data)
+    assert len(back[0]) == len(nodes) == 1000 * 511
+    np.testing.assert_array_equal(back[1], ptr)
+    for k in ("left", "right", "default_left"):
+        np.testing.assert_array_equal(back[0][k], nodes[k])
+    inner = nodes["left"] >= 0
+    np.testing.assert_array_equal(back[0]["split_feature"][inner], nodes["split_feature"][inner])
+    for k in ("split_cond", "leaf_value", "sum_hess", "split_gain"):
+        np.testing.assert_array_equal(back[0][k].view(np.uint32), nodes[k].view(np.uint32))
