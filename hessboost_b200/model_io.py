@@ -17,6 +17,7 @@ reg:squarederror, binary:logistic and multi:softmax (no categories, vector
 leaves, linear leaves, DART weights or boosters besides gbtree).
 """
 
+import ctypes
 import json
 
 import numpy as np
@@ -274,8 +275,6 @@ _UNSUPPORTED = ("gblinear.weights", "gblinear.bias", "shrinkage.factors", "shrin
 
 def xxh64(data):
     """XXH64 (seed 0) of `data`, the container's checksum (hb_xxh64)."""
-    import ctypes
-
     from . import lib
 
     buf = bytes(data)
