@@ -165,15 +165,21 @@ def make_data():
 
 
 # ------------------------------------------------------------------ reference
-def cpu_rounds(x, y, k_max, budget_s, warm=1):
+def oracle_trainer(x, y, fixed_point=False):
     """The oracle (the reference's CPU hist path restated in C++, OpenMP over
-    the host cores): preparation untimed, then rounds timed, at most
-    `k_max`, stopping once `budget_s` seconds are spent."""
+    the host cores) prepared on the C2 matrix: cuts, bins, intercept."""
     sys.path.insert(0, os.path.join(ROOT, "tests"))
     import oracle_lib as O
 
     O.build()
-    tr = O.Trainer(x, y, objective=1, max_depth=8, eta=0.1, max_bin=256)
+    return O.Trainer(x, y, objective=1, max_depth=8, eta=0.1, max_bin=256, fixed_point=fixed_point)
+
+
+def cpu_rounds(x, y, k_max, budget_s, warm=1, keep=False):
+    """The oracle's rounds: preparation untimed, `warm` untimed rounds, then
+    rounds timed, at most `k_max`, stopping once `budget_s` seconds are
+    spent. Returns (rounds, seconds[, trainer when `keep`])."""
+    tr = oracle_trainer(x, y)
     for _ in range(warm):
         tr.rounds(1)
     done, t0 = 0, time.perf_counter()
@@ -183,6 +189,8 @@ def cpu_rounds(x, y, k_max, budget_s, warm=1):
         if time.perf_counter() - t0 > budget_s:
             break
     dt = time.perf_counter() - t0
+    if keep:
+        return done, dt, tr
     tr.close()
     return done, dt
 
@@ -193,15 +201,15 @@ def run_reference(args):
         return
     cores = os.cpu_count() or 1
     x, y = make_data()
-    warm = min(args.warmup, 1)
-    k, dt = cpu_rounds(x, y, max(1, args.steps), budget_s=120.0, warm=warm)
+    warm = args.warmup
+    k, dt = cpu_rounds(x, y, max(1, args.steps), budget_s=240.0, warm=warm)
     value = k / dt
     sample = (f"{k} timed round(s) of the C2 workload ({N_ROWS:,} rows) after binning and {warm} untimed round(s) "
               f"(C++ restatement of hessboost's CPU hist path, OpenMP on {cores} threads; "
               "the Rust reference cannot be built offline)")
     emit({
         "impl": "reference", "metric": METRIC, "value": value, "unit": UNIT,
-        "n_gpus": args.gpus, "steps": k, "warmup": min(args.warmup, 1),
+        "n_gpus": args.gpus, "steps": k, "warmup": warm,
         "ms_per_step": 1000.0 * dt / k, "higher_is_better": True, "scaling": "strong",
         "vs_baseline": None, "dtype": "f64", "data": "synthetic", "config": config(args.gpus),
         "cpu_baseline": {"value": value, "unit": UNIT, "cores": cores, "kind": "port", "sample": sample},
@@ -489,6 +497,37 @@ def run_c4(args):
     })
 
 
+# ------------------------------------------------------------------ probe
+PROBE_KINDS = {
+    0: "red.shared.add.u32, conflict-free",
+    1: "red.shared.add.u64, conflict-free",
+    2: "atom.shared.add.u32, result used",
+    3: "ld.shared.u32 + st.shared.u32",
+    4: "k_hist32 update: 4 x red.u32 at a random row, diagonal column",
+    5: "64-bit update: 2 x red.u64 at a random row, diagonal column",
+    6: "red.shared.add.u32, 32 lanes on one word",
+}
+
+
+def run_probe(args):
+    """Shared-memory throughput of the histogram update patterns
+    (hb_probe_smem): lane operations per SM clock, one CTA per SM."""
+    import ctypes
+
+    import hessboost_b200 as H
+
+    out = {}
+    for threads in (512, 1024):
+        for kind, what in PROBE_KINDS.items():
+            v = ctypes.c_double()
+            st = H.lib().hb_probe_smem(0, kind, threads, 4096, ctypes.byref(v))
+            if st != H.HB_OK:
+                raise SystemExit(f"hb_probe_smem kind {kind}: status {st}")
+            out.setdefault(str(threads), {})[f"{kind}: {what}"] = round(v.value, 2)
+    emit({"probe": "smem", "unit": "lane operations per SM clock (slowest SM)",
+          "iters": 4096, "results_by_threads_per_cta": out})
+
+
 # ------------------------------------------------------------------ ours
 def main():
     ap = argparse.ArgumentParser()
@@ -497,13 +536,23 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-parity", action="store_true",
+                    help="skip the comparison of the first trees with the oracle (N=1)")
+    ap.add_argument("--parity-rounds", type=int, default=3)
     ap.add_argument("--rows", type=int, default=None,
                     help="rows of the synthetic matrix (default: the workload's own, 10M for "
                          "C2 and 100M for C5; smaller values are for profiling captures)")
     ap.add_argument("--workload", default="c2", choices=["c2", "c3", "c4", "c5"],
                     help="c2: boosting rounds (the headline); c3: multiclass rounds; "
                          "c4: lossguide rounds over a CSR index; c5: batch prediction")
+    ap.add_argument("--probe", choices=["smem"], default=None,
+                    help="smem: measure the shared-memory atomic throughput the histogram "
+                         "kernels are bound by (hb_probe_smem), instead of a workload")
     args = ap.parse_args()
+    if args.probe:
+        claim_stdout()
+        run_probe(args)
+        return
     if args.rows is not None and args.workload == "c2":
         set_rows(args.rows)
     claim_stdout()
@@ -632,18 +681,6 @@ def main():
                  + st["rows_built_gathered"] * (N_COLS + 8 + 4 + bitmap))
     achieved = alg_bytes / (hist_ms / 1000.0) / 1e9 if hist_ms > 0 else 0.0
     peak, peak_kind = peaks()
-    # DRAM bytes per launch: the ratio of DRAM traffic to algorithmic bytes
-    # that one ncu capture of a round's histogram launches measured (traffic
-    # grows with the rows, so it carries to this workload), times this run's
-    # algorithmic bytes per launch
-    traffic = None
-    prof = os.path.join(ROOT, "profiles", "k_hist32_traffic.json")
-    if os.path.exists(prof) and hist_launches:
-        try:
-            ratio = float(json.load(open(prof))["dram_bytes_per_algorithmic_byte"])
-            traffic = ratio * alg_bytes / hist_launches
-        except Exception:  # noqa: BLE001
-            traffic = None
     log(f"[rank {rank}] {args.steps} rounds {ms:.1f} ms; kernel ms {json.dumps(st['ms'])}")
     # per-family breakdown (events around every kernel family), outside the
     # timed region
@@ -680,37 +717,50 @@ def main():
            "scope": "hb_engine_upload of the binned shard + hb_train_begin + hb_train_rounds(K) from "
                     "pinned host buffers on an engine already created (and, for N > 1, already "
                     "connected); trees read back"}
+    # the forest of the end-to-end run (K trees from the base margin): the
+    # same bytes at every GPU count when the sums are exact
+    from hessboost_b200 import model_io
 
-    cpu = None
+    forest = {"xxh64": f"{model_io.xxh64(np.ascontiguousarray(nodes2).tobytes()):016x}",
+              "trees": int(len(ptr2) - 1), "nodes": int(len(nodes2)),
+              "scope": "hb_tree_node records of the end-to-end run's K trees, grown from the base margin"}
+
+    cpu, parity = None, None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         cores = os.cpu_count() or 1
-        k, dt = cpu_rounds(x, y, 3, budget_s=25.0, warm=1)
+        k, dt, tr64 = cpu_rounds(x, y, 3, budget_s=25.0, warm=1, keep=True)
         cpu = {"value": k / dt, "unit": UNIT, "cores": cores, "kind": "port",
                "sample": f"{k} round(s) of the C2 workload ({N_ROWS:,} rows) after binning and 1 untimed round (C++ restatement of "
                          f"hessboost's CPU hist path, OpenMP, {cores} threads)"}
+        if not args.no_parity:
+            parity = c2_parity(eng, params, x, y_shard, base, nodes2, ptr2, tr64, args.parity_rounds)
+        tr64.close()
 
     if rank == 0:
         line = {
             "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True,
             "scaling": "strong", "vs_baseline": None, "dtype": "int64", "data": "synthetic",
-            "config": dict(config(world), rows_per_s=value * N_ROWS,
-                           trees_nodes=int(len(nodes)),
-                           kernel_ms_per_round=per_round,
-                           prep=prep,
-                           timing="device time of the K rounds from CUDA events the engine records "
+            "config": config(world),
+            "details": {"rows_per_s": value * N_ROWS, "trees_nodes": int(len(nodes)),
+                        "kernel_ms_per_round": per_round, "prep": prep,
+                        "timing": "device time of the K rounds from CUDA events the engine records "
                                   "on its stream around them (rounds replayed as a CUDA graph; "
                                   "event nodes around each histogram launch); per-family "
-                                  "breakdown from a separate instrumented run"),
+                                  "breakdown from a separate instrumented run"},
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
-                         "frac": achieved / peak, "traffic": traffic,
+                         "frac": achieved / peak, "traffic": None,
                          "kernel": "k_hist32", "launches": hist_launches,
-                         "traffic_source": "profiles/k_hist32_c2_5M.md (DRAM/algorithmic ratio "
-                                           "of one ncu capture, scaled to these launches)",
                          "avg_launch_ms": hist_ms / max(hist_launches, 1),
                          "alg_bytes_per_launch": alg_bytes / max(hist_launches, 1),
+                         "alg_bytes_rule": f"per built row: {N_COLS} B of bins + 8 B (g, h) pair + "
+                                           f"{bitmap} B missing bitmap + 4 B row id when gathered",
+                         "traffic_note": "DRAM bytes per launch come from an ncu capture, not from "
+                                         "this run",
                          "peak_kind": peak_kind + " (MEASURED_PEAKS.json hbm_gbs)"},
             "cpu_baseline": cpu,
+            "parity": parity,
+            "forest": forest,
             "e2e": e2e,
             "gpu_launches": launches,
             "clocks": clocks,
@@ -719,6 +769,41 @@ def main():
     eng.close()
     if world > 1:
         dist.destroy_process_group()
+
+
+def c2_parity(eng, params, x, y, base, nodes, ptr, tr64, rounds):
+    """The GPU's first trees at C2 against the oracle on the same 10M-row
+    matrix: (1) the oracle's fixed-point mode, every node field and the
+    training margins bit for bit; (2) the oracle's f64 mode (the reference's
+    summation), round by round from the same margins, under the north-star
+    criteria (tests/parity.py)."""
+    import parity as P
+
+    t0 = time.perf_counter()
+    rounds = min(rounds, len(ptr) - 1)
+    trq = oracle_trainer(x, y, fixed_point=True)
+    on, op = trq.rounds(rounds)
+    om = trq.margins()[:, 0]
+    trq.close()
+    gn = nodes[: int(ptr[rounds])]
+    exact, where = P.forest_bit_exact(gn, ptr[: rounds + 1], on, op)
+    eng.train_begin(y, base)
+    eng.train_rounds(params, rounds)
+    gm = eng.read_margins()
+    m_exact = bool(np.array_equal(gm.view(np.uint32), om.view(np.uint32)))
+    t1 = time.perf_counter()
+    eng.train_begin(y, base)
+    f64 = P.forced_f64_rounds(eng, params, tr64, rounds)
+    t2 = time.perf_counter()
+    log(f"parity: fixed {t1 - t0:.1f}s f64 {t2 - t1:.1f}s")
+    return {"rows": int(len(y)), "fixed_point_rounds": rounds,
+            "fixed_point_bit_exact": bool(exact), "fixed_point_first_difference": where or None,
+            "fixed_point_margins_bit_exact": m_exact,
+            "f64": f64,
+            "pass": bool(exact and m_exact and f64["pass"]),
+            "criteria": "fixed point: every node field and margin bit for bit; f64 mode, each round "
+                        "from the same margins: structure equal except gain ties (1e-5), leaves "
+                        "rtol 1e-5 atol 1e-7, margins rtol 1e-6 atol 1e-7"}
 
 
 if __name__ == "__main__":

@@ -254,6 +254,8 @@ SIGNATURES = {
                                ctypes.c_uint64, _u64p],
     "hb_engine_upload_csr": [_vp, _u64p, _u32p, _f32p, ctypes.c_uint64, ctypes.c_uint32, ctypes.c_uint32, _u32p,
                              _f32p, ctypes.c_uint64, _u64p],
+    "hb_probe_smem": [ctypes.c_int32, ctypes.c_int32, ctypes.c_int32, ctypes.c_int32,
+                      ctypes.POINTER(ctypes.c_double)],
 }
 _STRING_RESULT = ("hb_engine_last_error", "hb_sketch_last_error")
 
@@ -699,6 +701,16 @@ class Engine:
         rows = np.ascontiguousarray(rows, np.uint32)
         out = (GradStats * self.matrix.total_bins)()
         self._c(lib().hb_build(self.h, _ptr(rows, ctypes.c_uint32), rows.size, out), "hb_build")
+        return np.ctypeslib.as_array(out).view(np.float64).reshape(-1, 2).copy()
+
+    def build_features(self, rows, features):
+        """hb_build_features: the histogram of `rows`; the bins of `features`
+        are the ones the caller reads."""
+        rows = np.ascontiguousarray(rows, np.uint32)
+        feats = np.ascontiguousarray(features, np.uint32)
+        out = (GradStats * self.matrix.total_bins)()
+        self._c(lib().hb_build_features(self.h, _ptr(rows, ctypes.c_uint32), rows.size,
+                                        _ptr(feats, ctypes.c_uint32), feats.size, out), "hb_build_features")
         return np.ctypeslib.as_array(out).view(np.float64).reshape(-1, 2).copy()
 
     def build_noalloc(self, rows_ptr, n, out_ptr):

@@ -1901,4 +1901,9 @@ hb_status engine_fail(hb_engine* e, const char* what, cudaError_t code) { return
 
 hb_status engine_refuse(hb_engine* e, const char* why) { return refuse(e, why); }
 
+hb_status engine_invalid(hb_engine* e, const char* why) {
+  refuse(e, why);
+  return HB_INVALID_ARGUMENT;
+}
+
 }  // namespace hb

@@ -27,5 +27,7 @@ void engine_view(const hb_engine* e, EngineView* v);
 hb_status engine_fail(hb_engine* e, const char* what, cudaError_t code);
 // Record why a call was refused; the engine stays usable.
 hb_status engine_refuse(hb_engine* e, const char* why);
+// Record why an argument was rejected; returns HB_INVALID_ARGUMENT.
+hb_status engine_invalid(hb_engine* e, const char* why);
 
 }  // namespace hb

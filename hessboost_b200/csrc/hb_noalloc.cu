@@ -11,10 +11,16 @@
 //                          256 bins); zeroed by every call
 //   [512 KiB, +256)        the one histogram entry (HEntry)
 //   [512 KiB + 256, +256)  the level state the histogram kernels read
-//   [512 KiB + 512, +8)    bad-row counter (must be zero when a call starts:
-//                          zero at module load and returned to zero by every
-//                          call) and the status word the host reads back
+//   [512 KiB + 512, +8)    bad-row counter and the status word the host
+//                          reads back; both are set to zero at the start of
+//                          every call (cudaMemsetAsync, which allocates
+//                          nothing), so a call that failed half way cannot
+//                          leave a stale verdict for the next one
 // An index with more bins than kNoAllocMaxBins is refused.
+//
+// Ordering: the kernels run on the engine's stream. `rows_dev` must hold its
+// final values before the call starts: a caller that produced it on another
+// stream synchronises that stream (or the device) first.
 //
 // The first call on a device (with that device current) looks up the
 // scratch's device address with cudaGetSymbolAddress; that may load this
@@ -78,9 +84,8 @@ __global__ void k_na_prepare(longlong2* __restrict__ hist, uint32_t total_bins,
 }
 
 // One entry over all n rows, or, when a row id was bad, no entry at all (the
-// histogram kernels then read no row). Publishes the verdict and clears the
-// counter for the next call.
-__global__ void k_na_gate(uint64_t n, LevelState* __restrict__ ls, unsigned* __restrict__ bad,
+// histogram kernels then read no row). Publishes the verdict.
+__global__ void k_na_gate(uint64_t n, LevelState* __restrict__ ls, const unsigned* __restrict__ bad,
                           unsigned* __restrict__ status) {
   const unsigned b = *bad;
   LevelState s{};
@@ -88,7 +93,6 @@ __global__ void k_na_gate(uint64_t n, LevelState* __restrict__ ls, unsigned* __r
   s.hist_rows = b ? 0 : n;
   *ls = s;
   *status = b;
-  *bad = 0;
 }
 
 bool on_device(const void* p, int device) {
@@ -115,9 +119,11 @@ extern "C" hb_status hb_build_noalloc(hb_engine* e, const uint32_t* rows_dev, ui
   const DevConst& c = *v.c;
   if (c.total_bins > kNoAllocMaxBins)
     return engine_refuse(e, "hb_build_noalloc: the index has more than 32768 bins, the scratch limit");
-  if (!out_dev || (n && !rows_dev) || n > c.n_rows) return HB_INVALID_ARGUMENT;
+  if (!out_dev) return engine_invalid(e, "hb_build_noalloc: out_dev is NULL");
+  if (n && !rows_dev) return engine_invalid(e, "hb_build_noalloc: rows_dev is NULL");
+  if (n > c.n_rows) return engine_invalid(e, "hb_build_noalloc: more row ids than the index has rows");
   if (reinterpret_cast<uintptr_t>(out_dev) % 8 || reinterpret_cast<uintptr_t>(rows_dev) % 4)
-    return HB_INVALID_ARGUMENT;
+    return engine_invalid(e, "hb_build_noalloc: out_dev must be 8-byte and rows_dev 4-byte aligned");
   if (!on_device(out_dev, v.device) || (n && !on_device(rows_dev, v.device)))
     return engine_refuse(e, "hb_build_noalloc: rows and out must be device memory of the engine's GPU");
 
@@ -136,6 +142,9 @@ extern "C" hb_status hb_build_noalloc(hb_engine* e, const uint32_t* rows_dev, ui
   unsigned* status = bad + 1;
 
   cudaStream_t s = v.stream;
+  // the counter and the verdict start at zero whatever an earlier call left
+  rc = cudaMemsetAsync(bad, 0, 2 * sizeof(unsigned), s);
+  if (rc != cudaSuccess) return engine_fail(e, "hb_build_noalloc: clear the verdict", rc);
   const uint64_t work = std::max<uint64_t>(n, c.total_bins);
   const int grid = (int)std::max<uint64_t>(1, std::min<uint64_t>((work + 255) / 256, 4ull * v.n_sm));
   k_na_prepare<<<grid, 256, 0, s>>>(hist, c.total_bins, rows_dev, n, c.n_rows, entry, bad);

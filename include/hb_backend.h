@@ -225,7 +225,12 @@ hb_status hb_build_features(hb_engine* e, const uint32_t* rows, uint64_t n,
  * up that array's address, and should come before any stream capture.
  * Calls on one device share the array; the library serialises them, since
  * overlapping calls would race on it. Bad row ids (not ascending, or past
- * the index) are refused with out_dev zeroed; no row is read. */
+ * the index) are refused with out_dev zeroed; no row is read. The kernels
+ * run on the engine's stream, so rows_dev must be complete when the call
+ * starts (synchronise the stream that wrote it first). HB_INVALID_ARGUMENT,
+ * with the reason in hb_engine_last_error, for a NULL buffer, more row ids
+ * than the index has rows, or out_dev not 8-byte / rows_dev not 4-byte
+ * aligned. */
 hb_status hb_build_noalloc(hb_engine* e, const uint32_t* rows_dev, uint64_t n,
                            hb_grad_stats* out_dev);
 
@@ -414,6 +419,16 @@ hb_status hb_engine_upload_csr(hb_engine* e, const uint64_t* indptr, const uint3
  * container (container.rs:245 `xxh64`). The section table itself is laid
  * out by the Python host (model_io.to_native_binary). */
 hb_status hb_xxh64(const void* data, uint64_t len, uint64_t* out);
+
+/* ---- measurement (no counterpart in the reference) ------------------ */
+/* The shared-memory throughput a histogram update pattern reaches on GPU
+ * `device`: one CTA of `threads` threads per SM issues `iters` iterations
+ * of pattern `kind` (0 conflict-free red.u32, 1 red.u64, 2 atom.u32 with
+ * its result used, 3 ld+st, 4 four red.u32 at random rows, 5 two red.u64
+ * at random rows, 6 one word per warp); *lane_ops_per_clk receives lane
+ * operations per SM clock cycle (clock64), the slowest SM's. */
+hb_status hb_probe_smem(int32_t device, int32_t kind, int32_t threads, int32_t iters,
+                        double* lane_ops_per_clk);
 
 #ifdef __cplusplus
 }

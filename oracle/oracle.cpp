@@ -1145,6 +1145,19 @@ int64_t orc_trainer_rounds(orc_trainer* tr, int32_t rounds, orc_node* nodes, uin
 
 void orc_trainer_free(orc_trainer* tr) { delete tr; }
 
+uint64_t orc_trainer_margins(const orc_trainer* tr, float* out, uint64_t cap) {
+  if (!tr) return 0;
+  const uint64_t n = tr->margins.size();
+  if (out && cap >= n) std::copy(tr->margins.begin(), tr->margins.end(), out);
+  return n;
+}
+
+int32_t orc_trainer_set_margins(orc_trainer* tr, const float* m, uint64_t n) {
+  if (!tr || !m || n != tr->margins.size()) return -2;
+  std::copy(m, m + n, tr->margins.begin());
+  return 0;
+}
+
 int64_t orc_train(const orc_params* pp, const float* x, uint64_t n, uint64_t nc,
                   const float* labels, int32_t rounds, orc_node* nodes, uint64_t nodes_cap,
                   uint64_t* tree_ptr, float* base_out, float* margins_out) {

@@ -89,6 +89,12 @@ orc_trainer* orc_trainer_new(const orc_params* p, const float* x, uint64_t n, ui
 int64_t orc_trainer_rounds(orc_trainer* t, int32_t rounds, orc_node* nodes, uint64_t nodes_cap,
                            uint64_t* tree_ptr);
 void orc_trainer_free(orc_trainer* t);
+/* The session's training margins (n * n_outputs, row-major): copied to `out`
+ * when `cap` holds them; returns their count. */
+uint64_t orc_trainer_margins(const orc_trainer* t, float* out, uint64_t cap);
+/* Replace the session's training margins (the next round's gradients are
+ * taken there); -2 when `n` is not the session's margin count. */
+int32_t orc_trainer_set_margins(orc_trainer* t, const float* m, uint64_t n);
 
 /* The same on a CSR matrix (DMatrix::from_csr: absent cells missing),
  * binned into a CSR index of global bins (only stored cells are read). */

@@ -120,6 +120,10 @@ def lib():
         L.orc_cuts_csr.restype = ctypes.c_int64
         L.orc_cuts_csr.argtypes = [u64p, u32p, f32p, ctypes.c_uint64, ctypes.c_uint64, ctypes.c_int32, u32p, f32p,
                                    ctypes.c_uint64]
+        L.orc_trainer_margins.restype = ctypes.c_uint64
+        L.orc_trainer_margins.argtypes = [ctypes.c_void_p, f32p, ctypes.c_uint64]
+        L.orc_trainer_set_margins.restype = ctypes.c_int32
+        L.orc_trainer_set_margins.argtypes = [ctypes.c_void_p, f32p, ctypes.c_uint64]
         L.orc_fixed_scale.restype = ctypes.c_int32
         L.orc_fixed_scale.argtypes = [ctypes.c_float, ctypes.c_uint64]
         _lib = L
@@ -392,6 +396,17 @@ class Trainer:
         got = lib().orc_trainer_rounds(self.h, k, nodes.ctypes.data_as(ctypes.POINTER(OrcNode)), cap, _p(ptr, ctypes.c_uint64))
         assert got >= 0, got
         return nodes[: int(ptr[got])].copy(), ptr[: got + 1].copy()
+
+    def margins(self):
+        """The session's training margins, (n, n_outputs)."""
+        n = int(lib().orc_trainer_margins(self.h, None, 0))
+        out = np.zeros(n, np.float32)
+        lib().orc_trainer_margins(self.h, _p(out, ctypes.c_float), n)
+        return out.reshape(-1, self.p.n_outputs)
+
+    def set_margins(self, m):
+        m = np.ascontiguousarray(m, np.float32).ravel()
+        assert lib().orc_trainer_set_margins(self.h, _p(m, ctypes.c_float), m.size) == 0
 
     def close(self):
         if self.h:

@@ -23,6 +23,13 @@ def test_reference_arm_prints_the_contract_line():
         assert key in d, key
     assert d["value"] > 0 and d["unit"] == "rounds/s" and d["higher_is_better"] is True
     assert d["config"]["rows"] == 20000
+    # the same run parameters and config as the GPU arm's line
+    assert d["steps"] == 2 and d["warmup"] == 1
+    sys.path.insert(0, ROOT)
+    import bench
+
+    bench.set_rows(20000)
+    assert d["config"] == json.loads(json.dumps(bench.config(1)))
     cb = d["cpu_baseline"]
     assert cb["value"] == d["value"] and cb["kind"] in ("port", "reference") and cb["cores"] >= 1
     assert d["e2e"] == {"value": d["value"], "unit": d["unit"], "h2d_bytes_per_step": 0,

@@ -122,11 +122,11 @@ def test_softmax_intercepts_match_oracle():
                                       O.intercepts(2, y, k).view(np.uint32))
 
 
-def test_integration_ffi_block_binds_every_entry_point():
-    # the Rust `extern "C"` block a maintainer would add declares exactly the
+def test_rust_ffi_module_binds_every_entry_point():
+    # the Rust `extern "C"` module a maintainer would add declares exactly the
     # header's entry points
-    doc = open(os.path.join(os.path.dirname(HEADER), "..", "INTEGRATION.md")).read()
-    assert sorted(set(re.findall(r"pub fn (hb_\w+)\(", doc))) == declared_symbols()
+    src = open(os.path.join(os.path.dirname(HEADER), "hb_backend_ffi.rs")).read()
+    assert sorted(set(re.findall(r"pub fn (hb_\w+)\(", src))) == declared_symbols()
 
 
 @pytest.mark.parametrize("bad,name", [

@@ -1,5 +1,11 @@
 """hb_build_noalloc (the node histogram on caller-owned device buffers, with
-static scratch) against hb_build, the entry point it varies.
+static scratch) against hb_build, the entry point it varies, and against the
+CPU oracle's fixed-point histogram of the same rows.
+
+Some callers cannot allocate device memory while they run: a host framework
+that hands all of HBM to its own pool allocator, or one that forbids
+cudaMalloc once training has started. This entry point serves them, and the
+tests below check both its results and that it allocates nothing.
 
 Tolerance: none. Both entry points sum the same int64 fixed-point values
 with the same kernel and dequantise once, so their f64 outputs are equal
@@ -14,6 +20,7 @@ import numpy as np
 import pytest
 
 import hessboost_b200 as H
+import oracle_lib as O
 from hessboost_b200 import synth
 
 pytestmark = pytest.mark.gpu
@@ -46,8 +53,53 @@ def staged():
     rng = np.random.default_rng(5)
     e.load_margins((rng.standard_normal(m.n_rows) * 0.5).astype(np.float32))
     assert e.gradients(H.HB_LOSS_LOGISTIC, y)
+    e.x = x
     yield e, m
     e.close()
+
+
+def test_matches_oracle_fixed_point(staged):
+    """The no-allocation histogram equals the oracle's int64 fixed-point sums
+    of the same rows, dequantised with the engine's scales."""
+    e, m = staged
+    gp, sg, sh = e.read_gradients()
+    rows = np.arange(1, m.n_rows, 7, dtype=np.uint32)
+    q = O.hist(e.x, m.feature_offset, m.cut_values, rows, gp, fixed_point=True, sg=sg, sh=sh)
+    want = np.stack([q[:, 0].astype(np.float64) * 2.0 ** -sg, q[:, 1].astype(np.float64) * 2.0 ** -sh], 1)
+    np.testing.assert_array_equal(_noalloc(e, rows, m.total_bins), want)
+
+
+def test_allocates_no_device_memory(staged):
+    """After the first call (which only looks up the static array's address),
+    further calls leave the device's free memory unchanged."""
+    e, m = staged
+    rows_a = _device(np.arange(0, m.n_rows, 2).astype(np.int32), torch.int32)
+    rows_b = _device(np.arange(1, m.n_rows, 5).astype(np.int32), torch.int32)
+    out = torch.zeros((m.total_bins, 2), dtype=torch.float64, device="cuda:0")
+    torch.cuda.synchronize()
+    e.build_noalloc(rows_a.data_ptr(), rows_a.numel(), out.data_ptr())
+    free0 = torch.cuda.mem_get_info(0)[0]
+    for r in (rows_b, rows_a, rows_b):
+        e.build_noalloc(r.data_ptr(), r.numel(), out.data_ptr())
+    torch.cuda.synchronize()
+    assert torch.cuda.mem_get_info(0)[0] == free0
+
+
+def test_invalid_arguments_record_a_reason(staged):
+    e, m = staged
+    rows = torch.arange(10, dtype=torch.int32, device="cuda:0")
+    out = torch.zeros((m.total_bins, 2), dtype=torch.float64, device="cuda:0")
+    torch.cuda.synchronize()
+    cases = [(rows.data_ptr(), m.n_rows + 1, out.data_ptr(), "more row ids"),
+             (rows.data_ptr(), 10, 0, "NULL"),
+             (rows.data_ptr() + 2, 4, out.data_ptr(), "aligned")]
+    for rp, n, op, why in cases:
+        with pytest.raises(H.HbError, match=why) as ex:
+            e.build_noalloc(rp, n, op)
+        assert ex.value.status == H.HB_INVALID_ARGUMENT
+    # still usable
+    np.testing.assert_allclose(_noalloc(e, np.arange(0, m.n_rows, 3, dtype=np.uint32), m.total_bins),
+                               e.build(np.arange(0, m.n_rows, 3, dtype=np.uint32)), **TOL)
 
 
 def test_two_calls_in_a_row_match_build(staged):
