@@ -86,11 +86,32 @@ class RegParams(ctypes.Structure):
     ]
 
 
+def node_gain(total, reg, lower=-math.inf, upper=math.inf):
+    """xgb_node_gain (src/tree/builder/shared.rs:136) of a node with
+    statistics `total` = (G, H) and monotone bounds [lower, upper]: the
+    scorer's root gain a ScanRequest carries (f32)."""
+    g, h = float(total[0]), float(total[1])
+    if h <= 0.0:
+        return 0.0
+    a = reg.alpha
+    t = g - a if g > a else (g + a if g < -a else 0.0)
+    w = -t / (h + reg.lambda_)
+    if reg.max_delta_step != 0.0 and abs(w) > reg.max_delta_step:
+        w = math.copysign(reg.max_delta_step, w)
+    w32 = np.float32(w)
+    lo, up = np.float32(lower), np.float32(upper)
+    w32 = lo if w32 < lo else (up if w32 > up else w32)
+    wf = float(w32)
+    gain = -(2.0 * g * wf + (h + reg.lambda_) * float(np.float32(w32 * w32)) + 2.0 * a * abs(wf))
+    return float(np.float32(gain))
+
+
 class ScanRequest(ctypes.Structure):
     _fields_ = [
         ("slot", ctypes.c_uint32),
         ("n_features", ctypes.c_uint32),
         ("features", ctypes.POINTER(ctypes.c_uint32)),
+        ("directions", ctypes.POINTER(ctypes.c_int8)),
         ("total", GradStats),
         ("root_gain", ctypes.c_float),
         ("lower", ctypes.c_float),
@@ -164,6 +185,8 @@ class TrainParamsC(ctypes.Structure):
         ("scale_pos_weight", ctypes.c_float),
         ("base_score", ctypes.c_float),
         ("num_class", ctypes.c_int32),
+        ("n_monotone", ctypes.c_int32),
+        ("monotone", ctypes.POINTER(ctypes.c_int8)),
     ]
 
 
@@ -313,6 +336,7 @@ class TrainingParams:
     base_score: float = float("nan")
     max_bin: int = 256
     num_class: int = 0
+    monotone_constraints: tuple = ()  # per feature: 1 increasing, -1 decreasing, 0 none
 
     def validate(self):
         """The reference's parameter checks for these fields
@@ -355,6 +379,16 @@ class TrainingParams:
                "lossguide growth needs a bound: set max_leaves or max_depth")
         ensure("grow_policy", self.grow_policy in ("depthwise", "lossguide"),
                f"must be depthwise or lossguide, got {self.grow_policy!r}")
+        ensure("monotone_constraints", all(int(v) in (-1, 0, 1) and int(v) == v for v in self.monotone_constraints),
+               "every entry must be 1 (increasing), -1 (decreasing) or 0 (none)")
+        return self
+
+    def validate_for(self, n_features):
+        """validate_constraints (src/training/validate.rs:283): the
+        constraints name only features of the training matrix."""
+        if len(self.monotone_constraints) > n_features:
+            raise ValueError("invalid parameter `monotone_constraints`: contains more entries than the "
+                             "training matrix has features")
         return self
 
     def loss_kind(self):
@@ -393,6 +427,10 @@ class TrainingParams:
         c.scale_pos_weight = self.scale_pos_weight
         c.base_score = self.base_score
         c.num_class = self.num_class
+        if len(self.monotone_constraints):
+            c._mono = np.ascontiguousarray(self.monotone_constraints, np.int8)  # kept alive with the struct
+            c.n_monotone = c._mono.size
+            c.monotone = c._mono.ctypes.data_as(ctypes.POINTER(ctypes.c_int8))
         return c
 
     def reg(self):
@@ -795,17 +833,27 @@ class Engine:
                                         _ptr(sib, ctypes.c_uint32), len(siblings)), "hb_build_resident")
 
     def scan_resident(self, reg, requests):
+        """requests: (slot, (G, H), features[, directions[, (lower, upper)[, root_gain]]]);
+        root_gain defaults to the node's gain at its bounds under `reg`."""
         keep = []
         arr = (ScanRequest * len(requests))()
-        for i, (slot, total, features) in enumerate(requests):
+        for i, req in enumerate(requests):
+            slot, total, features = req[:3]
             f = np.ascontiguousarray(features, np.uint32)
             keep.append(f)
             arr[i].slot = slot
             arr[i].n_features = f.size
             arr[i].features = _ptr(f, ctypes.c_uint32)
+            if len(req) > 3 and req[3] is not None:
+                d = np.ascontiguousarray(req[3], np.int8)
+                assert d.size == f.size
+                keep.append(d)
+                arr[i].directions = d.ctypes.data_as(ctypes.POINTER(ctypes.c_int8))
             arr[i].total = GradStats(*total)
-            arr[i].lower = -math.inf
-            arr[i].upper = math.inf
+            lo, up = req[4] if len(req) > 4 and req[4] is not None else (-math.inf, math.inf)
+            arr[i].lower = lo
+            arr[i].upper = up
+            arr[i].root_gain = req[5] if len(req) > 5 else node_gain(total, reg, lo, up)
         out = (NodeScan * len(requests))()
         self._c(lib().hb_scan_resident(self.h, ctypes.byref(reg), arr, len(requests), out), "hb_scan_resident")
         return [out[i] for i in range(len(requests))]
@@ -1035,6 +1083,8 @@ def train(params, x=None, y=None, rounds=10, device=0, matrix=None, engine=None)
     refuses the input (a feature with 2^24 or more present values), the
     reference's host sketch bins it instead, with the same cuts."""
     params.validate()
+    if x is not None or matrix is not None:
+        params.validate_for((matrix.n_cols if matrix is not None else np.asarray(x).shape[1]))
     y = np.ascontiguousarray(y, np.float32)
     eng = engine or Engine(device)
     try:

@@ -150,6 +150,10 @@ struct hb_engine {
   size_t wstride = 0;      // WNodes per class in wtree
   int lg_alloc = 0;     // leaves the lossguide buffers hold (0: none)
   int alloc_classes = 0;
+  // monotone constraints of the training run (one direction per feature)
+  // and the per-(node, feature) directions of a RowEngine scan
+  DevBuf<int8_t> mono, scan_dirs;
+  std::vector<int8_t> h_mono;
 };
 
 namespace {
@@ -609,6 +613,10 @@ hb_status grow_tree_device(hb_engine* e, const hb_train_params* p, bool to_fores
                                              : grow_device(e, p, to_forest);
 }
 
+hb_status stage_monotone(hb_engine* e, const hb_train_params* p);
+
+// The parameters device growth takes (refused otherwise), and the run's
+// monotone constraints staged on the device.
 hb_status check_params(hb_engine* e, const hb_train_params* p) {
   if (!p) return HB_INVALID_ARGUMENT;
   if (p->grow_policy == HB_GROW_LOSSGUIDE) {
@@ -635,6 +643,35 @@ hb_status check_params(hb_engine* e, const hb_train_params* p) {
   } else if (e->n_out != 1) {
     return refuse(e, "a multi:softmax run is loaded (hb_train_begin resets it)");
   }
+  if (!e->uploaded) return refuse(e, "no index uploaded");
+  return stage_monotone(e, p);
+}
+
+// The run's monotone constraints on the device (before any capture): one
+// direction per feature, or none (c.mono = NULL) when every one is 0.
+hb_status stage_monotone(hb_engine* e, const hb_train_params* p) {
+  std::vector<int8_t> d(e->c.n_cols, 0);
+  bool any = false;
+  if (p->n_monotone < 0 || (p->n_monotone > 0 && !p->monotone)) return HB_INVALID_ARGUMENT;
+  if ((uint32_t)p->n_monotone > e->c.n_cols)
+    return refuse(e, "more monotone constraints than features");
+  for (int32_t f = 0; f < p->n_monotone; ++f) {
+    const int8_t v = p->monotone[f];
+    if (v < -1 || v > 1) return refuse(e, "a monotone constraint must be -1, 0 or 1");
+    d[f] = v;
+    any = any || v != 0;
+  }
+  if (!any) {
+    e->c.mono = nullptr;
+    return HB_OK;
+  }
+  if (d != e->h_mono || !e->mono.p) {
+    HB_CK(e, e->mono.alloc(d.size()));
+    HB_CK(e, cudaMemcpyAsync(e->mono.p, d.data(), d.size(), cudaMemcpyHostToDevice, e->stream));
+    HB_CK(e, cudaStreamSynchronize(e->stream));
+    e->h_mono = d;
+  }
+  e->c.mono = e->mono.p;
   return HB_OK;
 }
 
@@ -730,6 +767,8 @@ hb_status hb_engine_destroy(hb_engine* e) {
   e->seg_total.release();
   e->row_stats.release();
   e->flags.release();
+  e->mono.release();
+  e->scan_dirs.release();
   if (e->stream) cudaStreamDestroy(e->stream);
   delete e;
   return HB_OK;
@@ -1434,30 +1473,48 @@ hb_status hb_scan_resident(hb_engine* e, const hb_reg_params* reg, const hb_scan
   c.alpha = reg->alpha;
   c.mds = reg->max_delta_step;
   c.mcw = reg->min_child_weight;
+  c.mono = nullptr;  // the requests' own directions apply
   cudaStream_t s = e->stream;
   Scale h;
   HB_CK(e, cudaMemcpyAsync(&h, e->scale.p, sizeof(Scale), cudaMemcpyDeviceToHost, s));
   HB_CK(e, cudaStreamSynchronize(s));
+  // every request is checked before any launch
   std::vector<Front> fr(n);
+  std::vector<int8_t> dirs((size_t)n * c.n_cols, 0);
   for (uint32_t k = 0; k < n; ++k) {
-    if (req[k].slot >= e->resident_slots) return refuse(e, "slot not reserved");
-    fr[k].slot = (int32_t)req[k].slot;
-    fr[k].g = std::llrint(std::ldexp(req[k].total.grad, h.sg));
-    fr[k].h = std::llrint(std::ldexp(req[k].total.hess, h.sh));
+    const hb_scan_request& q = req[k];
+    if (q.slot >= e->resident_slots) return refuse(e, "slot not reserved");
+    if (q.n_features && !q.features) return HB_INVALID_ARGUMENT;
+    for (uint32_t j = 0; j < q.n_features; ++j) {
+      const uint32_t f = q.features[j];
+      if (f >= c.n_cols) return HB_INVALID_ARGUMENT;
+      const int8_t d = q.directions ? q.directions[j] : 0;
+      if (d < -1 || d > 1) return refuse(e, "a monotone direction must be -1, 0 or 1");
+      dirs[(size_t)k * c.n_cols + f] = d;
+    }
+    fr[k].slot = (int32_t)q.slot;
+    fr[k].g = std::llrint(std::ldexp(q.total.grad, h.sg));
+    fr[k].h = std::llrint(std::ldexp(q.total.hess, h.sh));
+    fr[k].lower = (double)q.lower;
+    fr[k].upper = (double)q.upper;
+    fr[k].root_gain = q.root_gain;
+    fr[k].root_gain_given = 1;
   }
   HB_CK(e, e->front[0].alloc(n));
   HB_CK(e, e->cand.alloc((size_t)n * c.n_cols));
+  HB_CK(e, e->scan_dirs.alloc(dirs.size()));
   e->alloc_depth = -1;
   LevelState lsh{};
-  lsh.n_front = (int32_t)n;
   HB_CK(e, cudaMemcpyAsync(e->front[0].p, fr.data(), sizeof(Front) * n, cudaMemcpyHostToDevice, s));
-  HB_CK(e, cudaMemcpyAsync(e->ls.p, &lsh, sizeof(LevelState), cudaMemcpyHostToDevice, s));
+  HB_CK(e, cudaMemcpyAsync(e->scan_dirs.p, dirs.data(), dirs.size(), cudaMemcpyHostToDevice, s));
   for (uint32_t k0 = 0; k0 < n; k0 += 65535) {  // grid.y holds at most 65,535 nodes
     const uint32_t m = std::min<uint32_t>(65535u, n - k0);
     lsh.n_front = (int32_t)m;
     HB_CK(e, cudaMemcpyAsync(e->ls.p, &lsh, sizeof(LevelState), cudaMemcpyHostToDevice, s));
     launch_scan(c, e->fo.p, e->resident.p, e->front[0].p + k0, e->ls.p, nullptr, 0, e->scale.p,
-                (int)m, e->cand.p + (size_t)k0 * c.n_cols, s);
+                (int)m, e->cand.p + (size_t)k0 * c.n_cols, s, e->scan_dirs.p + (size_t)k0 * c.n_cols);
+    // the level state is read by the launch before the next chunk's copy
+    HB_CK(e, cudaStreamSynchronize(s));
   }
   HB_CK(e, cudaGetLastError());
   std::vector<Cand> cd((size_t)n * c.n_cols);
@@ -1465,27 +1522,34 @@ hb_status hb_scan_resident(hb_engine* e, const hb_reg_params* reg, const hb_scan
   HB_CK(e, cudaStreamSynchronize(s));
   const double ig = std::ldexp(1.0, -h.sg), ih = std::ldexp(1.0, -h.sh);
   for (uint32_t k = 0; k < n; ++k) {
+    // the features' winners merged in the request's order from the empty
+    // split (merge_scans, cuda-kernels/src/categorical.rs:637): a finite
+    // loss replaces the incumbent when larger, or, from a lower feature,
+    // when not smaller (need_replace, src/tree/builder/mod.rs:313)
     float best = 0.0f;
-    int best_f = -1;
+    uint32_t best_feature = 0;
+    int chosen = -1;
     for (uint32_t j = 0; j < req[k].n_features; ++j) {
       const uint32_t f = req[k].features[j];
-      if (f >= c.n_cols) return HB_INVALID_ARGUMENT;
-      const Cand& x = cd[(size_t)k * c.n_cols + f];
-      if (x.loss > best) {
-        best = x.loss;
-        best_f = (int)f;
+      const float loss = cd[(size_t)k * c.n_cols + f].loss;
+      if (std::isinf(loss) || std::isnan(loss)) continue;
+      const bool replace = best_feature <= f ? loss > best : !(best > loss);
+      if (replace) {
+        best = loss;
+        best_feature = f;
+        chosen = (int)f;
       }
     }
     hb_node_scan& o = out[k];
     std::memset(&o, 0, sizeof(o));
-    if (best_f < 0) {
+    if (chosen < 0) {
       o.kind = HB_SCAN_EMPTY;
       continue;
     }
-    const Cand& x = cd[(size_t)k * c.n_cols + best_f];
-    const uint32_t fs = e->h_fo[best_f];
+    const Cand& x = cd[(size_t)k * c.n_cols + chosen];
+    const uint32_t fs = e->h_fo[chosen];
     o.kind = HB_SCAN_NUMERIC;
-    o.feature = (uint32_t)best_f;
+    o.feature = (uint32_t)chosen;
     o.loss_chg = x.loss;
     o.backward = x.default_left ? 1 : 0;
     if (!x.default_left) {

@@ -64,15 +64,23 @@ struct DevConst {
   double lambda, alpha, gamma, mcw, mds;
   float eta;
   int32_t max_depth;
+  // monotone direction per feature (+1, -1, 0; constraints.rs:12), device
+  // memory, or NULL when no feature is constrained
+  const int8_t* mono;
 };
 
-// One frontier entry of the level being grown.
+// One frontier entry of the level being grown. The first 32 bytes are read
+// as two int4 by the histogram plan (load_front_cg).
 struct Front {
   int32_t node;       // tree node id
   int32_t slot;       // histogram slot (or -1)
   uint32_t begin;     // segment in the current row buffer
   uint32_t len;
   long long g, h;     // node statistics (fixed point)
+  // the node's monotone weight bounds (constraints.rs:44 `Bounds`)
+  double lower = -__builtin_huge_val(), upper = __builtin_huge_val();
+  float root_gain = 0.0f;       // the caller's root gain (RowEngine scans) ...
+  int32_t root_gain_given = 0;  // ... used when set, else computed
 };
 
 // The best candidate of one (node, feature) pair.
@@ -155,6 +163,7 @@ struct LgNode {
   int32_t bin;        // last global bin going left, -1 = below every bin
   int32_t default_left;
   long long lg, lh;   // that split's left child statistics
+  double lower, upper;  // the node's monotone weight bounds
 };
 
 struct LgState {

@@ -929,9 +929,44 @@ __device__ __forceinline__ double xgb_calc_weight(double g, double h, const DevC
   return w;
 }
 
-// xgb_weight with the default (infinite) monotone bounds.
-__device__ __forceinline__ float xgb_weight(double g, double h, const DevConst& c) {
-  return __double2float_rn(xgb_calc_weight(g, h, c));
+// shared.rs:113 `xgb_weight`: rounded to f32, then clamped to the node's
+// monotone bounds as f32 (shared.rs:100 `apply_bounds`).
+__device__ __forceinline__ float xgb_weight(double g, double h, const DevConst& c,
+                                            float lo = -INFINITY, float up = INFINITY) {
+  const float w = __double2float_rn(xgb_calc_weight(g, h, c));
+  return w < lo ? lo : (w > up ? up : w);
+}
+
+// f64::midpoint: (a + b) / 2 without intermediate overflow.
+__device__ __forceinline__ double midpoint(double a, double b) {
+  const double lo = DBL_MIN * 2.0, hi = DBL_MAX / 2.0;
+  const double aa = fabs(a), ab = fabs(b);
+  if (aa <= hi && ab <= hi) return (a + b) / 2.0;
+  if (aa < lo) return a + b / 2.0;
+  if (ab < lo) return a / 2.0 + b;
+  return a / 2.0 + b / 2.0;
+}
+
+// f64::clamp (a NaN passes through)
+__device__ __forceinline__ double clamp_bounds(double w, double lower, double upper) {
+  return w < lower ? lower : (w > upper ? upper : w);
+}
+
+// constraints.rs:82 `child_bounds`: the children's bounds after a split on
+// a feature of direction `dir` with bounded child weights wl, wr.
+__device__ __forceinline__ void child_bounds(double lower, double upper, int dir, float wl, float wr,
+                                             double* l_lo, double* l_up, double* r_lo, double* r_up) {
+  *l_lo = *r_lo = lower;
+  *l_up = *r_up = upper;
+  if (dir == 0) return;
+  const double mid = midpoint((double)wl, (double)wr);
+  if (dir > 0) {
+    *l_up = mid;
+    *r_lo = mid;
+  } else {
+    *l_lo = mid;
+    *r_up = mid;
+  }
 }
 
 __device__ __forceinline__ double gain_given_weight(double g, double h, const DevConst& c, float w) {
@@ -939,16 +974,21 @@ __device__ __forceinline__ double gain_given_weight(double g, double h, const De
   return -(2.0 * g * (double)w + (h + c.lambda) * (double)ww + 2.0 * c.alpha * (double)fabsf(w));
 }
 
-__device__ __forceinline__ float node_gain(double g, double h, const DevConst& c) {
+__device__ __forceinline__ float node_gain(double g, double h, const DevConst& c,
+                                           float lo = -INFINITY, float up = INFINITY) {
   if (h <= 0.0) return 0.0f;
-  return __double2float_rn(gain_given_weight(g, h, c, xgb_weight(g, h, c)));
+  return __double2float_rn(gain_given_weight(g, h, c, xgb_weight(g, h, c, lo, up)));
 }
 
+// SplitScorer::loss_chg (split.rs:37): -inf for invalid children or child
+// weights against the feature's monotone direction (constraints.rs:117).
 __device__ __forceinline__ float cand_loss(double lg, double lh, double rg, double rh,
-                                           float root_gain, const DevConst& c) {
+                                           float root_gain, const DevConst& c, float lo = -INFINITY,
+                                           float up = INFINITY, int dir = 0) {
   if (!(lh > 0.0 && rh > 0.0 && lh >= c.mcw && rh >= c.mcw)) return -INFINITY;
-  const float wl = xgb_weight(lg, lh, c);
-  const float wr = xgb_weight(rg, rh, c);
+  const float wl = xgb_weight(lg, lh, c, lo, up);
+  const float wr = xgb_weight(rg, rh, c, lo, up);
+  if (dir > 0 ? !(wl <= wr) : (dir < 0 ? !(wl >= wr) : false)) return -INFINITY;
   const float gain = __fadd_rn(__double2float_rn(gain_given_weight(lg, lh, c, wl)),
                                __double2float_rn(gain_given_weight(rg, rh, c, wr)));
   return __fsub_rn(gain, root_gain);
@@ -981,7 +1021,7 @@ __global__ void __launch_bounds__(kSplitThreads)
     k_scan(DevConst c, const uint32_t* __restrict__ fo, longlong2* __restrict__ hist,
            const Front* __restrict__ front, const LevelState* __restrict__ ls,
            const Triple* __restrict__ pairs, int sib_base, const Scale* __restrict__ scale,
-           Cand* __restrict__ cand) {
+           Cand* __restrict__ cand, const int8_t* __restrict__ dirs) {
   const int f = blockIdx.x;
   const int k = blockIdx.y;
   if (k >= ls->n_front) return;
@@ -1052,7 +1092,13 @@ __global__ void __launch_bounds__(kSplitThreads)
   const bool has_missing = !c.dense && !(tot_g == fr.g && tot_h == fr.h);
 
   const double ig = scale->ig, ih = scale->ih;
-  const float root_gain = node_gain(ll2d(fr.g) * ig, ll2d(fr.h) * ih, c);
+  // the node's bounds and the feature's direction (search.rs:130-144):
+  // per (node, feature) from `dirs` (RowEngine scans), else the training
+  // run's per-feature constraints
+  const float lo = (float)fr.lower, up = (float)fr.upper;
+  const int dir = dirs ? (int)dirs[(uint64_t)k * c.n_cols + f] : (c.mono ? (int)c.mono[f] : 0);
+  const float root_gain =
+      fr.root_gain_given ? fr.root_gain : node_gain(ll2d(fr.g) * ig, ll2d(fr.h) * ih, c, lo, up);
   float best = -INFINITY;
   int best_seq = INT_MAX;
   long long blg = 0, blh = 0;
@@ -1062,7 +1108,7 @@ __global__ void __launch_bounds__(kSplitThreads)
   // t + 1), so it keeps any tie: an empty bin is never the first maximum.
   if (t < nb && (v.x != 0 || v.y != 0)) {
     const float l = cand_loss(ll2d(incl_g) * ig, ll2d(incl_h) * ih, ll2d(fr.g - incl_g) * ig,
-                              ll2d(fr.h - incl_h) * ih, root_gain, c);
+                              ll2d(fr.h - incl_h) * ih, root_gain, c, lo, up, dir);
     if (isfinite(l)) {
       best = l;
       best_seq = t;
@@ -1075,7 +1121,7 @@ __global__ void __launch_bounds__(kSplitThreads)
       const long long rg = tot_g - excl_g, rh = tot_h - excl_h;
       const long long lg2 = fr.g - rg, lh2 = fr.h - rh;
       const float lb = cand_loss(ll2d(lg2) * ig, ll2d(lh2) * ih, ll2d(rg) * ig, ll2d(rh) * ih,
-                                 root_gain, c);
+                                 root_gain, c, lo, up, dir);
       const int seq = nb + (nb - 1 - t);
       if (isfinite(lb) && cand_better(lb, seq, best, best_seq)) {
         best = lb;
@@ -1146,7 +1192,7 @@ __global__ void __launch_bounds__(kScanWarps * 32)
     k_scan_w(DevConst c, const uint32_t* __restrict__ fo, longlong2* __restrict__ hist,
              const Front* __restrict__ front, const LevelState* __restrict__ ls,
              const Triple* __restrict__ pairs, int sib_base, const Scale* __restrict__ scale,
-             Cand* __restrict__ cand) {
+             Cand* __restrict__ cand, const int8_t* __restrict__ dirs) {
   const int k = blockIdx.y;
   if (k >= ls->n_front) return;
   const int lane = threadIdx.x & 31;
@@ -1211,7 +1257,13 @@ __global__ void __launch_bounds__(kScanWarps * 32)
   eh -= lh_;
   const bool has_missing = !c.dense && !(tot_g == fr.g && tot_h == fr.h);
   const double ig = scale->ig, ih = scale->ih;
-  const float root_gain = node_gain(ll2d(fr.g) * ig, ll2d(fr.h) * ih, c);
+  // the node's bounds and the feature's direction (search.rs:130-144):
+  // per (node, feature) from `dirs` (RowEngine scans), else the training
+  // run's per-feature constraints
+  const float lo = (float)fr.lower, up = (float)fr.upper;
+  const int dir = dirs ? (int)dirs[(uint64_t)k * c.n_cols + f] : (c.mono ? (int)c.mono[f] : 0);
+  const float root_gain =
+      fr.root_gain_given ? fr.root_gain : node_gain(ll2d(fr.g) * ig, ll2d(fr.h) * ih, c, lo, up);
   float best = -INFINITY;
   int best_seq = INT_MAX;
   long long blg = 0, blh = 0;
@@ -1225,7 +1277,7 @@ __global__ void __launch_bounds__(kScanWarps * 32)
     run_h += vh[i];
     if (t < nb && (vg[i] != 0 || vh[i] != 0)) {
       const float l = cand_loss(ll2d(run_g) * ig, ll2d(run_h) * ih, ll2d(fr.g - run_g) * ig,
-                                ll2d(fr.h - run_h) * ih, root_gain, c);
+                                ll2d(fr.h - run_h) * ih, root_gain, c, lo, up, dir);
       if (isfinite(l) && cand_better(l, t, best, best_seq)) {
         best = l;
         best_seq = t;
@@ -1238,7 +1290,7 @@ __global__ void __launch_bounds__(kScanWarps * 32)
         const long long rg = tot_g - excl_g, rh = tot_h - excl_h;
         const long long lg2 = fr.g - rg, lh2 = fr.h - rh;
         const float lb = cand_loss(ll2d(lg2) * ig, ll2d(lh2) * ih, ll2d(rg) * ig, ll2d(rh) * ih,
-                                   root_gain, c);
+                                   root_gain, c, lo, up, dir);
         const int seq = nb + (nb - 1 - t);
         if (isfinite(lb) && cand_better(lb, seq, best, best_seq)) {
           best = lb;
@@ -1395,8 +1447,12 @@ __global__ void __launch_bounds__(kApplyThreads)
       nd.split_bin = best.bin;
       nd.split_gain = best.loss;
       tree[fr.node] = nd;
-      tree[left_id] = make_leaf(xgb_weight(dlg, dlh, c), (float)dlh);
-      tree[left_id + 1] = make_leaf(xgb_weight(drg, drh, c), (float)drh);
+      // the children's bounded weights (RegTree::expand), and their
+      // monotone bounds from them (hist/mod.rs:648)
+      const float wl = xgb_weight(dlg, dlh, c, (float)fr.lower, (float)fr.upper);
+      const float wr = xgb_weight(drg, drh, c, (float)fr.lower, (float)fr.upper);
+      tree[left_id] = make_leaf(wl, (float)dlh);
+      tree[left_id + 1] = make_leaf(wr, (float)drh);
       const bool terminal = c.max_depth > 0 && depth + 1 >= c.max_depth;
       int lslot = -1, rslot = -1;
       if (!terminal) {
@@ -1414,6 +1470,8 @@ __global__ void __launch_bounds__(kApplyThreads)
       r.slot = rslot;
       r.g = rg;
       r.h = rh;
+      child_bounds(fr.lower, fr.upper, c.mono ? (int)c.mono[best_f] : 0, wl, wr, &l.lower, &l.upper,
+                   &r.lower, &r.upper);
       next[2 * pos] = l;
       next[2 * pos + 1] = r;
       d.feature = best_f;
@@ -1430,8 +1488,10 @@ __global__ void __launch_bounds__(kApplyThreads)
       wtree[fr.node] = wn;
       n_items_k = (int)((fr.len + kTile - 1) / kTile);
     } else {
-      // finalize_leaf_values (shared.rs:174) then scale_leaves(eta).
-      const float w = __double2float_rn(calc_weight(ll2d(fr.g) * ig, ll2d(fr.h) * ih, c));
+      // finalize_leaf_values (shared.rs:174; calc_weight_bounded,
+      // constraints.rs:70) then scale_leaves(eta).
+      const float w = __double2float_rn(
+          clamp_bounds(calc_weight(ll2d(fr.g) * ig, ll2d(fr.h) * ih, c), fr.lower, fr.upper));
       const float v = __fmul_rn(w, c.eta);
       tree[fr.node].leaf_value = v;
       d.leaf_value = v;
@@ -1519,7 +1579,8 @@ __device__ LgNode lg_pop(LgNode* heap, int& n) {
 // finalize_leaf_values (shared.rs:174) then scale_leaves(eta), as k_apply
 __device__ void lg_leaf(const LgNode& e, const DevConst& c, double ig, double ih,
                         hb_tree_node* tree, WNode* wtree) {
-  const float w = __double2float_rn(calc_weight(ll2d(e.g) * ig, ll2d(e.h) * ih, c));
+  const float w =
+      __double2float_rn(clamp_bounds(calc_weight(ll2d(e.g) * ig, ll2d(e.h) * ih, c), e.lower, e.upper));
   const float v = __fmul_rn(w, c.eta);
   tree[e.nid].leaf_value = v;
   WNode wn;
@@ -1614,6 +1675,8 @@ __global__ void __launch_bounds__(kLgThreads)
       x.len = fr.len;
       x.g = fr.g;
       x.h = fr.h;
+      x.lower = fr.lower;
+      x.upper = fr.upper;
       if (bf >= 0) {
         const Cand cd = cand[(uint64_t)warp * c.n_cols + bf];
         x.loss = cd.loss;
@@ -1696,8 +1759,10 @@ __device__ void lg_step_serial(const DevConst& c, const uint32_t* __restrict__ f
     nd.split_bin = e.bin;
     nd.split_gain = e.loss;
     tree[e.nid] = nd;
-    tree[left_id] = make_leaf(xgb_weight(dlg, dlh, c), (float)dlh);
-    tree[left_id + 1] = make_leaf(xgb_weight(drg, drh, c), (float)drh);
+    const float wl = xgb_weight(dlg, dlh, c, (float)e.lower, (float)e.upper);
+    const float wr = xgb_weight(drg, drh, c, (float)e.lower, (float)e.upper);
+    tree[left_id] = make_leaf(wl, (float)dlh);
+    tree[left_id + 1] = make_leaf(wr, (float)drh);
     ndepth[left_id] = ndepth[left_id + 1] = e.depth + 1;
     const uint32_t fs = fo[e.feature];
     const uint32_t limit = e.bin < 0 ? 0u : (uint32_t)(e.bin + 1) - fs;
@@ -1714,6 +1779,8 @@ __device__ void lg_step_serial(const DevConst& c, const uint32_t* __restrict__ f
     f0.len = e.len;
     f0.g = e.g;
     f0.h = e.h;
+    f0.lower = e.lower;
+    f0.upper = e.upper;
     front[0] = f0;
     Decision d{};
     d.split = 1;
@@ -1735,6 +1802,8 @@ __device__ void lg_step_serial(const DevConst& c, const uint32_t* __restrict__ f
     r.slot = left_id + 1;
     r.g = rg_q;
     r.h = rh_q;
+    child_bounds(e.lower, e.upper, c.mono ? (int)c.mono[e.feature] : 0, wl, wr, &l.lower, &l.upper,
+                 &r.lower, &r.upper);
     next[0] = l;
     next[1] = r;
     LevelState lv{};
@@ -2272,21 +2341,21 @@ void launch_subtract(const Triple* pairs, const LevelState* ls, int max_pairs, u
 
 void launch_scan(const DevConst& c, const uint32_t* fo, longlong2* hist, const Front* front,
                  const LevelState* ls, const Triple* pairs, int sib_base, const Scale* scale,
-                 int max_front, Cand* cand, cudaStream_t s) {
+                 int max_front, Cand* cand, cudaStream_t s, const int8_t* dirs) {
   if (max_front < 1 || c.n_cols == 0) return;
   // features of <= 128 bins: a warp per (node, feature); wider: a CTA
   if (c.max_bins <= 128 && !c.scan_cta) {
     dim3 grid((c.n_cols + kScanWarps - 1) / kScanWarps, max_front);
     if (c.max_bins <= 32)
-      k_scan_w<1><<<grid, kScanWarps * 32, 0, s>>>(c, fo, hist, front, ls, pairs, sib_base, scale, cand);
+      k_scan_w<1><<<grid, kScanWarps * 32, 0, s>>>(c, fo, hist, front, ls, pairs, sib_base, scale, cand, dirs);
     else if (c.max_bins <= 64)
-      k_scan_w<2><<<grid, kScanWarps * 32, 0, s>>>(c, fo, hist, front, ls, pairs, sib_base, scale, cand);
+      k_scan_w<2><<<grid, kScanWarps * 32, 0, s>>>(c, fo, hist, front, ls, pairs, sib_base, scale, cand, dirs);
     else
-      k_scan_w<4><<<grid, kScanWarps * 32, 0, s>>>(c, fo, hist, front, ls, pairs, sib_base, scale, cand);
+      k_scan_w<4><<<grid, kScanWarps * 32, 0, s>>>(c, fo, hist, front, ls, pairs, sib_base, scale, cand, dirs);
     return;
   }
   dim3 grid(c.n_cols, max_front);
-  k_scan<<<grid, kSplitThreads, 0, s>>>(c, fo, hist, front, ls, pairs, sib_base, scale, cand);
+  k_scan<<<grid, kSplitThreads, 0, s>>>(c, fo, hist, front, ls, pairs, sib_base, scale, cand, dirs);
 }
 
 void launch_apply(const DevConst& c, const uint32_t* fo, const float* cuts, const Cand* cand,

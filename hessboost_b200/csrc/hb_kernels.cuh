@@ -56,10 +56,12 @@ int hist_grid(int n_sm);
 void launch_subtract(const Triple* pairs, const LevelState* ls, int max_pairs, uint32_t total_bins,
                      longlong2* hist, cudaStream_t s);
 // Split scan of every frontier node; a node whose slot is >= sib_base (with
-// `pairs`) first gets its sibling histogram parent - built.
+// `pairs`) first gets its sibling histogram parent - built. `dirs`
+// ([max_front][n_cols] monotone directions) overrides the run's per-feature
+// constraints (c.mono) when set.
 void launch_scan(const DevConst& c, const uint32_t* fo, longlong2* hist, const Front* front,
                  const LevelState* ls, const Triple* pairs, int sib_base, const Scale* scale,
-                 int max_front, Cand* cand, cudaStream_t s);
+                 int max_front, Cand* cand, cudaStream_t s, const int8_t* dirs = nullptr);
 void launch_apply(const DevConst& c, const uint32_t* fo, const float* cuts, const Cand* cand,
                   const Front* front, Front* next, Decision* dec, PItem* items, LevelState* ls,
                   LevelState* ls_next, hb_tree_node* tree, WNode* wtree, const Scale* scale,

@@ -102,12 +102,15 @@ typedef struct hb_reg_params {
   double min_child_weight;
 } hb_reg_params;
 
-/* ScanRequest (src/tree/hist/mod.rs:303) for numeric features without
- * monotone constraints: `features` lists the features to scan. */
+/* ScanRequest (src/tree/hist/mod.rs:303): the node's histogram slot, its
+ * statistics, root_gain and monotone bounds as the scorer uses them (f32),
+ * and the features to scan, `features[i]` with monotone direction
+ * `directions[i]` (+1, -1, 0; NULL: all 0), merged in that order. */
 typedef struct hb_scan_request {
   uint32_t slot;
   uint32_t n_features;
   const uint32_t* features;
+  const int8_t* directions;
   hb_grad_stats total;
   float root_gain;
   float lower;
@@ -194,6 +197,11 @@ typedef struct hb_train_params {
   float scale_pos_weight;
   float base_score;         /* NaN: estimate from the labels */
   int32_t num_class;        /* HB_LOSS_SOFTMAX: classes (3, or 5..64); else 0 or 1 */
+  /* monotone_constraints (src/config/params.rs, Monotone): one direction
+   * per feature, +1 increasing, -1 decreasing, 0 none; features past
+   * n_monotone are unconstrained. NULL / 0: none. */
+  int32_t n_monotone;
+  const int8_t* monotone;
 } hb_train_params;
 
 /* ---- engine (CudaHistBackend::new + upload) ------------------------- */

@@ -27,9 +27,10 @@ pub struct hb_partitioned { pub left: hb_segment, pub right: hb_segment }
 #[repr(C)] pub struct hb_reg_params { pub lambda: f64, pub alpha: f64,
                                       pub max_delta_step: f64, pub min_child_weight: f64 }
 #[repr(C)] pub struct hb_scan_request { pub slot: u32, pub n_features: u32,
-                                        pub features: *const u32, pub total: hb_grad_stats,
+                                        pub features: *const u32, pub directions: *const i8,
+                                        pub total: hb_grad_stats,
                                         pub root_gain: f32, pub lower: f32, pub upper: f32,
-                                        pub reserved: u32 }
+                                        pub reserved: u32 }   // ScanRequest: features[i], directions[i]
 #[repr(C)] #[derive(Default)]
 pub struct hb_node_scan { pub kind: u32, pub feature: u32, pub loss_chg: f32, pub backward: u32,
                           pub offset: u32, pub reserved: u32, pub acc: hb_grad_stats }
@@ -50,7 +51,8 @@ pub struct hb_tree_node { pub left: i32, pub right: i32, pub split_feature: u32,
                                         pub lambda: f32, pub alpha: f32, pub gamma: f32,
                                         pub min_child_weight: f32, pub max_delta_step: f32,
                                         pub scale_pos_weight: f32, pub base_score: f32,
-                                        pub num_class: i32 }     // TrainingParams (hist fields)
+                                        pub num_class: i32, pub n_monotone: i32,
+                                        pub monotone: *const i8 }  // TrainingParams (hist fields)
 pub const HB_TIMERS: usize = 8;
 #[repr(C)] #[derive(Default)]
 pub struct hb_engine_stats { pub ms: [f64; HB_TIMERS], pub timed_launches: [u64; HB_TIMERS],

@@ -147,7 +147,40 @@ struct Params {
   double lambda, alpha, gamma, mcw, mds;  // RegParams: every value rounded to f32 (gain.rs:83)
   float spw;
   bool fixed;
+  std::vector<int8_t> mono;  // constraints.rs:12 `MonotoneConstraints` (+1, -1, 0)
+  int8_t dir(size_t f) const { return f < mono.size() ? mono[f] : 0; }  // constraints.rs:37
 };
+
+// constraints.rs:44 `Bounds`: a node's leaf-weight interval.
+struct Bounds {
+  double lower = -INFINITY, upper = INFINITY;
+  double clamp(double w) const { return std::min(std::max(w, lower), upper); }  // f64::clamp
+};
+
+// f64::midpoint (Rust core): (a + b) / 2 without intermediate overflow.
+inline double midpoint(double a, double b) {
+  const double lo = DBL_MIN * 2.0, hi = DBL_MAX / 2.0;
+  const double aa = std::fabs(a), ab = std::fabs(b);
+  if (aa <= hi && ab <= hi) return (a + b) / 2.0;
+  if (aa < lo) return a + b / 2.0;
+  if (ab < lo) return a / 2.0 + b;
+  return a / 2.0 + b / 2.0;
+}
+
+// constraints.rs:82 `child_bounds`
+inline std::pair<Bounds, Bounds> child_bounds(Bounds parent, int dir, double wl, double wr) {
+  if (dir == 0) return {parent, parent};
+  const double mid = midpoint(wl, wr);
+  if (dir > 0) return {Bounds{parent.lower, mid}, Bounds{mid, parent.upper}};
+  return {Bounds{mid, parent.upper}, Bounds{parent.lower, mid}};
+}
+
+// constraints.rs:117 `satisfies`
+inline bool satisfies(int dir, double wl, double wr) {
+  if (dir > 0) return wl <= wr;
+  if (dir < 0) return wl >= wr;
+  return true;
+}
 
 // ---------------------------------------------------------------------------
 // Split scoring (src/tree/builder/shared.rs:82-141, split.rs:37-58).
@@ -164,9 +197,11 @@ inline double xgb_calc_weight(double g, double h, const Params& p) {  // shared.
   return w;
 }
 
-inline float xgb_weight(double g, double h, const Params& p) {  // shared.rs:113 (no bounds)
+// shared.rs:113 `xgb_weight`: rounded to f32, then clamped to the node's
+// bounds (shared.rs:100 `apply_bounds`, the bounds rounded to f32).
+inline float xgb_weight(double g, double h, const Params& p, Bounds b = Bounds{}) {
   float w = (float)xgb_calc_weight(g, h, p);
-  const float lower = -INFINITY, upper = INFINITY;
+  const float lower = (float)b.lower, upper = (float)b.upper;
   if (w < lower) return lower;
   if (w > upper) return upper;
   return w;
@@ -177,9 +212,9 @@ inline double gain_given_weight(double g, double h, const Params& p, float w) { 
   return -(2.0 * g * (double)w + (h + p.lambda) * (double)ww + 2.0 * p.alpha * (double)std::fabs(w));
 }
 
-inline float xgb_node_gain(double g, double h, const Params& p) {  // shared.rs:136
+inline float xgb_node_gain(double g, double h, const Params& p, Bounds b = Bounds{}) {  // shared.rs:136
   if (h <= 0.0) return 0.0f;
-  return (float)gain_given_weight(g, h, p, xgb_weight(g, h, p));
+  return (float)gain_given_weight(g, h, p, xgb_weight(g, h, p, b));
 }
 
 inline bool children_valid(double lh, double rh, double mcw) {  // builder/mod.rs:182
@@ -413,6 +448,57 @@ struct Tree {
   }
 };
 
+// One feature's candidates in for_each_numeric_split order (split.rs:391),
+// offered to `best` with need_replace: the forward pass over the bins
+// (missing right), then, when the node has missing values of the feature,
+// the backward pass (missing left). A candidate is scored by
+// SplitScorer::loss_chg (split.rs:37): both children valid, the bounded
+// child weights in the feature's monotone direction, the two f32 child
+// gains added in f32 minus the node's root gain. True when a candidate
+// replaced `best`.
+template <class Mode>
+bool scan_feature(const Mode& mode, const Params& p, const typename Mode::Stat* hist,
+                  typename Mode::Stat total, float root_gain, Bounds bounds, int dir, uint32_t f,
+                  uint32_t fs, uint32_t fe, bool dense, Best<typename Mode::Stat>& best) {
+  using S = typename Mode::Stat;
+  bool found = false;
+  auto offer = [&](int32_t bin, bool default_left, S left, S right) {
+    double lg = mode.g(left), lh = mode.h(left), rg = mode.g(right), rh = mode.h(right);
+    if (!children_valid(lh, rh, p.mcw)) return;
+    float wl = xgb_weight(lg, lh, p, bounds);
+    float wr = xgb_weight(rg, rh, p, bounds);
+    if (!satisfies(dir, (double)wl, (double)wr)) return;
+    float gain = (float)gain_given_weight(lg, lh, p, wl) + (float)gain_given_weight(rg, rh, p, wr);
+    float loss = gain - root_gain;
+    if (need_replace((float)best.loss_chg, best.feature, loss, f)) {
+      found = true;
+      best.loss_chg = (double)loss;
+      best.feature = f;
+      best.bin = bin;
+      best.default_left = default_left;
+      best.left = left;
+      best.right = right;
+      best.w_left = (double)wl;
+      best.w_right = (double)wr;
+    }
+  };
+  if (fe <= fs + 1) return false;  // search.rs:214 degenerate feature
+  S acc{};
+  for (uint32_t b = fs; b < fe; ++b) {
+    acc = Mode::add(acc, hist[b]);
+    offer((int32_t)b, false, acc, Mode::sub(total, acc));
+  }
+  if (dense || Mode::eq(acc, total)) return found;
+  S suffix{};
+  for (uint32_t off = fe - fs; off-- > 0;) {
+    suffix = Mode::add(suffix, hist[fs + off]);
+    // SplitPos::backward (builder/mod.rs:263)
+    int32_t bin = off == 0 ? -1 : (int32_t)(fs + off - 1);
+    offer(bin, true, Mode::sub(total, suffix), suffix);
+  }
+  return found;
+}
+
 // ---------------------------------------------------------------------------
 // HistTreeBuilder (src/tree/builder/hist/mod.rs) for one tree, parameterised
 // by the summation mode.
@@ -439,18 +525,20 @@ class Builder {
     S root_stats = root_sum(all);
     Tree tree((float)mode_.h(root_stats));
     stats_.assign(1, root_stats);
+    bounds_.assign(1, Bounds{});
     Entry root{0, 0, std::move(all), {}, {}};
     root.hist = build_hist(ix_, root.rows, values_, mode_);
-    root.best = evaluate(root.hist, root_stats);
+    root.best = evaluate(root.hist, root_stats, bounds_[0]);
     if (p_.grow_policy == 0) {
       grow_depthwise(tree, std::move(root), leaf_rows);
     } else {
       grow_lossguide(tree, std::move(root), leaf_rows);
     }
-    // finalize_leaf_values (shared.rs:174)
+    // finalize_leaf_values (shared.rs:174): calc_weight_bounded
+    // (constraints.rs:70), the weight clamped to the leaf's bounds in f64
     for (size_t id = 0; id < tree.nodes.size(); ++id) {
       if (tree.nodes[id].left == -1) {
-        double w = calc_weight(mode_.g(stats_[id]), mode_.h(stats_[id]), p_);
+        double w = bounds_[id].clamp(calc_weight(mode_.g(stats_[id]), mode_.h(stats_[id]), p_));
         tree.nodes[id].leaf_value = (float)w;
       }
     }
@@ -467,66 +555,29 @@ class Builder {
 
   // HistTreeBuilder::evaluate (search.rs:37) over every feature, with the
   // sequential candidate order of for_each_numeric_split (split.rs:391)
-  // and xgb_update's tie rule (builder/mod.rs:334).
+  // and xgb_update's tie rule (builder/mod.rs:334). The node's root gain
+  // and child weights use its monotone bounds (search.rs:130 `node_scorer`),
+  // each feature its direction (`scorer`).
   //
   // The features are scored in parallel, each from the empty split, and
   // their winners merged in feature order: the incumbent's feature never
   // exceeds the candidate's, so need_replace is a strict `>` throughout,
   // and the merge keeps the first maximum of the sequential scan.
-  Best<S> evaluate(const std::vector<S>& hist, S total) const {
-    const float root_gain = xgb_node_gain(mode_.g(total), mode_.h(total), p_);
+  Best<S> evaluate(const std::vector<S>& hist, S total, Bounds bounds) const {
+    const float root_gain = xgb_node_gain(mode_.g(total), mode_.h(total), p_, bounds);
     const long long nc = (long long)ix_.n_cols;
     std::vector<Best<S>> per(nc);
     std::vector<uint8_t> found(nc, 0);
 #pragma omp parallel for schedule(dynamic, 4) if (nc >= 16)
-    for (long long f = 0; f < nc; ++f) found[f] = evaluate_feature(hist, total, root_gain, (uint32_t)f, per[f]);
+    for (long long f = 0; f < nc; ++f)
+      found[f] = scan_feature(mode_, p_, hist.data(), total, root_gain, bounds, p_.dir((size_t)f),
+                              (uint32_t)f, ix_.cuts.feature_offset[f], ix_.cuts.feature_offset[f + 1],
+                              ix_.dense, per[f]);
     Best<S> best;
     for (long long f = 0; f < nc; ++f)
       if (found[f] && need_replace((float)best.loss_chg, best.feature, (float)per[f].loss_chg, (uint32_t)f))
         best = per[f];
     return best;
-  }
-
-  // One feature's candidates in scan order, from the empty split; true when
-  // one of them replaced it.
-  bool evaluate_feature(const std::vector<S>& hist, S total, float root_gain, uint32_t f,
-                        Best<S>& best) const {
-    bool found = false;
-    auto offer = [&](uint32_t f, int32_t bin, bool default_left, S left, S right) {
-      double lg = mode_.g(left), lh = mode_.h(left), rg = mode_.g(right), rh = mode_.h(right);
-      if (!children_valid(lh, rh, p_.mcw)) return;  // split.rs:37 `loss_chg`
-      float wl = xgb_weight(lg, lh, p_);
-      float wr = xgb_weight(rg, rh, p_);
-      float gain = (float)gain_given_weight(lg, lh, p_, wl) + (float)gain_given_weight(rg, rh, p_, wr);
-      float loss = gain - root_gain;
-      if (need_replace((float)best.loss_chg, best.feature, loss, f)) {
-        found = true;
-        best.loss_chg = (double)loss;
-        best.feature = f;
-        best.bin = bin;
-        best.default_left = default_left;
-        best.left = left;
-        best.right = right;
-        best.w_left = (double)wl;
-        best.w_right = (double)wr;
-      }
-    };
-    uint32_t fs = ix_.cuts.feature_offset[f], fe = ix_.cuts.feature_offset[f + 1];
-    if (fe <= fs + 1) return false;  // search.rs:214 degenerate feature
-    S acc{};
-    for (uint32_t b = fs; b < fe; ++b) {
-      acc = Mode::add(acc, hist[b]);
-      offer(f, (int32_t)b, false, acc, Mode::sub(total, acc));
-    }
-    if (ix_.dense || Mode::eq(acc, total)) return found;
-    S suffix{};
-    for (uint32_t off = fe - fs; off-- > 0;) {
-      suffix = Mode::add(suffix, hist[fs + off]);
-      // SplitPos::backward (builder/mod.rs:263)
-      int32_t bin = off == 0 ? -1 : (int32_t)(fs + off - 1);
-      offer(f, bin, true, Mode::sub(total, suffix), suffix);
-    }
-    return found;
   }
 
   // prepare_split (hist/mod.rs:639): expand the node, record child stats.
@@ -538,6 +589,10 @@ class Builder {
     tree.nodes[e.nid].split_gain = (float)b.loss_chg;
     stats_.push_back(b.left);
     stats_.push_back(b.right);
+    // hist/mod.rs:648: monotone child bounds from the bounded child weights
+    auto cb = child_bounds(bounds_[e.nid], p_.dir(b.feature), b.w_left, b.w_right);
+    bounds_.push_back(cb.first);
+    bounds_.push_back(cb.second);
     return ids;
   }
 
@@ -599,8 +654,8 @@ class Builder {
       l.hist = std::move(sib);
       r.hist = std::move(small);
     }
-    l.best = evaluate(l.hist, e.best.left);
-    r.best = evaluate(r.hist, e.best.right);
+    l.best = evaluate(l.hist, e.best.left, bounds_[lid]);
+    r.best = evaluate(r.hist, e.best.right, bounds_[rid]);
   }
 
   void grow_depthwise(Tree& tree, Entry root,
@@ -716,6 +771,7 @@ class Builder {
   const typename std::conditional<std::is_same<Mode, F64Mode>::value, GradPair, IS>::type* values_ =
       nullptr;
   std::vector<S> stats_;
+  std::vector<Bounds> bounds_;  // hist/mod.rs:916 `NodeStore` bounds, by node id
 };
 
 // shared.rs:164 `sum_rows`: an f64 chain in row order.
@@ -962,6 +1018,7 @@ void orc_intercepts(int32_t objective, const float* labels, uint64_t n, int32_t 
 
 int32_t orc_fixed_scale(float max_abs, uint64_t n) { return fixed_scale(max_abs, n); }
 
+
 }  // extern "C"
 
 struct orc_trainer {
@@ -995,6 +1052,7 @@ orc::Params params_from(const orc_params* pp) {
   p.mds = (double)pp->max_delta_step;
   p.spw = pp->scale_pos_weight;
   p.fixed = pp->fixed_point != 0;
+  if (pp->monotone && pp->n_monotone > 0) p.mono.assign(pp->monotone, pp->monotone + pp->n_monotone);
   return p;
 }
 
@@ -1155,6 +1213,50 @@ uint64_t orc_trainer_margins(const orc_trainer* tr, float* out, uint64_t cap) {
 int32_t orc_trainer_set_margins(orc_trainer* tr, const float* m, uint64_t n) {
   if (!tr || !m || n != tr->margins.size()) return -2;
   std::copy(m, m + n, tr->margins.begin());
+  return 0;
+}
+
+int32_t orc_scan_node(const orc_params* pp, const uint32_t* feature_offset, uint32_t n_cols, int32_t dense,
+                      const int64_t* hist, int64_t total_g, int64_t total_h, int32_t sg, int32_t sh,
+                      float lower, float upper, const uint32_t* features, const int8_t* directions,
+                      uint32_t n_features, orc_scan* out) {
+  if (!pp || !feature_offset || !hist || !out || (n_features && !features)) return -2;
+  using namespace orc;
+  Params p = params_from(pp);
+  FixMode mode;
+  mode.sg = sg;
+  mode.sh = sh;
+  const IS* h = reinterpret_cast<const IS*>(hist);
+  const IS total{total_g, total_h};
+  Bounds b{(double)lower, (double)upper};
+  const float root_gain = xgb_node_gain(mode.g(total), mode.h(total), p, b);
+  // features in the request's order, each scanned from the empty split,
+  // merged with need_replace (search.rs:164 `merge`)
+  Best<IS> best;
+  bool any = false;
+  for (uint32_t j = 0; j < n_features; ++j) {
+    const uint32_t f = features[j];
+    if (f >= n_cols) return -2;
+    Best<IS> one;
+    const int dir = directions ? directions[j] : 0;
+    if (scan_feature(mode, p, h, total, root_gain, b, dir, f, feature_offset[f], feature_offset[f + 1],
+                     dense != 0, one) &&
+        need_replace((float)best.loss_chg, best.feature, (float)one.loss_chg, f)) {
+      best = one;
+      any = true;
+    }
+  }
+  std::memset(out, 0, sizeof(*out));
+  out->found = any ? 1 : 0;
+  out->feature = best.feature;
+  out->bin = best.bin;
+  out->default_left = best.default_left ? 1 : 0;
+  out->loss_chg = (float)best.loss_chg;
+  out->root_gain = root_gain;
+  out->left_g = best.left.grad;
+  out->left_h = best.left.hess;
+  out->w_left = (float)best.w_left;
+  out->w_right = (float)best.w_right;
   return 0;
 }
 

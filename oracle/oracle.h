@@ -42,6 +42,9 @@ typedef struct orc_params {
   float base_score;        /* NaN: estimate from the labels */
   int32_t fixed_point;     /* 0: the reference's f64 sums; 1: int64 fixed-point sums */
   int32_t n_threads;       /* 0: all */
+  const int8_t* monotone;  /* per feature +1 / -1 / 0 (monotone_constraints); NULL: none */
+  int32_t n_monotone;
+  int32_t reserved;
 } orc_params;
 
 /* HistCuts::from_dmatrix of a dense row-major matrix (NaN = missing).
@@ -122,6 +125,25 @@ void orc_hist(const float* x, uint64_t n_rows, uint64_t n_cols, const uint32_t* 
               const float* cut_values, const uint32_t* rows, uint64_t n_node_rows,
               const float* gpair, int32_t fixed_point, int32_t sg, int32_t sh, double* out_f64,
               int64_t* out_i64);
+
+/* One node's split search in fixed point (the RowEngine scan seam): the
+ * node's int64 histogram (2 per bin) and totals with scales 2^sg, 2^sh, its
+ * monotone bounds, and the features to scan in order with their directions
+ * (NULL: none); the winner of HistTreeBuilder::evaluate over them. */
+typedef struct orc_scan {
+  int32_t found;          /* 0: no candidate beats the empty split */
+  uint32_t feature;
+  int32_t bin;            /* last global bin going left, -1 = below every bin */
+  uint32_t default_left;
+  float loss_chg;
+  float root_gain;
+  int64_t left_g, left_h; /* left child statistics (fixed point) */
+  float w_left, w_right;  /* bounded child weights */
+} orc_scan;
+int32_t orc_scan_node(const orc_params* p, const uint32_t* feature_offset, uint32_t n_cols, int32_t dense,
+                      const int64_t* hist, int64_t total_g, int64_t total_h, int32_t sg, int32_t sh,
+                      float lower, float upper, const uint32_t* features, const int8_t* directions,
+                      uint32_t n_features, orc_scan* out);
 
 /* The fixed-point scale exponent for values of largest magnitude `max_abs`
  * summed over `n` rows: every |rint(v * 2^s)| * n stays within 2^62. */

@@ -69,6 +69,24 @@ class OrcParams(ctypes.Structure):
         ("base_score", ctypes.c_float),
         ("fixed_point", ctypes.c_int32),
         ("n_threads", ctypes.c_int32),
+        ("monotone", ctypes.POINTER(ctypes.c_int8)),
+        ("n_monotone", ctypes.c_int32),
+        ("reserved", ctypes.c_int32),
+    ]
+
+
+class OrcScan(ctypes.Structure):
+    _fields_ = [
+        ("found", ctypes.c_int32),
+        ("feature", ctypes.c_uint32),
+        ("bin", ctypes.c_int32),
+        ("default_left", ctypes.c_uint32),
+        ("loss_chg", ctypes.c_float),
+        ("root_gain", ctypes.c_float),
+        ("left_g", ctypes.c_int64),
+        ("left_h", ctypes.c_int64),
+        ("w_left", ctypes.c_float),
+        ("w_right", ctypes.c_float),
     ]
 
 
@@ -124,6 +142,10 @@ def lib():
         L.orc_trainer_margins.argtypes = [ctypes.c_void_p, f32p, ctypes.c_uint64]
         L.orc_trainer_set_margins.restype = ctypes.c_int32
         L.orc_trainer_set_margins.argtypes = [ctypes.c_void_p, f32p, ctypes.c_uint64]
+        L.orc_scan_node.restype = ctypes.c_int32
+        L.orc_scan_node.argtypes = [P(OrcParams), u32p, ctypes.c_uint32, ctypes.c_int32, P(ctypes.c_int64),
+                                    ctypes.c_int64, ctypes.c_int64, ctypes.c_int32, ctypes.c_int32, ctypes.c_float,
+                                    ctypes.c_float, u32p, P(ctypes.c_int8), ctypes.c_uint32, P(OrcScan)]
         L.orc_fixed_scale.restype = ctypes.c_int32
         L.orc_fixed_scale.argtypes = [ctypes.c_float, ctypes.c_uint64]
         _lib = L
@@ -203,6 +225,11 @@ def params(**kw):
     p.base_score = kw.get("base_score", float("nan"))
     p.fixed_point = 1 if kw.get("fixed_point", False) else 0
     p.n_threads = kw.get("n_threads", 0)
+    mono = kw.get("monotone")
+    if mono is not None:
+        p._mono = np.ascontiguousarray(mono, np.int8)  # kept alive with the struct
+        p.monotone = p._mono.ctypes.data_as(ctypes.POINTER(ctypes.c_int8))
+        p.n_monotone = p._mono.size
     return p
 
 
@@ -325,6 +352,24 @@ def hist(x, off, cuts, rows, gpair, fixed_point=False, sg=0, sh=0):
 
 
 # ---------------------------------------------------------------- golden data
+def scan_node(hist_q, feature_offset, dense, total_q, sg, sh, features, directions=None,
+              bounds=(-np.inf, np.inf), **kw):
+    """One node's fixed-point split search (orc_scan_node): `hist_q` the
+    int64 (g, h) histogram, `total_q` the node's int64 totals."""
+    p = params(**kw)
+    h = np.ascontiguousarray(hist_q, np.int64)
+    off = np.ascontiguousarray(feature_offset, np.uint32)
+    f = np.ascontiguousarray(features, np.uint32)
+    d = None if directions is None else np.ascontiguousarray(directions, np.int8)
+    out = OrcScan()
+    st = lib().orc_scan_node(ctypes.byref(p), _p(off, ctypes.c_uint32), off.size - 1, 1 if dense else 0,
+                             _p(h, ctypes.c_int64), int(total_q[0]), int(total_q[1]), sg, sh,
+                             float(bounds[0]), float(bounds[1]), _p(f, ctypes.c_uint32),
+                             None if d is None else _p(d, ctypes.c_int8), f.size, ctypes.byref(out))
+    assert st == 0, st
+    return out
+
+
 def bits_to_f32(bits):
     return np.array(bits, dtype=np.uint32).view(np.float32)
 

@@ -149,11 +149,26 @@ CASES = {
     "lossguide_large": dict(gen=lambda: synth.logistic_c2(600_003, 28, seed=19), rounds=2,
                             kw=dict(objective="binary:logistic", grow_policy="lossguide", max_depth=0,
                                     max_leaves=96, eta=0.1)),
+    # monotone constraints (constraints.rs): bounded child weights, direction
+    # checks, child bounds at the midpoint, bounded leaves; depthwise with
+    # missing values, lossguide, and the CTA scan (256 bins) and warp scan
+    # (64 bins)
+    "monotone_depthwise": dict(gen=lambda: synth.logistic_c2(40_009, 8, seed=24), rounds=4,
+                               kw=dict(objective="binary:logistic", max_depth=6, eta=0.3,
+                                       monotone_constraints=(1, -1, 0, 1, 0, 0, -1, 0))),
+    "monotone_bins64": dict(gen=lambda: synth.regression_c1(30_011, 6, seed=25), rounds=4,
+                            kw=dict(max_depth=5, max_bin=64, min_child_weight=0.0, reg_lambda=0.5,
+                                    monotone_constraints=(-1, 1, 1, 0, 0, 1))),
+    "monotone_lossguide": dict(gen=lambda: synth.logistic_c2(20_011, 8, seed=26), rounds=3,
+                               kw=dict(objective="binary:logistic", grow_policy="lossguide", max_depth=0,
+                                       max_leaves=24, eta=0.3, monotone_constraints=(1, 1, -1, 0, 0, 0, 0, -1))),
 }
 
 
 def _orc_kw(kw):
     m = dict(kw)
+    if "monotone_constraints" in m:
+        m["monotone"] = list(m.pop("monotone_constraints"))
     if "objective" in m:
         m["objective"] = 1 if m["objective"] == "binary:logistic" else 0
     if "grow_policy" in m:
@@ -175,7 +190,8 @@ def test_training_matches_oracle_fixed_point(case):
     np.testing.assert_array_equal(_bits(pred), _bits(omarg[:, 0]))
 
 
-@pytest.mark.parametrize("case", ["c1_regression", "c2_logistic", "c2_large", "regularised", "few_bins"])
+@pytest.mark.parametrize("case", ["c1_regression", "c2_logistic", "c2_large", "regularised", "few_bins",
+                                  "monotone_depthwise"])
 def test_training_against_reference_f64_mode(case):
     """North-star criteria against the reference's own summation (the
     oracle's f64 mode), round by round: each round both start from the
@@ -459,6 +475,81 @@ def test_backend_build_features_and_prepare_match_oracle():
         got2 = e.build(rows)
         np.testing.assert_array_equal(got2[:, 0], og2)
         np.testing.assert_array_equal(got2[:, 1], oh2)
+    finally:
+        e.close()
+
+
+def test_monotone_training_is_monotone():
+    """A constrained feature moves the prediction one way only: rows that
+    differ only in feature 0 (increasing) or feature 1 (decreasing) predict
+    in that order."""
+    x, y = synth.logistic_c2(30_011, 6, seed=27)
+    m = gpu_train(x, y, 6, objective="binary:logistic", max_depth=6, eta=0.3,
+                  monotone_constraints=(1, -1, 0, 0, 0, 0))
+    rng = np.random.default_rng(3)
+    base = rng.standard_normal((64, 6)).astype(np.float32)
+    grid = np.linspace(-3, 3, 41, dtype=np.float32)
+    for f, sign in ((0, 1.0), (1, -1.0)):
+        rows = np.repeat(base, grid.size, axis=0)
+        rows[:, f] = np.tile(grid, base.shape[0])
+        p = m.predict_margin(rows).reshape(base.shape[0], grid.size)
+        assert np.all(sign * np.diff(p, axis=1) >= 0.0), f
+
+
+def test_scan_resident_matches_oracle_scan():
+    """RowEngine::scan_resident against the oracle's fixed-point search of
+    the same histograms: the winning feature, loss change (bits), direction,
+    offset and accumulated statistics, for requests in feature order, in a
+    shuffled order (the merge keeps need_replace's lower-feature rule), with
+    monotone directions and with finite bounds; a node with missing values
+    (the backward pass scored) and one without."""
+    e, x, mtx, gp, sg, sh = _setup_engine(n=20_011, f=7, seed=41, missing=0.15)
+    n = x.shape[0]
+    fo = mtx.feature_offset
+    try:
+        root = e.begin_tree(np.arange(n))
+        (left, right), = e.partition([(root, 2, 90, False)])
+        lrows, rrows = e.rows([left, right])
+        assert e.reserve_hists(3)
+        e.build_resident([(root, 0), (left, 1), (right, 2)])
+        q = np.rint(gp.astype(np.float64) * [2.0 ** sg, 2.0 ** sh]).astype(np.int64)
+        for params in (H.TrainingParams(), H.TrainingParams(reg_lambda=2.5, alpha=0.3, min_child_weight=5.0,
+                                                            max_delta_step=0.4)):
+            reg = params.reg()
+            okw = dict(reg_lambda=params.reg_lambda, alpha=params.alpha,
+                       min_child_weight=params.min_child_weight, max_delta_step=params.max_delta_step)
+            cases = [
+                (np.arange(7), None, (-np.inf, np.inf)),
+                (np.array([5, 2, 6, 0, 3, 1, 4]), None, (-np.inf, np.inf)),
+                (np.array([3, 1, 0, 6]), np.array([1, -1, 1, 0]), (-np.inf, np.inf)),
+                (np.arange(7), np.array([1, 1, -1, 0, 1, -1, 0]), (-0.05, 0.08)),
+                (np.array([4, 0, 2]), np.array([-1, 0, 1]), (-0.02, np.float32(0.3))),
+            ]
+            for slot, rows in ((0, np.arange(n)), (1, lrows), (2, rrows)):
+                hq = O.hist(x, fo, mtx.cut_values, rows, gp, fixed_point=True, sg=sg, sh=sh)
+                tq = q[rows].sum(axis=0)
+                total = (tq[0] * 2.0 ** -sg, tq[1] * 2.0 ** -sh)
+                reqs = [(slot, total, f, d, b) for f, d, b in cases]
+                got = e.scan_resident(reg, reqs)
+                for (f, d, b), r in zip(cases, got):
+                    want = O.scan_node(hq, fo, mtx.dense, tq, sg, sh, f, d, b, **okw)
+                    lo, up = np.float32(b[0]), np.float32(b[1])
+                    assert np.float32(H.node_gain(total, reg, lo, up)) == np.float32(want.root_gain)
+                    what = f"slot {slot} features {list(f)} dirs {d} bounds {b}"
+                    assert r.kind == (H.HB_SCAN_NUMERIC if want.found else H.HB_SCAN_EMPTY), what
+                    if not want.found:
+                        continue
+                    assert r.feature == want.feature, what
+                    assert np.float32(r.loss_chg).view(np.uint32) == np.float32(want.loss_chg).view(np.uint32), what
+                    assert r.backward == want.default_left, what
+                    fs = int(fo[want.feature])
+                    if want.default_left:
+                        assert r.offset == (0 if want.bin < 0 else want.bin - fs + 1), what
+                        acc = (tq[0] - want.left_g, tq[1] - want.left_h)
+                    else:
+                        assert r.offset == want.bin - fs, what
+                        acc = (want.left_g, want.left_h)
+                    assert r.acc.grad == acc[0] * 2.0 ** -sg and r.acc.hess == acc[1] * 2.0 ** -sh, what
     finally:
         e.close()
 
