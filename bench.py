@@ -539,6 +539,8 @@ def main():
     ap.add_argument("--no-parity", action="store_true",
                     help="skip the comparison of the first trees with the oracle (N=1)")
     ap.add_argument("--parity-rounds", type=int, default=3)
+    ap.add_argument("--no-row-engine", action="store_true",
+                    help="skip timing the RowEngine host loop (device_round over the trait calls)")
     ap.add_argument("--rows", type=int, default=None,
                     help="rows of the synthetic matrix (default: the workload's own, 10M for "
                          "C2 and 100M for C5; smaller values are for profiling captures)")
@@ -689,6 +691,32 @@ def main():
     breakdown = eng.stats()
     per_round = {k: v / max(breakdown["rounds"], 1) for k, v in breakdown["ms"].items()}
 
+    # ---- the reference's unchanged device round over the RowEngine calls
+    # (device_round + build_on_device: a host level loop, one C-ABI call per
+    # trait method), one GPU
+    row_engine = None
+    if world == 1 and not args.no_row_engine:
+        from hessboost_b200.device_builder import RowEngineTrainer
+
+        eng.load_margins(np.full(end - begin, base, np.float32))
+        rt = RowEngineTrainer(eng, params, y_shard)
+        rt.round()  # warm-up: slot reservation, first allocations
+        k_re = max(1, min(args.steps, 10))
+        c0 = rt.calls
+        t0 = time.perf_counter()
+        for _ in range(k_re):
+            rt.round()
+        torch.cuda.synchronize()
+        dt = time.perf_counter() - t0
+        row_engine = {"value": k_re / dt, "unit": UNIT, "rounds": k_re,
+                      "ms_per_round": 1000.0 * dt / k_re,
+                      "calls_per_round": (rt.calls - c0) / k_re,
+                      "whole_round_ms_per_round": ms / args.steps,
+                      "scope": "hessboost_b200.device_builder.RowEngineTrainer: gradients, begin_tree, "
+                               "root_total, reserve_hists, build_resident, scan_resident per level, "
+                               "partition, add_leaf_values through the C ABI, host wall clock"}
+        log(f"row engine: {1000.0 * dt / k_re:.2f} ms/round ({row_engine['calls_per_round']:.0f} calls)")
+
     # ---- end to end through the C ABI from pinned host buffers
     barrier()
     pin = lambda a: torch.from_numpy(np.ascontiguousarray(a)).pin_memory().numpy()  # noqa: E731
@@ -761,6 +789,7 @@ def main():
             "cpu_baseline": cpu,
             "parity": parity,
             "forest": forest,
+            "row_engine": row_engine,
             "e2e": e2e,
             "gpu_launches": launches,
             "clocks": clocks,

@@ -37,6 +37,7 @@ __all__ = [
 HB_OK, HB_REFUSED, HB_DEVICE_FAILED, HB_INVALID_ARGUMENT = 0, 1, 2, 3
 HB_LOSS_SQUARED_ERROR, HB_LOSS_LOGISTIC, HB_LOSS_SOFTMAX = 0, 1, 2
 HB_GROW_DEPTHWISE, HB_GROW_LOSSGUIDE = 0, 1
+HB_SCAN_EMPTY, HB_SCAN_REPLAY, HB_SCAN_NUMERIC = 0, 1, 2  # NodeScan kinds
 
 
 class HbError(RuntimeError):

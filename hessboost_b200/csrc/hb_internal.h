@@ -31,6 +31,10 @@ constexpr int kTileWords = kTile / 32;
 constexpr int kHistThreads = 1024;
 constexpr int kGroupFeatures = 32;       // features per histogram CTA group
 
+// Fixed-point range: every |q| * rows <= 2^kFixedTop, so each sum is an
+// integer below 2^53, exact in an f64.
+constexpr int kFixedTop = 53;
+
 // Per-tree scale of the fixed-point gradients: q = rint(v * 2^s).
 struct Scale {
   int32_t sg, sh;

@@ -342,14 +342,17 @@ __global__ void k_pair_maxima(const float2* __restrict__ gpair, uint64_t n, Scal
   reduce_scale(mg, mh, nonfinite, scale);
 }
 
-// The exponent s with |rint(v * 2^s)| * n <= 2^62 for every |v| <= max.
+// The exponent s with |rint(v * 2^s)| * n <= 2^53 for every |v| <= max:
+// every sum of n such values, and so every histogram bin, total and sibling
+// difference, is an integer an f64 holds exactly (the f64 ABI then carries
+// the fixed-point sums without loss).
 __device__ int fixed_scale(float max_abs, uint64_t n) {
   if (!(max_abs > 0.0f) || !isfinite(max_abs)) return 0;
   int e;
   frexpf(max_abs, &e);  // max_abs < 2^e
   int c = 0;
   while (c < 64 && (1ull << c) < n) ++c;
-  return 62 - c - e;
+  return kFixedTop - c - e;
 }
 
 __device__ __forceinline__ double pow2d(int e) {
@@ -2257,12 +2260,16 @@ void launch_encode(const uint8_t* col, const uint64_t* colmiss, uint64_t n_rows,
 }
 
 // The split of the 32-bit kernel for `global_rows` rows: lo bits K and the
-// rows between folds R (0: the 32-bit kernel does not apply).
+// rows between folds R (0: the 32-bit kernel does not apply). A value holds
+// Q = kFixedTop - c bits (|q| <= 2^Q, c = ceil(log2 rows)); R = 2^r rows of
+// lo parts (< 2^K each) stay below 2^32 and of hi parts (|hi| <= 2^(Q-K))
+// within +-2^30.
 static void split_for_rows(uint64_t global_rows, int& lo_bits, int& flush_rows) {
   int c = 0;
   while (c < 64 && (1ull << c) < global_rows) ++c;
-  const int K = (64 - c + 1) / 2;
-  const int r = std::min(32 - K, c + K - 32);
+  const int Q = kFixedTop - c;
+  const int K = (Q + 3) / 2;
+  const int r = std::min(32 - K, 30 - (Q - K));
   lo_bits = K;
   flush_rows = (r >= 10 && r < 31) ? (1 << r) : 0;  // at least two 512-row passes per fold
 }

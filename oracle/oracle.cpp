@@ -943,7 +943,7 @@ int32_t fixed_scale(float max_abs, uint64_t n) {
   std::frexp(max_abs, &e);  // max_abs < 2^e
   int c = 0;
   while (c < 64 && (uint64_t(1) << c) < n) ++c;
-  return 62 - c - e;
+  return 53 - c - e;  // every sum of n values within 2^53: exact in an f64
 }
 
 }  // namespace orc

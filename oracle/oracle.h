@@ -146,7 +146,8 @@ int32_t orc_scan_node(const orc_params* p, const uint32_t* feature_offset, uint3
                       uint32_t n_features, orc_scan* out);
 
 /* The fixed-point scale exponent for values of largest magnitude `max_abs`
- * summed over `n` rows: every |rint(v * 2^s)| * n stays within 2^62. */
+ * summed over `n` rows: every |rint(v * 2^s)| * n stays within 2^53, so
+ * every sum is an integer an f64 holds exactly. */
 int32_t orc_fixed_scale(float max_abs, uint64_t n);
 
 #ifdef __cplusplus

@@ -2,8 +2,9 @@
 of the reference's own integer summation (src/backend/exact_sum.rs tests
 `domain_boundary`, `in_domain_sums_match_the_cpu_chain`,
 `the_cpu_chain_rounds_just_past_the_bound`), restated for the fixed-point
-form the CUDA path sums in: q = rint(v * 2^s), s = 62 - ceil(log2 n) - e with
-max|v| < 2^e.
+form the CUDA path sums in: q = rint(v * 2^s), s = 53 - ceil(log2 n) - e with
+max|v| < 2^e, so that every sum of n such values is an integer below 2^53,
+held exactly by an f64 (the C ABI's GradStats).
 
 Checked on the CPU oracle, whose fixed-point histograms the GPU kernels
 equal bit for bit (tests/test_gpu_parity.py)."""
@@ -37,18 +38,18 @@ def _xorshift(seed):
 
 def test_scale_keeps_every_sum_inside_int64():
     # `domain_boundary` in fixed-point terms: n values of magnitude up to
-    # max|v| < 2^e sum to at most n * max|v| * 2^s <= 2^62 once scaled
+    # max|v| < 2^e sum to at most n * max|v| * 2^s <= 2^53 once scaled
     for max_abs in (1.0, float(np.nextafter(np.float32(1.0), np.float32(0.0))), 4.0, 2.0**-10, 2.0**60):
-        for n in (1, 2, 3, 4096, 1 << 41, 1 << 53):
+        for n in (1, 2, 3, 4096, 1 << 24, 1 << 41):
             s = O.fixed_scale(max_abs, n)
             q = round(float(np.float32(max_abs)) * 2.0**s)
-            assert q * n <= 1 << 62, (max_abs, n, s)
+            assert q * n <= 1 << 53, (max_abs, n, s)
             # and it wastes at most one bit each to rounding n and max|v|
             # up to powers of two
-            assert 4 * q * (1 << (n - 1).bit_length()) > 1 << 62, (max_abs, n, s)
-    # zeros take the identity scale; the smallest subnormal scales up past 2^62
+            assert 4 * q * (1 << (n - 1).bit_length()) > 1 << 53, (max_abs, n, s)
+    # zeros take the identity scale; the smallest subnormal scales up past 2^53
     assert O.fixed_scale(0.0, 1 << 60) == 0
-    assert O.fixed_scale(float(np.uint32(1).view(np.float32)), 1) == 62 + 148
+    assert O.fixed_scale(float(np.uint32(1).view(np.float32)), 1) == 53 + 148
 
 
 @pytest.mark.parametrize("case", range(40))
@@ -56,10 +57,12 @@ def test_in_domain_fixed_sums_match_the_f64_chain(case):
     # `in_domain_sums_match_the_cpu_chain`: mostly-positive values with full
     # 24-bit significands near the top of the exact range, mixed with odd
     # small ones. Where the f64 sums are exact the fixed-point sums equal
-    # them bit for bit, whatever the row grouping.
+    # them bit for bit, whatever the row grouping. The scale keeps
+    # max|v| < 2^e strictly, so the largest value is one bit below the f64
+    # domain's 2^(53 - ceil(log2 n)) to keep a grain of 1.
     rnd = _xorshift(0x9E3779B97F4A7C15 + case)
     n = 4096 + next(rnd) % 4096
-    top = 53 - math.ceil(math.log2(n))
+    top = 52 - math.ceil(math.log2(n))
     vals = []
     for _ in range(n):
         r = next(rnd)
@@ -95,10 +98,12 @@ def test_in_domain_fixed_sums_match_the_f64_chain(case):
     np.testing.assert_array_equal(a, b)
 
 
-def test_fixed_sums_keep_the_bit_the_f64_chain_rounds_away():
+def test_fixed_sums_stay_exact_past_the_f64_chain_bound():
     # `the_cpu_chain_rounds_just_past_the_bound`: 1 + k * 2^30 with
-    # k = 2^23 + 1 is 2^53 + 2^30 + 1, which no f64 holds; the f64 chain
-    # drops the 1, the int64 sum keeps it.
+    # k = 2^23 + 1 is 2^53 + 2^30 + 1, which no f64 holds, and the f64 chain
+    # rounds it in an order-dependent way. The fixed-point scale puts the
+    # grain where the n-row sum stays within 2^53: here 4, so the 1 rounds to
+    # 0 once, at quantisation, and the integer sum is exact in an f64.
     k = (1 << 23) + 1
     n = k + 1
     g = np.full(n, 2.0**30, np.float32)
@@ -108,9 +113,10 @@ def test_fixed_sums_keep_the_bit_the_f64_chain_rounds_away():
     gp = np.stack([g, np.ones(n, np.float32)], 1)
     rows = np.arange(n, dtype=np.uint32)
     sg = O.fixed_scale(2.0**30, n)
-    exact = 1 + k * (1 << 30)
+    assert sg == -2
+    want = sum(int(np.rint(np.float64(v) * 2.0**sg)) for v in (1.0, 2.0**30)) + (k - 1) * (1 << 28)
     fixed = O.hist(x, off, cuts, rows, gp, fixed_point=True, sg=sg, sh=0)
-    assert int(fixed[0, 0]) == exact << sg
+    assert int(fixed[0, 0]) == want and want < 1 << 53
+    assert float(int(fixed[0, 0])) == int(fixed[0, 0])  # the f64 ABI carries it exactly
     chain = np.cumsum(g.astype(np.float64))[-1]  # sequential f64 adds in row order
-    assert int(chain) == exact - 1
-    assert int(O.hist(x, off, cuts, rows, gp)[0, 0]) == exact - 1
+    assert int(chain) == 1 + k * (1 << 30) - 1

@@ -600,3 +600,33 @@ def test_scan_kernels_agree(monkeypatch, max_bin):
             runs.append(H.train(p, y=y, rounds=2, matrix=m))
     for a, b in ((0, 2), (1, 3)):
         assert_forest_equal(runs[a].nodes, runs[a].tree_ptr, runs[b].nodes, runs[b].tree_ptr, "warp vs cta")
+
+
+@pytest.mark.parametrize("case", ["c2_logistic", "c2_large", "regularised", "monotone_depthwise", "c1_regression"])
+def test_row_engine_rounds_equal_whole_round_path(case):
+    """The reference's unchanged device round (device_round +
+    build_on_device, restated over the RowEngine calls in
+    hessboost_b200.device_builder) grows the same trees, bit for bit, as
+    hb_train_rounds, and leaves the same margins."""
+    from hessboost_b200.device_builder import RowEngineTrainer
+
+    spec = CASES[case]
+    x, y = spec["gen"]()
+    params = H.TrainingParams(**spec["kw"])
+    mtx = H.BinnedMatrix.from_dense(x, params.max_bin)
+    base = H.base_margin(params, y)
+    e = H.Engine()
+    try:
+        e.upload(mtx)
+        e.train_begin(y, base)
+        want_nodes, want_ptr = e.train_rounds(params, spec["rounds"])
+        want_margins = e.read_margins()
+        e.load_margins(np.full(mtx.n_rows, base, np.float32))
+        tr = RowEngineTrainer(e, params, y)
+        got = [tr.round() for _ in range(spec["rounds"])]
+        got_margins = e.read_margins()
+    finally:
+        e.close()
+    ptr = np.concatenate([[0], np.cumsum([len(t) for t in got])]).astype(np.uint64)
+    assert_forest_equal(np.concatenate(got), ptr, want_nodes, want_ptr, case)
+    np.testing.assert_array_equal(_bits(got_margins), _bits(want_margins))
