@@ -278,6 +278,7 @@ SIGNATURES = {
                                ctypes.c_uint64, _u64p],
     "hb_engine_upload_csr": [_vp, _u64p, _u32p, _f32p, ctypes.c_uint64, ctypes.c_uint32, ctypes.c_uint32, _u32p,
                              _f32p, ctypes.c_uint64, _u64p],
+    "hb_engine_inject_fault": [_vp, ctypes.c_int32],
     "hb_probe_smem": [ctypes.c_int32, ctypes.c_int32, ctypes.c_int32, ctypes.c_int32,
                       ctypes.POINTER(ctypes.c_double)],
 }
@@ -603,7 +604,16 @@ class BinnedMatrix:
     @classmethod
     def from_dense(cls, x, max_bin=256, cuts=None, device=None):
         """Host sketch and binning; with ``device`` (a GPU ordinal) and no
-        given cuts, both run on that GPU (hb_sketch_dense)."""
+        given cuts, both run on that GPU (hb_sketch_dense). A matrix whose
+        features may take more than 256 bins (max_bin > 256) is binned into
+        the CSR index instead (present cells stored, NaN absent: the same
+        cuts and trees as the dense index, src/data/ghist.rs:6-21)."""
+        if max_bin > 256:
+            x = np.ascontiguousarray(x, np.float32)
+            present = ~np.isnan(x)
+            indptr = np.concatenate([[0], np.cumsum(present.sum(axis=1))]).astype(np.uint64)
+            indices = np.nonzero(present)[1].astype(np.uint32)
+            return cls.from_csr(indptr, indices, x[present], x.shape[1], max_bin, cuts=cuts)
         if device is not None and cuts is None:
             off, vals, cols, miss, dense = sketch_dense(x, max_bin, device)
             return cls(off, vals, cols, miss, dense)
@@ -751,6 +761,11 @@ class Engine:
         self._c(lib().hb_build_features(self.h, _ptr(rows, ctypes.c_uint32), rows.size,
                                         _ptr(feats, ctypes.c_uint32), feats.size, out), "hb_build_features")
         return np.ctypeslib.as_array(out).view(np.float64).reshape(-1, 2).copy()
+
+    def inject_fault(self, after_calls):
+        """Arm a host-side fault: the engine's `after_calls`-th checked CUDA
+        call outside stream capture fails as a device error (-1 disarms)."""
+        self._c(lib().hb_engine_inject_fault(self.h, int(after_calls)), "hb_engine_inject_fault")
 
     def build_noalloc(self, rows_ptr, n, out_ptr):
         """hb_build_noalloc on caller-owned device buffers: `rows_ptr` holds n

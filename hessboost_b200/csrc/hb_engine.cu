@@ -154,6 +154,10 @@ struct hb_engine {
   // and the per-(node, feature) directions of a RowEngine scan
   DevBuf<int8_t> mono, scan_dirs;
   std::vector<int8_t> h_mono;
+  // fault injection (hb_engine_inject_fault): checked calls left before the
+  // one that fails (-1: none armed); no injection while a graph is captured
+  int64_t fault_after = -1;
+  bool capturing = false;
 };
 
 namespace {
@@ -179,10 +183,15 @@ hb_status refuse(hb_engine* e, const std::string& why) {
   return HB_REFUSED;
 }
 
-#define HB_CK(e, call)                             \
-  do {                                             \
-    cudaError_t _c = (call);                       \
-    if (_c != cudaSuccess) return fail(e, #call, _c); \
+// A checked CUDA call. With a fault armed (hb_engine_inject_fault) the
+// engine's n-th checked call outside stream capture fails before it runs,
+// as a device error: the call itself never reaches CUDA.
+#define HB_CK(e, call)                                                          \
+  do {                                                                          \
+    if ((e)->fault_after >= 0 && !(e)->capturing && (e)->fault_after-- == 0)    \
+      return fail(e, "injected fault before " #call, cudaErrorMemoryAllocation); \
+    cudaError_t _c = (call);                                                    \
+    if (_c != cudaSuccess) return fail(e, #call, _c);                           \
   } while (0)
 
 #define HB_NCCL(e, call)                                              \
@@ -847,13 +856,50 @@ static hb_status upload_csr(hb_engine* e, const hb_ghist* g, const RawSource* ra
 // CudaHistBackend::new + upload (src/backend/cuda/mod.rs:1626,1687) of the
 // index `g`; with `raw`, the bins (and the dense flag) come from binning the
 // raw device matrix against g's cuts instead of from g.
+// The CSR form (ghist.rs:6-21 `rows`: each present cell's global bin, in
+// feature order within its row) of a dense index given as feature-major
+// local bins and a missing bitmap: the layout an index wider than the row
+// records hold (kMaxRecordFeatures features) trains on. Absent cells are the
+// missing ones, the reference's own equivalence of the two layouts.
+static void dense_to_csr(const hb_ghist* g, std::vector<uint64_t>& ptr, std::vector<uint32_t>& bins) {
+  const uint64_t n = g->n_rows, words = (n + 63) / 64;
+  ptr.assign(n + 1, 0);
+  auto present = [&](uint64_t r, uint32_t f) {
+    return !g->missing || !((g->missing[(uint64_t)f * words + r / 64] >> (r % 64)) & 1ull);
+  };
+  for (uint64_t r = 0; r < n; ++r) {
+    uint64_t k = 0;
+    for (uint32_t f = 0; f < g->n_cols; ++f) k += present(r, f);
+    ptr[r + 1] = ptr[r] + k;
+  }
+  bins.resize(ptr[n]);
+  for (uint64_t r = 0; r < n; ++r) {
+    uint64_t at = ptr[r];
+    for (uint32_t f = 0; f < g->n_cols; ++f)
+      if (present(r, f)) bins[at++] = g->feature_offset[f] + g->columns[(uint64_t)f * n + r];
+  }
+}
+
 static hb_status upload_index(hb_engine* e, const hb_ghist* g, const RawSource* raw) {
-  const bool csr = raw ? raw->ip != nullptr : (g && !g->columns && g->row_ptr);
+  bool csr = raw ? raw->ip != nullptr : (g && !g->columns && g->row_ptr);
   if (!g || !g->feature_offset || !g->cut_values || (!raw && !g->columns && !csr) ||
       (raw && !raw->x && !raw->ip) || g->n_rows == 0 || g->n_cols == 0)
     return HB_INVALID_ARGUMENT;
   if (g->n_rows >= (1ull << 32)) return refuse(e, "at most 2^32 - 1 rows per device");
-  if (!csr && g->n_cols > 224) return refuse(e, "at most 224 features per device index");
+  std::vector<uint64_t> wide_ptr;
+  std::vector<uint32_t> wide_bins;
+  hb_ghist wide_g;
+  if (!csr && g->n_cols > kMaxRecordFeatures) {
+    if (raw) return refuse(e, "a raw dense matrix of more than 224 features: upload its CSR form");
+    dense_to_csr(g, wide_ptr, wide_bins);
+    wide_g = *g;
+    wide_g.columns = nullptr;
+    wide_g.missing = nullptr;
+    wide_g.row_ptr = wide_ptr.data();
+    wide_g.row_bins = wide_bins.empty() ? nullptr : wide_bins.data();
+    g = &wide_g;
+    csr = true;
+  }
   DevConst& c = e->c;
   const uint64_t shard_rows = e->shard_global;
   c = DevConst{};
@@ -864,16 +910,19 @@ static hb_status upload_index(hb_engine* e, const hb_ghist* g, const RawSource* 
   c.total_bins = e->h_fo.back();
   uint32_t widest = 0;
   for (uint32_t f = 0; f < g->n_cols; ++f) widest = std::max(widest, e->h_fo[f + 1] - e->h_fo[f]);
-  if (widest > 256) return refuse(e, "features of more than 256 bins need 16-bit bins");
+  if (!csr && widest > 256) return refuse(e, "features of more than 256 bins need the CSR index");
+  if (widest > 65535) return refuse(e, "at most 65,535 bins per feature");
   c.max_bins = widest;
   c.mask_off = (g->n_cols + 3) / 4 * 4;
   c.stride = (c.mask_off + 4 * ((g->n_cols + 31) / 32) + 15) / 16 * 16;
   c.dense = g->dense ? 1 : 0;
   c.n_groups = (g->n_cols + kGroupFeatures - 1) / kGroupFeatures;
-  // Both histogram kernels give the same exact sums; HB_HIST_KERNEL=64
-  // selects the 64-bit-atomic one for every size (comparison runs).
+  // Every histogram kernel gives the same exact sums; HB_HIST_KERNEL=64
+  // selects the 64-bit-atomic one for every size, =staged the cp.async-staged
+  // 32-bit one instead of k_hist32r (comparison runs).
   const char* hk = std::getenv("HB_HIST_KERNEL");
   c.hist64 = (hk && std::strcmp(hk, "64") == 0) ? 1u : 0u;
+  c.hist_staged = (hk && std::strcmp(hk, "staged") == 0) ? 1u : 0u;
   // HB_SCAN_KERNEL=cta keeps the CTA-per-feature scan for every width.
   const char* sk = std::getenv("HB_SCAN_KERNEL");
   c.scan_cta = (sk && std::strcmp(sk, "cta") == 0) ? 1u : 0u;
@@ -978,7 +1027,7 @@ hb_status hb_engine_upload_dense(hb_engine* e, const float* x, uint64_t n_rows, 
     return refuse(e, "a row shard needs the whole matrix's cuts: hb_sketch_dense of the whole "
                      "matrix, then hb_bin_dense of the shard and hb_engine_upload");
   if (n_rows >= (1ull << 32)) return refuse(e, "at most 2^32 - 1 rows per device");
-  if (n_cols > 224) return refuse(e, "at most 224 features per device index");
+  if (n_cols > kMaxRecordFeatures) return refuse(e, "at most 224 features per raw dense upload");
   cudaStream_t s = e->stream;
   DevBuf<float> dx;
   HB_CK(e, dx.alloc((size_t)n_rows * n_cols));
@@ -1657,10 +1706,12 @@ static hb_status graph_rounds(hb_engine* e, const hb_train_params* p, int rounds
   cudaStream_t s = e->stream;
   auto capture = [&](int n, cudaGraphExec_t* exec) -> hb_status {
     HB_CK(e, cudaStreamBeginCapture(s, cudaStreamCaptureModeThreadLocal));
+    e->capturing = true;
     hb_status st = HB_OK;
     for (int r = 0; r < n && st == HB_OK; ++r) st = round_work(e, p);
     cudaGraph_t g = nullptr;
     cudaError_t ce = cudaStreamEndCapture(s, &g);
+    e->capturing = false;
     if (st != HB_OK) {
       if (g) cudaGraphDestroy(g);
       return st;
@@ -1858,6 +1909,13 @@ hb_status hb_train(hb_engine* e, const hb_train_params* p, const float* labels, 
   st = hb_train_begin(e, labels, n, base_margin);
   if (st != HB_OK) return st;
   return hb_train_rounds(e, p, rounds, nodes, nodes_cap, tree_ptr);
+}
+
+hb_status hb_engine_inject_fault(hb_engine* e, int32_t after_calls) {
+  if (!e) return HB_INVALID_ARGUMENT;
+  if (after_calls < -1) return HB_INVALID_ARGUMENT;
+  e->fault_after = after_calls;
+  return HB_OK;
 }
 
 hb_status hb_engine_reset_stats(hb_engine* e, int32_t timing) {

@@ -402,7 +402,7 @@ hb_status hb_bin_csr(const uint64_t* indptr, const uint32_t* indices, const floa
   const uint64_t nnz = indptr[n_rows];
   if (nnz && !row_bins) return HB_INVALID_ARGUMENT;
   for (uint32_t f = 0; f < n_cols; ++f)
-    if (feature_offset[f + 1] <= feature_offset[f] || feature_offset[f + 1] - feature_offset[f] > 256)
+    if (feature_offset[f + 1] <= feature_offset[f] || feature_offset[f + 1] - feature_offset[f] > 65535)
       return HB_REFUSED;
   std::copy(indptr, indptr + n_rows + 1, row_ptr);
   std::atomic<int> short_row{0};

@@ -30,6 +30,7 @@ constexpr int kTile = 2048;              // partition tile (rows per CTA)
 constexpr int kTileWords = kTile / 32;
 constexpr int kHistThreads = 1024;
 constexpr int kGroupFeatures = 32;       // features per histogram CTA group
+constexpr uint32_t kMaxRecordFeatures = 224;  // widest dense index kept as row records
 
 // Fixed-point range: every |q| * rows <= 2^kFixedTop, so each sum is an
 // integer below 2^53, exact in an f64.
@@ -57,6 +58,7 @@ struct DevConst {
   uint32_t dense;         // index-level: no missing cell anywhere
   uint32_t n_groups;      // feature groups of kGroupFeatures
   uint32_t hist64;        // 1: always the 64-bit-atomic histogram kernel
+  uint32_t hist_staged;   // 1: the cp.async-staged 32-bit kernel instead of k_hist32r
   uint32_t scan_cta;      // 1: always the CTA-per-feature split scan
   // CSR index (csr = 1): each row's global bins ascending, absent = missing;
   // fo = the device copy of feature_offset (both layouts)
@@ -74,8 +76,10 @@ struct DevConst {
 };
 
 // One frontier entry of the level being grown. The first 32 bytes are read
-// as two int4 by the histogram plan (load_front_cg).
-struct Front {
+// as two int4 by the histogram plan (load_front_cg), so every entry of a
+// Front array starts on a 16-byte boundary: 16-byte alignment, a size that is
+// a multiple of 16.
+struct alignas(16) Front {
   int32_t node;       // tree node id
   int32_t slot;       // histogram slot (or -1)
   uint32_t begin;     // segment in the current row buffer
@@ -86,6 +90,7 @@ struct Front {
   float root_gain = 0.0f;       // the caller's root gain (RowEngine scans) ...
   int32_t root_gain_given = 0;  // ... used when set, else computed
 };
+static_assert(sizeof(Front) % 16 == 0 && alignof(Front) == 16, "Front entries must be 16-byte aligned");
 
 // The best candidate of one (node, feature) pair.
 struct Cand {

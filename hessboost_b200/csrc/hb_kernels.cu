@@ -40,6 +40,44 @@ __device__ __forceinline__ uint32_t pick_word(const uint4& a, const uint4& b, in
 }
 
 
+// L2 cache policies (createpolicy) and loads/stores that carry them: data
+// read once streams through L2 evict-first; the (g, h) pairs, re-read by
+// every histogram launch of a round, stay evict-last.
+__device__ __forceinline__ uint64_t l2_evict_first() {
+  uint64_t p;
+  asm("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(p));
+  return p;
+}
+__device__ __forceinline__ uint64_t l2_evict_last() {
+  uint64_t p;
+  asm("createpolicy.fractional.L2::evict_last.b64 %0, 1.0;" : "=l"(p));
+  return p;
+}
+__device__ __forceinline__ uint4 ld_hint16(const void* ptr, uint64_t pol) {
+  uint4 v;
+  asm("ld.global.nc.L1::no_allocate.L2::cache_hint.v4.u32 {%0, %1, %2, %3}, [%4], %5;"
+      : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+      : "l"(ptr), "l"(pol));
+  return v;
+}
+__device__ __forceinline__ uint32_t ld_hint4(const void* ptr, uint64_t pol) {
+  uint32_t v;
+  asm("ld.global.nc.L1::no_allocate.L2::cache_hint.u32 %0, [%1], %2;" : "=r"(v) : "l"(ptr), "l"(pol));
+  return v;
+}
+__device__ __forceinline__ float2 ld_hint8(const float2* ptr, uint64_t pol) {
+  float2 v;
+  asm("ld.global.nc.L1::no_allocate.L2::cache_hint.v2.f32 {%0, %1}, [%2], %3;"
+      : "=f"(v.x), "=f"(v.y)
+      : "l"(ptr), "l"(pol));
+  return v;
+}
+
+__device__ __forceinline__ void st_hint8(float2* ptr, float2 v, uint64_t pol) {
+  asm volatile("st.global.L2::cache_hint.v2.f32 [%0], {%1, %2}, %3;" ::"l"(ptr), "f"(v.x), "f"(v.y), "l"(pol)
+               : "memory");
+}
+
 // ---------------------------------------------------------------------------
 // Objectives.
 
@@ -219,6 +257,7 @@ __global__ void k_gradients(int kind, float* __restrict__ margin,
   extern __shared__ WNode s_tree[];
   if (wtree && !(pending && *pending)) wtree = nullptr;  // no tree waiting for the margins
   if (wtree) stage_tree(wtree, ls_last, s_tree);
+  const uint64_t pol_keep = l2_evict_last();  // the round's histogram launches re-read the pairs
   float mg = 0.0f, mh = 0.0f;
   bool nonfinite = false;
   const unsigned lane = threadIdx.x & 31;
@@ -249,7 +288,7 @@ __global__ void k_gradients(int kind, float* __restrict__ margin,
       h = w;
     }
     if (in) {
-      gpair[i] = make_float2(g, h);
+      st_hint8(gpair + i, make_float2(g, h), pol_keep);
       fold_max(g, h, mg, mh, nonfinite);
     }
   }
@@ -901,6 +940,254 @@ __global__ void __launch_bounds__(kH32Threads, 1)
   }
 }
 
+// The split-accumulator histogram without shared-memory staging: each
+// thread loads its row (row id, record bytes, mask, (g, h) pair) straight
+// into registers, the 32 warps of the CTA hiding one another's load latency
+// behind their shared-memory atomics, with L2 eviction hints (records and
+// row ids streamed evict-first, the pairs evict-last, so the level
+// launches' random gathers of the pairs hit L2). The four 32-bit arrays are
+// the accumulators themselves: with every sum within 2^53 (kFixedTop) the
+// spill interval R is at least 2^14 rows at a million rows or more, so the
+// CTA adds its partial sums to the node histogram only at the end of an
+// entry or every R rows, and holds no register copy of them. One CTA of
+// kHRThreads threads per SM (G = 1), half that for two groups a CTA.
+template <int G>
+struct HR {
+  static constexpr int kThreads = G == 1 ? 1024 : 512;
+  static constexpr int kSlots = kNSlots / kThreads;  // slots a thread stages at a flush
+  static constexpr int kBinShift = G == 1 ? 8 : 7;
+  static constexpr size_t smem() { return (size_t)kSlotStride * 16; }
+};
+
+template <int G>
+struct HRRow {
+  uint4 a[G], b[G];
+  uint32_t m[G];
+  float2 p;
+};
+
+template <int G>
+__global__ void __launch_bounds__(HR<G>::kThreads, 1)
+    k_hist32r(DevConst c, const uint32_t* __restrict__ fo, const uint8_t* __restrict__ rec,
+              const float2* __restrict__ gpair, const Scale* __restrict__ scale,
+              const uint32_t* __restrict__ rows, const HEntry* __restrict__ entries,
+              const LevelState* __restrict__ ls, longlong2* __restrict__ hist,
+              long long* __restrict__ totals, unsigned long long* __restrict__ row_stats, int lo_bits,
+              int flush_rows) {
+  constexpr int kT = HR<G>::kThreads;
+  constexpr int kS = HR<G>::kSlots;
+  constexpr int kBS = HR<G>::kBinShift;
+  extern __shared__ __align__(16) uint32_t s32[];
+  const int n_entries = ls->n_hentries;
+  const uint64_t total = ls->hist_rows;
+  if (n_entries <= 0 || total == 0) return;
+  if (row_stats && blockIdx.x == 0 && blockIdx.y == 0 && threadIdx.x == 0)
+    atomicAdd(&row_stats[entries[0].identity ? 0 : 1], (unsigned long long)total);
+  const uint64_t per = (total + gridDim.x - 1) / gridDim.x;
+  const uint64_t a0 = (uint64_t)blockIdx.x * per;
+  const uint64_t b0 = min(total, a0 + per);
+  if (a0 >= b0) return;
+
+  const int g0 = blockIdx.y * G;
+  const int ng = min(G, (int)c.n_groups - g0);
+  uint32_t* lo_g = s32;
+  uint32_t* hi_g = s32 + kSlotStride;
+  uint32_t* lo_h = s32 + 2 * kSlotStride;
+  uint32_t* hi_h = s32 + 3 * kSlotStride;
+  {
+    uint4* z = reinterpret_cast<uint4*>(s32);
+    for (int i = threadIdx.x; i < kSlotStride; i += kT) z[i] = make_uint4(0u, 0u, 0u, 0u);
+  }
+  __syncthreads();
+
+  const uint64_t pol_stream = l2_evict_first(), pol_keep = l2_evict_last();
+  const double fg = scale->fg, fh = scale->fh;
+  const int tid = threadIdx.x;
+  const int lane = tid & 31;
+  const uint32_t lane4 = (uint32_t)lane << 2;
+  const uint32_t sbase = (uint32_t)__cvta_generic_to_shared(s32);
+  bool wide[G], mask_in_block[G];
+  uint32_t mask_at[G], dummy[G];
+  int mask_word[G];
+#pragma unroll
+  for (int lg = 0; lg < G; ++lg) {
+    const int g = g0 + lg;
+    const int nfg = lg < ng ? min(kGroupFeatures, (int)c.n_cols - g * kGroupFeatures) : 0;
+    wide[lg] = c.stride >= (uint32_t)(32 * g + 32);
+    mask_at[lg] = c.mask_off + 4 * g;
+    mask_in_block[lg] = mask_at[lg] >= (uint32_t)(32 * g) &&
+                        mask_at[lg] + 4 <= (uint32_t)(32 * g + (wide[lg] ? 32 : 16));
+    mask_word[lg] = (int)(mask_at[lg] - 32 * (uint32_t)g) >> 2;
+    dummy[lg] = nfg >= 32 ? 0u : (0xffffffffu << nfg);
+  }
+  const bool want_totals = totals != nullptr && g0 == 0;
+  const uint32_t lo_mask = (uint32_t)((1ull << lo_bits) - 1ull);
+  long long tg = 0, th = 0;
+
+  // The CTA's partial sums so far into the node histogram `slot`, and the
+  // accumulators back to zero: each thread combines its kS slots (runs of
+  // four consecutive words) into int64, stages them feature-major in the
+  // same shared memory (bins XOR-swizzled against bank conflicts), then
+  // each warp adds one feature's (g, h) words with contiguous 64-bit reds.
+  auto flush = [&](int slot) {
+    __syncthreads();
+    long long vg[kS], vh[kS];
+#pragma unroll
+    for (int j = 0; j < kS / 4; ++j) {
+      const int base = 4 * (tid + j * kT);
+      const uint4 a = *reinterpret_cast<const uint4*>(&lo_g[base]);
+      const uint4 b = *reinterpret_cast<const uint4*>(&hi_g[base]);
+      const uint4 p = *reinterpret_cast<const uint4*>(&lo_h[base]);
+      const uint4 q = *reinterpret_cast<const uint4*>(&hi_h[base]);
+      vg[4 * j + 0] = ((long long)(int)b.x << lo_bits) + (long long)a.x;
+      vg[4 * j + 1] = ((long long)(int)b.y << lo_bits) + (long long)a.y;
+      vg[4 * j + 2] = ((long long)(int)b.z << lo_bits) + (long long)a.z;
+      vg[4 * j + 3] = ((long long)(int)b.w << lo_bits) + (long long)a.w;
+      vh[4 * j + 0] = ((long long)(int)q.x << lo_bits) + (long long)p.x;
+      vh[4 * j + 1] = ((long long)(int)q.y << lo_bits) + (long long)p.y;
+      vh[4 * j + 2] = ((long long)(int)q.z << lo_bits) + (long long)p.z;
+      vh[4 * j + 3] = ((long long)(int)q.w << lo_bits) + (long long)p.w;
+    }
+    __syncthreads();
+    constexpr int kNB = 1 << kBS;
+    long long* stg = reinterpret_cast<long long*>(s32);
+#pragma unroll
+    for (int j = 0; j < kS; ++j) {
+      const int sl = 4 * (tid + (j >> 2) * kT) + (j & 3);
+      const int row = ((sl >> (kBS + 5)) << 5) | (sl & 31);
+      const int bin = (sl >> 5) & (kNB - 1);
+      const int at = 2 * (row * kNB + (bin ^ ((row >> 2) & 7)));
+      stg[at] = vg[j];
+      stg[at + 1] = vh[j];
+    }
+    __syncthreads();
+    unsigned long long* dstw = reinterpret_cast<unsigned long long*>(hist + (uint64_t)slot * c.total_bins);
+    const int warp = tid >> 5;
+    for (int row = warp; row < G * 32; row += kT / 32) {
+      const int lgs = row >> 5;
+      const int f = (g0 + lgs) * kGroupFeatures + (row & 31);
+      if (lgs >= ng || f >= (int)c.n_cols) continue;
+      const uint32_t fs = fo[f];
+      const uint32_t nw = 2 * (fo[f + 1] - fs);
+      for (uint32_t w = lane; w < nw; w += 32) {
+        const int bin = (int)(w >> 1);
+        const long long v = stg[2 * (row * kNB + (bin ^ ((row >> 2) & 7))) + (w & 1)];
+        if (v) atomicAdd(dstw + 2 * (uint64_t)fs + w, (unsigned long long)v);
+      }
+    }
+    __syncthreads();
+    uint4* z = reinterpret_cast<uint4*>(s32);
+    for (int i = tid; i < kSlotStride; i += kT) z[i] = make_uint4(0u, 0u, 0u, 0u);
+    __syncthreads();
+  };
+
+  int e = 0;
+  {
+    int hi = n_entries - 1;
+    while (e < hi) {
+      const int mid = (e + hi + 1) >> 1;
+      if (entries[mid].prefix <= a0) e = mid; else hi = mid - 1;
+    }
+  }
+  uint64_t pos = a0;
+  int since = 0;
+  while (pos < b0 && e < n_entries) {
+    const HEntry en = entries[e];
+    const uint64_t end_e = min(b0, en.prefix + en.len);
+    const int n_it = (int)((end_e - pos + kT - 1) / kT);
+    auto load = [&](uint64_t i, HRRow<G>& r) {
+      const uint32_t at = en.begin + (uint32_t)(i - en.prefix);
+      const uint32_t row = en.identity ? at : ld_hint4(rows + at, pol_stream);
+      const uint8_t* rr = rec + (uint64_t)row * c.stride;
+#pragma unroll
+      for (int lg = 0; lg < G; ++lg) {
+        if (lg < ng) {
+          const uint8_t* rp = rr + 32 * (g0 + lg);
+          r.a[lg] = ld_hint16(rp, pol_stream);
+          r.b[lg] = wide[lg] ? ld_hint16(rp + 16, pol_stream) : make_uint4(0u, 0u, 0u, 0u);
+          r.m[lg] = mask_in_block[lg] ? 0u : ld_hint4(rr + mask_at[lg], pol_stream);
+        }
+      }
+      r.p = ld_hint8(gpair + row, pol_keep);
+    };
+    for (int it = 0; it < n_it; ++it) {
+      const uint64_t i = pos + (uint64_t)it * kT + tid;
+      if (i < end_e) {
+        HRRow<G> cur;
+        load(i, cur);
+        const long long qg = __double2ll_rn((double)cur.p.x * fg);
+        const long long qh = __double2ll_rn((double)cur.p.y * fh);
+        if (want_totals) {
+          tg += qg;
+          th += qh;
+        }
+        const uint32_t lg_ = (uint32_t)qg & lo_mask, lh = (uint32_t)qh & lo_mask;
+        const uint32_t hg = (uint32_t)(qg >> lo_bits), hh = (uint32_t)(qh >> lo_bits);
+#pragma unroll
+        for (int lg = 0; lg < G; ++lg) {
+          if (lg >= ng) break;
+          const uint4 v1 = cur.b[lg];
+          uint32_t mask = mask_in_block[lg] ? pick_word(cur.a[lg], v1, mask_word[lg]) : cur.m[lg];
+          mask |= dummy[lg];
+          // the 32 record bytes rotated right by `lane` bytes (word rotation
+          // by lane / 4 in three select stages, then a byte funnel shift):
+          // step s reads byte s, the lane's feature (lane + s) mod 32
+          uint32_t w[8] = {cur.a[lg].x, cur.a[lg].y, cur.a[lg].z, cur.a[lg].w, v1.x, v1.y, v1.z, v1.w};
+          const int q = lane >> 2;
+          uint32_t t[8];
+#pragma unroll
+          for (int j = 0; j < 8; ++j) t[j] = (q & 4) ? w[(j + 4) & 7] : w[j];
+#pragma unroll
+          for (int j = 0; j < 8; ++j) w[j] = (q & 2) ? t[(j + 2) & 7] : t[j];
+#pragma unroll
+          for (int j = 0; j < 8; ++j) t[j] = (q & 1) ? w[(j + 1) & 7] : w[j];
+          const int sh = (lane & 3) * 8;
+#pragma unroll
+          for (int j = 0; j < 8; ++j) w[j] = __funnelshift_r(t[j], t[(j + 1) & 7], sh);
+          const uint32_t mrot = __funnelshift_r(mask, mask, lane);
+          const uint32_t grow = (uint32_t)lg << (kBS + 7);
+#pragma unroll
+          for (int st = 0; st < 32; ++st) {
+            const uint32_t word = w[st >> 2];
+            const int k = st & 3;
+            const uint32_t binx = (k == 0 ? (word << 7) : (word >> (8 * k - 7))) & (((1u << kBS) - 1u) << 7);
+            const uint32_t rowx = ((mrot >> st) & 1u) ? (uint32_t)(kTrashBin << 7) : (binx | grow);
+            const uint32_t ad = sbase + (rowx | ((lane4 + 4u * (uint32_t)st) & 124u));
+            asm volatile(
+                "red.shared.add.u32 [%0], %1;\n\t"
+                "red.shared.add.u32 [%0+%5], %2;\n\t"
+                "red.shared.add.u32 [%0+%6], %3;\n\t"
+                "red.shared.add.u32 [%0+%7], %4;" ::"r"(ad),
+                "r"(lg_), "r"(hg), "r"(lh), "r"(hh), "n"(kSlotStride * 4), "n"(kSlotStride * 8),
+                "n"(kSlotStride * 12)
+                : "memory");
+          }
+        }
+      }
+      since += kT;
+      if (since + kT > flush_rows && it + 1 < n_it) {  // the next pass could pass R rows
+        flush(en.slot);
+        since = 0;
+      }
+    }
+    flush(en.slot);
+    since = 0;
+    pos = end_e;
+    ++e;
+  }
+  if (want_totals) {
+    using BR = cub::BlockReduce<long long, kT>;
+    __shared__ typename BR::TempStorage tmp;
+    long long sgt = BR(tmp).Sum(tg);
+    __syncthreads();
+    long long sht = BR(tmp).Sum(th);
+    if (tid == 0) {
+      atomicAdd(reinterpret_cast<unsigned long long*>(&totals[0]), (unsigned long long)sgt);
+      atomicAdd(reinterpret_cast<unsigned long long*>(&totals[1]), (unsigned long long)sht);
+    }
+  }
+}
+
 // sibling = parent - built (int64, exact; src/tree/hist/mod.rs:32).
 __global__ void k_subtract(const Triple* __restrict__ pairs, const LevelState* __restrict__ ls,
                            uint32_t total_bins, longlong2* __restrict__ hist) {
@@ -1162,6 +1449,198 @@ __global__ void __launch_bounds__(kSplitThreads)
       gs = s_bs[w];
     }
   if (gs == INT_MAX) {  // no finite candidate in this feature
+    if (t == 0) {
+      Cand e;
+      e.loss = -INFINITY;
+      e.bin = -1;
+      e.default_left = 0;
+      e.pad = 0;
+      e.lg = e.lh = 0;
+      *out = e;
+    }
+  } else if (best_seq == gs) {
+    Cand e;
+    e.loss = best;
+    e.bin = bbin;
+    e.default_left = bdl;
+    e.pad = 0;
+    e.lg = blg;
+    e.lh = blh;
+    *out = e;
+  }
+}
+
+// The split scan for features of more than kSplitThreads bins (CSR indexes
+// with max_bin above 256): the same candidates, sequence numbers and
+// first-maximum rule as k_scan, the feature's bins taken kSplitThreads at a
+// time with the prefix carried between chunks. A first pass forms the
+// feature's total (and writes a sibling's histogram as parent - built), the
+// second scans and scores.
+__global__ void __launch_bounds__(kSplitThreads)
+    k_scan_wide(DevConst c, const uint32_t* __restrict__ fo, longlong2* __restrict__ hist,
+                const Front* __restrict__ front, const LevelState* __restrict__ ls,
+                const Triple* __restrict__ pairs, int sib_base, const Scale* __restrict__ scale,
+                Cand* __restrict__ cand, const int8_t* __restrict__ dirs) {
+  const int f = blockIdx.x;
+  const int k = blockIdx.y;
+  if (k >= ls->n_front) return;
+  const int t = threadIdx.x, lane = t & 31, warp = t >> 5;
+  const Front fr = front[k];
+  const uint32_t fs = fo[f];
+  const int nb = (int)(fo[f + 1] - fs);
+  Cand* out = cand + (uint64_t)k * c.n_cols + f;
+  if (nb <= 1 || fr.slot < 0) {
+    if (t == 0) {
+      Cand e;
+      e.loss = -INFINITY;
+      e.bin = -1;
+      e.default_left = 0;
+      e.pad = 0;
+      e.lg = e.lh = 0;
+      *out = e;
+    }
+    return;
+  }
+  const bool sib = pairs != nullptr && (sib_base >= 0 ? fr.slot >= sib_base : fr.slot == pairs[0].sibling);
+  Triple tr{};
+  if (sib) tr = pairs[sib_base >= 0 ? fr.slot - sib_base : 0];
+  __shared__ long long s_wg[kSplitThreads / 32], s_wh[kSplitThreads / 32];
+  __shared__ float s_bl[kSplitThreads / 32];
+  __shared__ int s_bs[kSplitThreads / 32];
+  // pass 1: the feature's total (sibling histograms written as they go)
+  long long sum_g = 0, sum_h = 0;
+  for (int c0 = 0; c0 < nb; c0 += kSplitThreads) {
+    const int b = c0 + t;
+    if (b < nb) {
+      longlong2 v;
+      if (sib) {
+        const longlong2 pv = hist[(uint64_t)tr.parent * c.total_bins + fs + b];
+        const longlong2 bv = hist[(uint64_t)tr.built * c.total_bins + fs + b];
+        v = make_longlong2(pv.x - bv.x, pv.y - bv.y);
+        hist[(uint64_t)fr.slot * c.total_bins + fs + b] = v;
+      } else {
+        v = hist[(uint64_t)fr.slot * c.total_bins + fs + b];
+      }
+      sum_g += v.x;
+      sum_h += v.y;
+    }
+  }
+#pragma unroll
+  for (int d = 16; d > 0; d >>= 1) {
+    sum_g += __shfl_xor_sync(kFull, sum_g, d);
+    sum_h += __shfl_xor_sync(kFull, sum_h, d);
+  }
+  if (lane == 0) {
+    s_wg[warp] = sum_g;
+    s_wh[warp] = sum_h;
+  }
+  __syncthreads();
+  long long tot_g = 0, tot_h = 0;
+#pragma unroll
+  for (int w = 0; w < kSplitThreads / 32; ++w) {
+    tot_g += s_wg[w];
+    tot_h += s_wh[w];
+  }
+  __syncthreads();
+  const bool has_missing = !c.dense && !(tot_g == fr.g && tot_h == fr.h);
+  const double ig = scale->ig, ih = scale->ih;
+  const float lo = (float)fr.lower, up = (float)fr.upper;
+  const int dir = dirs ? (int)dirs[(uint64_t)k * c.n_cols + f] : (c.mono ? (int)c.mono[f] : 0);
+  const float root_gain =
+      fr.root_gain_given ? fr.root_gain : node_gain(ll2d(fr.g) * ig, ll2d(fr.h) * ih, c, lo, up);
+  float best = -INFINITY;
+  int best_seq = INT_MAX;
+  long long blg = 0, blh = 0;
+  int bbin = -1, bdl = 0;
+  // pass 2: chunk by chunk, the block scan plus the carried prefix
+  long long carry_g = 0, carry_h = 0;
+  for (int c0 = 0; c0 < nb; c0 += kSplitThreads) {
+    const int b = c0 + t;
+    longlong2 v = make_longlong2(0, 0);
+    if (b < nb) v = hist[(uint64_t)fr.slot * c.total_bins + fs + b];
+    long long ig_ = v.x, ih_ = v.y;
+#pragma unroll
+    for (int d = 1; d < 32; d <<= 1) {
+      const long long tg = __shfl_up_sync(kFull, ig_, d);
+      const long long th = __shfl_up_sync(kFull, ih_, d);
+      if (lane >= d) {
+        ig_ += tg;
+        ih_ += th;
+      }
+    }
+    if (lane == 31) {
+      s_wg[warp] = ig_;
+      s_wh[warp] = ih_;
+    }
+    __syncthreads();
+    long long off_g = carry_g, off_h = carry_h, chunk_g = 0, chunk_h = 0;
+#pragma unroll
+    for (int w = 0; w < kSplitThreads / 32; ++w) {
+      if (w < warp) {
+        off_g += s_wg[w];
+        off_h += s_wh[w];
+      }
+      chunk_g += s_wg[w];
+      chunk_h += s_wh[w];
+    }
+    __syncthreads();
+    const long long incl_g = ig_ + off_g, incl_h = ih_ + off_h;
+    const long long excl_g = incl_g - v.x, excl_h = incl_h - v.y;
+    if (b < nb && (v.x != 0 || v.y != 0)) {
+      const float l = cand_loss(ll2d(incl_g) * ig, ll2d(incl_h) * ih, ll2d(fr.g - incl_g) * ig,
+                                ll2d(fr.h - incl_h) * ih, root_gain, c, lo, up, dir);
+      if (isfinite(l) && cand_better(l, b, best, best_seq)) {
+        best = l;
+        best_seq = b;
+        blg = incl_g;
+        blh = incl_h;
+        bbin = (int)fs + b;
+        bdl = 0;
+      }
+      if (has_missing) {
+        const long long rg = tot_g - excl_g, rh = tot_h - excl_h;
+        const long long lg2 = fr.g - rg, lh2 = fr.h - rh;
+        const float lb = cand_loss(ll2d(lg2) * ig, ll2d(lh2) * ih, ll2d(rg) * ig, ll2d(rh) * ih,
+                                   root_gain, c, lo, up, dir);
+        const int seq = nb + (nb - 1 - b);
+        if (isfinite(lb) && cand_better(lb, seq, best, best_seq)) {
+          best = lb;
+          best_seq = seq;
+          blg = lg2;
+          blh = lh2;
+          bbin = b == 0 ? -1 : (int)fs + b - 1;
+          bdl = 1;
+        }
+      }
+    }
+    carry_g += chunk_g;
+    carry_h += chunk_h;
+  }
+  float wb = best;
+  int ws = best_seq;
+#pragma unroll
+  for (int d = 16; d > 0; d >>= 1) {
+    const float ob = __shfl_xor_sync(kFull, wb, d);
+    const int os = __shfl_xor_sync(kFull, ws, d);
+    if (cand_better(ob, os, wb, ws)) {
+      wb = ob;
+      ws = os;
+    }
+  }
+  if (lane == 0) {
+    s_bl[warp] = wb;
+    s_bs[warp] = ws;
+  }
+  __syncthreads();
+  float gb = s_bl[0];
+  int gs = s_bs[0];
+#pragma unroll
+  for (int w = 1; w < kSplitThreads / 32; ++w)
+    if (cand_better(s_bl[w], s_bs[w], gb, gs)) {
+      gb = s_bl[w];
+      gs = s_bs[w];
+    }
+  if (gs == INT_MAX) {
     if (t == 0) {
       Cand e;
       e.loss = -INFINITY;
@@ -2287,7 +2766,10 @@ static int hist_groups_per_cta(const DevConst& c) {
 
 size_t hist_smem_bytes(const DevConst& c) {
   if (c.csr) return 0;
-  if (use_hist32(c)) return hist_groups_per_cta(c) == 2 ? H32<2>::smem() : H32<1>::smem();
+  if (use_hist32(c)) {
+    const size_t staged = hist_groups_per_cta(c) == 2 ? H32<2>::smem() : H32<1>::smem();
+    return std::max(staged, HR<1>::smem());
+  }
   return (size_t)c.max_bins * 32 * 16;
 }
 
@@ -2326,6 +2808,22 @@ void launch_hist(const DevConst& c, const uint32_t* fo, const uint8_t* rec, cons
     int K, R;
     split_for_rows(c.global_rows, K, R);
     grid.y = (c.n_groups + G - 1) / G;
+    if (!c.hist_staged) {
+      static size_t granted_r[2][64] = {{0}};
+      if (dev < 0 || dev >= 64 || granted_r[G - 1][dev] < smem) {
+        if (cudaFuncSetAttribute(G == 2 ? (const void*)k_hist32r<2> : (const void*)k_hist32r<1>,
+                                 cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) == cudaSuccess &&
+            dev >= 0 && dev < 64)
+          granted_r[G - 1][dev] = smem;
+      }
+      if (G == 2)
+        k_hist32r<2><<<grid, HR<2>::kThreads, smem, s>>>(c, fo, rec, gpair, scale, rows, entries, ls, hist,
+                                                          totals, row_stats, K, R);
+      else
+        k_hist32r<1><<<grid, HR<1>::kThreads, smem, s>>>(c, fo, rec, gpair, scale, rows, entries, ls, hist,
+                                                          totals, row_stats, K, R);
+      return;
+    }
     if (G == 2)
       k_hist32<2><<<grid, kH32Threads, smem, s>>>(c, fo, rec, gpair, scale, rows, entries, ls, hist,
                                                   totals, row_stats, K, R);
@@ -2362,6 +2860,10 @@ void launch_scan(const DevConst& c, const uint32_t* fo, longlong2* hist, const F
     return;
   }
   dim3 grid(c.n_cols, max_front);
+  if (c.max_bins > (uint32_t)kSplitThreads) {
+    k_scan_wide<<<grid, kSplitThreads, 0, s>>>(c, fo, hist, front, ls, pairs, sib_base, scale, cand, dirs);
+    return;
+  }
   k_scan<<<grid, kSplitThreads, 0, s>>>(c, fo, hist, front, ls, pairs, sib_base, scale, cand, dirs);
 }
 

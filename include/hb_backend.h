@@ -153,6 +153,10 @@ typedef struct hb_device_loss {
  *   CSR:     `columns` NULL; the stored entries' global bins row by row
  *            (ghist.rs:6-21 `rows`), ascending within a row, offsets in
  *            `row_ptr`; an absent feature is missing. */
+/* GHistIndex (src/data/ghist.rs:195). A dense index (columns set) keeps
+ * one-byte local bins, so each feature has at most 256 bins; one of more
+ * than 224 features is converted to the CSR form on upload. A CSR index
+ * (columns NULL) allows up to 65,535 bins a feature. */
 typedef struct hb_ghist {
   uint64_t n_rows;
   uint32_t n_cols;
@@ -378,7 +382,7 @@ hb_status hb_cuts_csr(const uint64_t* indptr, const uint32_t* indices, const flo
                       float* cut_values, uint64_t cap, uint64_t* total);
 /* The CSR index: row_ptr (n_rows + 1, = indptr) and every entry's global
  * bin, ascending within its row. HB_REFUSED when a feature has more than
- * 256 bins. */
+ * 65,535 bins. */
 hb_status hb_bin_csr(const uint64_t* indptr, const uint32_t* indices, const float* values,
                      uint64_t n_rows, uint32_t n_cols, const uint32_t* feature_offset,
                      const float* cut_values, uint64_t* row_ptr, uint32_t* row_bins,
@@ -427,6 +431,16 @@ hb_status hb_engine_upload_csr(hb_engine* e, const uint64_t* indptr, const uint3
  * container (container.rs:245 `xxh64`). The section table itself is laid
  * out by the Python host (model_io.to_native_binary). */
 hb_status hb_xxh64(const void* data, uint64_t len, uint64_t* out);
+
+/* ---- failure testing (no counterpart in the reference) -------------- */
+/* Arm a host-side fault: the engine's `after_calls`-th checked CUDA call
+ * from now on (0: the next one), counting only calls made outside stream
+ * capture, fails before it reaches CUDA, exactly as a device error would:
+ * that call returns HB_DEVICE_FAILED and the engine refuses every later
+ * call (the sticky state of src/backend/cuda/driver.rs:26-44), while the
+ * GPU and other engines are untouched. -1 disarms. For tests of the
+ * caller's fallback (src/tree/hist/mod.rs:209-212). */
+hb_status hb_engine_inject_fault(hb_engine* e, int32_t after_calls);
 
 /* ---- measurement (no counterpart in the reference) ------------------ */
 /* The shared-memory throughput a histogram update pattern reaches on GPU

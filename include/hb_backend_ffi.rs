@@ -9,6 +9,9 @@ pub const HB_OK: hb_status = 0;
 pub const HB_REFUSED: hb_status = 1;          // the trait's `None`
 pub const HB_DEVICE_FAILED: hb_status = 2;    // sticky: the engine refuses from now on
 pub const HB_INVALID_ARGUMENT: hb_status = 3;
+pub const HB_SCAN_EMPTY: u32 = 0;             // NodeScan kinds
+pub const HB_SCAN_REPLAY: u32 = 1;
+pub const HB_SCAN_NUMERIC: u32 = 2;
 
 #[repr(C)] pub struct hb_engine { _p: [u8; 0] }
 #[repr(C)] pub struct hb_predictor { _p: [u8; 0] }
@@ -154,4 +157,5 @@ extern "C" {
                                     d_out: *mut f32, stream: *mut c_void) -> hb_status;
     pub fn hb_probe_smem(device: i32, kind: i32, threads: i32, iters: i32,
                          lane_ops_per_clk: *mut f64) -> hb_status;
+    pub fn hb_engine_inject_fault(e: *mut hb_engine, after_calls: i32) -> hb_status;
 }

@@ -159,6 +159,16 @@ CASES = {
     "monotone_bins64": dict(gen=lambda: synth.regression_c1(30_011, 6, seed=25), rounds=4,
                             kw=dict(max_depth=5, max_bin=64, min_child_weight=0.0, reg_lambda=0.5,
                                     monotone_constraints=(-1, 1, 1, 0, 0, 1))),
+    # indexes the row records cannot hold: 300 features (the dense index
+    # converted to the CSR layout on upload) and features of up to 1024 bins
+    # (the CSR index, the chunked split scan), depthwise and lossguide
+    "wide_300": dict(gen=lambda: synth.logistic_c2(20_011, 300, seed=28), rounds=2,
+                     kw=dict(objective="binary:logistic", max_depth=5, eta=0.3)),
+    "bins_1024": dict(gen=lambda: synth.regression_c1(30_011, 8, seed=29), rounds=3,
+                      kw=dict(max_depth=6, max_bin=1024)),
+    "bins_1024_missing_lossguide": dict(gen=lambda: synth.logistic_c2(25_013, 6, seed=30, missing=0.1), rounds=3,
+                                        kw=dict(objective="binary:logistic", grow_policy="lossguide", max_depth=0,
+                                                max_leaves=20, max_bin=1024, eta=0.3)),
     "monotone_lossguide": dict(gen=lambda: synth.logistic_c2(20_011, 8, seed=26), rounds=3,
                                kw=dict(objective="binary:logistic", grow_policy="lossguide", max_depth=0,
                                        max_leaves=24, eta=0.3, monotone_constraints=(1, 1, -1, 0, 0, 0, 0, -1))),
