@@ -363,7 +363,13 @@ def run_c3(args):
     eng.train_rounds(params, min(args.steps, 5))
     bd = eng.stats()
     per_round = {k: v / max(bd["rounds"], 1) * 10 for k, v in bd["ms"].items()}  # 10 trees a round
+    # the first round's ten trees from the base margins, for the parity check
+    eng.train_begin_classes(y, base)
+    first_nodes, first_ptr = eng.train_rounds(params, 1)
     eng.close()
+    parity = None
+    if not args.no_parity:
+        parity = c3_parity(x, y, base, first_nodes, first_ptr)
     cpu = None
     if not args.no_cpu_baseline:
         sys.path.insert(0, os.path.join(ROOT, "tests"))
@@ -392,13 +398,46 @@ def run_c3(args):
                    "l2": f"inputs {'larger' if n * 128 > 126e6 else 'SMALLER'} than L2: "
                          f"{n:,} x 128 B records + 10 x {n * 8 / 1e6:,.0f} MB pairs per round"},
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
-                     "frac": achieved / peak, "traffic": None, "kernel": "k_hist32",
+                     "frac": achieved / peak, "traffic": None, "kernel": "k_hist32r",
                      "launches": hist_launches},
         "cpu_baseline": cpu,
+        "parity": parity,
         "e2e": None,
         "gpu_launches": int(st["kernel_launches"]),
         "clocks": clocks,
     })
+
+
+def c3_parity(x, y, base, nodes, ptr):
+    """The GPU's first C3 round (ten trees, one per class, from the class
+    intercepts) against the oracle's fixed-point mode on the same 2M x 100
+    matrix, under the north-star criteria (the device's softmax exp is CUDA's
+    double exp rounded once, the oracle's glibc expf, so not bit for bit):
+    trees, leaves and the margins after the round (GPU predictor on the
+    training rows)."""
+    import hessboost_b200 as H
+
+    sys.path.insert(0, os.path.join(ROOT, "tests"))
+    import oracle_lib as O
+    import parity as P
+
+    O.build()
+    t0 = time.perf_counter()
+    tr = O.Trainer(x, y, objective=2, n_outputs=10, max_depth=6, eta=0.2, max_bin=128, fixed_point=True)
+    on, op = tr.rounds(1)
+    om = tr.margins()
+    tr.close()
+    cmp = P.compare_forests(nodes, ptr, on, op)
+    bases = np.ascontiguousarray(base, np.float32)
+    pred = H.Predictor(nodes, ptr, bases, x.shape[1])
+    gm = pred.predict_margin(x)
+    pred.close()
+    ok, rel, exact = P.margins_ok(gm, om)
+    log(f"c3 parity: {time.perf_counter() - t0:.1f}s")
+    return dict(cmp, rows=int(x.shape[0]), rounds=1, margins_ok=ok, margin_max_rel=rel,
+                margin_bit_exact_frac=exact, pass_all=bool(cmp["pass"] and ok),
+                criteria="oracle fixed point, first round: structure equal except gain ties (1e-5), "
+                         "leaves rtol 1e-5 atol 1e-7, margins rtol 1e-6 atol 1e-7")
 
 
 C4_METRIC = "boost rounds/s (C4: 5M x 2,000 CSR at 2%, max_bin 64, lossguide 255 leaves)"

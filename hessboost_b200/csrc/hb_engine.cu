@@ -923,6 +923,9 @@ static hb_status upload_index(hb_engine* e, const hb_ghist* g, const RawSource* 
   const char* hk = std::getenv("HB_HIST_KERNEL");
   c.hist64 = (hk && std::strcmp(hk, "64") == 0) ? 1u : 0u;
   c.hist_staged = (hk && std::strcmp(hk, "staged") == 0) ? 1u : 0u;
+  // HB_L2_HINTS=0 drops the L2 eviction policies of the histogram loads
+  const char* lh = std::getenv("HB_L2_HINTS");
+  c.l2_hints = (lh && std::strcmp(lh, "0") == 0) ? 0u : 1u;
   // HB_SCAN_KERNEL=cta keeps the CTA-per-feature scan for every width.
   const char* sk = std::getenv("HB_SCAN_KERNEL");
   c.scan_cta = (sk && std::strcmp(sk, "cta") == 0) ? 1u : 0u;

@@ -73,6 +73,27 @@ __device__ __forceinline__ float2 ld_hint8(const float2* ptr, uint64_t pol) {
   return v;
 }
 
+// cp.async of 16 bytes (L1 bypassed) or 4 / 8 bytes into shared memory
+// with an L2 cache policy.
+__device__ __forceinline__ void cp_async16_hint(void* sdst, const void* gsrc, uint64_t pol) {
+  asm volatile("cp.async.cg.shared.global.L2::cache_hint [%0], [%1], 16, %2;" ::"r"(
+                   (uint32_t)__cvta_generic_to_shared(sdst)),
+               "l"(gsrc), "l"(pol)
+               : "memory");
+}
+template <int N>
+__device__ __forceinline__ void cp_async_small_hint(void* sdst, const void* gsrc, uint64_t pol) {
+  static_assert(N == 4 || N == 8, "cp.async.ca sizes");
+  asm volatile("cp.async.ca.shared.global.L2::cache_hint [%0], [%1], %2, %3;" ::"r"(
+                   (uint32_t)__cvta_generic_to_shared(sdst)),
+               "l"(gsrc), "n"(N), "l"(pol)
+               : "memory");
+}
+
+__device__ __forceinline__ void prefetch_l2(const void* ptr) {
+  asm volatile("prefetch.global.L2 [%0];" ::"l"(ptr));
+}
+
 __device__ __forceinline__ void st_hint8(float2* ptr, float2 v, uint64_t pol) {
   asm volatile("st.global.L2::cache_hint.v2.f32 [%0], {%1, %2}, %3;" ::"l"(ptr), "f"(v.x), "f"(v.y), "l"(pol)
                : "memory");
@@ -726,6 +747,10 @@ __global__ void __launch_bounds__(kH32Threads, 1)
   const bool want_totals = totals != nullptr && g0 == 0;
   const uint32_t lo_mask = (uint32_t)((1ull << lo_bits) - 1ull);
   long long tg = 0, th = 0;
+  // L2 policies of the staged copies: records evict-first (read once per
+  // launch), pairs evict-last (every launch of the round re-reads them)
+  const bool hints = c.l2_hints != 0;
+  const uint64_t pol_stream = l2_evict_first(), pol_keep = l2_evict_last();
 
   // Each thread owns kSlotsPerThread / 4 runs of four consecutive slots
   // (slot_of below), moved with 128-bit shared loads and stores.
@@ -785,13 +810,23 @@ __global__ void __launch_bounds__(kH32Threads, 1)
           if (lg < ng) {
             const uint8_t* rp = rr + 32 * (g0 + lg);
             StageRow* d = &srec[(st * G + lg) * kH32Threads + tid];
-            __pipeline_memcpy_async(&d->a, rp, 16);
-            if (wide[lg]) __pipeline_memcpy_async(&d->b, rp + 16, 16);
-            if (!mask_in_block[lg])
-              __pipeline_memcpy_async(&smask[(st * G + lg) * kH32Threads + tid], rr + mask_at[lg], 4);
+            if (hints) {
+              cp_async16_hint(&d->a, rp, pol_stream);
+              if (wide[lg]) cp_async16_hint(&d->b, rp + 16, pol_stream);
+              if (!mask_in_block[lg])
+                cp_async_small_hint<4>(&smask[(st * G + lg) * kH32Threads + tid], rr + mask_at[lg], pol_stream);
+            } else {
+              __pipeline_memcpy_async(&d->a, rp, 16);
+              if (wide[lg]) __pipeline_memcpy_async(&d->b, rp + 16, 16);
+              if (!mask_in_block[lg])
+                __pipeline_memcpy_async(&smask[(st * G + lg) * kH32Threads + tid], rr + mask_at[lg], 4);
+            }
           }
         }
-        __pipeline_memcpy_async(&sgp[st * kH32Threads + tid], &gpair[row], 8);
+        if (hints)
+          cp_async_small_hint<8>(&sgp[st * kH32Threads + tid], &gpair[row], pol_keep);
+        else
+          __pipeline_memcpy_async(&sgp[st * kH32Threads + tid], &gpair[row], 8);
       }
       __pipeline_commit();
     };
@@ -1112,6 +1147,14 @@ __global__ void __launch_bounds__(HR<G>::kThreads, 1)
     };
     for (int it = 0; it < n_it; ++it) {
       const uint64_t i = pos + (uint64_t)it * kT + tid;
+      // gathered rows: the record and pair of the row two passes ahead
+      // fetched into L2 now, so the load below waits on L2, not DRAM
+      const uint64_t ipf = i + 2 * (uint64_t)kT;
+      if (!en.identity && ipf < end_e) {
+        const uint32_t rowp = ld_hint4(rows + en.begin + (uint32_t)(ipf - en.prefix), pol_stream);
+        prefetch_l2(rec + (uint64_t)rowp * c.stride + 32 * g0);
+        prefetch_l2(gpair + rowp);
+      }
       if (i < end_e) {
         HRRow<G> cur;
         load(i, cur);

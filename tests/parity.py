@@ -133,3 +133,24 @@ def forced_f64_rounds(engine, params, trainer_f64, rounds):
             out["not_ties"].append({"round": r, "node": c["first_difference"], "gain_rel": c["gain_rel"]})
     out["pass"] = bool(out["leaf_ok"] and out["margins_ok"] and not out["not_ties"])
     return out
+
+
+def compare_forests(nodes, ptr, onodes, optr):
+    """Tree-by-tree north-star comparison of two forests grown from the same
+    margins (one round, or the first round of several): structure equal
+    except ties, leaf error before the first difference of each tree."""
+    out = {"trees": 0, "trees_structure_equal": 0, "ties": [], "not_ties": [], "leaf_ok": True,
+           "leaf_max_rel": 0.0}
+    for t, (g, o) in enumerate(zip(trees(nodes, ptr), trees(onodes, optr))):
+        c = compare_tree_f64(g, o)
+        out["trees"] += 1
+        out["leaf_ok"] &= c["leaf_ok"]
+        out["leaf_max_rel"] = max(out["leaf_max_rel"], c["leaf_max_rel"])
+        if c["structure_equal"]:
+            out["trees_structure_equal"] += 1
+        elif c["tie"]:
+            out["ties"].append({"tree": t, "node": c["first_difference"], "gain_rel": c["gain_rel"]})
+        else:
+            out["not_ties"].append({"tree": t, "node": c["first_difference"], "gain_rel": c["gain_rel"]})
+    out["pass"] = bool(out["leaf_ok"] and not out["not_ties"] and len(ptr) == len(optr))
+    return out
