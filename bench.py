@@ -408,6 +408,31 @@ def run_c3(args):
     })
 
 
+def c4_parity(indptr, indices, values, n_cols, y, nodes, ptr, margins):
+    """The GPU's first C4 round (one lossguide tree over the 5M x 2,000 CSR
+    index) against the oracle's fixed-point CSR trainer on the same matrix:
+    every node field and all training margins bit for bit."""
+    sys.path.insert(0, os.path.join(ROOT, "tests"))
+    import oracle_lib as O
+    import parity as P
+
+    O.build()
+    t0 = time.perf_counter()
+    tr = O.Trainer(None, y, csr=(indptr, indices, values, n_cols), objective=1, grow_policy=1,
+                   max_depth=0, max_leaves=255, max_bin=64, fixed_point=True)
+    on, op = tr.rounds(1)
+    om = tr.margins()[:, 0]
+    tr.close()
+    exact, where = P.forest_bit_exact(nodes, ptr, on, op)
+    m_exact = bool(np.array_equal(np.ascontiguousarray(margins, np.float32).view(np.uint32), om.view(np.uint32)))
+    log(f"c4 parity: {time.perf_counter() - t0:.1f}s")
+    return {"rows": int(len(y)), "rounds": 1, "fixed_point_bit_exact": bool(exact),
+            "fixed_point_first_difference": where or None, "fixed_point_margins_bit_exact": m_exact,
+            "pass": bool(exact and m_exact),
+            "criteria": "oracle fixed point (CSR index, lossguide), first round: every node field and "
+                        "margin bit for bit"}
+
+
 def c3_parity(x, y, base, nodes, ptr):
     """The GPU's first C3 round (ten trees, one per class, from the class
     intercepts) against the oracle's fixed-point mode on the same 2M x 100
@@ -492,7 +517,15 @@ def run_c4(args):
     eng.train_rounds(params, min(args.steps, 3))
     bd = eng.stats()
     per_round = {k: v / max(bd["rounds"], 1) for k, v in bd["ms"].items()}
+    # the first round from the base margin, for the parity check
+    base = H.base_margin(params, y)
+    eng.train_begin(y, base)
+    first_nodes, first_ptr = eng.train_rounds(params, 1)
+    first_margins = eng.read_margins()
     eng.close()
+    parity = None
+    if not args.no_parity:
+        parity = c4_parity(indptr, indices, values, f, y, first_nodes, first_ptr, first_margins)
     cpu = None
     if not args.no_cpu_baseline:
         sys.path.insert(0, os.path.join(ROOT, "tests"))
@@ -530,6 +563,7 @@ def run_c4(args):
                      "frac": achieved / peak, "traffic": None, "kernel": "k_hist_csr",
                      "launches": hist_launches},
         "cpu_baseline": cpu,
+        "parity": parity,
         "e2e": None,
         "gpu_launches": int(st["kernel_launches"]),
         "clocks": clocks,

@@ -11,6 +11,7 @@
 #include <cstdlib>
 #include <cstring>
 #include <string>
+#include <thread>
 #include <vector>
 
 #include "hb_engine_view.h"
@@ -154,10 +155,15 @@ struct hb_engine {
   // and the per-(node, feature) directions of a RowEngine scan
   DevBuf<int8_t> mono, scan_dirs;
   std::vector<int8_t> h_mono;
+  // RowEngine call buffers: leaf segments and values, partition end rows
+  DevBuf<uint2> seg_list;
+  DevBuf<float> seg_vals;
+  DevBuf<uint32_t> part_ends;
   // fault injection (hb_engine_inject_fault): checked calls left before the
   // one that fails (-1: none armed); no injection while a graph is captured
   int64_t fault_after = -1;
   bool capturing = false;
+  bool l2_window = false;  // the pairs' L2 access-policy window is set (HB_L2_PERSIST)
 };
 
 namespace {
@@ -656,6 +662,34 @@ hb_status check_params(hb_engine* e, const hb_train_params* p) {
   return stage_monotone(e, p);
 }
 
+// With HB_L2_PERSIST=1, the gradient pairs get an L2 access-policy window on
+// the engine's stream (persisting hits, a set-aside of at most the device's
+// maximum), so the round's gathered histogram launches read them from L2.
+// The set-aside is this process's context's; it ends with the context.
+hb_status keep_pairs_in_l2(hb_engine* e) {
+  const char* v = std::getenv("HB_L2_PERSIST");
+  if (!v || std::strcmp(v, "1") != 0 || e->l2_window) return HB_OK;
+  int max_persist = 0, max_window = 0;
+  HB_CK(e, cudaDeviceGetAttribute(&max_persist, cudaDevAttrMaxPersistingL2CacheSize, e->device));
+  HB_CK(e, cudaDeviceGetAttribute(&max_window, cudaDevAttrMaxAccessPolicyWindowSize, e->device));
+  const size_t want = sizeof(float2) * e->c.n_rows * (size_t)std::max(e->n_out, 1);
+  if (max_persist <= 0 || max_window <= 0 || want == 0) return HB_OK;
+  const size_t set_aside = std::min<size_t>(want, (size_t)max_persist);
+  HB_CK(e, cudaDeviceSetLimit(cudaLimitPersistingL2CacheSize, set_aside));
+  cudaStreamAttrValue a{};
+  a.accessPolicyWindow.base_ptr = e->gpair.p;
+  a.accessPolicyWindow.num_bytes = std::min<size_t>(want, (size_t)max_window);
+  a.accessPolicyWindow.hitRatio =
+      (float)std::min(1.0, (double)set_aside / (double)a.accessPolicyWindow.num_bytes);
+  a.accessPolicyWindow.hitProp = cudaAccessPropertyPersisting;
+  a.accessPolicyWindow.missProp = cudaAccessPropertyStreaming;
+  HB_CK(e, cudaStreamSetAttribute(e->stream, cudaStreamAttributeAccessPolicyWindow, &a));
+  e->l2_window = true;
+  std::fprintf(stderr, "hb: L2 window %zu of %zu pair bytes, set-aside %zu (max %d)\n",
+               (size_t)a.accessPolicyWindow.num_bytes, want, set_aside, max_persist);
+  return HB_OK;
+}
+
 // The run's monotone constraints on the device (before any capture): one
 // direction per feature, or none (c.mono = NULL) when every one is 0.
 hb_status stage_monotone(hb_engine* e, const hb_train_params* p) {
@@ -728,6 +762,11 @@ hb_status hb_engine_destroy(hb_engine* e) {
   if (!e) return HB_INVALID_ARGUMENT;
   cudaSetDevice(e->device);
   if (e->stream) cudaStreamSynchronize(e->stream);
+  // the pairs' persisting L2 lines back to normal and the set-aside released
+  if (e->l2_window) {
+    cudaCtxResetPersistingL2Cache();
+    cudaDeviceSetLimit(cudaLimitPersistingL2CacheSize, 0);
+  }
   // the round graph holds the level allreduces: release it before the communicator
   if (e->round_exec) cudaGraphExecDestroy(e->round_exec);
   e->round_exec = nullptr;
@@ -778,6 +817,9 @@ hb_status hb_engine_destroy(hb_engine* e) {
   e->flags.release();
   e->mono.release();
   e->scan_dirs.release();
+  e->seg_list.release();
+  e->seg_vals.release();
+  e->part_ends.release();
   if (e->stream) cudaStreamDestroy(e->stream);
   delete e;
   return HB_OK;
@@ -917,15 +959,13 @@ static hb_status upload_index(hb_engine* e, const hb_ghist* g, const RawSource* 
   c.stride = (c.mask_off + 4 * ((g->n_cols + 31) / 32) + 15) / 16 * 16;
   c.dense = g->dense ? 1 : 0;
   c.n_groups = (g->n_cols + kGroupFeatures - 1) / kGroupFeatures;
-  // Every histogram kernel gives the same exact sums; HB_HIST_KERNEL=64
-  // selects the 64-bit-atomic one for every size, =staged the cp.async-staged
-  // 32-bit one instead of k_hist32r (comparison runs).
+  // Both histogram kernels give the same exact sums; HB_HIST_KERNEL=64
+  // selects the 64-bit-atomic one for every size (comparison runs).
   const char* hk = std::getenv("HB_HIST_KERNEL");
   c.hist64 = (hk && std::strcmp(hk, "64") == 0) ? 1u : 0u;
-  c.hist_staged = (hk && std::strcmp(hk, "staged") == 0) ? 1u : 0u;
-  // HB_L2_HINTS=0 drops the L2 eviction policies of the histogram loads
+  // HB_L2_HINTS=1: evict-last prefetch of the pairs in the histogram kernel
   const char* lh = std::getenv("HB_L2_HINTS");
-  c.l2_hints = (lh && std::strcmp(lh, "0") == 0) ? 0u : 1u;
+  c.l2_hints = (lh && std::strcmp(lh, "1") == 0) ? 1u : 0u;
   // HB_SCAN_KERNEL=cta keeps the CTA-per-feature scan for every width.
   const char* sk = std::getenv("HB_SCAN_KERNEL");
   c.scan_cta = (sk && std::strcmp(sk, "cta") == 0) ? 1u : 0u;
@@ -1190,18 +1230,62 @@ static bool seg_ok(const hb_engine* e, const hb_segment* s) {
   return s && s->tree == e->tree_stamp && s->offset + s->len <= e->c.n_rows;
 }
 
+// check_rows (src/backend/cuda/mod.rs:817): every row inside the index,
+// strictly ascending, and whether the list is one contiguous run; chunks of
+// the list checked by the host's threads.
+static void check_rows(const uint32_t* rows, uint64_t n, uint64_t n_rows, bool& inside, bool& ascending,
+                       bool& run) {
+  inside = ascending = run = true;
+  if (!n) return;
+  const uint64_t chunk = 1 << 20;
+  const uint64_t n_chunks = (n + chunk - 1) / chunk;
+  std::vector<unsigned char> ok(3 * n_chunks, 1);
+  auto work = [&](uint64_t c0, uint64_t c1) {
+    for (uint64_t c = c0; c < c1; ++c) {
+      const uint64_t a = c * chunk, b = std::min(n, a + chunk);
+      bool in = true, asc = a == 0 || rows[a - 1] < rows[a], rn = true;
+      const uint32_t first = rows[0];
+      for (uint64_t i = a; i < b; ++i) {
+        in &= rows[i] < n_rows;
+        rn &= (uint64_t)rows[i] == (uint64_t)first + i;
+        if (i > a) asc &= rows[i - 1] < rows[i];
+      }
+      ok[3 * c] = in;
+      ok[3 * c + 1] = asc;
+      ok[3 * c + 2] = rn;
+    }
+  };
+  const unsigned hw = std::max(1u, std::min(16u, std::thread::hardware_concurrency()));
+  const uint64_t per = (n_chunks + hw - 1) / hw;
+  std::vector<std::thread> pool;
+  for (uint64_t c0 = per; c0 < n_chunks; c0 += per) pool.emplace_back(work, c0, std::min(n_chunks, c0 + per));
+  work(0, std::min(n_chunks, per));
+  for (auto& t : pool) t.join();
+  for (uint64_t c = 0; c < n_chunks; ++c) {
+    inside &= ok[3 * c] != 0;
+    ascending &= ok[3 * c + 1] != 0;
+    run &= ok[3 * c + 2] != 0;
+  }
+}
+
 hb_status hb_begin_tree(hb_engine* e, const uint32_t* rows, uint64_t n, hb_segment* root) {
   HB_ENTER(e);
   if (!e->uploaded) return refuse(e, "no index uploaded");
   if ((!rows && n) || !root || n > e->c.n_rows) return HB_INVALID_ARGUMENT;
-  for (uint64_t i = 0; i < n; ++i)
-    if (rows[i] >= e->c.n_rows || (i && rows[i] <= rows[i - 1])) return refuse(e, "rows must be ascending and distinct");
-  if (n) HB_CK(e, cudaMemcpyAsync(e->rows[0].p, rows, 4 * n, cudaMemcpyHostToDevice, e->stream));
+  bool inside, ascending, run;
+  check_rows(rows, n, e->c.n_rows, inside, ascending, run);
+  if (!inside || !ascending) return refuse(e, "rows must be ascending and distinct");
+  // a contiguous run is written on the device (place_rows, cuda/mod.rs:1830)
+  if (n && run)
+    launch_iota(e->rows[0].p, rows[0], n, e->n_sm, e->stream);
+  else if (n)
+    HB_CK(e, cudaMemcpyAsync(e->rows[0].p, rows, 4 * n, cudaMemcpyHostToDevice, e->stream));
+  HB_CK(e, cudaGetLastError());
   HB_CK(e, cudaStreamSynchronize(e->stream));
   ++e->tree_stamp;
   root->offset = 0;
   root->len = n;
-  root->contiguous = (n == 0 || (uint64_t)(rows[n - 1] - rows[0]) + 1 == n) ? 1 : 0;
+  root->contiguous = (n == 0 || run) ? 1 : 0;
   root->reserved = 0;
   root->tree = e->tree_stamp;
   return HB_OK;
@@ -1235,28 +1319,11 @@ hb_status hb_root_total(hb_engine* e, const hb_segment* seg, hb_grad_stats* out)
   HB_ENTER(e);
   if (!e->uploaded || !e->staged) return refuse(e, "no staged gradients");
   if (!seg_ok(e, seg) || !out) return HB_INVALID_ARGUMENT;
-  // The total is any feature's bins plus that feature's missing rows; the
-  // histogram kernel's totals path sums every row exactly.
-  std::vector<HEntry> en(1);
-  en[0].slot = 0;
-  en[0].identity = 0;
-  en[0].begin = (uint32_t)seg->offset;
-  en[0].len = (uint32_t)seg->len;
-  en[0].prefix = 0;
-  DevConst& c = e->c;
-  HB_CK(e, e->call_hist.alloc(c.total_bins));
-  HB_CK(e, e->entries.alloc(1));
-  HB_CK(e, e->ls.alloc(kMaxDepth + 2));
-  LevelState lsh{};
-  lsh.n_hentries = 1;
-  lsh.hist_rows = seg->len;
+  // The exact int64 sum of the segment's fixed-point pairs (the same
+  // integers the histograms sum, so any order).
   cudaStream_t s = e->stream;
-  HB_CK(e, cudaMemcpyAsync(e->entries.p, en.data(), sizeof(HEntry), cudaMemcpyHostToDevice, s));
-  HB_CK(e, cudaMemcpyAsync(e->ls.p, &lsh, sizeof(LevelState), cudaMemcpyHostToDevice, s));
-  HB_CK(e, cudaMemsetAsync(e->call_hist.p, 0, sizeof(longlong2) * c.total_bins, s));
   HB_CK(e, cudaMemsetAsync(e->seg_total.p, 0, 16, s));
-  launch_hist(c, e->fo.p, e->rec.p, e->gpair.p, e->scale.p, e->rows[0].p, e->entries.p, e->ls.p,
-              e->call_hist.p, e->seg_total.p, nullptr, hist_grid(e->n_sm), hist_smem_bytes(c), s);
+  launch_seg_total(e->rows[0].p, seg->offset, seg->len, e->gpair.p, e->scale.p, e->seg_total.p, e->n_sm, s);
   HB_CK(e, cudaGetLastError());
   long long t[2];
   Scale h;
@@ -1337,13 +1404,14 @@ hb_status hb_partition(hb_engine* e, const hb_row_split* splits, uint32_t n, hb_
                         e->item_off.p, e->front[1].p, e->rows[0].p, 0, e->rows[1].p, s);
   }
   HB_CK(e, cudaGetLastError());
-  for (uint32_t k = 0; k < n; ++k) {
-    if (fr[k].len)
-      HB_CK(e, cudaMemcpyAsync(e->rows[0].p + fr[k].begin, e->rows[1].p + fr[k].begin, 4ull * fr[k].len,
-                               cudaMemcpyDeviceToDevice, s));
-  }
+  // the children back in rows[0] and their end rows, one launch
+  HB_CK(e, e->part_ends.alloc(4 * (size_t)n));
+  launch_finish_partition(e->front[0].p, e->front[1].p, n, e->rows[1].p, e->rows[0].p, e->part_ends.p, s);
+  HB_CK(e, cudaGetLastError());
   std::vector<Front> nx(2 * (size_t)n);
+  std::vector<uint32_t> ends(4 * (size_t)n);
   HB_CK(e, cudaMemcpyAsync(nx.data(), e->front[1].p, sizeof(Front) * 2 * n, cudaMemcpyDeviceToHost, s));
+  HB_CK(e, cudaMemcpyAsync(ends.data(), e->part_ends.p, 4 * ends.size(), cudaMemcpyDeviceToHost, s));
   HB_CK(e, cudaStreamSynchronize(s));
   for (uint32_t k = 0; k < n; ++k) {
     for (int side = 0; side < 2; ++side) {
@@ -1353,15 +1421,8 @@ hb_status hb_partition(hb_engine* e, const hb_row_split* splits, uint32_t n, hb_
       sg.len = f.len;
       sg.tree = e->tree_stamp;
       sg.reserved = 0;
-      sg.contiguous = 0;
-      if (f.len) {
-        uint32_t ends[2];
-        HB_CK(e, cudaMemcpy(&ends[0], e->rows[0].p + f.begin, 4, cudaMemcpyDeviceToHost));
-        HB_CK(e, cudaMemcpy(&ends[1], e->rows[0].p + f.begin + f.len - 1, 4, cudaMemcpyDeviceToHost));
-        sg.contiguous = (uint64_t)(ends[1] - ends[0]) + 1 == f.len ? 1 : 0;
-      } else {
-        sg.contiguous = 1;
-      }
+      const uint32_t lo = ends[4 * k + 2 * side], hi = ends[4 * k + 2 * side + 1];
+      sg.contiguous = f.len == 0 || (uint64_t)(hi - lo) + 1 == f.len ? 1 : 0;
     }
   }
   return HB_OK;
@@ -1441,13 +1502,18 @@ hb_status hb_add_leaf_values(hb_engine* e, const hb_segment* segs, const float* 
   if (!e->margins_loaded) return refuse(e, "no margin run");
   for (uint32_t k = 0; k < n; ++k)
     if (!seg_ok(e, &segs[k])) return refuse(e, "stale or foreign segment");
-  for (uint32_t k = 0; k < n; ++k) {
-    if (segs[k].len)
-      launch_add_segment(e->rows[0].p, (uint32_t)segs[k].offset, (uint32_t)segs[k].len, values[k],
-                         e->margin.p, e->stream);
-  }
+  if (!n) return HB_OK;
+  if (!values) return HB_INVALID_ARGUMENT;
+  std::vector<uint2> sl(n);
+  for (uint32_t k = 0; k < n; ++k) sl[k] = make_uint2((uint32_t)segs[k].offset, (uint32_t)segs[k].len);
+  cudaStream_t s = e->stream;
+  HB_CK(e, e->seg_list.alloc(n));
+  HB_CK(e, e->seg_vals.alloc(n));
+  HB_CK(e, cudaMemcpyAsync(e->seg_list.p, sl.data(), sizeof(uint2) * n, cudaMemcpyHostToDevice, s));
+  HB_CK(e, cudaMemcpyAsync(e->seg_vals.p, values, sizeof(float) * n, cudaMemcpyHostToDevice, s));
+  launch_add_segments(e->rows[0].p, e->seg_list.p, e->seg_vals.p, n, e->margin.p, s);
   HB_CK(e, cudaGetLastError());
-  HB_CK(e, cudaStreamSynchronize(e->stream));
+  HB_CK(e, cudaStreamSynchronize(s));
   return HB_OK;
 }
 
@@ -1860,6 +1926,8 @@ hb_status hb_train_rounds(hb_engine* e, const hb_train_params* p, int32_t rounds
   const int trees = rounds * e->n_out;  // one tree per class and round
   HB_CK(e, e->forest.alloc(std::max<size_t>((size_t)trees * max_nodes, 1)));
   HB_CK(e, e->counts.alloc(std::max(trees, 1)));
+  st = keep_pairs_in_l2(e);
+  if (st != HB_OK) return st;
   HB_CK(e, cudaMemsetAsync(e->tree_counter.p, 0, 4, s));
   if (e->use_graphs && rounds > 0) {
     st = ensure_buffers(e, p);

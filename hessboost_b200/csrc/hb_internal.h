@@ -58,8 +58,7 @@ struct DevConst {
   uint32_t dense;         // index-level: no missing cell anywhere
   uint32_t n_groups;      // feature groups of kGroupFeatures
   uint32_t hist64;        // 1: always the 64-bit-atomic histogram kernel
-  uint32_t hist_staged;   // 1: the cp.async-staged 32-bit kernel instead of k_hist32r
-  uint32_t l2_hints;      // 1: histogram loads carry L2 eviction policies
+  uint32_t l2_hints;      // 1: the histogram kernel prefetches each pair's line evict-last
   uint32_t scan_cta;      // 1: always the CTA-per-feature split scan
   // CSR index (csr = 1): each row's global bins ascending, absent = missing;
   // fo = the device copy of feature_offset (both layouts)

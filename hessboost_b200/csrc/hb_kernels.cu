@@ -40,58 +40,18 @@ __device__ __forceinline__ uint32_t pick_word(const uint4& a, const uint4& b, in
 }
 
 
-// L2 cache policies (createpolicy) and loads/stores that carry them: data
-// read once streams through L2 evict-first; the (g, h) pairs, re-read by
-// every histogram launch of a round, stay evict-last.
-__device__ __forceinline__ uint64_t l2_evict_first() {
-  uint64_t p;
-  asm("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(p));
-  return p;
-}
+// L2 eviction priority of the (g, h) pairs: every histogram launch of a
+// round gathers them again, so they are written, and may be prefetched,
+// evict-last.
 __device__ __forceinline__ uint64_t l2_evict_last() {
   uint64_t p;
   asm("createpolicy.fractional.L2::evict_last.b64 %0, 1.0;" : "=l"(p));
   return p;
 }
-__device__ __forceinline__ uint4 ld_hint16(const void* ptr, uint64_t pol) {
-  uint4 v;
-  asm("ld.global.nc.L1::no_allocate.L2::cache_hint.v4.u32 {%0, %1, %2, %3}, [%4], %5;"
-      : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
-      : "l"(ptr), "l"(pol));
-  return v;
-}
-__device__ __forceinline__ uint32_t ld_hint4(const void* ptr, uint64_t pol) {
-  uint32_t v;
-  asm("ld.global.nc.L1::no_allocate.L2::cache_hint.u32 %0, [%1], %2;" : "=r"(v) : "l"(ptr), "l"(pol));
-  return v;
-}
-__device__ __forceinline__ float2 ld_hint8(const float2* ptr, uint64_t pol) {
-  float2 v;
-  asm("ld.global.nc.L1::no_allocate.L2::cache_hint.v2.f32 {%0, %1}, [%2], %3;"
-      : "=f"(v.x), "=f"(v.y)
-      : "l"(ptr), "l"(pol));
-  return v;
-}
 
-// cp.async of 16 bytes (L1 bypassed) or 4 / 8 bytes into shared memory
-// with an L2 cache policy.
-__device__ __forceinline__ void cp_async16_hint(void* sdst, const void* gsrc, uint64_t pol) {
-  asm volatile("cp.async.cg.shared.global.L2::cache_hint [%0], [%1], 16, %2;" ::"r"(
-                   (uint32_t)__cvta_generic_to_shared(sdst)),
-               "l"(gsrc), "l"(pol)
-               : "memory");
-}
-template <int N>
-__device__ __forceinline__ void cp_async_small_hint(void* sdst, const void* gsrc, uint64_t pol) {
-  static_assert(N == 4 || N == 8, "cp.async.ca sizes");
-  asm volatile("cp.async.ca.shared.global.L2::cache_hint [%0], [%1], %2, %3;" ::"r"(
-                   (uint32_t)__cvta_generic_to_shared(sdst)),
-               "l"(gsrc), "n"(N), "l"(pol)
-               : "memory");
-}
-
-__device__ __forceinline__ void prefetch_l2(const void* ptr) {
-  asm volatile("prefetch.global.L2 [%0];" ::"l"(ptr));
+// The line holding `ptr` fetched into L2 ahead of use, marked evict-last.
+__device__ __forceinline__ void prefetch_l2_keep(const void* ptr) {
+  asm volatile("prefetch.global.L2::evict_last [%0];" ::"l"(ptr));
 }
 
 __device__ __forceinline__ void st_hint8(float2* ptr, float2 v, uint64_t pol) {
@@ -747,10 +707,7 @@ __global__ void __launch_bounds__(kH32Threads, 1)
   const bool want_totals = totals != nullptr && g0 == 0;
   const uint32_t lo_mask = (uint32_t)((1ull << lo_bits) - 1ull);
   long long tg = 0, th = 0;
-  // L2 policies of the staged copies: records evict-first (read once per
-  // launch), pairs evict-last (every launch of the round re-reads them)
-  const bool hints = c.l2_hints != 0;
-  const uint64_t pol_stream = l2_evict_first(), pol_keep = l2_evict_last();
+  const bool keep_pairs = c.l2_hints != 0;
 
   // Each thread owns kSlotsPerThread / 4 runs of four consecutive slots
   // (slot_of below), moved with 128-bit shared loads and stores.
@@ -810,23 +767,16 @@ __global__ void __launch_bounds__(kH32Threads, 1)
           if (lg < ng) {
             const uint8_t* rp = rr + 32 * (g0 + lg);
             StageRow* d = &srec[(st * G + lg) * kH32Threads + tid];
-            if (hints) {
-              cp_async16_hint(&d->a, rp, pol_stream);
-              if (wide[lg]) cp_async16_hint(&d->b, rp + 16, pol_stream);
-              if (!mask_in_block[lg])
-                cp_async_small_hint<4>(&smask[(st * G + lg) * kH32Threads + tid], rr + mask_at[lg], pol_stream);
-            } else {
-              __pipeline_memcpy_async(&d->a, rp, 16);
-              if (wide[lg]) __pipeline_memcpy_async(&d->b, rp + 16, 16);
-              if (!mask_in_block[lg])
-                __pipeline_memcpy_async(&smask[(st * G + lg) * kH32Threads + tid], rr + mask_at[lg], 4);
-            }
+            __pipeline_memcpy_async(&d->a, rp, 16);
+            if (wide[lg]) __pipeline_memcpy_async(&d->b, rp + 16, 16);
+            if (!mask_in_block[lg])
+              __pipeline_memcpy_async(&smask[(st * G + lg) * kH32Threads + tid], rr + mask_at[lg], 4);
           }
         }
-        if (hints)
-          cp_async_small_hint<8>(&sgp[st * kH32Threads + tid], &gpair[row], pol_keep);
-        else
-          __pipeline_memcpy_async(&sgp[st * kH32Threads + tid], &gpair[row], 8);
+        // the pair's line kept in L2 (evict-last) for the round's later
+        // launches, which gather the same pairs again
+        if (keep_pairs) prefetch_l2_keep(&gpair[row]);
+        __pipeline_memcpy_async(&sgp[st * kH32Threads + tid], &gpair[row], 8);
       }
       __pipeline_commit();
     };
@@ -964,262 +914,6 @@ __global__ void __launch_bounds__(kH32Threads, 1)
   }
   if (want_totals) {
     using BR = cub::BlockReduce<long long, kH32Threads>;
-    __shared__ typename BR::TempStorage tmp;
-    long long sgt = BR(tmp).Sum(tg);
-    __syncthreads();
-    long long sht = BR(tmp).Sum(th);
-    if (tid == 0) {
-      atomicAdd(reinterpret_cast<unsigned long long*>(&totals[0]), (unsigned long long)sgt);
-      atomicAdd(reinterpret_cast<unsigned long long*>(&totals[1]), (unsigned long long)sht);
-    }
-  }
-}
-
-// The split-accumulator histogram without shared-memory staging: each
-// thread loads its row (row id, record bytes, mask, (g, h) pair) straight
-// into registers, the 32 warps of the CTA hiding one another's load latency
-// behind their shared-memory atomics, with L2 eviction hints (records and
-// row ids streamed evict-first, the pairs evict-last, so the level
-// launches' random gathers of the pairs hit L2). The four 32-bit arrays are
-// the accumulators themselves: with every sum within 2^53 (kFixedTop) the
-// spill interval R is at least 2^14 rows at a million rows or more, so the
-// CTA adds its partial sums to the node histogram only at the end of an
-// entry or every R rows, and holds no register copy of them. One CTA of
-// kHRThreads threads per SM (G = 1), half that for two groups a CTA.
-template <int G>
-struct HR {
-  static constexpr int kThreads = G == 1 ? 1024 : 512;
-  static constexpr int kSlots = kNSlots / kThreads;  // slots a thread stages at a flush
-  static constexpr int kBinShift = G == 1 ? 8 : 7;
-  static constexpr size_t smem() { return (size_t)kSlotStride * 16; }
-};
-
-template <int G>
-struct HRRow {
-  uint4 a[G], b[G];
-  uint32_t m[G];
-  float2 p;
-};
-
-template <int G>
-__global__ void __launch_bounds__(HR<G>::kThreads, 1)
-    k_hist32r(DevConst c, const uint32_t* __restrict__ fo, const uint8_t* __restrict__ rec,
-              const float2* __restrict__ gpair, const Scale* __restrict__ scale,
-              const uint32_t* __restrict__ rows, const HEntry* __restrict__ entries,
-              const LevelState* __restrict__ ls, longlong2* __restrict__ hist,
-              long long* __restrict__ totals, unsigned long long* __restrict__ row_stats, int lo_bits,
-              int flush_rows) {
-  constexpr int kT = HR<G>::kThreads;
-  constexpr int kS = HR<G>::kSlots;
-  constexpr int kBS = HR<G>::kBinShift;
-  extern __shared__ __align__(16) uint32_t s32[];
-  const int n_entries = ls->n_hentries;
-  const uint64_t total = ls->hist_rows;
-  if (n_entries <= 0 || total == 0) return;
-  if (row_stats && blockIdx.x == 0 && blockIdx.y == 0 && threadIdx.x == 0)
-    atomicAdd(&row_stats[entries[0].identity ? 0 : 1], (unsigned long long)total);
-  const uint64_t per = (total + gridDim.x - 1) / gridDim.x;
-  const uint64_t a0 = (uint64_t)blockIdx.x * per;
-  const uint64_t b0 = min(total, a0 + per);
-  if (a0 >= b0) return;
-
-  const int g0 = blockIdx.y * G;
-  const int ng = min(G, (int)c.n_groups - g0);
-  uint32_t* lo_g = s32;
-  uint32_t* hi_g = s32 + kSlotStride;
-  uint32_t* lo_h = s32 + 2 * kSlotStride;
-  uint32_t* hi_h = s32 + 3 * kSlotStride;
-  {
-    uint4* z = reinterpret_cast<uint4*>(s32);
-    for (int i = threadIdx.x; i < kSlotStride; i += kT) z[i] = make_uint4(0u, 0u, 0u, 0u);
-  }
-  __syncthreads();
-
-  const uint64_t pol_stream = l2_evict_first(), pol_keep = l2_evict_last();
-  const double fg = scale->fg, fh = scale->fh;
-  const int tid = threadIdx.x;
-  const int lane = tid & 31;
-  const uint32_t lane4 = (uint32_t)lane << 2;
-  const uint32_t sbase = (uint32_t)__cvta_generic_to_shared(s32);
-  bool wide[G], mask_in_block[G];
-  uint32_t mask_at[G], dummy[G];
-  int mask_word[G];
-#pragma unroll
-  for (int lg = 0; lg < G; ++lg) {
-    const int g = g0 + lg;
-    const int nfg = lg < ng ? min(kGroupFeatures, (int)c.n_cols - g * kGroupFeatures) : 0;
-    wide[lg] = c.stride >= (uint32_t)(32 * g + 32);
-    mask_at[lg] = c.mask_off + 4 * g;
-    mask_in_block[lg] = mask_at[lg] >= (uint32_t)(32 * g) &&
-                        mask_at[lg] + 4 <= (uint32_t)(32 * g + (wide[lg] ? 32 : 16));
-    mask_word[lg] = (int)(mask_at[lg] - 32 * (uint32_t)g) >> 2;
-    dummy[lg] = nfg >= 32 ? 0u : (0xffffffffu << nfg);
-  }
-  const bool want_totals = totals != nullptr && g0 == 0;
-  const uint32_t lo_mask = (uint32_t)((1ull << lo_bits) - 1ull);
-  long long tg = 0, th = 0;
-
-  // The CTA's partial sums so far into the node histogram `slot`, and the
-  // accumulators back to zero: each thread combines its kS slots (runs of
-  // four consecutive words) into int64, stages them feature-major in the
-  // same shared memory (bins XOR-swizzled against bank conflicts), then
-  // each warp adds one feature's (g, h) words with contiguous 64-bit reds.
-  auto flush = [&](int slot) {
-    __syncthreads();
-    long long vg[kS], vh[kS];
-#pragma unroll
-    for (int j = 0; j < kS / 4; ++j) {
-      const int base = 4 * (tid + j * kT);
-      const uint4 a = *reinterpret_cast<const uint4*>(&lo_g[base]);
-      const uint4 b = *reinterpret_cast<const uint4*>(&hi_g[base]);
-      const uint4 p = *reinterpret_cast<const uint4*>(&lo_h[base]);
-      const uint4 q = *reinterpret_cast<const uint4*>(&hi_h[base]);
-      vg[4 * j + 0] = ((long long)(int)b.x << lo_bits) + (long long)a.x;
-      vg[4 * j + 1] = ((long long)(int)b.y << lo_bits) + (long long)a.y;
-      vg[4 * j + 2] = ((long long)(int)b.z << lo_bits) + (long long)a.z;
-      vg[4 * j + 3] = ((long long)(int)b.w << lo_bits) + (long long)a.w;
-      vh[4 * j + 0] = ((long long)(int)q.x << lo_bits) + (long long)p.x;
-      vh[4 * j + 1] = ((long long)(int)q.y << lo_bits) + (long long)p.y;
-      vh[4 * j + 2] = ((long long)(int)q.z << lo_bits) + (long long)p.z;
-      vh[4 * j + 3] = ((long long)(int)q.w << lo_bits) + (long long)p.w;
-    }
-    __syncthreads();
-    constexpr int kNB = 1 << kBS;
-    long long* stg = reinterpret_cast<long long*>(s32);
-#pragma unroll
-    for (int j = 0; j < kS; ++j) {
-      const int sl = 4 * (tid + (j >> 2) * kT) + (j & 3);
-      const int row = ((sl >> (kBS + 5)) << 5) | (sl & 31);
-      const int bin = (sl >> 5) & (kNB - 1);
-      const int at = 2 * (row * kNB + (bin ^ ((row >> 2) & 7)));
-      stg[at] = vg[j];
-      stg[at + 1] = vh[j];
-    }
-    __syncthreads();
-    unsigned long long* dstw = reinterpret_cast<unsigned long long*>(hist + (uint64_t)slot * c.total_bins);
-    const int warp = tid >> 5;
-    for (int row = warp; row < G * 32; row += kT / 32) {
-      const int lgs = row >> 5;
-      const int f = (g0 + lgs) * kGroupFeatures + (row & 31);
-      if (lgs >= ng || f >= (int)c.n_cols) continue;
-      const uint32_t fs = fo[f];
-      const uint32_t nw = 2 * (fo[f + 1] - fs);
-      for (uint32_t w = lane; w < nw; w += 32) {
-        const int bin = (int)(w >> 1);
-        const long long v = stg[2 * (row * kNB + (bin ^ ((row >> 2) & 7))) + (w & 1)];
-        if (v) atomicAdd(dstw + 2 * (uint64_t)fs + w, (unsigned long long)v);
-      }
-    }
-    __syncthreads();
-    uint4* z = reinterpret_cast<uint4*>(s32);
-    for (int i = tid; i < kSlotStride; i += kT) z[i] = make_uint4(0u, 0u, 0u, 0u);
-    __syncthreads();
-  };
-
-  int e = 0;
-  {
-    int hi = n_entries - 1;
-    while (e < hi) {
-      const int mid = (e + hi + 1) >> 1;
-      if (entries[mid].prefix <= a0) e = mid; else hi = mid - 1;
-    }
-  }
-  uint64_t pos = a0;
-  int since = 0;
-  while (pos < b0 && e < n_entries) {
-    const HEntry en = entries[e];
-    const uint64_t end_e = min(b0, en.prefix + en.len);
-    const int n_it = (int)((end_e - pos + kT - 1) / kT);
-    auto load = [&](uint64_t i, HRRow<G>& r) {
-      const uint32_t at = en.begin + (uint32_t)(i - en.prefix);
-      const uint32_t row = en.identity ? at : ld_hint4(rows + at, pol_stream);
-      const uint8_t* rr = rec + (uint64_t)row * c.stride;
-#pragma unroll
-      for (int lg = 0; lg < G; ++lg) {
-        if (lg < ng) {
-          const uint8_t* rp = rr + 32 * (g0 + lg);
-          r.a[lg] = ld_hint16(rp, pol_stream);
-          r.b[lg] = wide[lg] ? ld_hint16(rp + 16, pol_stream) : make_uint4(0u, 0u, 0u, 0u);
-          r.m[lg] = mask_in_block[lg] ? 0u : ld_hint4(rr + mask_at[lg], pol_stream);
-        }
-      }
-      r.p = ld_hint8(gpair + row, pol_keep);
-    };
-    for (int it = 0; it < n_it; ++it) {
-      const uint64_t i = pos + (uint64_t)it * kT + tid;
-      // gathered rows: the record and pair of the row two passes ahead
-      // fetched into L2 now, so the load below waits on L2, not DRAM
-      const uint64_t ipf = i + 2 * (uint64_t)kT;
-      if (!en.identity && ipf < end_e) {
-        const uint32_t rowp = ld_hint4(rows + en.begin + (uint32_t)(ipf - en.prefix), pol_stream);
-        prefetch_l2(rec + (uint64_t)rowp * c.stride + 32 * g0);
-        prefetch_l2(gpair + rowp);
-      }
-      if (i < end_e) {
-        HRRow<G> cur;
-        load(i, cur);
-        const long long qg = __double2ll_rn((double)cur.p.x * fg);
-        const long long qh = __double2ll_rn((double)cur.p.y * fh);
-        if (want_totals) {
-          tg += qg;
-          th += qh;
-        }
-        const uint32_t lg_ = (uint32_t)qg & lo_mask, lh = (uint32_t)qh & lo_mask;
-        const uint32_t hg = (uint32_t)(qg >> lo_bits), hh = (uint32_t)(qh >> lo_bits);
-#pragma unroll
-        for (int lg = 0; lg < G; ++lg) {
-          if (lg >= ng) break;
-          const uint4 v1 = cur.b[lg];
-          uint32_t mask = mask_in_block[lg] ? pick_word(cur.a[lg], v1, mask_word[lg]) : cur.m[lg];
-          mask |= dummy[lg];
-          // the 32 record bytes rotated right by `lane` bytes (word rotation
-          // by lane / 4 in three select stages, then a byte funnel shift):
-          // step s reads byte s, the lane's feature (lane + s) mod 32
-          uint32_t w[8] = {cur.a[lg].x, cur.a[lg].y, cur.a[lg].z, cur.a[lg].w, v1.x, v1.y, v1.z, v1.w};
-          const int q = lane >> 2;
-          uint32_t t[8];
-#pragma unroll
-          for (int j = 0; j < 8; ++j) t[j] = (q & 4) ? w[(j + 4) & 7] : w[j];
-#pragma unroll
-          for (int j = 0; j < 8; ++j) w[j] = (q & 2) ? t[(j + 2) & 7] : t[j];
-#pragma unroll
-          for (int j = 0; j < 8; ++j) t[j] = (q & 1) ? w[(j + 1) & 7] : w[j];
-          const int sh = (lane & 3) * 8;
-#pragma unroll
-          for (int j = 0; j < 8; ++j) w[j] = __funnelshift_r(t[j], t[(j + 1) & 7], sh);
-          const uint32_t mrot = __funnelshift_r(mask, mask, lane);
-          const uint32_t grow = (uint32_t)lg << (kBS + 7);
-#pragma unroll
-          for (int st = 0; st < 32; ++st) {
-            const uint32_t word = w[st >> 2];
-            const int k = st & 3;
-            const uint32_t binx = (k == 0 ? (word << 7) : (word >> (8 * k - 7))) & (((1u << kBS) - 1u) << 7);
-            const uint32_t rowx = ((mrot >> st) & 1u) ? (uint32_t)(kTrashBin << 7) : (binx | grow);
-            const uint32_t ad = sbase + (rowx | ((lane4 + 4u * (uint32_t)st) & 124u));
-            asm volatile(
-                "red.shared.add.u32 [%0], %1;\n\t"
-                "red.shared.add.u32 [%0+%5], %2;\n\t"
-                "red.shared.add.u32 [%0+%6], %3;\n\t"
-                "red.shared.add.u32 [%0+%7], %4;" ::"r"(ad),
-                "r"(lg_), "r"(hg), "r"(lh), "r"(hh), "n"(kSlotStride * 4), "n"(kSlotStride * 8),
-                "n"(kSlotStride * 12)
-                : "memory");
-          }
-        }
-      }
-      since += kT;
-      if (since + kT > flush_rows && it + 1 < n_it) {  // the next pass could pass R rows
-        flush(en.slot);
-        since = 0;
-      }
-    }
-    flush(en.slot);
-    since = 0;
-    pos = end_e;
-    ++e;
-  }
-  if (want_totals) {
-    using BR = cub::BlockReduce<long long, kT>;
     __shared__ typename BR::TempStorage tmp;
     long long sgt = BR(tmp).Sum(tg);
     __syncthreads();
@@ -2711,7 +2405,89 @@ __global__ void k_add_segment(const uint32_t* __restrict__ rows, uint32_t begin,
   }
 }
 
+// RowEngine helpers (one launch each, in place of per-segment work on the
+// host):
+// rows[i] = first + i: the row list of a contiguous run, built on the device
+// instead of copied from the host.
+__global__ void k_iota(uint32_t* __restrict__ rows, uint32_t first, uint64_t n) {
+  for (uint64_t i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (uint64_t)gridDim.x * blockDim.x)
+    rows[i] = first + (uint32_t)i;
+}
+
+// Each segment (offset, len) gets its value added to the margins of its
+// rows: one CTA per segment, a grid-stride loop inside.
+__global__ void k_add_segments(const uint32_t* __restrict__ rows, const uint2* __restrict__ segs,
+                               const float* __restrict__ values, float* __restrict__ margin) {
+  const uint2 sg = segs[blockIdx.x];
+  const float v = values[blockIdx.x];
+  for (uint32_t i = threadIdx.x; i < sg.y; i += blockDim.x) {
+    const uint32_t r = rows[sg.x + i];
+    margin[r] = __fadd_rn(margin[r], v);
+  }
+}
+
+// A partition's last step: every split k's segment of the parent, which the
+// scatter wrote to rows_out, copied back to rows_in (where the children's
+// segments then live), and each child's first and last row id into
+// ends[4k .. 4k + 3] (the host tells contiguous segments from them).
+__global__ void k_finish_partition(const Front* __restrict__ parents, const Front* __restrict__ kids,
+                                   const uint32_t* __restrict__ rows_out, uint32_t* __restrict__ rows_in,
+                                   uint32_t* __restrict__ ends) {
+  const int k = blockIdx.x;
+  const Front p = parents[k];
+  for (uint32_t i = threadIdx.x; i < p.len; i += blockDim.x) rows_in[p.begin + i] = rows_out[p.begin + i];
+  if (threadIdx.x < 2) {
+    const Front f = kids[2 * k + threadIdx.x];
+    ends[4 * k + 2 * threadIdx.x] = f.len ? rows_out[f.begin] : 0u;
+    ends[4 * k + 2 * threadIdx.x + 1] = f.len ? rows_out[f.begin + f.len - 1] : 0u;
+  }
+}
+
+// The fixed-point totals of a segment's rows (exact int64 sums, the order
+// free): per-CTA sums added atomically into totals[0..1].
+__global__ void k_seg_total(const uint32_t* __restrict__ rows, uint64_t begin, uint64_t len,
+                            const float2* __restrict__ gpair, const Scale* __restrict__ scale,
+                            long long* __restrict__ totals) {
+  const double fg = scale->fg, fh = scale->fh;
+  long long tg = 0, th = 0;
+  for (uint64_t i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; i < len; i += (uint64_t)gridDim.x * blockDim.x) {
+    const float2 p = gpair[rows[begin + i]];
+    tg += __double2ll_rn((double)p.x * fg);
+    th += __double2ll_rn((double)p.y * fh);
+  }
+  using BR = cub::BlockReduce<long long, 256>;
+  __shared__ typename BR::TempStorage tmp;
+  const long long sg = BR(tmp).Sum(tg);
+  __syncthreads();
+  const long long sh = BR(tmp).Sum(th);
+  if (threadIdx.x == 0) {
+    atomicAdd(reinterpret_cast<unsigned long long*>(&totals[0]), (unsigned long long)sg);
+    atomicAdd(reinterpret_cast<unsigned long long*>(&totals[1]), (unsigned long long)sh);
+  }
+}
+
 }  // namespace
+
+void launch_iota(uint32_t* rows, uint32_t first, uint64_t n, int n_sm, cudaStream_t s) {
+  const int grid = (int)std::max<uint64_t>(1, std::min<uint64_t>((n + 255) / 256, (uint64_t)n_sm * 8));
+  k_iota<<<grid, 256, 0, s>>>(rows, first, n);
+}
+
+void launch_add_segments(const uint32_t* rows, const uint2* segs, const float* values, uint32_t n,
+                         float* margin, cudaStream_t s) {
+  if (n) k_add_segments<<<n, 256, 0, s>>>(rows, segs, values, margin);
+}
+
+void launch_finish_partition(const Front* parents, const Front* kids, uint32_t n, const uint32_t* rows_out,
+                             uint32_t* rows_in, uint32_t* ends, cudaStream_t s) {
+  if (n) k_finish_partition<<<n, 256, 0, s>>>(parents, kids, rows_out, rows_in, ends);
+}
+
+void launch_seg_total(const uint32_t* rows, uint64_t begin, uint64_t len, const float2* gpair,
+                      const Scale* scale, long long* totals, int n_sm, cudaStream_t s) {
+  const int grid = (int)std::max<uint64_t>(1, std::min<uint64_t>((len + 255) / 256, (uint64_t)n_sm * 4));
+  k_seg_total<<<grid, 256, 0, s>>>(rows, begin, len, gpair, scale, totals);
+}
 
 // ---------------------------------------------------------------------------
 // Launchers.
@@ -2809,10 +2585,7 @@ static int hist_groups_per_cta(const DevConst& c) {
 
 size_t hist_smem_bytes(const DevConst& c) {
   if (c.csr) return 0;
-  if (use_hist32(c)) {
-    const size_t staged = hist_groups_per_cta(c) == 2 ? H32<2>::smem() : H32<1>::smem();
-    return std::max(staged, HR<1>::smem());
-  }
+  if (use_hist32(c)) return hist_groups_per_cta(c) == 2 ? H32<2>::smem() : H32<1>::smem();
   return (size_t)c.max_bins * 32 * 16;
 }
 
@@ -2851,22 +2624,6 @@ void launch_hist(const DevConst& c, const uint32_t* fo, const uint8_t* rec, cons
     int K, R;
     split_for_rows(c.global_rows, K, R);
     grid.y = (c.n_groups + G - 1) / G;
-    if (!c.hist_staged) {
-      static size_t granted_r[2][64] = {{0}};
-      if (dev < 0 || dev >= 64 || granted_r[G - 1][dev] < smem) {
-        if (cudaFuncSetAttribute(G == 2 ? (const void*)k_hist32r<2> : (const void*)k_hist32r<1>,
-                                 cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) == cudaSuccess &&
-            dev >= 0 && dev < 64)
-          granted_r[G - 1][dev] = smem;
-      }
-      if (G == 2)
-        k_hist32r<2><<<grid, HR<2>::kThreads, smem, s>>>(c, fo, rec, gpair, scale, rows, entries, ls, hist,
-                                                          totals, row_stats, K, R);
-      else
-        k_hist32r<1><<<grid, HR<1>::kThreads, smem, s>>>(c, fo, rec, gpair, scale, rows, entries, ls, hist,
-                                                          totals, row_stats, K, R);
-      return;
-    }
     if (G == 2)
       k_hist32<2><<<grid, kH32Threads, smem, s>>>(c, fo, rec, gpair, scale, rows, entries, ls, hist,
                                                   totals, row_stats, K, R);

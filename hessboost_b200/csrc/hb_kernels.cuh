@@ -100,6 +100,16 @@ void launch_finish_tree(const hb_tree_node* tree, const LevelState* ls_last, hb_
                         cudaStream_t s);
 void launch_dequantize(const longlong2* hist, uint32_t n, const Scale* scale, double* out,
                        cudaStream_t s);
+// RowEngine helpers: an iota row list; leaf values added to every segment
+// at once; a partition's copy-back with the children's end rows; the
+// fixed-point totals of a segment.
+void launch_iota(uint32_t* rows, uint32_t first, uint64_t n, int n_sm, cudaStream_t s);
+void launch_add_segments(const uint32_t* rows, const uint2* segs, const float* values, uint32_t n,
+                         float* margin, cudaStream_t s);
+void launch_finish_partition(const Front* parents, const Front* kids, uint32_t n, const uint32_t* rows_out,
+                             uint32_t* rows_in, uint32_t* ends, cudaStream_t s);
+void launch_seg_total(const uint32_t* rows, uint64_t begin, uint64_t len, const float2* gpair,
+                      const Scale* scale, long long* totals, int n_sm, cudaStream_t s);
 void launch_add_segment(const uint32_t* rows, uint32_t begin, uint32_t len, float value,
                         float* margin, cudaStream_t s);
 
