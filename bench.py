@@ -776,6 +776,7 @@ def main():
         rt.round()  # warm-up: slot reservation, first allocations
         k_re = max(1, min(args.steps, 10))
         c0 = rt.calls
+        rt.seconds = {}
         t0 = time.perf_counter()
         for _ in range(k_re):
             rt.round()
@@ -784,6 +785,7 @@ def main():
         row_engine = {"value": k_re / dt, "unit": UNIT, "rounds": k_re,
                       "ms_per_round": 1000.0 * dt / k_re,
                       "calls_per_round": (rt.calls - c0) / k_re,
+                      "ms_per_round_by_call": {k: 1000.0 * v / k_re for k, v in rt.seconds.items()},
                       "whole_round_ms_per_round": ms / args.steps,
                       "scope": "hessboost_b200.device_builder.RowEngineTrainer: gradients, begin_tree, "
                                "root_total, reserve_hists, build_resident, scan_resident per level, "

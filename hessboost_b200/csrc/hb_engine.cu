@@ -163,7 +163,6 @@ struct hb_engine {
   // one that fails (-1: none armed); no injection while a graph is captured
   int64_t fault_after = -1;
   bool capturing = false;
-  bool l2_window = false;  // the pairs' L2 access-policy window is set (HB_L2_PERSIST)
 };
 
 namespace {
@@ -662,34 +661,6 @@ hb_status check_params(hb_engine* e, const hb_train_params* p) {
   return stage_monotone(e, p);
 }
 
-// With HB_L2_PERSIST=1, the gradient pairs get an L2 access-policy window on
-// the engine's stream (persisting hits, a set-aside of at most the device's
-// maximum), so the round's gathered histogram launches read them from L2.
-// The set-aside is this process's context's; it ends with the context.
-hb_status keep_pairs_in_l2(hb_engine* e) {
-  const char* v = std::getenv("HB_L2_PERSIST");
-  if (!v || std::strcmp(v, "1") != 0 || e->l2_window) return HB_OK;
-  int max_persist = 0, max_window = 0;
-  HB_CK(e, cudaDeviceGetAttribute(&max_persist, cudaDevAttrMaxPersistingL2CacheSize, e->device));
-  HB_CK(e, cudaDeviceGetAttribute(&max_window, cudaDevAttrMaxAccessPolicyWindowSize, e->device));
-  const size_t want = sizeof(float2) * e->c.n_rows * (size_t)std::max(e->n_out, 1);
-  if (max_persist <= 0 || max_window <= 0 || want == 0) return HB_OK;
-  const size_t set_aside = std::min<size_t>(want, (size_t)max_persist);
-  HB_CK(e, cudaDeviceSetLimit(cudaLimitPersistingL2CacheSize, set_aside));
-  cudaStreamAttrValue a{};
-  a.accessPolicyWindow.base_ptr = e->gpair.p;
-  a.accessPolicyWindow.num_bytes = std::min<size_t>(want, (size_t)max_window);
-  a.accessPolicyWindow.hitRatio =
-      (float)std::min(1.0, (double)set_aside / (double)a.accessPolicyWindow.num_bytes);
-  a.accessPolicyWindow.hitProp = cudaAccessPropertyPersisting;
-  a.accessPolicyWindow.missProp = cudaAccessPropertyStreaming;
-  HB_CK(e, cudaStreamSetAttribute(e->stream, cudaStreamAttributeAccessPolicyWindow, &a));
-  e->l2_window = true;
-  std::fprintf(stderr, "hb: L2 window %zu of %zu pair bytes, set-aside %zu (max %d)\n",
-               (size_t)a.accessPolicyWindow.num_bytes, want, set_aside, max_persist);
-  return HB_OK;
-}
-
 // The run's monotone constraints on the device (before any capture): one
 // direction per feature, or none (c.mono = NULL) when every one is 0.
 hb_status stage_monotone(hb_engine* e, const hb_train_params* p) {
@@ -762,11 +733,6 @@ hb_status hb_engine_destroy(hb_engine* e) {
   if (!e) return HB_INVALID_ARGUMENT;
   cudaSetDevice(e->device);
   if (e->stream) cudaStreamSynchronize(e->stream);
-  // the pairs' persisting L2 lines back to normal and the set-aside released
-  if (e->l2_window) {
-    cudaCtxResetPersistingL2Cache();
-    cudaDeviceSetLimit(cudaLimitPersistingL2CacheSize, 0);
-  }
   // the round graph holds the level allreduces: release it before the communicator
   if (e->round_exec) cudaGraphExecDestroy(e->round_exec);
   e->round_exec = nullptr;
@@ -963,9 +929,6 @@ static hb_status upload_index(hb_engine* e, const hb_ghist* g, const RawSource* 
   // selects the 64-bit-atomic one for every size (comparison runs).
   const char* hk = std::getenv("HB_HIST_KERNEL");
   c.hist64 = (hk && std::strcmp(hk, "64") == 0) ? 1u : 0u;
-  // HB_L2_HINTS=1: evict-last prefetch of the pairs in the histogram kernel
-  const char* lh = std::getenv("HB_L2_HINTS");
-  c.l2_hints = (lh && std::strcmp(lh, "1") == 0) ? 1u : 0u;
   // HB_SCAN_KERNEL=cta keeps the CTA-per-feature scan for every width.
   const char* sk = std::getenv("HB_SCAN_KERNEL");
   c.scan_cta = (sk && std::strcmp(sk, "cta") == 0) ? 1u : 0u;
@@ -1926,8 +1889,6 @@ hb_status hb_train_rounds(hb_engine* e, const hb_train_params* p, int32_t rounds
   const int trees = rounds * e->n_out;  // one tree per class and round
   HB_CK(e, e->forest.alloc(std::max<size_t>((size_t)trees * max_nodes, 1)));
   HB_CK(e, e->counts.alloc(std::max(trees, 1)));
-  st = keep_pairs_in_l2(e);
-  if (st != HB_OK) return st;
   HB_CK(e, cudaMemsetAsync(e->tree_counter.p, 0, 4, s));
   if (e->use_graphs && rounds > 0) {
     st = ensure_buffers(e, p);

@@ -49,11 +49,6 @@ __device__ __forceinline__ uint64_t l2_evict_last() {
   return p;
 }
 
-// The line holding `ptr` fetched into L2 ahead of use, marked evict-last.
-__device__ __forceinline__ void prefetch_l2_keep(const void* ptr) {
-  asm volatile("prefetch.global.L2::evict_last [%0];" ::"l"(ptr));
-}
-
 __device__ __forceinline__ void st_hint8(float2* ptr, float2 v, uint64_t pol) {
   asm volatile("st.global.L2::cache_hint.v2.f32 [%0], {%1, %2}, %3;" ::"l"(ptr), "f"(v.x), "f"(v.y), "l"(pol)
                : "memory");
@@ -707,7 +702,6 @@ __global__ void __launch_bounds__(kH32Threads, 1)
   const bool want_totals = totals != nullptr && g0 == 0;
   const uint32_t lo_mask = (uint32_t)((1ull << lo_bits) - 1ull);
   long long tg = 0, th = 0;
-  const bool keep_pairs = c.l2_hints != 0;
 
   // Each thread owns kSlotsPerThread / 4 runs of four consecutive slots
   // (slot_of below), moved with 128-bit shared loads and stores.
@@ -773,9 +767,6 @@ __global__ void __launch_bounds__(kH32Threads, 1)
               __pipeline_memcpy_async(&smask[(st * G + lg) * kH32Threads + tid], rr + mask_at[lg], 4);
           }
         }
-        // the pair's line kept in L2 (evict-last) for the round's later
-        // launches, which gather the same pairs again
-        if (keep_pairs) prefetch_l2_keep(&gpair[row]);
         __pipeline_memcpy_async(&sgp[st * kH32Threads + tid], &gpair[row], 8);
       }
       __pipeline_commit();

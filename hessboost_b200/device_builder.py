@@ -22,6 +22,7 @@ bit, because every histogram sum is an integer the f64 ABI carries exactly.
 """
 
 import math
+import time
 
 import numpy as np
 
@@ -120,8 +121,17 @@ class RowEngineTrainer:
         self.features = np.arange(self.n_cols, dtype=np.uint32)
         self.dirs = np.array(self.mono[: self.n_cols], np.int8)
         self.calls = 0
+        self.seconds = {}  # host wall time by entry point
         # resident_slots (device.rs:123): 2^(max_depth - 1) for depthwise
         self.n_slots = min(1 << (params.max_depth - 1), max(self.n_rows, 1))
+
+    def _t(self, name, fn, *a, **kw):
+        """One C-ABI call, counted and timed (host wall clock)."""
+        t0 = time.perf_counter()
+        out = fn(*a, **kw)
+        self.seconds[name] = self.seconds.get(name, 0.0) + time.perf_counter() - t0
+        self.calls += 1
+        return out
 
     # -- one node's scan decoded (resident_best, device.rs:642) -------------
     def _best(self, scan, total, bounds):
@@ -155,24 +165,21 @@ class RowEngineTrainer:
             return []
         reqs = [(n["slot"], n["stats"], self.features, self.dirs, n["bounds"],
                  node_gain(n["stats"], self.reg, *n["bounds"])) for n in nodes]
-        self.calls += 1
-        scans = self.e.scan_resident(self.reg, reqs)
+        scans = self._t("scan_resident", self.e.scan_resident, self.reg, reqs)
         return [self._best(s, n["stats"], n["bounds"]) for s, n in zip(scans, nodes)]
 
     def round(self):
         """One boosting round; returns the tree as an hb_tree_node array."""
         e = self.e
-        if not e.gradients(self.kind, self.labels, scale_pos_weight=self.p.scale_pos_weight):
+        if not self._t("gradients", e.gradients, self.kind, self.labels, scale_pos_weight=self.p.scale_pos_weight):
             raise HbError(1, "gradients", "non-finite gradients: the host grows this round")
-        seg = e.begin_tree(self.all_rows)
-        g, h = e.root_total(seg)
-        if not e.reserve_hists(self.n_slots):
+        seg = self._t("begin_tree", e.begin_tree, self.all_rows)
+        g, h = self._t("root_total", e.root_total, seg)
+        if not self._t("reserve_hists", e.reserve_hists, self.n_slots):
             raise HbError(1, "reserve_hists", "the device declined the slots")
-        self.calls += 4
         slots = _Slots(self.n_slots)
         root_slot = slots.take()
-        e.build_resident([(seg, root_slot)])
-        self.calls += 1
+        self._t("build_resident", e.build_resident, [(seg, root_slot)])
         inf = (-math.inf, math.inf)
         nodes = [dict(nid=0, depth=0, seg=seg, slot=root_slot, stats=(g, h), bounds=inf)]
         nodes[0]["best"] = self._scan(nodes)[0]
@@ -212,8 +219,7 @@ class RowEngineTrainer:
             if t["left"] == -1:
                 w = np.float32(calc_weight_bounded(*stats[nid], self.reg, *bounds[nid]))
                 t["leaf"] = np.float32(w * eta)
-        e.add_leaf_values([s for _, s in leaves], [tree[nid]["leaf"] for nid, _ in leaves])
-        self.calls += 1
+        self._t("add_leaf_values", e.add_leaf_values, [s for _, s in leaves], [tree[nid]["leaf"] for nid, _ in leaves])
         out = np.zeros(len(tree), NODE_DTYPE)
         for i, t in enumerate(tree):
             out[i] = (t["left"], t["right"], t["feature"], t["cond"], t["default_left"], t["leaf"],
@@ -231,8 +237,7 @@ class RowEngineTrainer:
             first = int(self.fo[b["feature"]])
             limit = 0 if b["bin"] < 0 else b["bin"] + 1 - first
             splits.append((n["seg"], b["feature"], limit, b["default_left"]))
-        parts = e.partition(splits)
-        self.calls += 1
+        parts = self._t("partition", e.partition, splits)
         for n, _, _, _, terminal in pending:
             if terminal:
                 slots.release(n["slot"])
@@ -249,8 +254,7 @@ class RowEngineTrainer:
                 kl["slot"], kr["slot"] = (built, n["slot"]) if left_smaller else (n["slot"], built)
             kids.append((kl, kr, terminal))
         if build:
-            e.build_resident(build, siblings=siblings)
-            self.calls += 1
+            self._t("build_resident", e.build_resident, build, siblings=siblings)
         searched = [k for kl, kr, t in kids if not t for k in (kl, kr)]
         for k, best in zip(searched, self._scan(searched)):
             k["best"] = best
