@@ -929,6 +929,7 @@ static hb_status upload_index(hb_engine* e, const hb_ghist* g, const RawSource* 
   // selects the 64-bit-atomic one for every size (comparison runs).
   const char* hk = std::getenv("HB_HIST_KERNEL");
   c.hist64 = (hk && std::strcmp(hk, "64") == 0) ? 1u : 0u;
+  c.hist_v1 = (hk && std::strcmp(hk, "v1") == 0) ? 1u : 0u;
   // HB_SCAN_KERNEL=cta keeps the CTA-per-feature scan for every width.
   const char* sk = std::getenv("HB_SCAN_KERNEL");
   c.scan_cta = (sk && std::strcmp(sk, "cta") == 0) ? 1u : 0u;
@@ -1369,7 +1370,9 @@ hb_status hb_partition(hb_engine* e, const hb_row_split* splits, uint32_t n, hb_
   HB_CK(e, cudaGetLastError());
   // the children back in rows[0] and their end rows, one launch
   HB_CK(e, e->part_ends.alloc(4 * (size_t)n));
-  launch_finish_partition(e->front[0].p, e->front[1].p, n, e->rows[1].p, e->rows[0].p, e->part_ends.p, s);
+  HB_CK(e, cudaMemsetAsync(e->part_ends.p, 0, 16 * (size_t)n, s));
+  launch_finish_partition(e->items.p, n_items, e->front[0].p, e->front[1].p, e->rows[1].p, e->rows[0].p,
+                          e->part_ends.p, s);
   HB_CK(e, cudaGetLastError());
   std::vector<Front> nx(2 * (size_t)n);
   std::vector<uint32_t> ends(4 * (size_t)n);
@@ -1483,12 +1486,14 @@ hb_status hb_add_leaf_values(hb_engine* e, const hb_segment* segs, const float* 
 hb_status hb_reserve_hists(hb_engine* e, uint32_t slots, int32_t* reserved) {
   HB_ENTER(e);
   if (!e->uploaded || !reserved) return HB_INVALID_ARGUMENT;
-  size_t free_b = 0, total_b = 0;
-  cudaMemGetInfo(&free_b, &total_b);
   const size_t need = (size_t)slots * e->c.total_bins * sizeof(longlong2);
-  if (need > free_b / 2) {
-    *reserved = 0;
-    return HB_OK;
+  if ((size_t)slots * e->c.total_bins > e->resident.n) {  // only a buffer that must grow asks the driver
+    size_t free_b = 0, total_b = 0;
+    cudaMemGetInfo(&free_b, &total_b);
+    if (need > free_b / 2) {
+      *reserved = 0;
+      return HB_OK;
+    }
   }
   HB_CK(e, e->resident.alloc(std::max<size_t>((size_t)slots * e->c.total_bins, 1)));
   e->resident_slots = slots;

@@ -106,8 +106,8 @@ void launch_dequantize(const longlong2* hist, uint32_t n, const Scale* scale, do
 void launch_iota(uint32_t* rows, uint32_t first, uint64_t n, int n_sm, cudaStream_t s);
 void launch_add_segments(const uint32_t* rows, const uint2* segs, const float* values, uint32_t n,
                          float* margin, cudaStream_t s);
-void launch_finish_partition(const Front* parents, const Front* kids, uint32_t n, const uint32_t* rows_out,
-                             uint32_t* rows_in, uint32_t* ends, cudaStream_t s);
+void launch_finish_partition(const PItem* items, int n_items, const Front* parents, const Front* kids,
+                             const uint32_t* rows_out, uint32_t* rows_in, uint32_t* ends, cudaStream_t s);
 void launch_seg_total(const uint32_t* rows, uint64_t begin, uint64_t len, const float2* gpair,
                       const Scale* scale, long long* totals, int n_sm, cudaStream_t s);
 void launch_add_segment(const uint32_t* rows, uint32_t begin, uint32_t len, float value,

@@ -22,6 +22,9 @@ def cases():
     yield "logistic", x, y, H.TrainingParams(objective="binary:logistic", max_depth=8, eta=0.1), 4
     x, y = synth.regression_c1(60_001, 28, seed=3)
     yield "regression", x, y, H.TrainingParams(objective="reg:squarederror", max_depth=6, eta=0.1), 4
+    x, y = synth.logistic_c2(100_003, 12, seed=21)
+    yield "monotone", x, y, H.TrainingParams(objective="binary:logistic", max_depth=6, eta=0.3,
+                                             monotone_constraints=(1, -1, 0, 1)), 3
 
 
 def main():
