@@ -38,6 +38,10 @@ N_ROWS = 10_000_000
 N_COLS = 28
 MISSING = 0.05
 PARAMS = dict(objective="binary:logistic", max_depth=8, eta=0.1, max_bin=256)
+# DRAM bytes (read + write) per k_hist32 launch at C2, 10M rows on one GPU:
+# the mean over one round's root and 7 level launches of an ncu capture
+# (profiles/k_hist32_c2_10M_traffic.md).
+HIST_TRAFFIC_C2 = 576.5e6
 
 
 # The one JSON line goes to the real stdout; everything else that writes to
@@ -78,6 +82,7 @@ def config(n_gpus):
         "parallelism": f"rows sharded over {n_gpus} GPU(s), one NCCL allreduce per level"
         if n_gpus > 1 else "1 GPU",
         "l2": _l2_note(),
+        "hist_kernel": os.environ.get("HB_HIST_KERNEL", "default"),
     }
 
 
@@ -398,7 +403,7 @@ def run_c3(args):
                    "l2": f"inputs {'larger' if n * 128 > 126e6 else 'SMALLER'} than L2: "
                          f"{n:,} x 128 B records + 10 x {n * 8 / 1e6:,.0f} MB pairs per round"},
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
-                     "frac": achieved / peak, "traffic": None, "kernel": "k_hist32r",
+                     "frac": achieved / peak, "traffic": None, "kernel": "k_hist32",
                      "launches": hist_launches},
         "cpu_baseline": cpu,
         "parity": parity,
@@ -852,14 +857,17 @@ def main():
                                   "event nodes around each histogram launch); per-family "
                                   "breakdown from a separate instrumented run"},
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
-                         "frac": achieved / peak, "traffic": None,
+                         "frac": achieved / peak,
+                         "traffic": HIST_TRAFFIC_C2 if (N_ROWS == 10_000_000 and world == 1) else None,
                          "kernel": "k_hist32", "launches": hist_launches,
                          "avg_launch_ms": hist_ms / max(hist_launches, 1),
                          "alg_bytes_per_launch": alg_bytes / max(hist_launches, 1),
                          "alg_bytes_rule": f"per built row: {N_COLS} B of bins + 8 B (g, h) pair + "
                                            f"{bitmap} B missing bitmap + 4 B row id when gathered",
-                         "traffic_note": "DRAM bytes per launch come from an ncu capture, not from "
-                                         "this run",
+                         "traffic_note": "DRAM bytes read + written per launch, averaged over one "
+                                         "round's 8 launches at 10M rows, from the ncu capture in "
+                                         "profiles/k_hist32_c2_10M_traffic.md (not from this run; "
+                                         "null at other sizes)",
                          "peak_kind": peak_kind + " (MEASURED_PEAKS.json hbm_gbs)"},
             "cpu_baseline": cpu,
             "parity": parity,

@@ -929,7 +929,6 @@ static hb_status upload_index(hb_engine* e, const hb_ghist* g, const RawSource* 
   // selects the 64-bit-atomic one for every size (comparison runs).
   const char* hk = std::getenv("HB_HIST_KERNEL");
   c.hist64 = (hk && std::strcmp(hk, "64") == 0) ? 1u : 0u;
-  c.hist_v1 = (hk && std::strcmp(hk, "v1") == 0) ? 1u : 0u;
   // HB_SCAN_KERNEL=cta keeps the CTA-per-feature scan for every width.
   const char* sk = std::getenv("HB_SCAN_KERNEL");
   c.scan_cta = (sk && std::strcmp(sk, "cta") == 0) ? 1u : 0u;

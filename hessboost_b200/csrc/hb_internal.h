@@ -58,7 +58,6 @@ struct DevConst {
   uint32_t dense;         // index-level: no missing cell anywhere
   uint32_t n_groups;      // feature groups of kGroupFeatures
   uint32_t hist64;        // 1: always the 64-bit-atomic histogram kernel
-  uint32_t hist_v1;       // 1: the 512-thread staged kernel (k_hist32) instead of k_hist32b
   uint32_t scan_cta;      // 1: always the CTA-per-feature split scan
   // CSR index (csr = 1): each row's global bins ascending, absent = missing;
   // fo = the device copy of feature_offset (both layouts)

@@ -916,274 +916,6 @@ __global__ void __launch_bounds__(kH32Threads, 1)
   }
 }
 
-// The staged histogram at twice the warps: with every sum within 2^53 the
-// 32-bit accumulators need adding to the node histogram only every R >= 2^14
-// rows, so no thread keeps a register copy of its slots (the 64 registers of
-// k_hist32's fold) and a CTA of 1024 threads fits the SM (64 registers a
-// thread). Two cp.async stages a thread keep 2048 rows a SM in flight; the
-// 32 warps hide one another's dependent-instruction latency, the largest
-// stall of the 16-warp kernel. Two groups a CTA (G = 2) keep 512 threads.
-template <int G>
-struct H32B {
-  static constexpr int kThreads = G == 1 ? 1024 : 512;
-  static constexpr int kStages = 2;
-  static constexpr int kSlots = kNSlots / kThreads;
-  static constexpr int kBinShift = G == 1 ? 8 : 7;
-  static constexpr size_t smem() {
-    return (size_t)kSlotStride * 16 +
-           (size_t)kStages * kThreads * (G * sizeof(StageRow) + sizeof(float2) + G * sizeof(uint32_t));
-  }
-};
-
-template <int G>
-__global__ void __launch_bounds__(H32B<G>::kThreads, 1)
-    k_hist32b(DevConst c, const uint32_t* __restrict__ fo, const uint8_t* __restrict__ rec,
-              const float2* __restrict__ gpair, const Scale* __restrict__ scale,
-              const uint32_t* __restrict__ rows, const HEntry* __restrict__ entries,
-              const LevelState* __restrict__ ls, longlong2* __restrict__ hist,
-              long long* __restrict__ totals, unsigned long long* __restrict__ row_stats, int lo_bits,
-              int flush_rows) {
-  constexpr int kT = H32B<G>::kThreads;
-  constexpr int kSt = H32B<G>::kStages;
-  constexpr int kS = H32B<G>::kSlots;
-  constexpr int kBS = H32B<G>::kBinShift;
-  extern __shared__ __align__(16) uint32_t s32[];
-  const int n_entries = ls->n_hentries;
-  const uint64_t total = ls->hist_rows;
-  if (n_entries <= 0 || total == 0) return;
-  if (row_stats && blockIdx.x == 0 && blockIdx.y == 0 && threadIdx.x == 0)
-    atomicAdd(&row_stats[entries[0].identity ? 0 : 1], (unsigned long long)total);
-  const uint64_t per = (total + gridDim.x - 1) / gridDim.x;
-  const uint64_t a0 = (uint64_t)blockIdx.x * per;
-  const uint64_t b0 = min(total, a0 + per);
-  if (a0 >= b0) return;
-
-  const int g0 = blockIdx.y * G;
-  const int ng = min(G, (int)c.n_groups - g0);
-  uint32_t* lo_g = s32;
-  uint32_t* hi_g = s32 + kSlotStride;
-  uint32_t* lo_h = s32 + 2 * kSlotStride;
-  uint32_t* hi_h = s32 + 3 * kSlotStride;
-  StageRow* srec = reinterpret_cast<StageRow*>(s32 + 4 * kSlotStride);   // [kSt][G][threads]
-  float2* sgp = reinterpret_cast<float2*>(srec + kSt * G * kT);          // [kSt][threads]
-  uint32_t* smask = reinterpret_cast<uint32_t*>(sgp + kSt * kT);         // [kSt][G][threads]
-  {
-    uint4* z = reinterpret_cast<uint4*>(s32);
-    for (int i = threadIdx.x; i < kSlotStride; i += kT) z[i] = make_uint4(0u, 0u, 0u, 0u);
-  }
-  __syncthreads();
-
-  const double fg = scale->fg, fh = scale->fh;
-  const int tid = threadIdx.x;
-  const int lane = tid & 31;
-  const uint32_t lane4 = (uint32_t)lane << 2;
-  const uint32_t sbase = (uint32_t)__cvta_generic_to_shared(s32);
-  bool wide[G], mask_in_block[G];
-  uint32_t mask_at[G], dummy[G];
-  int mask_word[G];
-#pragma unroll
-  for (int lg = 0; lg < G; ++lg) {
-    const int g = g0 + lg;
-    const int nfg = lg < ng ? min(kGroupFeatures, (int)c.n_cols - g * kGroupFeatures) : 0;
-    wide[lg] = c.stride >= (uint32_t)(32 * g + 32);
-    mask_at[lg] = c.mask_off + 4 * g;
-    mask_in_block[lg] = mask_at[lg] >= (uint32_t)(32 * g) &&
-                        mask_at[lg] + 4 <= (uint32_t)(32 * g + (wide[lg] ? 32 : 16));
-    mask_word[lg] = (int)(mask_at[lg] - 32 * (uint32_t)g) >> 2;
-    dummy[lg] = nfg >= 32 ? 0u : (0xffffffffu << nfg);
-  }
-  const bool want_totals = totals != nullptr && g0 == 0;
-  const uint32_t lo_mask = (uint32_t)((1ull << lo_bits) - 1ull);
-  long long tg = 0, th = 0;
-
-  // The CTA's sums so far into node histogram `slot`, the accumulators back
-  // to zero: each thread combines its kS slots (runs of four words) into
-  // int64, stages them feature-major in the same shared memory (bins
-  // XOR-swizzled against bank conflicts), then each warp adds one feature's
-  // (g, h) words to the node histogram with contiguous 64-bit reds.
-  auto flush = [&](int slot) {
-    __syncthreads();
-    long long vg[kS], vh[kS];
-#pragma unroll
-    for (int j = 0; j < kS / 4; ++j) {
-      const int base = 4 * (tid + j * kT);
-      const uint4 a = *reinterpret_cast<const uint4*>(&lo_g[base]);
-      const uint4 b = *reinterpret_cast<const uint4*>(&hi_g[base]);
-      const uint4 p = *reinterpret_cast<const uint4*>(&lo_h[base]);
-      const uint4 q = *reinterpret_cast<const uint4*>(&hi_h[base]);
-      vg[4 * j + 0] = ((long long)(int)b.x << lo_bits) + (long long)a.x;
-      vg[4 * j + 1] = ((long long)(int)b.y << lo_bits) + (long long)a.y;
-      vg[4 * j + 2] = ((long long)(int)b.z << lo_bits) + (long long)a.z;
-      vg[4 * j + 3] = ((long long)(int)b.w << lo_bits) + (long long)a.w;
-      vh[4 * j + 0] = ((long long)(int)q.x << lo_bits) + (long long)p.x;
-      vh[4 * j + 1] = ((long long)(int)q.y << lo_bits) + (long long)p.y;
-      vh[4 * j + 2] = ((long long)(int)q.z << lo_bits) + (long long)p.z;
-      vh[4 * j + 3] = ((long long)(int)q.w << lo_bits) + (long long)p.w;
-    }
-    __syncthreads();
-    constexpr int kNB = 1 << kBS;
-    long long* stg = reinterpret_cast<long long*>(s32);
-#pragma unroll
-    for (int j = 0; j < kS; ++j) {
-      const int sl = 4 * (tid + (j >> 2) * kT) + (j & 3);
-      const int row = ((sl >> (kBS + 5)) << 5) | (sl & 31);
-      const int bin = (sl >> 5) & (kNB - 1);
-      const int at = 2 * (row * kNB + (bin ^ ((row >> 2) & 7)));
-      stg[at] = vg[j];
-      stg[at + 1] = vh[j];
-    }
-    __syncthreads();
-    unsigned long long* dstw = reinterpret_cast<unsigned long long*>(hist + (uint64_t)slot * c.total_bins);
-    const int warp = tid >> 5;
-    for (int row = warp; row < G * 32; row += kT / 32) {
-      const int lgs = row >> 5;
-      const int f = (g0 + lgs) * kGroupFeatures + (row & 31);
-      if (lgs >= ng || f >= (int)c.n_cols) continue;
-      const uint32_t fs = fo[f];
-      const uint32_t nw = 2 * (fo[f + 1] - fs);
-      for (uint32_t w = lane; w < nw; w += 32) {
-        const int bin = (int)(w >> 1);
-        const long long v = stg[2 * (row * kNB + (bin ^ ((row >> 2) & 7))) + (w & 1)];
-        if (v) atomicAdd(dstw + 2 * (uint64_t)fs + w, (unsigned long long)v);
-      }
-    }
-    __syncthreads();
-    uint4* z = reinterpret_cast<uint4*>(s32);
-    for (int i = tid; i < kSlotStride; i += kT) z[i] = make_uint4(0u, 0u, 0u, 0u);
-    __syncthreads();
-  };
-
-  int e = 0;
-  {
-    int hi = n_entries - 1;
-    while (e < hi) {
-      const int mid = (e + hi + 1) >> 1;
-      if (entries[mid].prefix <= a0) e = mid; else hi = mid - 1;
-    }
-  }
-  uint64_t pos = a0;
-  int since = 0;
-  while (pos < b0 && e < n_entries) {
-    const HEntry en = entries[e];
-    const uint64_t end_e = min(b0, en.prefix + en.len);
-    const int n_it = (int)((end_e - pos + kT - 1) / kT);
-    auto row_at = [&](uint64_t i) -> uint32_t {
-      const uint32_t at = en.begin + (uint32_t)(i - en.prefix);
-      return en.identity ? at : rows[at];
-    };
-    // each thread copies its own future rows into its own staging slots and
-    // later reads only those: the pipeline needs no CTA barrier
-    auto issue = [&](int it, uint32_t row, bool valid) {
-      const int st = it % kSt;
-      if (valid) {
-        const uint8_t* rr = rec + (uint64_t)row * c.stride;
-#pragma unroll
-        for (int lg = 0; lg < G; ++lg) {
-          if (lg < ng) {
-            const uint8_t* rp = rr + 32 * (g0 + lg);
-            StageRow* d = &srec[(st * G + lg) * kT + tid];
-            __pipeline_memcpy_async(&d->a, rp, 16);
-            if (wide[lg]) __pipeline_memcpy_async(&d->b, rp + 16, 16);
-            if (!mask_in_block[lg]) __pipeline_memcpy_async(&smask[(st * G + lg) * kT + tid], rr + mask_at[lg], 4);
-          }
-        }
-        __pipeline_memcpy_async(&sgp[st * kT + tid], &gpair[row], 8);
-      }
-      __pipeline_commit();
-    };
-    {
-      const uint64_t i = pos + tid;
-      const bool v = i < end_e;
-      issue(0, v ? row_at(i) : 0u, v);
-    }
-    uint64_t ip = pos + (uint64_t)kT + tid;
-    bool pend_valid = ip < end_e;
-    uint32_t pend_row = pend_valid ? row_at(ip) : 0u;
-    for (int it = 0; it < n_it; ++it) {
-      issue(it + 1, pend_row, pend_valid);
-      ip = pos + (uint64_t)(it + 2) * kT + tid;
-      pend_valid = ip < end_e;
-      pend_row = pend_valid ? row_at(ip) : 0u;
-      __pipeline_wait_prior(1);
-      const uint64_t i = pos + (uint64_t)it * kT + tid;
-      if (i < end_e) {
-        const int st = it % kSt;
-        const float2 pr = sgp[st * kT + tid];
-        const long long qg = __double2ll_rn((double)pr.x * fg);
-        const long long qh = __double2ll_rn((double)pr.y * fh);
-        if (want_totals) {
-          tg += qg;
-          th += qh;
-        }
-        const uint32_t lg_ = (uint32_t)qg & lo_mask, lh = (uint32_t)qh & lo_mask;
-        const uint32_t hg = (uint32_t)(qg >> lo_bits), hh = (uint32_t)(qh >> lo_bits);
-#pragma unroll
-        for (int lg = 0; lg < G; ++lg) {
-          if (lg >= ng) break;
-          const StageRow sr = srec[(st * G + lg) * kT + tid];
-          const uint4 v1 = wide[lg] ? sr.b : make_uint4(0, 0, 0, 0);
-          uint32_t mask = mask_in_block[lg] ? pick_word(sr.a, v1, mask_word[lg]) : smask[(st * G + lg) * kT + tid];
-          mask |= dummy[lg];
-          // the 32 record bytes rotated right by `lane` bytes: step s reads
-          // the lane's feature (lane + s) mod 32
-          uint32_t w[8] = {sr.a.x, sr.a.y, sr.a.z, sr.a.w, v1.x, v1.y, v1.z, v1.w};
-          const int q = lane >> 2;
-          uint32_t t[8];
-#pragma unroll
-          for (int j = 0; j < 8; ++j) t[j] = (q & 4) ? w[(j + 4) & 7] : w[j];
-#pragma unroll
-          for (int j = 0; j < 8; ++j) w[j] = (q & 2) ? t[(j + 2) & 7] : t[j];
-#pragma unroll
-          for (int j = 0; j < 8; ++j) t[j] = (q & 1) ? w[(j + 1) & 7] : w[j];
-          const int sh = (lane & 3) * 8;
-#pragma unroll
-          for (int j = 0; j < 8; ++j) w[j] = __funnelshift_r(t[j], t[(j + 1) & 7], sh);
-          const uint32_t mrot = __funnelshift_r(mask, mask, lane);
-          const uint32_t grow = (uint32_t)lg << (kBS + 7);
-#pragma unroll
-          for (int s2 = 0; s2 < 32; ++s2) {
-            const uint32_t word = w[s2 >> 2];
-            const int k = s2 & 3;
-            const uint32_t binx = (k == 0 ? (word << 7) : (word >> (8 * k - 7))) & (((1u << kBS) - 1u) << 7);
-            const uint32_t rowx = ((mrot >> s2) & 1u) ? (uint32_t)(kTrashBin << 7) : (binx | grow);
-            const uint32_t ad = sbase + (rowx | ((lane4 + 4u * (uint32_t)s2) & 124u));
-            asm volatile(
-                "red.shared.add.u32 [%0], %1;\n\t"
-                "red.shared.add.u32 [%0+%5], %2;\n\t"
-                "red.shared.add.u32 [%0+%6], %3;\n\t"
-                "red.shared.add.u32 [%0+%7], %4;" ::"r"(ad),
-                "r"(lg_), "r"(hg), "r"(lh), "r"(hh), "n"(kSlotStride * 4), "n"(kSlotStride * 8),
-                "n"(kSlotStride * 12)
-                : "memory");
-          }
-        }
-      }
-      since += kT;
-      if (since + kT > flush_rows && it + 1 < n_it) {  // the next pass could pass R rows
-        __pipeline_wait_prior(0);
-        flush(en.slot);
-        since = 0;
-      }
-    }
-    __pipeline_wait_prior(0);
-    flush(en.slot);
-    since = 0;
-    pos = end_e;
-    ++e;
-  }
-  if (want_totals) {
-    using BR = cub::BlockReduce<long long, kT>;
-    __shared__ typename BR::TempStorage tmp;
-    long long sgt = BR(tmp).Sum(tg);
-    __syncthreads();
-    long long sht = BR(tmp).Sum(th);
-    if (tid == 0) {
-      atomicAdd(reinterpret_cast<unsigned long long*>(&totals[0]), (unsigned long long)sgt);
-      atomicAdd(reinterpret_cast<unsigned long long*>(&totals[1]), (unsigned long long)sht);
-    }
-  }
-}
-
 // sibling = parent - built (int64, exact; src/tree/hist/mod.rs:32).
 __global__ void k_subtract(const Triple* __restrict__ pairs, const LevelState* __restrict__ ls,
                            uint32_t total_bins, longlong2* __restrict__ hist) {
@@ -2847,8 +2579,7 @@ static int hist_groups_per_cta(const DevConst& c) {
 size_t hist_smem_bytes(const DevConst& c) {
   if (c.csr) return 0;
   if (use_hist32(c)) {
-    if (c.hist_v1) return hist_groups_per_cta(c) == 2 ? H32<2>::smem() : H32<1>::smem();
-    return hist_groups_per_cta(c) == 2 ? H32B<2>::smem() : H32B<1>::smem();
+    return hist_groups_per_cta(c) == 2 ? H32<2>::smem() : H32<1>::smem();
   }
   return (size_t)c.max_bins * 32 * 16;
 }
@@ -2888,22 +2619,6 @@ void launch_hist(const DevConst& c, const uint32_t* fo, const uint8_t* rec, cons
     int K, R;
     split_for_rows(c.global_rows, K, R);
     grid.y = (c.n_groups + G - 1) / G;
-    if (!c.hist_v1) {
-      static size_t granted_b[2][64] = {{0}};
-      if (dev < 0 || dev >= 64 || granted_b[G - 1][dev] < smem) {
-        if (cudaFuncSetAttribute(G == 2 ? (const void*)k_hist32b<2> : (const void*)k_hist32b<1>,
-                                 cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) == cudaSuccess &&
-            dev >= 0 && dev < 64)
-          granted_b[G - 1][dev] = smem;
-      }
-      if (G == 2)
-        k_hist32b<2><<<grid, H32B<2>::kThreads, smem, s>>>(c, fo, rec, gpair, scale, rows, entries, ls, hist,
-                                                            totals, row_stats, K, R);
-      else
-        k_hist32b<1><<<grid, H32B<1>::kThreads, smem, s>>>(c, fo, rec, gpair, scale, rows, entries, ls, hist,
-                                                            totals, row_stats, K, R);
-      return;
-    }
     if (G == 2)
       k_hist32<2><<<grid, kH32Threads, smem, s>>>(c, fo, rec, gpair, scale, rows, entries, ls, hist,
                                                   totals, row_stats, K, R);

@@ -583,18 +583,17 @@ def test_non_ascending_rows_are_refused():
 
 @pytest.mark.parametrize("n_cols,max_bin", [(28, 256), (70, 128)])
 def test_histogram_kernels_agree(monkeypatch, n_cols, max_bin):
-    """The 32-bit split-accumulator kernels (1024-thread k_hist32b, the
-    512-thread k_hist32) and the 64-bit-atomic one give the same exact int64
-    sums, one feature group a CTA (256 bins) and two (128 bins)."""
+    """The 32-bit split-accumulator kernel (k_hist32) and the 64-bit-atomic
+    one give the same exact int64 sums, one feature group a CTA (256 bins)
+    and two (128 bins)."""
     x, y = synth.logistic_c2(1_100_000, n_cols, seed=13)
     m = H.BinnedMatrix.from_dense(x, max_bin)
     p = H.TrainingParams(objective="binary:logistic", max_depth=8, max_bin=max_bin)
     runs = []
-    for kernel in ("32", "v1", "64"):
+    for kernel in ("32", "64"):
         monkeypatch.setenv("HB_HIST_KERNEL", kernel)
         runs.append(H.train(p, y=y, rounds=2, matrix=m))
-    for other, name in ((1, "v1"), (2, "64")):
-        assert_forest_equal(runs[0].nodes, runs[0].tree_ptr, runs[other].nodes, runs[other].tree_ptr, f"32 vs {name}")
+    assert_forest_equal(runs[0].nodes, runs[0].tree_ptr, runs[1].nodes, runs[1].tree_ptr, "32 vs 64")
 
 
 @pytest.mark.parametrize("max_bin", [16, 48, 128])
