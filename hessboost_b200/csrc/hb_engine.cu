@@ -75,6 +75,7 @@ struct hb_engine {
 
   // rows
   DevBuf<float2> gpair;
+
   DevBuf<float> margin, label, weight;
   const float* label_key = nullptr;
   const float* weight_key = nullptr;
@@ -163,10 +164,16 @@ struct hb_engine {
   // one that fails (-1: none armed); no injection while a graph is captured
   int64_t fault_after = -1;
   bool capturing = false;
+  // the row blocks hold this tree's pairs (the last gradient pass wrote
+  // them): the histogram launches of the growth paths read them there
+  bool blk_pairs = false;
 };
 
 namespace {
 inline float2* cur_gpair(hb_engine* e) { return e->gpair.p + (size_t)e->cls * e->c.n_rows; }
+// The pairs the growth paths' histogram launches read: null = the row blocks.
+inline const float2* hist_gpair(hb_engine* e) { return e->blk_pairs ? nullptr : cur_gpair(e); }
+
 inline Scale* cur_scale(hb_engine* e) { return e->scale.p + e->cls; }
 inline WNode* cur_wtree(hb_engine* e) { return e->wtree.p + (size_t)e->cls * e->wstride; }
 }  // namespace
@@ -319,10 +326,10 @@ hb_status flush_pending(hb_engine* e) {
                     e->stream);
   else if (e->n_out > 1)
     launch_walk_classes(e->n_out, e->wtree.p, (uint32_t)e->wstride, e->rec.p, e->c.stride,
-                        e->c.mask_off, e->c.n_rows, e->margin.p, e->flags.p, e->n_sm, e->stream);
+                        e->c.mask_off, e->c.blk, e->c.n_rows, e->margin.p, e->flags.p, e->n_sm, e->stream);
   else
     launch_walk(e->wtree.p, e->ls.p + e->walk_ls, e->walk_nodes, e->rec.p, e->c.stride,
-                e->c.mask_off, e->c.n_rows, e->margin.p, e->flags.p, e->n_sm, e->stream);
+                e->c.mask_off, e->c.blk, e->c.n_rows, e->margin.p, e->flags.p, e->n_sm, e->stream);
   mark_end(e);
   HB_CK(e, cudaMemsetAsync(e->flags.p, 0, sizeof(int), e->stream));
   e->kernel_launches += 1;
@@ -347,10 +354,13 @@ hb_status run_gradients(hb_engine* e, int kind, float spw, float min_hess, int w
                     e->stream);
     e->kernel_launches += 1;
   }
+  // single-output dense growth reads its pairs from the row blocks
+  const uint32_t blk_pair = (!csr && e->n_out == 1 && e->c.blk) ? e->c.blk_pair : 0u;
   launch_gradients(kind, e->margin.p, e->label.p, e->weight_key ? e->weight.p : nullptr, spw,
                    min_hess, e->c.n_rows, vector_rows(e), e->gpair.p, e->scale.p,
                    csr ? nullptr : e->wtree.p, e->ls.p + walk_ls, walk_nodes, e->rec.p, e->c.stride,
-                   e->c.mask_off, e->flags.p, e->n_sm, e->stream);
+                   e->c.mask_off, e->c.blk, blk_pair, e->flags.p, e->n_sm, e->stream);
+  e->blk_pairs = blk_pair != 0;
   mark_end(e);
   e->pending_tree = false;
   e->kernel_launches += 2;  // gradients (+ last tree's leaves) + scale
@@ -408,7 +418,7 @@ hb_status grow_device(hb_engine* e, const hb_train_params* p, bool to_forest) {
   const size_t smem = hist_smem_bytes(c);
   const int hgrid = hist_grid(e->n_sm);
   mark_begin(e, T_ROOT);
-  launch_hist(c, e->fo.p, e->rec.p, cur_gpair(e), cur_scale(e), nullptr, e->entries.p, e->ls.p, hist,
+  launch_hist(c, e->fo.p, e->rec.p, hist_gpair(e), cur_scale(e), nullptr, e->entries.p, e->ls.p, hist,
               totals, e->row_stats.p, hgrid, smem, s);
   mark_end(e);
   HB_CK(e, cudaGetLastError());
@@ -464,7 +474,7 @@ hb_status grow_device(hb_engine* e, const hb_train_params* p, bool to_forest) {
                         nx, rows_in, d == 0, rows_out, s);
     mark_end(e);
     mark_begin(e, T_HIST);
-    launch_hist(c, e->fo.p, e->rec.p, cur_gpair(e), cur_scale(e), rows_out, e->entries.p, lsn, hist,
+    launch_hist(c, e->fo.p, e->rec.p, hist_gpair(e), cur_scale(e), rows_out, e->entries.p, lsn, hist,
                 nullptr, e->row_stats.p, hgrid, smem, s);
     mark_end(e);
     if (e->comm) {
@@ -564,7 +574,7 @@ hb_status grow_lossguide(hb_engine* e, const hb_train_params* p, bool to_forest)
   const size_t smem = hist_smem_bytes(c);
   const int hgrid = hist_grid(e->n_sm);
   mark_begin(e, T_ROOT);
-  launch_hist(c, e->fo.p, e->rec.p, cur_gpair(e), cur_scale(e), nullptr, e->entries.p, ls0, hist, totals,
+  launch_hist(c, e->fo.p, e->rec.p, hist_gpair(e), cur_scale(e), nullptr, e->entries.p, ls0, hist, totals,
               e->row_stats.p, hgrid, smem, s);
   mark_end(e);
   launch_root_stats(fr, totals, s);
@@ -600,7 +610,7 @@ hb_status grow_lossguide(hb_engine* e, const hb_train_params* p, bool to_forest)
                         rows1, 0, rows0, s);
     mark_end(e);
     mark_begin(e, T_HIST);
-    launch_hist(c, e->fo.p, e->rec.p, cur_gpair(e), cur_scale(e), rows0, e->entries.p, ls2, hist, nullptr,
+    launch_hist(c, e->fo.p, e->rec.p, hist_gpair(e), cur_scale(e), rows0, e->entries.p, ls2, hist, nullptr,
                 e->row_stats.p, hgrid, smem, s);
     mark_end(e);
     mark_begin(e, T_SCAN);
@@ -718,6 +728,7 @@ hb_status hb_engine_create(int32_t device_ordinal, hb_engine** out) {
   cudaEventCreate(&e->run_ev[1]);
   const char* ng = std::getenv("HB_NO_GRAPHS");
   e->use_graphs = !(ng && ng[0] == '1');
+
   if (e->scale.alloc(1) != cudaSuccess || e->tree_counter.alloc(1) != cudaSuccess ||
       e->seg_total.alloc(2) != cudaSuccess || e->row_stats.alloc(2) != cudaSuccess ||
       cudaMemset(e->row_stats.p, 0, 16) != cudaSuccess || e->flags.alloc(4) != cudaSuccess ||
@@ -911,6 +922,7 @@ static hb_status upload_index(hb_engine* e, const hb_ghist* g, const RawSource* 
   DevConst& c = e->c;
   const uint64_t shard_rows = e->shard_global;
   c = DevConst{};
+  e->blk_pairs = false;
   c.n_rows = g->n_rows;
   c.global_rows = shard_rows > g->n_rows ? shard_rows : g->n_rows;
   c.n_cols = g->n_cols;
@@ -956,7 +968,11 @@ static hb_status upload_index(hb_engine* e, const hb_ghist* g, const RawSource* 
     return finish_upload(e);
   }
   HB_CK(e, e->col.alloc((size_t)c.n_cols * n));
-  HB_CK(e, e->rec.alloc((size_t)c.stride * n + 64));
+  // HB_ROW_BLOCKS=0 keeps records `stride` apart and the pairs apart
+  const char* rb = std::getenv("HB_ROW_BLOCKS");
+  c.blk = (rb && rb[0] == '0') ? 0u : block_rows(c.stride);
+  c.blk_pair = c.blk * c.stride;
+  HB_CK(e, e->rec.alloc(rec_bytes(n, c.stride, c.blk)));
   if (e->has_missing) HB_CK(e, e->colmiss.alloc((size_t)c.n_cols * words));
   HB_CK(e, e->gpair.alloc(n));
   HB_CK(e, e->margin.alloc(n));
@@ -985,9 +1001,9 @@ static hb_status upload_index(hb_engine* e, const hb_ghist* g, const RawSource* 
       HB_CK(e, cudaMemcpyAsync(e->colmiss.p, g->missing, 8 * (size_t)c.n_cols * words,
                                cudaMemcpyHostToDevice, s));
   }
-  HB_CK(e, cudaMemsetAsync(e->rec.p, 0, (size_t)c.stride * n + 64, s));
+  HB_CK(e, cudaMemsetAsync(e->rec.p, 0, rec_bytes(n, c.stride, c.blk), s));
   launch_encode(e->col.p, e->has_missing ? e->colmiss.p : nullptr, n, c.n_cols, c.stride,
-                c.mask_off, e->rec.p, s);
+                c.mask_off, c.blk, e->rec.p, s);
   HB_CK(e, cudaGetLastError());
   HB_CK(e, cudaStreamSynchronize(s));
   e->csr_ptr.release();
@@ -1111,6 +1127,7 @@ hb_status hb_prepare(hb_engine* e, const hb_grad_pair* gpair, uint64_t n) {
   if (!gpair || n != e->c.n_rows) return HB_INVALID_ARGUMENT;
   cudaStream_t s = e->stream;
   HB_CK(e, cudaMemcpyAsync(e->gpair.p, gpair, 8 * n, cudaMemcpyHostToDevice, s));
+  e->blk_pairs = false;
   HB_CK(e, cudaMemsetAsync(e->scale.p, 0, sizeof(Scale), s));
   launch_pair_maxima(e->gpair.p, n, e->scale.p, e->n_sm, s);
   HB_CK(e, cudaGetLastError());
@@ -1708,7 +1725,8 @@ static hb_status round_work(hb_engine* e, const hb_train_params* p) {
     }
     launch_softmax_gradients(e->n_out, e->margin.p, e->label.p, e->c.n_rows, 1e-16f, e->gpair.p,
                              e->scale.p, e->wtree.p, (uint32_t)e->wstride, e->rec.p, e->c.stride,
-                             e->c.mask_off, e->c.csr ? nullptr : e->flags.p, e->n_sm, s);
+                             e->c.mask_off, e->c.blk, e->c.csr ? nullptr : e->flags.p, e->n_sm, s);
+    e->blk_pairs = false;
     mark_end(e);
     HB_CK(e, cudaGetLastError());
     e->pending_tree = false;

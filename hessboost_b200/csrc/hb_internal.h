@@ -1,11 +1,12 @@
 // Internal declarations shared by the engine (host) and the kernels.
 //
 // Data layout in HBM (one engine = one GPU = one shard of rows):
-//   rec      [n_rows][stride] u8   row-major record: the feature-local bins
-//                                  (one byte per feature) followed by the
-//                                  missing mask (one bit per feature, u32
-//                                  words at mask_off); what the histogram
-//                                  kernels gather by row
+//   rec      row-major records: the feature-local bins (one byte per
+//            feature) followed by the missing mask (one bit per feature, u32
+//            words at mask_off), `stride` bytes a row; what the histogram
+//            kernels gather by row. Records of at most 48 bytes sit in row
+//            blocks: 128-byte lines of blk records and then those rows'
+//            (g, h) pairs (rec_offset, pair_offset)
 //   col      [n_cols][n_rows] u8   feature-major bins: what the partition
 //                                  reads for the split feature
 //   colmiss  [n_cols][words] u64   missing bitmap, feature-major
@@ -55,6 +56,11 @@ struct DevConst {
   uint32_t max_bins;      // largest per-feature bin count
   uint32_t stride;        // record bytes
   uint32_t mask_off;      // byte offset of the mask words in a record
+  // Row blocks (blk = 2, 3 or 5): each 128-byte line of the record array
+  // holds blk records and then those rows' (g, h) pairs, so a gathered row
+  // costs one line; blk = 0: records `stride` bytes apart, pairs elsewhere.
+  uint32_t blk;
+  uint32_t blk_pair;      // byte offset of a line's pairs (blk * stride)
   uint32_t dense;         // index-level: no missing cell anywhere
   uint32_t n_groups;      // feature groups of kGroupFeatures
   uint32_t hist64;        // 1: always the 64-bit-atomic histogram kernel
@@ -73,6 +79,34 @@ struct DevConst {
   // memory, or NULL when no feature is constrained
   const int8_t* mono;
 };
+
+constexpr uint32_t kBlockBytes = 128;
+
+
+// Rows per 128-byte block for a record width: records and their 8-byte pairs
+// must fit one line, at least two rows to it.
+inline uint32_t block_rows(uint32_t stride) {
+  return stride == 16 ? 5u : stride == 32 ? 3u : stride == 48 ? 2u : 0u;
+}
+
+// Byte offset of row r's record, and of its (g, h) pair inside the row
+// blocks (blk != 0).
+__host__ __device__ __forceinline__ uint32_t block_of(uint32_t r, uint32_t blk) {
+  return blk == 3u ? r / 3u : blk == 2u ? r >> 1 : r / 5u;
+}
+__host__ __device__ __forceinline__ uint64_t rec_offset(uint32_t r, uint32_t stride, uint32_t blk) {
+  if (!blk) return (uint64_t)r * stride;
+  const uint32_t q = block_of(r, blk);
+  return (uint64_t)q * kBlockBytes + (r - q * blk) * stride;
+}
+__host__ __device__ __forceinline__ uint64_t pair_offset(uint32_t r, uint32_t blk, uint32_t blk_pair) {
+  const uint32_t q = block_of(r, blk);
+  return (uint64_t)q * kBlockBytes + blk_pair + (r - q * blk) * 8u;
+}
+// Bytes of the record array for n rows (64 spare bytes for vector reads).
+inline uint64_t rec_bytes(uint64_t n, uint32_t stride, uint32_t blk) {
+  return (blk ? (n + blk - 1) / blk * kBlockBytes : n * stride) + 64;
+}
 
 // One frontier entry of the level being grown. The first 32 bytes are read
 // as two int4 by the histogram plan (load_front_cg), so every entry of a

@@ -13,6 +13,7 @@
 #include <cstdlib>
 #include <climits>
 #include <cmath>
+#include <vector>
 
 #include "hb_kernels.cuh"
 
@@ -213,14 +214,15 @@ __global__ void k_walk_csr(DevConst c, int K, const WNode* __restrict__ wtree, u
 // Add the previous tree's leaves to the margins: each row walks the tree
 // over its binned record (the partition's routing rule), in row order.
 __global__ void k_walk(const WNode* __restrict__ wtree, const LevelState* __restrict__ ls_last,
-                       const uint8_t* __restrict__ rec, uint32_t stride, uint32_t mask_off, uint64_t n,
-                       float* __restrict__ margin, const int* __restrict__ pending) {
+                       const uint8_t* __restrict__ rec, uint32_t stride, uint32_t mask_off, uint32_t blk,
+                       uint64_t n, float* __restrict__ margin, const int* __restrict__ pending) {
   extern __shared__ WNode s_tree[];
   if (!*pending) return;
   stage_tree(wtree, ls_last, s_tree);
   for (uint64_t i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n;
        i += (uint64_t)gridDim.x * blockDim.x) {
-    margin[i] = __fadd_rn(margin[i], walk_leaf(s_tree, rec + i * stride, stride, mask_off));
+    margin[i] = __fadd_rn(margin[i], walk_leaf(s_tree, rec + rec_offset((uint32_t)i, stride, blk), stride,
+                                               mask_off));
   }
 }
 
@@ -228,12 +230,15 @@ __global__ void k_gradients(int kind, float* __restrict__ margin,
                             const float* __restrict__ label, const float* __restrict__ weight,
                             float spw, float min_hess, uint64_t n, uint64_t vrows,
                             float2* __restrict__ gpair, Scale* scale, const WNode* __restrict__ wtree,
-                            const LevelState* __restrict__ ls_last, const uint8_t* __restrict__ rec,
-                            uint32_t stride, uint32_t mask_off, const int* __restrict__ pending) {
+                            const LevelState* __restrict__ ls_last, uint8_t* rec,
+                            uint32_t stride, uint32_t mask_off, uint32_t blk, uint32_t blk_pair,
+                            const int* __restrict__ pending) {
   extern __shared__ WNode s_tree[];
   if (wtree && !(pending && *pending)) wtree = nullptr;  // no tree waiting for the margins
   if (wtree) stage_tree(wtree, ls_last, s_tree);
-  const uint64_t pol_keep = l2_evict_last();  // the round's histogram launches re-read the pairs
+  // the round's histogram launches re-read the pairs: from the row blocks
+  // when there are any (blk_pair != 0), else from gpair, kept in L2
+  const uint64_t pol_keep = l2_evict_last();
   float mg = 0.0f, mh = 0.0f;
   bool nonfinite = false;
   const unsigned lane = threadIdx.x & 31;
@@ -243,7 +248,7 @@ __global__ void k_gradients(int kind, float* __restrict__ margin,
     bool in = i < n;
     float m = in ? margin[i] : 0.0f;
     if (wtree && in) {
-      m = __fadd_rn(m, walk_leaf(s_tree, rec + i * stride, stride, mask_off));
+      m = __fadd_rn(m, walk_leaf(s_tree, rec + rec_offset((uint32_t)i, stride, blk), stride, mask_off));
       margin[i] = m;
     }
     float y = in ? label[i] : 0.0f;
@@ -264,7 +269,19 @@ __global__ void k_gradients(int kind, float* __restrict__ margin,
       h = w;
     }
     if (in) {
-      st_hint8(gpair + i, make_float2(g, h), pol_keep);
+      if (blk_pair) {
+        // the pair into its row block; the block's last row also writes the
+        // zero tail of the line, so every sector of the pairs is written whole
+        gpair[i] = make_float2(g, h);
+        const uint32_t q = block_of((uint32_t)i, blk), j = (uint32_t)i - q * blk;
+        uint8_t* line = rec + (uint64_t)q * kBlockBytes;
+        *reinterpret_cast<float2*>(line + blk_pair + 8u * j) = make_float2(g, h);
+        if (j == blk - 1u)
+          for (uint32_t o = blk_pair + 8u * blk; o < kBlockBytes; o += 8u)
+            *reinterpret_cast<uint2*>(line + o) = make_uint2(0u, 0u);
+      } else {
+        st_hint8(gpair + i, make_float2(g, h), pol_keep);
+      }
       fold_max(g, h, mg, mh, nonfinite);
     }
   }
@@ -289,14 +306,14 @@ __global__ void k_softmax_gradients(int K, float* __restrict__ margin, const flo
                                     uint64_t n, float min_hess, float2* __restrict__ gpair,
                                     Scale* scale, const WNode* __restrict__ wtree, uint32_t wstride,
                                     const uint8_t* __restrict__ rec, uint32_t stride,
-                                    uint32_t mask_off, const int* __restrict__ pending) {
+                                    uint32_t mask_off, uint32_t blk, const int* __restrict__ pending) {
   __shared__ unsigned s_mg[kMaxClasses], s_mh[kMaxClasses], s_nf[kMaxClasses];
   for (int j = threadIdx.x; j < K; j += blockDim.x) s_mg[j] = s_mh[j] = s_nf[j] = 0u;
   __syncthreads();
   const bool walk = pending != nullptr && *pending != 0;
   const uint64_t step = (uint64_t)gridDim.x * blockDim.x;
   for (uint64_t i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += step) {
-    const uint8_t* rp = rec + i * stride;
+    const uint8_t* rp = rec + rec_offset((uint32_t)i, stride, blk);
     float wmax = FLT_MIN;
     for (int j = 0; j < K; ++j) {
       float v = margin[(uint64_t)j * n + i];
@@ -332,11 +349,12 @@ __global__ void k_softmax_gradients(int K, float* __restrict__ margin, const flo
 // trees, when *pending is set).
 __global__ void k_walk_classes(int K, const WNode* __restrict__ wtree, uint32_t wstride,
                                const uint8_t* __restrict__ rec, uint32_t stride, uint32_t mask_off,
-                               uint64_t n, float* __restrict__ margin, const int* __restrict__ pending) {
+                               uint32_t blk, uint64_t n, float* __restrict__ margin,
+                               const int* __restrict__ pending) {
   if (!*pending) return;
   for (uint64_t i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n;
        i += (uint64_t)gridDim.x * blockDim.x) {
-    const uint8_t* rp = rec + i * stride;
+    const uint8_t* rp = rec + rec_offset((uint32_t)i, stride, blk);
     for (int j = 0; j < K; ++j)
       margin[(uint64_t)j * n + i] = __fadd_rn(margin[(uint64_t)j * n + i],
                                              walk_leaf(wtree + (uint64_t)j * wstride, rp, stride, mask_off));
@@ -391,11 +409,11 @@ __global__ void k_scale(Scale* scale, uint64_t global_rows, int* pending) {
 // the layout the histogram gathers).
 __global__ void k_encode(const uint8_t* __restrict__ col, const uint64_t* __restrict__ colmiss,
                          uint64_t n_rows, uint32_t n_cols, uint32_t stride, uint32_t mask_off,
-                         uint8_t* __restrict__ rec) {
+                         uint32_t blk, uint8_t* __restrict__ rec) {
   const uint64_t words = (n_rows + 63) / 64;
   for (uint64_t r = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; r < n_rows;
        r += (uint64_t)gridDim.x * blockDim.x) {
-    uint32_t* out = reinterpret_cast<uint32_t*>(rec + r * stride);
+    uint32_t* out = reinterpret_cast<uint32_t*>(rec + rec_offset((uint32_t)r, stride, blk));
     uint32_t word = 0;
     for (uint32_t f = 0; f < n_cols; ++f) {
       word |= (uint32_t)col[(uint64_t)f * n_rows + r] << ((f & 3) * 8);
@@ -551,11 +569,12 @@ __global__ void __launch_bounds__(kHistThreads, 1)
     for (uint64_t i = pos + threadIdx.x; i < end_e; i += blockDim.x) {
       const uint32_t at = en.begin + (uint32_t)(i - en.prefix);
       const uint32_t row = en.identity ? at : rows[at];
-      const uint8_t* rp = rec + (uint64_t)row * c.stride;
+      const uint8_t* rp = rec + rec_offset(row, c.stride, c.blk);
       const uint4 v0 = *reinterpret_cast<const uint4*>(rp + 32 * g);
       const uint4 v1 = wide ? *reinterpret_cast<const uint4*>(rp + 32 * g + 16) : make_uint4(0, 0, 0, 0);
       const uint32_t mask = *reinterpret_cast<const uint32_t*>(rp + c.mask_off + 4 * g);
-      const float2 p = gpair[row];
+      const float2 p = gpair ? gpair[row]
+                             : *reinterpret_cast<const float2*>(rec + pair_offset(row, c.blk, c.blk_pair));
       const long long qg = __double2ll_rn((double)p.x * fg);
       const long long qh = __double2ll_rn((double)p.y * fh);
       if (want_totals) {
@@ -644,7 +663,11 @@ struct H32 {
   }
 };
 
-template <int G>
+// BLK: the record layout (c.blk: 0, or 2, 3, 5 rows a 128-byte block, whose
+// record widths are then 48, 32, 16 bytes), a compile-time constant so that
+// the row addressing folds; PIB: each row's pair comes from its row block
+// instead of `gpair`.
+template <int G, int BLK, bool PIB>
 __global__ void __launch_bounds__(kH32Threads, 1)
     k_hist32(DevConst c, const uint32_t* __restrict__ fo, const uint8_t* __restrict__ rec,
              const float2* __restrict__ gpair, const Scale* __restrict__ scale,
@@ -654,6 +677,8 @@ __global__ void __launch_bounds__(kH32Threads, 1)
              int flush_rows) {
   constexpr int kSt = H32<G>::kStages;
   constexpr int kBS = H32<G>::kBinShift;
+  constexpr uint32_t kRecW = BLK == 5 ? 16u : BLK == 3 ? 32u : BLK == 2 ? 48u : 0u;
+  static_assert(!PIB || BLK != 0, "pairs in row blocks need the block layout");
   extern __shared__ __align__(16) uint32_t s32[];
   const int n_entries = ls->n_hentries;
   const uint64_t total = ls->hist_rows;
@@ -755,7 +780,7 @@ __global__ void __launch_bounds__(kH32Threads, 1)
     auto issue = [&](int it, uint32_t row, bool valid) {
       const int st = it % kSt;
       if (valid) {
-        const uint8_t* rr = rec + (uint64_t)row * c.stride;
+        const uint8_t* rr = rec + (BLK ? rec_offset(row, kRecW, BLK) : (uint64_t)row * c.stride);
 #pragma unroll
         for (int lg = 0; lg < G; ++lg) {
           if (lg < ng) {
@@ -767,7 +792,10 @@ __global__ void __launch_bounds__(kH32Threads, 1)
               __pipeline_memcpy_async(&smask[(st * G + lg) * kH32Threads + tid], rr + mask_at[lg], 4);
           }
         }
-        __pipeline_memcpy_async(&sgp[st * kH32Threads + tid], &gpair[row], 8);
+        if (PIB)
+          __pipeline_memcpy_async(&sgp[st * kH32Threads + tid], rec + pair_offset(row, BLK, BLK * kRecW), 8);
+        else
+          __pipeline_memcpy_async(&sgp[st * kH32Threads + tid], &gpair[row], 8);
       }
       __pipeline_commit();
     };
@@ -914,6 +942,35 @@ __global__ void __launch_bounds__(kH32Threads, 1)
       atomicAdd(reinterpret_cast<unsigned long long*>(&totals[1]), (unsigned long long)sht);
     }
   }
+}
+
+// The k_hist32 instantiation for G groups a CTA, record layout blk and the
+// pairs' source (pib: the row blocks). Two groups a CTA need 33 or more
+// features, so 48-byte records (blk 2) or wider (blk 0).
+using H32Fn = void (*)(DevConst, const uint32_t*, const uint8_t*, const float2*, const Scale*,
+                       const uint32_t*, const HEntry*, const LevelState*, longlong2*, long long*,
+                       unsigned long long*, int, int);
+
+static H32Fn h32_fn(int G, uint32_t blk, bool pib) {
+  if (G == 2) {
+    if (blk == 2) return pib ? k_hist32<2, 2, true> : k_hist32<2, 2, false>;
+    return blk == 0 ? k_hist32<2, 0, false> : nullptr;
+  }
+  switch (blk) {
+    case 2: return pib ? k_hist32<1, 2, true> : k_hist32<1, 2, false>;
+    case 3: return pib ? k_hist32<1, 3, true> : k_hist32<1, 3, false>;
+    case 5: return pib ? k_hist32<1, 5, true> : k_hist32<1, 5, false>;
+    default: return k_hist32<1, 0, false>;
+  }
+}
+
+static std::vector<const void*> h32_kernels() {
+  std::vector<const void*> v;
+  for (int G = 1; G <= 2; ++G)
+    for (uint32_t blk : {0u, 2u, 3u, 5u})
+      for (bool pib : {false, true})
+        if (H32Fn f = (pib && blk == 0) ? nullptr : h32_fn(G, blk, pib)) v.push_back((const void*)f);
+  return v;
 }
 
 // sibling = parent - built (int64, exact; src/tree/hist/mod.rs:32).
@@ -2132,7 +2189,7 @@ __global__ void __launch_bounds__(kPartThreads)
       miss[j] = !csr_find(c.csr_bins, __ldg(c.csr_ptr + r), __ldg(c.csr_ptr + r + 1), csr_lo, csr_hi, lb);
       bin[j] = lb;
     } else if (use_record) {
-      const uint8_t* rp = rec + (uint64_t)r * c.stride;
+      const uint8_t* rp = rec + rec_offset(r, c.stride, c.blk);
       bin[j] = rp[d.feature];
       miss[j] = (*reinterpret_cast<const uint32_t*>(rp + mword) >> mbit) & 1u;
     } else {
@@ -2487,37 +2544,37 @@ void launch_seg_total(const uint32_t* rows, uint64_t begin, uint64_t len, const 
 void launch_gradients(int kind, float* margin, const float* label, const float* weight, float spw,
                       float min_hess, uint64_t n, uint64_t vrows, float2* gpair, Scale* scale,
                       const WNode* wtree, const LevelState* ls_last, int max_nodes,
-                      const uint8_t* rec, uint32_t stride, uint32_t mask_off, const int* pending,
-                      int n_sm, cudaStream_t s) {
+                      uint8_t* rec, uint32_t stride, uint32_t mask_off, uint32_t blk, uint32_t blk_pair,
+                      const int* pending, int n_sm, cudaStream_t s) {
   int grid = (int)std::min<uint64_t>((n + 255) / 256, (uint64_t)n_sm * 8);
   if (grid < 1) grid = 1;
   const size_t smem = wtree ? sizeof(WNode) * (size_t)max_nodes : 0;
   k_gradients<<<grid, 256, smem, s>>>(kind, margin, label, weight, spw, min_hess, n, vrows, gpair, scale,
-                                      wtree, ls_last, rec, stride, mask_off, pending);
+                                      wtree, ls_last, rec, stride, mask_off, blk, blk_pair, pending);
 }
 
 void launch_walk(const WNode* wtree, const LevelState* ls_last, int max_nodes, const uint8_t* rec,
-                 uint32_t stride, uint32_t mask_off, uint64_t n, float* margin, const int* pending,
-                 int n_sm, cudaStream_t s) {
+                 uint32_t stride, uint32_t mask_off, uint32_t blk, uint64_t n, float* margin,
+                 const int* pending, int n_sm, cudaStream_t s) {
   int grid = (int)std::min<uint64_t>((n + 255) / 256, (uint64_t)n_sm * 8);
   if (grid < 1) grid = 1;
-  k_walk<<<grid, 256, sizeof(WNode) * (size_t)max_nodes, s>>>(wtree, ls_last, rec, stride, mask_off, n,
-                                                              margin, pending);
+  k_walk<<<grid, 256, sizeof(WNode) * (size_t)max_nodes, s>>>(wtree, ls_last, rec, stride, mask_off, blk,
+                                                              n, margin, pending);
 }
 
 void hist_configure() {
   cudaFuncSetAttribute(k_hist, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024 - 1024);
-  cudaFuncSetAttribute(k_hist32<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024 - 1024);
-  cudaFuncSetAttribute(k_hist32<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024 - 1024);
+  for (const void* f : h32_kernels())
+    cudaFuncSetAttribute(f, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024 - 1024);
 }
 
 void launch_softmax_gradients(int K, float* margin, const float* label, uint64_t n, float min_hess,
                               float2* gpair, Scale* scale, const WNode* wtree, uint32_t wstride,
-                              const uint8_t* rec, uint32_t stride, uint32_t mask_off,
+                              const uint8_t* rec, uint32_t stride, uint32_t mask_off, uint32_t blk,
                               const int* pending, int n_sm, cudaStream_t s) {
   const int grid = (int)std::max<uint64_t>(1, std::min<uint64_t>((n + 255) / 256, (uint64_t)n_sm * 8));
   k_softmax_gradients<<<grid, 256, 0, s>>>(K, margin, label, n, min_hess, gpair, scale, wtree,
-                                           wstride, rec, stride, mask_off, pending);
+                                           wstride, rec, stride, mask_off, blk, pending);
 }
 
 void launch_walk_csr(const DevConst& c, int K, const WNode* wtree, uint32_t wstride, float* margin,
@@ -2527,10 +2584,10 @@ void launch_walk_csr(const DevConst& c, int K, const WNode* wtree, uint32_t wstr
 }
 
 void launch_walk_classes(int K, const WNode* wtree, uint32_t wstride, const uint8_t* rec,
-                         uint32_t stride, uint32_t mask_off, uint64_t n, float* margin,
+                         uint32_t stride, uint32_t mask_off, uint32_t blk, uint64_t n, float* margin,
                          const int* pending, int n_sm, cudaStream_t s) {
   const int grid = (int)std::max<uint64_t>(1, std::min<uint64_t>((n + 255) / 256, (uint64_t)n_sm * 8));
-  k_walk_classes<<<grid, 256, 0, s>>>(K, wtree, wstride, rec, stride, mask_off, n, margin, pending);
+  k_walk_classes<<<grid, 256, 0, s>>>(K, wtree, wstride, rec, stride, mask_off, blk, n, margin, pending);
 }
 
 void launch_pair_maxima(const float2* gpair, uint64_t n, Scale* scale, int n_sm, cudaStream_t s) {
@@ -2544,10 +2601,10 @@ void launch_scale(Scale* scale, uint64_t global_rows, int* pending, cudaStream_t
 }
 
 void launch_encode(const uint8_t* col, const uint64_t* colmiss, uint64_t n_rows, uint32_t n_cols,
-                   uint32_t stride, uint32_t mask_off, uint8_t* rec, cudaStream_t s) {
+                   uint32_t stride, uint32_t mask_off, uint32_t blk, uint8_t* rec, cudaStream_t s) {
   int grid = (int)std::min<uint64_t>((n_rows + 255) / 256, 4096);
   if (grid < 1) grid = 1;
-  k_encode<<<grid, 256, 0, s>>>(col, colmiss, n_rows, n_cols, stride, mask_off, rec);
+  k_encode<<<grid, 256, 0, s>>>(col, colmiss, n_rows, n_cols, stride, mask_off, blk, rec);
 }
 
 // The split of the 32-bit kernel for `global_rows` rows: lo bits K and the
@@ -2608,23 +2665,18 @@ void launch_hist(const DevConst& c, const uint32_t* fo, const uint8_t* rec, cons
   }
   dim3 grid(grid_x, c.n_groups);
   if (use_hist32(c)) {
-    const int G = hist_groups_per_cta(c);
-    static size_t granted32[2][64] = {{0}};
-    if (dev < 0 || dev >= 64 || granted32[G - 1][dev] < smem) {
-      if (cudaFuncSetAttribute(G == 2 ? (const void*)k_hist32<2> : (const void*)k_hist32<1>,
-                               cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) == cudaSuccess &&
-          dev >= 0 && dev < 64)
-        granted32[G - 1][dev] = smem;
+    // every instantiation was granted its shared memory by hist_configure
+    int G = hist_groups_per_cta(c);
+    H32Fn f = h32_fn(G, c.blk, gpair == nullptr);
+    if (!f) {
+      G = 1;
+      f = h32_fn(1, c.blk, gpair == nullptr);
     }
     int K, R;
     split_for_rows(c.global_rows, K, R);
     grid.y = (c.n_groups + G - 1) / G;
-    if (G == 2)
-      k_hist32<2><<<grid, kH32Threads, smem, s>>>(c, fo, rec, gpair, scale, rows, entries, ls, hist,
-                                                  totals, row_stats, K, R);
-    else
-      k_hist32<1><<<grid, kH32Threads, smem, s>>>(c, fo, rec, gpair, scale, rows, entries, ls, hist,
-                                                  totals, row_stats, K, R);
+    f<<<grid, kH32Threads, smem, s>>>(c, fo, rec, gpair, scale, rows, entries, ls, hist, totals, row_stats,
+                                      K, R);
     return;
   }
   k_hist<<<grid, kHistThreads, smem, s>>>(c, fo, rec, gpair, scale, rows, entries, ls, hist, totals,

@@ -10,29 +10,30 @@ namespace hb {
 // Objective gradients at `margin` (the host's bits, see hb_kernels.cu) plus
 // the largest |g|, |h| and a non-finite flag, folded into `scale`.
 // With `wtree` and *pending set, each row first adds its leaf of that tree
-// to its margin.
+// to its margin. With blk_pair != 0 each pair is also written into the
+// row's block (blk rows a 128-byte line of `rec`).
 void launch_gradients(int kind, float* margin, const float* label, const float* weight, float spw,
                       float min_hess, uint64_t n, uint64_t vrows, float2* gpair, Scale* scale,
                       const WNode* wtree, const LevelState* ls_last, int max_nodes,
-                      const uint8_t* rec, uint32_t stride, uint32_t mask_off, const int* pending,
-                      int n_sm, cudaStream_t s);
+                      uint8_t* rec, uint32_t stride, uint32_t mask_off, uint32_t blk, uint32_t blk_pair,
+                      const int* pending, int n_sm, cudaStream_t s);
 // When *pending is set, add each row's leaf of `wtree` to its margin.
 void launch_walk(const WNode* wtree, const LevelState* ls_last, int max_nodes, const uint8_t* rec,
-                 uint32_t stride, uint32_t mask_off, uint64_t n, float* margin, const int* pending,
-                 int n_sm, cudaStream_t s);
+                 uint32_t stride, uint32_t mask_off, uint32_t blk, uint64_t n, float* margin,
+                 const int* pending, int n_sm, cudaStream_t s);
 // multi:softmax gradients of K classes (class-major margins and pairs,
 // K <= 64), first adding each class's pending tree when *pending is set;
 // per-class maxima into scale[0..K).
 void launch_softmax_gradients(int K, float* margin, const float* label, uint64_t n, float min_hess,
                               float2* gpair, Scale* scale, const WNode* wtree, uint32_t wstride,
-                              const uint8_t* rec, uint32_t stride, uint32_t mask_off,
+                              const uint8_t* rec, uint32_t stride, uint32_t mask_off, uint32_t blk,
                               const int* pending, int n_sm, cudaStream_t s);
 // When *pending is set, add each class's tree leaves to its margins.
 // The pending trees' leaves added to the margins of a CSR index's rows.
 void launch_walk_csr(const DevConst& c, int K, const WNode* wtree, uint32_t wstride, float* margin,
                      const int* pending, int n_sm, cudaStream_t s);
 void launch_walk_classes(int K, const WNode* wtree, uint32_t wstride, const uint8_t* rec,
-                         uint32_t stride, uint32_t mask_off, uint64_t n, float* margin,
+                         uint32_t stride, uint32_t mask_off, uint32_t blk, uint64_t n, float* margin,
                          const int* pending, int n_sm, cudaStream_t s);
 // |g|, |h| maxima of staged pairs (HistogramBackend::prepare).
 void launch_pair_maxima(const float2* gpair, uint64_t n, Scale* scale, int n_sm, cudaStream_t s);
@@ -44,9 +45,10 @@ void launch_scale(Scale* scale, uint64_t global_rows, int* pending, cudaStream_t
 void hist_configure();
 // Feature-major bins (+ bitmap) -> row-major records.
 void launch_encode(const uint8_t* col, const uint64_t* colmiss, uint64_t n_rows, uint32_t n_cols,
-                   uint32_t stride, uint32_t mask_off, uint8_t* rec, cudaStream_t s);
+                   uint32_t stride, uint32_t mask_off, uint32_t blk, uint8_t* rec, cudaStream_t s);
 // Histograms of `entries` (level state `ls`) into `hist`; with `totals`
-// non-null also the fixed-point (g, h) totals of the rows.
+// non-null also the fixed-point (g, h) totals of the rows. A null `gpair`
+// reads each row's pair from its row block (c.blk != 0).
 void launch_hist(const DevConst& c, const uint32_t* fo, const uint8_t* rec, const float2* gpair,
                  const Scale* scale, const uint32_t* rows, const HEntry* entries,
                  const LevelState* ls, longlong2* hist, long long* totals,

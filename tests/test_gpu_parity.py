@@ -596,6 +596,23 @@ def test_histogram_kernels_agree(monkeypatch, n_cols, max_bin):
     assert_forest_equal(runs[0].nodes, runs[0].tree_ptr, runs[1].nodes, runs[1].tree_ptr, "32 vs 64")
 
 
+@pytest.mark.parametrize("n_cols,grow", [(6, "depthwise"), (28, "depthwise"), (28, "lossguide"), (40, "depthwise")])
+def test_row_block_layout_agrees(monkeypatch, n_cols, grow):
+    """Records in row blocks (5, 3 and 2 rows and their pairs to a 128-byte
+    line for 16-, 32- and 48-byte records) and records apart with the pairs
+    in their own array give the same forests and margins."""
+    x, y = synth.logistic_c2(250_007, n_cols, seed=40 + n_cols)
+    kw = dict(objective="binary:logistic", max_depth=7, eta=0.2)
+    if grow == "lossguide":
+        kw.update(grow_policy="lossguide", max_depth=0, max_leaves=40)
+    runs = []
+    for layout in ("1", "0"):
+        monkeypatch.setenv("HB_ROW_BLOCKS", layout)
+        runs.append(gpu_train(x, y, 3, **kw))
+    assert_forest_equal(runs[0].nodes, runs[0].tree_ptr, runs[1].nodes, runs[1].tree_ptr, "blocks vs apart")
+    np.testing.assert_array_equal(_bits(runs[0].predict_margin(x)), _bits(runs[1].predict_margin(x)))
+
+
 @pytest.mark.parametrize("max_bin", [16, 48, 128])
 def test_scan_kernels_agree(monkeypatch, max_bin):
     """The warp-per-feature split scan (features of <= 128 bins) and the
