@@ -104,6 +104,7 @@ struct hb_engine {
   bool pending_tree = false;  // host mirror of flags[0]: a grown tree's leaves await the margins
   int walk_ls = 1;            // the pending tree: e->ls index holding its node count
   int walk_nodes = 2;         // and the capacity of its WNode array
+  int walk_depth = 0;         // and its depth bound (depthwise growth; 0: none)
   DevBuf<int> flags;          // [0]: pending tree (read by the next gradient or walk kernel)
   // the captured round (CUDA graph) and what it was captured for
   cudaGraphExec_t round_exec = nullptr;
@@ -341,12 +342,13 @@ hb_status flush_pending(hb_engine* e) {
 // Gradients at the margins, first adding a pending tree's leaves when the
 // device flag says one waits (so a captured round serves every round).
 hb_status run_gradients(hb_engine* e, int kind, float spw, float min_hess, int walk_ls,
-                        int walk_nodes) {
+                        int walk_nodes, int walk_depth) {
   HB_CK(e, cudaMemsetAsync(e->scale.p, 0, sizeof(Scale), e->stream));
   mark_begin(e, T_GRAD);
   if (walk_ls < 0) {
     walk_ls = e->walk_ls;
     walk_nodes = e->walk_nodes;
+    walk_depth = e->walk_depth;
   }
   const bool csr = e->c.csr != 0;
   if (csr) {  // the pending tree's walk over CSR rows first
@@ -358,7 +360,7 @@ hb_status run_gradients(hb_engine* e, int kind, float spw, float min_hess, int w
   const uint32_t blk_pair = (!csr && e->n_out == 1 && e->c.blk) ? e->c.blk_pair : 0u;
   launch_gradients(kind, e->margin.p, e->label.p, e->weight_key ? e->weight.p : nullptr, spw,
                    min_hess, e->c.n_rows, vector_rows(e), e->gpair.p, e->scale.p,
-                   csr ? nullptr : e->wtree.p, e->ls.p + walk_ls, walk_nodes, e->rec.p, e->c.stride,
+                   csr ? nullptr : e->wtree.p, e->ls.p + walk_ls, walk_nodes, walk_depth, e->rec.p, e->c.stride,
                    e->c.mask_off, e->c.blk, blk_pair, e->flags.p, e->n_sm, e->stream);
   e->blk_pairs = blk_pair != 0;
   mark_end(e);
@@ -378,13 +380,15 @@ int lg_leaves(const hb_train_params* p) {
 
 // Where a grown tree's node count lives (an e->ls index) and how many nodes
 // its WNode array can hold: what the next pass's tree walk needs.
-void walk_shape(const hb_train_params* p, int& ls_index, int& nodes) {
+void walk_shape(const hb_train_params* p, int& ls_index, int& nodes, int& depth) {
   if (p->grow_policy == HB_GROW_LOSSGUIDE) {
     ls_index = 2;
     nodes = 2 * lg_leaves(p);
+    depth = 0;
   } else {
     ls_index = p->max_depth + 1;
     nodes = 2 << p->max_depth;
+    depth = p->max_depth;
   }
 }
 
@@ -491,6 +495,7 @@ hb_status grow_device(hb_engine* e, const hb_train_params* p, bool to_forest) {
   e->pending_tree = true;
   e->walk_ls = D + 1;
   e->walk_nodes = 2 << D;
+  e->walk_depth = D;
   if (to_forest) {
     launch_finish_tree(e->tree.p, e->ls.p + D + 1, e->forest.p, e->counts.p, e->tree_counter.p,
                        (uint32_t)(2u << D), s);
@@ -621,7 +626,7 @@ hb_status grow_lossguide(hb_engine* e, const hb_train_params* p, bool to_forest)
   }
   HB_CK(e, cudaMemsetAsync(e->flags.p, 0x01, sizeof(int), s));
   e->pending_tree = true;
-  walk_shape(p, e->walk_ls, e->walk_nodes);
+  walk_shape(p, e->walk_ls, e->walk_nodes, e->walk_depth);
   if (to_forest) {
     launch_finish_tree(e->tree.p, ls2, e->forest.p, e->counts.p, e->tree_counter.p,
                        (uint32_t)n_nodes, s);
@@ -1469,7 +1474,7 @@ hb_status hb_gradients(hb_engine* e, const hb_device_loss* loss, const float* la
   if (e->row_begin % 8) return refuse(e, "shards must start on a multiple of 8 rows");
   hb_status st = stage_labels(e, labels, weights, n);
   if (st != HB_OK) return st;
-  st = run_gradients(e, loss->kind, loss->scale_pos_weight, loss->min_hess, -1, 0);
+  st = run_gradients(e, loss->kind, loss->scale_pos_weight, loss->min_hess, -1, 0, 0);
   if (st != HB_OK) return st;
   Scale h;
   HB_CK(e, cudaMemcpyAsync(&h, e->scale.p, sizeof(Scale), cudaMemcpyDeviceToHost, e->stream));
@@ -1745,9 +1750,9 @@ static hb_status round_work(hb_engine* e, const hb_train_params* p) {
     e->staged = true;
     return HB_OK;
   }
-  int wl = 0, wn = 0;
-  walk_shape(p, wl, wn);
-  hb_status st = run_gradients(e, p->objective, p->scale_pos_weight, 1e-16f, wl, wn);
+  int wl = 0, wn = 0, wd = 0;
+  walk_shape(p, wl, wn, wd);
+  hb_status st = run_gradients(e, p->objective, p->scale_pos_weight, 1e-16f, wl, wn, wd);
   if (st != HB_OK) return st;
   return grow_tree_device(e, p, true);
 }
@@ -1836,7 +1841,7 @@ static hb_status graph_rounds(hb_engine* e, const hb_train_params* p, int rounds
   }
   HB_CK(e, cudaEventRecord(e->run_ev[1], s));
   e->pending_tree = true;
-  walk_shape(p, e->walk_ls, e->walk_nodes);
+  walk_shape(p, e->walk_ls, e->walk_nodes, e->walk_depth);
   return HB_OK;
 }
 

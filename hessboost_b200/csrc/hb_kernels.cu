@@ -13,6 +13,7 @@
 #include <cstdlib>
 #include <climits>
 #include <cmath>
+#include <utility>
 #include <vector>
 
 #include "hb_kernels.cuh"
@@ -26,6 +27,34 @@ constexpr float kBelowAll = -FLT_MAX;         // src/tree/builder/mod.rs:308
 constexpr double kRtEps = 1e-6;               // src/lib.rs:366
 
 __device__ __forceinline__ double ll2d(long long v) { return __ll2double_rn(v); }
+
+// Kernels of the round are launched with programmatic stream serialization
+// (launch_pdl): a kernel may be scheduled while the one before it on the
+// stream finishes, so each begins by waiting for that kernel's completion
+// and memory (griddepcontrol.wait, a no-op after a plain launch). This
+// hides the launch latency between the round's dependent kernels.
+__device__ __forceinline__ void pdl_wait() {
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  // let the next kernel be scheduled now: it waits for this one in turn
+  asm volatile("griddepcontrol.launch_dependents;");
+}
+
+bool g_pdl = true;  // HB_NO_PDL=1: plain launches
+
+template <typename... P, typename... A>
+static void launch_pdl(void (*kernel)(P...), dim3 grid, dim3 block, size_t smem, cudaStream_t s, A&&... args) {
+  cudaLaunchAttribute at[1];
+  at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  at[0].val.programmaticStreamSerializationAllowed = 1;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cfg.attrs = at;
+  cfg.numAttrs = g_pdl ? 1 : 0;
+  cudaLaunchKernelEx(&cfg, kernel, std::forward<A>(args)...);
+}
 
 // Word k (0..7) of a 32-byte record held as two uint4.
 __device__ __forceinline__ uint32_t pick_word(const uint4& a, const uint4& b, int k) {
@@ -125,24 +154,29 @@ __device__ __forceinline__ void reduce_scale(float mg, float mh, bool nonfinite,
 //    `vrows` rows (n - n % 8 for n >= 16, objective/mod.rs:195) every aligned
 //    group of 8 margins whose magnitudes are all <= 80 takes the vector
 //    sigmoid, any other group and the tail the scalar one.
+// The leaf of a 32-byte record held in registers (at most 28 features: one
+// mask word, word `mask_word` of the record).
+__device__ __forceinline__ float walk_leaf_rec32(const WNode* __restrict__ t, const uint4& a, const uint4& b,
+                                                 uint32_t mask_word) {
+  const uint32_t m = pick_word(a, b, (int)mask_word);
+  WNode nd = t[0];
+  while (nd.left >= 0) {
+    const uint32_t f = nd.feature & 0x7fffffffu;
+    const bool miss = (m >> f) & 1u;
+    const uint32_t bin = (pick_word(a, b, (int)(f >> 2)) >> ((f & 3) * 8)) & 0xffu;
+    const bool left = miss ? (nd.feature >> 31) != 0u : bin < nd.limit;
+    nd = t[nd.left + (left ? 0 : 1)];
+  }
+  return nd.leaf;
+}
+
 // The leaf of row r in the walked tree (WNode, staged in shared memory).
 __device__ __forceinline__ float walk_leaf(const WNode* __restrict__ t, const uint8_t* __restrict__ rp,
                                            uint32_t stride, uint32_t mask_off) {
+  if (stride == 32 && mask_off <= 28)
+    return walk_leaf_rec32(t, *reinterpret_cast<const uint4*>(rp), *reinterpret_cast<const uint4*>(rp + 16),
+                           mask_off >> 2);
   WNode nd = t[0];
-  if (stride == 32 && mask_off == 28) {
-    // the whole record (28 bins + the mask word) in registers
-    const uint4 a = *reinterpret_cast<const uint4*>(rp);
-    const uint4 b = *reinterpret_cast<const uint4*>(rp + 16);
-    const uint32_t m = b.w;
-    while (nd.left >= 0) {
-      const uint32_t f = nd.feature & 0x7fffffffu;
-      const bool miss = (m >> f) & 1u;
-      const uint32_t bin = (pick_word(a, b, (int)(f >> 2)) >> ((f & 3) * 8)) & 0xffu;
-      const bool left = miss ? (nd.feature >> 31) != 0u : bin < nd.limit;
-      nd = t[nd.left + (left ? 0 : 1)];
-    }
-    return nd.leaf;
-  }
   while (nd.left >= 0) {
     const uint32_t f = nd.feature & 0x7fffffffu;
     const uint32_t m = *reinterpret_cast<const uint32_t*>(rp + mask_off + 4 * (f >> 5));
@@ -199,6 +233,7 @@ __device__ __forceinline__ float walk_leaf_csr(const WNode* __restrict__ t, cons
 // waits.
 __global__ void k_walk_csr(DevConst c, int K, const WNode* __restrict__ wtree, uint32_t wstride,
                            float* __restrict__ margin, const int* __restrict__ pending) {
+  pdl_wait();
   if (!*pending) return;
   const uint64_t n = c.n_rows;
   for (uint64_t i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n;
@@ -233,6 +268,7 @@ __global__ void k_gradients(int kind, float* __restrict__ margin,
                             const LevelState* __restrict__ ls_last, uint8_t* rec,
                             uint32_t stride, uint32_t mask_off, uint32_t blk, uint32_t blk_pair,
                             const int* __restrict__ pending) {
+  pdl_wait();
   extern __shared__ WNode s_tree[];
   if (wtree && !(pending && *pending)) wtree = nullptr;  // no tree waiting for the margins
   if (wtree) stage_tree(wtree, ls_last, s_tree);
@@ -288,6 +324,191 @@ __global__ void k_gradients(int kind, float* __restrict__ margin,
   reduce_scale(mg, mh, nonfinite, scale);
 }
 
+// The same gradients over row blocks of three 32-byte records (13 to 28
+// features, one output), one thread per 128-byte block. Each thread issues
+// its three rows' loads (the whole line of records, three margins, three
+// labels) before using any. A tree of depth D <= kCtMaxDepth (ct_depth) is
+// walked as a complete tree, re-laid per CTA in shared memory: position p's
+// children are 2p + 1 and 2p + 2, a leaf above depth D passes every row on
+// to children that carry its value, so a walk is D steps of one node load
+// and one byte load (the record copied to shared memory) with no branch;
+// deeper trees (ct_depth = 0) walk the nodes from registers. The leaf is
+// the one the pointer walk reaches, bit for bit. A warp covers 96
+// consecutive rows, so every aligned group of 8 rows (the logistic vector
+// groups) lies within it; a row's group flag gathers the regular-margin
+// flags of the (at most four) lanes holding the group's rows.
+constexpr int kCtMaxDepth = 10;
+constexpr int kGradThreads = 256;
+constexpr int kRecPitch = 100;  // bytes of a thread's three staged records (25 words: no bank repeats)
+
+size_t gradients_b3_smem(int max_nodes, int ct_depth) {
+  size_t b = sizeof(WNode) * (size_t)max_nodes;
+  if (ct_depth > 0) {
+    const size_t inner = (size_t(1) << ct_depth) - 1;
+    b += 8 * inner + 4 * (inner + 1) + 2 * (2 * inner + 1) + (size_t)kGradThreads * kRecPitch;
+    b = (b + 15) / 16 * 16;
+  }
+  return b;
+}
+
+__global__ void __launch_bounds__(kGradThreads, 4)
+    k_gradients_b3(int kind, float* __restrict__ margin, const float* __restrict__ label,
+                   const float* __restrict__ weight, float spw, float min_hess, uint64_t n, uint64_t vrows,
+                   float2* __restrict__ gpair, Scale* scale, const WNode* __restrict__ wtree,
+                   const LevelState* __restrict__ ls_last, int max_nodes, int ct_depth,
+                   uint8_t* __restrict__ rec, uint32_t mask_word, const int* __restrict__ pending) {
+  pdl_wait();
+  extern __shared__ __align__(16) unsigned char s_dyn[];
+  WNode* s_tree = reinterpret_cast<WNode*>(s_dyn);
+  if (wtree && !(pending && *pending)) wtree = nullptr;  // no tree waiting for the margins
+  const int D = ct_depth;
+  const uint32_t inner = D > 0 ? (1u << D) - 1u : 0u;
+  uint2* s_ct = reinterpret_cast<uint2*>(s_tree + max_nodes);       // [inner]: feature | dl << 31, limit
+  float* s_leaf = reinterpret_cast<float*>(s_ct + inner);           // [inner + 1]
+  int16_t* s_pos = reinterpret_cast<int16_t*>(s_leaf + inner + 1);  // [2 inner + 1]: node of a position
+  uint8_t* s_rec = reinterpret_cast<uint8_t*>(s_pos + 2 * inner + 1) + 0;
+  s_rec = reinterpret_cast<uint8_t*>(((uintptr_t)s_rec + 15) & ~(uintptr_t)15);
+  if (wtree) {
+    stage_tree(wtree, ls_last, s_tree);
+    if (D > 0) {
+      if (threadIdx.x == 0) s_pos[0] = 0;
+      __syncthreads();
+      for (int d = 0; d < D; ++d) {
+        for (uint32_t p = (1u << d) - 1 + threadIdx.x; p < (2u << d) - 1; p += blockDim.x) {
+          const int k = s_pos[p];
+          const WNode nd = s_tree[k];
+          if (nd.left >= 0) {
+            s_ct[p] = make_uint2(nd.feature, nd.limit);
+            s_pos[2 * p + 1] = (int16_t)nd.left;
+            s_pos[2 * p + 2] = (int16_t)(nd.left + 1);
+          } else {  // a leaf: both children carry it
+            s_ct[p] = make_uint2(0u, 0u);
+            s_pos[2 * p + 1] = (int16_t)k;
+            s_pos[2 * p + 2] = (int16_t)k;
+          }
+        }
+        __syncthreads();
+      }
+      for (uint32_t p = threadIdx.x; p <= inner; p += blockDim.x) s_leaf[p] = s_tree[s_pos[inner + p]].leaf;
+      __syncthreads();
+    }
+  }
+  float mg = 0.0f, mh = 0.0f;
+  bool nonfinite = false;
+  const unsigned lane = threadIdx.x & 31;
+  uint8_t* my_rec = s_rec + threadIdx.x * kRecPitch;
+  const uint64_t nblk = (n + 2) / 3;
+  const uint64_t step = (uint64_t)gridDim.x * blockDim.x;
+  // the loop bound is per warp (its first block), so shuffles see every lane
+  for (uint64_t w0 = (uint64_t)blockIdx.x * blockDim.x + (threadIdx.x & ~31u); w0 < nblk; w0 += step) {
+    const uint64_t q = w0 + lane;
+    const uint64_t r0 = 3 * q;
+    uint8_t* line = rec + q * kBlockBytes;
+    uint4 L[6];
+    float m[3], y[3], w[3];
+    if (wtree && q < nblk) {
+#pragma unroll
+      for (int k = 0; k < 6; ++k) L[k] = reinterpret_cast<const uint4*>(line)[k];
+    }
+#pragma unroll
+    for (int j = 0; j < 3; ++j) {
+      const bool in = r0 + j < n;
+      m[j] = in ? margin[r0 + j] : 0.0f;
+      y[j] = in ? label[r0 + j] : 0.0f;
+      w[j] = (in && weight) ? weight[r0 + j] : 1.0f;
+    }
+    if (wtree && D > 0) {
+      if (q < nblk) {
+#pragma unroll
+        for (int k = 0; k < 6; ++k) {
+          uint32_t* d = reinterpret_cast<uint32_t*>(my_rec + 16 * k);
+          d[0] = L[k].x;
+          d[1] = L[k].y;
+          d[2] = L[k].z;
+          d[3] = L[k].w;
+        }
+      }
+      __syncwarp();
+      // the three walks step together (independent chains of shared loads)
+      uint32_t msk[3], idx[3] = {0u, 0u, 0u};
+#pragma unroll
+      for (int j = 0; j < 3; ++j) msk[j] = reinterpret_cast<const uint32_t*>(my_rec + 32 * j)[mask_word];
+      for (int d = 0; d < D; ++d) {
+#pragma unroll
+        for (int j = 0; j < 3; ++j) {
+          const uint2 cn = s_ct[idx[j]];
+          const uint32_t f = cn.x & 0x7fffffffu;
+          const bool miss = (msk[j] >> f) & 1u;
+          const bool left = miss ? (cn.x >> 31) != 0u : (uint32_t)my_rec[32 * j + f] < cn.y;
+          idx[j] = 2 * idx[j] + (left ? 1u : 2u);
+        }
+      }
+#pragma unroll
+      for (int j = 0; j < 3; ++j) {
+        if (r0 + j < n) {
+          m[j] = __fadd_rn(m[j], s_leaf[idx[j] - inner]);
+          margin[r0 + j] = m[j];
+        }
+      }
+      __syncwarp();
+    } else if (wtree) {
+#pragma unroll
+      for (int j = 0; j < 3; ++j) {
+        if (r0 + j < n) {
+          m[j] = __fadd_rn(m[j], walk_leaf_rec32(s_tree, L[2 * j], L[2 * j + 1], mask_word));
+          margin[r0 + j] = m[j];
+        }
+      }
+    }
+    float g[3], h[3];
+    if (kind == HB_LOSS_LOGISTIC) {
+      uint32_t f = 0;
+#pragma unroll
+      for (int j = 0; j < 3; ++j) f |= (fabsf(m[j]) <= 80.0f || r0 + j >= n) ? (1u << j) : 0u;
+#pragma unroll
+      for (int j = 0; j < 3; ++j) {
+        const uint32_t r = 3 * lane + j;  // row within the warp's 96
+        const uint32_t gs = r & ~7u;      // its group's first row
+        const uint32_t ta = gs / 3u;      // the lane holding it
+        uint32_t cat = 0;
+#pragma unroll
+        for (int k = 0; k < 4; ++k) cat |= __shfl_sync(kFull, f, min(ta + k, 31u)) << (3 * k);
+        const bool group_regular = ((cat >> (gs - 3u * ta)) & 0xffu) == 0xffu;
+        const uint64_t i = r0 + j;
+        const float p = (i < vrows && group_regular) ? sigmoid_vector(m[j]) : sigmoid_scalar(m[j]);
+        float wj = w[j];
+        if (y[j] == 1.0f) wj = __fmul_rn(wj, spw);
+        g[j] = __fmul_rn(__fsub_rn(p, y[j]), wj);
+        const float ph = __fmul_rn(p, __fsub_rn(1.0f, p));
+        h[j] = __fmul_rn(ph > min_hess ? ph : min_hess, wj);
+      }
+    } else {
+#pragma unroll
+      for (int j = 0; j < 3; ++j) {
+        float wj = w[j];
+        if (y[j] == 1.0f) wj = __fmul_rn(wj, spw);
+        g[j] = __fmul_rn(__fsub_rn(m[j], y[j]), wj);
+        h[j] = wj;
+      }
+    }
+    if (q < nblk) {
+#pragma unroll
+      for (int j = 0; j < 3; ++j) {
+        if (r0 + j < n) {
+          gpair[r0 + j] = make_float2(g[j], h[j]);
+          fold_max(g[j], h[j], mg, mh, nonfinite);
+        } else {
+          g[j] = h[j] = 0.0f;
+        }
+      }
+      uint4* ps = reinterpret_cast<uint4*>(line + 96);
+      ps[0] = make_uint4(__float_as_uint(g[0]), __float_as_uint(h[0]), __float_as_uint(g[1]), __float_as_uint(h[1]));
+      ps[1] = make_uint4(__float_as_uint(g[2]), __float_as_uint(h[2]), 0u, 0u);
+    }
+  }
+  reduce_scale(mg, mh, nonfinite, scale);
+}
+
 // multi:softmax gradients (objective/multiclass.rs:43), the reference's
 // per-row scalar kernel (simd/mod.rs:580), which x86_64 runs for every class
 // count but 2 and 4: shift = max(f32::MIN_POSITIVE, margins...), the
@@ -307,6 +528,7 @@ __global__ void k_softmax_gradients(int K, float* __restrict__ margin, const flo
                                     Scale* scale, const WNode* __restrict__ wtree, uint32_t wstride,
                                     const uint8_t* __restrict__ rec, uint32_t stride,
                                     uint32_t mask_off, uint32_t blk, const int* __restrict__ pending) {
+  pdl_wait();
   __shared__ unsigned s_mg[kMaxClasses], s_mh[kMaxClasses], s_nf[kMaxClasses];
   for (int j = threadIdx.x; j < K; j += blockDim.x) s_mg[j] = s_mh[j] = s_nf[j] = 0u;
   __syncthreads();
@@ -393,6 +615,7 @@ __device__ __forceinline__ double pow2d(int e) {
 }
 
 __global__ void k_scale(Scale* scale, uint64_t global_rows, int* pending) {
+  pdl_wait();
   if (pending) *pending = 0;  // the gradient pass before has added the pending tree
   Scale s = *scale;
   s.sg = fixed_scale(__uint_as_float(s.maxg_bits), global_rows);
@@ -451,6 +674,7 @@ __global__ void __launch_bounds__(kCsrThreads)
                const uint32_t* __restrict__ rows, const HEntry* __restrict__ entries,
                const LevelState* __restrict__ ls, longlong2* __restrict__ hist,
                long long* __restrict__ totals, unsigned long long* __restrict__ row_stats) {
+  pdl_wait();
   const int n_entries = ls->n_hentries;
   const uint64_t total = ls->hist_rows;
   if (n_entries <= 0 || total == 0) return;
@@ -525,6 +749,7 @@ __global__ void __launch_bounds__(kHistThreads, 1)
            const uint32_t* __restrict__ rows, const HEntry* __restrict__ entries,
            const LevelState* __restrict__ ls, longlong2* __restrict__ hist,
            long long* __restrict__ totals, unsigned long long* __restrict__ row_stats) {
+  pdl_wait();
   extern __shared__ unsigned long long smem[];
   const int n_entries = ls->n_hentries;
   const uint64_t total = ls->hist_rows;
@@ -675,6 +900,7 @@ __global__ void __launch_bounds__(kH32Threads, 1)
              const LevelState* __restrict__ ls, longlong2* __restrict__ hist,
              long long* __restrict__ totals, unsigned long long* __restrict__ row_stats, int lo_bits,
              int flush_rows) {
+  pdl_wait();
   constexpr int kSt = H32<G>::kStages;
   constexpr int kBS = H32<G>::kBinShift;
   constexpr uint32_t kRecW = BLK == 5 ? 16u : BLK == 3 ? 32u : BLK == 2 ? 48u : 0u;
@@ -1097,6 +1323,7 @@ __global__ void __launch_bounds__(kSplitThreads)
            const Front* __restrict__ front, const LevelState* __restrict__ ls,
            const Triple* __restrict__ pairs, int sib_base, const Scale* __restrict__ scale,
            Cand* __restrict__ cand, const int8_t* __restrict__ dirs) {
+  pdl_wait();
   const int f = blockIdx.x;
   const int k = blockIdx.y;
   if (k >= ls->n_front) return;
@@ -1266,6 +1493,7 @@ __global__ void __launch_bounds__(kSplitThreads)
                 const Front* __restrict__ front, const LevelState* __restrict__ ls,
                 const Triple* __restrict__ pairs, int sib_base, const Scale* __restrict__ scale,
                 Cand* __restrict__ cand, const int8_t* __restrict__ dirs) {
+  pdl_wait();
   const int f = blockIdx.x;
   const int k = blockIdx.y;
   if (k >= ls->n_front) return;
@@ -1460,6 +1688,7 @@ __global__ void __launch_bounds__(kScanWarps * 32)
              const Front* __restrict__ front, const LevelState* __restrict__ ls,
              const Triple* __restrict__ pairs, int sib_base, const Scale* __restrict__ scale,
              Cand* __restrict__ cand, const int8_t* __restrict__ dirs) {
+  pdl_wait();
   const int k = blockIdx.y;
   if (k >= ls->n_front) return;
   const int lane = threadIdx.x & 31;
@@ -1632,6 +1861,7 @@ __global__ void __launch_bounds__(kApplyThreads)
             Decision* __restrict__ dec, PItem* __restrict__ items, LevelState* ls,
             LevelState* ls_next, hb_tree_node* __restrict__ tree, WNode* __restrict__ wtree,
             const Scale* __restrict__ scale, int depth, int leaf_only) {
+  pdl_wait();
   using Scan = cub::BlockScan<int, kApplyThreads>;
   __shared__ typename Scan::TempStorage tmp;
   const int n_front = ls->n_front;
@@ -1873,6 +2103,7 @@ __global__ void __launch_bounds__(kLgThreads)
               hb_tree_node* __restrict__ tree, WNode* __restrict__ wtree,
               const Scale* __restrict__ scale, LgNode* __restrict__ heap, LgState* st,
               int32_t* __restrict__ ndepth, int max_leaves, int depth_limit, int final_step) {
+  pdl_wait();
   __shared__ LgNode s_new[2];
   __shared__ float s_bl[kLgThreads / 32];
   __shared__ int s_bf[kLgThreads / 32];
@@ -2099,6 +2330,7 @@ __device__ void lg_step_serial(const DevConst& c, const uint32_t* __restrict__ f
 // Lossguide state of a new tree: the root pending, one node, one leaf.
 __global__ void k_lg_setup(LgState* st, int32_t* ndepth, hb_tree_node* tree, const Front* root,
                            const Scale* scale, LevelState* ls_next) {
+  pdl_wait();
   LgState S{};
   S.heap_n = 0;
   S.n_nodes = 1;
@@ -2150,6 +2382,7 @@ __global__ void __launch_bounds__(kPartThreads)
                  const Decision* __restrict__ dec, const PItem* __restrict__ items,
                  const LevelState* __restrict__ ls, uint32_t* __restrict__ dirbits,
                  uint32_t* __restrict__ item_left, uint32_t* __restrict__ rows_copy) {
+  pdl_wait();
   const int it = blockIdx.x;
   if (it >= ls->n_items) return;
   const PItem pi = locate_item(dec, ls->n_front, it, front);
@@ -2233,6 +2466,7 @@ __global__ void __launch_bounds__(kScanThreads)
                 LevelState* ls, const uint32_t* __restrict__ item_left,
                 uint32_t* __restrict__ item_left_off, Front* next, HEntry* __restrict__ entries,
                 Triple* __restrict__ pairs, LevelState* __restrict__ ls_next) {
+  pdl_wait();
   using Scan = cub::BlockScan<uint32_t, kScanThreads>;
   __shared__ typename Scan::TempStorage tmp;
   const int k = blockIdx.x;
@@ -2285,6 +2519,7 @@ __global__ void __launch_bounds__(kPartThreads)
                    const uint32_t* __restrict__ dirbits, const uint32_t* __restrict__ item_left_off,
                    const Front* __restrict__ next, const uint32_t* __restrict__ rows_in,
                    int identity, uint32_t* __restrict__ rows_out) {
+  pdl_wait();
   const int it = blockIdx.x;
   if (it >= ls->n_items) return;
   const PItem pi = locate_item(dec, ls->n_front, it, front);
@@ -2398,6 +2633,7 @@ __device__ void hist_plan_body(const Front* __restrict__ front, const Decision* 
 }
 
 __global__ void k_root_setup(uint64_t n_rows, Front* front, HEntry* entries, LevelState* ls) {
+  pdl_wait();
   Front f{};
   f.node = 0;
   f.slot = 0;
@@ -2418,6 +2654,7 @@ __global__ void k_root_setup(uint64_t n_rows, Front* front, HEntry* entries, Lev
 }
 
 __global__ void k_root_stats(Front* front, const long long* totals) {
+  pdl_wait();
   front[0].g = totals[0];
   front[0].h = totals[1];
 }
@@ -2425,6 +2662,7 @@ __global__ void k_root_stats(Front* front, const long long* totals) {
 __global__ void k_finish_tree(const hb_tree_node* __restrict__ tree, const LevelState* ls_last,
                               hb_tree_node* __restrict__ forest, uint32_t* counts,
                               int32_t* tree_counter, uint32_t max_nodes) {
+  pdl_wait();
   const int t = *tree_counter;
   const int n = ls_last->n_nodes;
   for (int i = threadIdx.x; i < n; i += blockDim.x) forest[(uint64_t)t * max_nodes + i] = tree[i];
@@ -2543,13 +2781,24 @@ void launch_seg_total(const uint32_t* rows, uint64_t begin, uint64_t len, const 
 // Launchers.
 void launch_gradients(int kind, float* margin, const float* label, const float* weight, float spw,
                       float min_hess, uint64_t n, uint64_t vrows, float2* gpair, Scale* scale,
-                      const WNode* wtree, const LevelState* ls_last, int max_nodes,
+                      const WNode* wtree, const LevelState* ls_last, int max_nodes, int walk_depth,
                       uint8_t* rec, uint32_t stride, uint32_t mask_off, uint32_t blk, uint32_t blk_pair,
                       const int* pending, int n_sm, cudaStream_t s) {
   int grid = (int)std::min<uint64_t>((n + 255) / 256, (uint64_t)n_sm * 8);
   if (grid < 1) grid = 1;
   const size_t smem = wtree ? sizeof(WNode) * (size_t)max_nodes : 0;
-  k_gradients<<<grid, 256, smem, s>>>(kind, margin, label, weight, spw, min_hess, n, vrows, gpair, scale,
+  if (blk == 3 && blk_pair == 96 && stride == 32 && mask_off <= 28) {
+    const uint64_t nblk = (n + 2) / 3;
+    int g3 = (int)std::min<uint64_t>((nblk + kGradThreads - 1) / kGradThreads, (uint64_t)n_sm * 4);
+    if (g3 < 1) g3 = 1;
+    const int ct = (wtree && walk_depth > 0 && walk_depth <= kCtMaxDepth) ? walk_depth : 0;
+    // (hist_configure granted the largest size: a depth-10 tree)
+    const size_t sm3 = wtree ? gradients_b3_smem(max_nodes, ct) : 0;
+    launch_pdl(k_gradients_b3, dim3(g3), dim3(kGradThreads), sm3, s, kind, margin, label, weight, spw, min_hess,
+               n, vrows, gpair, scale, wtree, ls_last, max_nodes, ct, rec, mask_off >> 2, pending);
+    return;
+  }
+  launch_pdl(k_gradients, dim3(grid), dim3(256), smem, s, kind, margin, label, weight, spw, min_hess, n, vrows, gpair, scale,
                                       wtree, ls_last, rec, stride, mask_off, blk, blk_pair, pending);
 }
 
@@ -2563,7 +2812,11 @@ void launch_walk(const WNode* wtree, const LevelState* ls_last, int max_nodes, c
 }
 
 void hist_configure() {
+  const char* np = std::getenv("HB_NO_PDL");
+  g_pdl = !(np && np[0] == '1');
   cudaFuncSetAttribute(k_hist, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024 - 1024);
+  cudaFuncSetAttribute(k_gradients_b3, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                       (int)gradients_b3_smem(2 << kCtMaxDepth, kCtMaxDepth));
   for (const void* f : h32_kernels())
     cudaFuncSetAttribute(f, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024 - 1024);
 }
@@ -2573,14 +2826,14 @@ void launch_softmax_gradients(int K, float* margin, const float* label, uint64_t
                               const uint8_t* rec, uint32_t stride, uint32_t mask_off, uint32_t blk,
                               const int* pending, int n_sm, cudaStream_t s) {
   const int grid = (int)std::max<uint64_t>(1, std::min<uint64_t>((n + 255) / 256, (uint64_t)n_sm * 8));
-  k_softmax_gradients<<<grid, 256, 0, s>>>(K, margin, label, n, min_hess, gpair, scale, wtree,
+  launch_pdl(k_softmax_gradients, dim3(grid), dim3(256), 0, s, K, margin, label, n, min_hess, gpair, scale, wtree,
                                            wstride, rec, stride, mask_off, blk, pending);
 }
 
 void launch_walk_csr(const DevConst& c, int K, const WNode* wtree, uint32_t wstride, float* margin,
                      const int* pending, int n_sm, cudaStream_t s) {
   const int grid = (int)std::max<uint64_t>(1, std::min<uint64_t>((c.n_rows + 255) / 256, (uint64_t)n_sm * 8));
-  k_walk_csr<<<grid, 256, 0, s>>>(c, K, wtree, wstride, margin, pending);
+  launch_pdl(k_walk_csr, dim3(grid), dim3(256), 0, s, c, K, wtree, wstride, margin, pending);
 }
 
 void launch_walk_classes(int K, const WNode* wtree, uint32_t wstride, const uint8_t* rec,
@@ -2597,7 +2850,7 @@ void launch_pair_maxima(const float2* gpair, uint64_t n, Scale* scale, int n_sm,
 }
 
 void launch_scale(Scale* scale, uint64_t global_rows, int* pending, cudaStream_t s) {
-  k_scale<<<1, 1, 0, s>>>(scale, global_rows, pending);
+  launch_pdl(k_scale, dim3(1), dim3(1), 0, s, scale, global_rows, pending);
 }
 
 void launch_encode(const uint8_t* col, const uint64_t* colmiss, uint64_t n_rows, uint32_t n_cols,
@@ -2648,7 +2901,7 @@ void launch_hist(const DevConst& c, const uint32_t* fo, const uint8_t* rec, cons
                  const LevelState* ls, longlong2* hist, long long* totals,
                  unsigned long long* row_stats, int grid_x, size_t smem, cudaStream_t s) {
   if (c.csr) {
-    k_hist_csr<<<grid_x * (2048 / kCsrThreads), kCsrThreads, 0, s>>>(c, gpair, scale, rows, entries, ls,
+    launch_pdl(k_hist_csr, dim3(grid_x * (2048 / kCsrThreads)), dim3(kCsrThreads), 0, s, c, gpair, scale, rows, entries, ls,
                                                                     hist, totals, row_stats);
     return;
   }
@@ -2675,11 +2928,11 @@ void launch_hist(const DevConst& c, const uint32_t* fo, const uint8_t* rec, cons
     int K, R;
     split_for_rows(c.global_rows, K, R);
     grid.y = (c.n_groups + G - 1) / G;
-    f<<<grid, kH32Threads, smem, s>>>(c, fo, rec, gpair, scale, rows, entries, ls, hist, totals, row_stats,
+    launch_pdl(f, dim3(grid), dim3(kH32Threads), smem, s, c, fo, rec, gpair, scale, rows, entries, ls, hist, totals, row_stats,
                                       K, R);
     return;
   }
-  k_hist<<<grid, kHistThreads, smem, s>>>(c, fo, rec, gpair, scale, rows, entries, ls, hist, totals,
+  launch_pdl(k_hist, dim3(grid), dim3(kHistThreads), smem, s, c, fo, rec, gpair, scale, rows, entries, ls, hist, totals,
                                           row_stats);
 }
 
@@ -2699,26 +2952,26 @@ void launch_scan(const DevConst& c, const uint32_t* fo, longlong2* hist, const F
   if (c.max_bins <= 128 && !c.scan_cta) {
     dim3 grid((c.n_cols + kScanWarps - 1) / kScanWarps, max_front);
     if (c.max_bins <= 32)
-      k_scan_w<1><<<grid, kScanWarps * 32, 0, s>>>(c, fo, hist, front, ls, pairs, sib_base, scale, cand, dirs);
+      launch_pdl(k_scan_w<1>, dim3(grid), dim3(kScanWarps * 32), 0, s, c, fo, hist, front, ls, pairs, sib_base, scale, cand, dirs);
     else if (c.max_bins <= 64)
-      k_scan_w<2><<<grid, kScanWarps * 32, 0, s>>>(c, fo, hist, front, ls, pairs, sib_base, scale, cand, dirs);
+      launch_pdl(k_scan_w<2>, dim3(grid), dim3(kScanWarps * 32), 0, s, c, fo, hist, front, ls, pairs, sib_base, scale, cand, dirs);
     else
-      k_scan_w<4><<<grid, kScanWarps * 32, 0, s>>>(c, fo, hist, front, ls, pairs, sib_base, scale, cand, dirs);
+      launch_pdl(k_scan_w<4>, dim3(grid), dim3(kScanWarps * 32), 0, s, c, fo, hist, front, ls, pairs, sib_base, scale, cand, dirs);
     return;
   }
   dim3 grid(c.n_cols, max_front);
   if (c.max_bins > (uint32_t)kSplitThreads) {
-    k_scan_wide<<<grid, kSplitThreads, 0, s>>>(c, fo, hist, front, ls, pairs, sib_base, scale, cand, dirs);
+    launch_pdl(k_scan_wide, dim3(grid), dim3(kSplitThreads), 0, s, c, fo, hist, front, ls, pairs, sib_base, scale, cand, dirs);
     return;
   }
-  k_scan<<<grid, kSplitThreads, 0, s>>>(c, fo, hist, front, ls, pairs, sib_base, scale, cand, dirs);
+  launch_pdl(k_scan, dim3(grid), dim3(kSplitThreads), 0, s, c, fo, hist, front, ls, pairs, sib_base, scale, cand, dirs);
 }
 
 void launch_apply(const DevConst& c, const uint32_t* fo, const float* cuts, const Cand* cand,
                   const Front* front, Front* next, Decision* dec, PItem* items, LevelState* ls,
                   LevelState* ls_next, hb_tree_node* tree, WNode* wtree, const Scale* scale,
                   int depth, int leaf_only, cudaStream_t s) {
-  k_apply<<<1, kApplyThreads, 0, s>>>(c, fo, cuts, cand, front, next, dec, items, ls, ls_next, tree,
+  launch_pdl(k_apply, dim3(1), dim3(kApplyThreads), 0, s, c, fo, cuts, cand, front, next, dec, items, ls, ls_next, tree,
                                       wtree, scale, depth, leaf_only);
 }
 
@@ -2728,17 +2981,17 @@ void launch_part_count(const DevConst& c, const uint8_t* col, const uint64_t* co
                        const LevelState* ls, int max_items, uint32_t* dirbits, uint32_t* item_left,
                        cudaStream_t s, uint32_t* rows_copy) {
   if (c.csr)
-    k_part_count<true><<<max_items, kPartThreads, 0, s>>>(c, col, colmiss, rec, use_record, rows_in, identity,
+    launch_pdl(k_part_count<true>, dim3(max_items), dim3(kPartThreads), 0, s, c, col, colmiss, rec, use_record, rows_in, identity,
                                                         front, dec, items, ls, dirbits, item_left, rows_copy);
   else
-    k_part_count<false><<<max_items, kPartThreads, 0, s>>>(c, col, colmiss, rec, use_record, rows_in, identity,
+    launch_pdl(k_part_count<false>, dim3(max_items), dim3(kPartThreads), 0, s, c, col, colmiss, rec, use_record, rows_in, identity,
                                                          front, dec, items, ls, dirbits, item_left, rows_copy);
 }
 
 void launch_part_scan(const Front* front, const Decision* dec, LevelState* ls, int max_front,
                       const uint32_t* item_left, uint32_t* item_left_off, Front* next,
                       HEntry* entries, Triple* pairs, LevelState* ls_next, cudaStream_t s) {
-  k_part_scan<<<max_front, kScanThreads, 0, s>>>(front, dec, ls, item_left, item_left_off, next,
+  launch_pdl(k_part_scan, dim3(max_front), dim3(kScanThreads), 0, s, front, dec, ls, item_left, item_left_off, next,
                                                  entries, pairs, ls_next);
 }
 
@@ -2747,7 +3000,7 @@ void launch_part_scatter(const Front* front, const Decision* dec, const PItem* i
                          const uint32_t* item_left_off, const Front* next,
                          const uint32_t* rows_in, int identity, uint32_t* rows_out,
                          cudaStream_t s) {
-  k_part_scatter<<<max_items, kPartThreads, 0, s>>>(front, dec, items, ls, dirbits, item_left_off,
+  launch_pdl(k_part_scatter, dim3(max_items), dim3(kPartThreads), 0, s, front, dec, items, ls, dirbits, item_left_off,
                                                     next, rows_in, identity, rows_out);
 }
 
@@ -2767,30 +3020,30 @@ void launch_lg_step(const DevConst& c, const uint32_t* fo, const float* cuts, co
         dev >= 0 && dev < 64)
       granted[dev] = smem;
   }
-  k_lg_step<<<1, kLgThreads, smem, s>>>(c, fo, cuts, cand, pend, front, next, dec, ls, ls_next, tree,
+  launch_pdl(k_lg_step, dim3(1), dim3(kLgThreads), smem, s, c, fo, cuts, cand, pend, front, next, dec, ls, ls_next, tree,
                                         wtree, scale, heap, st, ndepth, max_leaves, depth_limit,
                                         final_step);
 }
 
 void launch_lg_setup(LgState* st, int32_t* ndepth, hb_tree_node* tree, const Front* root,
                      const Scale* scale, LevelState* ls_next, cudaStream_t s) {
-  k_lg_setup<<<1, 1, 0, s>>>(st, ndepth, tree, root, scale, ls_next);
+  launch_pdl(k_lg_setup, dim3(1), dim3(1), 0, s, st, ndepth, tree, root, scale, ls_next);
 }
 
 
 void launch_root_setup(uint64_t n_rows, Front* front, HEntry* entries, LevelState* ls,
                        cudaStream_t s) {
-  k_root_setup<<<1, 1, 0, s>>>(n_rows, front, entries, ls);
+  launch_pdl(k_root_setup, dim3(1), dim3(1), 0, s, n_rows, front, entries, ls);
 }
 
 void launch_root_stats(Front* front, const long long* totals, cudaStream_t s) {
-  k_root_stats<<<1, 1, 0, s>>>(front, totals);
+  launch_pdl(k_root_stats, dim3(1), dim3(1), 0, s, front, totals);
 }
 
 void launch_finish_tree(const hb_tree_node* tree, const LevelState* ls_last, hb_tree_node* forest,
                         uint32_t* counts, int32_t* tree_counter, uint32_t max_nodes,
                         cudaStream_t s) {
-  k_finish_tree<<<1, 256, 0, s>>>(tree, ls_last, forest, counts, tree_counter, max_nodes);
+  launch_pdl(k_finish_tree, dim3(1), dim3(256), 0, s, tree, ls_last, forest, counts, tree_counter, max_nodes);
 }
 
 void launch_dequantize(const longlong2* hist, uint32_t n, const Scale* scale, double* out,

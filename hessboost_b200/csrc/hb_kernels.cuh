@@ -10,11 +10,12 @@ namespace hb {
 // Objective gradients at `margin` (the host's bits, see hb_kernels.cu) plus
 // the largest |g|, |h| and a non-finite flag, folded into `scale`.
 // With `wtree` and *pending set, each row first adds its leaf of that tree
-// to its margin. With blk_pair != 0 each pair is also written into the
-// row's block (blk rows a 128-byte line of `rec`).
+// to its margin (walk_depth > 0: a depthwise tree of that depth, which the
+// row-block kernel walks as a complete tree). With blk_pair != 0 each pair
+// is also written into the row's block (blk rows a 128-byte line of `rec`).
 void launch_gradients(int kind, float* margin, const float* label, const float* weight, float spw,
                       float min_hess, uint64_t n, uint64_t vrows, float2* gpair, Scale* scale,
-                      const WNode* wtree, const LevelState* ls_last, int max_nodes,
+                      const WNode* wtree, const LevelState* ls_last, int max_nodes, int walk_depth,
                       uint8_t* rec, uint32_t stride, uint32_t mask_off, uint32_t blk, uint32_t blk_pair,
                       const int* pending, int n_sm, cudaStream_t s);
 // When *pending is set, add each row's leaf of `wtree` to its margin.

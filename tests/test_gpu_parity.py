@@ -112,6 +112,13 @@ CASES = {
     "regularised": dict(gen=lambda: synth.regression_c1(8000, 10, seed=4), rounds=3,
                         kw=dict(max_depth=5, reg_lambda=3.0, alpha=0.5, gamma=0.2, min_child_weight=20.0,
                                 max_delta_step=0.7)),
+    # 13-28 features (three records a row block): leaves above the depth
+    # limit from regularisation, and the deepest complete-tree walk (10)
+    "regularised_rows3": dict(gen=lambda: synth.logistic_c2(30_011, 20, seed=31), rounds=4,
+                              kw=dict(objective="binary:logistic", max_depth=6, reg_lambda=2.0, gamma=0.4,
+                                      min_child_weight=30.0, eta=0.3)),
+    "depth10_rows3": dict(gen=lambda: synth.logistic_c2(50_021, 16, seed=32), rounds=3,
+                          kw=dict(objective="binary:logistic", max_depth=10, eta=0.3)),
     "few_bins": dict(gen=lambda: synth.logistic_c2(6000, 12, seed=8), rounds=3,
                      kw=dict(objective="binary:logistic", max_depth=6, max_bin=16)),
     # enough rows for the 32-bit split-accumulator histogram kernel
