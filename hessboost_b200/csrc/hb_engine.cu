@@ -92,6 +92,12 @@ struct hb_engine {
   DevBuf<Decision> dec;
   DevBuf<PItem> items;
   DevBuf<uint32_t> dirbits, item_left, item_off;
+  // depthwise one-pass partition: per split, the rows placed so far in its
+  // left and right child (zero between levels)
+  DevBuf<uint32_t> fill;
+  // HB_STABLE_PARTITION=1: the three-pass stable partition in depthwise
+  // growth too (children keep ascending row order)
+  bool stable_partition = false;
   DevBuf<HEntry> entries;
   DevBuf<Triple> pairs;
   DevBuf<LevelState> ls;
@@ -287,6 +293,8 @@ hb_status ensure_growth_buffers(hb_engine* e, int max_depth) {
   HB_CK(e, e->dirbits.alloc((size_t)e->max_items * kTileWords));
   HB_CK(e, e->item_left.alloc(e->max_items));
   HB_CK(e, e->item_off.alloc(e->max_items));
+  HB_CK(e, e->fill.alloc((size_t)2 * max_front));
+  HB_CK(e, cudaMemset(e->fill.p, 0, sizeof(uint32_t) * 2 * max_front));
   HB_CK(e, e->entries.alloc(max_front));
   HB_CK(e, e->pairs.alloc(max_front));
   HB_CK(e, e->ls.alloc(kMaxDepth + 2));
@@ -418,6 +426,7 @@ hb_status grow_device(hb_engine* e, const hb_train_params* p, bool to_forest) {
 
   HB_CK(e, cudaMemsetAsync(e->ls.p, 0, sizeof(LevelState) * (kMaxDepth + 2), s));
   HB_CK(e, cudaMemsetAsync(e->hist_all.p, 0, sizeof(longlong2) * (1 + slots * c.total_bins), s));
+  HB_CK(e, cudaMemsetAsync(e->fill.p, 0, sizeof(uint32_t) * 2 * ((size_t)1 << D), s));
   launch_root_setup(c.n_rows, e->front[0].p, e->entries.p, e->ls.p, s);
   const size_t smem = hist_smem_bytes(c);
   const int hgrid = hist_grid(e->n_sm);
@@ -469,13 +478,20 @@ hb_status grow_device(hb_engine* e, const hb_train_params* p, bool to_forest) {
     mark_begin(e, T_PART);
     // feature columns, not row records: a level's gathers of one feature's
     // column and bitmap stay in L2, records do not
-    launch_part_count(c, e->col.p, e->has_missing ? e->colmiss.p : nullptr, e->rec.p, 0,
-                      rows_in, d == 0, fr, e->dec.p, e->items.p, lsd, max_items, e->dirbits.p,
-                      e->item_left.p, s);
-    launch_part_scan(fr, e->dec.p, lsd, max_front, e->item_left.p, e->item_off.p, nx,
-                     e->entries.p, e->pairs.p, lsn, s);
-    launch_part_scatter(fr, e->dec.p, e->items.p, lsd, max_items, e->dirbits.p, e->item_off.p,
-                        nx, rows_in, d == 0, rows_out, s);
+    if (e->stable_partition) {
+      launch_part_count(c, e->col.p, e->has_missing ? e->colmiss.p : nullptr, e->rec.p, 0,
+                        rows_in, d == 0, fr, e->dec.p, e->items.p, lsd, max_items, e->dirbits.p,
+                        e->item_left.p, s);
+      launch_part_scan(fr, e->dec.p, lsd, max_front, e->item_left.p, e->item_off.p, nx,
+                       e->entries.p, e->pairs.p, lsn, s);
+      launch_part_scatter(fr, e->dec.p, e->items.p, lsd, max_items, e->dirbits.p, e->item_off.p,
+                          nx, rows_in, d == 0, rows_out, s);
+      ++launches;
+    } else {
+      launch_part_onepass(c, e->col.p, e->has_missing ? e->colmiss.p : nullptr, rows_in, d == 0, fr,
+                          e->dec.p, lsd, max_items, e->fill.p, rows_out, s);
+      launch_part_plan(fr, e->dec.p, lsd, e->fill.p, nx, e->entries.p, e->pairs.p, lsn, s);
+    }
     mark_end(e);
     mark_begin(e, T_HIST);
     launch_hist(c, e->fo.p, e->rec.p, hist_gpair(e), cur_scale(e), rows_out, e->entries.p, lsn, hist,
@@ -486,7 +502,7 @@ hb_status grow_device(hb_engine* e, const hb_train_params* p, bool to_forest) {
       HB_NCCL(e, ncclAllReduce(hist + base * c.total_bins, hist + base * c.total_bins,
                                2 * half * c.total_bins, ncclInt64, ncclSum, e->comm, s));
     }
-    launches += 4;
+    launches += 3;  // partition (+ 1 for the stable one) and histogram
     HB_CK(e, cudaGetLastError());
     std::swap(rows_in, rows_out);
     cur ^= 1;
@@ -733,6 +749,8 @@ hb_status hb_engine_create(int32_t device_ordinal, hb_engine** out) {
   cudaEventCreate(&e->run_ev[1]);
   const char* ng = std::getenv("HB_NO_GRAPHS");
   e->use_graphs = !(ng && ng[0] == '1');
+  const char* sp = std::getenv("HB_STABLE_PARTITION");
+  e->stable_partition = sp && sp[0] == '1';
 
   if (e->scale.alloc(1) != cudaSuccess || e->tree_counter.alloc(1) != cudaSuccess ||
       e->seg_total.alloc(2) != cudaSuccess || e->row_stats.alloc(2) != cudaSuccess ||
@@ -782,6 +800,7 @@ hb_status hb_engine_destroy(hb_engine* e) {
   e->dirbits.release();
   e->item_left.release();
   e->item_off.release();
+  e->fill.release();
   e->entries.release();
   e->pairs.release();
   e->ls.release();
@@ -1813,7 +1832,7 @@ static hb_status graph_rounds(hb_engine* e, const hb_train_params* p, int rounds
                         e->item_off.p, e->entries.p, e->pairs.p, e->ls.p, e->tree.p,
                         e->wtree.p, e->forest.p, e->counts.p, e->tree_counter.p,
                         e->row_stats.p, e->flags.p, e->lg_heap.p, e->lg_state.p,
-                        e->lg_depth.p, e->csr_ptr.p, e->csr_bins.p};
+                        e->lg_depth.p, e->csr_ptr.p, e->csr_bins.p, e->fill.p};
   const int weighted = e->weight_key ? 1 : 0;
   std::vector<unsigned char> key(sizeof(hb_train_params) + sizeof(ptrs) + sizeof(int) * 2);
   std::memcpy(key.data(), p, sizeof(hb_train_params));

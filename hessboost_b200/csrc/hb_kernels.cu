@@ -2449,6 +2449,127 @@ __global__ void __launch_bounds__(kPartThreads)
   }
 }
 
+// One-pass partition of depthwise growth: one CTA per tile of a splitting
+// node (2048 rows), which routes its rows (the split feature's column and
+// missing bitmap, the partition's rule) and moves them at once: its left
+// rows to a chunk at the start of the node's segment, its right rows to a
+// chunk at the end, each chunk reserved with one atomic on the node's fill
+// counts (fill[2 pair], fill[2 pair + 1]; zero before the pass). Rows stay
+// ascending within a chunk, but the chunks of a child follow in the order
+// the CTAs reserved them, so a child's row order is not the stable one.
+// Nothing computed from a segment depends on its order: histograms are
+// exact integer sums and the leaf adds go by row. Saves the stable scheme's
+// second pass over the rows (the scatter) and its per-node tile scan.
+template <bool CSR>
+__global__ void __launch_bounds__(kPartThreads)
+    k_part_onepass(DevConst c, const uint8_t* __restrict__ col, const uint64_t* __restrict__ colmiss,
+                   const uint32_t* __restrict__ rows_in, int identity, const Front* __restrict__ front,
+                   const Decision* __restrict__ dec, const LevelState* __restrict__ ls,
+                   uint32_t* __restrict__ fill, uint32_t* __restrict__ rows_out) {
+  pdl_wait();
+  const int it = blockIdx.x;
+  if (it >= ls->n_items) return;
+  const PItem pi = locate_item(dec, ls->n_front, it, front);
+  if (pi.kind != 1) return;
+  const Front fr = front[pi.k];
+  const Decision d = dec[pi.k];
+  const uint8_t* colf = col + (uint64_t)d.feature * c.n_rows;
+  const uint64_t words = (c.n_rows + 63) / 64;
+  const uint64_t* missf = colmiss ? colmiss + (uint64_t)d.feature * words : nullptr;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const uint32_t base = fr.begin + pi.off;
+  uint32_t row[kPerThread];
+#pragma unroll
+  for (int j = 0; j < kPerThread; ++j) {
+    const uint32_t i = warp * 256 + j * 32 + lane;
+    const uint32_t at = base + min(i, pi.len - 1);
+    row[j] = identity ? at : rows_in[at];
+  }
+  const uint32_t csr_lo = CSR ? __ldg(c.fo + d.feature) : 0u;
+  const uint32_t csr_hi = CSR ? __ldg(c.fo + d.feature + 1) : 0u;
+  uint32_t bal[kPerThread];
+  uint32_t wl = 0;
+#pragma unroll
+  for (int j = 0; j < kPerThread; ++j) {
+    const uint32_t r = row[j];
+    bool miss;
+    uint32_t bin;
+    if (CSR) {
+      uint32_t lb = 0;
+      miss = !csr_find(c.csr_bins, __ldg(c.csr_ptr + r), __ldg(c.csr_ptr + r + 1), csr_lo, csr_hi, lb);
+      bin = lb;
+    } else {
+      bin = colf[r];
+      miss = missf && ((missf[r >> 6] >> (r & 63)) & 1ull);
+    }
+    const uint32_t i = warp * 256 + j * 32 + lane;
+    const bool left = i < pi.len && (miss ? (d.default_left != 0) : (bin < d.limit));
+    bal[j] = __ballot_sync(kFull, left);
+    wl += __popc(bal[j]);
+  }
+  // the warps' left counts, the tile's totals and the chunk reservations
+  __shared__ uint32_t s_wl[kPartThreads / 32];
+  __shared__ uint32_t s_base_l, s_base_r;
+  if (lane == 0) s_wl[warp] = wl;
+  __syncthreads();
+  uint32_t before = 0, tile_l = 0;
+  for (int w = 0; w < kPartThreads / 32; ++w) {
+    before += w < warp ? s_wl[w] : 0u;
+    tile_l += s_wl[w];
+  }
+  const uint32_t tile_r = pi.len - tile_l;
+  if (threadIdx.x == 0) {
+    s_base_l = tile_l ? atomicAdd(&fill[2 * d.pair], tile_l) : 0u;
+    s_base_r = tile_r ? atomicAdd(&fill[2 * d.pair + 1], tile_r) : 0u;
+  }
+  __syncthreads();
+  const uint32_t left0 = fr.begin + s_base_l;                        // this tile's left chunk
+  const uint32_t right0 = fr.begin + fr.len - s_base_r - tile_r;     // and right chunk
+  const uint32_t lt = (1u << lane) - 1u;
+#pragma unroll
+  for (int j = 0; j < kPerThread; ++j) {
+    const uint32_t i = warp * 256 + j * 32 + lane;
+    const uint32_t lrank = before + __popc(bal[j] & lt);  // left rows of the tile before row i
+    if (i < pi.len) {
+      if ((bal[j] >> lane) & 1u)
+        rows_out[left0 + lrank] = row[j];
+      else
+        rows_out[right0 + (i - lrank)] = row[j];
+    }
+    before += __popc(bal[j]);
+  }
+}
+
+// After k_part_onepass: the children's segments from the fill counts (the
+// left child first), the counts cleared for the next level, then the next
+// level's histogram plan. One CTA of kApplyThreads.
+__device__ void hist_plan_body(const Front* __restrict__ front, const Decision* __restrict__ dec,
+                               const LevelState* __restrict__ ls, const Front* next,
+                               HEntry* __restrict__ entries, Triple* __restrict__ pairs,
+                               LevelState* __restrict__ ls_next, int terminal);
+__global__ void __launch_bounds__(1024)
+    k_part_plan(const Front* __restrict__ front, const Decision* __restrict__ dec, const LevelState* ls,
+                uint32_t* __restrict__ fill, Front* next, HEntry* __restrict__ entries,
+                Triple* __restrict__ pairs, LevelState* __restrict__ ls_next) {
+  pdl_wait();
+  const int k = threadIdx.x;
+  if (k < ls->n_front) {
+    const Decision d = dec[k];
+    if (d.split) {
+      const Front fr = front[k];
+      const uint32_t L = fill[2 * d.pair];
+      next[2 * d.pair].begin = fr.begin;
+      next[2 * d.pair].len = L;
+      next[2 * d.pair + 1].begin = fr.begin + L;
+      next[2 * d.pair + 1].len = fr.len - L;
+      fill[2 * d.pair] = 0u;
+      fill[2 * d.pair + 1] = 0u;
+    }
+  }
+  __syncthreads();
+  hist_plan_body(front, dec, ls, next, entries, pairs, ls_next, 0);
+}
+
 // One CTA per splitting frontier node: exclusive scan of its tiles' left
 // counts (each thread sums kScanPer consecutive tiles, then one block scan
 // covers kScanThreads * kScanPer tiles); the children's segments. With
@@ -2986,6 +3107,24 @@ void launch_part_count(const DevConst& c, const uint8_t* col, const uint64_t* co
   else
     launch_pdl(k_part_count<false>, dim3(max_items), dim3(kPartThreads), 0, s, c, col, colmiss, rec, use_record, rows_in, identity,
                                                          front, dec, items, ls, dirbits, item_left, rows_copy);
+}
+
+void launch_part_onepass(const DevConst& c, const uint8_t* col, const uint64_t* colmiss,
+                         const uint32_t* rows_in, int identity, const Front* front, const Decision* dec,
+                         const LevelState* ls, int max_items, uint32_t* fill, uint32_t* rows_out,
+                         cudaStream_t s) {
+  if (c.csr)
+    launch_pdl(k_part_onepass<true>, dim3(max_items), dim3(kPartThreads), 0, s, c, col, colmiss, rows_in,
+               identity, front, dec, ls, fill, rows_out);
+  else
+    launch_pdl(k_part_onepass<false>, dim3(max_items), dim3(kPartThreads), 0, s, c, col, colmiss, rows_in,
+               identity, front, dec, ls, fill, rows_out);
+}
+
+void launch_part_plan(const Front* front, const Decision* dec, const LevelState* ls, uint32_t* fill,
+                      Front* next, HEntry* entries, Triple* pairs, LevelState* ls_next, cudaStream_t s) {
+  launch_pdl(k_part_plan, dim3(1), dim3(kApplyThreads), 0, s, front, dec, ls, fill, next, entries, pairs,
+             ls_next);
 }
 
 void launch_part_scan(const Front* front, const Decision* dec, LevelState* ls, int max_front,

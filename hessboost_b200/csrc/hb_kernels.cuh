@@ -74,6 +74,17 @@ void launch_part_count(const DevConst& c, const uint8_t* col, const uint64_t* co
                        const Front* front, const Decision* dec, const PItem* items,
                        const LevelState* ls, int max_items, uint32_t* dirbits, uint32_t* item_left,
                        cudaStream_t s, uint32_t* rows_copy = nullptr);
+// One-pass partition (depthwise growth): each tile's left rows to a chunk at
+// its node's segment start, right rows to one at the end, reserved on
+// fill[2 pair], fill[2 pair + 1] (zero before the pass); a child's row order
+// is not the stable one. Then launch_part_plan: the children's segments,
+// the fill counts cleared, the next level's histogram plan.
+void launch_part_onepass(const DevConst& c, const uint8_t* col, const uint64_t* colmiss,
+                         const uint32_t* rows_in, int identity, const Front* front, const Decision* dec,
+                         const LevelState* ls, int max_items, uint32_t* fill, uint32_t* rows_out,
+                         cudaStream_t s);
+void launch_part_plan(const Front* front, const Decision* dec, const LevelState* ls, uint32_t* fill,
+                      Front* next, HEntry* entries, Triple* pairs, LevelState* ls_next, cudaStream_t s);
 // Per-node scan of the tiles' left counts and the children's segments; with
 // `entries` (device growth) the last CTA also plans the next level's
 // histograms (built child = smaller Hessian; entries, sibling pairs, ls_next).

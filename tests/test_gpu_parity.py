@@ -620,6 +620,21 @@ def test_row_block_layout_agrees(monkeypatch, n_cols, grow):
     np.testing.assert_array_equal(_bits(runs[0].predict_margin(x)), _bits(runs[1].predict_margin(x)))
 
 
+@pytest.mark.parametrize("n_cols,missing", [(28, 0.05), (6, 0.2), (40, 0.0)])
+def test_one_pass_partition_agrees_with_the_stable_one(monkeypatch, n_cols, missing):
+    """Depthwise growth with the one-pass partition (children's rows in
+    reservation order) and with the stable three-pass one grows the same
+    forest and margins: nothing computed from a segment depends on the
+    order of its rows."""
+    x, y = synth.logistic_c2(300_007, n_cols, seed=60 + n_cols, missing=missing)
+    runs = []
+    for stable in ("0", "1"):
+        monkeypatch.setenv("HB_STABLE_PARTITION", stable)
+        runs.append(gpu_train(x, y, 4, objective="binary:logistic", max_depth=7, eta=0.3))
+    assert_forest_equal(runs[0].nodes, runs[0].tree_ptr, runs[1].nodes, runs[1].tree_ptr, "one pass vs stable")
+    np.testing.assert_array_equal(_bits(runs[0].predict_margin(x)), _bits(runs[1].predict_margin(x)))
+
+
 @pytest.mark.parametrize("max_bin", [16, 48, 128])
 def test_scan_kernels_agree(monkeypatch, max_bin):
     """The warp-per-feature split scan (features of <= 128 bins) and the
