@@ -281,6 +281,7 @@ SIGNATURES = {
     "hb_engine_inject_fault": [_vp, ctypes.c_int32],
     "hb_probe_smem": [ctypes.c_int32, ctypes.c_int32, ctypes.c_int32, ctypes.c_int32,
                       ctypes.POINTER(ctypes.c_double)],
+    "hb_peer_wait_probe": [ctypes.c_int32, ctypes.c_int32, _u64p, ctypes.POINTER(ctypes.c_double)],
 }
 _STRING_RESULT = ("hb_engine_last_error", "hb_sketch_last_error")
 

@@ -13,8 +13,8 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 CSRC = os.path.join(HERE, "csrc")
 OUT_DIR = os.path.join(HERE, "_lib")
 LIB = os.path.join(OUT_DIR, "libhb_cuda.so")
-SOURCES = ["hb_kernels.cu", "hb_engine.cu", "hb_predict.cu", "hb_noalloc.cu", "hb_probe.cu", "hb_sketch.cu", "hb_host_bins.cpp",
-           "hb_model_io.cpp"]
+SOURCES = ["hb_kernels.cu", "hb_engine.cu", "hb_peer.cu", "hb_predict.cu", "hb_noalloc.cu", "hb_probe.cu", "hb_sketch.cu",
+           "hb_host_bins.cpp", "hb_model_io.cpp"]
 NVCC = os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc")
 FLAGS = [
     "-gencode", "arch=compute_100a,code=sm_100a",

@@ -136,6 +136,15 @@ struct hb_engine {
   // sharding
   ncclComm_t comm = nullptr;
   int nranks = 1, rank = 0;
+  // Level histograms summed over peer memory (hb_peer.cu) instead of NCCL:
+  // every rank's hist_all and barrier block mapped here by CUDA IPC.
+  // HB_PEER_ALLREDUCE=0 keeps the NCCL allreduce.
+  bool peer_mode = true;
+  bool peer_ready = false;
+  const void* peer_for = nullptr;     // the hist_all the mapping was made for
+  DevBuf<unsigned long long> pbar;    // this rank's barrier block
+  std::vector<void*> peer_opened;     // IPC mappings to close
+  PeerSet ps{};
   uint64_t row_begin = 0;
   uint64_t shard_global = 0;  // rows of the whole matrix when this engine holds a shard (0: not sharded)
 
@@ -307,6 +316,119 @@ hb_status ensure_growth_buffers(hb_engine* e, int max_depth) {
   return HB_OK;
 }
 
+void close_peers(hb_engine* e) {
+  for (void* p : e->peer_opened) cudaIpcCloseMemHandle(p);
+  e->peer_opened.clear();
+  e->peer_ready = false;
+  e->peer_for = nullptr;
+}
+
+// Map every rank's hist_all and barrier block for the peer allreduce (a
+// collective: every rank of the communicator calls it at the same point,
+// before any round is captured). Re-mapped when this engine's hist_all has
+// moved; a failure to map leaves the NCCL allreduce in use.
+hb_status ensure_peers(hb_engine* e) {
+  if (!e->comm || !e->peer_mode || e->nranks < 2 || e->nranks > kPeerMax) return HB_OK;
+  // every rank remaps when any rank's buffer moved (one max-allreduce)
+  DevBuf<int> flag;
+  HB_CK(e, flag.alloc(1));
+  const int moved = (!e->peer_ready || e->peer_for != (const void*)e->hist_all.p) ? 1 : 0;
+  HB_CK(e, cudaMemcpyAsync(flag.p, &moved, 4, cudaMemcpyHostToDevice, e->stream));
+  HB_NCCL(e, ncclAllReduce(flag.p, flag.p, 1, ncclInt32, ncclMax, e->comm, e->stream));
+  int any = 0;
+  HB_CK(e, cudaMemcpyAsync(&any, flag.p, 4, cudaMemcpyDeviceToHost, e->stream));
+  HB_CK(e, cudaStreamSynchronize(e->stream));
+  if (!any) return HB_OK;
+  close_peers(e);
+  if (e->round_exec) cudaGraphExecDestroy(e->round_exec);  // captured with the old peers
+  e->round_exec = nullptr;
+  HB_CK(e, e->pbar.alloc(kPeerWords));
+  HB_CK(e, cudaMemset(e->pbar.p, 0, sizeof(unsigned long long) * kPeerWords));
+  // this rank's two IPC handles, gathered from every rank
+  const int n = e->nranks;
+  std::vector<unsigned char> mine(2 * sizeof(cudaIpcMemHandle_t)), all(n * mine.size());
+  cudaIpcMemHandle_t h0, h1;
+  cudaError_t ie = cudaIpcGetMemHandle(&h0, e->hist_all.p);
+  if (ie == cudaSuccess) ie = cudaIpcGetMemHandle(&h1, e->pbar.p);
+  int ok = ie == cudaSuccess ? 1 : 0;
+  if (!ok) cudaGetLastError();
+  std::memcpy(mine.data(), &h0, sizeof(h0));
+  std::memcpy(mine.data() + sizeof(h0), &h1, sizeof(h1));
+  DevBuf<unsigned char> xb;
+  HB_CK(e, xb.alloc(all.size()));
+  HB_CK(e, cudaMemcpyAsync(xb.p + (size_t)e->rank * mine.size(), mine.data(), mine.size(),
+                           cudaMemcpyHostToDevice, e->stream));
+  HB_NCCL(e, ncclAllGather(xb.p + (size_t)e->rank * mine.size(), xb.p, mine.size(), ncclUint8, e->comm,
+                           e->stream));
+  HB_CK(e, cudaMemcpyAsync(all.data(), xb.p, all.size(), cudaMemcpyDeviceToHost, e->stream));
+  HB_CK(e, cudaStreamSynchronize(e->stream));
+  PeerSet ps{};
+  ps.n = n;
+  ps.rank = e->rank;
+  const char* to = std::getenv("HB_PEER_TIMEOUT_MS");
+  ps.timeout_ns = (uint64_t)(to ? std::max(1, std::atoi(to)) : 5000) * 1000000ull;
+  for (int j = 0; j < n && ok; ++j) {
+    if (j == e->rank) {
+      ps.hist[j] = e->hist_all.p;
+      ps.bar[j] = e->pbar.p;
+      continue;
+    }
+    cudaIpcMemHandle_t a, b;
+    std::memcpy(&a, all.data() + (size_t)j * mine.size(), sizeof(a));
+    std::memcpy(&b, all.data() + (size_t)j * mine.size() + sizeof(a), sizeof(b));
+    void* pa = nullptr;
+    void* pb = nullptr;
+    if (cudaIpcOpenMemHandle(&pa, a, cudaIpcMemLazyEnablePeerAccess) != cudaSuccess ||
+        cudaIpcOpenMemHandle(&pb, b, cudaIpcMemLazyEnablePeerAccess) != cudaSuccess) {
+      cudaGetLastError();
+      if (pa) cudaIpcCloseMemHandle(pa);
+      ok = 0;
+      break;
+    }
+    e->peer_opened.push_back(pa);
+    e->peer_opened.push_back(pb);
+    ps.hist[j] = reinterpret_cast<longlong2*>(pa);
+    ps.bar[j] = reinterpret_cast<unsigned long long*>(pb);
+  }
+  // every rank takes the peer path only if every rank mapped every peer
+  HB_CK(e, cudaMemcpyAsync(flag.p, &ok, 4, cudaMemcpyHostToDevice, e->stream));
+  HB_NCCL(e, ncclAllReduce(flag.p, flag.p, 1, ncclInt32, ncclMin, e->comm, e->stream));
+  int all_ok = 0;
+  HB_CK(e, cudaMemcpyAsync(&all_ok, flag.p, 4, cudaMemcpyDeviceToHost, e->stream));
+  HB_CK(e, cudaStreamSynchronize(e->stream));
+  if (!all_ok) {
+    close_peers(e);
+    e->peer_mode = false;  // NCCL from now on
+    return HB_OK;
+  }
+  e->ps = ps;
+  e->peer_ready = true;
+  e->peer_for = e->hist_all.p;
+  return HB_OK;
+}
+
+// The sum over ranks of hist_all's longlong2 words [first, first + count).
+hb_status allreduce_hist(hb_engine* e, uint64_t first, uint64_t count) {
+  if (e->peer_ready && e->peer_for == (const void*)e->hist_all.p) {
+    launch_peer_allreduce(e->ps, first, count, e->n_sm, e->stream);
+    e->kernel_launches += 1;
+    HB_CK(e, cudaGetLastError());
+    return HB_OK;
+  }
+  HB_NCCL(e, ncclAllReduce(e->hist_all.p + first, e->hist_all.p + first, 2 * count, ncclInt64, ncclSum, e->comm,
+                           e->stream));
+  return HB_OK;
+}
+
+// A peer wait that timed out fails the engine (read after a synchronize).
+hb_status check_peers(hb_engine* e) {
+  if (!e->peer_ready) return HB_OK;
+  unsigned long long st = 0;
+  HB_CK(e, cudaMemcpy(&st, e->pbar.p + kPeerStatus, sizeof(st), cudaMemcpyDeviceToHost));
+  if (st) return fail(e, "peer histogram exchange: a rank did not arrive in time", cudaErrorTimeout);
+  return HB_OK;
+}
+
 // Stage this tree's scale: reduce the maxima over ranks, then the exponents.
 hb_status finish_scale(hb_engine* e) {
   if (e->comm) {
@@ -436,8 +558,8 @@ hb_status grow_device(hb_engine* e, const hb_train_params* p, bool to_forest) {
   mark_end(e);
   HB_CK(e, cudaGetLastError());
   if (e->comm) {
-    HB_NCCL(e, ncclAllReduce(e->hist_all.p, e->hist_all.p, 2 * (1 + (size_t)c.total_bins), ncclInt64,
-                             ncclSum, e->comm, s));
+    hb_status ast = allreduce_hist(e, 0, 1 + (uint64_t)c.total_bins);
+    if (ast != HB_OK) return ast;
   }
   launch_root_stats(e->front[0].p, totals, s);
 
@@ -498,9 +620,9 @@ hb_status grow_device(hb_engine* e, const hb_train_params* p, bool to_forest) {
                 nullptr, e->row_stats.p, hgrid, smem, s);
     mark_end(e);
     if (e->comm) {
-      const size_t base = (size_t(1) << (d + 1)) - 1, half = size_t(1) << d;
-      HB_NCCL(e, ncclAllReduce(hist + base * c.total_bins, hist + base * c.total_bins,
-                               2 * half * c.total_bins, ncclInt64, ncclSum, e->comm, s));
+      const uint64_t base = (uint64_t(1) << (d + 1)) - 1, half = uint64_t(1) << d;
+      hb_status ast = allreduce_hist(e, 1 + base * c.total_bins, half * c.total_bins);
+      if (ast != HB_OK) return ast;
     }
     launches += 3;  // partition (+ 1 for the stable one) and histogram
     HB_CK(e, cudaGetLastError());
@@ -751,6 +873,8 @@ hb_status hb_engine_create(int32_t device_ordinal, hb_engine** out) {
   e->use_graphs = !(ng && ng[0] == '1');
   const char* sp = std::getenv("HB_STABLE_PARTITION");
   e->stable_partition = sp && sp[0] == '1';
+  const char* pa = std::getenv("HB_PEER_ALLREDUCE");
+  e->peer_mode = !(pa && pa[0] == '0');
 
   if (e->scale.alloc(1) != cudaSuccess || e->tree_counter.alloc(1) != cudaSuccess ||
       e->seg_total.alloc(2) != cudaSuccess || e->row_stats.alloc(2) != cudaSuccess ||
@@ -770,6 +894,8 @@ hb_status hb_engine_destroy(hb_engine* e) {
   // the round graph holds the level allreduces: release it before the communicator
   if (e->round_exec) cudaGraphExecDestroy(e->round_exec);
   e->round_exec = nullptr;
+  close_peers(e);
+  e->pbar.release();
   if (e->comm) ncclCommDestroy(e->comm);
   for (auto x : e->ev) cudaEventDestroy(x);
   for (auto x : e->run_ev)
@@ -1938,13 +2064,15 @@ hb_status hb_train_rounds(hb_engine* e, const hb_train_params* p, int32_t rounds
   HB_CK(e, cudaMemsetAsync(e->tree_counter.p, 0, 4, s));
   if (e->use_graphs && rounds > 0) {
     st = ensure_buffers(e, p);
+    if (st == HB_OK) st = ensure_peers(e);
     if (st != HB_OK) return st;
     st = graph_rounds(e, p, rounds);
     if (st != HB_OK) return st;
   } else {
-    HB_CK(e, cudaEventRecord(e->run_ev[0], s));
     st = ensure_buffers(e, p);
+    if (st == HB_OK && rounds > 0) st = ensure_peers(e);
     if (st != HB_OK) return st;
+    HB_CK(e, cudaEventRecord(e->run_ev[0], s));
     for (int r = 0; r < rounds; ++r) {
       st = round_work(e, p);
       if (st != HB_OK) return st;
@@ -1957,6 +2085,8 @@ hb_status hb_train_rounds(hb_engine* e, const hb_train_params* p, int32_t rounds
   std::vector<uint32_t> cnt(std::max(trees, 1));
   HB_CK(e, cudaMemcpyAsync(cnt.data(), e->counts.p, 4 * (size_t)std::max(trees, 1), cudaMemcpyDeviceToHost, s));
   HB_CK(e, cudaStreamSynchronize(s));
+  st = check_peers(e);
+  if (st != HB_OK) return st;
   collect_timers(e);
   {
     float ms = 0.0f;
@@ -2058,6 +2188,7 @@ hb_status hb_comm_init(hb_engine* e, int32_t nranks, int32_t rank, const uint8_t
     HB_CK(e, cudaStreamSynchronize(e->stream));
     if (e->round_exec) cudaGraphExecDestroy(e->round_exec);  // captured with the old communicator
     e->round_exec = nullptr;
+    close_peers(e);
     ncclCommDestroy(e->comm);
     e->comm = nullptr;
   }

@@ -108,6 +108,24 @@ inline uint64_t rec_bytes(uint64_t n, uint32_t stride, uint32_t blk) {
   return (blk ? (n + blk - 1) / blk * kBlockBytes : n * stride) + 64;
 }
 
+// Peer-memory histogram exchange (hb_peer.cu): every rank's histogram
+// buffer and barrier block, mapped into this rank's address space. A
+// barrier block holds the arrive flags [kPeerMax], the depart flags
+// [kPeerMax] (one per rank, raised to the launch's epoch by that rank),
+// then the epoch of the last completed launch, a count of finished CTAs
+// and a sticky status word (nonzero: a wait timed out).
+constexpr int kPeerMax = 8;
+constexpr int kPeerThreads = 256;
+constexpr int kPeerArrive = 0, kPeerDepart = 1;
+constexpr int kPeerEpoch = 2 * kPeerMax, kPeerCount = kPeerEpoch + 1, kPeerStatus = kPeerEpoch + 2;
+constexpr int kPeerWords = kPeerEpoch + 8;
+struct PeerSet {
+  longlong2* hist[kPeerMax];
+  unsigned long long* bar[kPeerMax];
+  int n, rank;
+  uint64_t timeout_ns;
+};
+
 // One frontier entry of the level being grown. The first 32 bytes are read
 // as two int4 by the histogram plan (load_front_cg), so every entry of a
 // Front array starts on a 16-byte boundary: 16-byte alignment, a size that is

@@ -20,6 +20,8 @@
 
 namespace hb {
 
+bool g_pdl = true;
+
 namespace {
 
 constexpr unsigned kFull = 0xffffffffu;
@@ -27,34 +29,6 @@ constexpr float kBelowAll = -FLT_MAX;         // src/tree/builder/mod.rs:308
 constexpr double kRtEps = 1e-6;               // src/lib.rs:366
 
 __device__ __forceinline__ double ll2d(long long v) { return __ll2double_rn(v); }
-
-// Kernels of the round are launched with programmatic stream serialization
-// (launch_pdl): a kernel may be scheduled while the one before it on the
-// stream finishes, so each begins by waiting for that kernel's completion
-// and memory (griddepcontrol.wait, a no-op after a plain launch). This
-// hides the launch latency between the round's dependent kernels.
-__device__ __forceinline__ void pdl_wait() {
-  asm volatile("griddepcontrol.wait;" ::: "memory");
-  // let the next kernel be scheduled now: it waits for this one in turn
-  asm volatile("griddepcontrol.launch_dependents;");
-}
-
-bool g_pdl = true;  // HB_NO_PDL=1: plain launches
-
-template <typename... P, typename... A>
-static void launch_pdl(void (*kernel)(P...), dim3 grid, dim3 block, size_t smem, cudaStream_t s, A&&... args) {
-  cudaLaunchAttribute at[1];
-  at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-  at[0].val.programmaticStreamSerializationAllowed = 1;
-  cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = grid;
-  cfg.blockDim = block;
-  cfg.dynamicSmemBytes = smem;
-  cfg.stream = s;
-  cfg.attrs = at;
-  cfg.numAttrs = g_pdl ? 1 : 0;
-  cudaLaunchKernelEx(&cfg, kernel, std::forward<A>(args)...);
-}
 
 // Word k (0..7) of a 32-byte record held as two uint4.
 __device__ __forceinline__ uint32_t pick_word(const uint4& a, const uint4& b, int k) {

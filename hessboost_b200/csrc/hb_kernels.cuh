@@ -3,9 +3,39 @@
 
 #include <cuda_runtime.h>
 
+#include <utility>
+
 #include "hb_internal.h"
 
 namespace hb {
+
+// Kernels of the round are launched with programmatic stream serialization
+// (launch_pdl): a kernel may be scheduled while the one before it on the
+// stream finishes, so each begins with pdl_wait(), which waits for that
+// kernel's completion and memory (griddepcontrol.wait, a no-op after a
+// plain launch) and lets the next kernel be scheduled in turn. This hides
+// the launch latency between the round's dependent kernels.
+__device__ __forceinline__ void pdl_wait() {
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  asm volatile("griddepcontrol.launch_dependents;");
+}
+
+extern bool g_pdl;  // false (HB_NO_PDL=1): plain launches
+
+template <typename... P, typename... A>
+inline void launch_pdl(void (*kernel)(P...), dim3 grid, dim3 block, size_t smem, cudaStream_t s, A&&... args) {
+  cudaLaunchAttribute at[1];
+  at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  at[0].val.programmaticStreamSerializationAllowed = 1;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cfg.attrs = at;
+  cfg.numAttrs = g_pdl ? 1 : 0;
+  cudaLaunchKernelEx(&cfg, kernel, std::forward<A>(args)...);
+}
 
 // Objective gradients at `margin` (the host's bits, see hb_kernels.cu) plus
 // the largest |g|, |h| and a non-finite flag, folded into `scale`.
@@ -126,5 +156,11 @@ void launch_seg_total(const uint32_t* rows, uint64_t begin, uint64_t len, const 
                       const Scale* scale, long long* totals, int n_sm, cudaStream_t s);
 void launch_add_segment(const uint32_t* rows, uint32_t begin, uint32_t len, float value,
                         float* margin, cudaStream_t s);
+
+// Sum of the histogram words [first, first + count) (longlong2 units) over
+// the ranks of `ps`, left in every rank's buffer (hb_peer.cu).
+void launch_peer_allreduce(const PeerSet& ps, uint64_t first, uint64_t count, int n_sm, cudaStream_t s);
+// One CTA waiting, bounded by ps.timeout_ns, on a flag nothing raises.
+void launch_peer_wait_probe(const PeerSet& ps, cudaStream_t s);
 
 }  // namespace hb

@@ -452,6 +452,14 @@ hb_status hb_engine_inject_fault(hb_engine* e, int32_t after_calls);
 hb_status hb_probe_smem(int32_t device, int32_t kind, int32_t threads, int32_t iters,
                         double* lane_ops_per_clk);
 
+/* The bounded wait of the peer-memory histogram exchange, on one GPU: one
+ * CTA waits for a peer flag that nothing raises, limited to timeout_ms of
+ * the GPU's global timer. *status receives the barrier block's status word
+ * afterwards (1: the wait gave up), *waited_ms the kernel's event time.
+ * The multi-GPU exchange fails an engine the same way when a rank does not
+ * arrive (hb_train_rounds then returns HB_DEVICE_FAILED). */
+hb_status hb_peer_wait_probe(int32_t device, int32_t timeout_ms, uint64_t* status, double* waited_ms);
+
 #ifdef __cplusplus
 }
 #endif

@@ -158,4 +158,5 @@ extern "C" {
     pub fn hb_probe_smem(device: i32, kind: i32, threads: i32, iters: i32,
                          lane_ops_per_clk: *mut f64) -> hb_status;
     pub fn hb_engine_inject_fault(e: *mut hb_engine, after_calls: i32) -> hb_status;
+    pub fn hb_peer_wait_probe(device: i32, timeout_ms: i32, status: *mut u64, waited_ms: *mut f64) -> hb_status;
 }

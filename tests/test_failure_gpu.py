@@ -111,3 +111,18 @@ def test_fresh_engine_after_failures_trains_bit_exact(data):
     x, y, p, m, want = data
     got = H.train(p, y=y, rounds=3, matrix=m)
     assert _forest_bits(got) == _forest_bits(want)
+
+
+def test_peer_exchange_wait_gives_up():
+    """The peer-memory histogram exchange bounds every wait on another
+    rank's flag by the GPU's global timer: a wait on a flag that nothing
+    raises returns after the limit with the status word set (the engine
+    then fails with HB_DEVICE_FAILED), and the GPU stays usable."""
+    import ctypes
+
+    st, ms = ctypes.c_uint64(), ctypes.c_double()
+    assert H.lib().hb_peer_wait_probe(0, 200, ctypes.byref(st), ctypes.byref(ms)) == H.HB_OK
+    assert st.value == 1
+    assert 190.0 <= ms.value < 2000.0, ms.value
+    x, y = synth.logistic_c2(5_003, 6, seed=3)
+    H.train(H.TrainingParams(objective="binary:logistic", max_depth=3), x, y, 1)

@@ -32,12 +32,16 @@ def _free_port():
 
 
 @pytest.mark.skipif("_gpus() < 2")
-def test_two_gpus_grow_the_one_gpu_forest(tmp_path):
+@pytest.mark.parametrize("exchange", ["peer", "nccl"])
+def test_two_gpus_grow_the_one_gpu_forest(tmp_path, exchange):
+    """Both level-histogram exchanges: the peer-memory allreduce (the
+    default) and NCCL's (HB_PEER_ALLREDUCE=0)."""
     out = tmp_path / "sharded.npz"
     cmd = ["timeout", "-k", "30", "600", sys.executable, "-m", "torch.distributed.run", "--nnodes=1",
            "--nproc-per-node", "2", "--master-addr", "127.0.0.1", "--master-port", str(_free_port()),
            os.path.join(HERE, "mgpu_worker.py"), str(out)]
-    r = subprocess.run(cmd, capture_output=True, text=True)
+    env = dict(os.environ, HB_PEER_ALLREDUCE="1" if exchange == "peer" else "0", NCCL_NVLS_ENABLE="0")
+    r = subprocess.run(cmd, capture_output=True, text=True, env=env)
     assert r.returncode == 0, r.stdout[-3000:] + r.stderr[-3000:]
     got = np.load(out)
     for name, x, y, params, rounds in mgpu_worker.cases():
