@@ -34,8 +34,8 @@ def _free_port():
 @pytest.mark.skipif("_gpus() < 2")
 @pytest.mark.parametrize("exchange", ["peer", "nccl"])
 def test_two_gpus_grow_the_one_gpu_forest(tmp_path, exchange):
-    """Both level-histogram exchanges: the peer-memory allreduce (the
-    default) and NCCL's (HB_PEER_ALLREDUCE=0)."""
+    """Both level-histogram exchanges: NCCL's allreduce (the default) and
+    the peer-memory one (HB_PEER_ALLREDUCE=1)."""
     out = tmp_path / "sharded.npz"
     cmd = ["timeout", "-k", "30", "600", sys.executable, "-m", "torch.distributed.run", "--nnodes=1",
            "--nproc-per-node", "2", "--master-addr", "127.0.0.1", "--master-port", str(_free_port()),
