@@ -826,7 +826,7 @@ def main():
     torch.cuda.synchronize()
     e2e_s = allreduce_max(time.perf_counter() - t0)
     barrier()
-    h2d = (pcols.nbytes + (pmiss.nbytes if pmiss is not None else 0) + plab.nbytes + 4 * (end - begin)
+    h2d = (pcols.nbytes + (pmiss.nbytes if pmiss is not None else 0) + plab.nbytes
            + off.nbytes + cuts.nbytes)
     h2d_total = allreduce_sum(h2d)
     d2h_total = allreduce_sum(len(nodes2) * H.NODE_DTYPE.itemsize)

@@ -1998,11 +1998,8 @@ hb_status hb_train_begin(hb_engine* e, const float* labels, uint64_t n, float ba
   if (e->row_begin % 8) return refuse(e, "shards must start on a multiple of 8 rows");
   cudaStream_t s = e->stream;
   e->n_out = 1;
-  {
-    std::vector<float> m(n, base_margin);
-    HB_CK(e, cudaMemcpyAsync(e->margin.p, m.data(), 4 * n, cudaMemcpyHostToDevice, s));
-    HB_CK(e, cudaStreamSynchronize(s));
-  }
+  launch_fill(e->margin.p, base_margin, n, e->n_sm, s);  // every margin starts at the base
+  HB_CK(e, cudaGetLastError());
   e->margins_loaded = true;
   e->pending_tree = false;
   HB_CK(e, cudaMemsetAsync(e->flags.p, 0, sizeof(int), s));
@@ -2031,14 +2028,10 @@ hb_status hb_train_begin_classes(hb_engine* e, const float* labels, uint64_t n,
   HB_CK(e, e->margin.alloc(kn));
   HB_CK(e, e->gpair.alloc(kn));
   HB_CK(e, e->scale.alloc(n_classes));
-  {
-    std::vector<float> m(kn);
-    for (int k = 0; k < n_classes; ++k)
-      std::fill(m.begin() + (size_t)k * n, m.begin() + (size_t)(k + 1) * n, base_margins[k]);
-    HB_CK(e, cudaMemcpyAsync(e->margin.p, m.data(), 4 * kn, cudaMemcpyHostToDevice, s));
-    HB_CK(e, cudaMemcpyAsync(e->label.p, labels, 4 * n, cudaMemcpyHostToDevice, s));
-    HB_CK(e, cudaStreamSynchronize(s));
-  }
+  for (int k = 0; k < n_classes; ++k) launch_fill(e->margin.p + (size_t)k * n, base_margins[k], n, e->n_sm, s);
+  HB_CK(e, cudaGetLastError());
+  HB_CK(e, cudaMemcpyAsync(e->label.p, labels, 4 * n, cudaMemcpyHostToDevice, s));
+  HB_CK(e, cudaStreamSynchronize(s));
   e->label_key = nullptr;
   e->weight_key = nullptr;
   e->n_out = n_classes;

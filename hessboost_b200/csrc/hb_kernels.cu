@@ -2790,6 +2790,11 @@ __global__ void k_add_segment(const uint32_t* __restrict__ rows, uint32_t begin,
 // host):
 // rows[i] = first + i: the row list of a contiguous run, built on the device
 // instead of copied from the host.
+__global__ void k_fill(float* __restrict__ p, float v, uint64_t n) {
+  for (uint64_t i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (uint64_t)gridDim.x * blockDim.x)
+    p[i] = v;
+}
+
 __global__ void k_iota(uint32_t* __restrict__ rows, uint32_t first, uint64_t n) {
   for (uint64_t i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (uint64_t)gridDim.x * blockDim.x)
     rows[i] = first + (uint32_t)i;
@@ -2850,6 +2855,11 @@ __global__ void k_seg_total(const uint32_t* __restrict__ rows, uint64_t begin, u
 }
 
 }  // namespace
+
+void launch_fill(float* p, float v, uint64_t n, int n_sm, cudaStream_t s) {
+  const int grid = (int)std::max<uint64_t>(1, std::min<uint64_t>((n + 255) / 256, (uint64_t)n_sm * 8));
+  k_fill<<<grid, 256, 0, s>>>(p, v, n);
+}
 
 void launch_iota(uint32_t* rows, uint32_t first, uint64_t n, int n_sm, cudaStream_t s) {
   const int grid = (int)std::max<uint64_t>(1, std::min<uint64_t>((n + 255) / 256, (uint64_t)n_sm * 8));

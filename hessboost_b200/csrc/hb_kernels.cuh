@@ -147,6 +147,8 @@ void launch_dequantize(const longlong2* hist, uint32_t n, const Scale* scale, do
 // RowEngine helpers: an iota row list; leaf values added to every segment
 // at once; a partition's copy-back with the children's end rows; the
 // fixed-point totals of a segment.
+// p[0, n) = v.
+void launch_fill(float* p, float v, uint64_t n, int n_sm, cudaStream_t s);
 void launch_iota(uint32_t* rows, uint32_t first, uint64_t n, int n_sm, cudaStream_t s);
 void launch_add_segments(const uint32_t* rows, const uint2* segs, const float* values, uint32_t n,
                          float* margin, cudaStream_t s);
