@@ -635,6 +635,27 @@ def test_one_pass_partition_agrees_with_the_stable_one(monkeypatch, n_cols, miss
     np.testing.assert_array_equal(_bits(runs[0].predict_margin(x)), _bits(runs[1].predict_margin(x)))
 
 
+def test_engine_reused_across_uploads_of_one_shape():
+    """An engine keeps its captured round graph across uploads of the same
+    shape (the graph's key holds the index's constants and buffers): a
+    second matrix of the same shape, with other values, cuts and labels,
+    grows the forest a fresh engine grows; a matrix of another bin count
+    too (its graph is captured again)."""
+    p = H.TrainingParams(objective="binary:logistic", max_depth=6, eta=0.3)
+    mats = []
+    for seed, max_bin in ((71, 256), (72, 256), (73, 64)):
+        x, y = synth.logistic_c2(60_013, 28, seed=seed)
+        mats.append((H.BinnedMatrix.from_dense(x, max_bin), y))
+    eng = H.Engine()
+    try:
+        for m, y in mats:
+            got = H.train(p, y=y, rounds=3, matrix=m, engine=eng)
+            want = H.train(p, y=y, rounds=3, matrix=m)
+            assert_forest_equal(got.nodes, got.tree_ptr, want.nodes, want.tree_ptr, "reused engine")
+    finally:
+        eng.close()
+
+
 @pytest.mark.parametrize("max_bin", [16, 48, 128])
 def test_scan_kernels_agree(monkeypatch, max_bin):
     """The warp-per-feature split scan (features of <= 128 bins) and the
