@@ -854,7 +854,9 @@ struct StageRow {
 // (group << 7) | bin), else 1. A row's pair is staged once for all of them.
 template <int G>
 struct H32 {
-  static constexpr int kStages = G == 1 ? 3 : 2;    // rows staged ahead with cp.async
+  // rows staged ahead with cp.async: two stages leave the SM's L1 about 80 KB
+  // (three: about 57 KB, four: about 34 KB), which the gathered levels use
+  static constexpr int kStages = 2;
   static constexpr int kBinShift = G == 1 ? 8 : 7;  // log2(slot rows per group)
   static constexpr size_t smem() {
     return (size_t)kSlotStride * 16 +
