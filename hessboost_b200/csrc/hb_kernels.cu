@@ -371,13 +371,24 @@ __global__ void __launch_bounds__(kGradThreads, 4)
   bool nonfinite = false;
   const unsigned lane = threadIdx.x & 31;
   uint8_t* my_rec = s_rec + threadIdx.x * kRecPitch;
-  const uint64_t nblk = (n + 2) / 3;
-  const uint64_t step = (uint64_t)gridDim.x * blockDim.x;
+  // row indices in 32 bits (an engine holds fewer than 2^32 rows)
+  const uint32_t n32 = (uint32_t)n, v32 = (uint32_t)vrows;
+  const uint32_t nblk = (n32 + 2u) / 3u;
+  const uint32_t step = gridDim.x * blockDim.x;
+  // this lane's rows' logistic vector groups: for row j, the first of the
+  // (at most four) lanes holding its group, and the group's offset in them
+  uint32_t g_lane[3], g_off[3];
+#pragma unroll
+  for (int j = 0; j < 3; ++j) {
+    const uint32_t gs = (3u * lane + j) & ~7u;  // the group's first row within the warp's 96
+    g_lane[j] = gs / 3u;
+    g_off[j] = gs - 3u * g_lane[j];
+  }
   // the loop bound is per warp (its first block), so shuffles see every lane
-  for (uint64_t w0 = (uint64_t)blockIdx.x * blockDim.x + (threadIdx.x & ~31u); w0 < nblk; w0 += step) {
-    const uint64_t q = w0 + lane;
-    const uint64_t r0 = 3 * q;
-    uint8_t* line = rec + q * kBlockBytes;
+  for (uint32_t w0 = blockIdx.x * blockDim.x + (threadIdx.x & ~31u); w0 < nblk; w0 += step) {
+    const uint32_t q = w0 + lane;
+    const uint32_t r0 = 3u * q;
+    uint8_t* line = rec + (uint64_t)q * kBlockBytes;
     uint4 L[6];
     float m[3], y[3], w[3];
     if (wtree && q < nblk) {
@@ -386,7 +397,7 @@ __global__ void __launch_bounds__(kGradThreads, 4)
     }
 #pragma unroll
     for (int j = 0; j < 3; ++j) {
-      const bool in = r0 + j < n;
+      const bool in = r0 + j < n32;
       m[j] = in ? margin[r0 + j] : 0.0f;
       y[j] = in ? label[r0 + j] : 0.0f;
       w[j] = (in && weight) ? weight[r0 + j] : 1.0f;
@@ -419,7 +430,7 @@ __global__ void __launch_bounds__(kGradThreads, 4)
       }
 #pragma unroll
       for (int j = 0; j < 3; ++j) {
-        if (r0 + j < n) {
+        if (r0 + j < n32) {
           m[j] = __fadd_rn(m[j], s_leaf[idx[j] - inner]);
           margin[r0 + j] = m[j];
         }
@@ -428,7 +439,7 @@ __global__ void __launch_bounds__(kGradThreads, 4)
     } else if (wtree) {
 #pragma unroll
       for (int j = 0; j < 3; ++j) {
-        if (r0 + j < n) {
+        if (r0 + j < n32) {
           m[j] = __fadd_rn(m[j], walk_leaf_rec32(s_tree, L[2 * j], L[2 * j + 1], mask_word));
           margin[r0 + j] = m[j];
         }
@@ -438,18 +449,14 @@ __global__ void __launch_bounds__(kGradThreads, 4)
     if (kind == HB_LOSS_LOGISTIC) {
       uint32_t f = 0;
 #pragma unroll
-      for (int j = 0; j < 3; ++j) f |= (fabsf(m[j]) <= 80.0f || r0 + j >= n) ? (1u << j) : 0u;
+      for (int j = 0; j < 3; ++j) f |= (fabsf(m[j]) <= 80.0f || r0 + j >= n32) ? (1u << j) : 0u;
 #pragma unroll
       for (int j = 0; j < 3; ++j) {
-        const uint32_t r = 3 * lane + j;  // row within the warp's 96
-        const uint32_t gs = r & ~7u;      // its group's first row
-        const uint32_t ta = gs / 3u;      // the lane holding it
         uint32_t cat = 0;
 #pragma unroll
-        for (int k = 0; k < 4; ++k) cat |= __shfl_sync(kFull, f, min(ta + k, 31u)) << (3 * k);
-        const bool group_regular = ((cat >> (gs - 3u * ta)) & 0xffu) == 0xffu;
-        const uint64_t i = r0 + j;
-        const float p = (i < vrows && group_regular) ? sigmoid_vector(m[j]) : sigmoid_scalar(m[j]);
+        for (int k = 0; k < 4; ++k) cat |= __shfl_sync(kFull, f, min(g_lane[j] + k, 31u)) << (3 * k);
+        const bool group_regular = ((cat >> g_off[j]) & 0xffu) == 0xffu;
+        const float p = (r0 + j < v32 && group_regular) ? sigmoid_vector(m[j]) : sigmoid_scalar(m[j]);
         float wj = w[j];
         if (y[j] == 1.0f) wj = __fmul_rn(wj, spw);
         g[j] = __fmul_rn(__fsub_rn(p, y[j]), wj);
@@ -468,7 +475,7 @@ __global__ void __launch_bounds__(kGradThreads, 4)
     if (q < nblk) {
 #pragma unroll
       for (int j = 0; j < 3; ++j) {
-        if (r0 + j < n) {
+        if (r0 + j < n32) {
           gpair[r0 + j] = make_float2(g[j], h[j]);
           fold_max(g[j], h[j], mg, mh, nonfinite);
         } else {
