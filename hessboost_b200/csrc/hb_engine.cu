@@ -613,7 +613,7 @@ hb_status grow_device(hb_engine* e, const hb_train_params* p, bool to_forest) {
     } else {
       launch_part_onepass(c, e->col.p, e->has_missing ? e->colmiss.p : nullptr, rows_in, d == 0, fr,
                           e->dec.p, lsd, max_items, e->fill.p, rows_out, s);
-      launch_part_plan(fr, e->dec.p, lsd, e->fill.p, nx, e->entries.p, e->pairs.p, lsn, s);
+      launch_part_plan(fr, e->dec.p, lsd, e->fill.p, nx, e->entries.p, e->pairs.p, lsn, max_front, s);
     }
     mark_end(e);
     mark_begin(e, T_HIST);

@@ -1838,14 +1838,17 @@ __device__ __forceinline__ hb_tree_node make_leaf(float value, float sum_hess) {
 
 constexpr int kApplyThreads = 1024;
 
-__global__ void __launch_bounds__(kApplyThreads)
+// T threads, one per frontier node: 256 while the frontier fits, whose block
+// scans and barriers are shorter than 1024 threads'
+template <int T>
+__global__ void __launch_bounds__(T)
     k_apply(DevConst c, const uint32_t* __restrict__ fo, const float* __restrict__ cuts,
             const Cand* __restrict__ cand, const Front* __restrict__ front, Front* __restrict__ next,
             Decision* __restrict__ dec, PItem* __restrict__ items, LevelState* ls,
             LevelState* ls_next, hb_tree_node* __restrict__ tree, WNode* __restrict__ wtree,
             const Scale* __restrict__ scale, int depth, int leaf_only) {
   pdl_wait();
-  using Scan = cub::BlockScan<int, kApplyThreads>;
+  using Scan = cub::BlockScan<int, T>;
   __shared__ typename Scan::TempStorage tmp;
   const int n_front = ls->n_front;
   const int n_nodes = ls->n_nodes;
@@ -1856,10 +1859,10 @@ __global__ void __launch_bounds__(kApplyThreads)
   // Merge each node's per-feature winners, a warp per node: the largest
   // loss change, the lowest feature among equals, and only above the empty
   // split's 0 -- need_replace over ascending features.
-  __shared__ int s_best[kApplyThreads];
+  __shared__ int s_best[T];
   if (!leaf_only) {
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    for (int kk = warp; kk < n_front; kk += kApplyThreads / 32) {
+    for (int kk = warp; kk < n_front; kk += T / 32) {
       float bl = 0.0f;
       int bf = -1;
       for (uint32_t f = lane; f < c.n_cols; f += 32) {
@@ -2525,12 +2528,14 @@ __global__ void __launch_bounds__(kPartThreads)
 
 // After k_part_onepass: the children's segments from the fill counts (the
 // left child first), the counts cleared for the next level, then the next
-// level's histogram plan. One CTA of kApplyThreads.
+// level's histogram plan. One CTA of T threads, one per frontier node.
+template <int T>
 __device__ void hist_plan_body(const Front* __restrict__ front, const Decision* __restrict__ dec,
                                const LevelState* __restrict__ ls, const Front* next,
                                HEntry* __restrict__ entries, Triple* __restrict__ pairs,
                                LevelState* __restrict__ ls_next, int terminal);
-__global__ void __launch_bounds__(1024)
+template <int T>
+__global__ void __launch_bounds__(T)
     k_part_plan(const Front* __restrict__ front, const Decision* __restrict__ dec, const LevelState* ls,
                 uint32_t* __restrict__ fill, Front* next, HEntry* __restrict__ entries,
                 Triple* __restrict__ pairs, LevelState* __restrict__ ls_next) {
@@ -2550,7 +2555,7 @@ __global__ void __launch_bounds__(1024)
     }
   }
   __syncthreads();
-  hist_plan_body(front, dec, ls, next, entries, pairs, ls_next, 0);
+  hist_plan_body<T>(front, dec, ls, next, entries, pairs, ls_next, 0);
 }
 
 // One CTA per splitting frontier node: exclusive scan of its tiles' left
@@ -2558,6 +2563,7 @@ __global__ void __launch_bounds__(1024)
 // covers kScanThreads * kScanPer tiles); the children's segments. With
 // `entries`, the last CTA to finish then plans the next level's histograms
 // (hist_plan_body), which needs every node's segments.
+template <int T>
 __device__ void hist_plan_body(const Front* __restrict__ front, const Decision* __restrict__ dec,
                                const LevelState* __restrict__ ls, const Front* next,
                                HEntry* __restrict__ entries, Triple* __restrict__ pairs,
@@ -2614,7 +2620,7 @@ __global__ void __launch_bounds__(kScanThreads)
   __syncthreads();
   if (!s_last) return;
   __threadfence();
-  hist_plan_body(front, dec, ls, next, entries, pairs, ls_next, 0);
+  hist_plan_body<kScanThreads>(front, dec, ls, next, entries, pairs, ls_next, 0);
 }
 
 __global__ void __launch_bounds__(kPartThreads)
@@ -2690,11 +2696,12 @@ __device__ __forceinline__ Front load_front_cg(const Front* p) {
   return f;
 }
 
+template <int T>
 __device__ void hist_plan_body(const Front* __restrict__ front, const Decision* __restrict__ dec,
                                const LevelState* __restrict__ ls, const Front* next,
                                HEntry* __restrict__ entries, Triple* __restrict__ pairs,
                                LevelState* __restrict__ ls_next, int terminal) {
-  using Scan = cub::BlockScan<unsigned long long, kApplyThreads>;
+  using Scan = cub::BlockScan<unsigned long long, T>;
   __shared__ typename Scan::TempStorage tmp;
   const int k = threadIdx.x;
   const int n_front = ls->n_front;
@@ -3085,8 +3092,13 @@ void launch_apply(const DevConst& c, const uint32_t* fo, const float* cuts, cons
                   const Front* front, Front* next, Decision* dec, PItem* items, LevelState* ls,
                   LevelState* ls_next, hb_tree_node* tree, WNode* wtree, const Scale* scale,
                   int depth, int leaf_only, cudaStream_t s) {
-  launch_pdl(k_apply, dim3(1), dim3(kApplyThreads), 0, s, c, fo, cuts, cand, front, next, dec, items, ls, ls_next, tree,
-                                      wtree, scale, depth, leaf_only);
+  // the frontier at `depth` has at most 2^depth nodes
+  if (depth <= 8)
+    launch_pdl(k_apply<256>, dim3(1), dim3(256), 0, s, c, fo, cuts, cand, front, next, dec, items, ls, ls_next,
+               tree, wtree, scale, depth, leaf_only);
+  else
+    launch_pdl(k_apply<kApplyThreads>, dim3(1), dim3(kApplyThreads), 0, s, c, fo, cuts, cand, front, next, dec,
+               items, ls, ls_next, tree, wtree, scale, depth, leaf_only);
 }
 
 void launch_part_count(const DevConst& c, const uint8_t* col, const uint64_t* colmiss,
@@ -3115,9 +3127,13 @@ void launch_part_onepass(const DevConst& c, const uint8_t* col, const uint64_t* 
 }
 
 void launch_part_plan(const Front* front, const Decision* dec, const LevelState* ls, uint32_t* fill,
-                      Front* next, HEntry* entries, Triple* pairs, LevelState* ls_next, cudaStream_t s) {
-  launch_pdl(k_part_plan, dim3(1), dim3(kApplyThreads), 0, s, front, dec, ls, fill, next, entries, pairs,
-             ls_next);
+                      Front* next, HEntry* entries, Triple* pairs, LevelState* ls_next, int max_front,
+                      cudaStream_t s) {
+  if (max_front <= 256)
+    launch_pdl(k_part_plan<256>, dim3(1), dim3(256), 0, s, front, dec, ls, fill, next, entries, pairs, ls_next);
+  else
+    launch_pdl(k_part_plan<kApplyThreads>, dim3(1), dim3(kApplyThreads), 0, s, front, dec, ls, fill, next, entries,
+               pairs, ls_next);
 }
 
 void launch_part_scan(const Front* front, const Decision* dec, LevelState* ls, int max_front,

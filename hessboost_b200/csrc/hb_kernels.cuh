@@ -114,7 +114,8 @@ void launch_part_onepass(const DevConst& c, const uint8_t* col, const uint64_t* 
                          const LevelState* ls, int max_items, uint32_t* fill, uint32_t* rows_out,
                          cudaStream_t s);
 void launch_part_plan(const Front* front, const Decision* dec, const LevelState* ls, uint32_t* fill,
-                      Front* next, HEntry* entries, Triple* pairs, LevelState* ls_next, cudaStream_t s);
+                      Front* next, HEntry* entries, Triple* pairs, LevelState* ls_next, int max_front,
+                      cudaStream_t s);
 // Per-node scan of the tiles' left counts and the children's segments; with
 // `entries` (device growth) the last CTA also plans the next level's
 // histograms (built child = smaller Hessian; entries, sibling pairs, ls_next).
