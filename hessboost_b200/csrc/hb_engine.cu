@@ -602,7 +602,7 @@ hb_status grow_device(hb_engine* e, const hb_train_params* p, bool to_forest) {
     // feature columns, not row records: a level's gathers of one feature's
     // column and bitmap stay in L2, records do not
     if (e->stable_partition) {
-      launch_part_count(c, e->col.p, e->has_missing ? e->colmiss.p : nullptr, e->rec.p, 0,
+      launch_part_count(c, e->col.p, e->colmiss.p, e->rec.p, 0,
                         rows_in, d == 0, fr, e->dec.p, e->items.p, lsd, max_items, e->dirbits.p,
                         e->item_left.p, s);
       launch_part_scan(fr, e->dec.p, lsd, max_front, e->item_left.p, e->item_off.p, nx,
@@ -611,7 +611,7 @@ hb_status grow_device(hb_engine* e, const hb_train_params* p, bool to_forest) {
                           nx, rows_in, d == 0, rows_out, s);
       ++launches;
     } else {
-      launch_part_onepass(c, e->col.p, e->has_missing ? e->colmiss.p : nullptr, rows_in, d == 0, fr,
+      launch_part_onepass(c, e->col.p, e->colmiss.p, rows_in, d == 0, fr,
                           e->dec.p, lsd, max_items, e->fill.p, rows_out, s);
       launch_part_plan(fr, e->dec.p, lsd, e->fill.p, nx, e->entries.p, e->pairs.p, lsn, max_front, s);
     }
@@ -745,7 +745,7 @@ hb_status grow_lossguide(hb_engine* e, const hb_train_params* p, bool to_forest)
     // the count pass leaves a copy of the node's row ids in rows1, and the
     // scatter writes the children from it back into rows0, where every
     // pending node's rows stay
-    launch_part_count(c, e->col.p, e->has_missing ? e->colmiss.p : nullptr, e->rec.p, 0, rows0, k == 0,
+    launch_part_count(c, e->col.p, e->colmiss.p, e->rec.p, 0, rows0, k == 0,
                       fr, e->dec.p, e->items.p, ls1, e->max_items, e->dirbits.p, e->item_left.p, s,
                       rows1);
     launch_part_scan(fr, e->dec.p, ls1, 1, e->item_left.p, e->item_off.p, nx, e->entries.p,
@@ -1020,6 +1020,33 @@ static hb_status upload_csr(hb_engine* e, const hb_ghist* g, const RawSource* ra
   e->col.release();
   e->rec.release();
   e->colmiss.release();
+  c.csr_col = nullptr;
+  c.csr_colmiss = nullptr;
+  // The index also held feature-major when local bins fit a byte and the
+  // copy takes at most half the free memory (HB_CSR_COLUMNS=0: never): the
+  // partition and the walks read a row's split cell as one byte and one bit
+  // instead of binary-searching the row's bins.
+  const char* cc = std::getenv("HB_CSR_COLUMNS");
+  const uint64_t words = (n + 63) / 64;
+  // the bitmap unless every row stores every feature (an absent cell reads
+  // as missing, as the binary search finds it)
+  const uint64_t nnz = raw ? raw->nnz : g->row_ptr[n];
+  const bool bitmap = e->has_missing || nnz != n * (uint64_t)c.n_cols;
+  const uint64_t bytes = (uint64_t)c.n_cols * n + (bitmap ? 8ull * c.n_cols * words : 0ull);
+  size_t free_b = 0, total_b = 0;
+  if (!(cc && cc[0] == '0') && c.max_bins <= 256 && n && c.n_cols &&
+      cudaMemGetInfo(&free_b, &total_b) == cudaSuccess && bytes <= free_b / 2) {
+    HB_CK(e, e->col.alloc((size_t)c.n_cols * n));
+    HB_CK(e, cudaMemsetAsync(e->col.p, 0, (size_t)c.n_cols * n, s));
+    if (bitmap) {
+      HB_CK(e, e->colmiss.alloc((size_t)c.n_cols * words));
+      HB_CK(e, cudaMemsetAsync(e->colmiss.p, 0xFF, 8 * (size_t)c.n_cols * words, s));
+    }
+    launch_csr_columns(c, e->col.p, bitmap ? e->colmiss.p : nullptr, e->n_sm, s);
+    HB_CK(e, cudaGetLastError());
+    c.csr_col = e->col.p;
+    c.csr_colmiss = bitmap ? e->colmiss.p : nullptr;
+  }
   return HB_OK;
 }
 
@@ -1124,7 +1151,9 @@ static hb_status upload_index(hb_engine* e, const hb_ghist* g, const RawSource* 
   c.blk = (rb && rb[0] == '0') ? 0u : block_rows(c.stride);
   c.blk_pair = c.blk * c.stride;
   HB_CK(e, e->rec.alloc(rec_bytes(n, c.stride, c.blk)));
+  // the partition reads the bitmap whenever one is held
   if (e->has_missing) HB_CK(e, e->colmiss.alloc((size_t)c.n_cols * words));
+  else e->colmiss.release();
   HB_CK(e, e->gpair.alloc(n));
   HB_CK(e, e->margin.alloc(n));
   HB_CK(e, e->label.alloc(n));
@@ -1524,7 +1553,7 @@ hb_status hb_partition(hb_engine* e, const hb_row_split* splits, uint32_t n, hb_
     HB_CK(e, cudaMemcpyAsync(e->items.p, it.data(), sizeof(PItem) * n_items, cudaMemcpyHostToDevice, s));
   HB_CK(e, cudaMemcpyAsync(e->ls.p, &lsh, sizeof(LevelState), cudaMemcpyHostToDevice, s));
   if (n_items) {
-    launch_part_count(c, e->col.p, e->has_missing ? e->colmiss.p : nullptr, e->rec.p, 0,
+    launch_part_count(c, e->col.p, e->colmiss.p, e->rec.p, 0,
                       e->rows[0].p, 0, e->front[0].p, e->dec.p, e->items.p, e->ls.p, n_items,
                       e->dirbits.p, e->item_left.p, s);
   }

@@ -70,6 +70,11 @@ struct DevConst {
   uint32_t csr;
   const uint64_t* csr_ptr;
   const uint32_t* csr_bins;
+  // CSR index also held feature-major (NULL when not built): each cell's
+  // local bin (u8) at [f * n_rows + r] and the missing bitmap (absent cells
+  // set, NULL when every cell is present) at [f * words + r / 64]
+  const uint8_t* csr_col;
+  const uint64_t* csr_colmiss;
   const uint32_t* fo;
   // training parameters (RegParams rounded to f32 then widened)
   double lambda, alpha, gamma, mcw, mds;

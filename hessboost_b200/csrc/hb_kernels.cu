@@ -202,20 +202,70 @@ __device__ __forceinline__ float walk_leaf_csr(const WNode* __restrict__ t, cons
   return nd.leaf;
 }
 
+// The same leaf read from the feature-major copy of the index: one byte and
+// one bitmap bit per split instead of a binary search.
+__device__ __forceinline__ float walk_leaf_cols(const WNode* __restrict__ t, const DevConst& c,
+                                                uint64_t r, uint64_t words) {
+  WNode nd = t[0];
+  while (nd.left >= 0) {
+    const uint64_t f = nd.feature & 0x7fffffffu;
+    const bool miss = c.csr_colmiss && ((__ldg(c.csr_colmiss + f * words + (r >> 6)) >> (r & 63)) & 1ull);
+    const bool left = miss ? (nd.feature >> 31) != 0u : __ldg(c.csr_col + f * c.n_rows + r) < nd.limit;
+    nd = t[nd.left + (left ? 0 : 1)];
+  }
+  return nd.leaf;
+}
+
 // The pending trees' leaves (K outputs, trees wstride nodes apart, margins
 // class-major) added to the margins of CSR rows, when the flag says a tree
 // waits.
+template <bool COLS>
 __global__ void k_walk_csr(DevConst c, int K, const WNode* __restrict__ wtree, uint32_t wstride,
                            float* __restrict__ margin, const int* __restrict__ pending) {
   pdl_wait();
   if (!*pending) return;
-  const uint64_t n = c.n_rows;
+  const uint64_t n = c.n_rows, words = (n + 63) / 64;
   for (uint64_t i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n;
        i += (uint64_t)gridDim.x * blockDim.x) {
-    const uint64_t a = c.csr_ptr[i], b = c.csr_ptr[i + 1];
+    uint64_t a = 0, b = 0;
+    if (!COLS) {
+      a = c.csr_ptr[i];
+      b = c.csr_ptr[i + 1];
+    }
     for (int k = 0; k < K; ++k) {
       float* m = margin + (uint64_t)k * n + i;
-      *m = __fadd_rn(*m, walk_leaf_csr(wtree + (uint64_t)k * wstride, c, a, b));
+      const WNode* t = wtree + (uint64_t)k * wstride;
+      *m = __fadd_rn(*m, COLS ? walk_leaf_cols(t, c, i, words) : walk_leaf_csr(t, c, a, b));
+    }
+  }
+}
+
+// The feature-major copy of a CSR index: thread per row, each stored cell's
+// feature found by a binary search of the feature offsets (the row's bins
+// ascend, so the search starts at the last cell's feature). Only a
+// feature's first cell is written, the one csr_find returns. `col` zeroed
+// and `colmiss` all ones beforehand; the bitmap's words are shared by 64
+// rows, hence the atomics.
+__global__ void k_csr_columns(DevConst c, uint8_t* __restrict__ col,
+                              unsigned long long* __restrict__ colmiss) {
+  const uint64_t n = c.n_rows, words = (n + 63) / 64;
+  for (uint64_t r = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; r < n;
+       r += (uint64_t)gridDim.x * blockDim.x) {
+    const uint64_t a = c.csr_ptr[r], b = c.csr_ptr[r + 1];
+    uint32_t f = 0;
+    int prev = -1;
+    for (uint64_t j = a; j < b; ++j) {
+      const uint32_t gb = __ldg(c.csr_bins + j);
+      uint32_t lo = f, hi = c.n_cols - 1;  // the last feature whose first bin is <= gb
+      while (lo < hi) {
+        const uint32_t mid = (lo + hi + 1) >> 1;
+        if (__ldg(c.fo + mid) <= gb) lo = mid; else hi = mid - 1;
+      }
+      f = lo;
+      if ((int)f == prev) continue;
+      prev = (int)f;
+      col[(uint64_t)f * n + r] = (uint8_t)(gb - __ldg(c.fo + f));
+      if (colmiss) atomicAnd(colmiss + (uint64_t)f * words + (r >> 6), ~(1ull << (r & 63)));
     }
   }
 }
@@ -2954,7 +3004,16 @@ void launch_softmax_gradients(int K, float* margin, const float* label, uint64_t
 void launch_walk_csr(const DevConst& c, int K, const WNode* wtree, uint32_t wstride, float* margin,
                      const int* pending, int n_sm, cudaStream_t s) {
   const int grid = (int)std::max<uint64_t>(1, std::min<uint64_t>((c.n_rows + 255) / 256, (uint64_t)n_sm * 8));
-  launch_pdl(k_walk_csr, dim3(grid), dim3(256), 0, s, c, K, wtree, wstride, margin, pending);
+  if (c.csr_col)
+    launch_pdl(k_walk_csr<true>, dim3(grid), dim3(256), 0, s, c, K, wtree, wstride, margin, pending);
+  else
+    launch_pdl(k_walk_csr<false>, dim3(grid), dim3(256), 0, s, c, K, wtree, wstride, margin, pending);
+}
+
+void launch_csr_columns(const DevConst& c, uint8_t* col, uint64_t* colmiss, int n_sm, cudaStream_t s) {
+  if (!c.n_rows || !c.n_cols) return;
+  const int grid = (int)std::max<uint64_t>(1, std::min<uint64_t>((c.n_rows + 255) / 256, (uint64_t)n_sm * 8));
+  k_csr_columns<<<grid, 256, 0, s>>>(c, col, reinterpret_cast<unsigned long long*>(colmiss));
 }
 
 void launch_walk_classes(int K, const WNode* wtree, uint32_t wstride, const uint8_t* rec,
@@ -3106,7 +3165,7 @@ void launch_part_count(const DevConst& c, const uint8_t* col, const uint64_t* co
                        const Front* front, const Decision* dec, const PItem* items,
                        const LevelState* ls, int max_items, uint32_t* dirbits, uint32_t* item_left,
                        cudaStream_t s, uint32_t* rows_copy) {
-  if (c.csr)
+  if (c.csr && !col)  // a CSR index held feature-major reads its columns like a dense one
     launch_pdl(k_part_count<true>, dim3(max_items), dim3(kPartThreads), 0, s, c, col, colmiss, rec, use_record, rows_in, identity,
                                                         front, dec, items, ls, dirbits, item_left, rows_copy);
   else
@@ -3118,7 +3177,7 @@ void launch_part_onepass(const DevConst& c, const uint8_t* col, const uint64_t* 
                          const uint32_t* rows_in, int identity, const Front* front, const Decision* dec,
                          const LevelState* ls, int max_items, uint32_t* fill, uint32_t* rows_out,
                          cudaStream_t s) {
-  if (c.csr)
+  if (c.csr && !col)
     launch_pdl(k_part_onepass<true>, dim3(max_items), dim3(kPartThreads), 0, s, c, col, colmiss, rows_in,
                identity, front, dec, ls, fill, rows_out);
   else

@@ -63,6 +63,9 @@ void launch_softmax_gradients(int K, float* margin, const float* label, uint64_t
 // The pending trees' leaves added to the margins of a CSR index's rows.
 void launch_walk_csr(const DevConst& c, int K, const WNode* wtree, uint32_t wstride, float* margin,
                      const int* pending, int n_sm, cudaStream_t s);
+// The feature-major copy of the CSR index c (col zeroed, colmiss all ones,
+// or NULL when every cell is present).
+void launch_csr_columns(const DevConst& c, uint8_t* col, uint64_t* colmiss, int n_sm, cudaStream_t s);
 void launch_walk_classes(int K, const WNode* wtree, uint32_t wstride, const uint8_t* rec,
                          uint32_t stride, uint32_t mask_off, uint32_t blk, uint64_t n, float* margin,
                          const int* pending, int n_sm, cudaStream_t s);

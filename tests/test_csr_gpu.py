@@ -73,8 +73,17 @@ def _orc_kw(kw):
     return m
 
 
+@pytest.fixture(params=["1", "0"], ids=["columns", "search"])
+def csr_columns(request, monkeypatch):
+    """Both ways a CSR engine reads a row's split cell: the feature-major
+    copy of the index (default) and the binary search of the row's bins
+    (HB_CSR_COLUMNS=0)."""
+    monkeypatch.setenv("HB_CSR_COLUMNS", request.param)
+    return request.param
+
+
 @pytest.mark.parametrize("case", sorted(CASES))
-def test_csr_training_matches_oracle(case):
+def test_csr_training_matches_oracle(case, csr_columns):
     s = CASES[case]
     indptr, indices, values = _csr(s["n"], s["f"], s["density"], seed=len(case))
     x, y = _labels(indptr, indices, values, s["f"], 7, s["label"])
@@ -88,7 +97,7 @@ def test_csr_training_matches_oracle(case):
     np.testing.assert_array_equal(_bits(got), _bits(omarg.reshape(len(y), -1)))
 
 
-def test_csr_engine_matches_dense_engine():
+def test_csr_engine_matches_dense_engine(csr_columns):
     """Histograms, root totals, partitions (absent = missing) and the
     no-allocation entry of a CSR engine equal a dense engine's on the same
     cells."""
@@ -133,7 +142,7 @@ def test_csr_engine_matches_dense_engine():
     assert not np.any(miss[out["csr"][3]])
 
 
-def test_csr_c4_shape_lossguide():
+def test_csr_c4_shape_lossguide(csr_columns):
     """The C4 shape at test size: 60,000 rows x 2,000 features at 2% density,
     64 bins, lossguide with 255 leaves; the oracle trains on its own CSR index
     (stored cells only). Trees, and the training margins read back from the
