@@ -448,6 +448,17 @@ uint64_t vector_rows(hb_engine* e) {
   return std::min<uint64_t>(vg - e->row_begin, e->c.n_rows);
 }
 
+// This shard's rows that x86_64's short-row softmax kernel (2 or 4 classes)
+// takes in vectors of 8 / k whole rows: the matrix's first g - g % (8 / k)
+// rows when it holds at least 16 margins (simd/mod.rs:28, :156).
+static uint64_t softmax_vector_rows(hb_engine* e, int k) {
+  if (k != 2 && k != 4) return 0;
+  const uint64_t g = e->c.global_rows, rows = 8 / (uint64_t)k;
+  const uint64_t vg = g * (uint64_t)k >= 16 ? g - g % rows : 0;
+  if (vg <= e->row_begin) return 0;
+  return std::min<uint64_t>(vg - e->row_begin, e->c.n_rows);
+}
+
 // Add the last grown tree's leaves to the margins now (the next round's
 // gradient kernel does it otherwise).
 hb_status flush_pending(hb_engine* e) {
@@ -803,10 +814,8 @@ hb_status check_params(hb_engine* e, const hb_train_params* p) {
       p->objective != HB_LOSS_SOFTMAX)
     return HB_INVALID_ARGUMENT;
   if (p->objective == HB_LOSS_SOFTMAX) {
-    // x86_64 runs a separate vector kernel for 2 and 4 classes
-    // (simd/mod.rs:156); this engine restates the scalar one only
-    if (p->num_class < 3 || p->num_class == 4 || p->num_class > 64)
-      return refuse(e, "multi:softmax supports num_class 3 or 5..64");
+    if (p->num_class < 2 || p->num_class > 64)
+      return refuse(e, "multi:softmax supports num_class 2..64");
     if (e->n_out != p->num_class) return refuse(e, "start the run with hb_train_begin_classes");
   } else if (e->n_out != 1) {
     return refuse(e, "a multi:softmax run is loaded (hb_train_begin resets it)");
@@ -1903,7 +1912,8 @@ static hb_status round_work(hb_engine* e, const hb_train_params* p) {
       launch_walk_csr(e->c, e->n_out, e->wtree.p, (uint32_t)e->wstride, e->margin.p, e->flags.p, e->n_sm, s);
       e->kernel_launches += 1;
     }
-    launch_softmax_gradients(e->n_out, e->margin.p, e->label.p, e->c.n_rows, 1e-16f, e->gpair.p,
+    launch_softmax_gradients(e->n_out, e->margin.p, e->label.p, e->c.n_rows,
+                             softmax_vector_rows(e, e->n_out), 1e-16f, e->gpair.p,
                              e->scale.p, e->wtree.p, (uint32_t)e->wstride, e->rec.p, e->c.stride,
                              e->c.mask_off, e->c.blk, e->c.csr ? nullptr : e->flags.p, e->n_sm, s);
     e->blk_pairs = false;

@@ -598,6 +598,154 @@ __global__ void k_softmax_gradients(int K, float* __restrict__ margin, const flo
   }
 }
 
+// `_mm256_max_ps` / `_mm256_min_ps`: the second operand unless the first is
+// strictly greater (smaller), so a NaN in either gives the second.
+__device__ __forceinline__ float maxps(float a, float b) { return a > b ? a : b; }
+__device__ __forceinline__ float minps(float a, float b) { return a < b ? a : b; }
+
+// One row of K = 2 or 4 margins through x86_64.rs:191 `short_softmax_batch`:
+// row maximum and minimum by `row_reduce` (x86_64.rs:167: lane j takes
+// op(v[j], v[j ^ 1]), then for K = 4 op(r[j], r[j ^ 2])), shift =
+// maxps(MIN_POSITIVE, max); false when max - min <= 80 fails in a lane
+// (non-finite or wide: the row's vector takes the scalar path), otherwise
+// p[j] = exp_f32(v[j] - shift) * (1 / sum), the sum reduced the same way.
+template <int K>
+__device__ __forceinline__ bool softmax_short_row(const float (&v)[K], float (&p)[K]) {
+  float mx[K], mn[K];
+#pragma unroll
+  for (int j = 0; j < K; ++j) {
+    mx[j] = maxps(v[j], v[j ^ 1]);
+    mn[j] = minps(v[j], v[j ^ 1]);
+  }
+  if (K == 4) {
+    float t[K], u[K];
+#pragma unroll
+    for (int j = 0; j < K; ++j) {
+      t[j] = maxps(mx[j], mx[j ^ (K == 4 ? 2 : 0)]);
+      u[j] = minps(mn[j], mn[j ^ (K == 4 ? 2 : 0)]);
+    }
+#pragma unroll
+    for (int j = 0; j < K; ++j) {
+      mx[j] = t[j];
+      mn[j] = u[j];
+    }
+  }
+  bool regular = true;
+  float e[K], sum[K];
+#pragma unroll
+  for (int j = 0; j < K; ++j) {
+    const float shift = maxps(FLT_MIN, mx[j]);
+    regular = regular && __fsub_rn(shift, mn[j]) <= 80.0f;
+    e[j] = exp_vector(__fsub_rn(v[j], shift));
+  }
+#pragma unroll
+  for (int j = 0; j < K; ++j) sum[j] = __fadd_rn(e[j], e[j ^ 1]);
+  if (K == 4) {
+    float t[K];
+#pragma unroll
+    for (int j = 0; j < K; ++j) t[j] = __fadd_rn(sum[j], sum[j ^ (K == 4 ? 2 : 0)]);
+#pragma unroll
+    for (int j = 0; j < K; ++j) sum[j] = t[j];
+  }
+#pragma unroll
+  for (int j = 0; j < K; ++j) p[j] = __fmul_rn(e[j], __fdiv_rn(1.0f, sum[j]));
+  return regular;
+}
+
+// multi:softmax gradients for 2 and 4 classes, which x86_64 computes with
+// x86_64.rs:273 `short_softmax_gradient` (simd/mod.rs:156): 8-lane vectors
+// of 8 / K whole rows over the first `vrows` rows (n - n % (8 / K) of the
+// whole matrix when it holds at least 16 margins, MIN_SIMD_LEN,
+// simd/mod.rs:28), a vector holding an irregular row on the scalar path
+// (the flags of its rows' lanes gathered with a ballot), every other row
+// scalar (k_softmax_gradients' rule). Vector rows: g = p - [class ==
+// label], h = maxps((p 2)(1 - p), min_hess). Layout, leaf walk and maxima
+// as in k_softmax_gradients.
+template <int K>
+__global__ void k_softmax_short(float* __restrict__ margin, const float* __restrict__ label, uint64_t n,
+                                uint64_t vrows, float min_hess, float2* __restrict__ gpair, Scale* scale,
+                                const WNode* __restrict__ wtree, uint32_t wstride,
+                                const uint8_t* __restrict__ rec, uint32_t stride, uint32_t mask_off,
+                                uint32_t blk, const int* __restrict__ pending) {
+  pdl_wait();
+  constexpr unsigned kRows = 8 / K;  // rows of one vector
+  constexpr unsigned kMask = (1u << kRows) - 1u;
+  __shared__ unsigned s_mg[K], s_mh[K], s_nf[K];
+  if (threadIdx.x < K) s_mg[threadIdx.x] = s_mh[threadIdx.x] = s_nf[threadIdx.x] = 0u;
+  __syncthreads();
+  const bool walk = pending != nullptr && *pending != 0;
+  const unsigned lane = threadIdx.x & 31;
+  float mg[K], mh[K];
+  bool nf[K];
+#pragma unroll
+  for (int j = 0; j < K; ++j) {
+    mg[j] = mh[j] = 0.0f;
+    nf[j] = false;
+  }
+  const uint64_t step = (uint64_t)gridDim.x * blockDim.x;
+  for (uint64_t base = (uint64_t)blockIdx.x * blockDim.x; base < n; base += step) {
+    const uint64_t i = base + threadIdx.x;
+    const bool in = i < n;
+    float v[K];
+#pragma unroll
+    for (int j = 0; j < K; ++j) v[j] = in ? margin[(uint64_t)j * n + i] : 0.0f;
+    if (in && walk) {
+      const uint8_t* rp = rec + rec_offset((uint32_t)i, stride, blk);
+#pragma unroll
+      for (int j = 0; j < K; ++j) {
+        v[j] = __fadd_rn(v[j], walk_leaf(wtree + (uint64_t)j * wstride, rp, stride, mask_off));
+        margin[(uint64_t)j * n + i] = v[j];
+      }
+    }
+    float p[K];
+    const bool regular = softmax_short_row<K>(v, p);
+    const unsigned bal = __ballot_sync(kFull, regular || !in);
+    const bool vec = i < vrows && ((bal >> (lane & ~(kRows - 1u))) & kMask) == kMask;
+    if (!in) continue;
+    const float y = label[i];
+    float g[K], h[K];
+    if (vec) {
+#pragma unroll
+      for (int j = 0; j < K; ++j) {
+        g[j] = __fsub_rn(p[j], (float)j == y ? 1.0f : 0.0f);
+        h[j] = maxps(__fmul_rn(__fmul_rn(p[j], 2.0f), __fsub_rn(1.0f, p[j])), min_hess);
+      }
+    } else {
+      float wmax = FLT_MIN;
+#pragma unroll
+      for (int j = 0; j < K; ++j) wmax = fmaxf(v[j], wmax);
+      double wsum = 0.0;
+#pragma unroll
+      for (int j = 0; j < K; ++j) wsum += (double)exp_rounded(__fsub_rn(v[j], wmax));
+      const float ws = __double2float_rn(wsum);
+#pragma unroll
+      for (int j = 0; j < K; ++j) {
+        const float q = __fdiv_rn(exp_rounded(__fsub_rn(v[j], wmax)), ws);
+        h[j] = fmaxf(__fmul_rn(__fmul_rn(2.0f, q), __fsub_rn(1.0f, q)), min_hess);
+        g[j] = (float)j == y ? __fsub_rn(q, 1.0f) : q;
+      }
+    }
+#pragma unroll
+    for (int j = 0; j < K; ++j) {
+      gpair[(uint64_t)j * n + i] = make_float2(g[j], h[j]);
+      fold_max(g[j], h[j], mg[j], mh[j], nf[j]);
+    }
+  }
+#pragma unroll
+  for (int j = 0; j < K; ++j) {
+    if (nf[j]) atomicOr(&s_nf[j], 1u);
+    atomicMax(&s_mg[j], __float_as_uint(mg[j]));
+    atomicMax(&s_mh[j], __float_as_uint(mh[j]));
+  }
+  __syncthreads();
+  if (threadIdx.x < K) {
+    const int j = threadIdx.x;
+    if (s_mg[j]) atomicMax(&scale[j].maxg_bits, s_mg[j]);
+    if (s_mh[j]) atomicMax(&scale[j].maxh_bits, s_mh[j]);
+    if (s_nf[j]) atomicOr(&scale[j].nonfinite, 1u);
+  }
+}
+
 // Add each class's tree leaves to the class-major margins (the last round's
 // trees, when *pending is set).
 __global__ void k_walk_classes(int K, const WNode* __restrict__ wtree, uint32_t wstride,
@@ -2992,11 +3140,21 @@ void hist_configure() {
     cudaFuncSetAttribute(f, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024 - 1024);
 }
 
-void launch_softmax_gradients(int K, float* margin, const float* label, uint64_t n, float min_hess,
-                              float2* gpair, Scale* scale, const WNode* wtree, uint32_t wstride,
-                              const uint8_t* rec, uint32_t stride, uint32_t mask_off, uint32_t blk,
-                              const int* pending, int n_sm, cudaStream_t s) {
+void launch_softmax_gradients(int K, float* margin, const float* label, uint64_t n, uint64_t vrows,
+                              float min_hess, float2* gpair, Scale* scale, const WNode* wtree,
+                              uint32_t wstride, const uint8_t* rec, uint32_t stride, uint32_t mask_off,
+                              uint32_t blk, const int* pending, int n_sm, cudaStream_t s) {
   const int grid = (int)std::max<uint64_t>(1, std::min<uint64_t>((n + 255) / 256, (uint64_t)n_sm * 8));
+  if (K == 2) {
+    launch_pdl(k_softmax_short<2>, dim3(grid), dim3(256), 0, s, margin, label, n, vrows, min_hess, gpair, scale,
+               wtree, wstride, rec, stride, mask_off, blk, pending);
+    return;
+  }
+  if (K == 4) {
+    launch_pdl(k_softmax_short<4>, dim3(grid), dim3(256), 0, s, margin, label, n, vrows, min_hess, gpair, scale,
+               wtree, wstride, rec, stride, mask_off, blk, pending);
+    return;
+  }
   launch_pdl(k_softmax_gradients, dim3(grid), dim3(256), 0, s, K, margin, label, n, min_hess, gpair, scale, wtree,
                                            wstride, rec, stride, mask_off, blk, pending);
 }

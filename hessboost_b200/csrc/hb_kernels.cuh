@@ -55,10 +55,11 @@ void launch_walk(const WNode* wtree, const LevelState* ls_last, int max_nodes, c
 // multi:softmax gradients of K classes (class-major margins and pairs,
 // K <= 64), first adding each class's pending tree when *pending is set;
 // per-class maxima into scale[0..K).
-void launch_softmax_gradients(int K, float* margin, const float* label, uint64_t n, float min_hess,
-                              float2* gpair, Scale* scale, const WNode* wtree, uint32_t wstride,
-                              const uint8_t* rec, uint32_t stride, uint32_t mask_off, uint32_t blk,
-                              const int* pending, int n_sm, cudaStream_t s);
+// (K = 2 and 4: the first vrows rows in 8-lane vectors of whole rows.)
+void launch_softmax_gradients(int K, float* margin, const float* label, uint64_t n, uint64_t vrows,
+                              float min_hess, float2* gpair, Scale* scale, const WNode* wtree,
+                              uint32_t wstride, const uint8_t* rec, uint32_t stride, uint32_t mask_off,
+                              uint32_t blk, const int* pending, int n_sm, cudaStream_t s);
 // When *pending is set, add each class's tree leaves to its margins.
 // The pending trees' leaves added to the margins of a CSR index's rows.
 void launch_walk_csr(const DevConst& c, int K, const WNode* wtree, uint32_t wstride, float* margin,

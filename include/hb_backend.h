@@ -200,7 +200,7 @@ typedef struct hb_train_params {
   float max_delta_step;
   float scale_pos_weight;
   float base_score;         /* NaN: estimate from the labels */
-  int32_t num_class;        /* HB_LOSS_SOFTMAX: classes (3, or 5..64); else 0 or 1 */
+  int32_t num_class;        /* HB_LOSS_SOFTMAX: classes (2..64); else 0 or 1 */
   /* monotone_constraints (src/config/params.rs, Monotone): one direction
    * per feature, +1 increasing, -1 decreasing, 0 none; features past
    * n_monotone are unconstrained. NULL / 0: none. */

@@ -877,33 +877,106 @@ void squared_error_gradient(const float* m, const float* y, size_t n, float spw,
   }
 }
 
-// multi:softmax gradients (objective/multiclass.rs:43 through
-// simd/mod.rs:502), the per-row scalar kernel `softmax_gradient_row_scalar`
-// (simd/mod.rs:580), which x86_64 runs for every class count but 2 and 4
-// (simd/mod.rs:156): the shift is max(f32::MIN_POSITIVE, margins...), the
-// exponentials are summed in f64 and the sum rounded to f32, then
-// p = expf(m - shift) / sum, g = (p - [class == label]) w,
-// h = max(((2 p)(1 - p)) w, MIN_HESS). Margins row-major, k per row; out in
-// the same layout.
-void softmax_gradient(const float* m, const float* y, size_t n, int k, GradPair* out) {
-#pragma omp parallel for schedule(static)
-  for (long long i = 0; i < (long long)n; ++i) {
-    const float* row = m + (size_t)i * k;
-    float wmax = FLT_MIN;
-    for (int j = 0; j < k; ++j) wmax = std::fmax(row[j], wmax);
-    double wsum = 0.0;
-    for (int j = 0; j < k; ++j) wsum += (double)expf(row[j] - wmax);
-    const float ws = (float)wsum;
-    const size_t label = (size_t)y[i];
-    const float w = 1.0f;
-    for (int j = 0; j < k; ++j) {
-      const float p = expf(row[j] - wmax) / ws;
-      const float h = std::fmax(((2.0f * p) * (1.0f - p)) * w, MIN_HESS);
-      const float g = ((size_t)j == label ? p - 1.0f : p) * w;
-      out[(size_t)i * k + j].grad = g;
-      out[(size_t)i * k + j].hess = h;
+// `_mm256_max_ps` / `_mm256_min_ps`: the second operand unless the first is
+// strictly greater (smaller), so a NaN in either gives the second.
+static inline float maxps(float a, float b) { return a > b ? a : b; }
+static inline float minps(float a, float b) { return a < b ? a : b; }
+
+// One row of k = 2 or 4 margins through x86_64.rs:191 `short_softmax_batch`:
+// the row's maximum and minimum by `row_reduce` (x86_64.rs:167: lane j takes
+// op(v[j], v[j ^ 1]), then for k = 4 op(r[j], r[j ^ 2])), shift =
+// maxps(MIN_POSITIVE, max); false when max - min <= 80 fails in a lane (a
+// non-finite or wide row: its batch takes the scalar path); otherwise
+// p[j] = exp_f32(v[j] - shift) * (1 / sum), the sum reduced the same way.
+static bool softmax_short_row(const float* v, int k, float* p) {
+  float mx[4], mn[4], t[4], u[4];
+  for (int j = 0; j < k; ++j) {
+    mx[j] = maxps(v[j], v[j ^ 1]);
+    mn[j] = minps(v[j], v[j ^ 1]);
+  }
+  if (k == 4) {
+    for (int j = 0; j < 4; ++j) {
+      t[j] = maxps(mx[j], mx[j ^ 2]);
+      u[j] = minps(mn[j], mn[j ^ 2]);
+    }
+    for (int j = 0; j < 4; ++j) {
+      mx[j] = t[j];
+      mn[j] = u[j];
     }
   }
+  float shift[4], e[4], sum[4];
+  for (int j = 0; j < k; ++j) {
+    shift[j] = maxps(FLT_MIN, mx[j]);
+    if (!(shift[j] - mn[j] <= 80.0f)) return false;
+  }
+  for (int j = 0; j < k; ++j) e[j] = exp_vector(v[j] - shift[j]);
+  for (int j = 0; j < k; ++j) sum[j] = e[j] + e[j ^ 1];
+  if (k == 4) {
+    for (int j = 0; j < 4; ++j) t[j] = sum[j] + sum[j ^ 2];
+    for (int j = 0; j < 4; ++j) sum[j] = t[j];
+  }
+  for (int j = 0; j < k; ++j) p[j] = e[j] * (1.0f / sum[j]);
+  return true;
+}
+
+// simd/mod.rs:580 `softmax_gradient_row_scalar` for row i: the shift is
+// max(f32::MIN_POSITIVE, margins...), the exponentials are summed in f64 and
+// the sum rounded to f32, then p = expf(m - shift) / sum,
+// g = (p - [class == label]) w, h = max(((2 p)(1 - p)) w, MIN_HESS).
+static void softmax_row_scalar(const float* row, float y, int k, GradPair* out) {
+  float wmax = FLT_MIN;
+  for (int j = 0; j < k; ++j) wmax = std::fmax(row[j], wmax);
+  double wsum = 0.0;
+  for (int j = 0; j < k; ++j) wsum += (double)expf(row[j] - wmax);
+  const float ws = (float)wsum;
+  const size_t label = (size_t)y;
+  const float w = 1.0f;
+  for (int j = 0; j < k; ++j) {
+    const float p = expf(row[j] - wmax) / ws;
+    const float h = std::fmax(((2.0f * p) * (1.0f - p)) * w, MIN_HESS);
+    const float g = ((size_t)j == label ? p - 1.0f : p) * w;
+    out[j].grad = g;
+    out[j].hess = h;
+  }
+}
+
+// multi:softmax gradients (objective/multiclass.rs:43 through
+// simd/mod.rs:502). x86_64 runs the scalar row kernel for every class count
+// but 2 and 4. For those it runs x86_64.rs:273 `short_softmax_gradient`
+// (simd/mod.rs:156) when the margins hold at least 16 values
+// (MIN_SIMD_LEN, simd/mod.rs:28): vectors of 8 / k whole rows over the first
+// n - n % (8 / k) rows, a vector with an irregular row on the scalar path,
+// the remaining rows scalar. The vector rows' pairs: g = (p - [class ==
+// label]) w, h = maxps(((p 2)(1 - p)) w, MIN_HESS). The chunking of
+// objective/mod.rs:195 `rowwise_cells` keeps this whole-batch split. Margins
+// row-major, k per row; out in the same layout.
+void softmax_gradient(const float* m, const float* y, size_t n, int k, GradPair* out) {
+  const size_t rpb = (k == 2 || k == 4) ? (size_t)(8 / k) : 0;
+  const size_t vrows = (rpb && n * (size_t)k >= 16) ? n - n % rpb : 0;
+#pragma omp parallel for schedule(static)
+  for (long long b = 0; b < (long long)(vrows / (rpb ? rpb : 1)); ++b) {
+    float p[8];
+    bool regular = true;
+    for (size_t r = 0; r < rpb; ++r)
+      regular = softmax_short_row(m + ((size_t)b * rpb + r) * k, k, p + r * k) && regular;
+    for (size_t r = 0; r < rpb; ++r) {
+      const size_t i = (size_t)b * rpb + r;
+      if (!regular) {
+        softmax_row_scalar(m + i * k, y[i], k, out + i * k);
+        continue;
+      }
+      const size_t label = (size_t)y[i];
+      const float w = 1.0f;
+      for (int j = 0; j < k; ++j) {
+        const float q = p[r * k + j];
+        out[i * k + j].grad = (q - ((size_t)j == label ? 1.0f : 0.0f)) * w;
+        out[i * k + j].hess = maxps(((q * 2.0f) * (1.0f - q)) * w, MIN_HESS);
+      }
+    }
+  }
+#pragma omp parallel for schedule(static)
+  for (long long i = (long long)vrows; i < (long long)n; ++i)
+    softmax_row_scalar(m + (size_t)i * k, y[i], k, out + (size_t)i * k);
 }
 
 // multiclass.rs:68 `base_margins_info` (unweighted): class counts in f32,

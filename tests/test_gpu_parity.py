@@ -246,7 +246,9 @@ def _first_difference_is_a_tie(on, op, nodes, ptr):
 
 
 @pytest.mark.parametrize("n,f,k,depth,max_bin,rounds", [(20_011, 12, 5, 5, 64, 3),
-                                                        (60_000, 100, 10, 6, 128, 2)])
+                                                        (60_000, 100, 10, 6, 128, 2),
+                                                        (20_013, 12, 2, 5, 64, 3),
+                                                        (30_001, 20, 4, 6, 128, 3)])
 def test_softmax_training_matches_oracle(n, f, k, depth, max_bin, rounds):
     """multi:softmax, gradients on the device (C3's shape at the second
     size). The device exp is CUDA's double exp rounded once to f32, the
@@ -298,11 +300,24 @@ def test_lossguide_grow_tree_matches_oracle_and_refusals():
         e.close()
 
 
-def test_softmax_refuses_two_or_four_classes():
-    x, y = synth.multiclass_c3(2000, 5, 4, seed=1)
-    p = H.TrainingParams(objective="multi:softmax", num_class=4, max_depth=3)
+@pytest.mark.parametrize("k", [2, 4])
+def test_short_softmax_classes_bit_exact(k):
+    """2 and 4 classes take x86_64's short-row vector kernel (whole rows per
+    8-lane vector) on every row of a vector with no irregular row: its
+    exponential is the reference's own polynomial, so with every margin
+    regular the device's gradients, trees and margins equal the oracle's bit
+    for bit (a row count that leaves a scalar tail, and one class refused:
+    num_class 1)."""
+    x, y = synth.multiclass_c3(9_003, 8, k, seed=40 + k)
+    p = H.TrainingParams(objective="multi:softmax", num_class=k, max_depth=4, eta=0.3, max_bin=64)
+    m = H.train(p, x, y, 3)
+    on, op, obase, omarg = O.train(x, y, 3, objective=2, n_outputs=k, max_depth=4, eta=0.3, max_bin=64,
+                                   fixed_point=True)
+    np.testing.assert_array_equal(m.bases().view(np.uint32), obase.view(np.uint32))
+    assert_forest_equal(m.nodes, m.tree_ptr, on, op, f"softmax k={k}")
+    np.testing.assert_array_equal(_bits(m.predict_margin(x).reshape(omarg.shape)), _bits(omarg))
     with pytest.raises(H.HbError):
-        H.train(p, x, y, 1)
+        H.train(H.TrainingParams(objective="multi:softmax", num_class=1, max_depth=3), x, np.zeros_like(y), 1)
 
 
 def test_training_is_deterministic():

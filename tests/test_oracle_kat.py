@@ -118,6 +118,92 @@ def test_softmax_gradient_kat():
     np.testing.assert_allclose(g[:, :, 1], 2 * (1 / 3) * (2 / 3), atol=1e-6)
 
 
+def _softmax_scalar(m, y):
+    """simd/mod.rs:580 `softmax_gradient_row_scalar` in numpy (exp in f64
+    rounded to f32, within an ulp of expf): the comparison kernel of the
+    reference's own vector-softmax tests (simd/tests.rs:33)."""
+    n, k = m.shape
+    out = np.zeros((n, k, 2), np.float32)
+    tiny = np.float32(np.finfo(np.float32).tiny)
+    with np.errstate(all="ignore"):
+        for i in range(n):
+            row = m[i]
+            wmax = tiny
+            for v in row:
+                wmax = np.float32(np.fmax(v, wmax))
+            e = [np.float32(np.exp(np.float64(np.float32(v - wmax)))) for v in row]
+            ws = np.float32(sum(np.float64(v) for v in e))
+            for j in range(k):
+                p = np.float32(e[j] / ws)
+                h = np.float32(np.fmax(np.float32(np.float32(2 * p) * np.float32(1 - p)), np.float32(1e-16)))
+                out[i, j] = (np.float32(p - 1) if j == int(y[i]) else p, h)
+    return out
+
+
+@pytest.mark.parametrize("k", [2, 3, 4])
+def test_short_softmax_batches_match_scalar_across_boundaries(k):
+    """simd/tests.rs:133: 2 and 4 classes run x86_64's short-row vector
+    kernel (whole rows per 8-lane vector, the rest scalar), 3 the scalar
+    one; every row count around the batch and MIN_SIMD_LEN boundaries stays
+    within 1e-6 of the scalar kernel."""
+    for rows in list(range(1, 18)) + [127, 256, 257]:
+        m = (((np.arange(rows * k) * 71) % 211).astype(np.float32) * np.float32(0.375)
+             - np.float32(39.0)).reshape(rows, k)
+        y = (np.arange(rows) % k).astype(np.float32)
+        got = O.softmax_gradients(m, y)
+        want = _softmax_scalar(m, y)
+        assert np.all(np.abs(got - want) <= 1e-6 * np.maximum(np.abs(want), 1.0)), (k, rows)
+
+
+@pytest.mark.parametrize("k", [2, 4])
+def test_short_softmax_exceptional_rows_match_scalar(k):
+    """simd/tests.rs:164 with class-id labels (the engine refuses others): a
+    non-finite, wide (|m| > 80) or huge margin anywhere sends its vector to
+    the scalar path, so NaN, infinities and values agree with the scalar
+    kernel (values within 3e-7)."""
+    rows = 9
+    y = (np.arange(rows) % k).astype(np.float32)
+    for position in range(rows * k):
+        for exc in (np.nan, np.inf, -np.inf, -81.0, 81.0, -80.0, 80.0, np.finfo(np.float32).max):
+            m = np.zeros(rows * k, np.float32)
+            m[position] = exc
+            m = m.reshape(rows, k)
+            got = O.softmax_gradients(m, y)
+            want = _softmax_scalar(m, y)
+            assert np.array_equal(np.isnan(got), np.isnan(want)), (position, exc)
+            fin = np.isfinite(want)
+            assert np.array_equal(got[~fin & ~np.isnan(want)], want[~fin & ~np.isnan(want)])
+            assert np.all(np.abs(got[fin] - want[fin]) <= 3e-7), (position, exc)
+
+
+@pytest.mark.parametrize("k", [2, 4])
+def test_short_softmax_vector_rows(k):
+    """The vector kernel really runs for 2 and 4 classes: at 16 or more
+    margins its rows differ from the scalar kernel's in the last bits
+    somewhere (exp_f32's polynomial, p = e * (1 / sum)), while below
+    MIN_SIMD_LEN (simd/mod.rs:28) every row is the scalar kernel's; a vector
+    holding one irregular row computes all of its rows as the scalar
+    kernel does, which the same rows reproduce as a tail."""
+    rng = np.random.default_rng(k)
+    m = (rng.standard_normal((4096, k)) * 3).astype(np.float32)
+    y = rng.integers(0, k, 4096).astype(np.float32)
+    vec = O.softmax_gradients(m, y)
+    assert not np.array_equal(vec, _softmax_scalar(m, y))
+    rpb = 8 // k
+    small = 16 // k - 1  # n * k < 16: the whole batch scalar
+    forced = m[:64].copy()
+    forced[rpb - 1, 0] = np.nan  # the first vector's rows on the scalar path
+    np.testing.assert_array_equal(O.softmax_gradients(m[:small], y[:small])[: rpb - 1],
+                                  O.softmax_gradients(forced, y[:64])[: rpb - 1])
+    tail = O.softmax_gradients(m[: 16 + rpb - 1], y[: 16 + rpb - 1])[16:]  # rows past the last whole vector
+    wide = m[: 16 + rpb].copy()
+    wide[16 + rpb - 1, 0] = np.inf  # the vector of rows 16.. holds an irregular row
+    mixed = O.softmax_gradients(wide, y[: 16 + rpb])[16: 16 + rpb - 1]
+    np.testing.assert_array_equal(mixed, tail)
+    regular = O.softmax_gradients(m[: 16 + rpb], y[: 16 + rpb])[16: 16 + rpb - 1]
+    assert np.all(np.abs(regular - tail) <= 1e-6)
+
+
 def test_softmax_gradient_shift_and_rounding():
     """The shift is max(f32::MIN_POSITIVE, margins) and the f64 sum is
     rounded to f32 before the division (simd/mod.rs:580)."""
