@@ -80,7 +80,12 @@ struct hb_engine {
   const float* label_key = nullptr;
   const float* weight_key = nullptr;
   bool margins_loaded = false;
-  DevBuf<uint32_t> rows[2];
+  // Row ids: one allocation of 2n, rows[0] its first half and rows[1] its
+  // second (depthwise growth ping-pongs between them; lossguide's one-pass
+  // partition moves a node's rows to the other half, its positions read
+  // from rows[0] over the whole 2n)
+  DevBuf<uint32_t> rows_all;
+  uint32_t* rows[2] = {nullptr, nullptr};
   DevBuf<Scale> scale;
   bool staged = false;
 
@@ -174,8 +179,7 @@ struct hb_engine {
   DevBuf<int8_t> mono, scan_dirs;
   std::vector<int8_t> h_mono;
   // RowEngine call buffers: leaf segments and values, partition end rows
-  DevBuf<uint2> seg_list;
-  DevBuf<float> seg_vals;
+  DevBuf<uint4> seg_tiles;  // hb_add_leaf_values' row tiles
   DevBuf<uint32_t> part_ends;
   // fault injection (hb_engine_inject_fault): checked calls left before the
   // one that fails (-1: none armed); no injection while a graph is captured
@@ -576,8 +580,8 @@ hb_status grow_device(hb_engine* e, const hb_train_params* p, bool to_forest) {
   launch_root_stats(e->front[0].p, totals, s);
 
   int cur = 0;
-  uint32_t* rows_in = e->rows[0].p;
-  uint32_t* rows_out = e->rows[1].p;
+  uint32_t* rows_in = e->rows[0];
+  uint32_t* rows_out = e->rows[1];
   uint64_t launches = 3;
   for (int d = 0; d <= D; ++d) {
     const bool leaf_only = d == D;
@@ -623,8 +627,8 @@ hb_status grow_device(hb_engine* e, const hb_train_params* p, bool to_forest) {
       ++launches;
     } else {
       launch_part_onepass(c, e->col.p, e->colmiss.p, rows_in, d == 0, fr,
-                          e->dec.p, lsd, max_items, e->fill.p, rows_out, s);
-      launch_part_plan(fr, e->dec.p, lsd, e->fill.p, nx, e->entries.p, e->pairs.p, lsn, max_front, s);
+                          e->dec.p, lsd, max_items, e->fill.p, rows_out, 0u, s);
+      launch_part_plan(fr, e->dec.p, lsd, e->fill.p, nx, e->entries.p, e->pairs.p, lsn, max_front, 0u, s);
     }
     mark_end(e);
     mark_begin(e, T_HIST);
@@ -683,6 +687,7 @@ hb_status ensure_lossguide_buffers(hb_engine* e, int L) {
   HB_CK(e, e->lg_heap.alloc((size_t)L + 2));
   HB_CK(e, e->lg_state.alloc(1));
   HB_CK(e, e->lg_depth.alloc(n_nodes));
+  HB_CK(e, e->fill.alloc(2));
   e->wstride = (size_t)n_nodes;
   e->alloc_depth = -1;  // the depthwise sizes no longer hold
   e->lg_alloc = L;
@@ -700,8 +705,10 @@ hb_status ensure_buffers(hb_engine* e, const hb_train_params* p) {
 // heap step (k_lg_step) and, when it expanded a node, that node's partition,
 // the smaller-Hessian child's histogram and both children's scans (the
 // sibling made as parent - built by the scan). Histogram slot = node id, so
-// no slot is reused within a tree. Every node's rows stay in rows[0]: a
-// partition scatters into rows[1] and copies the segment back.
+// no slot is reused within a tree. A node's rows sit in either half of the
+// 2n row buffer: the one-pass partition moves its children to the other
+// half (the stable one, HB_STABLE_PARTITION=1, scatters into rows[1] and
+// copies the segment back, so every node stays in rows[0]).
 hb_status grow_lossguide(hb_engine* e, const hb_train_params* p, bool to_forest) {
   DevConst& c = e->c;
   const int L = lg_leaves(p);
@@ -741,8 +748,13 @@ hb_status grow_lossguide(hb_engine* e, const hb_train_params* p, bool to_forest)
   uint64_t launches = 5;
   const int max_leaves = p->max_leaves > 0 ? p->max_leaves : INT_MAX;
   const int depth_limit = p->max_depth > 0 ? p->max_depth : INT_MAX;
-  uint32_t* rows0 = e->rows[0].p;
-  uint32_t* rows1 = e->rows[1].p;
+  uint32_t* rows0 = e->rows[0];
+  uint32_t* rows1 = e->rows[1];
+  // one-pass partition unless the stable one is asked for (or positions in
+  // the 2n buffer would not fit 32 bits); fill zero before the first pass
+  const bool onepass = !e->stable_partition && 2 * c.n_rows < (1ull << 32);
+  const uint32_t half = (uint32_t)c.n_rows;
+  if (onepass) HB_CK(e, cudaMemsetAsync(e->fill.p, 0, 2 * sizeof(uint32_t), s));
   for (int k = 0; k < L; ++k) {
     const bool final_step = k == L - 1;
     mark_begin(e, T_APPLY);
@@ -753,16 +765,24 @@ hb_status grow_lossguide(hb_engine* e, const hb_train_params* p, bool to_forest)
     ++launches;
     if (final_step) break;
     mark_begin(e, T_PART);
-    // the count pass leaves a copy of the node's row ids in rows1, and the
-    // scatter writes the children from it back into rows0, where every
-    // pending node's rows stay
-    launch_part_count(c, e->col.p, e->colmiss.p, e->rec.p, 0, rows0, k == 0,
-                      fr, e->dec.p, e->items.p, ls1, e->max_items, e->dirbits.p, e->item_left.p, s,
-                      rows1);
-    launch_part_scan(fr, e->dec.p, ls1, 1, e->item_left.p, e->item_off.p, nx, e->entries.p,
-                     e->pairs.p, ls2, s);
-    launch_part_scatter(fr, e->dec.p, e->items.p, ls1, e->max_items, e->dirbits.p, e->item_off.p, nx,
-                        rows1, 0, rows0, s);
+    if (onepass) {
+      // the node's rows move to the other half of the 2n row buffer
+      launch_part_onepass(c, e->col.p, e->colmiss.p, rows0, k == 0, fr, e->dec.p, ls1, e->max_items,
+                          e->fill.p, rows0, half, s);
+      launch_part_plan(fr, e->dec.p, ls1, e->fill.p, nx, e->entries.p, e->pairs.p, ls2, 1, half, s);
+      launches -= 1;
+    } else {
+      // the count pass leaves a copy of the node's row ids in rows1, and the
+      // scatter writes the children from it back into rows0, where every
+      // pending node's rows stay
+      launch_part_count(c, e->col.p, e->colmiss.p, e->rec.p, 0, rows0, k == 0,
+                        fr, e->dec.p, e->items.p, ls1, e->max_items, e->dirbits.p, e->item_left.p, s,
+                        rows1);
+      launch_part_scan(fr, e->dec.p, ls1, 1, e->item_left.p, e->item_off.p, nx, e->entries.p,
+                       e->pairs.p, ls2, s);
+      launch_part_scatter(fr, e->dec.p, e->items.p, ls1, e->max_items, e->dirbits.p, e->item_off.p, nx,
+                          rows1, 0, rows0, s);
+    }
     mark_end(e);
     mark_begin(e, T_HIST);
     launch_hist(c, e->fo.p, e->rec.p, hist_gpair(e), cur_scale(e), rows0, e->entries.p, ls2, hist, nullptr,
@@ -921,8 +941,8 @@ hb_status hb_engine_destroy(hb_engine* e) {
   e->margin.release();
   e->label.release();
   e->weight.release();
-  e->rows[0].release();
-  e->rows[1].release();
+  e->rows_all.release();
+  e->rows[0] = e->rows[1] = nullptr;
   e->scale.release();
   e->hist_all.release();
   e->front[0].release();
@@ -954,8 +974,7 @@ hb_status hb_engine_destroy(hb_engine* e) {
   e->flags.release();
   e->mono.release();
   e->scan_dirs.release();
-  e->seg_list.release();
-  e->seg_vals.release();
+  e->seg_tiles.release();
   e->part_ends.release();
   if (e->stream) cudaStreamDestroy(e->stream);
   delete e;
@@ -964,6 +983,14 @@ hb_status hb_engine_destroy(hb_engine* e) {
 
 const char* hb_engine_last_error(const hb_engine* e) {
   return e ? e->err.c_str() : g_last_error.c_str();
+}
+
+// The two halves of the row-id buffer for an index of n rows.
+static cudaError_t alloc_rows(hb_engine* e, uint64_t n) {
+  cudaError_t ce = e->rows_all.alloc(std::max<uint64_t>(2 * n, 2));
+  e->rows[0] = e->rows_all.p;
+  e->rows[1] = e->rows_all.p ? e->rows_all.p + n : nullptr;
+  return ce;
 }
 
 // Engine state after a new index: nothing staged, no cached round graph.
@@ -1144,8 +1171,7 @@ static hb_status upload_index(hb_engine* e, const hb_ghist* g, const RawSource* 
     HB_CK(e, e->gpair.alloc(n));
     HB_CK(e, e->margin.alloc(n));
     HB_CK(e, e->label.alloc(n));
-    HB_CK(e, e->rows[0].alloc(n));
-    HB_CK(e, e->rows[1].alloc(n));
+    HB_CK(e, alloc_rows(e, n));
     cudaStream_t s = e->stream;
     HB_CK(e, cudaMemcpyAsync(e->fo.p, e->h_fo.data(), 4 * (c.n_cols + 1), cudaMemcpyHostToDevice, s));
     HB_CK(e, cudaMemcpyAsync(e->cuts.p, e->h_cuts.data(), 4 * c.total_bins, cudaMemcpyHostToDevice, s));
@@ -1166,8 +1192,7 @@ static hb_status upload_index(hb_engine* e, const hb_ghist* g, const RawSource* 
   HB_CK(e, e->gpair.alloc(n));
   HB_CK(e, e->margin.alloc(n));
   HB_CK(e, e->label.alloc(n));
-  HB_CK(e, e->rows[0].alloc(n));
-  HB_CK(e, e->rows[1].alloc(n));
+  HB_CK(e, alloc_rows(e, n));
   cudaStream_t s = e->stream;
   HB_CK(e, cudaMemcpyAsync(e->fo.p, e->h_fo.data(), 4 * (c.n_cols + 1), cudaMemcpyHostToDevice, s));
   HB_CK(e, cudaMemcpyAsync(e->cuts.p, e->h_cuts.data(), 4 * c.total_bins, cudaMemcpyHostToDevice, s));
@@ -1446,9 +1471,9 @@ hb_status hb_begin_tree(hb_engine* e, const uint32_t* rows, uint64_t n, hb_segme
   if (!inside || !ascending) return refuse(e, "rows must be ascending and distinct");
   // a contiguous run is written on the device (place_rows, cuda/mod.rs:1830)
   if (n && run)
-    launch_iota(e->rows[0].p, rows[0], n, e->n_sm, e->stream);
+    launch_iota(e->rows[0], rows[0], n, e->n_sm, e->stream);
   else if (n)
-    HB_CK(e, cudaMemcpyAsync(e->rows[0].p, rows, 4 * n, cudaMemcpyHostToDevice, e->stream));
+    HB_CK(e, cudaMemcpyAsync(e->rows[0], rows, 4 * n, cudaMemcpyHostToDevice, e->stream));
   HB_CK(e, cudaGetLastError());
   HB_CK(e, cudaStreamSynchronize(e->stream));
   ++e->tree_stamp;
@@ -1479,7 +1504,7 @@ hb_status hb_histograms(hb_engine* e, const hb_segment* segs, uint32_t n, hb_gra
   }
   if (!n) return HB_OK;
   HB_CK(e, e->call_hist.alloc((size_t)n * e->c.total_bins));
-  hb_status st = build_entries(e, en, e->call_hist.p, n, e->rows[0].p);
+  hb_status st = build_entries(e, en, e->call_hist.p, n, e->rows[0]);
   if (st != HB_OK) return st;
   return download_hist(e, e->call_hist.p, n, out);
 }
@@ -1492,7 +1517,7 @@ hb_status hb_root_total(hb_engine* e, const hb_segment* seg, hb_grad_stats* out)
   // integers the histograms sum, so any order).
   cudaStream_t s = e->stream;
   HB_CK(e, cudaMemsetAsync(e->seg_total.p, 0, 16, s));
-  launch_seg_total(e->rows[0].p, seg->offset, seg->len, e->gpair.p, e->scale.p, e->seg_total.p, e->n_sm, s);
+  launch_seg_total(e->rows[0], seg->offset, seg->len, e->gpair.p, e->scale.p, e->seg_total.p, e->n_sm, s);
   HB_CK(e, cudaGetLastError());
   long long t[2];
   Scale h;
@@ -1563,20 +1588,20 @@ hb_status hb_partition(hb_engine* e, const hb_row_split* splits, uint32_t n, hb_
   HB_CK(e, cudaMemcpyAsync(e->ls.p, &lsh, sizeof(LevelState), cudaMemcpyHostToDevice, s));
   if (n_items) {
     launch_part_count(c, e->col.p, e->colmiss.p, e->rec.p, 0,
-                      e->rows[0].p, 0, e->front[0].p, e->dec.p, e->items.p, e->ls.p, n_items,
+                      e->rows[0], 0, e->front[0].p, e->dec.p, e->items.p, e->ls.p, n_items,
                       e->dirbits.p, e->item_left.p, s);
   }
   launch_part_scan(e->front[0].p, e->dec.p, e->ls.p, (int)n, e->item_left.p, e->item_off.p,
                    e->front[1].p, nullptr, nullptr, nullptr, s);
   if (n_items) {
     launch_part_scatter(e->front[0].p, e->dec.p, e->items.p, e->ls.p, n_items, e->dirbits.p,
-                        e->item_off.p, e->front[1].p, e->rows[0].p, 0, e->rows[1].p, s);
+                        e->item_off.p, e->front[1].p, e->rows[0], 0, e->rows[1], s);
   }
   HB_CK(e, cudaGetLastError());
   // the children back in rows[0] and their end rows, one launch
   HB_CK(e, e->part_ends.alloc(4 * (size_t)n));
   HB_CK(e, cudaMemsetAsync(e->part_ends.p, 0, 16 * (size_t)n, s));
-  launch_finish_partition(e->items.p, n_items, e->front[0].p, e->front[1].p, e->rows[1].p, e->rows[0].p,
+  launch_finish_partition(e->items.p, n_items, e->front[0].p, e->front[1].p, e->rows[1], e->rows[0],
                           e->part_ends.p, s);
   HB_CK(e, cudaGetLastError());
   std::vector<Front> nx(2 * (size_t)n);
@@ -1605,7 +1630,7 @@ hb_status hb_rows(hb_engine* e, const hb_segment* segs, uint32_t n, uint32_t* ou
   for (uint32_t k = 0; k < n; ++k) {
     if (!seg_ok(e, &segs[k])) return refuse(e, "stale or foreign segment");
     if (segs[k].len)
-      HB_CK(e, cudaMemcpyAsync(out + at, e->rows[0].p + segs[k].offset, 4 * segs[k].len,
+      HB_CK(e, cudaMemcpyAsync(out + at, e->rows[0] + segs[k].offset, 4 * segs[k].len,
                                cudaMemcpyDeviceToHost, e->stream));
     at += segs[k].len;
   }
@@ -1675,14 +1700,21 @@ hb_status hb_add_leaf_values(hb_engine* e, const hb_segment* segs, const float* 
     if (!seg_ok(e, &segs[k])) return refuse(e, "stale or foreign segment");
   if (!n) return HB_OK;
   if (!values) return HB_INVALID_ARGUMENT;
-  std::vector<uint2> sl(n);
-  for (uint32_t k = 0; k < n; ++k) sl[k] = make_uint2((uint32_t)segs[k].offset, (uint32_t)segs[k].len);
+  // segments cut into tiles of kAddTile rows, so a large leaf spreads over
+  // many CTAs
+  std::vector<uint4> tiles;
+  for (uint32_t k = 0; k < n; ++k) {
+    uint32_t bits;
+    std::memcpy(&bits, values + k, 4);
+    for (uint64_t o = 0; o < segs[k].len; o += kAddTile)
+      tiles.push_back(make_uint4((uint32_t)(segs[k].offset + o),
+                                 (uint32_t)std::min<uint64_t>(kAddTile, segs[k].len - o), bits, 0u));
+  }
+  if (tiles.empty()) return HB_OK;
   cudaStream_t s = e->stream;
-  HB_CK(e, e->seg_list.alloc(n));
-  HB_CK(e, e->seg_vals.alloc(n));
-  HB_CK(e, cudaMemcpyAsync(e->seg_list.p, sl.data(), sizeof(uint2) * n, cudaMemcpyHostToDevice, s));
-  HB_CK(e, cudaMemcpyAsync(e->seg_vals.p, values, sizeof(float) * n, cudaMemcpyHostToDevice, s));
-  launch_add_segments(e->rows[0].p, e->seg_list.p, e->seg_vals.p, n, e->margin.p, s);
+  HB_CK(e, e->seg_tiles.alloc(tiles.size()));
+  HB_CK(e, cudaMemcpyAsync(e->seg_tiles.p, tiles.data(), sizeof(uint4) * tiles.size(), cudaMemcpyHostToDevice, s));
+  launch_add_segments(e->rows[0], e->seg_tiles.p, (uint32_t)tiles.size(), e->margin.p, s);
   HB_CK(e, cudaGetLastError());
   HB_CK(e, cudaStreamSynchronize(s));
   return HB_OK;
@@ -1728,7 +1760,7 @@ hb_status hb_build_resident(hb_engine* e, const hb_segment* segs, const uint32_t
   for (uint32_t k = 0; k < n; ++k)
     HB_CK(e, cudaMemsetAsync(e->resident.p + (size_t)slots[k] * tb, 0, sizeof(longlong2) * tb, s));
   if (n) {
-    hb_status st = build_entries(e, en, e->resident.p, 0, e->rows[0].p);
+    hb_status st = build_entries(e, en, e->resident.p, 0, e->rows[0]);
     if (st != HB_OK) return st;
   }
   if (n_siblings) {
@@ -1992,8 +2024,8 @@ static hb_status graph_rounds(hb_engine* e, const hb_train_params* p, int rounds
   // the round graph depends on the parameters, the communicator and every
   // buffer it touches (a buffer that grew has moved)
   const void* ptrs[] = {e->comm, e->rec.p, e->col.p, e->colmiss.p, e->fo.p, e->cuts.p,
-                        e->gpair.p, e->margin.p, e->label.p, e->weight.p, e->rows[0].p,
-                        e->rows[1].p, e->scale.p, e->hist_all.p, e->front[0].p, e->front[1].p,
+                        e->gpair.p, e->margin.p, e->label.p, e->weight.p, e->rows[0],
+                        e->rows[1], e->scale.p, e->hist_all.p, e->front[0].p, e->front[1].p,
                         e->cand.p, e->dec.p, e->items.p, e->dirbits.p, e->item_left.p,
                         e->item_off.p, e->entries.p, e->pairs.p, e->ls.p, e->tree.p,
                         e->wtree.p, e->forest.p, e->counts.p, e->tree_counter.p,

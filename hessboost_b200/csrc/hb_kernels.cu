@@ -2644,12 +2644,19 @@ __global__ void __launch_bounds__(kPartThreads)
 // Nothing computed from a segment depends on its order: histograms are
 // exact integer sums and the leaf adds go by row. Saves the stable scheme's
 // second pass over the rows (the scatter) and its per-node tile scan.
+// half = 0: the children take the parent's positions in rows_out (another
+// buffer); half = n (lossguide, rows_in == rows_out spanning 2n): they take
+// the positions half away in the other half of the buffer (seg_flip).
+__device__ __forceinline__ uint32_t seg_flip(uint32_t begin, uint32_t half) {
+  return half == 0u ? begin : begin >= half ? begin - half : begin + half;
+}
+
 template <bool CSR>
 __global__ void __launch_bounds__(kPartThreads)
     k_part_onepass(DevConst c, const uint8_t* __restrict__ col, const uint64_t* __restrict__ colmiss,
-                   const uint32_t* __restrict__ rows_in, int identity, const Front* __restrict__ front,
+                   const uint32_t* rows_in, int identity, const Front* __restrict__ front,
                    const Decision* __restrict__ dec, const LevelState* __restrict__ ls,
-                   uint32_t* __restrict__ fill, uint32_t* __restrict__ rows_out) {
+                   uint32_t* __restrict__ fill, uint32_t* rows_out, uint32_t half) {
   pdl_wait();
   const int it = blockIdx.x;
   if (it >= ls->n_items) return;
@@ -2707,8 +2714,9 @@ __global__ void __launch_bounds__(kPartThreads)
     s_base_r = tile_r ? atomicAdd(&fill[2 * d.pair + 1], tile_r) : 0u;
   }
   __syncthreads();
-  const uint32_t left0 = fr.begin + s_base_l;                        // this tile's left chunk
-  const uint32_t right0 = fr.begin + fr.len - s_base_r - tile_r;     // and right chunk
+  const uint32_t out0 = seg_flip(fr.begin, half);
+  const uint32_t left0 = out0 + s_base_l;                        // this tile's left chunk
+  const uint32_t right0 = out0 + fr.len - s_base_r - tile_r;     // and right chunk
   const uint32_t lt = (1u << lane) - 1u;
 #pragma unroll
   for (int j = 0; j < kPerThread; ++j) {
@@ -2736,7 +2744,7 @@ template <int T>
 __global__ void __launch_bounds__(T)
     k_part_plan(const Front* __restrict__ front, const Decision* __restrict__ dec, const LevelState* ls,
                 uint32_t* __restrict__ fill, Front* next, HEntry* __restrict__ entries,
-                Triple* __restrict__ pairs, LevelState* __restrict__ ls_next) {
+                Triple* __restrict__ pairs, LevelState* __restrict__ ls_next, uint32_t half) {
   pdl_wait();
   const int k = threadIdx.x;
   if (k < ls->n_front) {
@@ -2744,9 +2752,10 @@ __global__ void __launch_bounds__(T)
     if (d.split) {
       const Front fr = front[k];
       const uint32_t L = fill[2 * d.pair];
-      next[2 * d.pair].begin = fr.begin;
+      const uint32_t b = seg_flip(fr.begin, half);
+      next[2 * d.pair].begin = b;
       next[2 * d.pair].len = L;
-      next[2 * d.pair + 1].begin = fr.begin + L;
+      next[2 * d.pair + 1].begin = b + L;
       next[2 * d.pair + 1].len = fr.len - L;
       fill[2 * d.pair] = 0u;
       fill[2 * d.pair + 1] = 0u;
@@ -3016,12 +3025,12 @@ __global__ void k_iota(uint32_t* __restrict__ rows, uint32_t first, uint64_t n) 
 
 // Each segment (offset, len) gets its value added to the margins of its
 // rows: one CTA per segment, a grid-stride loop inside.
-__global__ void k_add_segments(const uint32_t* __restrict__ rows, const uint2* __restrict__ segs,
-                               const float* __restrict__ values, float* __restrict__ margin) {
-  const uint2 sg = segs[blockIdx.x];
-  const float v = values[blockIdx.x];
-  for (uint32_t i = threadIdx.x; i < sg.y; i += blockDim.x) {
-    const uint32_t r = rows[sg.x + i];
+__global__ void k_add_segments(const uint32_t* __restrict__ rows, const uint4* __restrict__ tiles,
+                               float* __restrict__ margin) {
+  const uint4 t = tiles[blockIdx.x];  // first row position, length, leaf value bits
+  const float v = __uint_as_float(t.z);
+  for (uint32_t i = threadIdx.x; i < t.y; i += blockDim.x) {
+    const uint32_t r = rows[t.x + i];
     margin[r] = __fadd_rn(margin[r], v);
   }
 }
@@ -3080,9 +3089,9 @@ void launch_iota(uint32_t* rows, uint32_t first, uint64_t n, int n_sm, cudaStrea
   k_iota<<<grid, 256, 0, s>>>(rows, first, n);
 }
 
-void launch_add_segments(const uint32_t* rows, const uint2* segs, const float* values, uint32_t n,
-                         float* margin, cudaStream_t s) {
-  if (n) k_add_segments<<<n, 256, 0, s>>>(rows, segs, values, margin);
+void launch_add_segments(const uint32_t* rows, const uint4* tiles, uint32_t n_tiles, float* margin,
+                         cudaStream_t s) {
+  if (n_tiles) k_add_segments<<<n_tiles, 256, 0, s>>>(rows, tiles, margin);
 }
 
 void launch_finish_partition(const PItem* items, int n_items, const Front* parents, const Front* kids,
@@ -3334,23 +3343,24 @@ void launch_part_count(const DevConst& c, const uint8_t* col, const uint64_t* co
 void launch_part_onepass(const DevConst& c, const uint8_t* col, const uint64_t* colmiss,
                          const uint32_t* rows_in, int identity, const Front* front, const Decision* dec,
                          const LevelState* ls, int max_items, uint32_t* fill, uint32_t* rows_out,
-                         cudaStream_t s) {
+                         uint32_t half, cudaStream_t s) {
   if (c.csr && !col)
     launch_pdl(k_part_onepass<true>, dim3(max_items), dim3(kPartThreads), 0, s, c, col, colmiss, rows_in,
-               identity, front, dec, ls, fill, rows_out);
+               identity, front, dec, ls, fill, rows_out, half);
   else
     launch_pdl(k_part_onepass<false>, dim3(max_items), dim3(kPartThreads), 0, s, c, col, colmiss, rows_in,
-               identity, front, dec, ls, fill, rows_out);
+               identity, front, dec, ls, fill, rows_out, half);
 }
 
 void launch_part_plan(const Front* front, const Decision* dec, const LevelState* ls, uint32_t* fill,
                       Front* next, HEntry* entries, Triple* pairs, LevelState* ls_next, int max_front,
-                      cudaStream_t s) {
+                      uint32_t half, cudaStream_t s) {
   if (max_front <= 256)
-    launch_pdl(k_part_plan<256>, dim3(1), dim3(256), 0, s, front, dec, ls, fill, next, entries, pairs, ls_next);
+    launch_pdl(k_part_plan<256>, dim3(1), dim3(256), 0, s, front, dec, ls, fill, next, entries, pairs, ls_next,
+               half);
   else
     launch_pdl(k_part_plan<kApplyThreads>, dim3(1), dim3(kApplyThreads), 0, s, front, dec, ls, fill, next, entries,
-               pairs, ls_next);
+               pairs, ls_next, half);
 }
 
 void launch_part_scan(const Front* front, const Decision* dec, LevelState* ls, int max_front,

@@ -108,18 +108,21 @@ void launch_part_count(const DevConst& c, const uint8_t* col, const uint64_t* co
                        const Front* front, const Decision* dec, const PItem* items,
                        const LevelState* ls, int max_items, uint32_t* dirbits, uint32_t* item_left,
                        cudaStream_t s, uint32_t* rows_copy = nullptr);
-// One-pass partition (depthwise growth): each tile's left rows to a chunk at
-// its node's segment start, right rows to one at the end, reserved on
-// fill[2 pair], fill[2 pair + 1] (zero before the pass); a child's row order
-// is not the stable one. Then launch_part_plan: the children's segments,
-// the fill counts cleared, the next level's histogram plan.
+// One-pass partition: each tile's left rows to a chunk at its node's
+// segment start, right rows to one at the end, reserved on fill[2 pair],
+// fill[2 pair + 1] (zero before the pass); a child's row order is not the
+// stable one. Then launch_part_plan: the children's segments, the fill
+// counts cleared, the next level's histogram plan. half = 0: the children
+// keep the parent's positions in rows_out (depthwise growth); half = n: the
+// positions n away in the other half of one 2n buffer (lossguide growth,
+// rows_in == rows_out).
 void launch_part_onepass(const DevConst& c, const uint8_t* col, const uint64_t* colmiss,
                          const uint32_t* rows_in, int identity, const Front* front, const Decision* dec,
                          const LevelState* ls, int max_items, uint32_t* fill, uint32_t* rows_out,
-                         cudaStream_t s);
+                         uint32_t half, cudaStream_t s);
 void launch_part_plan(const Front* front, const Decision* dec, const LevelState* ls, uint32_t* fill,
                       Front* next, HEntry* entries, Triple* pairs, LevelState* ls_next, int max_front,
-                      cudaStream_t s);
+                      uint32_t half, cudaStream_t s);
 // Per-node scan of the tiles' left counts and the children's segments; with
 // `entries` (device growth) the last CTA also plans the next level's
 // histograms (built child = smaller Hessian; entries, sibling pairs, ls_next).
@@ -155,8 +158,11 @@ void launch_dequantize(const longlong2* hist, uint32_t n, const Scale* scale, do
 // p[0, n) = v.
 void launch_fill(float* p, float v, uint64_t n, int n_sm, cudaStream_t s);
 void launch_iota(uint32_t* rows, uint32_t first, uint64_t n, int n_sm, cudaStream_t s);
-void launch_add_segments(const uint32_t* rows, const uint2* segs, const float* values, uint32_t n,
-                         float* margin, cudaStream_t s);
+// Each tile (first row position, length <= kAddTile, leaf value bits) adds
+// its value to the margins of its rows, a CTA per tile.
+constexpr uint32_t kAddTile = 8192;
+void launch_add_segments(const uint32_t* rows, const uint4* tiles, uint32_t n_tiles, float* margin,
+                         cudaStream_t s);
 void launch_finish_partition(const PItem* items, int n_items, const Front* parents, const Front* kids,
                              const uint32_t* rows_out, uint32_t* rows_in, uint32_t* ends, cudaStream_t s);
 void launch_seg_total(const uint32_t* rows, uint64_t begin, uint64_t len, const float2* gpair,

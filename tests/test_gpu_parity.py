@@ -650,6 +650,35 @@ def test_one_pass_partition_agrees_with_the_stable_one(monkeypatch, n_cols, miss
     np.testing.assert_array_equal(_bits(runs[0].predict_margin(x)), _bits(runs[1].predict_margin(x)))
 
 
+@pytest.mark.parametrize("layout", ["dense", "csr"])
+def test_lossguide_one_pass_partition_agrees_with_the_stable_one(monkeypatch, layout):
+    """Lossguide growth with the one-pass partition (a node's children move
+    to the other half of the 2n row buffer, in reservation order) and with
+    the stable partition (every node in the first half) grows the same
+    forest and training margins, dense with missing values and over a CSR
+    index."""
+    if layout == "dense":
+        x, y = synth.logistic_c2(200_003, 12, seed=81, missing=0.1)
+        m = H.BinnedMatrix.from_dense(x)
+    else:
+        indptr, indices, values, y = synth.sparse_c4(150_001, 300, density=0.05, seed=82)
+        m = H.BinnedMatrix.from_csr(indptr, indices, values, 300, 64)
+    p = H.TrainingParams(objective="binary:logistic", grow_policy="lossguide", max_depth=0, max_leaves=63,
+                         eta=0.3, max_bin=256 if layout == "dense" else 64)
+    runs = []
+    for stable in ("0", "1"):
+        monkeypatch.setenv("HB_STABLE_PARTITION", stable)
+        e = H.Engine()
+        try:
+            e.upload(m)
+            nodes, ptr = e.train(p, y, 4, H.base_margin(p, y))
+            runs.append((nodes, ptr, e.read_margins()))
+        finally:
+            e.close()
+    assert_forest_equal(runs[0][0], runs[0][1], runs[1][0], runs[1][1], f"lossguide {layout}")
+    np.testing.assert_array_equal(_bits(runs[0][2]), _bits(runs[1][2]))
+
+
 def test_engine_reused_across_uploads_of_one_shape():
     """An engine keeps its captured round graph across uploads of the same
     shape (the graph's key holds the index's constants and buffers): a
