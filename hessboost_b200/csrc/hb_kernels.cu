@@ -2652,7 +2652,7 @@ __device__ __forceinline__ uint32_t seg_flip(uint32_t begin, uint32_t half) {
 }
 
 template <bool CSR>
-__global__ void __launch_bounds__(kPartThreads)
+__global__ void __launch_bounds__(kPartThreads, 6)
     k_part_onepass(DevConst c, const uint8_t* __restrict__ col, const uint64_t* __restrict__ colmiss,
                    const uint32_t* rows_in, int identity, const Front* __restrict__ front,
                    const Decision* __restrict__ dec, const LevelState* __restrict__ ls,
@@ -2666,15 +2666,18 @@ __global__ void __launch_bounds__(kPartThreads)
   const Decision d = dec[pi.k];
   const uint8_t* colf = col + (uint64_t)d.feature * c.n_rows;
   const uint64_t words = (c.n_rows + 63) / 64;
-  const uint64_t* missf = colmiss ? colmiss + (uint64_t)d.feature * words : nullptr;
+  // the bitmap read as 32-bit words (bit r & 31 of word r >> 5)
+  const uint32_t* missw = colmiss ? reinterpret_cast<const uint32_t*>(colmiss + (uint64_t)d.feature * words)
+                                  : nullptr;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const uint32_t base = fr.begin + pi.off;
+  const uint32_t t0 = warp * 256 + lane;  // position of row j: t0 + 32 j
+  const uint32_t* rin = rows_in + base + t0;
   uint32_t row[kPerThread];
 #pragma unroll
-  for (int j = 0; j < kPerThread; ++j) {
-    const uint32_t i = warp * 256 + j * 32 + lane;
-    const uint32_t at = base + min(i, pi.len - 1);
-    row[j] = identity ? at : rows_in[at];
+  for (int j = 0; j < kPerThread; ++j) {  // past the tile's end: row 0, read but not moved
+    const bool in = t0 + j * 32 < pi.len;
+    row[j] = !in ? 0u : identity ? base + t0 + j * 32 : rin[j * 32];
   }
   const uint32_t csr_lo = CSR ? __ldg(c.fo + d.feature) : 0u;
   const uint32_t csr_hi = CSR ? __ldg(c.fo + d.feature + 1) : 0u;
@@ -2691,10 +2694,9 @@ __global__ void __launch_bounds__(kPartThreads)
       bin = lb;
     } else {
       bin = colf[r];
-      miss = missf && ((missf[r >> 6] >> (r & 63)) & 1ull);
+      miss = missw && ((missw[r >> 5] >> (r & 31)) & 1u);
     }
-    const uint32_t i = warp * 256 + j * 32 + lane;
-    const bool left = i < pi.len && (miss ? (d.default_left != 0) : (bin < d.limit));
+    const bool left = t0 + j * 32 < pi.len && (miss ? (d.default_left != 0) : (bin < d.limit));
     bal[j] = __ballot_sync(kFull, left);
     wl += __popc(bal[j]);
   }
@@ -2704,9 +2706,11 @@ __global__ void __launch_bounds__(kPartThreads)
   if (lane == 0) s_wl[warp] = wl;
   __syncthreads();
   uint32_t before = 0, tile_l = 0;
+#pragma unroll
   for (int w = 0; w < kPartThreads / 32; ++w) {
-    before += w < warp ? s_wl[w] : 0u;
-    tile_l += s_wl[w];
+    const uint32_t v = s_wl[w];
+    before += w < warp ? v : 0u;
+    tile_l += v;
   }
   const uint32_t tile_r = pi.len - tile_l;
   if (threadIdx.x == 0) {
@@ -2715,19 +2719,17 @@ __global__ void __launch_bounds__(kPartThreads)
   }
   __syncthreads();
   const uint32_t out0 = seg_flip(fr.begin, half);
-  const uint32_t left0 = out0 + s_base_l;                        // this tile's left chunk
-  const uint32_t right0 = out0 + fr.len - s_base_r - tile_r;     // and right chunk
+  // row at position i of the tile, lrank left rows before it: left to
+  // left0 + lrank, right to right0 + (i - lrank)
+  const uint32_t left0 = out0 + s_base_l;
+  const uint32_t right0 = out0 + fr.len - s_base_r - tile_r;
   const uint32_t lt = (1u << lane) - 1u;
 #pragma unroll
   for (int j = 0; j < kPerThread; ++j) {
-    const uint32_t i = warp * 256 + j * 32 + lane;
-    const uint32_t lrank = before + __popc(bal[j] & lt);  // left rows of the tile before row i
-    if (i < pi.len) {
-      if ((bal[j] >> lane) & 1u)
-        rows_out[left0 + lrank] = row[j];
-      else
-        rows_out[right0 + (i - lrank)] = row[j];
-    }
+    const uint32_t i = t0 + j * 32;
+    const uint32_t lrank = before + __popc(bal[j] & lt);
+    const uint32_t dst = ((bal[j] >> lane) & 1u) ? left0 + lrank : right0 + (i - lrank);
+    if (i < pi.len) rows_out[dst] = row[j];
     before += __popc(bal[j]);
   }
 }
