@@ -100,6 +100,9 @@ struct hb_engine {
   // depthwise one-pass partition: per split, the rows placed so far in its
   // left and right child (zero between levels)
   DevBuf<uint32_t> fill;
+  // each frontier node's best feature from the scan (a 64-bit maximum),
+  // read and cleared by the apply / lossguide step: zero between uses
+  DevBuf<unsigned long long> best_key;
   // HB_STABLE_PARTITION=1: the three-pass stable partition in depthwise
   // growth too (children keep ascending row order)
   bool stable_partition = false;
@@ -309,6 +312,8 @@ hb_status ensure_growth_buffers(hb_engine* e, int max_depth) {
   HB_CK(e, e->item_off.alloc(e->max_items));
   HB_CK(e, e->fill.alloc((size_t)2 * max_front));
   HB_CK(e, cudaMemset(e->fill.p, 0, sizeof(uint32_t) * 2 * max_front));
+  HB_CK(e, e->best_key.alloc(max_front));
+  HB_CK(e, cudaMemset(e->best_key.p, 0, sizeof(unsigned long long) * max_front));
   HB_CK(e, e->entries.alloc(max_front));
   HB_CK(e, e->pairs.alloc(max_front));
   HB_CK(e, e->ls.alloc(kMaxDepth + 2));
@@ -596,13 +601,13 @@ hb_status grow_device(hb_engine* e, const hb_train_params* p, bool to_forest) {
       // parent - built, made by the scan itself
       const int sib_base = d == 0 ? INT_MAX : (1 << d) - 1 + (1 << (d - 1));
       launch_scan(c, e->fo.p, hist, fr, lsd, d == 0 ? nullptr : e->pairs.p, sib_base, cur_scale(e),
-                  max_front, e->cand.p, s);
+                  max_front, e->cand.p, s, nullptr, e->best_key.p);
       mark_end(e);
       ++launches;
     }
     mark_begin(e, T_APPLY);
     launch_apply(c, e->fo.p, e->cuts.p, e->cand.p, fr, nx, e->dec.p, e->items.p, lsd, lsn,
-                 e->tree.p, cur_wtree(e), cur_scale(e), d, leaf_only ? 1 : 0, s);
+                 e->tree.p, cur_wtree(e), cur_scale(e), d, leaf_only ? 1 : 0, e->best_key.p, s);
     mark_end(e);
     ++launches;
     HB_CK(e, cudaGetLastError());
@@ -688,6 +693,8 @@ hb_status ensure_lossguide_buffers(hb_engine* e, int L) {
   HB_CK(e, e->lg_state.alloc(1));
   HB_CK(e, e->lg_depth.alloc(n_nodes));
   HB_CK(e, e->fill.alloc(2));
+  HB_CK(e, e->best_key.alloc(2));
+  HB_CK(e, cudaMemset(e->best_key.p, 0, 2 * sizeof(unsigned long long)));
   e->wstride = (size_t)n_nodes;
   e->alloc_depth = -1;  // the depthwise sizes no longer hold
   e->lg_alloc = L;
@@ -742,7 +749,7 @@ hb_status grow_lossguide(hb_engine* e, const hb_train_params* p, bool to_forest)
   launch_root_stats(fr, totals, s);
   launch_lg_setup(e->lg_state.p, e->lg_depth.p, e->tree.p, fr, cur_scale(e), ls2, s);
   mark_begin(e, T_SCAN);
-  launch_scan(c, e->fo.p, hist, fr, ls0, nullptr, 0, cur_scale(e), 1, e->cand.p, s);
+  launch_scan(c, e->fo.p, hist, fr, ls0, nullptr, 0, cur_scale(e), 1, e->cand.p, s, nullptr, e->best_key.p);
   mark_end(e);
   HB_CK(e, cudaGetLastError());
   uint64_t launches = 5;
@@ -760,7 +767,7 @@ hb_status grow_lossguide(hb_engine* e, const hb_train_params* p, bool to_forest)
     mark_begin(e, T_APPLY);
     launch_lg_step(c, e->fo.p, e->cuts.p, e->cand.p, k == 0 ? fr : nx, fr, nx, e->dec.p, ls1, ls2,
                    e->tree.p, e->wtree.p, cur_scale(e), e->lg_heap.p, L + 2, e->lg_state.p, e->lg_depth.p,
-                   max_leaves, depth_limit, final_step ? 1 : 0, s);
+                   max_leaves, depth_limit, final_step ? 1 : 0, e->best_key.p, s);
     mark_end(e);
     ++launches;
     if (final_step) break;
@@ -789,7 +796,8 @@ hb_status grow_lossguide(hb_engine* e, const hb_train_params* p, bool to_forest)
                 e->row_stats.p, hgrid, smem, s);
     mark_end(e);
     mark_begin(e, T_SCAN);
-    launch_scan(c, e->fo.p, hist, nx, ls2, e->pairs.p, -1, cur_scale(e), 2, e->cand.p, s);
+    launch_scan(c, e->fo.p, hist, nx, ls2, e->pairs.p, -1, cur_scale(e), 2, e->cand.p, s, nullptr,
+                e->best_key.p);
     mark_end(e);
     launches += 5;
     HB_CK(e, cudaGetLastError());
@@ -957,6 +965,7 @@ hb_status hb_engine_destroy(hb_engine* e) {
   e->item_left.release();
   e->item_off.release();
   e->fill.release();
+  e->best_key.release();
   e->entries.release();
   e->pairs.release();
   e->ls.release();
@@ -2030,7 +2039,7 @@ static hb_status graph_rounds(hb_engine* e, const hb_train_params* p, int rounds
                         e->item_off.p, e->entries.p, e->pairs.p, e->ls.p, e->tree.p,
                         e->wtree.p, e->forest.p, e->counts.p, e->tree_counter.p,
                         e->row_stats.p, e->flags.p, e->lg_heap.p, e->lg_state.p,
-                        e->lg_depth.p, e->csr_ptr.p, e->csr_bins.p, e->fill.p};
+                        e->lg_depth.p, e->csr_ptr.p, e->csr_bins.p, e->fill.p, e->best_key.p};
   const int weighted = e->weight_key ? 1 : 0;
   std::vector<unsigned char> key(sizeof(hb_train_params) + sizeof(ptrs) + sizeof(int) * 2);
   std::memcpy(key.data(), p, sizeof(hb_train_params));

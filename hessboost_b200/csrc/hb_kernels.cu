@@ -1499,11 +1499,26 @@ __device__ __forceinline__ bool cand_better(float l, int seq, float bl, int bseq
   return l > bl || (l == bl && seq < bseq);
 }
 
+// A node's best split over its features, kept as one 64-bit maximum: the
+// merge rule of builder/mod.rs:313 (`need_replace` over ascending features:
+// the largest loss change above 0, the lowest feature among equals) is the
+// maximum of (loss bits, ~feature) over the features whose loss is above 0,
+// since the bits of positive floats order as the floats do. Each scan's
+// winner adds its feature with one atomicMax; the level's apply (or the
+// lossguide step) reads the node's key and clears it. 0: no candidate.
+__device__ __forceinline__ unsigned long long cand_key(float loss, uint32_t f) {
+  return ((unsigned long long)__float_as_uint(loss) << 32) | (unsigned long long)(0xffffffffu - f);
+}
+__device__ __forceinline__ int key_feature(unsigned long long key) {
+  return key ? (int)(0xffffffffu - (uint32_t)key) : -1;
+}
+
 __global__ void __launch_bounds__(kSplitThreads)
     k_scan(DevConst c, const uint32_t* __restrict__ fo, longlong2* __restrict__ hist,
            const Front* __restrict__ front, const LevelState* __restrict__ ls,
            const Triple* __restrict__ pairs, int sib_base, const Scale* __restrict__ scale,
-           Cand* __restrict__ cand, const int8_t* __restrict__ dirs) {
+           Cand* __restrict__ cand, const int8_t* __restrict__ dirs,
+             unsigned long long* __restrict__ best_key) {
   pdl_wait();
   const int f = blockIdx.x;
   const int k = blockIdx.y;
@@ -1660,6 +1675,7 @@ __global__ void __launch_bounds__(kSplitThreads)
     e.lg = blg;
     e.lh = blh;
     *out = e;
+    if (best_key && best > 0.0f) atomicMax(best_key + k, cand_key(best, (uint32_t)f));
   }
 }
 
@@ -1673,7 +1689,8 @@ __global__ void __launch_bounds__(kSplitThreads)
     k_scan_wide(DevConst c, const uint32_t* __restrict__ fo, longlong2* __restrict__ hist,
                 const Front* __restrict__ front, const LevelState* __restrict__ ls,
                 const Triple* __restrict__ pairs, int sib_base, const Scale* __restrict__ scale,
-                Cand* __restrict__ cand, const int8_t* __restrict__ dirs) {
+                Cand* __restrict__ cand, const int8_t* __restrict__ dirs,
+             unsigned long long* __restrict__ best_key) {
   pdl_wait();
   const int f = blockIdx.x;
   const int k = blockIdx.y;
@@ -1853,6 +1870,7 @@ __global__ void __launch_bounds__(kSplitThreads)
     e.lg = blg;
     e.lh = blh;
     *out = e;
+    if (best_key && best > 0.0f) atomicMax(best_key + k, cand_key(best, (uint32_t)f));
   }
 }
 
@@ -1868,7 +1886,8 @@ __global__ void __launch_bounds__(kScanWarps * 32)
     k_scan_w(DevConst c, const uint32_t* __restrict__ fo, longlong2* __restrict__ hist,
              const Front* __restrict__ front, const LevelState* __restrict__ ls,
              const Triple* __restrict__ pairs, int sib_base, const Scale* __restrict__ scale,
-             Cand* __restrict__ cand, const int8_t* __restrict__ dirs) {
+             Cand* __restrict__ cand, const int8_t* __restrict__ dirs,
+             unsigned long long* __restrict__ best_key) {
   pdl_wait();
   const int k = blockIdx.y;
   if (k >= ls->n_front) return;
@@ -2010,6 +2029,7 @@ __global__ void __launch_bounds__(kScanWarps * 32)
     e.lg = blg;
     e.lh = blh;
     *out = e;
+    if (best_key && best > 0.0f) atomicMax(best_key + k, cand_key(best, (uint32_t)f));
   }
 }
 
@@ -2044,7 +2064,8 @@ __global__ void __launch_bounds__(T)
             const Cand* __restrict__ cand, const Front* __restrict__ front, Front* __restrict__ next,
             Decision* __restrict__ dec, PItem* __restrict__ items, LevelState* ls,
             LevelState* ls_next, hb_tree_node* __restrict__ tree, WNode* __restrict__ wtree,
-            const Scale* __restrict__ scale, int depth, int leaf_only) {
+            const Scale* __restrict__ scale, int depth, int leaf_only,
+            unsigned long long* __restrict__ best_key) {
   pdl_wait();
   using Scan = cub::BlockScan<int, T>;
   __shared__ typename Scan::TempStorage tmp;
@@ -2054,34 +2075,12 @@ __global__ void __launch_bounds__(T)
   const double ig = scale->ig, ih = scale->ih;
   if (depth == 0 && k == 0 && n_front > 0) tree[0] = make_leaf(0.0f, (float)(ll2d(front[0].h) * ih));
 
-  // Merge each node's per-feature winners, a warp per node: the largest
-  // loss change, the lowest feature among equals, and only above the empty
-  // split's 0 -- need_replace over ascending features.
-  __shared__ int s_best[T];
-  if (!leaf_only) {
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    for (int kk = warp; kk < n_front; kk += T / 32) {
-      float bl = 0.0f;
-      int bf = -1;
-      for (uint32_t f = lane; f < c.n_cols; f += 32) {
-        const float l = cand[(uint64_t)kk * c.n_cols + f].loss;
-        if (l > bl) {
-          bl = l;
-          bf = (int)f;
-        }
-      }
-#pragma unroll
-      for (int o = 16; o > 0; o >>= 1) {
-        const float ol = __shfl_xor_sync(kFull, bl, o);
-        const int of = __shfl_xor_sync(kFull, bf, o);
-        if (ol > bl || (ol == bl && of >= 0 && (bf < 0 || of < bf))) {
-          bl = ol;
-          bf = of;
-        }
-      }
-      if (lane == 0) s_best[kk] = bf;
-    }
-    __syncthreads();
+  // each node's best feature: its key from the scan (cand_key), cleared for
+  // the next level
+  int bf_k = -1;
+  if (!leaf_only && k < n_front) {
+    bf_k = key_feature(best_key[k]);
+    best_key[k] = 0ull;
   }
   Front fr{};
   Cand best{};
@@ -2093,7 +2092,7 @@ __global__ void __launch_bounds__(T)
       best.loss = 0.0f;
       best.bin = -1;
       best.default_left = 1;
-      const int bf = s_best[k];
+      const int bf = bf_k;
       if (bf >= 0) {
         best = cand[(uint64_t)k * c.n_cols + bf];
         best_f = (uint32_t)bf;
@@ -2211,8 +2210,7 @@ __global__ void __launch_bounds__(T)
 // Rust's BinaryHeap as the host builder uses it (push: sift_up; pop: swap
 // the last into the root, sift_down_to_bottom, sift_up), keyed by the
 // f64::total_cmp order of the best loss change.
-constexpr int kLgThreads = 512;  // 8 warps per pending node (at most two)
-constexpr int kLgWarpsPerNode = 8;
+constexpr int kLgThreads = 256;  // the heap's copies in and out
 
 __device__ __forceinline__ long long total_key(double v) {
   const long long b = __double_as_longlong(v);
@@ -2286,11 +2284,10 @@ __global__ void __launch_bounds__(kLgThreads)
               Front* next, Decision* dec, LevelState* ls, LevelState* ls_next,
               hb_tree_node* __restrict__ tree, WNode* __restrict__ wtree,
               const Scale* __restrict__ scale, LgNode* __restrict__ heap, LgState* st,
-              int32_t* __restrict__ ndepth, int max_leaves, int depth_limit, int final_step) {
+              int32_t* __restrict__ ndepth, int max_leaves, int depth_limit, int final_step,
+              unsigned long long* __restrict__ best_key) {
   pdl_wait();
   __shared__ LgNode s_new[2];
-  __shared__ float s_bl[kLgThreads / 32];
-  __shared__ int s_bf[kLgThreads / 32];
   __shared__ int s_n;
   extern __shared__ __align__(16) unsigned char lg_dyn[];
   LgNode* sheap = reinterpret_cast<LgNode*>(lg_dyn);  // the heap, worked in shared memory
@@ -2298,85 +2295,46 @@ __global__ void __launch_bounds__(kLgThreads)
   if (S0.done) return;
   const double ig = scale->ig, ih = scale->ih;
   const int np = S0.n_pending;
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   {  // bring the heap in (8-byte words, all threads)
     const unsigned long long* src = reinterpret_cast<const unsigned long long*>(heap);
     unsigned long long* dst = reinterpret_cast<unsigned long long*>(sheap);
     const int words = S0.heap_n * (int)(sizeof(LgNode) / 8);
     for (int i = threadIdx.x; i < words; i += kLgThreads) dst[i] = src[i];
   }
-  // each pending node's best split over its features: the largest loss
-  // change above 0, the lowest feature among equals (need_replace,
-  // builder/mod.rs:313); kLgWarpsPerNode warps a node, each over every
-  // kLgWarpsPerNode-th block of 32 features, then the warps' results merged
-  // by the same rule (it is associative)
-  const int node = warp / kLgWarpsPerNode, sub = warp % kLgWarpsPerNode;
-  if (node < np) {
-    float bl = 0.0f;
-    int bf = -1;
-    for (uint32_t f = sub * 32 + lane; f < c.n_cols; f += 32 * kLgWarpsPerNode) {
-      const float l = cand[(uint64_t)node * c.n_cols + f].loss;
-      if (l > bl) {
-        bl = l;
-        bf = (int)f;
-      }
+  // each pending node's best split over its features (need_replace,
+  // builder/mod.rs:313): its key from the scan (cand_key), cleared for the
+  // next step
+  if (threadIdx.x < np) {
+    const int node = threadIdx.x;
+    const int bf = key_feature(best_key[node]);
+    best_key[node] = 0ull;
+    const Front fr = pend[node];
+    LgNode x;
+    x.nid = fr.node;
+    x.depth = ndepth[fr.node];
+    x.begin = fr.begin;
+    x.len = fr.len;
+    x.g = fr.g;
+    x.h = fr.h;
+    x.lower = fr.lower;
+    x.upper = fr.upper;
+    if (bf >= 0) {
+      const Cand cd = cand[(uint64_t)node * c.n_cols + bf];
+      x.loss = cd.loss;
+      x.feature = bf;
+      x.bin = cd.bin;
+      x.default_left = cd.default_left;
+      x.lg = cd.lg;
+      x.lh = cd.lh;
+    } else {
+      x.loss = 0.0f;
+      x.feature = -1;
+      x.bin = -1;
+      x.default_left = 1;
+      x.lg = x.lh = 0;
     }
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) {
-      const float ol = __shfl_xor_sync(kFull, bl, o);
-      const int of = __shfl_xor_sync(kFull, bf, o);
-      if (ol > bl || (ol == bl && of >= 0 && (bf < 0 || of < bf))) {
-        bl = ol;
-        bf = of;
-      }
-    }
-    if (lane == 0) {
-      s_bl[warp] = bl;
-      s_bf[warp] = bf;
-    }
-  }
-  __syncthreads();
-  if (node < np && sub == 0 && lane == 0) {
-    float bl = s_bl[warp];
-    int bf = s_bf[warp];
-    for (int k = 1; k < kLgWarpsPerNode; ++k) {
-      const float ol = s_bl[warp + k];
-      const int of = s_bf[warp + k];
-      if (ol > bl || (ol == bl && of >= 0 && (bf < 0 || of < bf))) {
-        bl = ol;
-        bf = of;
-      }
-    }
-    {
-      const int warp = node;  // the pending node's index below
-      const Front fr = pend[warp];
-      LgNode x;
-      x.nid = fr.node;
-      x.depth = ndepth[fr.node];
-      x.begin = fr.begin;
-      x.len = fr.len;
-      x.g = fr.g;
-      x.h = fr.h;
-      x.lower = fr.lower;
-      x.upper = fr.upper;
-      if (bf >= 0) {
-        const Cand cd = cand[(uint64_t)warp * c.n_cols + bf];
-        x.loss = cd.loss;
-        x.feature = bf;
-        x.bin = cd.bin;
-        x.default_left = cd.default_left;
-        x.lg = cd.lg;
-        x.lh = cd.lh;
-      } else {
-        x.loss = 0.0f;
-        x.feature = -1;
-        x.bin = -1;
-        x.default_left = 1;
-        x.lg = x.lh = 0;
-      }
-      x.key = total_key((double)x.loss);
-      s_new[warp] = x;
-    }
+    x.key = total_key((double)x.loss);
+    s_new[node] = x;
   }
   __syncthreads();
   if (threadIdx.x == 0) lg_step_serial(c, fo, cuts, front, next, dec, ls, ls_next, tree, wtree, ig, ih,
@@ -3295,38 +3253,39 @@ void launch_subtract(const Triple* pairs, const LevelState* ls, int max_pairs, u
 
 void launch_scan(const DevConst& c, const uint32_t* fo, longlong2* hist, const Front* front,
                  const LevelState* ls, const Triple* pairs, int sib_base, const Scale* scale,
-                 int max_front, Cand* cand, cudaStream_t s, const int8_t* dirs) {
+                 int max_front, Cand* cand, cudaStream_t s, const int8_t* dirs,
+                 unsigned long long* best_key) {
   if (max_front < 1 || c.n_cols == 0) return;
   // features of <= 128 bins: a warp per (node, feature); wider: a CTA
   if (c.max_bins <= 128 && !c.scan_cta) {
     dim3 grid((c.n_cols + kScanWarps - 1) / kScanWarps, max_front);
     if (c.max_bins <= 32)
-      launch_pdl(k_scan_w<1>, dim3(grid), dim3(kScanWarps * 32), 0, s, c, fo, hist, front, ls, pairs, sib_base, scale, cand, dirs);
+      launch_pdl(k_scan_w<1>, dim3(grid), dim3(kScanWarps * 32), 0, s, c, fo, hist, front, ls, pairs, sib_base, scale, cand, dirs, best_key);
     else if (c.max_bins <= 64)
-      launch_pdl(k_scan_w<2>, dim3(grid), dim3(kScanWarps * 32), 0, s, c, fo, hist, front, ls, pairs, sib_base, scale, cand, dirs);
+      launch_pdl(k_scan_w<2>, dim3(grid), dim3(kScanWarps * 32), 0, s, c, fo, hist, front, ls, pairs, sib_base, scale, cand, dirs, best_key);
     else
-      launch_pdl(k_scan_w<4>, dim3(grid), dim3(kScanWarps * 32), 0, s, c, fo, hist, front, ls, pairs, sib_base, scale, cand, dirs);
+      launch_pdl(k_scan_w<4>, dim3(grid), dim3(kScanWarps * 32), 0, s, c, fo, hist, front, ls, pairs, sib_base, scale, cand, dirs, best_key);
     return;
   }
   dim3 grid(c.n_cols, max_front);
   if (c.max_bins > (uint32_t)kSplitThreads) {
-    launch_pdl(k_scan_wide, dim3(grid), dim3(kSplitThreads), 0, s, c, fo, hist, front, ls, pairs, sib_base, scale, cand, dirs);
+    launch_pdl(k_scan_wide, dim3(grid), dim3(kSplitThreads), 0, s, c, fo, hist, front, ls, pairs, sib_base, scale, cand, dirs, best_key);
     return;
   }
-  launch_pdl(k_scan, dim3(grid), dim3(kSplitThreads), 0, s, c, fo, hist, front, ls, pairs, sib_base, scale, cand, dirs);
+  launch_pdl(k_scan, dim3(grid), dim3(kSplitThreads), 0, s, c, fo, hist, front, ls, pairs, sib_base, scale, cand, dirs, best_key);
 }
 
 void launch_apply(const DevConst& c, const uint32_t* fo, const float* cuts, const Cand* cand,
                   const Front* front, Front* next, Decision* dec, PItem* items, LevelState* ls,
                   LevelState* ls_next, hb_tree_node* tree, WNode* wtree, const Scale* scale,
-                  int depth, int leaf_only, cudaStream_t s) {
+                  int depth, int leaf_only, unsigned long long* best_key, cudaStream_t s) {
   // the frontier at `depth` has at most 2^depth nodes
   if (depth <= 8)
     launch_pdl(k_apply<256>, dim3(1), dim3(256), 0, s, c, fo, cuts, cand, front, next, dec, items, ls, ls_next,
-               tree, wtree, scale, depth, leaf_only);
+               tree, wtree, scale, depth, leaf_only, best_key);
   else
     launch_pdl(k_apply<kApplyThreads>, dim3(1), dim3(kApplyThreads), 0, s, c, fo, cuts, cand, front, next, dec,
-               items, ls, ls_next, tree, wtree, scale, depth, leaf_only);
+               items, ls, ls_next, tree, wtree, scale, depth, leaf_only, best_key);
 }
 
 void launch_part_count(const DevConst& c, const uint8_t* col, const uint64_t* colmiss,
@@ -3386,7 +3345,7 @@ void launch_lg_step(const DevConst& c, const uint32_t* fo, const float* cuts, co
                     const Front* pend, Front* front, Front* next, Decision* dec, LevelState* ls,
                     LevelState* ls_next, hb_tree_node* tree, WNode* wtree, const Scale* scale,
                     LgNode* heap, int heap_cap, LgState* st, int32_t* ndepth, int max_leaves,
-                    int depth_limit, int final_step, cudaStream_t s) {
+                    int depth_limit, int final_step, unsigned long long* best_key, cudaStream_t s) {
   const size_t smem = sizeof(LgNode) * (size_t)heap_cap;
   static size_t granted[64] = {0};
   int dev = 0;
@@ -3399,7 +3358,7 @@ void launch_lg_step(const DevConst& c, const uint32_t* fo, const float* cuts, co
   }
   launch_pdl(k_lg_step, dim3(1), dim3(kLgThreads), smem, s, c, fo, cuts, cand, pend, front, next, dec, ls, ls_next, tree,
                                         wtree, scale, heap, st, ndepth, max_leaves, depth_limit,
-                                        final_step);
+                                        final_step, best_key);
 }
 
 void launch_lg_setup(LgState* st, int32_t* ndepth, hb_tree_node* tree, const Front* root,

@@ -95,14 +95,17 @@ void launch_subtract(const Triple* pairs, const LevelState* ls, int max_pairs, u
 // Split scan of every frontier node; a node whose slot is >= sib_base (with
 // `pairs`) first gets its sibling histogram parent - built. `dirs`
 // ([max_front][n_cols] monotone directions) overrides the run's per-feature
-// constraints (c.mono) when set.
+// constraints (c.mono) when set. With best_key, each node's winning feature
+// also goes to best_key[node] (a 64-bit maximum, zero beforehand), which the
+// level's apply or the lossguide step reads and clears.
 void launch_scan(const DevConst& c, const uint32_t* fo, longlong2* hist, const Front* front,
                  const LevelState* ls, const Triple* pairs, int sib_base, const Scale* scale,
-                 int max_front, Cand* cand, cudaStream_t s, const int8_t* dirs = nullptr);
+                 int max_front, Cand* cand, cudaStream_t s, const int8_t* dirs = nullptr,
+                 unsigned long long* best_key = nullptr);
 void launch_apply(const DevConst& c, const uint32_t* fo, const float* cuts, const Cand* cand,
                   const Front* front, Front* next, Decision* dec, PItem* items, LevelState* ls,
                   LevelState* ls_next, hb_tree_node* tree, WNode* wtree, const Scale* scale,
-                  int depth, int leaf_only, cudaStream_t s);
+                  int depth, int leaf_only, unsigned long long* best_key, cudaStream_t s);
 void launch_part_count(const DevConst& c, const uint8_t* col, const uint64_t* colmiss,
                        const uint8_t* rec, int use_record, const uint32_t* rows_in, int identity,
                        const Front* front, const Decision* dec, const PItem* items,
@@ -141,7 +144,7 @@ void launch_lg_step(const DevConst& c, const uint32_t* fo, const float* cuts, co
                     const Front* pend, Front* front, Front* next, Decision* dec, LevelState* ls,
                     LevelState* ls_next, hb_tree_node* tree, WNode* wtree, const Scale* scale,
                     LgNode* heap, int heap_cap, LgState* st, int32_t* ndepth, int max_leaves,
-                    int depth_limit, int final_step, cudaStream_t s);
+                    int depth_limit, int final_step, unsigned long long* best_key, cudaStream_t s);
 void launch_lg_setup(LgState* st, int32_t* ndepth, hb_tree_node* tree, const Front* root,
                      const Scale* scale, LevelState* ls_next, cudaStream_t s);
 void launch_root_setup(uint64_t n_rows, Front* front, HEntry* entries, LevelState* ls,
