@@ -112,7 +112,8 @@ struct hb_engine {
   DevBuf<hb_tree_node> tree;
   DevBuf<WNode> wtree;
   // lossguide growth: the heap of waiting nodes, its state, node depths
-  DevBuf<LgNode> lg_heap;
+  DevBuf<LgKey> lg_heap;
+  DevBuf<LgNode> lg_pool;  // lossguide: each heap node's data at its node id
   DevBuf<LgState> lg_state;
   DevBuf<int32_t> lg_depth;
   bool pending_tree = false;  // host mirror of flags[0]: a grown tree's leaves await the margins
@@ -690,6 +691,7 @@ hb_status ensure_lossguide_buffers(hb_engine* e, int L) {
   HB_CK(e, e->tree.alloc(n_nodes));
   HB_CK(e, e->wtree.alloc(n_nodes));
   HB_CK(e, e->lg_heap.alloc((size_t)L + 2));
+  HB_CK(e, e->lg_pool.alloc((size_t)n_nodes));
   HB_CK(e, e->lg_state.alloc(1));
   HB_CK(e, e->lg_depth.alloc(n_nodes));
   HB_CK(e, e->fill.alloc(2));
@@ -766,7 +768,8 @@ hb_status grow_lossguide(hb_engine* e, const hb_train_params* p, bool to_forest)
     const bool final_step = k == L - 1;
     mark_begin(e, T_APPLY);
     launch_lg_step(c, e->fo.p, e->cuts.p, e->cand.p, k == 0 ? fr : nx, fr, nx, e->dec.p, ls1, ls2,
-                   e->tree.p, e->wtree.p, cur_scale(e), e->lg_heap.p, L + 2, e->lg_state.p, e->lg_depth.p,
+                   e->tree.p, e->wtree.p, cur_scale(e), e->lg_heap.p, e->lg_pool.p, L + 2, e->lg_state.p,
+                   e->lg_depth.p,
                    max_leaves, depth_limit, final_step ? 1 : 0, e->best_key.p, s);
     mark_end(e);
     ++launches;
@@ -959,6 +962,7 @@ hb_status hb_engine_destroy(hb_engine* e) {
   e->dec.release();
   e->items.release();
   e->lg_heap.release();
+  e->lg_pool.release();
   e->lg_state.release();
   e->lg_depth.release();
   e->dirbits.release();
@@ -2038,7 +2042,7 @@ static hb_status graph_rounds(hb_engine* e, const hb_train_params* p, int rounds
                         e->cand.p, e->dec.p, e->items.p, e->dirbits.p, e->item_left.p,
                         e->item_off.p, e->entries.p, e->pairs.p, e->ls.p, e->tree.p,
                         e->wtree.p, e->forest.p, e->counts.p, e->tree_counter.p,
-                        e->row_stats.p, e->flags.p, e->lg_heap.p, e->lg_state.p,
+                        e->row_stats.p, e->flags.p, e->lg_heap.p, e->lg_pool.p, e->lg_state.p,
                         e->lg_depth.p, e->csr_ptr.p, e->csr_bins.p, e->fill.p, e->best_key.p};
   const int weighted = e->weight_key ? 1 : 0;
   std::vector<unsigned char> key(sizeof(hb_train_params) + sizeof(ptrs) + sizeof(int) * 2);

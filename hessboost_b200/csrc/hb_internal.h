@@ -12,7 +12,10 @@
 //   colmiss  [n_cols][words] u64   missing bitmap, feature-major
 //   gpair    [n_rows] float2       this tree's (g, h)
 //   margin   [n_rows] f32, label [n_rows] f32
-//   rows[2]  [n_rows] u32          row ids, one segment per node (ping-pong)
+//   rows[2]  [n_rows] u32          row ids, one segment per node: the two
+//                                  halves of one 2n buffer (depthwise levels
+//                                  ping-pong; lossguide moves a node's
+//                                  children to the other half)
 //   hist     [slots][total_bins] longlong2 (fixed-point g, h), level-major
 //            slot layout: level L owns slots [2^L - 1, 2^(L+1) - 1); within
 //            a level the built children come first, their siblings second
@@ -229,6 +232,16 @@ struct LgNode {
   int32_t default_left;
   long long lg, lh;   // that split's left child statistics
   double lower, upper;  // the node's monotone weight bounds
+};
+
+// A lossguide heap entry: the node's key and its id (the node's LgNode is
+// kept at that id in a per-tree pool). The heap moves these 16 bytes, its
+// comparisons are of the key alone, so it pops in the same order as a heap
+// of whole nodes.
+struct LgKey {
+  long long key;
+  int32_t nid;
+  int32_t pad;
 };
 
 struct LgState {

@@ -2217,8 +2217,8 @@ __device__ __forceinline__ long long total_key(double v) {
   return b ^ (long long)((unsigned long long)(b >> 63) >> 1);
 }
 
-__device__ void lg_sift_up(LgNode* heap, int start, int pos) {
-  const LgNode hole = heap[pos];
+__device__ void lg_sift_up(LgKey* heap, int start, int pos) {
+  const LgKey hole = heap[pos];
   while (pos > start) {
     const int parent = (pos - 1) / 2;
     if (hole.key <= heap[parent].key) break;
@@ -2228,16 +2228,16 @@ __device__ void lg_sift_up(LgNode* heap, int start, int pos) {
   heap[pos] = hole;
 }
 
-__device__ LgNode lg_pop(LgNode* heap, int& n) {
-  LgNode item = heap[n - 1];
+__device__ LgKey lg_pop(LgKey* heap, int& n) {
+  LgKey item = heap[n - 1];
   --n;
   if (n > 0) {
-    const LgNode root = heap[0];
+    const LgKey root = heap[0];
     heap[0] = item;
     item = root;
     const int end = n;
     int pos = 0;
-    const LgNode hole = heap[0];
+    const LgKey hole = heap[0];
     int child = 1;
     while (end >= 2 && child <= end - 2) {
       if (heap[child].key <= heap[child + 1].key) child += 1;
@@ -2274,36 +2274,32 @@ __device__ void lg_step_serial(const DevConst& c, const uint32_t* __restrict__ f
                                const float* __restrict__ cuts, Front* front, Front* next,
                                Decision* dec, LevelState* ls, LevelState* ls_next,
                                hb_tree_node* __restrict__ tree, WNode* __restrict__ wtree, double ig,
-                               double ih, LgNode* heap, LgState* st, const LgState S0,
-                               const LgNode* s_new, int32_t* __restrict__ ndepth, int max_leaves,
-                               int depth_limit, int final_step, int& n_out);
+                               double ih, LgKey* heap, const LgNode* pool, LgState* st,
+                               const LgState S0, const LgKey* s_new, int32_t* __restrict__ ndepth,
+                               int max_leaves, int depth_limit, int final_step, int& n_out,
+                               int& n_rest);
 
 __global__ void __launch_bounds__(kLgThreads)
     k_lg_step(DevConst c, const uint32_t* __restrict__ fo, const float* __restrict__ cuts,
               const Cand* __restrict__ cand, const Front* __restrict__ pend, Front* front,
               Front* next, Decision* dec, LevelState* ls, LevelState* ls_next,
               hb_tree_node* __restrict__ tree, WNode* __restrict__ wtree,
-              const Scale* __restrict__ scale, LgNode* __restrict__ heap, LgState* st,
-              int32_t* __restrict__ ndepth, int max_leaves, int depth_limit, int final_step,
-              unsigned long long* __restrict__ best_key) {
+              const Scale* __restrict__ scale, LgKey* __restrict__ heap, LgNode* __restrict__ pool,
+              LgState* st, int32_t* __restrict__ ndepth, int max_leaves, int depth_limit,
+              int final_step, unsigned long long* __restrict__ best_key) {
   pdl_wait();
-  __shared__ LgNode s_new[2];
-  __shared__ int s_n;
+  __shared__ LgKey s_new[2];
+  __shared__ int s_n, s_rest;
   extern __shared__ __align__(16) unsigned char lg_dyn[];
-  LgNode* sheap = reinterpret_cast<LgNode*>(lg_dyn);  // the heap, worked in shared memory
+  LgKey* sheap = reinterpret_cast<LgKey*>(lg_dyn);  // the heap, worked in shared memory
   const LgState S0 = *st;
   if (S0.done) return;
   const double ig = scale->ig, ih = scale->ih;
   const int np = S0.n_pending;
-  {  // bring the heap in (8-byte words, all threads)
-    const unsigned long long* src = reinterpret_cast<const unsigned long long*>(heap);
-    unsigned long long* dst = reinterpret_cast<unsigned long long*>(sheap);
-    const int words = S0.heap_n * (int)(sizeof(LgNode) / 8);
-    for (int i = threadIdx.x; i < words; i += kLgThreads) dst[i] = src[i];
-  }
+  for (int i = threadIdx.x; i < S0.heap_n; i += kLgThreads) sheap[i] = heap[i];  // the heap in
   // each pending node's best split over its features (need_replace,
   // builder/mod.rs:313): its key from the scan (cand_key), cleared for the
-  // next step
+  // next step; the node into the pool at its id
   if (threadIdx.x < np) {
     const int node = threadIdx.x;
     const int bf = key_feature(best_key[node]);
@@ -2334,18 +2330,21 @@ __global__ void __launch_bounds__(kLgThreads)
       x.lg = x.lh = 0;
     }
     x.key = total_key((double)x.loss);
-    s_new[node] = x;
+    pool[x.nid] = x;
+    LgKey k;
+    k.key = x.key;
+    k.nid = x.nid;
+    k.pad = 0;
+    s_new[node] = k;
   }
   __syncthreads();
   if (threadIdx.x == 0) lg_step_serial(c, fo, cuts, front, next, dec, ls, ls_next, tree, wtree, ig, ih,
-                                       sheap, st, S0, s_new, ndepth, max_leaves, depth_limit, final_step, s_n);
+                                       sheap, pool, st, S0, s_new, ndepth, max_leaves, depth_limit,
+                                       final_step, s_n, s_rest);
   __syncthreads();
-  {  // the heap back out
-    const unsigned long long* src = reinterpret_cast<const unsigned long long*>(sheap);
-    unsigned long long* dst = reinterpret_cast<unsigned long long*>(heap);
-    const int words = s_n * (int)(sizeof(LgNode) / 8);
-    for (int i = threadIdx.x; i < words; i += kLgThreads) dst[i] = src[i];
-  }
+  // when growth ended, the nodes left in the heap become leaves
+  for (int i = threadIdx.x; i < s_rest; i += kLgThreads) lg_leaf(pool[sheap[i].nid], c, ig, ih, tree, wtree);
+  for (int i = threadIdx.x; i < s_n; i += kLgThreads) heap[i] = sheap[i];  // the heap out
 }
 
 // The heap work of a lossguide step, one thread, on the shared copy of the
@@ -2355,9 +2354,10 @@ __device__ void lg_step_serial(const DevConst& c, const uint32_t* __restrict__ f
                                const float* __restrict__ cuts, Front* front, Front* next,
                                Decision* dec, LevelState* ls, LevelState* ls_next,
                                hb_tree_node* __restrict__ tree, WNode* __restrict__ wtree, double ig,
-                               double ih, LgNode* heap, LgState* st, const LgState S0,
-                               const LgNode* s_new, int32_t* __restrict__ ndepth, int max_leaves,
-                               int depth_limit, int final_step, int& n_out) {
+                               double ih, LgKey* heap, const LgNode* pool, LgState* st,
+                               const LgState S0, const LgKey* s_new, int32_t* __restrict__ ndepth,
+                               int max_leaves, int depth_limit, int final_step, int& n_out,
+                               int& n_rest) {
   const int np = S0.n_pending;
   LgState S = S0;
   int n = S.heap_n;
@@ -2371,7 +2371,7 @@ __device__ void lg_step_serial(const DevConst& c, const uint32_t* __restrict__ f
   ls_next->n_front = 0;
   bool expanded = false;
   while (n > 0) {
-    const LgNode e = lg_pop(heap, n);
+    const LgNode e = pool[lg_pop(heap, n).nid];
     if (S.n_leaves >= max_leaves) {
       lg_leaf(e, c, ig, ih, tree, wtree);
       S.done = 1;
@@ -2458,8 +2458,9 @@ __device__ void lg_step_serial(const DevConst& c, const uint32_t* __restrict__ f
     break;
   }
   if (!expanded) S.done = 1;
-  if (S.done) {  // the nodes left in the heap are leaves
-    for (int i = 0; i < n; ++i) lg_leaf(heap[i], c, ig, ih, tree, wtree);
+  n_rest = 0;
+  if (S.done) {  // the nodes left in the heap are leaves (the whole CTA writes them)
+    n_rest = n;
     n = 0;
   }
   S.heap_n = n;
@@ -3344,9 +3345,10 @@ void launch_part_scatter(const Front* front, const Decision* dec, const PItem* i
 void launch_lg_step(const DevConst& c, const uint32_t* fo, const float* cuts, const Cand* cand,
                     const Front* pend, Front* front, Front* next, Decision* dec, LevelState* ls,
                     LevelState* ls_next, hb_tree_node* tree, WNode* wtree, const Scale* scale,
-                    LgNode* heap, int heap_cap, LgState* st, int32_t* ndepth, int max_leaves,
-                    int depth_limit, int final_step, unsigned long long* best_key, cudaStream_t s) {
-  const size_t smem = sizeof(LgNode) * (size_t)heap_cap;
+                    LgKey* heap, LgNode* pool, int heap_cap, LgState* st, int32_t* ndepth,
+                    int max_leaves, int depth_limit, int final_step, unsigned long long* best_key,
+                    cudaStream_t s) {
+  const size_t smem = sizeof(LgKey) * (size_t)heap_cap;
   static size_t granted[64] = {0};
   int dev = 0;
   cudaGetDevice(&dev);
@@ -3357,7 +3359,7 @@ void launch_lg_step(const DevConst& c, const uint32_t* fo, const float* cuts, co
       granted[dev] = smem;
   }
   launch_pdl(k_lg_step, dim3(1), dim3(kLgThreads), smem, s, c, fo, cuts, cand, pend, front, next, dec, ls, ls_next, tree,
-                                        wtree, scale, heap, st, ndepth, max_leaves, depth_limit,
+                                        wtree, scale, heap, pool, st, ndepth, max_leaves, depth_limit,
                                         final_step, best_key);
 }
 

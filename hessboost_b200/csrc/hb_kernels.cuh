@@ -143,8 +143,9 @@ void launch_part_scatter(const Front* front, const Decision* dec, const PItem* i
 void launch_lg_step(const DevConst& c, const uint32_t* fo, const float* cuts, const Cand* cand,
                     const Front* pend, Front* front, Front* next, Decision* dec, LevelState* ls,
                     LevelState* ls_next, hb_tree_node* tree, WNode* wtree, const Scale* scale,
-                    LgNode* heap, int heap_cap, LgState* st, int32_t* ndepth, int max_leaves,
-                    int depth_limit, int final_step, unsigned long long* best_key, cudaStream_t s);
+                    LgKey* heap, LgNode* pool, int heap_cap, LgState* st, int32_t* ndepth,
+                    int max_leaves, int depth_limit, int final_step, unsigned long long* best_key,
+                    cudaStream_t s);
 void launch_lg_setup(LgState* st, int32_t* ndepth, hb_tree_node* tree, const Front* root,
                      const Scale* scale, LevelState* ls_next, cudaStream_t s);
 void launch_root_setup(uint64_t n_rows, Front* front, HEntry* entries, LevelState* ls,
