@@ -369,7 +369,7 @@ size_t gradients_b3_smem(int max_nodes, int ct_depth) {
   size_t b = sizeof(WNode) * (size_t)max_nodes;
   if (ct_depth > 0) {
     const size_t inner = (size_t(1) << ct_depth) - 1;
-    b += 8 * inner + 4 * (inner + 1) + 2 * (2 * inner + 1) + (size_t)kGradThreads * kRecPitch;
+    b += 4 * inner + 4 * (inner + 1) + 2 * (2 * inner + 1) + (size_t)kGradThreads * kRecPitch;
     b = (b + 15) / 16 * 16;
   }
   return b;
@@ -387,7 +387,10 @@ __global__ void __launch_bounds__(kGradThreads, 4)
   if (wtree && !(pending && *pending)) wtree = nullptr;  // no tree waiting for the margins
   const int D = ct_depth;
   const uint32_t inner = D > 0 ? (1u << D) - 1u : 0u;
-  uint2* s_ct = reinterpret_cast<uint2*>(s_tree + max_nodes);       // [inner]: feature | dl << 31, limit
+  // [inner]: feature | min(limit, 256) << 8 | dl << 31 (the records hold at
+  // most 28 features of 8-bit bins, so one word a node: one shared wavefront
+  // a step)
+  uint32_t* s_ct = reinterpret_cast<uint32_t*>(s_tree + max_nodes);
   float* s_leaf = reinterpret_cast<float*>(s_ct + inner);           // [inner + 1]
   int16_t* s_pos = reinterpret_cast<int16_t*>(s_leaf + inner + 1);  // [2 inner + 1]: node of a position
   uint8_t* s_rec = reinterpret_cast<uint8_t*>(s_pos + 2 * inner + 1) + 0;
@@ -402,11 +405,11 @@ __global__ void __launch_bounds__(kGradThreads, 4)
           const int k = s_pos[p];
           const WNode nd = s_tree[k];
           if (nd.left >= 0) {
-            s_ct[p] = make_uint2(nd.feature, nd.limit);
+            s_ct[p] = (nd.feature & 0x800000ffu) | (min(nd.limit, 256u) << 8);
             s_pos[2 * p + 1] = (int16_t)nd.left;
             s_pos[2 * p + 2] = (int16_t)(nd.left + 1);
           } else {  // a leaf: both children carry it
-            s_ct[p] = make_uint2(0u, 0u);
+            s_ct[p] = 0u;
             s_pos[2 * p + 1] = (int16_t)k;
             s_pos[2 * p + 2] = (int16_t)k;
           }
@@ -471,10 +474,10 @@ __global__ void __launch_bounds__(kGradThreads, 4)
       for (int d = 0; d < D; ++d) {
 #pragma unroll
         for (int j = 0; j < 3; ++j) {
-          const uint2 cn = s_ct[idx[j]];
-          const uint32_t f = cn.x & 0x7fffffffu;
+          const uint32_t cn = s_ct[idx[j]];
+          const uint32_t f = cn & 0xffu;
           const bool miss = (msk[j] >> f) & 1u;
-          const bool left = miss ? (cn.x >> 31) != 0u : (uint32_t)my_rec[32 * j + f] < cn.y;
+          const bool left = miss ? (cn >> 31) != 0u : (uint32_t)my_rec[32 * j + f] < ((cn >> 8) & 0x1ffu);
           idx[j] = 2 * idx[j] + (left ? 1u : 2u);
         }
       }
