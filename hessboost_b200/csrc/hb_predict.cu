@@ -66,7 +66,9 @@ __global__ void k_predict(const PNode* __restrict__ nodes, const uint32_t* __res
 // walk is then d steps with no child pointers and no leaf test.
 //
 // k_predict_chunked keeps a tile of rows in shared memory (feature-major,
-// stride tile + 1 so a warp's reads of one feature are conflict-free) and
+// stride tile, a multiple of 32: thread t reads its row's values from bank
+// t % 32 whatever feature each lane's node asks for, so the walk's feature
+// reads never conflict; only the tile's staging writes do) and
 // streams the forest through two shared buffers of kChunkBytes with
 // cp.async, the next chunk loading while the current one is walked. The
 // margin is summed in tree order with the same f32 operations as k_predict.
@@ -77,7 +79,7 @@ constexpr int kPredSmemBudget = 224 * 1024;
 
 struct CNode {
   float cond;
-  uint32_t meta;  // feature * (tile + 1): its row in the shared tile | default_left << 31
+  uint32_t meta;  // feature * tile: its row in the shared tile | default_left << 31
 };
 struct TreeHdr {
   uint32_t off;    // byte offset of the tree in its chunk
@@ -105,7 +107,7 @@ __global__ void __launch_bounds__(kPredThreads, 1)
                       const float* __restrict__ x, uint64_t n_rows, uint32_t n_cols, int tile,
                       uint32_t x_bytes, float* __restrict__ out) {
   extern __shared__ __align__(16) unsigned char sm[];
-  float* s_x = reinterpret_cast<float*>(sm);  // [n_cols][tile + 1]
+  float* s_x = reinterpret_cast<float*>(sm);  // [n_cols][tile]
   unsigned char* const buf0 = sm + x_bytes;  // chunk c lives at buf0 + (c & 1) * kChunkBytes
   const int tid = threadIdx.x;
   const uint64_t n_tiles = (n_rows + tile - 1) / tile;
@@ -117,7 +119,7 @@ __global__ void __launch_bounds__(kPredThreads, 1)
     const int nv = rows * (int)n_cols;
     for (int i = tid; i < nv; i += kPredThreads) {
       const int r = i / (int)n_cols, f = i - r * (int)n_cols;
-      s_x[f * (tile + 1) + r] = __ldg(xt + i);
+      s_x[f * tile + r] = __ldg(xt + i);
     }
     auto issue = [&](int c) {
       const ChunkHdr ch = chunks[c];
@@ -273,7 +275,7 @@ bool build_complete(const hb_tree_node* nodes, const uint64_t* tree_ptr, uint64_
         work.push_back({2 * it.p + 2, it.id, it.k + 1});
       } else {
         cn[it.p].cond = s.split_cond;
-        cn[it.p].meta = s.split_feature * (uint32_t)(tile + 1) | (s.default_left ? 0x80000000u : 0u);
+        cn[it.p].meta = s.split_feature * (uint32_t)tile | (s.default_left ? 0x80000000u : 0u);
         work.push_back({2 * it.p + 1, s.left, it.k + 1});
         work.push_back({2 * it.p + 2, s.right, it.k + 1});
       }
@@ -385,7 +387,7 @@ hb_status hb_predictor_create(int32_t device_ordinal, const hb_tree_node* nodes,
                        chunks, heads)) {
       p->tile = tile;
       p->n_chunks = (int)chunks.size();
-      p->x_bytes = (uint32_t)((4ull * n_features * (tile + 1) + 15) & ~15ull);
+      p->x_bytes = (uint32_t)((4ull * n_features * tile + 15) & ~15ull);
       p->smem = p->x_bytes + 2 * (size_t)kChunkBytes;
       p->base0 = base[0];
       ok = cudaMalloc(&p->carena, carena.size()) == cudaSuccess &&
