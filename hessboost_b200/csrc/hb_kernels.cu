@@ -444,7 +444,31 @@ __global__ void __launch_bounds__(kGradThreads, 4)
     uint8_t* line = rec + (uint64_t)q * kBlockBytes;
     uint4 L[6];
     float m[3], y[3], w[3];
-    if (wtree && q < nblk) {
+    if (wtree && D > 0) {
+      // The warp's 32 row blocks, 96 record bytes each, loaded in block
+      // order: chunk c = lane + 32 k is 16-byte part c % 6 of block c / 6,
+      // so a load reads about six blocks instead of 32 (one a lane). Each
+      // chunk then goes to its block's staging row.
+      const uint32_t nl = min(32u, nblk - w0);
+      const uint4* gsrc = reinterpret_cast<const uint4*>(rec + (uint64_t)w0 * kBlockBytes);
+      uint8_t* wrec = s_rec + (threadIdx.x & ~31u) * kRecPitch;
+#pragma unroll
+      for (int k = 0; k < 6; ++k) {
+        const uint32_t cq = lane + 32u * k, li = cq / 6u;
+        if (li < nl) L[k] = gsrc[li * (kBlockBytes / 16u) + (cq - 6u * li)];
+      }
+#pragma unroll
+      for (int k = 0; k < 6; ++k) {
+        const uint32_t cq = lane + 32u * k, li = cq / 6u;
+        if (li < nl) {
+          uint32_t* d = reinterpret_cast<uint32_t*>(wrec + li * kRecPitch + 16u * (cq - 6u * li));
+          d[0] = L[k].x;
+          d[1] = L[k].y;
+          d[2] = L[k].z;
+          d[3] = L[k].w;
+        }
+      }
+    } else if (wtree && q < nblk) {
 #pragma unroll
       for (int k = 0; k < 6; ++k) L[k] = reinterpret_cast<const uint4*>(line)[k];
     }
@@ -456,16 +480,6 @@ __global__ void __launch_bounds__(kGradThreads, 4)
       w[j] = (in && weight) ? weight[r0 + j] : 1.0f;
     }
     if (wtree && D > 0) {
-      if (q < nblk) {
-#pragma unroll
-        for (int k = 0; k < 6; ++k) {
-          uint32_t* d = reinterpret_cast<uint32_t*>(my_rec + 16 * k);
-          d[0] = L[k].x;
-          d[1] = L[k].y;
-          d[2] = L[k].z;
-          d[3] = L[k].w;
-        }
-      }
       __syncwarp();
       // the three walks step together (independent chains of shared loads)
       uint32_t msk[3], idx[3] = {0u, 0u, 0u};
