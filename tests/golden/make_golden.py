@@ -21,8 +21,9 @@ reference's tests compute them (f32 arithmetic throughout).
   the native binary format, and ``native/saved_<version>_<name>.bin`` is the
   binary file of every extracted prediction model.
 
-Usage: ``python tests/golden/make_golden.py [/path/to/reference]``.  The
-output is committed, so the tests never need the reference at run time.
+Usage: ``python tests/golden/make_golden.py /path/to/reference`` (the root of
+a hessboost 0.4.9 checkout).  The output is committed, so the tests never
+need the reference at run time.
 """
 
 import json
@@ -152,4 +153,6 @@ def main(ref):
 
 
 if __name__ == "__main__":
-    main(sys.argv[1] if len(sys.argv) > 1 else "/root/reference")
+    if len(sys.argv) != 2:
+        sys.exit("usage: python tests/golden/make_golden.py /path/to/hessboost-checkout")
+    main(sys.argv[1])
